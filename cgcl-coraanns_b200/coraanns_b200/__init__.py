@@ -1,0 +1,260 @@
+"""Python binding of libcoraanns_b200.so (the C ABI in include/cora_b200.h).
+
+``HybridIndex`` mirrors the reference's ``coraanns::HybridIndex``
+(include/coraanns/search/hybrid.cuh:18-203 of the reference project): same method names,
+argument meaning and error behaviour, with the C++ exception types mapped to
+``InvalidArgument`` (std::invalid_argument, a ``LogicError``), ``LogicError``
+(std::logic_error) and ``RuntimeError`` (std::runtime_error).
+
+There is no CPU fallback: importing this module fails if the CUDA library was not built.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+
+PKG_ROOT = Path(__file__).resolve().parent.parent
+LIB_PATH = PKG_ROOT / "_build" / "libcoraanns_b200.so"
+HEADER = PKG_ROOT.parent / "include" / "cora_b200.h"
+
+if not LIB_PATH.exists():
+    raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {PKG_ROOT}` "
+                      "(or __graft_entry__.build()); there is no CPU fallback")
+
+_lib = C.CDLL(str(LIB_PATH))
+
+CORA_OK, CORA_EINVAL, CORA_ESTATE, CORA_ERUNTIME, CORA_ECUDA, CORA_ENOMEM = range(6)
+
+# Exported symbols, in the order include/cora_b200.h declares them.
+EXPORTS = [
+    "cora_last_error", "cora_create", "cora_destroy", "cora_load_from_raw_pointers",
+    "cora_load_index_file", "cora_index_info", "cora_prepare_workspace", "cora_free_workspace",
+    "cora_reset_buffer", "cora_search", "cora_search_device", "cora_check_device",
+    "cora_seed_thresholds", "cora_capture_thresholds", "cora_set_vanguard_size",
+    "cora_get_vanguard_size", "cora_set_queue_capacity", "cora_set_queue_spill_capacity",
+    "cora_get_queue_capacity", "cora_set_profiling", "cora_set_candidate_stats",
+    "cora_set_gpu_filter_timing", "cora_set_cross_query_reuse", "cora_set_cpu_secondary_filter",
+    "cora_set_ip_kernel_type", "cora_get_ip_kernel_type", "cora_get_last_submitted_count",
+    "cora_get_last_refined_count", "cora_get_last_spilled_count", "cora_get_last_gpu_filter_ms",
+    "cora_debug_copy", "cora_get_candidate_capacity",
+]
+
+_p = C.c_void_p
+_u64 = C.c_uint64
+
+
+def _sig(name, res, *args):
+    f = getattr(_lib, name)
+    f.restype = res
+    f.argtypes = list(args)
+
+
+_sig("cora_last_error", C.c_char_p)
+_sig("cora_create", C.c_int, C.POINTER(_p), C.c_int)
+_sig("cora_destroy", None, _p)
+_sig("cora_load_from_raw_pointers", C.c_int, _p, _u64, _u64, _u64, _u64, _u64, _p, _p, _p, _p,
+     _p, _p, _p, _p)
+_sig("cora_load_index_file", C.c_int, _p, C.c_char_p)
+_sig("cora_index_info", C.c_int, _p, _p)
+_sig("cora_prepare_workspace", C.c_int, _p, _u64, _u64, _u64)
+_sig("cora_free_workspace", None, _p)
+_sig("cora_reset_buffer", C.c_int, _p, _p, _u64)
+_sig("cora_search", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p, C.c_int)
+_sig("cora_search_device", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p, _p)
+_sig("cora_check_device", C.c_int, _p)
+_sig("cora_seed_thresholds", C.c_int, _p, _p, _u64)
+_sig("cora_capture_thresholds", C.c_int, _p, _p, _u64)
+_sig("cora_set_vanguard_size", C.c_int, _p, _u64)
+_sig("cora_get_vanguard_size", _u64, _p)
+_sig("cora_set_queue_capacity", C.c_int, _p, _u64)
+_sig("cora_set_queue_spill_capacity", C.c_int, _p, _u64)
+_sig("cora_get_queue_capacity", _u64, _p)
+for _n in ("cora_set_profiling", "cora_set_candidate_stats", "cora_set_gpu_filter_timing",
+           "cora_set_cross_query_reuse", "cora_set_cpu_secondary_filter", "cora_set_ip_kernel_type"):
+    _sig(_n, None, _p, C.c_int)
+_sig("cora_get_ip_kernel_type", C.c_int, _p)
+_sig("cora_get_last_submitted_count", _u64, _p)
+_sig("cora_get_last_refined_count", _u64, _p)
+_sig("cora_get_last_spilled_count", _u64, _p)
+_sig("cora_get_last_gpu_filter_ms", C.c_float, _p)
+_sig("cora_debug_copy", C.c_int, _p, C.c_int, _p, _u64)
+_sig("cora_get_candidate_capacity", _u64, _p)
+
+
+class LogicError(Exception):
+    """std::logic_error"""
+
+
+class InvalidArgument(LogicError, ValueError):
+    """std::invalid_argument (a std::logic_error in C++)"""
+
+
+class CoraRuntimeError(RuntimeError):
+    """std::runtime_error"""
+
+
+def _check(rc):
+    if rc == CORA_OK:
+        return
+    msg = _lib.cora_last_error().decode(errors="replace")
+    if rc == CORA_EINVAL:
+        raise InvalidArgument(msg)
+    if rc == CORA_ESTATE:
+        raise LogicError(msg)
+    if rc == CORA_ENOMEM:
+        raise MemoryError(msg)
+    raise CoraRuntimeError(msg)
+
+
+def _ptr(a):
+    return None if a is None else C.c_void_p(a.ctypes.data)
+
+
+class KernelType:
+    Lut4Bit = 0
+    Bitwise = 1
+
+
+class HybridIndex:
+    """coraanns::HybridIndex over the C ABI; owns one engine on one GPU."""
+
+    def __init__(self, device: int = 0):
+        h = C.c_void_p()
+        _check(_lib.cora_create(C.byref(h), int(device)))
+        self._h = h
+        self.device = device
+
+    def close(self):
+        if getattr(self, "_h", None):
+            _lib.cora_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    # -- loading ---------------------------------------------------------------------
+    def load_from_raw_pointers(self, num_vecs, d, p_d, n_centroids, ex_b, h_centroids,
+                               h_rotator, h_short_data, h_short_factors, h_long_code,
+                               h_ex_factors, h_ids, h_cluster_sizes):
+        arrs = [np.ascontiguousarray(a, dt) if a is not None else None for a, dt in (
+            (h_centroids, np.float32), (h_rotator, np.float32), (h_short_data, np.uint32),
+            (h_short_factors, np.float32), (h_long_code, np.uint8), (h_ex_factors, np.float32),
+            (h_ids, np.uint32), (h_cluster_sizes, np.uint64))]
+        _check(_lib.cora_load_from_raw_pointers(self._h, num_vecs, d, p_d, n_centroids, ex_b,
+                                                *[_ptr(a) for a in arrs]))
+
+    def load_search_data(self, sd: dict):
+        """Load the arrays of a SearchData-layout dict (keys as oracle/py_oracle.py)."""
+        self.load_from_raw_pointers(sd["num"], sd["dim"], sd["D"], sd["nlist"], sd["ex_bits"],
+                                    sd["centroids"], sd["rotator"], sd["short_data"],
+                                    sd["short_factors"], sd["long_codes"], sd["ex_factors"],
+                                    sd["ids"], sd["sizes"])
+
+    def load_index_file(self, path):
+        _check(_lib.cora_load_index_file(self._h, str(path).encode()))
+
+    def index_info(self):
+        out = np.zeros(6, np.uint64)
+        _check(_lib.cora_index_info(self._h, _ptr(out)))
+        return dict(zip(("num", "dim", "padded_dim", "nlist", "ex_bits", "max_cluster"),
+                        map(int, out)))
+
+    # -- workspace -------------------------------------------------------------------
+    def prepare_workspace(self, max_queries, max_topk, max_nprobe):
+        _check(_lib.cora_prepare_workspace(self._h, max_queries, max_topk, max_nprobe))
+
+    def free_workspace(self):
+        _lib.cora_free_workspace(self._h)
+
+    def reset_buffer(self, h_queries, num_queries=None):
+        q = np.ascontiguousarray(h_queries, np.float32)
+        n = q.shape[0] if num_queries is None else num_queries
+        _check(_lib.cora_reset_buffer(self._h, _ptr(q), n))
+
+    # -- search ----------------------------------------------------------------------
+    def search(self, h_queries, topk, nprobe, batch_q=4, num_queries=None):
+        q = np.ascontiguousarray(h_queries, np.float32)
+        n = q.shape[0] if num_queries is None else num_queries
+        dists = np.empty((n, topk), np.float32)
+        ids = np.empty((n, topk), np.uint32)
+        _check(_lib.cora_search(self._h, _ptr(q), n, topk, nprobe, _ptr(dists), _ptr(ids),
+                                int(batch_q)))
+        return dists, ids
+
+    def search_device(self, d_queries: int, num_queries, topk, nprobe, d_dists: int,
+                      d_ids: int, stream: int = 0):
+        """Enqueue a search on device pointers (e.g. torch tensors' data_ptr())."""
+        _check(_lib.cora_search_device(self._h, C.c_void_p(d_queries), num_queries, topk, nprobe,
+                                       C.c_void_p(d_dists), C.c_void_p(d_ids),
+                                       C.c_void_p(stream) if stream else None))
+
+    def check_device(self):
+        _check(_lib.cora_check_device(self._h))
+
+    def seed_thresholds(self, h_in, nq=None):
+        t = np.ascontiguousarray(h_in, np.float32)
+        _check(_lib.cora_seed_thresholds(self._h, _ptr(t), t.shape[0] if nq is None else nq))
+
+    def capture_thresholds(self, nq):
+        out = np.empty(nq, np.float32)
+        _check(_lib.cora_capture_thresholds(self._h, _ptr(out), nq))
+        return out
+
+    # -- knobs -----------------------------------------------------------------------
+    def set_vanguard_size(self, size):
+        _check(_lib.cora_set_vanguard_size(self._h, size))
+
+    def get_vanguard_size(self):
+        return int(_lib.cora_get_vanguard_size(self._h))
+
+    def set_queue_capacity(self, capacity):
+        _check(_lib.cora_set_queue_capacity(self._h, capacity))
+
+    def set_queue_spill_capacity(self, capacity):
+        _check(_lib.cora_set_queue_spill_capacity(self._h, capacity))
+
+    def get_queue_capacity(self):
+        return int(_lib.cora_get_queue_capacity(self._h))
+
+    def set_profiling(self, on): _lib.cora_set_profiling(self._h, int(bool(on)))
+    def set_candidate_stats(self, on): _lib.cora_set_candidate_stats(self._h, int(bool(on)))
+    def set_gpu_filter_timing(self, on): _lib.cora_set_gpu_filter_timing(self._h, int(bool(on)))
+    def set_cross_query_reuse(self, on): _lib.cora_set_cross_query_reuse(self._h, int(bool(on)))
+    def set_cpu_secondary_filter(self, on): _lib.cora_set_cpu_secondary_filter(self._h, int(bool(on)))
+    def set_ip_kernel_type(self, t): _lib.cora_set_ip_kernel_type(self._h, int(t))
+    def get_ip_kernel_type(self): return int(_lib.cora_get_ip_kernel_type(self._h))
+
+    def get_last_submitted_count(self): return int(_lib.cora_get_last_submitted_count(self._h))
+    def get_last_refined_count(self): return int(_lib.cora_get_last_refined_count(self._h))
+    def get_last_spilled_count(self): return int(_lib.cora_get_last_spilled_count(self._h))
+    def get_last_gpu_filter_ms(self): return float(_lib.cora_get_last_gpu_filter_ms(self._h))
+
+    # -- diagnostics -----------------------------------------------------------------
+    def candidate_capacity(self):
+        return int(_lib.cora_get_candidate_capacity(self._h))
+
+    def debug(self, what: str, nq: int, nprobe: int = 0):
+        info = self.index_info()
+        D = info["padded_dim"]
+        W4 = 4 * ((D + 127) // 128)
+        spec = {
+            "rotated": (0, np.float32, (nq, D)),
+            "probe_ids": (1, np.int32, (nq, nprobe)),
+            "probe_g": (2, np.float32, (nq, nprobe)),
+            "cand_count": (3, np.uint32, (nq,)),
+            "thresholds1": (4, np.float32, (nq,)),
+            "planes": (5, np.uint32, (nq, 8, W4)),
+            "scalars": (6, np.float32, (nq, 4)),
+            "cand_gids": (7, np.uint32, (nq, self.candidate_capacity())),
+        }[what]
+        out = np.empty(spec[2], spec[1])
+        _check(_lib.cora_debug_copy(self._h, spec[0], _ptr(out), out.nbytes))
+        return out

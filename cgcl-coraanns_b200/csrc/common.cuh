@@ -1,0 +1,169 @@
+// Shared device utilities for the IVF-RaBitQ search kernels (sm_100a).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cora {
+
+// ---- ordering ------------------------------------------------------------------------
+// Monotone float -> uint32 map; every (value, id) order in the search contract is the
+// lexicographic order of (ord_f32(value), id) packed as a uint64 key.
+__host__ __device__ __forceinline__ uint32_t ord_f32(float f) {
+#ifdef __CUDA_ARCH__
+    const uint32_t u = __float_as_uint(f);
+#else
+    uint32_t u;
+    __builtin_memcpy(&u, &f, 4);
+#endif
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__host__ __device__ __forceinline__ float unord_f32(uint32_t o) {
+    const uint32_t u = (o & 0x80000000u) ? (o & 0x7FFFFFFFu) : ~o;
+#ifdef __CUDA_ARCH__
+    return __uint_as_float(u);
+#else
+    float f;
+    __builtin_memcpy(&f, &u, 4);
+    return f;
+#endif
+}
+__host__ __device__ __forceinline__ uint64_t make_key(float v, uint32_t id) {
+    return (static_cast<uint64_t>(ord_f32(v)) << 32) | id;
+}
+constexpr uint64_t kKeyMax = ~0ull;
+
+// ---- device error word ---------------------------------------------------------------
+// Kernels never trap; a bounded wait that gives up, or a capacity overflow, sets a bit
+// here and the host turns it into an error after the stream synchronises.
+enum DeviceError : int {
+    kDevOk = 0,
+    kDevCandidateOverflow = 1,
+    kDevWaitTimeout = 2,
+    kDevBadInput = 4,
+};
+
+// ---- TMA bulk copies (cp.async.bulk, no multicast) with bounded mbarrier waits -------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Waits for the mbarrier phase with a wall-clock limit (default 2 s). On timeout it
+// records kDevWaitTimeout and returns false; the caller stops issuing work and exits.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err,
+                                                  uint64_t limit_ns = 2000000000ull) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (global_ns() - t0 > limit_ns) {
+            atomicOr(err, kDevWaitTimeout);
+            return false;
+        }
+        __nanosleep(64);
+    }
+}
+// 1-D bulk copy global -> shared; both addresses 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void *smem_dst, const void *gmem_src, uint32_t bytes,
+                                         uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---- block-wide bitonic sort of a power-of-two uint64 array in shared memory ---------
+// Callers synchronise before the call; the function ends with a barrier.
+__device__ __forceinline__ void block_bitonic_sort(uint64_t *a, int n) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const uint64_t x = a[i], y = a[ixj];
+                    const bool up = (i & k) == 0;
+                    if ((x > y) == up) {
+                        a[i] = y;
+                        a[ixj] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__host__ __device__ __forceinline__ int next_pow2(int x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+// Streaming block top-S of uint64 keys (ascending). Shared layout: buf[0, S) holds the
+// current best (sorted; unused slots kKeyMax), buf[S, S + stage_cap) stages new keys,
+// buf is sized `sort_n` = next_pow2(S + stage_cap). Keys must be < threshold() to be
+// staged; at most stage_cap keys may be staged between two flush() calls.
+struct BlockTopK {
+    uint64_t *buf;
+    int S, stage_cap, sort_n;
+    int *n_staged;      // shared counter
+    uint64_t *thresh;   // shared: current S-th best key (kKeyMax while fewer than S)
+
+    __device__ void init(uint64_t limit_key) {
+        for (int i = threadIdx.x; i < sort_n; i += blockDim.x) buf[i] = kKeyMax;
+        if (threadIdx.x == 0) {
+            *n_staged = 0;
+            *thresh = limit_key;
+        }
+        __syncthreads();
+    }
+    __device__ __forceinline__ void offer(uint64_t key) {
+        if (key < *thresh) {
+            const int pos = atomicAdd(n_staged, 1);
+            buf[S + pos] = key;
+        }
+    }
+    // All threads call after their offers. `limit_key` caps the threshold (strict bound).
+    __device__ void flush(uint64_t limit_key) {
+        __syncthreads();
+        const int n = *n_staged;
+        if (n == 0) return;
+        for (int i = S + n + threadIdx.x; i < sort_n; i += blockDim.x) buf[i] = kKeyMax;
+        __syncthreads();
+        block_bitonic_sort(buf, sort_n);
+        if (threadIdx.x == 0) {
+            *n_staged = 0;
+            const uint64_t t = buf[S - 1];
+            *thresh = t < limit_key ? t : limit_key;
+        }
+        __syncthreads();
+    }
+};
+
+}  // namespace cora

@@ -1,0 +1,893 @@
+// B200-native IVF-RaBitQ search engine: host orchestration and the C ABI of
+// include/cora_b200.h. One engine owns one GPU's copy (or shard) of an index, its
+// workspace and one CUDA stream; every search is a fixed sequence of kernels on that
+// stream with no host round trip until the results are read back.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cfloat>
+#include <climits>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/cora_b200.h"
+#include "common.cuh"
+#include "kernels_query.cuh"
+#include "kernels_refine.cuh"
+#include "kernels_scan.cuh"
+
+namespace cora {
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string &m) : std::runtime_error(m), code(c) {}
+};
+[[noreturn]] void fail(int code, const std::string &msg) { throw Error(code, msg); }
+
+#define CUDA_TRY(call)                                                                  \
+    do {                                                                                \
+        cudaError_t e_ = (call);                                                        \
+        if (e_ != cudaSuccess)                                                          \
+            ::cora::fail(CORA_ECUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+// Limits of the reference (include/coraanns/search/parameters.hpp:9-13).
+constexpr uint64_t kDefaultVanguard = 5, kMaxQueryChunk = 65535, kMaxProbeCount = 65536;
+constexpr uint64_t kDefaultQueueCapacity = 1ull << 26, kDefaultSpillCapacity = 1ull << 24;
+constexpr uint64_t kMaxTopk = 4096, kMaxProbeFast = 4096, kMaxPaddedDim = 1024;
+constexpr int kVanguardMinKeep = 20;
+
+// parameters.hpp:15-25
+void validate_search_shape(uint64_t queries, uint64_t topk, uint64_t nprobe, uint64_t centroids,
+                           uint64_t padded_dim) {
+    if (queries == 0 || queries > kMaxQueryChunk)
+        fail(CORA_EINVAL, "query count must be in [1, 65535]; split larger batches");
+    if (topk == 0 || topk > INT_MAX / queries)
+        fail(CORA_EINVAL, "topk must be positive and queries * topk must fit an int");
+    if (nprobe == 0 || nprobe > kMaxProbeCount || nprobe > centroids)
+        fail(CORA_EINVAL, "nprobe must be in [1, min(nlist, 65536)]");
+    if (centroids > INT_MAX / queries || padded_dim == 0 || padded_dim > INT_MAX / (queries * 4))
+        fail(CORA_EINVAL, "query workspace exceeds kernel indexing limits");
+}
+
+template <typename T>
+struct DevBuf {
+    T *p = nullptr;
+    size_t n = 0;
+    void alloc(size_t count) {
+        release();
+        if (count == 0) return;
+        CUDA_TRY(cudaMalloc(&p, count * sizeof(T)));
+        n = count;
+    }
+    void release() noexcept {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = 0;
+    }
+    ~DevBuf() { release(); }
+};
+
+}  // namespace
+
+struct Engine {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    cudaStream_t last_stream = nullptr;
+    cudaEvent_t ev_filter0 = nullptr, ev_filter1 = nullptr;
+    int num_sms = 148;
+
+    // index
+    bool loaded = false;
+    uint64_t N = 0, dim = 0, D = 0, nlist = 0, ex_bits = 0, max_cluster = 0;
+    int G16 = 0, W4 = 0, LC = 0;
+    DevBuf<float> centroids, rotator;
+    DevBuf<uint4> scan4;
+    DevBuf<uint8_t> long_codes;
+    DevBuf<float2> ex_factors;
+    DevBuf<uint32_t> ids, cl_start, cl_size;
+    DevBuf<uint8_t> owned;  // optional shard ownership mask (all clusters when empty)
+
+    // options (hybrid.cuh:66-113)
+    uint64_t vanguard = kDefaultVanguard;
+    uint64_t queue_capacity = kDefaultQueueCapacity, spill_capacity = kDefaultSpillCapacity;
+    bool profiling = false, candidate_stats = false, gpu_filter_timing = false;
+    bool cross_query_reuse = true, cpu_secondary_filter = true;
+    int ip_kernel_type = 0;
+
+    // workspace
+    bool ws_ready = false;
+    uint64_t ws_q = 0, ws_k = 0, ws_np = 0, ws_vg = 0, cap = 0;
+    DevBuf<float> raw_q, qr, gmat, probe_g, T0, T1, out_d;
+    DevBuf<QueryScalars> scal;
+    DevBuf<uint32_t> planes, cand_cnt, seed_cnt, pair_cnt, pair_off, pair_cur, item_off, pairs,
+        n_items, out_i;
+    DevBuf<int> probe_ids, item_counter, err;
+    DevBuf<uint64_t> bound, cand_rec, cand_key;
+    DevBuf<ScanItem> items;
+    DevBuf<unsigned long long> stats;
+    std::vector<float> h_T0;  // host mirror kept for capture/seed without device syncs
+
+    // last-search state
+    uint64_t last_nq = 0, last_np = 0, last_submitted = 0, last_refined = 0;
+    float last_filter_ms = 0.0f;
+
+    explicit Engine(int dev) : device(dev) {
+        CUDA_TRY(cudaSetDevice(device));
+        CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+        CUDA_TRY(cudaEventCreate(&ev_filter0));
+        CUDA_TRY(cudaEventCreate(&ev_filter1));
+        CUDA_TRY(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device));
+        last_stream = stream;
+    }
+    ~Engine() {
+        cudaSetDevice(device);
+        if (stream) cudaStreamSynchronize(stream);
+        free_workspace();
+        if (ev_filter0) cudaEventDestroy(ev_filter0);
+        if (ev_filter1) cudaEventDestroy(ev_filter1);
+        if (stream) cudaStreamDestroy(stream);
+    }
+
+    // ---------------------------------------------------------------- loading
+    void load(uint64_t num_vecs, uint64_t d, uint64_t p_d, uint64_t n_centroids, uint64_t ex_b,
+              const float *h_centroids, const float *h_rotator, const uint32_t *h_short,
+              const float *h_short_factors, const uint8_t *h_long, const float *h_exf,
+              const uint32_t *h_ids, const uint64_t *h_sizes) {
+        if (loaded) fail(CORA_ESTATE, "index already loaded");
+        if (!num_vecs || num_vecs > UINT32_MAX || !d || p_d < d || p_d % 64 || !n_centroids ||
+            ex_b > 8 || !h_centroids || !h_rotator || !h_short || !h_short_factors || !h_ids ||
+            !h_sizes)
+            fail(CORA_EINVAL, "invalid index shape or missing index data");
+        if (ex_b != 7 || !h_long || !h_exf)
+            fail(CORA_EINVAL, "this engine refines with 7-bit extended codes (8-bit RaBitQ); "
+                              "ex_bits must be 7 and extended codes present");
+        if (p_d > kMaxPaddedDim) fail(CORA_EINVAL, "padded_dim above 1024 is not supported");
+        uint64_t count = 0, largest = 0;
+        std::vector<uint32_t> starts(n_centroids), sizes(n_centroids);
+        for (uint64_t c = 0; c < n_centroids; ++c) {
+            if (h_sizes[c] > num_vecs - count) fail(CORA_EINVAL, "cluster sizes exceed index size");
+            starts[c] = static_cast<uint32_t>(count);
+            sizes[c] = static_cast<uint32_t>(h_sizes[c]);
+            count += h_sizes[c];
+            largest = std::max<uint64_t>(largest, h_sizes[c]);
+        }
+        if (count != num_vecs) fail(CORA_EINVAL, "cluster sizes differ from index size");
+        CUDA_TRY(cudaSetDevice(device));
+        N = num_vecs;
+        dim = d;
+        D = p_d;
+        nlist = n_centroids;
+        ex_bits = ex_b;
+        max_cluster = largest;
+        G16 = static_cast<int>((D + 127) / 128);
+        W4 = 4 * G16;
+        LC = static_cast<int>(D * ex_bits / 8);
+        centroids.alloc(nlist * D);
+        rotator.alloc(dim * D);
+        CUDA_TRY(cudaMemcpy(centroids.p, h_centroids, nlist * D * 4, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(rotator.p, h_rotator, dim * D * 4, cudaMemcpyHostToDevice));
+        cl_start.alloc(nlist);
+        cl_size.alloc(nlist);
+        CUDA_TRY(cudaMemcpy(cl_start.p, starts.data(), nlist * 4, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(cl_size.p, sizes.data(), nlist * 4, cudaMemcpyHostToDevice));
+        long_codes.alloc(N * LC);
+        ex_factors.alloc(N);
+        ids.alloc(N);
+        CUDA_TRY(cudaMemcpy(long_codes.p, h_long, N * LC, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(ex_factors.p, h_exf, N * 8, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(ids.p, h_ids, N * 4, cudaMemcpyHostToDevice));
+        // Repack the adapter's word-major 1-bit codes + float[N][3] factors into scan planes.
+        DevBuf<uint32_t> tmp_short;
+        DevBuf<float> tmp_fac;
+        tmp_short.alloc(N * (D / 32));
+        tmp_fac.alloc(N * 3);
+        CUDA_TRY(cudaMemcpy(tmp_short.p, h_short, N * (D / 32) * 4, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(tmp_fac.p, h_short_factors, N * 12, cudaMemcpyHostToDevice));
+        scan4.alloc(N * (G16 + 1));
+        repack_scan_planes(tmp_short.p, tmp_fac.p);
+        CUDA_TRY(cudaStreamSynchronize(stream));
+        loaded = true;
+    }
+
+    void repack_scan_planes(const uint32_t *d_short, const float *d_fac);
+
+    // ---------------------------------------------------------------- workspace
+    uint64_t vanguard_depth(uint64_t nprobe) const {
+        const uint64_t v = std::max<uint64_t>(vanguard, 1);
+        return std::min(v, nprobe);
+    }
+
+    void prepare_workspace(uint64_t max_q, uint64_t max_k, uint64_t max_np) {
+        if (!loaded) fail(CORA_ESTATE, "load an index before preparing workspace");
+        validate_search_shape(max_q, max_k, max_np, nlist, D);
+        if (max_k > kMaxTopk) fail(CORA_EINVAL, "topk above 4096 is not supported");
+        if (max_np > kMaxProbeFast) fail(CORA_EINVAL, "nprobe above 4096 is not supported");
+        free_workspace();
+        CUDA_TRY(cudaSetDevice(device));
+        ws_q = max_q;
+        ws_k = max_k;
+        ws_np = max_np;
+        ws_vg = vanguard_depth(max_np);
+        const uint64_t pool = queue_capacity + spill_capacity;
+        const uint64_t keep = std::max<uint64_t>(max_k, kVanguardMinKeep);
+        cap = std::max<uint64_t>(1, pool / max_q);
+        cap = std::min<uint64_t>(cap, max_np * max_cluster + ws_vg * keep);
+        cap = std::min<uint64_t>(cap, UINT32_MAX / 2);
+        raw_q.alloc(max_q * dim);
+        qr.alloc(max_q * D);
+        scal.alloc(max_q);
+        planes.alloc(max_q * 8 * W4);
+        gmat.alloc(max_q * nlist);
+        probe_ids.alloc(max_q * max_np);
+        probe_g.alloc(max_q * max_np);
+        T0.alloc(max_q);
+        T1.alloc(max_q);
+        bound.alloc(max_q * std::max<uint64_t>(ws_vg, 1));
+        cand_cnt.alloc(max_q);
+        seed_cnt.alloc(max_q);
+        cand_rec.alloc(max_q * cap);
+        cand_key.alloc(max_q * cap);
+        pair_cnt.alloc(nlist);
+        pair_off.alloc(nlist + 1);
+        pair_cur.alloc(nlist);
+        item_off.alloc(nlist);
+        pairs.alloc(max_q * max_np);
+        items.alloc(max_q * max_np);  // at most one item per pair
+        n_items.alloc(1);
+        item_counter.alloc(1);
+        err.alloc(1);
+        stats.alloc(2);
+        out_d.alloc(max_q * max_k);
+        out_i.alloc(max_q * max_k);
+        h_T0.assign(max_q, FLT_MAX);
+        CUDA_TRY(cudaMemcpy(T0.p, h_T0.data(), max_q * 4, cudaMemcpyHostToDevice));
+        ws_ready = true;
+    }
+
+    void free_workspace() noexcept {
+        ws_ready = false;
+        ws_q = ws_k = ws_np = ws_vg = cap = 0;
+        for (auto *b : {&raw_q, &qr, &gmat, &probe_g, &T0, &T1, &out_d}) b->release();
+        scal.release();
+        for (auto *b : {&planes, &cand_cnt, &seed_cnt, &pair_cnt, &pair_off, &pair_cur, &item_off,
+                        &pairs, &n_items, &out_i})
+            b->release();
+        probe_ids.release();
+        item_counter.release();
+        err.release();
+        bound.release();
+        cand_rec.release();
+        cand_key.release();
+        items.release();
+        stats.release();
+        h_T0.clear();
+    }
+
+    void require_ws() const {
+        if (!ws_ready) fail(CORA_ESTATE, "prepare workspace before searching");
+    }
+    void validate_ws(uint64_t q, uint64_t k, uint64_t np) const {
+        require_ws();
+        if (q == 0 || q > ws_q || k == 0 || k > ws_k || np == 0 || np > ws_np)
+            fail(CORA_EINVAL, "search shape exceeds the prepared workspace");
+    }
+
+    void set_vanguard(uint64_t size) {
+        if (ws_ready && vanguard_depth_for(size, ws_np) > ws_vg)
+            fail(CORA_ESTATE, "prepare workspace again before increasing vanguard size");
+        vanguard = size;
+    }
+    static uint64_t vanguard_depth_for(uint64_t v, uint64_t np) {
+        return std::min<uint64_t>(std::max<uint64_t>(v, 1), np);
+    }
+
+    void reset_buffer(const float *h_q, uint64_t nq) {
+        validate_ws(nq, 1, 1);
+        if (!h_q) fail(CORA_EINVAL, "missing queries");
+        CUDA_TRY(cudaSetDevice(device));
+        CUDA_TRY(cudaMemcpyAsync(raw_q.p, h_q, nq * dim * 4, cudaMemcpyHostToDevice, stream));
+        std::fill(h_T0.begin(), h_T0.end(), FLT_MAX);
+        CUDA_TRY(cudaMemcpyAsync(T0.p, h_T0.data(), ws_q * 4, cudaMemcpyHostToDevice, stream));
+        CUDA_TRY(cudaStreamSynchronize(stream));
+    }
+    void seed_thresholds(const float *in, uint64_t nq) {
+        validate_ws(nq, 1, 1);
+        if (!in) fail(CORA_EINVAL, "missing threshold input");
+        CUDA_TRY(cudaSetDevice(device));
+        std::copy(in, in + nq, h_T0.begin());
+        CUDA_TRY(cudaMemcpyAsync(T0.p, in, nq * 4, cudaMemcpyHostToDevice, stream));
+        CUDA_TRY(cudaStreamSynchronize(stream));
+    }
+    void capture_thresholds(float *out, uint64_t nq) const {
+        validate_ws(nq, 1, 1);
+        if (!out) fail(CORA_EINVAL, "missing threshold output");
+        CUDA_TRY(cudaMemcpy(out, T0.p, nq * 4, cudaMemcpyDeviceToHost));
+    }
+
+    // ---------------------------------------------------------------- search
+    void enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, float *d_od,
+                        uint32_t *d_oi, cudaStream_t st);
+    void finish(cudaStream_t st) {
+        int h_err = 0;
+        unsigned long long h_stats[2] = {0, 0};
+        CUDA_TRY(cudaMemcpyAsync(&h_err, err.p, 4, cudaMemcpyDeviceToHost, st));
+        CUDA_TRY(cudaMemcpyAsync(h_stats, stats.p, 16, cudaMemcpyDeviceToHost, st));
+        CUDA_TRY(cudaStreamSynchronize(st));
+        last_submitted = h_stats[0];
+        last_refined = h_stats[0];
+        if (gpu_filter_timing) CUDA_TRY(cudaEventElapsedTime(&last_filter_ms, ev_filter0, ev_filter1));
+        if (h_err & kDevCandidateOverflow)
+            fail(CORA_ERUNTIME,
+                 "HBM queue spill capacity exhausted; increase --queue-capacity or "
+                 "--queue-spill-capacity, or reduce --query-chunk.");
+        if (h_err & kDevWaitTimeout) fail(CORA_ERUNTIME, "a device-side wait timed out");
+        if (h_err) fail(CORA_ERUNTIME, "device reported an error");
+    }
+
+    void search_host(const float *h_q, uint64_t nq, uint64_t k, uint64_t np, float *h_d,
+                     uint32_t *h_i, int batch_q) {
+        validate_ws(nq, k, np);
+        if (!h_q || !h_d || !h_i || batch_q < 1 || batch_q > 6)
+            fail(CORA_EINVAL, "invalid search buffers or batch-q (expected 1..6)");
+        CUDA_TRY(cudaSetDevice(device));
+        CUDA_TRY(cudaMemcpyAsync(raw_q.p, h_q, nq * dim * 4, cudaMemcpyHostToDevice, stream));
+        enqueue_search(raw_q.p, nq, k, np, out_d.p, out_i.p, stream);
+        CUDA_TRY(cudaMemcpyAsync(h_d, out_d.p, nq * k * 4, cudaMemcpyDeviceToHost, stream));
+        CUDA_TRY(cudaMemcpyAsync(h_i, out_i.p, nq * k * 4, cudaMemcpyDeviceToHost, stream));
+        finish(stream);
+    }
+
+    void debug_copy(int what, void *out, uint64_t bytes);
+};
+
+// ------------------------------------------------------------------------------------
+// repack: adapter layout -> scan planes (one CTA per cluster)
+// ------------------------------------------------------------------------------------
+__global__ void repack_kernel(const uint32_t *__restrict__ short_data,
+                              const float *__restrict__ fac, const uint32_t *__restrict__ cl_start,
+                              const uint32_t *__restrict__ cl_size, int W, int G16,
+                              uint4 *__restrict__ scan4) {
+    const int c = blockIdx.x;
+    const uint32_t s = cl_start[c], n = cl_size[c];
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        for (int g = 0; g < G16; ++g) {
+            uint32_t w[4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+                const int word = 4 * g + t;
+                w[t] = word < W ? short_data[(size_t)s * W + (size_t)word * n + i] : 0u;
+            }
+            scan4[(size_t)(G16 + 1) * s + (size_t)g * n + i] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        const float *f = fac + (size_t)(s + i) * 3;
+        scan4[(size_t)(G16 + 1) * s + (size_t)G16 * n + i] =
+            make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), 0u);
+    }
+}
+
+void Engine::repack_scan_planes(const uint32_t *d_short, const float *d_fac) {
+    repack_kernel<<<static_cast<unsigned>(nlist), 256, 0, stream>>>(
+        d_short, d_fac, cl_start.p, cl_size.p, static_cast<int>(D / 32), G16, scan4.p);
+    CUDA_TRY(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------------------------
+// search pipeline
+// ------------------------------------------------------------------------------------
+namespace {
+template <int G16>
+size_t vanguard_smem(int sort_n) {
+    using Sh = ScanShape<G16>;
+    return 2 * Sh::kStageEntries * 16 + 8 * Sh::W4 * 4 + (size_t)sort_n * 8;
+}
+template <int G16>
+size_t main_smem() {
+    using Sh = ScanShape<G16>;
+    return 2 * Sh::kStageEntries * 16 + (size_t)kMaxPairsPerItem * 8 * Sh::W4 * 4;
+}
+
+template <int G16>
+void launch_scan(const IndexView &ix, const SearchView &sv, int van_sort_n, uint64_t n_van,
+                 const ScanItem *items, const uint32_t *n_items, const uint32_t *pairs,
+                 int *item_counter, int num_sms, cudaStream_t st, bool vanguard_phase) {
+    if (vanguard_phase) {
+        const size_t sm = vanguard_smem<G16>(van_sort_n);
+        CUDA_TRY(cudaFuncSetAttribute(vanguard_kernel<G16>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        vanguard_kernel<G16><<<static_cast<unsigned>(n_van), kScanThreads, sm, st>>>(ix, sv,
+                                                                                     van_sort_n);
+        CUDA_TRY(cudaGetLastError());
+    } else {
+        const size_t sm = main_smem<G16>();
+        CUDA_TRY(cudaFuncSetAttribute(scan_main_kernel<G16>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        int per_sm = 0;
+        CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_main_kernel<G16>,
+                                                               kScanThreads, sm));
+        const int grid = std::max(1, per_sm) * num_sms;
+        scan_main_kernel<G16><<<grid, kScanThreads, sm, st>>>(ix, sv, items, n_items, pairs,
+                                                             item_counter);
+        CUDA_TRY(cudaGetLastError());
+    }
+}
+
+void dispatch_scan(int G16, const IndexView &ix, const SearchView &sv, int van_sort_n,
+                   uint64_t n_van, const ScanItem *items, const uint32_t *n_items,
+                   const uint32_t *pairs, int *item_counter, int num_sms, cudaStream_t st,
+                   bool vanguard_phase) {
+#define CORA_SCAN_CASE(G) \
+    case G: launch_scan<G>(ix, sv, van_sort_n, n_van, items, n_items, pairs, item_counter, num_sms, st, vanguard_phase); break;
+    switch (G16) {
+        CORA_SCAN_CASE(1)
+        CORA_SCAN_CASE(2)
+        CORA_SCAN_CASE(3)
+        CORA_SCAN_CASE(4)
+        CORA_SCAN_CASE(5)
+        CORA_SCAN_CASE(6)
+        CORA_SCAN_CASE(7)
+        CORA_SCAN_CASE(8)
+        default: fail(CORA_EINVAL, "unsupported padded dimension");
+    }
+#undef CORA_SCAN_CASE
+}
+}  // namespace
+
+void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, float *d_od,
+                            uint32_t *d_oi, cudaStream_t st) {
+    last_stream = st;
+    last_nq = nq;
+    last_np = np;
+    const int inq = static_cast<int>(nq), inp = static_cast<int>(np), ik = static_cast<int>(k);
+    const uint64_t veff = vanguard_depth(np);
+    const uint64_t keep = std::max<uint64_t>(k, kVanguardMinKeep);
+
+    CUDA_TRY(cudaMemsetAsync(err.p, 0, 4, st));
+    CUDA_TRY(cudaMemsetAsync(stats.p, 0, 16, st));
+    CUDA_TRY(cudaMemsetAsync(cand_cnt.p, 0, nq * 4, st));
+
+    // 1. rotation + query factors + bit-planes
+    {
+        const size_t sm = (size_t)kRotQueries * (dim + D) * 4;
+        CUDA_TRY(cudaFuncSetAttribute(rotate_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)sm));
+        const float c_b = -static_cast<float>((1u << (ex_bits + 1)) - 1u) / 2.0f;
+        rotate_prep_kernel<<<static_cast<unsigned>((nq + kRotQueries - 1) / kRotQueries), 256, sm, st>>>(
+            d_q, inq, static_cast<int>(dim), static_cast<int>(D), W4, rotator.p, c_b, qr.p, scal.p,
+            planes.p);
+        CUDA_TRY(cudaGetLastError());
+    }
+    // 2. coarse distances + top-nprobe
+    {
+        dim3 grid(static_cast<unsigned>((nlist + kDistTile - 1) / kDistTile),
+                  static_cast<unsigned>((nq + kDistTile - 1) / kDistTile));
+        centroid_dist_kernel<<<grid, 256, 0, st>>>(qr.p, inq, centroids.p, static_cast<int>(nlist),
+                                                   static_cast<int>(D), gmat.p);
+        CUDA_TRY(cudaGetLastError());
+        const int sort_n = next_pow2(inp + kProbeTile);
+        const size_t sm = (size_t)sort_n * 8;
+        CUDA_TRY(cudaFuncSetAttribute(select_probes_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        select_probes_kernel<<<inq, 256, sm, st>>>(gmat.p, static_cast<int>(nlist), inp, sort_n,
+                                                   probe_ids.p, probe_g.p);
+        CUDA_TRY(cudaGetLastError());
+    }
+    IndexView ix{scan4.p, cl_start.p, cl_size.p, long_codes.p, ex_factors.p, ids.p,
+                 static_cast<int>(nlist), static_cast<int>(D), G16, LC};
+    SearchView sv{inq, ik, inp, static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
+                  scal.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, T1.p, bound.p, cand_cnt.p,
+                  seed_cnt.p, cand_rec.p, cand_key.p, err.p};
+    const uint8_t *own = owned.n ? owned.p : nullptr;
+    // 3. per-cluster grouping of every (query, probe) pair
+    {
+        const size_t total = nq * np;
+        const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
+        CUDA_TRY(cudaMemsetAsync(pair_cnt.p, 0, nlist * 4, st));
+        CUDA_TRY(cudaMemsetAsync(pair_cur.p, 0, nlist * 4, st));
+        CUDA_TRY(cudaMemsetAsync(item_counter.p, 0, 4, st));
+        // cross-query reuse groups up to kMaxPairsPerItem queries per cluster read
+        const int ppi = cross_query_reuse ? kMaxPairsPerItem : 1;
+        count_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, 0, own, pair_cnt.p);
+        scan_pairs_kernel<<<1, 1024, 0, st>>>(pair_cnt.p, static_cast<int>(nlist), ppi,
+                                               pair_off.p, item_off.p, n_items.p);
+        scatter_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, 0, own, pair_off.p,
+                                                     pair_cur.p, pairs.p);
+        emit_items_kernel<<<static_cast<unsigned>((nlist + 255) / 256), 256, 0, st>>>(
+            pair_cnt.p, pair_off.p, item_off.p, static_cast<int>(nlist), ppi, items.p);
+        CUDA_TRY(cudaGetLastError());
+    }
+    if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter0, st));
+    // 4. vanguard seeds -> refine -> T1
+    const int van_sort_n = next_pow2(static_cast<int>(keep) + (G16 <= 2 ? 512 : 256));
+    dispatch_scan(G16, ix, sv, van_sort_n, nq * veff, items.p, n_items.p, pairs.p, item_counter.p,
+                  num_sms, st, true);
+    refine_kernel<<<inq, kRefineThreads, 0, st>>>(ix, sv, 0);
+    CUDA_TRY(cudaGetLastError());
+    const int merge_sort_n = next_pow2(ik + kMergeTile);
+    CUDA_TRY(cudaFuncSetAttribute(threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  merge_sort_n * 8));
+    threshold_kernel<<<inq, 256, (size_t)merge_sort_n * 8, st>>>(sv, merge_sort_n);
+    CUDA_TRY(cudaGetLastError());
+    // 5. main scan against T1, then refine the new candidates
+    dispatch_scan(G16, ix, sv, van_sort_n, 0, items.p, n_items.p, pairs.p, item_counter.p, num_sms,
+                  st, false);
+    if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));
+    refine_kernel<<<inq, kRefineThreads, 0, st>>>(ix, sv, 1);
+    CUDA_TRY(cudaGetLastError());
+    // 6. final top-k
+    CUDA_TRY(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  merge_sort_n * 8));
+    merge_kernel<<<inq, 256, (size_t)merge_sort_n * 8, st>>>(sv, merge_sort_n, d_od, d_oi,
+                                                             stats.p);
+    CUDA_TRY(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------------------------
+// diagnostics
+// ------------------------------------------------------------------------------------
+void Engine::debug_copy(int what, void *out, uint64_t bytes) {
+    require_ws();
+    CUDA_TRY(cudaSetDevice(device));
+    CUDA_TRY(cudaStreamSynchronize(last_stream));
+    const uint64_t nq = last_nq, np = last_np;
+    auto copy = [&](const void *src, uint64_t want) {
+        if (bytes != want) fail(CORA_EINVAL, "debug_copy: byte count does not match the array");
+        CUDA_TRY(cudaMemcpy(out, src, want, cudaMemcpyDeviceToHost));
+    };
+    switch (what) {
+        case 0: copy(qr.p, nq * D * 4); break;
+        case 1: copy(probe_ids.p, nq * np * 4); break;
+        case 2: copy(probe_g.p, nq * np * 4); break;
+        case 3: copy(cand_cnt.p, nq * 4); break;
+        case 4: copy(T1.p, nq * 4); break;
+        case 5: copy(planes.p, nq * 8 * W4 * 4); break;
+        case 6: copy(scal.p, nq * 16); break;
+        case 7: {
+            if (bytes != nq * cap * 4) fail(CORA_EINVAL, "debug_copy: byte count does not match");
+            std::vector<uint64_t> rec(nq * cap);
+            std::vector<uint32_t> cnt(nq);
+            CUDA_TRY(cudaMemcpy(rec.data(), cand_rec.p, nq * cap * 8, cudaMemcpyDeviceToHost));
+            CUDA_TRY(cudaMemcpy(cnt.data(), cand_cnt.p, nq * 4, cudaMemcpyDeviceToHost));
+            auto *o = static_cast<uint32_t *>(out);
+            for (uint64_t q = 0; q < nq; ++q) {
+                const uint64_t n = std::min<uint64_t>(cnt[q], cap);
+                for (uint64_t i = 0; i < cap; ++i)
+                    o[q * cap + i] = i < n ? static_cast<uint32_t>(rec[q * cap + i] & 0xFFFFFFFFu)
+                                           : 0xFFFFFFFFu;
+                std::sort(o + q * cap, o + q * cap + n);
+            }
+            break;
+        }
+        default: fail(CORA_EINVAL, "debug_copy: unknown array");
+    }
+}
+
+// ------------------------------------------------------------------------------------
+// index file -> adapter arrays (ivf.hpp:447-539 + search_data.cpp:45-123)
+// ------------------------------------------------------------------------------------
+namespace {
+struct FileIndex {
+    uint64_t num = 0, dim = 0, nlist = 0, ex_bits = 0, D = 0;
+    std::vector<uint64_t> sizes;
+    std::vector<float> rotator, centroids, short_factors, ex_factors;
+    std::vector<uint32_t> short_data, ids;
+    std::vector<uint8_t> long_codes;
+};
+
+FileIndex read_index_file(const char *path) {
+    std::ifstream in(path, std::ios::binary);
+    if (!in) fail(CORA_EINVAL, std::string("Cannot open IVF index: ") + path);
+    FileIndex f;
+    uint64_t hdr[4];
+    uint8_t types[2];
+    in.read(reinterpret_cast<char *>(hdr), sizeof(hdr));
+    in.read(reinterpret_cast<char *>(types), 2);
+    if (!in) fail(CORA_EINVAL, "truncated IVF index header");
+    f.num = hdr[0];
+    f.dim = hdr[1];
+    f.nlist = hdr[2];
+    f.ex_bits = hdr[3];
+    if (types[0] != 0) fail(CORA_EINVAL, "only matrix-rotator indexes are supported");
+    if (!f.num || !f.dim || !f.nlist || f.ex_bits > 8) fail(CORA_EINVAL, "invalid IVF index header");
+    f.D = (f.dim + 63) / 64 * 64;
+    const uint64_t D = f.D, W = D / 32;
+    f.sizes.resize(f.nlist);
+    in.read(reinterpret_cast<char *>(f.sizes.data()), 8 * f.nlist);
+    uint64_t total = 0, blocks = 0;
+    for (auto s : f.sizes) {
+        total += s;
+        blocks += (s + 31) / 32;
+    }
+    if (!in || total != f.num) fail(CORA_EINVAL, "The sum of cluster num != total number of points");
+    f.rotator.resize(f.dim * D);
+    in.read(reinterpret_cast<char *>(f.rotator.data()), 4 * f.dim * D);
+    const std::streampos begin = in.tellg();
+    in.seekg(0, std::ios::end);
+    const uint64_t remaining = static_cast<uint64_t>(in.tellg() - begin);
+    in.seekg(begin);
+    const uint64_t rec = D * 4 + 32 * 12;
+    const uint64_t ex_stride = f.ex_bits ? D * f.ex_bits / 8 + 8 : 0;
+    const uint64_t payload = blocks * rec + f.num * ex_stride + 4 * f.num;
+    if (remaining == payload)
+        fail(CORA_EINVAL, "HNSW-sidecar centroid storage (nlist >= 20000 indexes) is not supported");
+    if (remaining != payload + 4 * D * f.nlist)
+        fail(CORA_EINVAL, "IVF index size does not match a supported centroid layout");
+    f.centroids.resize(f.nlist * D);
+    in.read(reinterpret_cast<char *>(f.centroids.data()), 4 * D * f.nlist);
+    std::vector<uint8_t> batch(blocks * rec);
+    in.read(reinterpret_cast<char *>(batch.data()), batch.size());
+    std::vector<uint8_t> ex(f.num * ex_stride);
+    in.read(reinterpret_cast<char *>(ex.data()), ex.size());
+    f.ids.resize(f.num);
+    in.read(reinterpret_cast<char *>(f.ids.data()), 4 * f.num);
+    if (!in) fail(CORA_EINVAL, "Failed to read IVF index payload");
+
+    // FastScan batches of 32 vectors -> word-major 1-bit codes per cluster. In a batch,
+    // dims 8i..8i+7 occupy 32 bytes; dims with (dim % 8) < 4 sit in the first 16, the
+    // others in the last 16; vector v's nibble is in byte inv_perm[v % 16], low nibble for
+    // v < 16, high nibble otherwise; its bit (3 - dim % 4) holds the sign bit.
+    static const int perm[16] = {0, 8, 1, 9, 2, 10, 3, 11, 4, 12, 5, 13, 6, 14, 7, 15};
+    int inv_perm[16];
+    for (int j = 0; j < 16; ++j) inv_perm[perm[j]] = j;
+    f.short_data.assign(f.num * W, 0u);
+    f.short_factors.assign(f.num * 3, 0.0f);
+    std::vector<uint64_t> cstart(f.nlist + 1, 0), bstart(f.nlist + 1, 0);
+    for (uint64_t c = 0; c < f.nlist; ++c) {
+        cstart[c + 1] = cstart[c] + f.sizes[c];
+        bstart[c + 1] = bstart[c] + (f.sizes[c] + 31) / 32;
+    }
+#pragma omp parallel for schedule(dynamic, 16)
+    for (int64_t c = 0; c < static_cast<int64_t>(f.nlist); ++c) {
+        const uint64_t n = f.sizes[c], s = cstart[c];
+        for (uint64_t i = 0; i < n; i += 32) {
+            const uint8_t *blk = batch.data() + (bstart[c] + i / 32) * rec;
+            const float *fa = reinterpret_cast<const float *>(blk + D * 4);
+            const uint64_t len = std::min<uint64_t>(32, n - i);
+            for (uint64_t v = 0; v < len; ++v) {
+                for (uint64_t w = 0; w < W; ++w) {
+                    uint32_t word = 0;
+                    for (int b = 0; b < 32; ++b) {
+                        const uint64_t d = w * 32 + b;
+                        const uint8_t byte =
+                            blk[(d / 8) * 32 + ((d % 8) < 4 ? 0 : 16) + inv_perm[v % 16]];
+                        const uint8_t nib = v < 16 ? (byte & 0x0F) : (byte >> 4);
+                        word |= static_cast<uint32_t>((nib >> (3 - (d % 4))) & 1u) << (31 - b);
+                    }
+                    f.short_data[s * W + w * n + i + v] = word;
+                }
+                for (int t = 0; t < 3; ++t) f.short_factors[(s + i + v) * 3 + t] = fa[t * 32 + v];
+            }
+        }
+    }
+    const uint64_t lc = D * f.ex_bits / 8;
+    f.long_codes.resize(f.num * lc);
+    f.ex_factors.resize(f.num * 2);
+    for (uint64_t i = 0; i < f.num; ++i) {
+        std::memcpy(f.long_codes.data() + i * lc, ex.data() + i * ex_stride, lc);
+        std::memcpy(f.ex_factors.data() + i * 2, ex.data() + i * ex_stride + lc, 8);
+    }
+    return f;
+}
+}  // namespace
+
+}  // namespace cora
+
+// ======================================================================================
+// C ABI
+// ======================================================================================
+using cora::Engine;
+
+struct cora_engine {
+    std::unique_ptr<Engine> e;
+};
+
+namespace {
+template <typename F>
+int guarded(F &&f) {
+    try {
+        f();
+        return CORA_OK;
+    } catch (const cora::Error &e) {
+        cora::g_last_error = e.what();
+        return e.code;
+    } catch (const std::bad_alloc &e) {
+        cora::g_last_error = e.what();
+        return CORA_ENOMEM;
+    } catch (const std::exception &e) {
+        cora::g_last_error = e.what();
+        return CORA_ERUNTIME;
+    }
+}
+Engine &eng(cora_engine *h) {
+    if (!h || !h->e) cora::fail(CORA_EINVAL, "null engine");
+    return *h->e;
+}
+const Engine &eng(const cora_engine *h) {
+    if (!h || !h->e) cora::fail(CORA_EINVAL, "null engine");
+    return *h->e;
+}
+}  // namespace
+
+extern "C" {
+
+const char *cora_last_error(void) { return cora::g_last_error.c_str(); }
+
+int cora_create(cora_engine **out, int device) {
+    return guarded([&] {
+        if (!out) cora::fail(CORA_EINVAL, "null output handle");
+        auto h = std::make_unique<cora_engine>();
+        h->e = std::make_unique<Engine>(device);
+        *out = h.release();
+    });
+}
+
+void cora_destroy(cora_engine *engine) { delete engine; }
+
+int cora_load_from_raw_pointers(cora_engine *engine, uint64_t num_vecs, uint64_t d, uint64_t p_d,
+                                uint64_t n_centroids, uint64_t ex_b, const float *h_centroids,
+                                const float *h_rotator, const uint32_t *h_short_data,
+                                const float *h_short_factors, const uint8_t *h_long_code,
+                                const float *h_ex_factors, const uint32_t *h_ids,
+                                const uint64_t *h_cluster_sizes) {
+    return guarded([&] {
+        eng(engine).load(num_vecs, d, p_d, n_centroids, ex_b, h_centroids, h_rotator, h_short_data,
+                         h_short_factors, h_long_code, h_ex_factors, h_ids, h_cluster_sizes);
+    });
+}
+
+int cora_load_index_file(cora_engine *engine, const char *path) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        if (e.loaded) cora::fail(CORA_ESTATE, "index already loaded");
+        if (!path) cora::fail(CORA_EINVAL, "null index path");
+        cora::FileIndex f = cora::read_index_file(path);
+        e.load(f.num, f.dim, f.D, f.nlist, f.ex_bits, f.centroids.data(), f.rotator.data(),
+               f.short_data.data(), f.short_factors.data(), f.long_codes.data(), f.ex_factors.data(),
+               f.ids.data(), f.sizes.data());
+    });
+}
+
+int cora_index_info(const cora_engine *engine, uint64_t *out6) {
+    return guarded([&] {
+        const Engine &e = eng(engine);
+        if (!e.loaded) cora::fail(CORA_ESTATE, "no index loaded");
+        if (!out6) cora::fail(CORA_EINVAL, "null output");
+        const uint64_t v[6] = {e.N, e.dim, e.D, e.nlist, e.ex_bits, e.max_cluster};
+        std::memcpy(out6, v, sizeof(v));
+    });
+}
+
+int cora_prepare_workspace(cora_engine *engine, uint64_t max_queries, uint64_t max_topk,
+                           uint64_t max_nprobe) {
+    return guarded([&] { eng(engine).prepare_workspace(max_queries, max_topk, max_nprobe); });
+}
+
+void cora_free_workspace(cora_engine *engine) {
+    if (engine && engine->e) engine->e->free_workspace();
+}
+
+int cora_reset_buffer(cora_engine *engine, const float *h_queries, uint64_t num_queries) {
+    return guarded([&] { eng(engine).reset_buffer(h_queries, num_queries); });
+}
+
+int cora_search(cora_engine *engine, const float *h_queries, uint64_t num_queries, uint64_t topk,
+                uint64_t nprobe, float *h_final_dists, uint32_t *h_final_pids, int batch_q) {
+    return guarded([&] {
+        eng(engine).search_host(h_queries, num_queries, topk, nprobe, h_final_dists, h_final_pids,
+                                batch_q);
+    });
+}
+
+int cora_search_device(cora_engine *engine, const float *d_queries, uint64_t num_queries,
+                       uint64_t topk, uint64_t nprobe, float *d_final_dists,
+                       uint32_t *d_final_pids, void *stream) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        e.validate_ws(num_queries, topk, nprobe);
+        if (!d_queries || !d_final_dists || !d_final_pids)
+            cora::fail(CORA_EINVAL, "invalid device search buffers");
+        CUDA_TRY(cudaSetDevice(e.device));
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e.stream;
+        e.enqueue_search(d_queries, num_queries, topk, nprobe, d_final_dists, d_final_pids, st);
+    });
+}
+
+int cora_check_device(cora_engine *engine) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        e.require_ws();
+        CUDA_TRY(cudaSetDevice(e.device));
+        e.finish(e.last_stream);
+    });
+}
+
+int cora_seed_thresholds(cora_engine *engine, const float *h_in, uint64_t nq) {
+    return guarded([&] { eng(engine).seed_thresholds(h_in, nq); });
+}
+
+int cora_capture_thresholds(const cora_engine *engine, float *h_out, uint64_t nq) {
+    return guarded([&] { eng(engine).capture_thresholds(h_out, nq); });
+}
+
+int cora_set_vanguard_size(cora_engine *engine, uint64_t size) {
+    return guarded([&] { eng(engine).set_vanguard(size); });
+}
+uint64_t cora_get_vanguard_size(const cora_engine *engine) {
+    return engine && engine->e ? engine->e->vanguard : 0;
+}
+
+// hybrid.cu:166-185
+int cora_set_queue_capacity(cora_engine *engine, uint64_t capacity) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        if (capacity == 0 || (capacity & (capacity - 1)) != 0 || capacity > (SIZE_MAX >> 5))
+            cora::fail(CORA_EINVAL, "queue-capacity must be a positive power of two");
+        if (e.ws_ready) cora::fail(CORA_ESTATE, "set queue capacity before prepare_workspace");
+        e.queue_capacity = capacity;
+    });
+}
+int cora_set_queue_spill_capacity(cora_engine *engine, uint64_t capacity) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        if (capacity > (SIZE_MAX >> 5)) cora::fail(CORA_EINVAL, "queue-spill-capacity is too large");
+        if (e.ws_ready) cora::fail(CORA_ESTATE, "set spill capacity before prepare_workspace");
+        e.spill_capacity = capacity;
+    });
+}
+uint64_t cora_get_queue_capacity(const cora_engine *engine) {
+    return engine && engine->e ? engine->e->queue_capacity : 0;
+}
+
+void cora_set_profiling(cora_engine *engine, int enabled) {
+    if (engine && engine->e) engine->e->profiling = enabled != 0;
+}
+void cora_set_candidate_stats(cora_engine *engine, int enabled) {
+    if (engine && engine->e) engine->e->candidate_stats = enabled != 0;
+}
+void cora_set_gpu_filter_timing(cora_engine *engine, int enabled) {
+    if (engine && engine->e) engine->e->gpu_filter_timing = enabled != 0;
+}
+void cora_set_cross_query_reuse(cora_engine *engine, int enabled) {
+    if (engine && engine->e) engine->e->cross_query_reuse = enabled != 0;
+}
+void cora_set_cpu_secondary_filter(cora_engine *engine, int enabled) {
+    if (engine && engine->e) engine->e->cpu_secondary_filter = enabled != 0;
+}
+void cora_set_ip_kernel_type(cora_engine *engine, int kernel_type) {
+    if (engine && engine->e) engine->e->ip_kernel_type = kernel_type;
+}
+int cora_get_ip_kernel_type(const cora_engine *engine) {
+    return engine && engine->e ? engine->e->ip_kernel_type : 0;
+}
+
+uint64_t cora_get_last_submitted_count(const cora_engine *engine) {
+    return engine && engine->e ? engine->e->last_submitted : 0;
+}
+uint64_t cora_get_last_refined_count(const cora_engine *engine) {
+    return engine && engine->e ? engine->e->last_refined : 0;
+}
+uint64_t cora_get_last_spilled_count(const cora_engine *) { return 0; }
+float cora_get_last_gpu_filter_ms(const cora_engine *engine) {
+    return engine && engine->e ? engine->e->last_filter_ms : 0.0f;
+}
+
+int cora_debug_copy(cora_engine *engine, int what, void *h_out, uint64_t bytes) {
+    return guarded([&] {
+        if (!h_out) cora::fail(CORA_EINVAL, "null output");
+        eng(engine).debug_copy(what, h_out, bytes);
+    });
+}
+
+uint64_t cora_get_candidate_capacity(const cora_engine *engine) {
+    return engine && engine->e ? engine->e->cap : 0;
+}
+
+}  // extern "C"

@@ -1,0 +1,396 @@
+// 1-bit RaBitQ estimator scan: per-cluster query grouping, vanguard seeding and the main
+// pruned scan.
+//
+// Device scan layout ("scan planes"): for cluster c with start s_c (its first vector's
+// position in the reference's cluster order) and size n_c, uint4 entry
+//   scan4[(G16 + 1) * s_c + g * n_c + i]
+// holds, for g < G16, 1-bit code words 4g..4g+3 of vector i (word w covers dims 32w..32w+31
+// with dim 32w+b at bit 31-b, as src/index/search_data.cpp:71), and for g == G16 the
+// factors {f_add, f_rescale, f_error, 0}. Each plane of a cluster is contiguous, so a tile
+// of TV vectors is G16 + 1 TMA bulk copies of TV * 16 bytes.
+//
+// Estimator (reference src/search/filter_kernels.cuh:79-114, 693-696):
+//   ip_int = sum_{j<7} popc(x & plane_j) << j  -  popc(x & plane_7) << 7      (exact)
+//   ip1    = width * ip_int
+//   low    = (f_add + g) + f_rescale * (ip1 + k1) - f_error * sqrt(max(g, 0))
+#pragma once
+#include "common.cuh"
+#include "kernels_query.cuh"
+
+namespace cora {
+
+constexpr int kScanThreads = 256;
+constexpr int kMaxPairsPerItem = 32;
+
+template <int G16>
+struct ScanShape {
+    static constexpr int TV = G16 <= 2 ? 512 : 256;   // vectors per staged tile
+    static constexpr int W4 = 4 * G16;                 // 32-bit code words per vector
+    static constexpr int kStageEntries = (G16 + 1) * TV;
+};
+
+struct ScanItem {
+    uint32_t cluster, pair_begin, pair_count, pad;
+};
+
+struct IndexView {
+    const uint4 *scan4;          // scan planes
+    const uint32_t *cl_start;    // nlist
+    const uint32_t *cl_size;     // nlist
+    const uint8_t *long_codes;   // N x LC
+    const float2 *ex_factors;    // N
+    const uint32_t *ids;         // N
+    int nlist, D, G16, LC;
+};
+
+struct SearchView {
+    int nq, k, nprobe, veff, keep, cap;
+    const QueryScalars *scal;    // nq
+    const uint32_t *planes;      // nq x 8 x W4
+    const float *qr;             // nq x D
+    const int *probe_ids;        // nq x nprobe
+    const float *probe_g;        // nq x nprobe
+    float *T0;                   // nq (merge_kernel stores the k-th distance back)
+    float *T1;                   // nq
+    uint64_t *bound;             // nq x veff
+    uint32_t *cand_cnt;          // nq
+    uint32_t *seed_cnt;          // nq
+    uint64_t *cand_rec;          // nq x cap : gid | (probe rank << 32)
+    uint64_t *cand_key;          // nq x cap : ord(ex) << 32 | id
+    int *err;
+};
+
+// ---- per-cluster query grouping (CSR of (query, probe rank) pairs by cluster) --------
+// Pairs with probe rank in [r_lo, nprobe) whose cluster is owned by this shard
+// (owner == nullptr: all) are grouped; a pair is packed as (q << 16) | r.
+__global__ void count_pairs_kernel(const int *__restrict__ probe_ids, int nq, int nprobe,
+                                   int r_lo, const uint8_t *__restrict__ owned,
+                                   uint32_t *__restrict__ cnt) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)nq * nprobe) return;
+    const int r = static_cast<int>(i % nprobe);
+    if (r < r_lo) return;
+    const int c = probe_ids[i];
+    if (owned && !owned[c]) return;
+    atomicAdd(cnt + c, 1u);
+}
+
+// Single-CTA exclusive scan of pair counts into offsets and of per-cluster item counts
+// (ceil(count / ppi), ppi = pairs per item <= kMaxPairsPerItem) into item offsets; the item
+// total lands in *n_items.
+__global__ void __launch_bounds__(1024) scan_pairs_kernel(const uint32_t *__restrict__ cnt,
+                                                          int nlist, int ppi,
+                                                          uint32_t *__restrict__ off,
+                                                          uint32_t *__restrict__ item_off,
+                                                          uint32_t *__restrict__ n_items) {
+    __shared__ uint32_t s_pairs[1024], s_items[1024];
+    const int t = threadIdx.x;
+    const int per = (nlist + 1023) / 1024;
+    const int b = t * per, e = min(nlist, b + per);
+    uint32_t sp = 0, si = 0;
+    for (int c = b; c < e; ++c) {
+        sp += cnt[c];
+        si += (cnt[c] + ppi - 1) / ppi;
+    }
+    s_pairs[t] = sp;
+    s_items[t] = si;
+    __syncthreads();
+    for (int d = 1; d < 1024; d <<= 1) {
+        const uint32_t vp = t >= d ? s_pairs[t - d] : 0, vi = t >= d ? s_items[t - d] : 0;
+        __syncthreads();
+        s_pairs[t] += vp;
+        s_items[t] += vi;
+        __syncthreads();
+    }
+    uint32_t rp = s_pairs[t] - sp, ri = s_items[t] - si;
+    for (int c = b; c < e; ++c) {
+        off[c] = rp;
+        item_off[c] = ri;
+        rp += cnt[c];
+        ri += (cnt[c] + ppi - 1) / ppi;
+    }
+    if (t == 1023) {
+        off[nlist] = s_pairs[1023];
+        *n_items = s_items[1023];
+    }
+}
+
+__global__ void scatter_pairs_kernel(const int *__restrict__ probe_ids, int nq, int nprobe,
+                                     int r_lo, const uint8_t *__restrict__ owned,
+                                     const uint32_t *__restrict__ off,
+                                     uint32_t *__restrict__ cursor,
+                                     uint32_t *__restrict__ pairs) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)nq * nprobe) return;
+    const int r = static_cast<int>(i % nprobe);
+    if (r < r_lo) return;
+    const int c = probe_ids[i];
+    if (owned && !owned[c]) return;
+    const int q = static_cast<int>(i / nprobe);
+    const uint32_t pos = atomicAdd(cursor + c, 1u);
+    pairs[off[c] + pos] = (static_cast<uint32_t>(q) << 16) | static_cast<uint32_t>(r);
+}
+
+__global__ void emit_items_kernel(const uint32_t *__restrict__ cnt,
+                                  const uint32_t *__restrict__ off,
+                                  const uint32_t *__restrict__ item_off, int nlist, int ppi,
+                                  ScanItem *__restrict__ items) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= nlist) return;
+    const uint32_t n = cnt[c];
+    const uint32_t base = item_off[c];
+    const uint32_t up = static_cast<uint32_t>(ppi);
+    for (uint32_t t = 0; t * up < n; ++t) {
+        ScanItem it;
+        it.cluster = static_cast<uint32_t>(c);
+        it.pair_begin = off[c] + t * up;
+        it.pair_count = min(up, n - t * up);
+        it.pad = 0;
+        items[base + t] = it;
+    }
+}
+
+// ---- shared pieces ------------------------------------------------------------------
+template <int G16>
+__device__ __forceinline__ void issue_tile(uint4 *stage_buf, uint64_t *bar, const uint4 *scan4,
+                                           size_t cbase, int n, int v0, int tv) {
+    const uint32_t bytes = static_cast<uint32_t>(tv) * 16u;
+    mbar_arrive_expect_tx(bar, bytes * (G16 + 1));
+#pragma unroll
+    for (int g = 0; g <= G16; ++g)
+        bulk_g2s(stage_buf + g * ScanShape<G16>::TV, scan4 + cbase + (size_t)g * n + v0, bytes,
+                 bar);
+}
+
+template <int G16>
+__device__ __forceinline__ int ip_int_from_planes(const uint4 (&code)[G16],
+                                                  const uint32_t *__restrict__ P) {
+    constexpr int W4 = ScanShape<G16>::W4;
+    int acc[8];
+#pragma unroll
+    for (int p = 0; p < 8; ++p) acc[p] = 0;
+#pragma unroll
+    for (int g = 0; g < G16; ++g) {
+#pragma unroll
+        for (int p = 0; p < 8; ++p) {
+            const uint4 qw = *reinterpret_cast<const uint4 *>(P + p * W4 + 4 * g);
+            acc[p] += __popc(code[g].x & qw.x) + __popc(code[g].y & qw.y) +
+                      __popc(code[g].z & qw.z) + __popc(code[g].w & qw.w);
+        }
+    }
+    int ip = -(acc[7] << 7);
+#pragma unroll
+    for (int p = 0; p < 7; ++p) ip += acc[p] << p;
+    return ip;
+}
+
+__device__ __forceinline__ float lower_bound_dist(float4 f, float ip1, float g, float k1,
+                                                  float gerr) {
+    const float a = __fadd_rn(f.x, g);
+    const float b = __fmul_rn(f.y, __fadd_rn(ip1, k1));
+    const float e = __fmul_rn(f.z, gerr);
+    return __fsub_rn(__fadd_rn(a, b), e);
+}
+
+// ---- vanguard seeding: one CTA per (query, probe rank < veff) ------------------------
+// Keeps the best `keep` (low, gid) keys among low < T0 of the probe's cluster, writes
+// them as seed candidates and records the seed boundary key for the main scan
+// (kKeyMax when every candidate of the pair became a seed).
+template <int G16>
+__global__ void __launch_bounds__(kScanThreads) vanguard_kernel(IndexView ix, SearchView sv,
+                                                                int sort_n) {
+    using Sh = ScanShape<G16>;
+    constexpr int TV = Sh::TV, W4 = Sh::W4;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint4 *stage = reinterpret_cast<uint4 *>(smem_raw);                      // [2][(G16+1)TV]
+    uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + 2 * Sh::kStageEntries);
+    uint64_t *s_keys = reinterpret_cast<uint64_t *>(s_planes + 8 * W4);     // sort_n
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ int n_staged, n_total, s_abort;
+    __shared__ uint64_t thresh;
+    __shared__ uint32_t s_base;
+
+    const int pi = blockIdx.x;
+    const int q = pi / sv.veff, r = pi % sv.veff;
+    const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
+    const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
+    const uint32_t s = ix.cl_start[c];
+    const int n = static_cast<int>(ix.cl_size[c]);
+    const QueryScalars qs = sv.scal[q];
+    const float T0 = sv.T0[q];
+    const float gerr = __fsqrt_rn(fmaxf(g, 0.0f));
+    const size_t cbase = (size_t)(G16 + 1) * s;
+
+    for (int i = threadIdx.x; i < 8 * W4; i += blockDim.x)
+        s_planes[i] = sv.planes[(size_t)q * 8 * W4 + i];
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_barrier_init();
+        n_total = 0;
+        s_abort = 0;
+    }
+    BlockTopK tk{s_keys, sv.keep, TV, sort_n, &n_staged, &thresh};
+    tk.init(kKeyMax);  // also synchronises the barrier init and the planes
+    const int ntiles = (n + TV - 1) / TV;
+    uint32_t phase[2] = {0, 0};
+    if (threadIdx.x == 0 && ntiles > 0) issue_tile<G16>(stage, &bars[0], ix.scan4, cbase, n, 0, min(TV, n));
+    for (int t = 0; t < ntiles; ++t) {
+        const int b = t & 1;
+        const int v0 = t * TV, tv = min(TV, n - v0);
+        if (!mbar_wait_bounded(&bars[b], phase[b], sv.err)) s_abort = 1;
+        phase[b] ^= 1;
+        __syncthreads();
+        if (s_abort) return;
+        if (threadIdx.x == 0 && t + 1 < ntiles)
+            issue_tile<G16>(stage + (b ^ 1) * Sh::kStageEntries, &bars[b ^ 1], ix.scan4, cbase, n,
+                            v0 + TV, min(TV, n - v0 - TV));
+        const uint4 *sb = stage + b * Sh::kStageEntries;
+        for (int i = threadIdx.x; i < tv; i += blockDim.x) {
+            uint4 code[G16];
+#pragma unroll
+            for (int gg = 0; gg < G16; ++gg) code[gg] = sb[gg * TV + i];
+            const uint4 fr = sb[G16 * TV + i];
+            const float4 f = make_float4(__uint_as_float(fr.x), __uint_as_float(fr.y),
+                                         __uint_as_float(fr.z), 0.0f);
+            const int ip = ip_int_from_planes<G16>(code, s_planes);
+            const float ip1 = __fadd_rn(__fmul_rn(qs.width, (float)ip), 0.0f);
+            const float low = lower_bound_dist(f, ip1, g, qs.k1, gerr);
+            if (low < T0) {
+                atomicAdd(&n_total, 1);
+                tk.offer(make_key(low, s + v0 + i));
+            }
+        }
+        tk.flush(kKeyMax);  // includes the barrier that frees stage buffer b
+    }
+    const int total = n_total;
+    const int nkeep = min(total, sv.keep);
+    if (threadIdx.x == 0) {
+        s_base = nkeep ? atomicAdd(sv.cand_cnt + q, static_cast<uint32_t>(nkeep)) : 0u;
+        sv.bound[(size_t)q * sv.veff + r] = total <= sv.keep ? kKeyMax : s_keys[sv.keep - 1];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nkeep; i += blockDim.x) {
+        const uint32_t slot = s_base + i;
+        const uint32_t gid = static_cast<uint32_t>(s_keys[i] & 0xFFFFFFFFu);
+        if (slot < static_cast<uint32_t>(sv.cap))
+            sv.cand_rec[(size_t)q * sv.cap + slot] = gid | (static_cast<uint64_t>(r) << 32);
+        else
+            atomicOr(sv.err, kDevCandidateOverflow);
+    }
+}
+
+// ---- main scan: persistent CTAs over (cluster, <= 32 pairs) items --------------------
+template <int G16>
+__global__ void __launch_bounds__(kScanThreads, 2) scan_main_kernel(
+    IndexView ix, SearchView sv, const ScanItem *__restrict__ items,
+    const uint32_t *__restrict__ n_items_ptr, const uint32_t *__restrict__ pairs,
+    int *__restrict__ item_counter) {
+    using Sh = ScanShape<G16>;
+    constexpr int TV = Sh::TV, W4 = Sh::W4;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint4 *stage = reinterpret_cast<uint4 *>(smem_raw);
+    uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + 2 * Sh::kStageEntries);
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ uint64_t s_bnd[kMaxPairsPerItem];
+    __shared__ float s_T1[kMaxPairsPerItem], s_g[kMaxPairsPerItem], s_k1[kMaxPairsPerItem],
+        s_w[kMaxPairsPerItem], s_gerr[kMaxPairsPerItem];
+    __shared__ int s_q[kMaxPairsPerItem], s_r[kMaxPairsPerItem];
+    __shared__ int s_item, s_abort;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_barrier_init();
+        s_abort = 0;
+    }
+    __syncthreads();
+    const uint32_t n_items = *n_items_ptr;
+    const int lane = threadIdx.x & 31;
+    uint32_t phase[2] = {0, 0};
+    while (true) {
+        if (threadIdx.x == 0) s_item = atomicAdd(item_counter, 1);
+        __syncthreads();
+        const int it = s_item;
+        if (it >= static_cast<int>(n_items)) break;
+        const ScanItem item = items[it];
+        const int c = static_cast<int>(item.cluster);
+        const uint32_t s = ix.cl_start[c];
+        const int n = static_cast<int>(ix.cl_size[c]);
+        const int pc = static_cast<int>(item.pair_count);
+        const size_t cbase = (size_t)(G16 + 1) * s;
+        const int ntiles = (n + TV - 1) / TV;
+        if (threadIdx.x == 0 && ntiles > 0)
+            issue_tile<G16>(stage, &bars[0], ix.scan4, cbase, n, 0, min(TV, n));
+        if (threadIdx.x < pc) {
+            const uint32_t pr = pairs[item.pair_begin + threadIdx.x];
+            const int q = static_cast<int>(pr >> 16), r = static_cast<int>(pr & 0xFFFFu);
+            const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
+            const QueryScalars qs = sv.scal[q];
+            s_q[threadIdx.x] = q;
+            s_r[threadIdx.x] = r;
+            s_T1[threadIdx.x] = sv.T1[q];
+            s_g[threadIdx.x] = g;
+            s_k1[threadIdx.x] = qs.k1;
+            s_w[threadIdx.x] = qs.width;
+            s_gerr[threadIdx.x] = __fsqrt_rn(fmaxf(g, 0.0f));
+            s_bnd[threadIdx.x] = r < sv.veff ? sv.bound[(size_t)q * sv.veff + r] : 0ull;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < pc * 8 * W4; i += blockDim.x) {
+            const int j = i / (8 * W4);
+            s_planes[i] = sv.planes[(size_t)s_q[j] * 8 * W4 + (i - j * 8 * W4)];
+        }
+        __syncthreads();
+        for (int t = 0; t < ntiles; ++t) {
+            const int b = t & 1;
+            const int v0 = t * TV, tv = min(TV, n - v0);
+            if (!mbar_wait_bounded(&bars[b], phase[b], sv.err)) s_abort = 1;
+            phase[b] ^= 1;
+            __syncthreads();
+            if (s_abort) return;
+            if (threadIdx.x == 0 && t + 1 < ntiles)
+                issue_tile<G16>(stage + (b ^ 1) * Sh::kStageEntries, &bars[b ^ 1], ix.scan4, cbase,
+                                n, v0 + TV, min(TV, n - v0 - TV));
+            const uint4 *sb = stage + b * Sh::kStageEntries;
+            for (int base = 0; base < tv; base += kScanThreads) {
+                const int i = base + threadIdx.x;
+                const bool valid = i < tv;
+                uint4 code[G16];
+                float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int gg = 0; gg < G16; ++gg) code[gg] = valid ? sb[gg * TV + i] : make_uint4(0, 0, 0, 0);
+                if (valid) {
+                    const uint4 fr = sb[G16 * TV + i];
+                    f = make_float4(__uint_as_float(fr.x), __uint_as_float(fr.y),
+                                    __uint_as_float(fr.z), 0.0f);
+                }
+                const uint32_t gid = s + static_cast<uint32_t>(v0 + i);
+                for (int j = 0; j < pc; ++j) {
+                    const int ip = ip_int_from_planes<G16>(code, s_planes + j * 8 * W4);
+                    const float ip1 = __fadd_rn(__fmul_rn(s_w[j], (float)ip), 0.0f);
+                    const float low = lower_bound_dist(f, ip1, s_g[j], s_k1[j], s_gerr[j]);
+                    const bool cand = valid && (low < s_T1[j]) && (make_key(low, gid) > s_bnd[j]);
+                    const uint32_t mask = __ballot_sync(0xffffffffu, cand);
+                    if (mask) {
+                        const int leader = __ffs(mask) - 1;
+                        uint32_t slot0 = 0;
+                        if (lane == leader) slot0 = atomicAdd(sv.cand_cnt + s_q[j], __popc(mask));
+                        slot0 = __shfl_sync(0xffffffffu, slot0, leader);
+                        if (cand) {
+                            const uint32_t slot = slot0 + __popc(mask & ((1u << lane) - 1u));
+                            if (slot < static_cast<uint32_t>(sv.cap))
+                                sv.cand_rec[(size_t)s_q[j] * sv.cap + slot] =
+                                    gid | (static_cast<uint64_t>(s_r[j]) << 32);
+                            else
+                                atomicOr(sv.err, kDevCandidateOverflow);
+                        }
+                    }
+                }
+            }
+            __syncthreads();  // stage buffer b is free again
+        }
+    }
+}
+
+}  // namespace cora

@@ -1,0 +1,149 @@
+/*
+ * cora_b200 — C ABI of the B200-native IVF-RaBitQ search engine (libcoraanns_b200.so).
+ *
+ * This is the drop-in boundary for the search hot path of CoraANNS. Every entry point
+ * replaces one method of the reference's coraanns::HybridIndex
+ * (include/coraanns/search/hybrid.cuh of the reference project); the line cited beside
+ * each declaration is the method it replaces. The header-only C++ shim
+ * cgcl-coraanns_b200/include/coraanns/search/hybrid.hpp wraps these functions back into
+ * a class with the reference's exact method signatures and exception types.
+ *
+ * Conventions
+ *  - plain pointers and sizes only; "h_" pointers are host memory, "d_" pointers device
+ *    memory of the engine's device;
+ *  - every function returning int returns a cora_status; on failure
+ *    cora_last_error() (thread-local) holds the message;
+ *  - one engine serves one search at a time (the reference's rule); calls are blocking
+ *    unless stated otherwise;
+ *  - results are row-major nq x topk, ascending by (distance, id), padded with
+ *    (FLT_MAX, 0); ids are the original vector ids of the index.
+ */
+#ifndef CORA_B200_H
+#define CORA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes; the shim maps them to the reference's exception types. */
+typedef enum {
+    CORA_OK = 0,
+    CORA_EINVAL = 1,   /* std::invalid_argument */
+    CORA_ESTATE = 2,   /* std::logic_error */
+    CORA_ERUNTIME = 3, /* std::runtime_error (e.g. candidate capacity exhausted) */
+    CORA_ECUDA = 4,    /* std::runtime_error from a CUDA call */
+    CORA_ENOMEM = 5    /* std::bad_alloc */
+} cora_status;
+
+typedef struct cora_engine cora_engine;
+
+/* Thread-local message of the last failing call on this thread. */
+const char *cora_last_error(void);
+
+/* HybridIndex() (hybrid.cuh:116): binds `device`, creates the engine's stream. */
+int cora_create(cora_engine **out, int device);
+/* ~HybridIndex() (hybrid.cuh:119): releases every device resource. NULL is a no-op. */
+void cora_destroy(cora_engine *engine);
+
+/* load_from_raw_pointers (hybrid.cuh:186-190). Same argument meaning, with size_t*
+ * cluster sizes passed as uint64_t*. Validation as hybrid.cu:107-121 (num <= UINT32_MAX,
+ * p_d % 64 == 0, p_d >= d, ex_b <= 8, sizes sum to num; CORA_ESTATE if already loaded),
+ * plus this engine's limits: ex_b == 7 and p_d <= 1024. Unlike the reference, the
+ * extended codes, factors and ids are copied to HBM, so the host arrays need only live
+ * for the duration of the call. */
+int cora_load_from_raw_pointers(cora_engine *engine, uint64_t num_vecs, uint64_t d, uint64_t p_d,
+                                uint64_t n_centroids, uint64_t ex_b, const float *h_centroids,
+                                const float *h_rotator, const uint32_t *h_short_data,
+                                const float *h_short_factors, const uint8_t *h_long_code,
+                                const float *h_ex_factors, const uint32_t *h_ids,
+                                const uint64_t *h_cluster_sizes);
+
+/* IVF::load (third_party/rabitq/.../index/ivf/ivf.hpp:447-539) + index::SearchData
+ * (src/index/search_data.cpp:9-127) + load_from_raw_pointers in one call: reads an
+ * IVF-RaBitQ index file with embedded (flat) centroids and a matrix rotator. */
+int cora_load_index_file(cora_engine *engine, const char *path);
+
+/* Index shape after loading: out[0..5] = num, dim, padded_dim, nlist, ex_bits,
+ * largest cluster size. */
+int cora_index_info(const cora_engine *engine, uint64_t *out6);
+
+/* prepare_workspace (hybrid.cuh:167): validate_search_shape (parameters.hpp:15-25),
+ * CORA_ESTATE without an index; frees and reallocates. */
+int cora_prepare_workspace(cora_engine *engine, uint64_t max_queries, uint64_t max_topk,
+                           uint64_t max_nprobe);
+/* free_workspace (hybrid.cuh:168): idempotent. */
+void cora_free_workspace(cora_engine *engine);
+/* reset_buffer (hybrid.cuh:169): stages queries and resets every threshold to FLT_MAX;
+ * CORA_ESTATE without a workspace, CORA_EINVAL if num_queries exceeds it. */
+int cora_reset_buffer(cora_engine *engine, const float *h_queries, uint64_t num_queries);
+
+/* search (hybrid.cuh:195-196): blocking; CORA_EINVAL unless 1 <= batch_q <= 6 or if the
+ * shape exceeds the workspace; CORA_ERUNTIME with "spill capacity exhausted" when the
+ * per-query candidate capacity ((queue + spill capacity) / max_queries) overflows. */
+int cora_search(cora_engine *engine, const float *h_queries, uint64_t num_queries,
+                uint64_t topk, uint64_t nprobe, float *h_final_dists, uint32_t *h_final_pids,
+                int batch_q);
+
+/* Device-resident variant of search (no reference counterpart; used by multi-GPU
+ * callers and for kernel-only timing): queries, outputs in device memory, enqueued on
+ * `stream` (a cudaStream_t, NULL for the engine's own stream); returns without
+ * synchronising. Errors raised on the device are reported by cora_check_device(). */
+int cora_search_device(cora_engine *engine, const float *d_queries, uint64_t num_queries,
+                       uint64_t topk, uint64_t nprobe, float *d_final_dists,
+                       uint32_t *d_final_pids, void *stream);
+/* Synchronises the engine's last stream and turns device-side error flags into a status. */
+int cora_check_device(cora_engine *engine);
+
+/* seed_thresholds / capture_thresholds (hybrid.cuh:192-193). */
+int cora_seed_thresholds(cora_engine *engine, const float *h_in, uint64_t nq);
+int cora_capture_thresholds(const cora_engine *engine, float *h_out, uint64_t nq);
+
+/* set_vanguard_size / get_vanguard_size (hybrid.cuh:155-158): CORA_ESTATE when raising
+ * the depth above the one the workspace was prepared for (hybrid.cu:87-91). */
+int cora_set_vanguard_size(cora_engine *engine, uint64_t size);
+uint64_t cora_get_vanguard_size(const cora_engine *engine);
+
+/* set_queue_capacity / set_queue_spill_capacity / get_queue_capacity
+ * (hybrid.cuh:143-147, validation hybrid.cu:166-185). Their sum bounds the candidate
+ * records held in HBM per search. */
+int cora_set_queue_capacity(cora_engine *engine, uint64_t capacity);
+int cora_set_queue_spill_capacity(cora_engine *engine, uint64_t capacity);
+uint64_t cora_get_queue_capacity(const cora_engine *engine);
+
+/* Knobs (hybrid.cuh:121-135,160-165). cross_query_reuse=0 processes one query per
+ * cluster work item; cpu_secondary_filter and ip_kernel_type are accepted for drop-in
+ * compatibility (refinement runs on the GPU; the scan always uses the integer estimator). */
+void cora_set_profiling(cora_engine *engine, int enabled);
+void cora_set_candidate_stats(cora_engine *engine, int enabled);
+void cora_set_gpu_filter_timing(cora_engine *engine, int enabled);
+void cora_set_cross_query_reuse(cora_engine *engine, int enabled);
+void cora_set_cpu_secondary_filter(cora_engine *engine, int enabled);
+void cora_set_ip_kernel_type(cora_engine *engine, int kernel_type);
+int cora_get_ip_kernel_type(const cora_engine *engine);
+
+/* Counters of the last search (hybrid.cuh:137-153). submitted = candidates that passed
+ * the 1-bit lower bound (seeds included); refined = candidates refined with ex codes;
+ * spilled is always 0 (no host ring). */
+uint64_t cora_get_last_submitted_count(const cora_engine *engine);
+uint64_t cora_get_last_refined_count(const cora_engine *engine);
+uint64_t cora_get_last_spilled_count(const cora_engine *engine);
+float cora_get_last_gpu_filter_ms(const cora_engine *engine);
+
+/* Diagnostics for parity tests (no reference counterpart): copies an intermediate of
+ * the last search to host memory. what: 0 rotated queries (nq x D f32), 1 probe ids
+ * (nq x nprobe i32), 2 probe distances (nq x nprobe f32), 3 per-query candidate counts
+ * (nq u32), 4 thresholds after seeding (nq f32), 5 query bit-planes
+ * (nq x 8 x W4 u32, W4 = 4 * ceil(D / 128)), 6 query scalars (nq x {width, k1, kb, sumq}),
+ * 7 candidate gids (nq x cap u32, per query sorted ascending, unused slots 0xFFFFFFFF).
+ * `bytes` must equal the size of the requested array. */
+int cora_debug_copy(cora_engine *engine, int what, void *h_out, uint64_t bytes);
+/* Candidate capacity per query of the current workspace (array 7 above is nq x cap). */
+uint64_t cora_get_candidate_capacity(const cora_engine *engine);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CORA_B200_H */

@@ -1,0 +1,387 @@
+/*
+ * TEST INFRASTRUCTURE ONLY — CPU oracle for the IVF-RaBitQ search hot path.
+ * See cora_oracle.h for the contract and the reference lines each step restates.
+ * Built with -ffp-contract=off -fno-fast-math so every fp32 operation rounds once.
+ */
+#include "cora_oracle.h"
+
+#include <float.h>
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* Monotone map float -> uint32 used for every (value, id) ordering in the contract. */
+static inline uint32_t ord_f32(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+typedef struct {
+    uint64_t key; /* (ord(value) << 32) | id */
+    float value;
+    float ip1;
+    uint32_t gid;
+    uint32_t probe;
+} entry_t;
+
+static int cmp_entry(const void *a, const void *b) {
+    const uint64_t x = ((const entry_t *)a)->key, y = ((const entry_t *)b)->key;
+    return (x > y) - (x < y);
+}
+static int cmp_u32(const void *a, const void *b) {
+    const uint32_t x = *(const uint32_t *)a, y = *(const uint32_t *)b;
+    return (x > y) - (x < y);
+}
+
+/* hybrid.cu:436-440 (cuBLAS SGEMM q' = q*P) restated with fp64 accumulation in ascending
+ * input-dimension order. fp32*fp32 products are exact in fp64, so a fused or unfused
+ * multiply-add gives the same bits. */
+void cora_oracle_rotate(const cora_oracle_index *ix, const float *q, uint64_t nq, float *qr) {
+    const uint64_t dim = ix->dim, D = ix->padded_dim;
+    for (uint64_t n = 0; n < nq; ++n)
+        for (uint64_t j = 0; j < D; ++j) {
+            double acc = 0.0;
+            for (uint64_t i = 0; i < dim; ++i)
+                acc += (double)q[n * dim + i] * (double)ix->rotator[i * D + j];
+            qr[n * D + j] = (float)acc;
+        }
+}
+
+/* query_kernels.cuh:73-94 (sumq, k1 = -0.5 sumq, kb = -(2^(ex+1)-1)/2 sumq) and
+ * query_kernels.cuh:117-189 (width = max(amax/127, 1e-30), qint = clamp(rn(q'/width)),
+ * plane j word w bit (31-b) = bit j of qint[32w+b]). sumq accumulates in fp64: lane l of
+ * 32 sums dims l, l+32, ... in ascending order, then an xor butterfly (16,8,4,2,1). */
+void cora_oracle_query_prep(uint64_t D, uint64_t ex_bits, const float *qr, uint64_t nq,
+                            float *sumq, float *k1, float *kb, float *width, int32_t *qint,
+                            uint32_t *planes) {
+    const uint64_t W = D / 32;
+    const float c1 = -0.5f;
+    const float cb = -(float)((1u << (ex_bits + 1)) - 1u) / 2.0f;
+    for (uint64_t n = 0; n < nq; ++n) {
+        const float *x = qr + n * D;
+        double part[32], next[32];
+        float amax = 0.0f;
+        for (int l = 0; l < 32; ++l) {
+            double acc = 0.0;
+            for (uint64_t j = (uint64_t)l; j < D; j += 32) acc += (double)x[j];
+            part[l] = acc;
+        }
+        for (int off = 16; off >= 1; off >>= 1) {
+            for (int l = 0; l < 32; ++l) next[l] = part[l] + part[l ^ off];
+            memcpy(part, next, sizeof(part));
+        }
+        for (uint64_t j = 0; j < D; ++j) amax = fmaxf(amax, fabsf(x[j]));
+        const float sf = (float)part[0];
+        if (sumq) sumq[n] = sf;
+        if (k1) k1[n] = sf * c1;
+        if (kb) kb[n] = sf * cb;
+        const float w = fmaxf(amax / 127.0f, 1e-30f);
+        const float inv = 1.0f / w;
+        if (width) width[n] = w;
+        uint32_t *pl = planes ? planes + n * 8 * W : NULL;
+        if (pl) memset(pl, 0, 8 * W * sizeof(uint32_t));
+        for (uint64_t j = 0; j < D; ++j) {
+            const float p = x[j] * inv;
+            int v = (int)nearbyintf(p); /* round half to even, as __float2int_rn */
+            if (v < -128) v = -128;
+            if (v > 127) v = 127;
+            if (qint) qint[n * D + j] = v;
+            if (pl) {
+                const uint32_t bits = (uint32_t)v & 0xFFu;
+                for (int b = 0; b < 8; ++b)
+                    if ((bits >> b) & 1u) pl[b * W + j / 32] |= 1u << (31 - (j % 32));
+            }
+        }
+    }
+}
+
+/* g_add = ||q' - c'||^2 (hybrid.cu:465-477 computes ||q||^2+||c||^2-2q.c in fp32; here
+ * it is one fp64 fma chain in ascending dimension order, rounded once). */
+float cora_oracle_centroid_dist(const float *qr, const float *c, uint64_t D) {
+    double acc = 0.0;
+    for (uint64_t j = 0; j < D; ++j) {
+        const double d = (double)qr[j] - (double)c[j];
+        acc = fma(d, d, acc);
+    }
+    return (float)acc;
+}
+
+static void probe_one(const cora_oracle_index *ix, const float *x, uint64_t nprobe,
+                      int32_t *pid_out, float *pg_out, entry_t *scratch) {
+    const uint64_t D = ix->padded_dim;
+    for (uint64_t c = 0; c < ix->nlist; ++c) {
+        const float g = cora_oracle_centroid_dist(x, ix->centroids + c * D, D);
+        scratch[c].value = g;
+        scratch[c].key = ((uint64_t)ord_f32(g) << 32) | (uint32_t)c;
+    }
+    qsort(scratch, ix->nlist, sizeof(entry_t), cmp_entry);
+    for (uint64_t r = 0; r < nprobe; ++r) {
+        pid_out[r] = (int32_t)(scratch[r].key & 0xFFFFFFFFu);
+        pg_out[r] = scratch[r].value;
+    }
+}
+
+/* select_k(select_min, sorted) over g_add, hybrid.cu:485-493, ties by cluster id. */
+void cora_oracle_probe(const cora_oracle_index *ix, const float *qr, uint64_t nq,
+                       uint64_t nprobe, int32_t *probe_ids, float *probe_g) {
+    entry_t *scratch = (entry_t *)malloc(ix->nlist * sizeof(entry_t));
+    for (uint64_t n = 0; n < nq; ++n)
+        probe_one(ix, qr + n * ix->padded_dim, nprobe, probe_ids + n * nprobe,
+                  probe_g + n * nprobe, scratch);
+    free(scratch);
+}
+
+static uint64_t *cluster_starts(const cora_oracle_index *ix) {
+    uint64_t *s = (uint64_t *)malloc((ix->nlist + 1) * sizeof(uint64_t));
+    s[0] = 0;
+    for (uint64_t c = 0; c < ix->nlist; ++c) s[c + 1] = s[c] + ix->cluster_sizes[c];
+    return s;
+}
+
+static int32_t ip_int_at(const cora_oracle_index *ix, uint64_t start, uint64_t n, uint64_t i,
+                         const uint32_t *planes) {
+    const uint64_t W = ix->padded_dim / 32;
+    int32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (uint64_t w = 0; w < W; ++w) {
+        const uint32_t x = ix->short_data[start * W + w * n + i];
+        for (int j = 0; j < 8; ++j) acc[j] += __builtin_popcount(x & planes[j * W + w]);
+    }
+    /* filter_kernels.cuh:100-104: the high plane carries weight -2^7 */
+    int32_t ip = -(acc[7] << 7);
+    for (int j = 0; j < 7; ++j) ip += acc[j] << j;
+    return ip;
+}
+
+int32_t cora_oracle_ip_int(const cora_oracle_index *ix, uint64_t gid, const uint32_t *planes) {
+    uint64_t start = 0, c = 0;
+    while (start + ix->cluster_sizes[c] <= gid) start += ix->cluster_sizes[c++];
+    return ip_int_at(ix, start, ix->cluster_sizes[c], gid - start, planes);
+}
+
+/* filter_kernels.cuh:693-696: low = f_add + g + f_rescale*(ip1 + k1) - f_error*sqrt(g),
+ * with sqrt's argument clamped at zero. */
+float cora_oracle_low(const cora_oracle_index *ix, uint64_t gid, float ip1, float g, float k1) {
+    const float *f = ix->short_factors + gid * 3;
+    const float gerr = sqrtf(fmaxf(g, 0.0f));
+    const float a = f[0] + g;
+    const float b = f[1] * (ip1 + k1);
+    const float e = f[2] * gerr;
+    return (a + b) - e;
+}
+
+/* Inverse of pack_excode.hpp:216-264 (packing_7bit_excode), per 64 dims = 56 bytes. */
+void cora_oracle_decode_ex7(const uint8_t *code, uint64_t D, uint8_t *u) {
+    for (uint64_t b = 0; b < D / 64; ++b) {
+        const uint8_t *p = code + b * 56;
+        uint8_t *o = u + b * 64;
+        for (int k = 0; k < 16; ++k) {
+            o[k] = p[k] & 63u;
+            o[16 + k] = p[16 + k] & 63u;
+            o[32 + k] = p[32 + k] & 63u;
+            o[48 + k] = (uint8_t)((p[k] >> 6) | ((p[16 + k] >> 6) << 2) | ((p[32 + k] >> 6) << 4));
+        }
+        uint64_t top = 0;
+        for (int t = 0; t < 8; ++t) top |= (uint64_t)p[48 + t] << (8 * t);
+        for (int d = 0; d < 64; ++d) o[d] |= (uint8_t)(((top >> (8 * (d % 8) + d / 8)) & 1u) << 6);
+    }
+}
+
+/* Refinement inner product of the full (1 + ex_bits)-bit code with the rotated query:
+ * ipT = sum_i q'_i * (2^ex_bits * b_i + u_i), b the 1-bit code (bit 31-(i%32) of word i/32),
+ * u the decoded 7-bit ex code. The reference forms the same quantity as
+ * 2^ex_bits * ip1 + ip2 (cpu_refinement.cpp:183-191) with ip1 taken from its fp16-LUT or
+ * 8-bit-query scan; here it is one fp64 accumulation (all products exact): lane l of 32
+ * accumulates dims 64b+l then 64b+32+l for ascending blocks b, then an xor butterfly
+ * (offsets 16, 8, 4, 2, 1) combines the lanes, and the sum is rounded once to fp32. */
+float cora_oracle_ip_total(const float *qr, const uint32_t *bits, const uint8_t *code,
+                           uint64_t D) {
+    uint8_t u[4096];
+    double part[32], next[32];
+    cora_oracle_decode_ex7(code, D, u);
+    for (int l = 0; l < 32; ++l) {
+        double acc = 0.0;
+        for (uint64_t b = 0; b < D / 64; ++b) {
+            for (int h = 0; h < 2; ++h) {
+                const uint64_t d = 64 * b + 32 * h + l;
+                const uint32_t bit = (bits[d / 32] >> (31 - (d % 32))) & 1u;
+                acc += (double)qr[d] * (double)(128u * bit + u[d]);
+            }
+        }
+        part[l] = acc;
+    }
+    for (int off = 16; off >= 1; off >>= 1) {
+        for (int l = 0; l < 32; ++l) next[l] = part[l] + part[l ^ off];
+        memcpy(part, next, sizeof(part));
+    }
+    return (float)part[0];
+}
+
+/* cpu_refinement.cpp:189-191: ex = f_add_ex + g + f_rescale_ex * (ipT + kb), where
+ * ipT = 2^ex_bits * ip1 + ip2 is the full-code inner product above. */
+float cora_oracle_ex(const cora_oracle_index *ix, uint64_t gid, float ip_total, float g,
+                     float kb) {
+    const float *f = ix->ex_factors + gid * 2;
+    return (f[0] + g) + (f[1] * (ip_total + kb));
+}
+
+static void vector_bits(const cora_oracle_index *ix, uint64_t start, uint64_t n, uint64_t i,
+                        uint32_t *out) {
+    const uint64_t W = ix->padded_dim / 32;
+    for (uint64_t w = 0; w < W; ++w) out[w] = ix->short_data[start * W + w * n + i];
+}
+
+static float refine(const cora_oracle_index *ix, const float *x, uint64_t start, uint64_t n,
+                    uint64_t i, float g, float kb) {
+    uint32_t bits[128];
+    const uint64_t D = ix->padded_dim, LC = D * ix->ex_bits / 8, gid = start + i;
+    vector_bits(ix, start, n, i, bits);
+    const float ipt = cora_oracle_ip_total(x, bits, ix->long_codes + gid * LC, D);
+    return cora_oracle_ex(ix, gid, ipt, g, kb);
+}
+
+static void push(entry_t **v, uint64_t *n, uint64_t *cap, entry_t e) {
+    if (*n == *cap) {
+        *cap = *cap ? *cap * 2 : 256;
+        *v = (entry_t *)realloc(*v, *cap * sizeof(entry_t));
+    }
+    (*v)[(*n)++] = e;
+}
+
+int cora_oracle_search(const cora_oracle_index *ix, const float *q, uint64_t nq, uint64_t k,
+                       uint64_t nprobe, uint64_t vanguard, const float *thresholds0,
+                       float *out_dist, uint32_t *out_ids, uint64_t *cand_count,
+                       float *thresholds1, int32_t *probe_ids_out, float *probe_g_out,
+                       uint32_t *cand_gids, uint64_t cand_cap, int threads) {
+    if (!ix || !q || !out_dist || !out_ids || k == 0 || k > CORA_ORACLE_VANGUARD_MAX_KEEP ||
+        nprobe == 0 || nprobe > ix->nlist ||
+        ix->padded_dim % 64 || ix->padded_dim > 4096 || ix->ex_bits != 7)
+        return -1;
+    const uint64_t D = ix->padded_dim, W = D / 32;
+    const uint64_t keep = k > CORA_ORACLE_VANGUARD_MIN_KEEP ? k : CORA_ORACLE_VANGUARD_MIN_KEEP;
+    /* Seeding depth: the vanguard size, but at least the nearest probe, so that the
+     * static main-phase threshold always prunes (the reference's CPU refiner lowers its
+     * thresholds continuously instead, cpu_refinement.cpp:217-228). */
+    const uint64_t vdepth = vanguard > 0 ? vanguard : 1;
+    const uint64_t veff = vdepth < nprobe ? vdepth : nprobe;
+    uint64_t *starts = cluster_starts(ix);
+    if (threads < 1) threads = 1;
+
+#pragma omp parallel for schedule(dynamic, 1) num_threads(threads)
+    for (int64_t qi = 0; qi < (int64_t)nq; ++qi) {
+        const uint64_t n = (uint64_t)qi;
+        float *x = (float *)malloc(D * sizeof(float));
+        uint32_t *planes = (uint32_t *)malloc(8 * W * sizeof(uint32_t));
+        entry_t *scratch = (entry_t *)malloc(ix->nlist * sizeof(entry_t));
+        int32_t *pid = (int32_t *)malloc(nprobe * sizeof(int32_t));
+        float *pg = (float *)malloc(nprobe * sizeof(float));
+        entry_t *res = NULL, *pair = NULL;
+        uint64_t nres = 0, cres = 0, npair = 0, cpair = 0;
+        float sumq, k1, kb, width;
+
+        cora_oracle_rotate(ix, q + n * ix->dim, 1, x);
+        cora_oracle_query_prep(D, ix->ex_bits, x, 1, &sumq, &k1, &kb, &width, NULL, planes);
+        probe_one(ix, x, nprobe, pid, pg, scratch);
+        if (probe_ids_out) memcpy(probe_ids_out + n * nprobe, pid, nprobe * sizeof(int32_t));
+        if (probe_g_out) memcpy(probe_g_out + n * nprobe, pg, nprobe * sizeof(float));
+
+        const float T0 = thresholds0 ? thresholds0[n] : FLT_MAX;
+        uint64_t *bound = (uint64_t *)malloc((veff ? veff : 1) * sizeof(uint64_t));
+        int *take_all = (int *)malloc((veff ? veff : 1) * sizeof(int));
+
+        /* Vanguard: the first veff probes keep their top max(k,20) by (low, gid) among
+         * low < T0 as seeds (filter_kernels.cuh:308-468), refined right away. */
+        for (uint64_t r = 0; r < veff; ++r) {
+            const uint64_t c = (uint64_t)pid[r], s = starts[c], nc = ix->cluster_sizes[c];
+            const float g = pg[r];
+            npair = 0;
+            for (uint64_t i = 0; i < nc; ++i) {
+                const float ip1 = width * (float)ip_int_at(ix, s, nc, i, planes) + 0.0f;
+                const float low = cora_oracle_low(ix, s + i, ip1, g, k1);
+                if (low < T0) {
+                    entry_t e = {((uint64_t)ord_f32(low) << 32) | (uint32_t)(s + i), low, ip1,
+                                 (uint32_t)(s + i), (uint32_t)r};
+                    push(&pair, &npair, &cpair, e);
+                }
+            }
+            qsort(pair, npair, sizeof(entry_t), cmp_entry);
+            take_all[r] = npair <= keep;
+            bound[r] = take_all[r] ? 0 : pair[keep - 1].key;
+            const uint64_t ns = take_all[r] ? npair : keep;
+            for (uint64_t i = 0; i < ns; ++i) {
+                const uint32_t gid = pair[i].gid;
+                const float ex = refine(ix, x, s, nc, gid - s, g, kb);
+                entry_t e = {((uint64_t)ord_f32(ex) << 32) | ix->ids[gid], ex, pair[i].ip1, gid,
+                             (uint32_t)r};
+                push(&res, &nres, &cres, e);
+            }
+        }
+        /* T1 = k-th smallest seed distance below T0, when at least k exist. */
+        float T1 = T0;
+        {
+            uint64_t nv = 0;
+            for (uint64_t i = 0; i < nres; ++i)
+                if (res[i].value < T0) ++nv;
+            if (nv >= k) {
+                entry_t *tmp = (entry_t *)malloc(nv * sizeof(entry_t));
+                uint64_t m = 0;
+                for (uint64_t i = 0; i < nres; ++i)
+                    if (res[i].value < T0) tmp[m++] = res[i];
+                qsort(tmp, nv, sizeof(entry_t), cmp_entry);
+                T1 = tmp[k - 1].value;
+                free(tmp);
+            }
+        }
+        if (thresholds1) thresholds1[n] = T1;
+
+        /* Main scan over every probe against the static T1; vanguard probes skip their
+         * seeds (keys at or below the recorded boundary). */
+        for (uint64_t r = 0; r < nprobe; ++r) {
+            const uint64_t c = (uint64_t)pid[r], s = starts[c], nc = ix->cluster_sizes[c];
+            const float g = pg[r];
+            if (r < veff && take_all[r]) continue;
+            for (uint64_t i = 0; i < nc; ++i) {
+                const float ip1 = width * (float)ip_int_at(ix, s, nc, i, planes) + 0.0f;
+                const float low = cora_oracle_low(ix, s + i, ip1, g, k1);
+                if (!(low < T1)) continue;
+                if (r < veff) {
+                    const uint64_t key = ((uint64_t)ord_f32(low) << 32) | (uint32_t)(s + i);
+                    if (key <= bound[r]) continue;
+                }
+                const uint32_t gid = (uint32_t)(s + i);
+                const float ex = refine(ix, x, s, nc, i, g, kb);
+                entry_t e = {((uint64_t)ord_f32(ex) << 32) | ix->ids[gid], ex, ip1, gid,
+                             (uint32_t)r};
+                push(&res, &nres, &cres, e);
+            }
+        }
+        if (cand_count) cand_count[n] = nres;
+        if (cand_gids && cand_cap) {
+            uint32_t *g = cand_gids + n * cand_cap;
+            const uint64_t m = nres < cand_cap ? nres : cand_cap;
+            uint32_t *all = (uint32_t *)malloc((nres ? nres : 1) * sizeof(uint32_t));
+            for (uint64_t i = 0; i < nres; ++i) all[i] = res[i].gid;
+            qsort(all, nres, sizeof(uint32_t), cmp_u32);
+            for (uint64_t i = 0; i < cand_cap; ++i) g[i] = i < m ? all[i] : 0xFFFFFFFFu;
+            free(all);
+        }
+        /* Output: ascending (ex, id) among ex < T0, padded with (FLT_MAX, 0)
+         * (cpu_refinement.cpp:197-230,269-283). */
+        qsort(res, nres, sizeof(entry_t), cmp_entry);
+        uint64_t o = 0;
+        for (uint64_t i = 0; i < nres && o < k; ++i) {
+            if (!(res[i].value < T0)) continue;
+            out_dist[n * k + o] = res[i].value;
+            out_ids[n * k + o] = (uint32_t)(res[i].key & 0xFFFFFFFFu);
+            ++o;
+        }
+        for (; o < k; ++o) {
+            out_dist[n * k + o] = FLT_MAX;
+            out_ids[n * k + o] = 0;
+        }
+        free(x); free(planes); free(scratch); free(pid); free(pg); free(res); free(pair);
+        free(bound); free(take_all);
+    }
+    free(starts);
+    return 0;
+}

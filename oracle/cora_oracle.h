@@ -1,0 +1,97 @@
+/*
+ * TEST INFRASTRUCTURE ONLY — the CPU oracle for the IVF-RaBitQ search hot path.
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg may load this
+ * library, and only as the checker. The product (libcoraanns_b200.so) never links it.
+ *
+ * It restates, single-threaded per query and in a fixed evaluation order, the arithmetic
+ * of the reference's hybrid search path (paths within the reference project):
+ *   rotation           src/search/hybrid.cu:436-440 (q' = q * P)
+ *   query factors      src/search/query_kernels.cuh:73-94      (sumq, k1, kb)
+ *   query bit-planes   src/search/query_kernels.cuh:117-189    (8-bit symmetric, Bq = 8)
+ *   coarse distances   src/search/hybrid.cu:465-477 + select_k :485-493
+ *   1-bit estimator    src/search/filter_kernels.cuh:79-114    (popcount ip_int)
+ *   lower bound        src/search/filter_kernels.cuh:693-696 / index/estimator.hpp:65-70
+ *   ex refinement      src/search/cpu_refinement.cpp:183-191   (8-bit code IP)
+ *   7-bit decode       third_party/rabitq/.../utils/space.hpp:677-762, layout
+ *                      third_party/rabitq/.../quantization/pack_excode.hpp:216-264
+ *   top-k              src/search/cpu_refinement.cpp:202-230,269-283
+ *   vanguard seeding   src/search/filter_kernels.cuh:308-468,470-582 (keep max(topk,20))
+ *
+ * Determinism contract (the CUDA kernels follow it operation for operation):
+ *  - rotation and centroid distances accumulate in fp64 in ascending index order (fp64
+ *    fma; products of two fp32 values are exact in fp64) and round once to fp32; sumq
+ *    accumulates in fp64 over 32 strided lanes combined by an xor butterfly;
+ *  - ip_int is exact integer arithmetic; ip1 = width * (float)ip_int;
+ *  - low / ex follow the reference's expression trees in fp32, round-to-nearest, with no
+ *    contraction (built with -ffp-contract=off);
+ *  - the refinement inner product of the full 8-bit code, ipT = <q', 128 b + u>, is
+ *    accumulated in fp64 by 32 "lanes" (lane l owns dims 64b+l and 64b+32+l of every
+ *    64-dim block b, ascending b) and combined by an xor butterfly (16,8,4,2,1); the
+ *    reference adds 128 * ip1 from its scan instead, which with the 8-bit query planes
+ *    loses accuracy (ip1's quantisation error is multiplied by 128);
+ *  - coarse probes are ordered by (g_add, cluster id); results by (ex, original id);
+ *  - thresholds are static per phase (seeded T0, then T1 from the vanguard seeds), so the
+ *    candidate set {v : low(v) < T} is a pure function of the inputs. The first
+ *    max(vanguard, 1) probes keep their best max(k, 20) vectors by (low, gid) among
+ *    low < T0 as seeds; T1 = min(T0, k-th smallest seed distance). The main phase scans
+ *    every probe, skipping seeds, with candidates low < T1; results are the best k by
+ *    (ex, id) among seeds and candidates with ex < T0.
+ *
+ * Inputs use the reference adapter's packed layout (src/index/search_data.cpp:45-123):
+ * word-major 1-bit codes per cluster with bit (31-b) of word w holding dim 32w+b, float[N][3]
+ * short factors, compact ex codes N x (D*ex_bits/8) and float[N][2] ex factors.
+ */
+#ifndef CORA_ORACLE_H
+#define CORA_ORACLE_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    uint64_t num, dim, padded_dim, nlist, ex_bits;
+    const float *centroids;        /* nlist x D, rotated */
+    const float *rotator;          /* dim x D, row-major */
+    const uint32_t *short_data;    /* N x D/32, word-major per cluster */
+    const float *short_factors;    /* N x 3: f_add, f_rescale, f_error */
+    const uint8_t *long_codes;     /* N x D*ex_bits/8 */
+    const float *ex_factors;       /* N x 2: f_add_ex, f_rescale_ex */
+    const uint32_t *ids;           /* N original ids, cluster order */
+    const uint64_t *cluster_sizes; /* nlist */
+} cora_oracle_index;
+
+#define CORA_ORACLE_VANGUARD_MIN_KEEP 20
+#define CORA_ORACLE_VANGUARD_MAX_KEEP 4096 /* also the largest supported topk */
+
+void cora_oracle_rotate(const cora_oracle_index *ix, const float *q, uint64_t nq, float *qr);
+void cora_oracle_query_prep(uint64_t D, uint64_t ex_bits, const float *qr, uint64_t nq,
+                            float *sumq, float *k1, float *kb, float *width, int32_t *qint,
+                            uint32_t *planes);
+float cora_oracle_centroid_dist(const float *qr, const float *c, uint64_t D);
+void cora_oracle_probe(const cora_oracle_index *ix, const float *qr, uint64_t nq,
+                       uint64_t nprobe, int32_t *probe_ids, float *probe_g);
+int32_t cora_oracle_ip_int(const cora_oracle_index *ix, uint64_t gid, const uint32_t *planes);
+float cora_oracle_low(const cora_oracle_index *ix, uint64_t gid, float ip1, float g, float k1);
+void cora_oracle_decode_ex7(const uint8_t *code, uint64_t D, uint8_t *u);
+float cora_oracle_ip_total(const float *qr, const uint32_t *bits, const uint8_t *code,
+                           uint64_t D);
+float cora_oracle_ex(const cora_oracle_index *ix, uint64_t gid, float ip_total, float g,
+                     float kb);
+
+/* Full search. Outputs are row-major nq x k. thresholds0 may be NULL (FLT_MAX).
+ * Optional outputs (NULL to skip): cand_count[nq] (= seeds + main candidates),
+ * thresholds1[nq] (threshold after vanguard seeding), probe_ids/probe_g [nq x nprobe],
+ * cand_gids[nq x cand_cap] (sorted ascending gids of all candidates, truncated at cap).
+ * Returns 0, or -1 on invalid arguments. `threads` > 1 parallelises over queries. */
+int cora_oracle_search(const cora_oracle_index *ix, const float *q, uint64_t nq, uint64_t k,
+                       uint64_t nprobe, uint64_t vanguard, const float *thresholds0,
+                       float *out_dist, uint32_t *out_ids, uint64_t *cand_count,
+                       float *thresholds1, int32_t *probe_ids, float *probe_g,
+                       uint32_t *cand_gids, uint64_t cand_cap, int threads);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

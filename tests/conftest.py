@@ -1,0 +1,80 @@
+"""Shared test setup: the gpu marker, import paths, golden fixtures and KAT builders."""
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+GOLDEN = ROOT / "tests" / "golden"
+sys.path.insert(0, str(ROOT / "oracle"))
+sys.path.insert(0, str(ROOT / "cgcl-coraanns_b200"))
+sys.path.insert(0, str(ROOT))
+
+GOLDEN_NAMES = ["demo", "d96", "d200", "d150"]
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200); run with -m gpu")
+
+
+def has_gpu() -> bool:
+    try:
+        import torch
+        return torch.cuda.is_available()
+    except Exception:  # pragma: no cover
+        return False
+
+
+@pytest.fixture(scope="session")
+def golden():
+    """name -> (index path, npz dict)."""
+    out = {}
+    for name in GOLDEN_NAMES:
+        with np.load(GOLDEN / f"{name}.npz") as z:
+            out[name] = (GOLDEN / f"{name}.index", {k: z[k] for k in z.files})
+    return out
+
+
+def regen_base(meta, gen):
+    """Regenerate a fixture's base vectors from its recorded seed (make_golden.make_data)."""
+    n, dim, nlist, nq, seed = (int(x) for x in meta)
+    sigma = float(gen[0])
+    rng = np.random.default_rng(seed)
+    centres = rng.normal(size=(nlist, dim)).astype(np.float32)
+    lab = rng.integers(0, nlist, n)
+    return (centres[lab] + sigma * rng.normal(size=(n, dim))).astype(np.float32)
+
+
+# ------------------------------------------------------------------------------------
+# Known-answer fixtures ported from the reference's GPU tests
+# (tests/gpu_cpu_ring_queue_test.cpp:17-50, tests/gpu_cpu_highk_vanguard_test.cpp:82-107,
+#  tests/gpu_search_lifecycle_test.cpp:18-37): identity rotation, all-zero codes,
+# f_add = -1e6 so that every vector passes the 1-bit filter, unique f_add_ex.
+# ------------------------------------------------------------------------------------
+def kat_fixture(count=32768, topk=100, clusters=8, queries=5, dim=96, padded=128, f_add=-1e6):
+    sd = dict(num=count, dim=dim, D=padded, nlist=clusters, ex_bits=7)
+    sd["centroids"] = np.zeros((clusters, padded), np.float32)
+    rot = np.zeros((dim, padded), np.float32)
+    rot[np.arange(dim), np.arange(dim)] = 1.0
+    sd["rotator"] = rot
+    sd["short_data"] = np.zeros(count * padded // 32, np.uint32)
+    sf = np.zeros((count, 3), np.float32)
+    sf[:, 0] = f_add
+    sd["short_factors"] = sf
+    sd["long_codes"] = np.zeros(count * padded * 7 // 8, np.uint8)
+    lf = np.zeros((count, 2), np.float32)
+    i = np.arange(count, dtype=np.int64)
+    lf[:, 0] = (0.01 * ((i * 7919) % count).astype(np.float32)).astype(np.float32)
+    sd["ex_factors"] = lf
+    sd["ids"] = np.arange(count, dtype=np.uint32)
+    sd["sizes"] = np.full(clusters, count // clusters, np.uint64)
+    q = np.zeros((queries, dim), np.float32)
+    for a in range(queries):
+        for d in range(dim):
+            q[a, d] = np.float32(0.01) * np.float32(1 + (a + d) % 7)
+    order = np.argsort(lf[:, 0], kind="stable")
+    expected = np.sort(order[:topk]).astype(np.uint32)
+    return sd, q, expected

@@ -1,0 +1,150 @@
+"""GPU parity: the CUDA path through the C ABI against the oracle, bit for bit.
+
+Each test compares the pipeline stage by stage (rotated queries, query scalars and
+bit-planes, probe lists, seeded thresholds, candidate counts and sets, final distances and
+ids), so the first failing assertion names the first diverging kernel.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import py_oracle as po
+from conftest import GOLDEN_NAMES
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def cb():
+    import coraanns_b200
+    return coraanns_b200
+
+
+def _engine(cb, path=None, sd=None, nq=1, k=10, nprobe=1, vanguard=5):
+    e = cb.HybridIndex(0)
+    e.set_vanguard_size(vanguard)
+    if path is not None:
+        e.load_index_file(path)
+    else:
+        e.load_search_data(sd)
+    e.prepare_workspace(nq, k, nprobe)
+    return e
+
+
+def _check_stages(e, q, k, nprobe, ref, tag):
+    nq = q.shape[0]
+    if "qr" in ref:
+        assert e.debug("rotated", nq).tobytes() == ref["qr"].tobytes(), f"{tag}: rotation"
+    if "scalars" in ref:
+        assert e.debug("scalars", nq).tobytes() == ref["scalars"].astype(np.float32).tobytes(), \
+            f"{tag}: query scalars"
+    if "planes" in ref:
+        got = e.debug("planes", nq)
+        W = ref["planes"].shape[2]
+        assert np.array_equal(got[:, :, :W], ref["planes"]), f"{tag}: query bit-planes"
+        assert not got[:, :, W:].any(), f"{tag}: padding planes"
+    assert np.array_equal(e.debug("probe_ids", nq, nprobe), ref["probe_ids"]), f"{tag}: probes"
+    assert e.debug("probe_g", nq, nprobe).tobytes() == ref["probe_g"].tobytes(), f"{tag}: probe g"
+    assert e.debug("thresholds1", nq).tobytes() == ref["thresholds1"].tobytes(), f"{tag}: T1"
+    assert np.array_equal(e.debug("cand_count", nq).astype(np.uint64), ref["cand_count"]), \
+        f"{tag}: candidate counts"
+
+
+@pytest.mark.parametrize("loader", ["file", "raw"])
+@pytest.mark.parametrize("name", GOLDEN_NAMES)
+def test_golden_parity(cb, golden, name, loader):
+    path, z = golden[name]
+    q = z["queries"]
+    grid = z["grid"]
+    kmax, npmax = int(grid[:, 0].max()), int(grid[:, 1].max())
+    if loader == "file":
+        e = _engine(cb, path=path, nq=len(q), k=kmax, nprobe=npmax)
+    else:
+        e = _engine(cb, sd=po.search_data(po.read_ivf_file(path)), nq=len(q), k=kmax,
+                    nprobe=npmax)
+    for k, nprobe, van in grid:
+        k, nprobe, van = int(k), int(nprobe), int(van)
+        tag = f"{name}/{loader} k{k}_np{nprobe}_v{van}"
+        e.set_vanguard_size(van)
+        e.reset_buffer(q)
+        d, i = e.search(q, k, nprobe)
+        key = f"k{k}_np{nprobe}_v{van}"
+        ref = dict(qr=z["qr"], scalars=z["scalars"], planes=z["planes"],
+                   probe_ids=z[f"probe_{key}"], probe_g=z[f"probeg_{key}"],
+                   thresholds1=z[f"t1_{key}"], cand_count=z[f"cand_{key}"])
+        _check_stages(e, q, k, nprobe, ref, tag)
+        assert np.array_equal(i, z[f"ids_{key}"]), f"{tag}: ids"
+        assert d.tobytes() == z[f"dist_{key}"].tobytes(), f"{tag}: distances"
+        assert e.get_last_submitted_count() == int(z[f"cand_{key}"].sum())
+    e.close()
+
+
+def _synthetic(n, dim, nlist, nq, seed, sigma=0.25):
+    from coraanns_b200 import builder
+    rng = np.random.default_rng(seed)
+    centres = rng.normal(size=(nlist, dim)).astype(np.float32)
+    lab = rng.integers(0, nlist, n)
+    data = (centres[lab] + sigma * rng.normal(size=(n, dim))).astype(np.float32)
+    q = (centres[rng.integers(0, nlist, nq)] + sigma * rng.normal(size=(nq, dim))).astype(np.float32)
+    sd = builder.build_index(data, centres, lab, seed=seed)
+    return sd, q
+
+
+@pytest.mark.parametrize("n,dim,nlist,nq,k,nprobe,van", [
+    (200_000, 96, 256, 256, 10, 16, 5),
+    (200_000, 96, 256, 64, 100, 24, 5),
+    (60_000, 768, 64, 48, 10, 8, 5),
+    (100_000, 128, 128, 300, 10, 32, 0),
+])
+def test_live_oracle_parity_larger(cb, n, dim, nlist, nq, k, nprobe, van):
+    """Bit-exact parity with the oracle on indexes larger than the fixtures (more tiles per
+    cluster, more pairs per item, D = 768)."""
+    sd, q = _synthetic(n, dim, nlist, nq, seed=n + dim)
+    o = po.OracleIndex(sd)
+    ref = o.search(q, k, nprobe, vanguard=van, with_details=True,
+                   cand_cap=0)
+    e = _engine(cb, sd=sd, nq=nq, k=k, nprobe=nprobe, vanguard=van)
+    e.reset_buffer(q)
+    d, i = e.search(q, k, nprobe)
+    _check_stages(e, q, k, nprobe, ref, f"synthetic n{n} d{dim}")
+    assert np.array_equal(i, ref["ids"])
+    assert d.tobytes() == ref["dist"].tobytes()
+    e.close()
+
+
+def test_candidate_sets_identical(cb, golden):
+    """L3: with fixed thresholds the candidate set {v : low(v) < T} is identical."""
+    path, z = golden["demo"]
+    q = z["queries"][:16]
+    o = po.oracle_from_file(path)
+    e = _engine(cb, path=path, nq=16, k=10, nprobe=8)
+    t = np.full(16, 40.0, np.float32)
+    e.reset_buffer(q)
+    e.seed_thresholds(t)
+    e.search(q, 10, 8)
+    got = e.debug("cand_gids", 16)
+    cap = got.shape[1]
+    ref = o.search(q, 10, 8, vanguard=5, thresholds=t, with_details=True, cand_cap=cap)
+    assert np.array_equal(got, ref["cand_gids"])
+    e.close()
+
+
+def test_device_entry_point_matches_host(cb, golden):
+    """cora_search_device on device buffers returns what cora_search returns."""
+    import torch
+    path, z = golden["d96"]
+    q = z["queries"]
+    e = _engine(cb, path=path, nq=len(q), k=10, nprobe=6)
+    e.reset_buffer(q)
+    d_h, i_h = e.search(q, 10, 6)
+    dq = torch.from_numpy(q).cuda()
+    dd = torch.empty((len(q), 10), dtype=torch.float32, device="cuda")
+    di = torch.empty((len(q), 10), dtype=torch.int32, device="cuda")
+    e.reset_buffer(q)
+    torch.cuda.synchronize()
+    e.search_device(dq.data_ptr(), len(q), 10, 6, dd.data_ptr(), di.data_ptr())
+    e.check_device()
+    assert dd.cpu().numpy().tobytes() == d_h.tobytes()
+    assert np.array_equal(di.cpu().numpy().view(np.uint32), i_h)
+    e.close()

@@ -1,0 +1,162 @@
+"""CPU tests: the oracle pinned against the reference's own outputs and known answers.
+
+These never touch a GPU. They establish that oracle/cora_oracle.c restates the reference
+path faithfully before any CUDA result is compared against it.
+"""
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import pytest
+
+import py_oracle as po
+from conftest import GOLDEN_NAMES, kat_fixture, regen_base
+
+SD_KEYS = ("centroids", "rotator", "short_data", "short_factors", "long_codes", "ex_factors",
+           "ids", "sizes")
+
+
+@pytest.mark.parametrize("name", GOLDEN_NAMES)
+def test_searchdata_restatement_matches_reference_hashes(golden, name):
+    """L0 layout: the numpy restatement of src/index/search_data.cpp:45-123 reproduces the
+    reference adapter's arrays byte for byte (hashes recorded from the compiled reference)."""
+    path, z = golden[name]
+    sd = po.search_data(po.read_ivf_file(path))
+    got = [hashlib.sha256(np.ascontiguousarray(sd[k]).tobytes()).hexdigest() for k in SD_KEYS]
+    assert got == list(z["sd_sha"])
+
+
+@pytest.mark.parametrize("name", GOLDEN_NAMES)
+def test_oracle_reproduces_golden_outputs(golden, name):
+    """The oracle is deterministic: rerunning it gives the committed outputs bit for bit."""
+    path, z = golden[name]
+    o = po.oracle_from_file(path)
+    for k, nprobe, van in z["grid"]:
+        tag = f"k{k}_np{nprobe}_v{van}"
+        det = o.search(z["queries"], int(k), int(nprobe), vanguard=int(van), with_details=True)
+        assert np.array_equal(det["ids"], z[f"ids_{tag}"]), tag
+        assert det["dist"].tobytes() == z[f"dist_{tag}"].tobytes(), tag
+        assert np.array_equal(det["cand_count"], z[f"cand_{tag}"]), tag
+        assert det["thresholds1"].tobytes() == z[f"t1_{tag}"].tobytes(), tag
+        assert np.array_equal(det["probe_ids"], z[f"probe_{tag}"]), tag
+
+
+@pytest.mark.parametrize("name", GOLDEN_NAMES)
+def test_ex_code_inner_product_matches_reference_decoder(golden, name):
+    """The oracle's 8-bit-code inner product minus 128*<q',b> equals the reference's
+    ip64_fxu7_avx (third_party/.../utils/space.hpp:677-762) on recorded pairs (fp32 sums in
+    the reference vs fp64 here: 1e-4 relative)."""
+    path, z = golden[name]
+    sd = po.search_data(po.read_ivf_file(path))
+    D = int(sd["D"])
+    W = D // 32
+    lc = D * 7 // 8
+    codes = sd["long_codes"].reshape(-1, lc)
+    starts = np.concatenate([[0], np.cumsum(sd["sizes"].astype(np.int64))])
+    for (qi, gid), ref_ip in zip(z["ex_pairs"], z["ex_ref_ip"]):
+        c = int(np.searchsorted(starts, gid, side="right") - 1)
+        s, n = int(starts[c]), int(sd["sizes"][c])
+        words = np.array([sd["short_data"][s * W + w * n + (gid - s)] for w in range(W)], np.uint32)
+        bits = np.array([(words[j // 32] >> (31 - j % 32)) & 1 for j in range(D)], np.float64)
+        x = z["qr"][qi]
+        total = po.lib().cora_oracle_ip_total(np.ascontiguousarray(x), words, codes[gid].copy(), D)
+        ip2 = total - 128.0 * float((x.astype(np.float64) * bits).sum())
+        assert abs(ip2 - float(ref_ip)) <= 1e-4 * max(1.0, abs(float(ref_ip))) * 4
+
+
+@pytest.mark.parametrize("name", GOLDEN_NAMES)
+def test_recall_on_par_with_reference_cpu(golden, name):
+    """L5: distance-aware recall@k of the oracle's answers is at least the reference CPU
+    search's (the rabitq_cpu loop, recorded) minus 0.02 at every recorded grid point."""
+    path, z = golden[name]
+    base = regen_base(z["meta"], z["gen"])
+    gt = z["gt_ids"]
+    assert np.array_equal(po.exact_knn(base, z["queries"][:4], 10)[0], gt[:4, :10])
+    for k, nprobe, van in z["grid"]:
+        tag = f"k{k}_np{nprobe}_v{van}"
+        mine = po.distance_recall(base, z["queries"], gt, z[f"ids_{tag}"], int(k))
+        ref = po.distance_recall(base, z["queries"], gt, z[f"refcpu_k{k}_np{nprobe}"], int(k))
+        assert mine >= ref - 0.02, (tag, mine, ref)
+
+
+def test_query_prep_matches_reference_formulas(golden):
+    """query_kernels.cuh:117-189: planes reconstruct qint exactly; width = amax / 127."""
+    _, z = golden["demo"]
+    o = po.oracle_from_file(golden["demo"][0])
+    prep = o.query_prep(z["qr"])
+    qint = prep["qint"]
+    assert qint.min() >= -128 and qint.max() <= 127
+    amax = np.abs(z["qr"]).max(1)
+    assert np.array_equal(prep["width"], np.maximum(amax / np.float32(127), np.float32(1e-30)))
+    D = z["qr"].shape[1]
+    for q in range(4):
+        rec = np.zeros(D, np.int64)
+        for b in range(8):
+            for j in range(D):
+                bit = (prep["planes"][q, b, j // 32] >> (31 - j % 32)) & 1
+                rec[j] += int(bit) << b
+        rec = np.where(rec >= 128, rec - 256, rec)
+        assert np.array_equal(rec, qint[q])
+    assert np.array_equal(prep["planes"], z["planes"])
+
+
+# ------------------------------------------------------------------------------------
+# known-answer tests of the reference's GPU suite, run on the oracle
+# ------------------------------------------------------------------------------------
+@pytest.mark.parametrize("vanguard", [0, 5])
+def test_kat_exact_ids_and_payloads(vanguard):
+    """gpu_cpu_ring_queue_test.cpp:67-98: every vector is a candidate (count n*N), ids are
+    the smallest f_add_ex, distances = f_add_ex + ||q||^2 within 1e-4."""
+    sd, q, expected = kat_fixture()
+    o = po.OracleIndex(sd)
+    det = o.search(q, 100, 8, vanguard=vanguard, with_details=True)
+    assert det["cand_count"].tolist() == [32768] * 5
+    for a in range(5):
+        assert np.array_equal(np.sort(det["ids"][a]), expected)
+        qn = np.float32(0)
+        for d in range(96):
+            qn = np.float32(qn + q[a, d] * q[a, d])
+        exp = sd["ex_factors"][det["ids"][a], 0] + qn
+        assert np.abs(det["dist"][a] - exp).max() < 1e-4
+
+
+def test_kat_empty_results_are_flt_max():
+    """gpu_cpu_ring_queue_test.cpp:148-167: f_add = FLT_MAX -> no candidates, FLT_MAX out."""
+    sd, q, _ = kat_fixture(f_add=np.finfo(np.float32).max)
+    det = po.OracleIndex(sd).search(q, 100, 8, with_details=True)
+    assert det["cand_count"].sum() == 0
+    assert np.all(det["dist"] == np.finfo(np.float32).max) and np.all(det["ids"] == 0)
+
+
+def test_kat_seeded_negative_thresholds_reject_everything():
+    """gpu_cpu_ring_queue_test.cpp:192-199: thresholds seeded to -FLT_MAX -> 0 candidates."""
+    sd, q, _ = kat_fixture()
+    t = np.full(5, -np.finfo(np.float32).max, np.float32)
+    det = po.OracleIndex(sd).search(q, 100, 8, thresholds=t, with_details=True)
+    assert det["cand_count"].sum() == 0
+
+
+@pytest.mark.parametrize("k", [10, 100, 513, 1024])
+def test_kat_highk_vanguard_on_off_agree(k):
+    """gpu_cpu_highk_vanguard_test.cpp:146-183: vanguard on/off and chunking give identical
+    ids and distances; ids are the k smallest f_add_ex."""
+    sd, q, _ = kat_fixture(topk=k)
+    o = po.OracleIndex(sd)
+    d0, i0 = o.search(q, k, 8, vanguard=0)
+    d5, i5 = o.search(q, k, 8, vanguard=5)
+    d2, i2 = o.search(q[:2], k, 8, vanguard=5)
+    assert np.array_equal(i0, i5) and d0.tobytes() == d5.tobytes()
+    assert np.array_equal(i2, i5[:2]) and d2.tobytes() == d5[:2].tobytes()
+    order = np.argsort(sd["ex_factors"][:, 0], kind="stable")[:k]
+    assert np.array_equal(np.sort(i0[0]), np.sort(order.astype(np.uint32)))
+
+
+@pytest.mark.skipif(not po.ref_available(), reason="reference harness not built here")
+def test_searchdata_restatement_matches_live_reference(golden):
+    """Same as the hash test, against the compiled reference adapter run live."""
+    path, _ = golden["d96"]
+    rsd = po.RefIVF(path).search_data()
+    sd = po.search_data(po.read_ivf_file(path))
+    for k in SD_KEYS:
+        assert np.asarray(sd[k]).tobytes() == np.asarray(rsd[k]).tobytes(), k
