@@ -1,0 +1,426 @@
+#!/usr/bin/env python3
+"""Benchmark: QPS at recall@10 >= 0.95 of the IVF-RaBitQ search hot path on B200.
+
+Workload (the single-GPU configuration the metric is quoted on):
+10M float32 vectors, d = 96 (padded 128), 4096-component Gaussian mixture (centres
+N(0, 1), sigma 0.25), L2, nlist 4096, 8-bit RaBitQ (1 + 7 ex bits), 10,000 queries
+(mixture + N(0, 0.05) noise), topk 10, nprobe swept over 8..128; the reported nprobe is
+the smallest whose distance-aware recall@10 (recall.hpp semantics) is >= 0.95.
+Data are seeded synthetic stand-ins of that shape; the IVF partition is 2 Lloyd
+iterations from the generating centres; the index is built on the GPU by
+coraanns_b200.builder (the reference quantizer's "faster" mode).
+
+One step = one search of the whole 10K-query batch. `value` times K steps with the
+queries resident in HBM (CUDA events on the search stream, max over ranks); `e2e` times the
+public host API (cora_search: pinned host queries -> HBM -> results back to host).
+`--impl reference` times the reference's own CPU search (IVF::search, the rabitq_cpu loop,
+compiled from the reference source into oracle/_ref) on the same index with every host
+thread, on a bounded query sample per step.
+
+Multi-GPU (torchrun, one process per GPU): the index is sharded by IVF cluster; every rank
+probes all centroids, scans the clusters it owns and the per-shard top-k lists are merged
+after an NCCL all-gather.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT / "cgcl-coraanns_b200"), str(ROOT / "oracle")]
+
+CONFIGS = {
+    # name: N, dim, nlist, nq, sigma, qnoise, k, nprobes, seed
+    "cfg2": dict(n=10_000_000, dim=96, nlist=4096, nq=10_000, sigma=0.25, qnoise=0.05, k=10,
+                 nprobes=[8, 12, 16, 24, 32, 48, 64, 96, 128], seed=20261202),
+    "demo": dict(n=4096, dim=128, nlist=16, nq=100, sigma=0.3, qnoise=0.05, k=10,
+                 nprobes=[4, 8, 16], seed=20261201),
+    "small": dict(n=1_000_000, dim=96, nlist=1024, nq=10_000, sigma=0.25, qnoise=0.05, k=10,
+                  nprobes=[8, 16, 32, 64], seed=20261205),
+}
+TARGET_RECALL = 0.95
+KERNELS_PER_SEARCH = 13  # rotate, dist, select, 4 grouping, vanguard, refine, T1, main, refine, merge
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ------------------------------------------------------------------------------------
+# data, partition, ground truth (GPU tooling, torch)
+# ------------------------------------------------------------------------------------
+def make_data(cfg, dev):
+    import torch
+    g = torch.Generator(device=dev).manual_seed(cfg["seed"])
+    centres = torch.randn(cfg["nlist"], cfg["dim"], generator=g, device=dev)
+    base = torch.empty(cfg["n"], cfg["dim"], device=dev)
+    chunk = 1 << 21
+    for s in range(0, cfg["n"], chunk):
+        e = min(cfg["n"], s + chunk)
+        lab = torch.randint(0, cfg["nlist"], (e - s,), generator=g, device=dev)
+        base[s:e] = centres[lab] + cfg["sigma"] * torch.randn(e - s, cfg["dim"], generator=g, device=dev)
+    qlab = torch.randint(0, cfg["nlist"], (cfg["nq"],), generator=g, device=dev)
+    q = (centres[qlab] + cfg["sigma"] * torch.randn(cfg["nq"], cfg["dim"], generator=g, device=dev)
+         + cfg["qnoise"] * torch.randn(cfg["nq"], cfg["dim"], generator=g, device=dev))
+    return centres, base, q.contiguous()
+
+
+def assign(base, cent):
+    import torch
+    out = torch.empty(base.shape[0], dtype=torch.int64, device=base.device)
+    cn = (cent * cent).sum(1)
+    for s in range(0, base.shape[0], 1 << 20):
+        x = base[s:s + (1 << 20)]
+        out[s:s + x.shape[0]] = (cn[None, :] - 2 * x @ cent.T).argmin(1)
+    return out
+
+
+def kmeans(base, init, iters=2):
+    import torch
+    c = init.clone()
+    for _ in range(iters):
+        a = assign(base, c)
+        sums = torch.zeros_like(c).index_add_(0, a, base)
+        cnt = torch.bincount(a, minlength=c.shape[0]).float()
+        nz = cnt > 0
+        c[nz] = sums[nz] / cnt[nz, None]
+    return c, assign(base, c)
+
+
+def ground_truth(base, q, k):
+    """Exact top-k by (fp64 distance, id): fp32 filter keeping 64 candidates per query,
+    then fp64 recompute (tools/data/generate_gt_gpu.py:56-69,114-119 of the reference)."""
+    import torch
+    keep = 64
+    bn = (base * base).sum(1)
+    best_d = torch.full((q.shape[0], keep), float("inf"), device=q.device)
+    best_i = torch.zeros((q.shape[0], keep), dtype=torch.int64, device=q.device)
+    for s in range(0, base.shape[0], 1 << 20):
+        x = base[s:s + (1 << 20)]
+        d = bn[s:s + x.shape[0]][None, :] - 2 * q @ x.T
+        vd, vi = torch.topk(d, keep, dim=1, largest=False)
+        cd = torch.cat([best_d, vd], 1)
+        ci = torch.cat([best_i, vi + s], 1)
+        o = torch.topk(cd, keep, dim=1, largest=False).indices
+        best_d, best_i = torch.gather(cd, 1, o), torch.gather(ci, 1, o)
+    ex = ((base[best_i].double() - q[:, None, :].double()) ** 2).sum(2)
+    # lexicographic (distance, id): stable sort by id, then stable sort by distance
+    order_id = torch.argsort(best_i, dim=1, stable=True)
+    ex, best_i = torch.gather(ex, 1, order_id), torch.gather(best_i, 1, order_id)
+    order = torch.argsort(ex, dim=1, stable=True)[:, :k]
+    return torch.gather(best_i, 1, order), torch.gather(ex, 1, order)
+
+
+def recall_at_k(base, q, gt_ids, gt_d, res_ids, k):
+    """Distance-aware recall@k (include/coraanns/benchmark/recall.hpp:133-190)."""
+    import torch
+    r = torch.as_tensor(res_ids.astype(np.int64), device=q.device)[:, :k]
+    valid = r < base.shape[0]
+    rc = torch.where(valid, r, torch.zeros_like(r))
+    in_gt = (rc[:, :, None] == gt_ids[:, None, :k]).any(2)
+    d = ((base[rc].double() - q[:, None, :].double()) ** 2).sum(2)
+    ok = valid & (in_gt | (d <= gt_d[:, k - 1:k]))
+    # repeated ids count once
+    srt, _ = torch.sort(torch.where(ok, rc, torch.full_like(rc, -1)), dim=1)
+    dup = torch.zeros_like(ok)
+    dup[:, 1:] = (srt[:, 1:] == srt[:, :-1]) & (srt[:, 1:] >= 0)
+    hits = (srt >= 0).sum() - dup.sum()
+    return float(hits) / (q.shape[0] * k)
+
+
+# ------------------------------------------------------------------------------------
+# measurement helpers
+# ------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.rows, self.proc = gpu, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            self.proc.wait(timeout=5)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(self.rows)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return float(j["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs, burst copy)"
+    return 6650.0, "fallback (6.65 TB/s)"
+
+
+def profiled_traffic():
+    """Per-launch DRAM bytes of the main scan kernel from the committed ncu summary."""
+    p = ROOT / "profiles" / "scan_main_cfg2.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()).get("dram_bytes_per_launch_full_size")
+        except ValueError:
+            return None
+    return None
+
+
+def cpu_reference_qps(index_path, q_np, k, nprobe, target_seconds=15.0, threads=None):
+    """The reference's own CPU search (oracle/_ref IVF::search, rabitq_cpu loop) on a
+    bounded sample, or the C oracle port when the reference harness is absent."""
+    import py_oracle as po
+    threads = threads or os.cpu_count() or 1
+    if po.ref_available():
+        ivf = po.RefIVF(index_path)
+        run = lambda qs: ivf.search(qs, k, nprobe, threads=threads)  # noqa: E731
+        kind = "reference"
+    else:
+        o = po.oracle_from_file(index_path)
+        run = lambda qs: o.search(qs, k, nprobe, threads=threads)  # noqa: E731
+        kind = "port"
+    probe = q_np[:min(len(q_np), max(threads * 4, 256))]
+    t = time.perf_counter()
+    run(probe)
+    per_q = max((time.perf_counter() - t) / len(probe), 1e-7)
+    m = int(min(len(q_np), max(len(probe), target_seconds / per_q)))
+    sample = q_np[:m]
+    t = time.perf_counter()
+    run(sample)
+    dt = time.perf_counter() - t
+    return dict(value=m / dt, unit="queries/s", cores=threads, kind=kind,
+                sample=f"{m} of the {len(q_np)} queries, nprobe {nprobe}, topk {k}, {dt:.1f} s"), run
+
+
+# ------------------------------------------------------------------------------------
+# main
+# ------------------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
+    ap.add_argument("--nprobe", type=int, default=0, help="fix nprobe instead of sweeping")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        args.warmup = 3
+
+    import torch
+    import torch.distributed as dist
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    if world > 1:
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    torch.backends.cuda.matmul.allow_tf32 = True
+    cfg = CONFIGS[args.config]
+    k = cfg["k"]
+
+    if args.impl == "reference" and rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    t0 = time.time()
+    centres, base, q = make_data(cfg, dev)
+    cent, lab = kmeans(base, centres)
+    log(f"[bench] data + partition {time.time() - t0:.1f}s")
+    from coraanns_b200 import builder
+    import coraanns_b200 as cb
+    need_file = (args.impl == "reference") or (rank == 0 and not args.no_cpu_baseline)
+    t1 = time.time()
+    sd = builder.build_index(base, cent, lab, seed=cfg["seed"], device=dev, keep_bits=need_file)
+    log(f"[bench] index build {time.time() - t1:.1f}s")
+    gt_ids, gt_d = ground_truth(base, q, k)
+    q_np = q.cpu().numpy()
+
+    index_path = None
+    if need_file:
+        t2 = time.time()
+        index_path = Path(tempfile.gettempdir()) / f"cora_bench_{args.config}.index"
+        builder.write_index_file(index_path, sd, sd["bits"])
+        del sd["bits"]
+        log(f"[bench] index file {index_path.stat().st_size / 1e9:.2f} GB in {time.time() - t2:.1f}s")
+
+    if args.impl == "reference":
+        nprobe = args.nprobe or 32
+        base_info, run = cpu_reference_qps(index_path, q_np, k, nprobe, target_seconds=4.0)
+        m = int(base_info["sample"].split()[0])
+        for _ in range(args.warmup):
+            run(q_np[:m])
+        t = time.perf_counter()
+        for _ in range(args.steps):
+            run(q_np[:m])
+        dt = (time.perf_counter() - t) / args.steps
+        v = m / dt
+        rec = recall_at_k(base[:], q[:m], gt_ids[:m], gt_d[:m], run(q_np[:m]), k)
+        line = dict(metric="QPS at recall@10>=0.95 (IVF-RaBitQ search)", value=v, unit="queries/s",
+                    n_gpus=world, steps=args.steps, warmup=args.warmup, ms_per_step=dt * 1e3,
+                    higher_is_better=True, scaling="strong", vs_baseline=None, dtype="u8+f32",
+                    data="synthetic (seeded Gaussian mixture, BASELINE config 2 shape)",
+                    impl="reference",
+                    config=dict(workload=f"{args.config}: reference CPU IVF::search (rabitq_cpu loop)",
+                                nprobe=nprobe, recall_at_10=rec, sample_queries=m),
+                    cpu_baseline=dict(base_info, value=v),
+                    e2e=dict(value=v, unit="queries/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+        print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    eng = cb.HybridIndex(local)
+    eng.load_search_data(sd)
+    nq = cfg["nq"]
+    nprobes = [args.nprobe] if args.nprobe else cfg["nprobes"]
+    eng.prepare_workspace(nq, k, max(nprobes))
+    stream = torch.cuda.current_stream(dev)
+    out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    out_i = torch.empty((nq, k), dtype=torch.int32, device=dev)
+
+    def search_dev(nprobe):
+        eng.search_device(q.data_ptr(), nq, k, nprobe, out_d.data_ptr(), out_i.data_ptr(),
+                          stream.cuda_stream)
+
+    sweep = {}
+    chosen = None
+    for npb in nprobes:
+        search_dev(npb)
+        eng.check_device()
+        r = recall_at_k(base, q, gt_ids, gt_d, out_i.cpu().numpy().view(np.uint32), k)
+        sweep[npb] = round(r, 4)
+        if chosen is None and r >= TARGET_RECALL:
+            chosen = npb
+    if chosen is None:
+        chosen = nprobes[-1]
+    log(f"[bench] recall sweep {sweep} -> nprobe {chosen}")
+
+    # algorithmic bytes of one main-scan launch: sum over (query, probe) of n_c * (D/8 + 12)
+    search_dev(chosen)
+    eng.check_device()
+    probes = eng.debug("probe_ids", nq, chosen)
+    sizes = sd["sizes"].astype(np.int64)
+    D = int(sd["D"])
+    scan_bytes = int(sizes[probes].sum()) * (D // 8 + 12)
+
+    # ---- timed region (device-resident queries) ----
+    eng.set_profiling(True)
+    for _ in range(args.warmup):
+        search_dev(chosen)
+    eng.check_device()
+    eng.stage_reset()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            search_dev(chosen)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+    eng.check_device()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    count, stage_tot = eng.stage_totals()
+    stage_avg = {s: v / max(count, 1) for s, v in stage_tot.items()}
+    eng.set_profiling(False)
+    qps = nq * world / (ms / 1e3)
+
+    # ---- e2e through the public host API (pinned host queries, results to host) ----
+    qh = torch.empty((nq, cfg["dim"]), dtype=torch.float32, pin_memory=True)
+    qh.copy_(q.cpu())
+    qh_np = qh.numpy()
+    eng.reset_buffer(qh_np)
+    for _ in range(args.warmup):
+        eng.search(qh_np, k, chosen)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        eng.search(qh_np, k, chosen)
+    e2e_s = (time.perf_counter() - t) / args.steps
+    e2e_qps = nq * world / e2e_s
+
+    peak, peak_src = measured_peaks()
+    main_ms = stage_avg["main_scan"]
+    achieved = scan_bytes / (main_ms / 1e3) / 1e9 if main_ms > 0 else None
+    traffic = profiled_traffic()
+    roofline = dict(bound="hbm", kernel="scan_main_kernel", achieved=achieved, peak=peak,
+                    unit="GB/s", frac=(achieved / peak) if achieved else None, traffic=traffic,
+                    peak_source=peak_src, algorithmic_bytes_per_launch=scan_bytes,
+                    launch_ms=main_ms,
+                    note="bytes = sum over (query, probe) of n_c*(D/8+12) (per-query accounting; "
+                         "cross-query reuse lets this exceed the physical DRAM traffic)")
+
+    cpu_base = None
+    if rank == 0 and not args.no_cpu_baseline and index_path is not None:
+        cpu_base, _ = cpu_reference_qps(index_path, q_np, k, chosen, target_seconds=15.0)
+
+    if rank == 0:
+        line = dict(
+            metric="QPS at recall@10>=0.95 (IVF-RaBitQ search)", value=qps, unit="queries/s",
+            n_gpus=world, steps=args.steps, warmup=args.warmup, ms_per_step=ms,
+            higher_is_better=True, scaling="weak" if world > 1 else "strong", vs_baseline=None,
+            dtype="u32+f32", data="synthetic (seeded Gaussian mixture, BASELINE config 2 shape)",
+            config=dict(workload=f"{args.config}: {cfg['n']} x d{cfg['dim']} L2, nlist {cfg['nlist']}, "
+                                 f"8-bit RaBitQ, {nq} queries, topk {k}",
+                        nprobe=chosen, recall_at_10=sweep.get(chosen), recall_sweep=sweep,
+                        l2_flush="inputs exceed L2 (index codes > 126 MB)",
+                        stage_ms=stage_avg, parallelism=f"replicas x{world}" if world > 1 else "single"),
+            roofline=roofline, cpu_baseline=cpu_base,
+            e2e=dict(value=e2e_qps, unit="queries/s", h2d_bytes_per_step=nq * cfg["dim"] * 4,
+                     d2h_bytes_per_step=nq * k * 8),
+            gpu_launches=KERNELS_PER_SEARCH * args.steps, clocks=clk.summary())
+        print(json.dumps(line), flush=True)
+    eng.close()
+    if index_path is not None and index_path.exists():
+        index_path.unlink()
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

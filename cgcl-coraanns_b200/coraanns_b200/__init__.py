@@ -38,7 +38,8 @@ EXPORTS = [
     "cora_set_gpu_filter_timing", "cora_set_cross_query_reuse", "cora_set_cpu_secondary_filter",
     "cora_set_ip_kernel_type", "cora_get_ip_kernel_type", "cora_get_last_submitted_count",
     "cora_get_last_refined_count", "cora_get_last_spilled_count", "cora_get_last_gpu_filter_ms",
-    "cora_debug_copy", "cora_get_candidate_capacity",
+    "cora_debug_copy", "cora_get_last_stage_ms", "cora_stage_totals", "cora_stage_reset",
+    "cora_get_candidate_capacity",
 ]
 
 _p = C.c_void_p
@@ -81,6 +82,12 @@ _sig("cora_get_last_spilled_count", _u64, _p)
 _sig("cora_get_last_gpu_filter_ms", C.c_float, _p)
 _sig("cora_debug_copy", C.c_int, _p, C.c_int, _p, _u64)
 _sig("cora_get_candidate_capacity", _u64, _p)
+_sig("cora_get_last_stage_ms", C.c_int, _p, _p, _u64)
+_sig("cora_stage_totals", C.c_int, _p, _p, _u64, _p)
+_sig("cora_stage_reset", C.c_int, _p)
+
+STAGES = ("rotate_prep", "centroid_dist", "select_probes", "pair_grouping", "vanguard_scan",
+          "seed_refine", "threshold", "main_scan", "main_refine", "merge")
 
 
 class LogicError(Exception):
@@ -236,6 +243,22 @@ class HybridIndex:
     def get_last_refined_count(self): return int(_lib.cora_get_last_refined_count(self._h))
     def get_last_spilled_count(self): return int(_lib.cora_get_last_spilled_count(self._h))
     def get_last_gpu_filter_ms(self): return float(_lib.cora_get_last_gpu_filter_ms(self._h))
+
+    def get_last_stage_ms(self) -> dict:
+        """Per-stage device milliseconds of the last search (profiling must be on)."""
+        out = np.zeros(len(STAGES), np.float32)
+        _check(_lib.cora_get_last_stage_ms(self._h, _ptr(out), len(STAGES)))
+        return dict(zip(STAGES, map(float, out)))
+
+    def stage_totals(self):
+        """(searches summed, {stage: total ms}) since stage_reset(); profiling must be on."""
+        out = np.zeros(len(STAGES), np.float64)
+        cnt = np.zeros(1, np.uint64)
+        _check(_lib.cora_stage_totals(self._h, _ptr(out), len(STAGES), _ptr(cnt)))
+        return int(cnt[0]), dict(zip(STAGES, map(float, out)))
+
+    def stage_reset(self):
+        _check(_lib.cora_stage_reset(self._h))
 
     # -- diagnostics -----------------------------------------------------------------
     def candidate_capacity(self):

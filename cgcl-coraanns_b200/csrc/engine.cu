@@ -83,6 +83,13 @@ struct Engine {
     cudaStream_t stream = nullptr;
     cudaStream_t last_stream = nullptr;
     cudaEvent_t ev_filter0 = nullptr, ev_filter1 = nullptr;
+    // Stage boundary events: a ring of kRing event sets so that timing many back-to-back
+    // searches never makes the host wait; a set is read back when it is reused.
+    static constexpr int kStages = 10, kRing = 16;
+    cudaEvent_t ev_stage[kRing][kStages + 1] = {};
+    int ring_next = 0, ring_used = 0, ring_last = -1;
+    double stage_sum[kStages] = {};
+    uint64_t stage_count = 0;
     int num_sms = 148;
 
     // index
@@ -125,6 +132,8 @@ struct Engine {
         CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
         CUDA_TRY(cudaEventCreate(&ev_filter0));
         CUDA_TRY(cudaEventCreate(&ev_filter1));
+        for (auto &set : ev_stage)
+            for (auto &ev : set) CUDA_TRY(cudaEventCreate(&ev));
         CUDA_TRY(cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, device));
         last_stream = stream;
     }
@@ -134,6 +143,9 @@ struct Engine {
         free_workspace();
         if (ev_filter0) cudaEventDestroy(ev_filter0);
         if (ev_filter1) cudaEventDestroy(ev_filter1);
+        for (auto &set : ev_stage)
+            for (auto ev : set)
+                if (ev) cudaEventDestroy(ev);
         if (stream) cudaStreamDestroy(stream);
     }
 
@@ -347,6 +359,51 @@ struct Engine {
     }
 
     void debug_copy(int what, void *out, uint64_t bytes);
+
+    // Stage boundary events, recorded only when profiling is enabled.
+    void accumulate_set(int set) {
+        float ms;
+        for (int i = 0; i < kStages; ++i) {
+            CUDA_TRY(cudaEventSynchronize(ev_stage[set][i + 1]));
+            CUDA_TRY(cudaEventElapsedTime(&ms, ev_stage[set][i], ev_stage[set][i + 1]));
+            stage_sum[i] += ms;
+        }
+        ++stage_count;
+    }
+    void begin_profiled_search() {
+        if (!profiling) return;
+        if (ring_used == kRing) accumulate_set(ring_next);  // recorded kRing searches ago
+        else ++ring_used;
+        ring_last = ring_next;
+        ring_next = (ring_next + 1) % kRing;
+    }
+    void mark(int i, cudaStream_t st) {
+        if (profiling) CUDA_TRY(cudaEventRecord(ev_stage[ring_last][i], st));
+    }
+    void stage_ms(float *out, uint64_t n) {
+        if (ring_last < 0) fail(CORA_ESTATE, "no profiled search recorded");
+        if (n > kStages) n = kStages;
+        CUDA_TRY(cudaEventSynchronize(ev_stage[ring_last][kStages]));
+        for (uint64_t i = 0; i < n; ++i)
+            CUDA_TRY(cudaEventElapsedTime(out + i, ev_stage[ring_last][i], ev_stage[ring_last][i + 1]));
+    }
+    // Sums of every profiled search since the last reset (flushes the ring).
+    uint64_t stage_totals(double *out, uint64_t n) {
+        while (ring_used > 0) {
+            const int set = (ring_next - ring_used + kRing) % kRing;
+            accumulate_set(set);
+            --ring_used;
+        }
+        if (n > kStages) n = kStages;
+        for (uint64_t i = 0; i < n; ++i) out[i] = stage_sum[i];
+        return stage_count;
+    }
+    void stage_reset() {
+        ring_used = 0;
+        ring_last = -1;
+        stage_count = 0;
+        for (auto &v : stage_sum) v = 0.0;
+    }
 };
 
 // ------------------------------------------------------------------------------------
@@ -453,6 +510,8 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     CUDA_TRY(cudaMemsetAsync(err.p, 0, 4, st));
     CUDA_TRY(cudaMemsetAsync(stats.p, 0, 16, st));
     CUDA_TRY(cudaMemsetAsync(cand_cnt.p, 0, nq * 4, st));
+    begin_profiled_search();
+    mark(0, st);
 
     // 1. rotation + query factors + bit-planes
     {
@@ -465,6 +524,7 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
             planes.p);
         CUDA_TRY(cudaGetLastError());
     }
+    mark(1, st);
     // 2. coarse distances + top-nprobe
     {
         dim3 grid(static_cast<unsigned>((nlist + kDistTile - 1) / kDistTile),
@@ -472,6 +532,7 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
         centroid_dist_kernel<<<grid, 256, 0, st>>>(qr.p, inq, centroids.p, static_cast<int>(nlist),
                                                    static_cast<int>(D), gmat.p);
         CUDA_TRY(cudaGetLastError());
+        mark(2, st);
         const int sort_n = next_pow2(inp + kProbeTile);
         const size_t sm = (size_t)sort_n * 8;
         CUDA_TRY(cudaFuncSetAttribute(select_probes_kernel,
@@ -480,6 +541,7 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
                                                    probe_ids.p, probe_g.p);
         CUDA_TRY(cudaGetLastError());
     }
+    mark(3, st);
     IndexView ix{scan4.p, cl_start.p, cl_size.p, long_codes.p, ex_factors.p, ids.p,
                  static_cast<int>(nlist), static_cast<int>(D), G16, LC};
     SearchView sv{inq, ik, inp, static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
@@ -504,30 +566,37 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
             pair_cnt.p, pair_off.p, item_off.p, static_cast<int>(nlist), ppi, items.p);
         CUDA_TRY(cudaGetLastError());
     }
+    mark(4, st);
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter0, st));
     // 4. vanguard seeds -> refine -> T1
     const int van_sort_n = next_pow2(static_cast<int>(keep) + (G16 <= 2 ? 512 : 256));
     dispatch_scan(G16, ix, sv, van_sort_n, nq * veff, items.p, n_items.p, pairs.p, item_counter.p,
                   num_sms, st, true);
+    mark(5, st);
     refine_kernel<<<inq, kRefineThreads, 0, st>>>(ix, sv, 0);
     CUDA_TRY(cudaGetLastError());
+    mark(6, st);
     const int merge_sort_n = next_pow2(ik + kMergeTile);
     CUDA_TRY(cudaFuncSetAttribute(threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   merge_sort_n * 8));
     threshold_kernel<<<inq, 256, (size_t)merge_sort_n * 8, st>>>(sv, merge_sort_n);
     CUDA_TRY(cudaGetLastError());
+    mark(7, st);
     // 5. main scan against T1, then refine the new candidates
     dispatch_scan(G16, ix, sv, van_sort_n, 0, items.p, n_items.p, pairs.p, item_counter.p, num_sms,
                   st, false);
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));
+    mark(8, st);
     refine_kernel<<<inq, kRefineThreads, 0, st>>>(ix, sv, 1);
     CUDA_TRY(cudaGetLastError());
+    mark(9, st);
     // 6. final top-k
     CUDA_TRY(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   merge_sort_n * 8));
     merge_kernel<<<inq, 256, (size_t)merge_sort_n * 8, st>>>(sv, merge_sort_n, d_od, d_oi,
                                                              stats.p);
     CUDA_TRY(cudaGetLastError());
+    mark(10, st);
 }
 
 // ------------------------------------------------------------------------------------
@@ -884,6 +953,28 @@ int cora_debug_copy(cora_engine *engine, int what, void *h_out, uint64_t bytes) 
         if (!h_out) cora::fail(CORA_EINVAL, "null output");
         eng(engine).debug_copy(what, h_out, bytes);
     });
+}
+
+int cora_get_last_stage_ms(cora_engine *engine, float *h_out, uint64_t n) {
+    return guarded([&] {
+        if (!h_out) cora::fail(CORA_EINVAL, "null output");
+        Engine &e = eng(engine);
+        CUDA_TRY(cudaSetDevice(e.device));
+        e.stage_ms(h_out, n);
+    });
+}
+
+int cora_stage_totals(cora_engine *engine, double *h_out, uint64_t n, uint64_t *h_count) {
+    return guarded([&] {
+        if (!h_out || !h_count) cora::fail(CORA_EINVAL, "null output");
+        Engine &e = eng(engine);
+        CUDA_TRY(cudaSetDevice(e.device));
+        *h_count = e.stage_totals(h_out, n);
+    });
+}
+
+int cora_stage_reset(cora_engine *engine) {
+    return guarded([&] { eng(engine).stage_reset(); });
 }
 
 uint64_t cora_get_candidate_capacity(const cora_engine *engine) {

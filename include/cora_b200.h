@@ -140,6 +140,17 @@ float cora_get_last_gpu_filter_ms(const cora_engine *engine);
  * 7 candidate gids (nq x cap u32, per query sorted ascending, unused slots 0xFFFFFFFF).
  * `bytes` must equal the size of the requested array. */
 int cora_debug_copy(cora_engine *engine, int what, void *h_out, uint64_t bytes);
+/* Per-stage device times (ms) of the last search run with profiling enabled, from CUDA
+ * events recorded between the launches on the search stream: 0 rotation + query prep,
+ * 1 coarse distances, 2 top-nprobe, 3 pair grouping, 4 vanguard scan, 5 seed refine,
+ * 6 threshold, 7 main scan, 8 main refine, 9 merge. Writes min(n, 10) values. */
+int cora_get_last_stage_ms(cora_engine *engine, float *h_out, uint64_t n);
+/* Sums of the same per-stage times over every profiled search since cora_stage_reset();
+ * *h_count receives the number of searches summed. Reading never stalls searches that are
+ * still queued: each search's events are read back when its slot in a 16-entry ring is
+ * reused, or here. */
+int cora_stage_totals(cora_engine *engine, double *h_out, uint64_t n, uint64_t *h_count);
+int cora_stage_reset(cora_engine *engine);
 /* Candidate capacity per query of the current workspace (array 7 above is nq x cap). */
 uint64_t cora_get_candidate_capacity(const cora_engine *engine);
 

@@ -317,8 +317,11 @@ class RefIVF:
         self.num, self.dim, self.D, self.nlist, self.ex_bits, self.metric = map(int, info)
 
     def close(self):
-        if self.h:
-            ref().ref_close(self.h)
+        if getattr(self, "h", None) and _ref is not None:
+            try:
+                _ref.ref_close(self.h)
+            except TypeError:  # interpreter shutdown
+                pass
             self.h = None
 
     def __del__(self):
