@@ -315,7 +315,11 @@ def main():
     nq = cfg["nq"]
     nprobes = [args.nprobe] if args.nprobe else cfg["nprobes"]
     eng.prepare_workspace(nq, k, max(nprobes))
-    stream = torch.cuda.current_stream(dev)
+    # A dedicated (non-default) stream: the engine enqueues every kernel of a search on it and
+    # the timing events are recorded on it too. torch's default stream is the legacy NULL
+    # stream, which the engine's non-blocking streams do not order against.
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.synchronize()
     out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
     out_i = torch.empty((nq, k), dtype=torch.int32, device=dev)
 

@@ -154,9 +154,12 @@ struct BlockTopK {
         __syncthreads();
         const int n = *n_staged;
         if (n == 0) return;
-        for (int i = S + n + threadIdx.x; i < sort_n; i += blockDim.x) buf[i] = kKeyMax;
+        // Only the occupied prefix is sorted: [S + n, m) is padded with kKeyMax and every
+        // slot at or beyond m already holds kKeyMax.
+        const int m = next_pow2(S + n);
+        for (int i = S + n + threadIdx.x; i < m; i += blockDim.x) buf[i] = kKeyMax;
         __syncthreads();
-        block_bitonic_sort(buf, sort_n);
+        block_bitonic_sort(buf, m);
         if (threadIdx.x == 0) {
             *n_staged = 0;
             const uint64_t t = buf[S - 1];

@@ -113,7 +113,7 @@ struct Engine {
     // workspace
     bool ws_ready = false;
     uint64_t ws_q = 0, ws_k = 0, ws_np = 0, ws_vg = 0, cap = 0;
-    DevBuf<float> raw_q, qr, gmat, probe_g, T0, T1, out_d;
+    DevBuf<float> raw_q, qr, gmat, probe_g, T0, T1, Tcap, out_d;
     DevBuf<QueryScalars> scal;
     DevBuf<uint32_t> planes, cand_cnt, seed_cnt, pair_cnt, pair_off, pair_cur, item_off, pairs,
         n_items, out_i;
@@ -243,6 +243,7 @@ struct Engine {
         probe_g.alloc(max_q * max_np);
         T0.alloc(max_q);
         T1.alloc(max_q);
+        Tcap.alloc(max_q);
         bound.alloc(max_q * std::max<uint64_t>(ws_vg, 1));
         cand_cnt.alloc(max_q);
         seed_cnt.alloc(max_q);
@@ -268,7 +269,7 @@ struct Engine {
     void free_workspace() noexcept {
         ws_ready = false;
         ws_q = ws_k = ws_np = ws_vg = cap = 0;
-        for (auto *b : {&raw_q, &qr, &gmat, &probe_g, &T0, &T1, &out_d}) b->release();
+        for (auto *b : {&raw_q, &qr, &gmat, &probe_g, &T0, &T1, &Tcap, &out_d}) b->release();
         scal.release();
         for (auto *b : {&planes, &cand_cnt, &seed_cnt, &pair_cnt, &pair_off, &pair_cur, &item_off,
                         &pairs, &n_items, &out_i})
@@ -309,6 +310,7 @@ struct Engine {
         CUDA_TRY(cudaMemcpyAsync(raw_q.p, h_q, nq * dim * 4, cudaMemcpyHostToDevice, stream));
         std::fill(h_T0.begin(), h_T0.end(), FLT_MAX);
         CUDA_TRY(cudaMemcpyAsync(T0.p, h_T0.data(), ws_q * 4, cudaMemcpyHostToDevice, stream));
+        CUDA_TRY(cudaMemcpyAsync(Tcap.p, h_T0.data(), ws_q * 4, cudaMemcpyHostToDevice, stream));
         CUDA_TRY(cudaStreamSynchronize(stream));
     }
     void seed_thresholds(const float *in, uint64_t nq) {
@@ -317,12 +319,13 @@ struct Engine {
         CUDA_TRY(cudaSetDevice(device));
         std::copy(in, in + nq, h_T0.begin());
         CUDA_TRY(cudaMemcpyAsync(T0.p, in, nq * 4, cudaMemcpyHostToDevice, stream));
+        CUDA_TRY(cudaMemcpyAsync(Tcap.p, in, nq * 4, cudaMemcpyHostToDevice, stream));
         CUDA_TRY(cudaStreamSynchronize(stream));
     }
     void capture_thresholds(float *out, uint64_t nq) const {
         validate_ws(nq, 1, 1);
         if (!out) fail(CORA_EINVAL, "missing threshold output");
-        CUDA_TRY(cudaMemcpy(out, T0.p, nq * 4, cudaMemcpyDeviceToHost));
+        CUDA_TRY(cudaMemcpy(out, Tcap.p, nq * 4, cudaMemcpyDeviceToHost));
     }
 
     // ---------------------------------------------------------------- search
@@ -545,7 +548,7 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     IndexView ix{scan4.p, cl_start.p, cl_size.p, long_codes.p, ex_factors.p, ids.p,
                  static_cast<int>(nlist), static_cast<int>(D), G16, LC};
     SearchView sv{inq, ik, inp, static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
-                  scal.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, T1.p, bound.p, cand_cnt.p,
+                  scal.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p, cand_cnt.p,
                   seed_cnt.p, cand_rec.p, cand_key.p, err.p};
     const uint8_t *own = owned.n ? owned.p : nullptr;
     // 3. per-cluster grouping of every (query, probe) pair

@@ -114,9 +114,9 @@ __global__ void __launch_bounds__(256) threshold_kernel(SearchView sv, int sort_
 }
 
 // One CTA per query: final top-k by (ex, id) among all refined candidates with ex < T0.
-// Writes distances / ids (padded with FLT_MAX / 0), updates T0 to the k-th distance when k
-// results exist (the state capture_thresholds() reports) and adds the candidate count to
-// stats[0].
+// Writes distances / ids (padded with FLT_MAX / 0), records the query's threshold after the
+// search (its k-th distance when k results exist, else T0; what capture_thresholds()
+// reports) and adds the candidate count to stats[0].
 __global__ void __launch_bounds__(256) merge_kernel(SearchView sv, int sort_n,
                                                     float *__restrict__ out_d,
                                                     uint32_t *__restrict__ out_i,
@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(256) merge_kernel(SearchView sv, int sort_n,
     }
     if (threadIdx.x == 0) {
         const uint64_t kth = smem_k[sv.k - 1];
-        if (kth != kKeyMax) sv.T0[q] = unord_f32(static_cast<uint32_t>(kth >> 32));
+        sv.Tcap[q] = kth != kKeyMax ? unord_f32(static_cast<uint32_t>(kth >> 32)) : T0;
         atomicAdd(stats, static_cast<unsigned long long>(cnt));
     }
 }

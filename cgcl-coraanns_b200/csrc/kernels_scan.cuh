@@ -50,7 +50,8 @@ struct SearchView {
     const float *qr;             // nq x D
     const int *probe_ids;        // nq x nprobe
     const float *probe_g;        // nq x nprobe
-    float *T0;                   // nq (merge_kernel stores the k-th distance back)
+    const float *T0;             // nq, seeded thresholds (never modified by a search)
+    float *Tcap;                 // nq, thresholds after the search (capture_thresholds)
     float *T1;                   // nq
     uint64_t *bound;             // nq x veff
     uint32_t *cand_cnt;          // nq
