@@ -39,7 +39,7 @@ EXPORTS = [
     "cora_set_ip_kernel_type", "cora_get_ip_kernel_type", "cora_get_last_submitted_count",
     "cora_get_last_refined_count", "cora_get_last_spilled_count", "cora_get_last_gpu_filter_ms",
     "cora_debug_copy", "cora_get_last_stage_ms", "cora_stage_totals", "cora_stage_reset",
-    "cora_get_candidate_capacity",
+    "cora_set_vanguard_lows_budget", "cora_get_vanguard_mode", "cora_get_candidate_capacity",
 ]
 
 _p = C.c_void_p
@@ -85,6 +85,8 @@ _sig("cora_get_candidate_capacity", _u64, _p)
 _sig("cora_get_last_stage_ms", C.c_int, _p, _p, _u64)
 _sig("cora_stage_totals", C.c_int, _p, _p, _u64, _p)
 _sig("cora_stage_reset", C.c_int, _p)
+_sig("cora_set_vanguard_lows_budget", C.c_int, _p, _u64)
+_sig("cora_get_vanguard_mode", C.c_int, _p)
 
 STAGES = ("rotate_prep", "centroid_dist", "select_probes", "pair_grouping", "vanguard_scan",
           "seed_refine", "threshold", "main_scan", "main_refine", "merge")
@@ -259,6 +261,13 @@ class HybridIndex:
 
     def stage_reset(self):
         _check(_lib.cora_stage_reset(self._h))
+
+    def set_vanguard_lows_budget(self, nbytes):
+        _check(_lib.cora_set_vanguard_lows_budget(self._h, int(nbytes)))
+
+    def get_vanguard_mode(self):
+        """1: vanguard lower bounds kept in HBM between passes; 0: vanguard rescan."""
+        return int(_lib.cora_get_vanguard_mode(self._h))
 
     # -- diagnostics -----------------------------------------------------------------
     def candidate_capacity(self):

@@ -125,6 +125,88 @@ __host__ __device__ __forceinline__ int next_pow2(int x) {
     return p;
 }
 
+// ---- block-wide radix selection of the S smallest uint64 keys ------------------------
+// Keys are unique (an id sits in the low 32 bits); kKeyMax marks an item filtered out.
+// MSB-first passes over 8-bit digits narrow the prefix of the S-th smallest key, stopping
+// as soon as the digit bucket holding it is taken whole. The selected keys are written to
+// out[0, S) in ascending order (kKeyMax where fewer than S exist). `key_at(i)` yields key i
+// of n; `scratch` is 256 + 3 ints of shared memory; out holds next_pow2(S) keys.
+// All threads of the block must call this function.
+template <typename KeyAt>
+__device__ void block_select_smallest(KeyAt key_at, uint32_t n, int S, uint64_t *out,
+                                      int *scratch) {
+    int *hist = scratch;            // 256 bins
+    int *s_sel = scratch + 256;     // [0] chosen digit, [1] rank in bin / cursor, [2] bin size
+    const int tid = threadIdx.x;
+    const int S2 = next_pow2(S);
+    for (int i = tid; i < S2; i += blockDim.x) out[i] = kKeyMax;
+    uint64_t prefix = 0;            // digits fixed so far
+    int shift = 64;                 // keys match prefix on bits >= shift
+    uint32_t rank = static_cast<uint32_t>(S);  // 1-based rank still to locate
+    bool take_all = n <= static_cast<uint32_t>(S);
+    while (!take_all && shift > 0) {
+        shift -= 8;
+        for (int b = tid; b < 256; b += blockDim.x) hist[b] = 0;
+        __syncthreads();
+        for (uint32_t i = tid; i < n; i += blockDim.x) {
+            const uint64_t k = key_at(i);
+            if (shift + 8 >= 64 || (k >> (shift + 8)) == (prefix >> (shift + 8)))
+                atomicAdd(&hist[(k >> shift) & 255u], 1);
+        }
+        __syncthreads();
+        if (tid < 32) {  // warp 0 scans the 256 bins (8 per lane) and picks the digit
+            int local[8], sum = 0;
+#pragma unroll
+            for (int t = 0; t < 8; ++t) {
+                local[t] = hist[tid * 8 + t];
+                sum += local[t];
+            }
+            int incl = sum;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, incl, off);
+                if (tid >= off) incl += v;
+            }
+            int before = incl - sum;
+            const bool mine = before < static_cast<int>(rank) && static_cast<int>(rank) <= incl;
+            if (mine) {
+                for (int t = 0; t < 8; ++t) {
+                    if (before + local[t] >= static_cast<int>(rank)) {
+                        s_sel[0] = tid * 8 + t;
+                        s_sel[1] = static_cast<int>(rank) - before;  // rank inside the bin
+                        s_sel[2] = local[t];
+                        break;
+                    }
+                    before += local[t];
+                }
+            }
+        }
+        __syncthreads();
+        const int digit = s_sel[0];
+        const int in_bin = s_sel[1];
+        const int bin_size = s_sel[2];
+        __syncthreads();
+        prefix |= static_cast<uint64_t>(digit) << shift;
+        rank = static_cast<uint32_t>(in_bin);
+        if (in_bin == bin_size) take_all = true;  // the whole bucket is selected
+    }
+    // Select every key whose bits >= shift are <= prefix's (all keys when take_all && n<=S).
+    if (tid == 0) s_sel[1] = 0;
+    __syncthreads();
+    const bool everything = n <= static_cast<uint32_t>(S);
+    for (uint32_t i = tid; i < n; i += blockDim.x) {
+        const uint64_t k = key_at(i);
+        const bool sel = everything || (shift >= 64 ? true : (k >> shift) <= (prefix >> shift));
+        if (sel) {
+            const int pos = atomicAdd(&s_sel[1], 1);
+            if (pos < S) out[pos] = k;
+        }
+    }
+    __syncthreads();
+    block_bitonic_sort(out, S2);
+}
+
+
 // Streaming block top-S of uint64 keys (ascending). Shared layout: buf[0, S) holds the
 // current best (sorted; unused slots kKeyMax), buf[S, S + stage_cap) stages new keys,
 // buf is sized `sort_n` = next_pow2(S + stage_cap). Keys must be < threshold() to be

@@ -109,6 +109,9 @@ struct Engine {
     bool profiling = false, candidate_stats = false, gpu_filter_timing = false;
     bool cross_query_reuse = true, cpu_secondary_filter = true;
     int ip_kernel_type = 0;
+    // Upper bound on the HBM buffer holding the vanguard pairs' lower bounds; larger
+    // worst cases fall back to rescanning the vanguard clusters.
+    uint64_t lows_budget = 16ull << 30;
 
     // workspace
     bool ws_ready = false;
@@ -118,7 +121,9 @@ struct Engine {
     DevBuf<uint32_t> planes, cand_cnt, seed_cnt, pair_cnt, pair_off, pair_cur, item_off, pairs,
         n_items, out_i;
     DevBuf<int> probe_ids, item_counter, err;
-    DevBuf<uint64_t> bound, cand_rec, cand_key;
+    DevBuf<uint64_t> bound, cand_rec, cand_key, vg_off;
+    DevBuf<float> lows;
+    std::vector<uint32_t> h_sizes_sorted;  // cluster sizes, descending (lows worst case)
     DevBuf<ScanItem> items;
     DevBuf<unsigned long long> stats;
     std::vector<float> h_T0;  // host mirror kept for capture/seed without device syncs
@@ -173,6 +178,8 @@ struct Engine {
             largest = std::max<uint64_t>(largest, h_sizes[c]);
         }
         if (count != num_vecs) fail(CORA_EINVAL, "cluster sizes differ from index size");
+        h_sizes_sorted = sizes;
+        std::sort(h_sizes_sorted.begin(), h_sizes_sorted.end(), std::greater<uint32_t>());
         CUDA_TRY(cudaSetDevice(device));
         N = num_vecs;
         dim = d;
@@ -245,6 +252,18 @@ struct Engine {
         T1.alloc(max_q);
         Tcap.alloc(max_q);
         bound.alloc(max_q * std::max<uint64_t>(ws_vg, 1));
+        vg_off.alloc(max_q * std::max<uint64_t>(ws_vg, 1) + 1);
+        {
+            // worst case of the lows buffer: every query probes the ws_vg largest clusters
+            uint64_t worst = 0;
+            for (uint64_t r = 0; r < ws_vg && r < h_sizes_sorted.size(); ++r)
+                worst += h_sizes_sorted[r];
+            worst *= max_q;
+            size_t free_b = 0, total_b = 0;
+            CUDA_TRY(cudaMemGetInfo(&free_b, &total_b));
+            const uint64_t limit = std::min<uint64_t>(lows_budget, free_b / 4);
+            if (worst > 0 && worst * 4 <= limit) lows.alloc(worst);
+        }
         cand_cnt.alloc(max_q);
         seed_cnt.alloc(max_q);
         cand_rec.alloc(max_q * cap);
@@ -278,6 +297,8 @@ struct Engine {
         item_counter.release();
         err.release();
         bound.release();
+        vg_off.release();
+        lows.release();
         cand_rec.release();
         cand_key.release();
         items.release();
@@ -445,47 +466,65 @@ void Engine::repack_scan_planes(const uint32_t *d_short, const float *d_fac) {
 // ------------------------------------------------------------------------------------
 namespace {
 template <int G16>
-size_t vanguard_smem(int sort_n) {
+size_t rescan_smem(int sort_n) {
     using Sh = ScanShape<G16>;
     return 2 * Sh::kStageEntries * 16 + 8 * Sh::W4 * 4 + (size_t)sort_n * 8;
 }
 template <int G16>
-size_t main_smem() {
+size_t scan_smem() {
     using Sh = ScanShape<G16>;
     return 2 * Sh::kStageEntries * 16 + (size_t)kMaxPairsPerItem * 8 * Sh::W4 * 4;
 }
 
+enum class ScanPhase { kRescanVanguard, kWriteLows, kMain };
+
+struct ScanLaunch {
+    IndexView ix;
+    SearchView sv;
+    int rescan_sort_n;
+    uint64_t n_van;
+    const ScanItem *items;
+    const uint32_t *n_items;
+    const uint32_t *pairs;
+    int *item_counter;
+    const uint8_t *owned;
+    int num_sms;
+    cudaStream_t st;
+};
+
+template <int G16, bool kLows>
+void launch_grouped(const ScanLaunch &L) {
+    const size_t sm = scan_smem<G16>();
+    CUDA_TRY(cudaFuncSetAttribute(scan_kernel<G16, kLows>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    int per_sm = 0;
+    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_kernel<G16, kLows>,
+                                                           kScanThreads, sm));
+    const int grid = std::max(1, per_sm) * L.num_sms;
+    scan_kernel<G16, kLows><<<grid, kScanThreads, sm, L.st>>>(L.ix, L.sv, L.items, L.n_items,
+                                                            L.pairs, L.item_counter);
+    CUDA_TRY(cudaGetLastError());
+}
+
 template <int G16>
-void launch_scan(const IndexView &ix, const SearchView &sv, int van_sort_n, uint64_t n_van,
-                 const ScanItem *items, const uint32_t *n_items, const uint32_t *pairs,
-                 int *item_counter, int num_sms, cudaStream_t st, bool vanguard_phase) {
-    if (vanguard_phase) {
-        const size_t sm = vanguard_smem<G16>(van_sort_n);
-        CUDA_TRY(cudaFuncSetAttribute(vanguard_kernel<G16>,
+void launch_scan(const ScanLaunch &L, ScanPhase phase) {
+    if (phase == ScanPhase::kRescanVanguard) {
+        const size_t sm = rescan_smem<G16>(L.rescan_sort_n);
+        CUDA_TRY(cudaFuncSetAttribute(vanguard_rescan_kernel<G16>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        vanguard_kernel<G16><<<static_cast<unsigned>(n_van), kScanThreads, sm, st>>>(ix, sv,
-                                                                                     van_sort_n);
+        vanguard_rescan_kernel<G16><<<static_cast<unsigned>(L.n_van), kScanThreads, sm, L.st>>>(
+            L.ix, L.sv, L.rescan_sort_n, L.owned);
         CUDA_TRY(cudaGetLastError());
+    } else if (phase == ScanPhase::kWriteLows) {
+        launch_grouped<G16, true>(L);
     } else {
-        const size_t sm = main_smem<G16>();
-        CUDA_TRY(cudaFuncSetAttribute(scan_main_kernel<G16>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        int per_sm = 0;
-        CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_main_kernel<G16>,
-                                                               kScanThreads, sm));
-        const int grid = std::max(1, per_sm) * num_sms;
-        scan_main_kernel<G16><<<grid, kScanThreads, sm, st>>>(ix, sv, items, n_items, pairs,
-                                                             item_counter);
-        CUDA_TRY(cudaGetLastError());
+        launch_grouped<G16, false>(L);
     }
 }
 
-void dispatch_scan(int G16, const IndexView &ix, const SearchView &sv, int van_sort_n,
-                   uint64_t n_van, const ScanItem *items, const uint32_t *n_items,
-                   const uint32_t *pairs, int *item_counter, int num_sms, cudaStream_t st,
-                   bool vanguard_phase) {
+void dispatch_scan(int G16, const ScanLaunch &L, ScanPhase phase) {
 #define CORA_SCAN_CASE(G) \
-    case G: launch_scan<G>(ix, sv, van_sort_n, n_van, items, n_items, pairs, item_counter, num_sms, st, vanguard_phase); break;
+    case G: launch_scan<G>(L, phase); break;
     switch (G16) {
         CORA_SCAN_CASE(1)
         CORA_SCAN_CASE(2)
@@ -536,68 +575,97 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
                                                    static_cast<int>(D), gmat.p);
         CUDA_TRY(cudaGetLastError());
         mark(2, st);
-        const int sort_n = next_pow2(inp + kProbeTile);
-        const size_t sm = (size_t)sort_n * 8;
+        const size_t sm = (size_t)next_pow2(inp) * 8;
         CUDA_TRY(cudaFuncSetAttribute(select_probes_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        select_probes_kernel<<<inq, 256, sm, st>>>(gmat.p, static_cast<int>(nlist), inp, sort_n,
+        select_probes_kernel<<<inq, 256, sm, st>>>(gmat.p, static_cast<int>(nlist), inp,
                                                    probe_ids.p, probe_g.p);
         CUDA_TRY(cudaGetLastError());
     }
     mark(3, st);
+    const bool lows_mode = lows.n > 0;
     IndexView ix{scan4.p, cl_start.p, cl_size.p, long_codes.p, ex_factors.p, ids.p,
                  static_cast<int>(nlist), static_cast<int>(D), G16, LC};
     SearchView sv{inq, ik, inp, static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
                   scal.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p, cand_cnt.p,
-                  seed_cnt.p, cand_rec.p, cand_key.p, err.p};
+                  seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n, err.p};
     const uint8_t *own = owned.n ? owned.p : nullptr;
-    // 3. per-cluster grouping of every (query, probe) pair
-    {
+    const int rescan_sort_n = next_pow2(static_cast<int>(keep) + (G16 <= 2 ? 512 : 256));
+    ScanLaunch L{ix, sv, rescan_sort_n, nq * veff, items.p, n_items.p, pairs.p, item_counter.p,
+                 own, num_sms, st};
+    // Per-cluster grouping of the (query, probe rank) pairs with rank in [r_lo, r_hi):
+    // cross-query reuse serves up to kMaxPairsPerItem queries from one cluster read.
+    auto group_pairs = [&](int r_lo, int r_hi) {
         const size_t total = nq * np;
         const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
         CUDA_TRY(cudaMemsetAsync(pair_cnt.p, 0, nlist * 4, st));
         CUDA_TRY(cudaMemsetAsync(pair_cur.p, 0, nlist * 4, st));
         CUDA_TRY(cudaMemsetAsync(item_counter.p, 0, 4, st));
-        // cross-query reuse groups up to kMaxPairsPerItem queries per cluster read
         const int ppi = cross_query_reuse ? kMaxPairsPerItem : 1;
-        count_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, 0, own, pair_cnt.p);
+        count_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own,
+                                                   pair_cnt.p);
         scan_pairs_kernel<<<1, 1024, 0, st>>>(pair_cnt.p, static_cast<int>(nlist), ppi,
                                                pair_off.p, item_off.p, n_items.p);
-        scatter_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, 0, own, pair_off.p,
-                                                     pair_cur.p, pairs.p);
+        scatter_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own,
+                                                     pair_off.p, pair_cur.p, pairs.p);
         emit_items_kernel<<<static_cast<unsigned>((nlist + 255) / 256), 256, 0, st>>>(
             pair_cnt.p, pair_off.p, item_off.p, static_cast<int>(nlist), ppi, items.p);
+        CUDA_TRY(cudaGetLastError());
+    };
+    const int iveff = static_cast<int>(veff);
+    const unsigned n_van = static_cast<unsigned>(nq * veff);
+    // 3. vanguard pairs: seeds (best `keep` keys per pair among low < T0)
+    if (lows_mode) {
+        group_pairs(0, iveff);
+        vanguard_offsets_kernel<<<1, 1024, 0, st>>>(probe_ids.p, cl_size.p, own, inq, inp, iveff,
+                                                    lows.n, vg_off.p, err.p);
         CUDA_TRY(cudaGetLastError());
     }
     mark(4, st);
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter0, st));
-    // 4. vanguard seeds -> refine -> T1
-    const int van_sort_n = next_pow2(static_cast<int>(keep) + (G16 <= 2 ? 512 : 256));
-    dispatch_scan(G16, ix, sv, van_sort_n, nq * veff, items.p, n_items.p, pairs.p, item_counter.p,
-                  num_sms, st, true);
+    if (lows_mode) {
+        dispatch_scan(G16, L, ScanPhase::kWriteLows);
+        const size_t sm = (size_t)next_pow2(static_cast<int>(keep)) * 8;
+        CUDA_TRY(cudaFuncSetAttribute(vanguard_select_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        vanguard_select_kernel<<<n_van, 256, sm, st>>>(ix, sv, own);
+        CUDA_TRY(cudaGetLastError());
+    } else {
+        dispatch_scan(G16, L, ScanPhase::kRescanVanguard);
+    }
     mark(5, st);
-    refine_kernel<<<inq, kRefineThreads, 0, st>>>(ix, sv, 0);
+    const size_t refine_sm = (size_t)D * 4 + np * sizeof(ProbeInfo);
+    CUDA_TRY(cudaFuncSetAttribute(refine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)refine_sm));
+    refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 0);
     CUDA_TRY(cudaGetLastError());
     mark(6, st);
-    const int merge_sort_n = next_pow2(ik + kMergeTile);
+    const size_t sel_sm = (size_t)next_pow2(ik) * 8;
     CUDA_TRY(cudaFuncSetAttribute(threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  merge_sort_n * 8));
-    threshold_kernel<<<inq, 256, (size_t)merge_sort_n * 8, st>>>(sv, merge_sort_n);
+                                  (int)sel_sm));
+    threshold_kernel<<<inq, 256, sel_sm, st>>>(sv);
     CUDA_TRY(cudaGetLastError());
     mark(7, st);
-    // 5. main scan against T1, then refine the new candidates
-    dispatch_scan(G16, ix, sv, van_sort_n, 0, items.p, n_items.p, pairs.p, item_counter.p, num_sms,
-                  st, false);
+    // 4. main pass against T1: the other probes are scanned; the vanguard probes are either
+    //    filtered from their stored lows or rescanned, skipping their seeds in both cases.
+    if (lows_mode) {
+        group_pairs(iveff, inp);
+        dispatch_scan(G16, L, ScanPhase::kMain);
+        vanguard_filter_kernel<<<n_van, 256, 0, st>>>(ix, sv, own);
+        CUDA_TRY(cudaGetLastError());
+    } else {
+        group_pairs(0, inp);
+        dispatch_scan(G16, L, ScanPhase::kMain);
+    }
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));
     mark(8, st);
-    refine_kernel<<<inq, kRefineThreads, 0, st>>>(ix, sv, 1);
+    refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 1);
     CUDA_TRY(cudaGetLastError());
     mark(9, st);
-    // 6. final top-k
+    // 5. final top-k
     CUDA_TRY(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  merge_sort_n * 8));
-    merge_kernel<<<inq, 256, (size_t)merge_sort_n * 8, st>>>(sv, merge_sort_n, d_od, d_oi,
-                                                             stats.p);
+                                  (int)sel_sm));
+    merge_kernel<<<inq, 256, sel_sm, st>>>(sv, d_od, d_oi, stats.p);
     CUDA_TRY(cudaGetLastError());
     mark(10, st);
 }
@@ -978,6 +1046,18 @@ int cora_stage_totals(cora_engine *engine, double *h_out, uint64_t n, uint64_t *
 
 int cora_stage_reset(cora_engine *engine) {
     return guarded([&] { eng(engine).stage_reset(); });
+}
+
+int cora_set_vanguard_lows_budget(cora_engine *engine, uint64_t bytes) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        if (e.ws_ready) cora::fail(CORA_ESTATE, "set the lows budget before prepare_workspace");
+        e.lows_budget = bytes;
+    });
+}
+
+int cora_get_vanguard_mode(const cora_engine *engine) {
+    return engine && engine->e ? (engine->e->lows.n > 0 ? 1 : 0) : -1;
 }
 
 uint64_t cora_get_candidate_capacity(const cora_engine *engine) {

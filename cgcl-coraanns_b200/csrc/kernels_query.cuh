@@ -150,27 +150,18 @@ __global__ void __launch_bounds__(256) centroid_dist_kernel(
     }
 }
 
-// One CTA per query: the nprobe smallest (g, c) keys, ascending, via the streaming block
-// top-k (tiles of kProbeTile centroids). Dynamic shared memory: sort_n uint64 keys.
-constexpr int kProbeTile = 1024;
+// One CTA per query: the nprobe smallest (g, c) keys, ascending, by block radix selection
+// over the query's row of distances. Dynamic shared memory: next_pow2(nprobe) keys.
 __global__ void __launch_bounds__(256) select_probes_kernel(const float *__restrict__ g,
-                                                            int nlist, int nprobe, int sort_n,
+                                                            int nlist, int nprobe,
                                                             int *__restrict__ probe_ids,
                                                             float *__restrict__ probe_g) {
     extern __shared__ uint64_t smem_k[];
-    __shared__ int n_staged;
-    __shared__ uint64_t thresh;
+    __shared__ int scratch[256 + 3];
     const int q = blockIdx.x;
-    BlockTopK tk{smem_k, nprobe, kProbeTile, sort_n, &n_staged, &thresh};
-    tk.init(kKeyMax);
     const float *row = g + (size_t)q * nlist;
-    for (int base = 0; base < nlist; base += kProbeTile) {
-        for (int i = threadIdx.x; i < kProbeTile; i += blockDim.x) {
-            const int c = base + i;
-            if (c < nlist) tk.offer(make_key(row[c], static_cast<uint32_t>(c)));
-        }
-        tk.flush(kKeyMax);
-    }
+    auto key_at = [&](uint32_t c) -> uint64_t { return make_key(row[c], c); };
+    block_select_smallest(key_at, static_cast<uint32_t>(nlist), nprobe, smem_k, scratch);
     for (int r = threadIdx.x; r < nprobe; r += blockDim.x) {
         const uint64_t key = smem_k[r];
         probe_ids[(size_t)q * nprobe + r] = static_cast<int>(key & 0xFFFFFFFFu);

@@ -18,14 +18,56 @@ namespace cora {
 
 constexpr int kRefineThreads = 256;
 
-// One CTA per query; warp per candidate. mode 0 refines the vanguard seeds [0, cnt) and
-// records the seed count; mode 1 refines the main candidates [seed_cnt, cnt).
-// The 8-bit-code inner product accumulates in fp64: lane l owns dims 64b+l and 64b+32+l
-// of every 64-dim block b (ascending), then an xor butterfly combines the lanes.
+struct ProbeInfo {  // per (query, probe rank), staged in shared memory by refine_kernel
+    uint32_t start, size;
+    float g;
+};
+
+// Inner product of the full 8-bit code of one vector with the rotated query x (in shared
+// memory): lane l accumulates dims 64b+l and 64b+32+l of every 64-dim block b in fp64
+// (exact products), then an xor butterfly combines the lanes; every lane returns the sum.
+__device__ __forceinline__ double code_ip(const float *__restrict__ x, const uint4 *code_base,
+                                          uint32_t n, const uint8_t *ex, int nblocks, int lane) {
+    double acc = 0.0;
+    for (int b = 0; b < nblocks; ++b) {
+        const uint4 cw = __ldg(code_base + (size_t)(b >> 1) * n);
+        const uint32_t w0 = (b & 1) ? cw.z : cw.x;
+        const uint32_t w1 = (b & 1) ? cw.w : cw.y;
+        const uint8_t *p = ex + 56 * b;
+        const unsigned long long top = __ldg(reinterpret_cast<const unsigned long long *>(p + 48));
+        uint32_t u0 = __ldg(p + lane) & 63u;
+        uint32_t u1;
+        if (lane < 16) {
+            u1 = __ldg(p + 32 + lane) & 63u;
+        } else {
+            const int k = lane - 16;
+            u1 = (static_cast<uint32_t>(__ldg(p + k)) >> 6) |
+                 ((static_cast<uint32_t>(__ldg(p + 16 + k)) >> 6) << 2) |
+                 ((static_cast<uint32_t>(__ldg(p + 32 + k)) >> 6) << 4);
+        }
+        u0 |= static_cast<uint32_t>((top >> (8 * (lane & 7) + (lane >> 3))) & 1ull) << 6;
+        u1 |= static_cast<uint32_t>((top >> (8 * (lane & 7) + 4 + (lane >> 3))) & 1ull) << 6;
+        const uint32_t b0 = (w0 >> (31 - lane)) & 1u, b1 = (w1 >> (31 - lane)) & 1u;
+        acc = __fma_rn((double)x[64 * b + lane], (double)(128u * b0 + u0), acc);
+        acc = __fma_rn((double)x[64 * b + 32 + lane], (double)(128u * b1 + u1), acc);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1)
+        acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+    return acc;
+}
+
+// One CTA per query; warp per candidate, two candidates in flight per warp. mode 0 refines
+// the vanguard seeds [0, cnt) and records the seed count; mode 1 refines the main
+// candidates [seed_cnt, cnt). Dynamic shared memory: D floats + nprobe ProbeInfo.
 __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, SearchView sv,
                                                                 int mode) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float *x = reinterpret_cast<float *>(smem_raw);
+    ProbeInfo *pinfo = reinterpret_cast<ProbeInfo *>(x + ix.D);
     const int q = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int kWarps = kRefineThreads / 32;
     const uint32_t cnt = sv.cand_cnt[q];
     const uint32_t cap = static_cast<uint32_t>(sv.cap);
     uint32_t from, to;
@@ -37,78 +79,60 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
         from = sv.seed_cnt[q];
         to = min(cnt, cap);
     }
-    const float kb = sv.scal[q].kb;
-    const float *x = sv.qr + (size_t)q * ix.D;
-    const int nblocks = ix.D / 64;
-    const int G16 = ix.G16;
-    for (uint32_t i = from + warp; i < to; i += kRefineThreads / 32) {
-        const uint64_t rec = sv.cand_rec[(size_t)q * sv.cap + i];
-        const uint32_t gid = static_cast<uint32_t>(rec & 0xFFFFFFFFu);
-        const int r = static_cast<int>(rec >> 32);
+    if (from >= to) return;  // uniform across the block
+    for (int j = threadIdx.x; j < ix.D; j += blockDim.x) x[j] = sv.qr[(size_t)q * ix.D + j];
+    const int np = mode == 0 ? sv.veff : sv.nprobe;
+    for (int r = threadIdx.x; r < np; r += blockDim.x) {
         const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
-        const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
-        const uint32_t s = ix.cl_start[c];
-        const uint32_t n = ix.cl_size[c];
-        const uint32_t iv = gid - s;
-        const uint4 *code_base = ix.scan4 + (size_t)(G16 + 1) * s + iv;
-        const uint8_t *ex = ix.long_codes + (size_t)gid * ix.LC;
-        double acc = 0.0;
-        for (int b = 0; b < nblocks; ++b) {
-            const uint4 cw = __ldg(code_base + (size_t)(b >> 1) * n);
-            const uint32_t w0 = (b & 1) ? cw.z : cw.x;
-            const uint32_t w1 = (b & 1) ? cw.w : cw.y;
-            const uint8_t *p = ex + 56 * b;
-            const unsigned long long top = __ldg(reinterpret_cast<const unsigned long long *>(p + 48));
-            uint32_t u0 = __ldg(p + lane) & 63u;
-            uint32_t u1;
-            if (lane < 16) {
-                u1 = __ldg(p + 32 + lane) & 63u;
-            } else {
-                const int k = lane - 16;
-                u1 = (static_cast<uint32_t>(__ldg(p + k)) >> 6) |
-                     ((static_cast<uint32_t>(__ldg(p + 16 + k)) >> 6) << 2) |
-                     ((static_cast<uint32_t>(__ldg(p + 32 + k)) >> 6) << 4);
-            }
-            u0 |= static_cast<uint32_t>((top >> (8 * (lane & 7) + (lane >> 3))) & 1ull) << 6;
-            u1 |= static_cast<uint32_t>((top >> (8 * (lane & 7) + 4 + (lane >> 3))) & 1ull) << 6;
-            const uint32_t b0 = (w0 >> (31 - lane)) & 1u, b1 = (w1 >> (31 - lane)) & 1u;
-            acc = __fma_rn((double)x[64 * b + lane], (double)(128u * b0 + u0), acc);
-            acc = __fma_rn((double)x[64 * b + 32 + lane], (double)(128u * b1 + u1), acc);
-        }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1)
-            acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+        pinfo[r] = ProbeInfo{ix.cl_start[c], ix.cl_size[c], sv.probe_g[(size_t)q * sv.nprobe + r]};
+    }
+    __syncthreads();
+    const float kb = sv.scal[q].kb;
+    const int nblocks = ix.D / 64;
+    const size_t planes_per = static_cast<size_t>(ix.G16 + 1);
+    for (uint32_t i0 = from + warp; i0 < to; i0 += 2 * kWarps) {
+        const uint32_t i1 = i0 + kWarps;
+        const bool has1 = i1 < to;
+        const uint64_t rec0 = sv.cand_rec[(size_t)q * sv.cap + i0];
+        const uint64_t rec1 = has1 ? sv.cand_rec[(size_t)q * sv.cap + i1] : rec0;
+        const uint32_t gid0 = static_cast<uint32_t>(rec0 & 0xFFFFFFFFu);
+        const uint32_t gid1 = static_cast<uint32_t>(rec1 & 0xFFFFFFFFu);
+        const ProbeInfo p0 = pinfo[rec0 >> 32], p1 = pinfo[rec1 >> 32];
+        const float2 f0 = ix.ex_factors[gid0], f1 = ix.ex_factors[gid1];
+        const uint32_t id0 = ix.ids[gid0], id1 = ix.ids[gid1];
+        const double a0 = code_ip(x, ix.scan4 + planes_per * p0.start + (gid0 - p0.start), p0.size,
+                                  ix.long_codes + (size_t)gid0 * ix.LC, nblocks, lane);
+        const double a1 = code_ip(x, ix.scan4 + planes_per * p1.start + (gid1 - p1.start), p1.size,
+                                  ix.long_codes + (size_t)gid1 * ix.LC, nblocks, lane);
         if (lane == 0) {
-            const float ipt = __double2float_rn(acc);
-            const float2 f = ix.ex_factors[gid];
-            const float ex_d = __fadd_rn(__fadd_rn(f.x, g), __fmul_rn(f.y, __fadd_rn(ipt, kb)));
-            sv.cand_key[(size_t)q * sv.cap + i] = make_key(ex_d, ix.ids[gid]);
+            const float ex0 = __fadd_rn(__fadd_rn(f0.x, p0.g),
+                                        __fmul_rn(f0.y, __fadd_rn(__double2float_rn(a0), kb)));
+            sv.cand_key[(size_t)q * sv.cap + i0] = make_key(ex0, id0);
+            if (has1) {
+                const float ex1 = __fadd_rn(__fadd_rn(f1.x, p1.g),
+                                            __fmul_rn(f1.y, __fadd_rn(__double2float_rn(a1), kb)));
+                sv.cand_key[(size_t)q * sv.cap + i1] = make_key(ex1, id1);
+            }
         }
     }
 }
 
-constexpr int kMergeTile = 1024;
-
 // One CTA per query: T1 = min(T0, k-th smallest seed distance below T0) when at least k
-// seeds are below T0, else T0. Dynamic shared memory: sort_n = next_pow2(k + 1024) keys.
-__global__ void __launch_bounds__(256) threshold_kernel(SearchView sv, int sort_n) {
-    extern __shared__ uint64_t smem_k[];
-    __shared__ int n_staged;
-    __shared__ uint64_t thresh;
+// seeds are below T0, else T0. Dynamic shared memory: next_pow2(k) keys.
+__global__ void __launch_bounds__(256) threshold_kernel(SearchView sv) {
+    extern __shared__ uint64_t s_keys[];
+    __shared__ int scratch[256 + 3];
     const int q = blockIdx.x;
     const float T0 = sv.T0[q];
     const uint32_t n = sv.seed_cnt[q];
-    BlockTopK tk{smem_k, sv.k, kMergeTile, sort_n, &n_staged, &thresh};
-    tk.init(kKeyMax);
-    for (uint32_t base = 0; base < n; base += kMergeTile) {
-        for (uint32_t i = base + threadIdx.x; i < min(n, base + kMergeTile); i += blockDim.x) {
-            const uint64_t key = sv.cand_key[(size_t)q * sv.cap + i];
-            if (unord_f32(static_cast<uint32_t>(key >> 32)) < T0) tk.offer(key);
-        }
-        tk.flush(kKeyMax);
-    }
+    const uint64_t *keys = sv.cand_key + (size_t)q * sv.cap;
+    auto key_at = [&](uint32_t i) -> uint64_t {
+        const uint64_t key = keys[i];
+        return unord_f32(static_cast<uint32_t>(key >> 32)) < T0 ? key : kKeyMax;
+    };
+    block_select_smallest(key_at, n, sv.k, s_keys, scratch);
     if (threadIdx.x == 0) {
-        const uint64_t kth = smem_k[sv.k - 1];
+        const uint64_t kth = s_keys[sv.k - 1];
         sv.T1[q] = kth == kKeyMax ? T0 : fminf(T0, unord_f32(static_cast<uint32_t>(kth >> 32)));
     }
 }
@@ -116,35 +140,30 @@ __global__ void __launch_bounds__(256) threshold_kernel(SearchView sv, int sort_
 // One CTA per query: final top-k by (ex, id) among all refined candidates with ex < T0.
 // Writes distances / ids (padded with FLT_MAX / 0), records the query's threshold after the
 // search (its k-th distance when k results exist, else T0; what capture_thresholds()
-// reports) and adds the candidate count to stats[0].
-__global__ void __launch_bounds__(256) merge_kernel(SearchView sv, int sort_n,
-                                                    float *__restrict__ out_d,
+// reports) and adds the candidate count to stats[0]. Dynamic shared memory: next_pow2(k).
+__global__ void __launch_bounds__(256) merge_kernel(SearchView sv, float *__restrict__ out_d,
                                                     uint32_t *__restrict__ out_i,
                                                     unsigned long long *__restrict__ stats) {
-    extern __shared__ uint64_t smem_k[];
-    __shared__ int n_staged;
-    __shared__ uint64_t thresh;
+    extern __shared__ uint64_t s_keys[];
+    __shared__ int scratch[256 + 3];
     const int q = blockIdx.x;
     const float T0 = sv.T0[q];
     const uint32_t cnt = sv.cand_cnt[q];
     const uint32_t n = min(cnt, static_cast<uint32_t>(sv.cap));
-    BlockTopK tk{smem_k, sv.k, kMergeTile, sort_n, &n_staged, &thresh};
-    tk.init(kKeyMax);
-    for (uint32_t base = 0; base < n; base += kMergeTile) {
-        for (uint32_t i = base + threadIdx.x; i < min(n, base + kMergeTile); i += blockDim.x) {
-            const uint64_t key = sv.cand_key[(size_t)q * sv.cap + i];
-            if (unord_f32(static_cast<uint32_t>(key >> 32)) < T0) tk.offer(key);
-        }
-        tk.flush(kKeyMax);
-    }
+    const uint64_t *keys = sv.cand_key + (size_t)q * sv.cap;
+    auto key_at = [&](uint32_t i) -> uint64_t {
+        const uint64_t key = keys[i];
+        return unord_f32(static_cast<uint32_t>(key >> 32)) < T0 ? key : kKeyMax;
+    };
+    block_select_smallest(key_at, n, sv.k, s_keys, scratch);
     for (int j = threadIdx.x; j < sv.k; j += blockDim.x) {
-        const uint64_t key = smem_k[j];
+        const uint64_t key = s_keys[j];
         const bool ok = key != kKeyMax;
         out_d[(size_t)q * sv.k + j] = ok ? unord_f32(static_cast<uint32_t>(key >> 32)) : FLT_MAX;
         out_i[(size_t)q * sv.k + j] = ok ? static_cast<uint32_t>(key & 0xFFFFFFFFu) : 0u;
     }
     if (threadIdx.x == 0) {
-        const uint64_t kth = smem_k[sv.k - 1];
+        const uint64_t kth = s_keys[sv.k - 1];
         sv.Tcap[q] = kth != kKeyMax ? unord_f32(static_cast<uint32_t>(kth >> 32)) : T0;
         atomicAdd(stats, static_cast<unsigned long long>(cnt));
     }

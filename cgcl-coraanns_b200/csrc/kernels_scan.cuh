@@ -13,6 +13,16 @@
 //   ip_int = sum_{j<7} popc(x & plane_j) << j  -  popc(x & plane_7) << 7      (exact)
 //   ip1    = width * ip_int
 //   low    = (f_add + g) + f_rescale * (ip1 + k1) - f_error * sqrt(max(g, 0))
+//
+// Search phases (all on one stream):
+//  1. vanguard pairs (probe rank r < veff) are grouped by cluster and scanned once; their
+//     lower bounds are stored in an HBM buffer (`lows`, 4 B per (pair, vector));
+//  2. per vanguard pair, the best `keep` keys (low, gid) among low < T0 become seeds;
+//  3. after the seeds are refined, T1 = min(T0, k-th smallest seed distance);
+//  4. the remaining pairs (r >= veff) are grouped by cluster and scanned against T1, and the
+//     stored lows of the vanguard pairs are filtered against T1 (skipping their seeds).
+// When the lows buffer would not fit its budget, step 1-2 run as one kernel per vanguard
+// pair instead (vanguard_rescan_kernel) and step 4 rescans the vanguard clusters.
 #pragma once
 #include "common.cuh"
 #include "kernels_query.cuh"
@@ -58,19 +68,22 @@ struct SearchView {
     uint32_t *seed_cnt;          // nq
     uint64_t *cand_rec;          // nq x cap : gid | (probe rank << 32)
     uint64_t *cand_key;          // nq x cap : ord(ex) << 32 | id
+    float *lows;                 // vanguard lower bounds (lows mode), see vg_off
+    uint64_t *vg_off;            // nq x veff + 1 offsets into lows
+    uint64_t lows_cap;           // capacity of lows (floats)
     int *err;
 };
 
 // ---- per-cluster query grouping (CSR of (query, probe rank) pairs by cluster) --------
-// Pairs with probe rank in [r_lo, nprobe) whose cluster is owned by this shard
-// (owner == nullptr: all) are grouped; a pair is packed as (q << 16) | r.
+// Pairs with probe rank in [r_lo, r_hi) whose cluster is owned by this shard (owned ==
+// nullptr: all) are grouped; a pair is packed as (q << 16) | r.
 __global__ void count_pairs_kernel(const int *__restrict__ probe_ids, int nq, int nprobe,
-                                   int r_lo, const uint8_t *__restrict__ owned,
+                                   int r_lo, int r_hi, const uint8_t *__restrict__ owned,
                                    uint32_t *__restrict__ cnt) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)nq * nprobe) return;
     const int r = static_cast<int>(i % nprobe);
-    if (r < r_lo) return;
+    if (r < r_lo || r >= r_hi) return;
     const int c = probe_ids[i];
     if (owned && !owned[c]) return;
     atomicAdd(cnt + c, 1u);
@@ -117,14 +130,14 @@ __global__ void __launch_bounds__(1024) scan_pairs_kernel(const uint32_t *__rest
 }
 
 __global__ void scatter_pairs_kernel(const int *__restrict__ probe_ids, int nq, int nprobe,
-                                     int r_lo, const uint8_t *__restrict__ owned,
+                                     int r_lo, int r_hi, const uint8_t *__restrict__ owned,
                                      const uint32_t *__restrict__ off,
                                      uint32_t *__restrict__ cursor,
                                      uint32_t *__restrict__ pairs) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)nq * nprobe) return;
     const int r = static_cast<int>(i % nprobe);
-    if (r < r_lo) return;
+    if (r < r_lo || r >= r_hi) return;
     const int c = probe_ids[i];
     if (owned && !owned[c]) return;
     const int q = static_cast<int>(i / nprobe);
@@ -148,6 +161,44 @@ __global__ void emit_items_kernel(const uint32_t *__restrict__ cnt,
         it.pair_count = min(up, n - t * up);
         it.pad = 0;
         items[base + t] = it;
+    }
+}
+
+// Offsets of every vanguard pair's slice of the lows buffer: one CTA, pairs in
+// (query, rank) order. Non-owned clusters (sharded search) get empty slices. Sets
+// kDevCandidateOverflow if the total exceeds the buffer (sized for the worst case).
+__global__ void __launch_bounds__(1024) vanguard_offsets_kernel(
+    const int *__restrict__ probe_ids, const uint32_t *__restrict__ cl_size,
+    const uint8_t *__restrict__ owned, int nq, int nprobe, int veff, uint64_t cap,
+    uint64_t *__restrict__ vg_off, int *__restrict__ err) {
+    __shared__ uint64_t s_sum[1024];
+    const int t = threadIdx.x;
+    const int per = (nq + 1023) / 1024;
+    const int b = t * per, e = min(nq, b + per);
+    uint64_t sum = 0;
+    for (int q = b; q < e; ++q)
+        for (int r = 0; r < veff; ++r) {
+            const int c = probe_ids[(size_t)q * nprobe + r];
+            if (!owned || owned[c]) sum += cl_size[c];
+        }
+    s_sum[t] = sum;
+    __syncthreads();
+    for (int d = 1; d < 1024; d <<= 1) {
+        const uint64_t v = t >= d ? s_sum[t - d] : 0;
+        __syncthreads();
+        s_sum[t] += v;
+        __syncthreads();
+    }
+    uint64_t run = s_sum[t] - sum;
+    for (int q = b; q < e; ++q)
+        for (int r = 0; r < veff; ++r) {
+            vg_off[(size_t)q * veff + r] = run;
+            const int c = probe_ids[(size_t)q * nprobe + r];
+            if (!owned || owned[c]) run += cl_size[c];
+        }
+    if (t == 1023) {
+        vg_off[(size_t)nq * veff] = s_sum[1023];
+        if (s_sum[1023] > cap) atomicOr(err, kDevCandidateOverflow);
     }
 }
 
@@ -193,13 +244,216 @@ __device__ __forceinline__ float lower_bound_dist(float4 f, float ip1, float g, 
     return __fsub_rn(__fadd_rn(a, b), e);
 }
 
-// ---- vanguard seeding: one CTA per (query, probe rank < veff) ------------------------
-// Keeps the best `keep` (low, gid) keys among low < T0 of the probe's cluster, writes
-// them as seed candidates and records the seed boundary key for the main scan
-// (kKeyMax when every candidate of the pair became a seed).
+// Warp-aggregated append of a candidate record to query q's slice: one atomic per warp
+// and query (the warp-ballot compaction of survivors).
+__device__ __forceinline__ void emit_candidate(const SearchView &sv, bool cand, int q,
+                                               uint64_t rec, int lane) {
+    const uint32_t mask = __ballot_sync(0xffffffffu, cand);
+    if (!mask) return;
+    const int leader = __ffs(mask) - 1;
+    uint32_t slot0 = 0;
+    if (lane == leader) slot0 = atomicAdd(sv.cand_cnt + q, __popc(mask));
+    slot0 = __shfl_sync(0xffffffffu, slot0, leader);
+    if (cand) {
+        const uint32_t slot = slot0 + __popc(mask & ((1u << lane) - 1u));
+        if (slot < static_cast<uint32_t>(sv.cap))
+            sv.cand_rec[(size_t)q * sv.cap + slot] = rec;
+        else
+            atomicOr(sv.err, kDevCandidateOverflow);
+    }
+}
+
+// Writes the seeds of one vanguard pair (keys sorted ascending in s_keys[0, nkeep)) and its
+// boundary key (kKeyMax when every candidate became a seed). Thread 0 reserves the slots.
+__device__ __forceinline__ void write_seeds(const SearchView &sv, int q, int r, int total,
+                                            const uint64_t *s_keys, uint32_t *s_base) {
+    const int nkeep = min(total, sv.keep);
+    if (threadIdx.x == 0) {
+        *s_base = nkeep ? atomicAdd(sv.cand_cnt + q, static_cast<uint32_t>(nkeep)) : 0u;
+        sv.bound[(size_t)q * sv.veff + r] = total <= sv.keep ? kKeyMax : s_keys[sv.keep - 1];
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < nkeep; i += blockDim.x) {
+        const uint32_t slot = *s_base + i;
+        const uint32_t gid = static_cast<uint32_t>(s_keys[i] & 0xFFFFFFFFu);
+        if (slot < static_cast<uint32_t>(sv.cap))
+            sv.cand_rec[(size_t)q * sv.cap + slot] = gid | (static_cast<uint64_t>(r) << 32);
+        else
+            atomicOr(sv.err, kDevCandidateOverflow);
+    }
+}
+
+// ---- grouped scan: persistent CTAs over (cluster, <= 32 pairs) items -----------------
+// kWriteLows: store every low in the pair's slice of sv.lows (vanguard pass).
+// otherwise:  emit candidates low < T1 (main pass; vanguard seeds are skipped through the
+//             boundary key when vanguard pairs are rescanned).
+template <int G16, bool kWriteLows>
+__global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
+    IndexView ix, SearchView sv, const ScanItem *__restrict__ items,
+    const uint32_t *__restrict__ n_items_ptr, const uint32_t *__restrict__ pairs,
+    int *__restrict__ item_counter) {
+    using Sh = ScanShape<G16>;
+    constexpr int TV = Sh::TV, W4 = Sh::W4;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    uint4 *stage = reinterpret_cast<uint4 *>(smem_raw);
+    uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + 2 * Sh::kStageEntries);
+    __shared__ __align__(8) uint64_t bars[2];
+    __shared__ uint64_t s_bnd[kMaxPairsPerItem];
+    __shared__ float s_T1[kMaxPairsPerItem], s_g[kMaxPairsPerItem], s_k1[kMaxPairsPerItem],
+        s_w[kMaxPairsPerItem], s_gerr[kMaxPairsPerItem];
+    __shared__ int s_q[kMaxPairsPerItem], s_r[kMaxPairsPerItem];
+    __shared__ int s_item, s_abort;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_barrier_init();
+        s_abort = 0;
+    }
+    __syncthreads();
+    const uint32_t n_items = *n_items_ptr;
+    const int lane = threadIdx.x & 31;
+    uint32_t phase[2] = {0, 0};
+    while (true) {
+        if (threadIdx.x == 0) s_item = atomicAdd(item_counter, 1);
+        __syncthreads();
+        const int it = s_item;
+        if (it >= static_cast<int>(n_items)) break;
+        const ScanItem item = items[it];
+        const int c = static_cast<int>(item.cluster);
+        const uint32_t s = ix.cl_start[c];
+        const int n = static_cast<int>(ix.cl_size[c]);
+        const int pc = static_cast<int>(item.pair_count);
+        const size_t cbase = (size_t)(G16 + 1) * s;
+        const int ntiles = (n + TV - 1) / TV;
+        if (threadIdx.x == 0 && ntiles > 0)
+            issue_tile<G16>(stage, &bars[0], ix.scan4, cbase, n, 0, min(TV, n));
+        if (threadIdx.x < pc) {
+            const uint32_t pr = pairs[item.pair_begin + threadIdx.x];
+            const int q = static_cast<int>(pr >> 16), r = static_cast<int>(pr & 0xFFFFu);
+            const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
+            const QueryScalars qs = sv.scal[q];
+            s_q[threadIdx.x] = q;
+            s_r[threadIdx.x] = r;
+            s_g[threadIdx.x] = g;
+            s_k1[threadIdx.x] = qs.k1;
+            s_w[threadIdx.x] = qs.width;
+            s_gerr[threadIdx.x] = __fsqrt_rn(fmaxf(g, 0.0f));
+            if (kWriteLows) {
+                // slice offset of this vanguard pair, carried in s_bnd
+                s_bnd[threadIdx.x] = sv.vg_off[(size_t)q * sv.veff + r];
+            } else {
+                s_T1[threadIdx.x] = sv.T1[q];
+                s_bnd[threadIdx.x] = r < sv.veff ? sv.bound[(size_t)q * sv.veff + r] : 0ull;
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < pc * 8 * W4; i += blockDim.x) {
+            const int j = i / (8 * W4);
+            s_planes[i] = sv.planes[(size_t)s_q[j] * 8 * W4 + (i - j * 8 * W4)];
+        }
+        __syncthreads();
+        for (int t = 0; t < ntiles; ++t) {
+            const int b = t & 1;
+            const int v0 = t * TV, tv = min(TV, n - v0);
+            if (!mbar_wait_bounded(&bars[b], phase[b], sv.err)) s_abort = 1;
+            phase[b] ^= 1;
+            __syncthreads();
+            if (s_abort) return;
+            if (threadIdx.x == 0 && t + 1 < ntiles)
+                issue_tile<G16>(stage + (b ^ 1) * Sh::kStageEntries, &bars[b ^ 1], ix.scan4, cbase,
+                                n, v0 + TV, min(TV, n - v0 - TV));
+            const uint4 *sb = stage + b * Sh::kStageEntries;
+            for (int base = 0; base < tv; base += kScanThreads) {
+                const int i = base + threadIdx.x;
+                const bool valid = i < tv;
+                uint4 code[G16];
+                float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                for (int gg = 0; gg < G16; ++gg)
+                    code[gg] = valid ? sb[gg * TV + i] : make_uint4(0, 0, 0, 0);
+                if (valid) {
+                    const uint4 fr = sb[G16 * TV + i];
+                    f = make_float4(__uint_as_float(fr.x), __uint_as_float(fr.y),
+                                    __uint_as_float(fr.z), 0.0f);
+                }
+                const uint32_t gid = s + static_cast<uint32_t>(v0 + i);
+                for (int j = 0; j < pc; ++j) {
+                    const int ip = ip_int_from_planes<G16>(code, s_planes + j * 8 * W4);
+                    const float ip1 = __fadd_rn(__fmul_rn(s_w[j], (float)ip), 0.0f);
+                    const float low = lower_bound_dist(f, ip1, s_g[j], s_k1[j], s_gerr[j]);
+                    if (kWriteLows) {
+                        if (valid) sv.lows[s_bnd[j] + v0 + i] = low;
+                    } else {
+                        const bool cand = valid && (low < s_T1[j]) && (make_key(low, gid) > s_bnd[j]);
+                        emit_candidate(sv, cand, s_q[j], gid | (static_cast<uint64_t>(s_r[j]) << 32),
+                                       lane);
+                    }
+                }
+            }
+            __syncthreads();  // stage buffer b is free again
+        }
+    }
+}
+
+// ---- lows mode: per vanguard pair seed selection and candidate filtering -------------
+// One CTA per vanguard pair: seeds are the best `keep` keys among low < T0.
+// Dynamic shared memory: next_pow2(keep) keys.
+__global__ void __launch_bounds__(256) vanguard_select_kernel(IndexView ix, SearchView sv,
+                                                              const uint8_t *__restrict__ owned) {
+    extern __shared__ uint64_t s_keys[];
+    __shared__ int scratch[256 + 3];
+    __shared__ int s_total;
+    __shared__ uint32_t s_base;
+    const int pi = blockIdx.x;
+    const int q = pi / sv.veff, r = pi % sv.veff;
+    const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
+    if (owned && !owned[c]) return;
+    const uint32_t s = ix.cl_start[c];
+    const uint32_t n = ix.cl_size[c];
+    const float *L = sv.lows + sv.vg_off[pi];
+    const float T0 = sv.T0[q];
+    if (threadIdx.x == 0) s_total = 0;
+    __syncthreads();
+    int mine = 0;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) mine += L[i] < T0;
+    atomicAdd(&s_total, mine);
+    auto key_at = [&](uint32_t i) -> uint64_t {
+        const float l = L[i];
+        return l < T0 ? make_key(l, s + i) : kKeyMax;
+    };
+    block_select_smallest(key_at, n, sv.keep, s_keys, scratch);
+    write_seeds(sv, q, r, s_total, s_keys, &s_base);
+}
+
+// One CTA per vanguard pair: candidates low < T1 that are not seeds (key > boundary).
+__global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, SearchView sv,
+                                                              const uint8_t *__restrict__ owned) {
+    const int pi = blockIdx.x;
+    const int q = pi / sv.veff, r = pi % sv.veff;
+    const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
+    if (owned && !owned[c]) return;
+    const uint32_t s = ix.cl_start[c];
+    const uint32_t n = ix.cl_size[c];
+    const float *L = sv.lows + sv.vg_off[pi];
+    const float T1 = sv.T1[q];
+    const uint64_t bnd = sv.bound[(size_t)q * sv.veff + r];
+    const int lane = threadIdx.x & 31;
+    for (uint32_t base = 0; base < n; base += blockDim.x) {
+        const uint32_t i = base + threadIdx.x;
+        bool cand = false;
+        if (i < n) {
+            const float l = L[i];
+            cand = (l < T1) && (make_key(l, s + i) > bnd);
+        }
+        emit_candidate(sv, cand, q, (s + i) | (static_cast<uint64_t>(r) << 32), lane);
+    }
+}
+
+// ---- rescan mode: one CTA per vanguard pair scans the cluster and keeps its seeds ----
 template <int G16>
-__global__ void __launch_bounds__(kScanThreads) vanguard_kernel(IndexView ix, SearchView sv,
-                                                                int sort_n) {
+__global__ void __launch_bounds__(kScanThreads) vanguard_rescan_kernel(
+    IndexView ix, SearchView sv, int sort_n, const uint8_t *__restrict__ owned) {
     using Sh = ScanShape<G16>;
     constexpr int TV = Sh::TV, W4 = Sh::W4;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -214,6 +468,7 @@ __global__ void __launch_bounds__(kScanThreads) vanguard_kernel(IndexView ix, Se
     const int pi = blockIdx.x;
     const int q = pi / sv.veff, r = pi % sv.veff;
     const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
+    if (owned && !owned[c]) return;
     const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
     const uint32_t s = ix.cl_start[c];
     const int n = static_cast<int>(ix.cl_size[c]);
@@ -264,134 +519,7 @@ __global__ void __launch_bounds__(kScanThreads) vanguard_kernel(IndexView ix, Se
         }
         tk.flush(kKeyMax);  // includes the barrier that frees stage buffer b
     }
-    const int total = n_total;
-    const int nkeep = min(total, sv.keep);
-    if (threadIdx.x == 0) {
-        s_base = nkeep ? atomicAdd(sv.cand_cnt + q, static_cast<uint32_t>(nkeep)) : 0u;
-        sv.bound[(size_t)q * sv.veff + r] = total <= sv.keep ? kKeyMax : s_keys[sv.keep - 1];
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < nkeep; i += blockDim.x) {
-        const uint32_t slot = s_base + i;
-        const uint32_t gid = static_cast<uint32_t>(s_keys[i] & 0xFFFFFFFFu);
-        if (slot < static_cast<uint32_t>(sv.cap))
-            sv.cand_rec[(size_t)q * sv.cap + slot] = gid | (static_cast<uint64_t>(r) << 32);
-        else
-            atomicOr(sv.err, kDevCandidateOverflow);
-    }
-}
-
-// ---- main scan: persistent CTAs over (cluster, <= 32 pairs) items --------------------
-template <int G16>
-__global__ void __launch_bounds__(kScanThreads, 2) scan_main_kernel(
-    IndexView ix, SearchView sv, const ScanItem *__restrict__ items,
-    const uint32_t *__restrict__ n_items_ptr, const uint32_t *__restrict__ pairs,
-    int *__restrict__ item_counter) {
-    using Sh = ScanShape<G16>;
-    constexpr int TV = Sh::TV, W4 = Sh::W4;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    uint4 *stage = reinterpret_cast<uint4 *>(smem_raw);
-    uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + 2 * Sh::kStageEntries);
-    __shared__ __align__(8) uint64_t bars[2];
-    __shared__ uint64_t s_bnd[kMaxPairsPerItem];
-    __shared__ float s_T1[kMaxPairsPerItem], s_g[kMaxPairsPerItem], s_k1[kMaxPairsPerItem],
-        s_w[kMaxPairsPerItem], s_gerr[kMaxPairsPerItem];
-    __shared__ int s_q[kMaxPairsPerItem], s_r[kMaxPairsPerItem];
-    __shared__ int s_item, s_abort;
-
-    if (threadIdx.x == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
-        fence_barrier_init();
-        s_abort = 0;
-    }
-    __syncthreads();
-    const uint32_t n_items = *n_items_ptr;
-    const int lane = threadIdx.x & 31;
-    uint32_t phase[2] = {0, 0};
-    while (true) {
-        if (threadIdx.x == 0) s_item = atomicAdd(item_counter, 1);
-        __syncthreads();
-        const int it = s_item;
-        if (it >= static_cast<int>(n_items)) break;
-        const ScanItem item = items[it];
-        const int c = static_cast<int>(item.cluster);
-        const uint32_t s = ix.cl_start[c];
-        const int n = static_cast<int>(ix.cl_size[c]);
-        const int pc = static_cast<int>(item.pair_count);
-        const size_t cbase = (size_t)(G16 + 1) * s;
-        const int ntiles = (n + TV - 1) / TV;
-        if (threadIdx.x == 0 && ntiles > 0)
-            issue_tile<G16>(stage, &bars[0], ix.scan4, cbase, n, 0, min(TV, n));
-        if (threadIdx.x < pc) {
-            const uint32_t pr = pairs[item.pair_begin + threadIdx.x];
-            const int q = static_cast<int>(pr >> 16), r = static_cast<int>(pr & 0xFFFFu);
-            const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
-            const QueryScalars qs = sv.scal[q];
-            s_q[threadIdx.x] = q;
-            s_r[threadIdx.x] = r;
-            s_T1[threadIdx.x] = sv.T1[q];
-            s_g[threadIdx.x] = g;
-            s_k1[threadIdx.x] = qs.k1;
-            s_w[threadIdx.x] = qs.width;
-            s_gerr[threadIdx.x] = __fsqrt_rn(fmaxf(g, 0.0f));
-            s_bnd[threadIdx.x] = r < sv.veff ? sv.bound[(size_t)q * sv.veff + r] : 0ull;
-        }
-        __syncthreads();
-        for (int i = threadIdx.x; i < pc * 8 * W4; i += blockDim.x) {
-            const int j = i / (8 * W4);
-            s_planes[i] = sv.planes[(size_t)s_q[j] * 8 * W4 + (i - j * 8 * W4)];
-        }
-        __syncthreads();
-        for (int t = 0; t < ntiles; ++t) {
-            const int b = t & 1;
-            const int v0 = t * TV, tv = min(TV, n - v0);
-            if (!mbar_wait_bounded(&bars[b], phase[b], sv.err)) s_abort = 1;
-            phase[b] ^= 1;
-            __syncthreads();
-            if (s_abort) return;
-            if (threadIdx.x == 0 && t + 1 < ntiles)
-                issue_tile<G16>(stage + (b ^ 1) * Sh::kStageEntries, &bars[b ^ 1], ix.scan4, cbase,
-                                n, v0 + TV, min(TV, n - v0 - TV));
-            const uint4 *sb = stage + b * Sh::kStageEntries;
-            for (int base = 0; base < tv; base += kScanThreads) {
-                const int i = base + threadIdx.x;
-                const bool valid = i < tv;
-                uint4 code[G16];
-                float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-                for (int gg = 0; gg < G16; ++gg) code[gg] = valid ? sb[gg * TV + i] : make_uint4(0, 0, 0, 0);
-                if (valid) {
-                    const uint4 fr = sb[G16 * TV + i];
-                    f = make_float4(__uint_as_float(fr.x), __uint_as_float(fr.y),
-                                    __uint_as_float(fr.z), 0.0f);
-                }
-                const uint32_t gid = s + static_cast<uint32_t>(v0 + i);
-                for (int j = 0; j < pc; ++j) {
-                    const int ip = ip_int_from_planes<G16>(code, s_planes + j * 8 * W4);
-                    const float ip1 = __fadd_rn(__fmul_rn(s_w[j], (float)ip), 0.0f);
-                    const float low = lower_bound_dist(f, ip1, s_g[j], s_k1[j], s_gerr[j]);
-                    const bool cand = valid && (low < s_T1[j]) && (make_key(low, gid) > s_bnd[j]);
-                    const uint32_t mask = __ballot_sync(0xffffffffu, cand);
-                    if (mask) {
-                        const int leader = __ffs(mask) - 1;
-                        uint32_t slot0 = 0;
-                        if (lane == leader) slot0 = atomicAdd(sv.cand_cnt + s_q[j], __popc(mask));
-                        slot0 = __shfl_sync(0xffffffffu, slot0, leader);
-                        if (cand) {
-                            const uint32_t slot = slot0 + __popc(mask & ((1u << lane) - 1u));
-                            if (slot < static_cast<uint32_t>(sv.cap))
-                                sv.cand_rec[(size_t)s_q[j] * sv.cap + slot] =
-                                    gid | (static_cast<uint64_t>(s_r[j]) << 32);
-                            else
-                                atomicOr(sv.err, kDevCandidateOverflow);
-                        }
-                    }
-                }
-            }
-            __syncthreads();  // stage buffer b is free again
-        }
-    }
+    write_seeds(sv, q, r, n_total, s_keys, &s_base);
 }
 
 }  // namespace cora

@@ -151,6 +151,14 @@ int cora_get_last_stage_ms(cora_engine *engine, float *h_out, uint64_t n);
  * reused, or here. */
 int cora_stage_totals(cora_engine *engine, double *h_out, uint64_t n, uint64_t *h_count);
 int cora_stage_reset(cora_engine *engine);
+/* Budget (bytes, default 16 GiB, capped at a quarter of free HBM) of the buffer that keeps
+ * the vanguard pairs' 1-bit lower bounds between the seeding and main passes, so that the
+ * vanguard clusters are scanned once. prepare_workspace sizes it for the worst case
+ * (every query probing the largest clusters); above the budget the vanguard clusters are
+ * rescanned instead (same results). 0 forces rescanning. Set before prepare_workspace. */
+int cora_set_vanguard_lows_budget(cora_engine *engine, uint64_t bytes);
+/* 1 when the prepared workspace keeps vanguard lower bounds, 0 when it rescans, -1 on NULL. */
+int cora_get_vanguard_mode(const cora_engine *engine);
 /* Candidate capacity per query of the current workspace (array 7 above is nq x cap). */
 uint64_t cora_get_candidate_capacity(const cora_engine *engine);
 

@@ -21,9 +21,11 @@ def cb():
     return coraanns_b200
 
 
-def _engine(cb, path=None, sd=None, nq=1, k=10, nprobe=1, vanguard=5):
+def _engine(cb, path=None, sd=None, nq=1, k=10, nprobe=1, vanguard=5, mode="lows"):
     e = cb.HybridIndex(0)
     e.set_vanguard_size(vanguard)
+    if mode == "rescan":
+        e.set_vanguard_lows_budget(0)
     if path is not None:
         e.load_index_file(path)
     else:
@@ -51,18 +53,19 @@ def _check_stages(e, q, k, nprobe, ref, tag):
         f"{tag}: candidate counts"
 
 
-@pytest.mark.parametrize("loader", ["file", "raw"])
+@pytest.mark.parametrize("loader,mode", [("file", "lows"), ("raw", "lows"), ("file", "rescan")])
 @pytest.mark.parametrize("name", GOLDEN_NAMES)
-def test_golden_parity(cb, golden, name, loader):
+def test_golden_parity(cb, golden, name, loader, mode):
     path, z = golden[name]
     q = z["queries"]
     grid = z["grid"]
     kmax, npmax = int(grid[:, 0].max()), int(grid[:, 1].max())
     if loader == "file":
-        e = _engine(cb, path=path, nq=len(q), k=kmax, nprobe=npmax)
+        e = _engine(cb, path=path, nq=len(q), k=kmax, nprobe=npmax, mode=mode)
     else:
         e = _engine(cb, sd=po.search_data(po.read_ivf_file(path)), nq=len(q), k=kmax,
-                    nprobe=npmax)
+                    nprobe=npmax, mode=mode)
+    assert e.get_vanguard_mode() == (1 if mode == "lows" else 0)
     for k, nprobe, van in grid:
         k, nprobe, van = int(k), int(nprobe), int(van)
         tag = f"{name}/{loader} k{k}_np{nprobe}_v{van}"
@@ -91,20 +94,22 @@ def _synthetic(n, dim, nlist, nq, seed, sigma=0.25):
     return sd, q
 
 
-@pytest.mark.parametrize("n,dim,nlist,nq,k,nprobe,van", [
-    (200_000, 96, 256, 256, 10, 16, 5),
-    (200_000, 96, 256, 64, 100, 24, 5),
-    (60_000, 768, 64, 48, 10, 8, 5),
-    (100_000, 128, 128, 300, 10, 32, 0),
+@pytest.mark.parametrize("n,dim,nlist,nq,k,nprobe,van,mode", [
+    (200_000, 96, 256, 256, 10, 16, 5, "lows"),
+    (200_000, 96, 256, 256, 10, 16, 5, "rescan"),
+    (200_000, 96, 256, 64, 100, 24, 5, "lows"),
+    (60_000, 768, 64, 48, 10, 8, 5, "lows"),
+    (60_000, 768, 64, 48, 10, 8, 3, "rescan"),
+    (100_000, 128, 128, 300, 10, 32, 0, "lows"),
 ])
-def test_live_oracle_parity_larger(cb, n, dim, nlist, nq, k, nprobe, van):
+def test_live_oracle_parity_larger(cb, n, dim, nlist, nq, k, nprobe, van, mode):
     """Bit-exact parity with the oracle on indexes larger than the fixtures (more tiles per
-    cluster, more pairs per item, D = 768)."""
+    cluster, more pairs per item, D = 768), in both vanguard modes."""
     sd, q = _synthetic(n, dim, nlist, nq, seed=n + dim)
     o = po.OracleIndex(sd)
     ref = o.search(q, k, nprobe, vanguard=van, with_details=True,
                    cand_cap=0)
-    e = _engine(cb, sd=sd, nq=nq, k=k, nprobe=nprobe, vanguard=van)
+    e = _engine(cb, sd=sd, nq=nq, k=k, nprobe=nprobe, vanguard=van, mode=mode)
     e.reset_buffer(q)
     d, i = e.search(q, k, nprobe)
     _check_stages(e, q, k, nprobe, ref, f"synthetic n{n} d{dim}")
