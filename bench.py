@@ -347,6 +347,7 @@ def main():
     search_dev(chosen)
     eng.check_device()
     probes = eng.debug("probe_ids", nq, chosen)
+    cand_per_query = eng.get_last_submitted_count() / nq
     sizes = sd["sizes"].astype(np.int64)
     D = int(sd["D"])
     scan_bytes = int(sizes[probes].sum()) * (D // 8 + 12)
@@ -421,6 +422,8 @@ def main():
             config=dict(workload=f"{args.config}: {cfg['n']} x d{cfg['dim']} L2, nlist {cfg['nlist']}, "
                                  f"8-bit RaBitQ, {nq} queries, topk {k}",
                         nprobe=chosen, recall_at_10=sweep.get(chosen), recall_sweep=sweep,
+                        candidates_per_query=cand_per_query,
+                        vanguard_mode="lows" if mode == 1 else "rescan",
                         l2_flush="inputs exceed L2 (index codes > 126 MB)",
                         stage_ms=stage_avg, parallelism=f"replicas x{world}" if world > 1 else "single"),
             roofline=roofline, cpu_baseline=cpu_base,

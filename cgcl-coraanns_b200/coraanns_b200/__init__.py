@@ -88,8 +88,9 @@ _sig("cora_stage_reset", C.c_int, _p)
 _sig("cora_set_vanguard_lows_budget", C.c_int, _p, _u64)
 _sig("cora_get_vanguard_mode", C.c_int, _p)
 
-STAGES = ("rotate_prep", "centroid_dist", "select_probes", "pair_grouping", "vanguard_scan",
-          "seed_refine", "threshold", "main_scan", "main_refine", "merge")
+STAGES = ("rotate_prep", "centroid_dist", "select_probes", "vanguard_grouping",
+          "vanguard_scan", "vanguard_select", "seed_refine", "threshold", "main_grouping",
+          "main_scan", "vanguard_filter", "main_refine", "merge")
 
 
 class LogicError(Exception):

@@ -85,7 +85,7 @@ struct Engine {
     cudaEvent_t ev_filter0 = nullptr, ev_filter1 = nullptr;
     // Stage boundary events: a ring of kRing event sets so that timing many back-to-back
     // searches never makes the host wait; a set is read back when it is reused.
-    static constexpr int kStages = 10, kRing = 16;
+    static constexpr int kStages = 13, kRing = 16;
     cudaEvent_t ev_stage[kRing][kStages + 1] = {};
     int ring_next = 0, ring_used = 0, ring_last = -1;
     double stage_sum[kStages] = {};
@@ -623,51 +623,52 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     }
     mark(4, st);
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter0, st));
-    if (lows_mode) {
+    if (lows_mode)
         dispatch_scan(G16, L, ScanPhase::kWriteLows);
-        const size_t sm = (size_t)next_pow2(static_cast<int>(keep)) * 8;
+    else
+        dispatch_scan(G16, L, ScanPhase::kRescanVanguard);
+    mark(5, st);
+    if (lows_mode) {
+        const size_t sm = (size_t)next_pow2(static_cast<int>(keep)) * 8 + kSelectStage * 4;
         CUDA_TRY(cudaFuncSetAttribute(vanguard_select_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
         vanguard_select_kernel<<<n_van, 256, sm, st>>>(ix, sv, own);
         CUDA_TRY(cudaGetLastError());
-    } else {
-        dispatch_scan(G16, L, ScanPhase::kRescanVanguard);
     }
-    mark(5, st);
+    mark(6, st);
     const size_t refine_sm = (size_t)D * 4 + np * sizeof(ProbeInfo);
     CUDA_TRY(cudaFuncSetAttribute(refine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)refine_sm));
     refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 0);
     CUDA_TRY(cudaGetLastError());
-    mark(6, st);
+    mark(7, st);
     const size_t sel_sm = (size_t)next_pow2(ik) * 8;
     CUDA_TRY(cudaFuncSetAttribute(threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)sel_sm));
     threshold_kernel<<<inq, 256, sel_sm, st>>>(sv);
     CUDA_TRY(cudaGetLastError());
-    mark(7, st);
+    mark(8, st);
     // 4. main pass against T1: the other probes are scanned; the vanguard probes are either
     //    filtered from their stored lows or rescanned, skipping their seeds in both cases.
+    group_pairs(lows_mode ? iveff : 0, inp);
+    mark(9, st);
+    dispatch_scan(G16, L, ScanPhase::kMain);
+    mark(10, st);
     if (lows_mode) {
-        group_pairs(iveff, inp);
-        dispatch_scan(G16, L, ScanPhase::kMain);
         vanguard_filter_kernel<<<n_van, 256, 0, st>>>(ix, sv, own);
         CUDA_TRY(cudaGetLastError());
-    } else {
-        group_pairs(0, inp);
-        dispatch_scan(G16, L, ScanPhase::kMain);
     }
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));
-    mark(8, st);
+    mark(11, st);
     refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 1);
     CUDA_TRY(cudaGetLastError());
-    mark(9, st);
+    mark(12, st);
     // 5. final top-k
     CUDA_TRY(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)sel_sm));
     merge_kernel<<<inq, 256, sel_sm, st>>>(sv, d_od, d_oi, stats.p);
     CUDA_TRY(cudaGetLastError());
-    mark(10, st);
+    mark(13, st);
 }
 
 // ------------------------------------------------------------------------------------

@@ -25,9 +25,11 @@ struct ProbeInfo {  // per (query, probe rank), staged in shared memory by refin
 
 // Inner product of the full 8-bit code of one vector with the rotated query x (in shared
 // memory): lane l accumulates dims 64b+l and 64b+32+l of every 64-dim block b in fp64
-// (exact products), then an xor butterfly combines the lanes; every lane returns the sum.
-__device__ __forceinline__ double code_ip(const float *__restrict__ x, const uint4 *code_base,
-                                          uint32_t n, const uint8_t *ex, int nblocks, int lane) {
+// (exact products); this returns the lane's partial sum, and an xor butterfly over the
+// warp (lane_sum) combines the lanes so that every lane holds the total.
+__device__ __forceinline__ double code_ip_partial(const float *__restrict__ x,
+                                                  const uint4 *code_base, uint32_t n,
+                                                  const uint8_t *ex, int nblocks, int lane) {
     double acc = 0.0;
     for (int b = 0; b < nblocks; ++b) {
         const uint4 cw = __ldg(code_base + (size_t)(b >> 1) * n);
@@ -51,15 +53,21 @@ __device__ __forceinline__ double code_ip(const float *__restrict__ x, const uin
         acc = __fma_rn((double)x[64 * b + lane], (double)(128u * b0 + u0), acc);
         acc = __fma_rn((double)x[64 * b + 32 + lane], (double)(128u * b1 + u1), acc);
     }
+    return acc;
+}
+
+__device__ __forceinline__ double lane_sum(double acc) {
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1)
         acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
     return acc;
 }
 
-// One CTA per query; warp per candidate, two candidates in flight per warp. mode 0 refines
-// the vanguard seeds [0, cnt) and records the seed count; mode 1 refines the main
-// candidates [seed_cnt, cnt). Dynamic shared memory: D floats + nprobe ProbeInfo.
+constexpr int kRefineInFlight = 4;  // candidates per warp whose loads overlap
+
+// One CTA per query; warp per candidate, kRefineInFlight candidates in flight per warp.
+// mode 0 refines the vanguard seeds [0, cnt) and records the seed count; mode 1 refines the
+// main candidates [seed_cnt, cnt). Dynamic shared memory: D floats + nprobe ProbeInfo.
 __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, SearchView sv,
                                                                 int mode) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -90,28 +98,30 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
     const float kb = sv.scal[q].kb;
     const int nblocks = ix.D / 64;
     const size_t planes_per = static_cast<size_t>(ix.G16 + 1);
-    for (uint32_t i0 = from + warp; i0 < to; i0 += 2 * kWarps) {
-        const uint32_t i1 = i0 + kWarps;
-        const bool has1 = i1 < to;
-        const uint64_t rec0 = sv.cand_rec[(size_t)q * sv.cap + i0];
-        const uint64_t rec1 = has1 ? sv.cand_rec[(size_t)q * sv.cap + i1] : rec0;
-        const uint32_t gid0 = static_cast<uint32_t>(rec0 & 0xFFFFFFFFu);
-        const uint32_t gid1 = static_cast<uint32_t>(rec1 & 0xFFFFFFFFu);
-        const ProbeInfo p0 = pinfo[rec0 >> 32], p1 = pinfo[rec1 >> 32];
-        const float2 f0 = ix.ex_factors[gid0], f1 = ix.ex_factors[gid1];
-        const uint32_t id0 = ix.ids[gid0], id1 = ix.ids[gid1];
-        const double a0 = code_ip(x, ix.scan4 + planes_per * p0.start + (gid0 - p0.start), p0.size,
-                                  ix.long_codes + (size_t)gid0 * ix.LC, nblocks, lane);
-        const double a1 = code_ip(x, ix.scan4 + planes_per * p1.start + (gid1 - p1.start), p1.size,
-                                  ix.long_codes + (size_t)gid1 * ix.LC, nblocks, lane);
-        if (lane == 0) {
-            const float ex0 = __fadd_rn(__fadd_rn(f0.x, p0.g),
-                                        __fmul_rn(f0.y, __fadd_rn(__double2float_rn(a0), kb)));
-            sv.cand_key[(size_t)q * sv.cap + i0] = make_key(ex0, id0);
-            if (has1) {
-                const float ex1 = __fadd_rn(__fadd_rn(f1.x, p1.g),
-                                            __fmul_rn(f1.y, __fadd_rn(__double2float_rn(a1), kb)));
-                sv.cand_key[(size_t)q * sv.cap + i1] = make_key(ex1, id1);
+    for (uint32_t i0 = from + warp; i0 < to; i0 += kRefineInFlight * kWarps) {
+        uint32_t idx[kRefineInFlight], gid[kRefineInFlight];
+        ProbeInfo pi[kRefineInFlight];
+        double part[kRefineInFlight];
+#pragma unroll
+        for (int t = 0; t < kRefineInFlight; ++t) {
+            idx[t] = min(i0 + t * kWarps, to - 1);  // duplicates of the last one are not stored
+            const uint64_t rec = sv.cand_rec[(size_t)q * sv.cap + idx[t]];
+            gid[t] = static_cast<uint32_t>(rec & 0xFFFFFFFFu);
+            pi[t] = pinfo[rec >> 32];
+        }
+#pragma unroll
+        for (int t = 0; t < kRefineInFlight; ++t)
+            part[t] = code_ip_partial(x, ix.scan4 + planes_per * pi[t].start + (gid[t] - pi[t].start),
+                                      pi[t].size, ix.long_codes + (size_t)gid[t] * ix.LC, nblocks,
+                                      lane);
+#pragma unroll
+        for (int t = 0; t < kRefineInFlight; ++t) {
+            const double ip = lane_sum(part[t]);
+            if (lane == 0 && i0 + t * kWarps < to) {
+                const float2 f = ix.ex_factors[gid[t]];
+                const float ex_d = __fadd_rn(__fadd_rn(f.x, pi[t].g),
+                                             __fmul_rn(f.y, __fadd_rn(__double2float_rn(ip), kb)));
+                sv.cand_key[(size_t)q * sv.cap + idx[t]] = make_key(ex_d, ix.ids[gid[t]]);
             }
         }
     }

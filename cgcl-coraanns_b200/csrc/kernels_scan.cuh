@@ -397,8 +397,10 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
 }
 
 // ---- lows mode: per vanguard pair seed selection and candidate filtering -------------
-// One CTA per vanguard pair: seeds are the best `keep` keys among low < T0.
-// Dynamic shared memory: next_pow2(keep) keys.
+// One CTA per vanguard pair: seeds are the best `keep` keys among low < T0. The pair's lows
+// are staged in shared memory when they fit (kSelectStage floats), so the radix passes
+// read them from there. Dynamic shared memory: next_pow2(keep) keys + kSelectStage floats.
+constexpr uint32_t kSelectStage = 8192;
 __global__ void __launch_bounds__(256) vanguard_select_kernel(IndexView ix, SearchView sv,
                                                               const uint8_t *__restrict__ owned) {
     extern __shared__ uint64_t s_keys[];
@@ -411,13 +413,21 @@ __global__ void __launch_bounds__(256) vanguard_select_kernel(IndexView ix, Sear
     if (owned && !owned[c]) return;
     const uint32_t s = ix.cl_start[c];
     const uint32_t n = ix.cl_size[c];
-    const float *L = sv.lows + sv.vg_off[pi];
+    const float *Lg = sv.lows + sv.vg_off[pi];
+    float *s_lows = reinterpret_cast<float *>(s_keys + next_pow2(sv.keep));
+    const bool staged = n <= kSelectStage;
+    const float *L = staged ? s_lows : Lg;
     const float T0 = sv.T0[q];
     if (threadIdx.x == 0) s_total = 0;
     __syncthreads();
     int mine = 0;
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) mine += L[i] < T0;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const float l = Lg[i];
+        if (staged) s_lows[i] = l;
+        mine += l < T0;
+    }
     atomicAdd(&s_total, mine);
+    __syncthreads();
     auto key_at = [&](uint32_t i) -> uint64_t {
         const float l = L[i];
         return l < T0 ? make_key(l, s + i) : kKeyMax;

@@ -142,8 +142,9 @@ float cora_get_last_gpu_filter_ms(const cora_engine *engine);
 int cora_debug_copy(cora_engine *engine, int what, void *h_out, uint64_t bytes);
 /* Per-stage device times (ms) of the last search run with profiling enabled, from CUDA
  * events recorded between the launches on the search stream: 0 rotation + query prep,
- * 1 coarse distances, 2 top-nprobe, 3 pair grouping, 4 vanguard scan, 5 seed refine,
- * 6 threshold, 7 main scan, 8 main refine, 9 merge. Writes min(n, 10) values. */
+ * 1 coarse distances, 2 top-nprobe, 3 vanguard pair grouping, 4 vanguard scan (lows pass
+ * or rescan), 5 vanguard seed selection, 6 seed refine, 7 threshold, 8 main pair grouping,
+ * 9 main scan, 10 vanguard lows filter, 11 main refine, 12 merge. Writes min(n, 13). */
 int cora_get_last_stage_ms(cora_engine *engine, float *h_out, uint64_t n);
 /* Sums of the same per-stage times over every profiled search since cora_stage_reset();
  * *h_count receives the number of searches summed. Reading never stalls searches that are
