@@ -407,7 +407,7 @@ def main():
                          "of codes touched; cross-query reuse lets this exceed the physical DRAM "
                          "traffic)")
     mode = eng.get_vanguard_mode()
-    launches = (20 if mode == 1 else 13) * args.steps
+    launches = (21 if mode == 1 else 13) * args.steps
 
     cpu_base = None
     if rank == 0 and not args.no_cpu_baseline and index_path is not None:

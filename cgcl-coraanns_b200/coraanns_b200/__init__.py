@@ -39,7 +39,8 @@ EXPORTS = [
     "cora_set_ip_kernel_type", "cora_get_ip_kernel_type", "cora_get_last_submitted_count",
     "cora_get_last_refined_count", "cora_get_last_spilled_count", "cora_get_last_gpu_filter_ms",
     "cora_debug_copy", "cora_get_last_stage_ms", "cora_stage_totals", "cora_stage_reset",
-    "cora_set_vanguard_lows_budget", "cora_get_vanguard_mode", "cora_get_candidate_capacity",
+    "cora_set_vanguard_lows_budget", "cora_set_tuning", "cora_get_vanguard_mode",
+    "cora_get_candidate_capacity",
 ]
 
 _p = C.c_void_p
@@ -87,6 +88,7 @@ _sig("cora_stage_totals", C.c_int, _p, _p, _u64, _p)
 _sig("cora_stage_reset", C.c_int, _p)
 _sig("cora_set_vanguard_lows_budget", C.c_int, _p, _u64)
 _sig("cora_get_vanguard_mode", C.c_int, _p)
+_sig("cora_set_tuning", C.c_int, _p, C.c_char_p, C.c_int64)
 
 STAGES = ("rotate_prep", "centroid_dist", "select_probes", "vanguard_grouping",
           "vanguard_scan", "vanguard_select", "seed_refine", "threshold", "main_grouping",
@@ -265,6 +267,9 @@ class HybridIndex:
 
     def set_vanguard_lows_budget(self, nbytes):
         _check(_lib.cora_set_vanguard_lows_budget(self._h, int(nbytes)))
+
+    def set_tuning(self, key: str, value: int):
+        _check(_lib.cora_set_tuning(self._h, key.encode(), int(value)))
 
     def get_vanguard_mode(self):
         """1: vanguard lower bounds kept in HBM between passes; 0: vanguard rescan."""

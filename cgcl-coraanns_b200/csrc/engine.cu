@@ -112,6 +112,7 @@ struct Engine {
     // Upper bound on the HBM buffer holding the vanguard pairs' lower bounds; larger
     // worst cases fall back to rescanning the vanguard clusters.
     uint64_t lows_budget = 16ull << 30;
+    int warp_select_limit = kWarpSelectBuf;  // see vanguard_select_warp_kernel
 
     // workspace
     bool ws_ready = false;
@@ -121,6 +122,7 @@ struct Engine {
     DevBuf<uint32_t> planes, cand_cnt, seed_cnt, pair_cnt, pair_off, pair_cur, item_off, pairs,
         n_items, out_i;
     DevBuf<int> probe_ids, item_counter, err;
+    DevBuf<uint32_t> select_fallback;  // [0] count, [1..] vanguard pairs for block selection
     DevBuf<uint64_t> bound, cand_rec, cand_key, vg_off;
     DevBuf<float> lows;
     std::vector<uint32_t> h_sizes_sorted;  // cluster sizes, descending (lows worst case)
@@ -253,6 +255,7 @@ struct Engine {
         Tcap.alloc(max_q);
         bound.alloc(max_q * std::max<uint64_t>(ws_vg, 1));
         vg_off.alloc(max_q * std::max<uint64_t>(ws_vg, 1) + 1);
+        select_fallback.alloc(max_q * std::max<uint64_t>(ws_vg, 1) + 1);
         {
             // worst case of the lows buffer: every query probes the ws_vg largest clusters
             uint64_t worst = 0;
@@ -298,6 +301,7 @@ struct Engine {
         err.release();
         bound.release();
         vg_off.release();
+        select_fallback.release();
         lows.release();
         cand_rec.release();
         cand_key.release();
@@ -588,7 +592,8 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
                  static_cast<int>(nlist), static_cast<int>(D), G16, LC};
     SearchView sv{inq, ik, inp, static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
                   scal.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p, cand_cnt.p,
-                  seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n, err.p};
+                  seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n, err.p,
+                  warp_select_limit};
     const uint8_t *own = owned.n ? owned.p : nullptr;
     const int rescan_sort_n = next_pow2(static_cast<int>(keep) + (G16 <= 2 ? 512 : 256));
     ScanLaunch L{ix, sv, rescan_sort_n, nq * veff, items.p, n_items.p, pairs.p, item_counter.p,
@@ -632,7 +637,18 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
         const size_t sm = (size_t)next_pow2(static_cast<int>(keep)) * 8 + kSelectStage * 4;
         CUDA_TRY(cudaFuncSetAttribute(vanguard_select_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        vanguard_select_kernel<<<n_van, 256, sm, st>>>(ix, sv, own);
+        if (keep <= static_cast<uint64_t>(kWarpSelectMax)) {
+            // one warp per pair; the rare pair with too many keys below the first bound
+            // is finished by a grid-stride block selection over the queued list
+            CUDA_TRY(cudaMemsetAsync(select_fallback.p, 0, 4, st));
+            vanguard_select_warp_kernel<<<(n_van + 7) / 8, 256, 0, st>>>(ix, sv, own,
+                                                                         select_fallback.p);
+            CUDA_TRY(cudaGetLastError());
+            vanguard_select_kernel<<<static_cast<unsigned>(2 * num_sms), 256, sm, st>>>(
+                ix, sv, own, select_fallback.p);
+        } else {
+            vanguard_select_kernel<<<n_van, 256, sm, st>>>(ix, sv, own, nullptr);
+        }
         CUDA_TRY(cudaGetLastError());
     }
     mark(6, st);
@@ -655,7 +671,7 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     dispatch_scan(G16, L, ScanPhase::kMain);
     mark(10, st);
     if (lows_mode) {
-        vanguard_filter_kernel<<<n_van, 256, 0, st>>>(ix, sv, own);
+        vanguard_filter_kernel<<<(n_van + 7) / 8, 256, 0, st>>>(ix, sv, own);
         CUDA_TRY(cudaGetLastError());
     }
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));
@@ -1054,6 +1070,24 @@ int cora_set_vanguard_lows_budget(cora_engine *engine, uint64_t bytes) {
         Engine &e = eng(engine);
         if (e.ws_ready) cora::fail(CORA_ESTATE, "set the lows budget before prepare_workspace");
         e.lows_budget = bytes;
+    });
+}
+
+int cora_set_tuning(cora_engine *engine, const char *key, int64_t value) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        const std::string k = key ? key : "";
+        if (k == "warp_select_limit") {
+            if (value < 0 || value > cora::kWarpSelectBuf)
+                cora::fail(CORA_EINVAL, "warp_select_limit must be in [0, 256]");
+            e.warp_select_limit = static_cast<int>(value);
+        } else if (k == "vanguard_lows_budget") {
+            if (value < 0) cora::fail(CORA_EINVAL, "vanguard_lows_budget must be >= 0");
+            if (e.ws_ready) cora::fail(CORA_ESTATE, "set the lows budget before prepare_workspace");
+            e.lows_budget = static_cast<uint64_t>(value);
+        } else {
+            cora::fail(CORA_EINVAL, "unknown tuning key: " + k);
+        }
     });
 }
 

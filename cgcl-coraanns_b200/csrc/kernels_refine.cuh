@@ -16,66 +16,51 @@
 
 namespace cora {
 
-constexpr int kRefineThreads = 256;
+constexpr int kRefineThreads = 128;
 
 struct ProbeInfo {  // per (query, probe rank), staged in shared memory by refine_kernel
     uint32_t start, size;
     float g;
 };
 
-// Inner product of the full 8-bit code of one vector with the rotated query x (in shared
-// memory): lane l accumulates dims 64b+l and 64b+32+l of every 64-dim block b in fp64
-// (exact products); this returns the lane's partial sum, and an xor butterfly over the
-// warp (lane_sum) combines the lanes so that every lane holds the total.
-__device__ __forceinline__ double code_ip_partial(const float *__restrict__ x,
-                                                  const uint4 *code_base, uint32_t n,
-                                                  const uint8_t *ex, int nblocks, int lane) {
-    double acc = 0.0;
-    for (int b = 0; b < nblocks; ++b) {
-        const uint4 cw = __ldg(code_base + (size_t)(b >> 1) * n);
-        const uint32_t w0 = (b & 1) ? cw.z : cw.x;
-        const uint32_t w1 = (b & 1) ? cw.w : cw.y;
-        const uint8_t *p = ex + 56 * b;
-        const unsigned long long top = __ldg(reinterpret_cast<const unsigned long long *>(p + 48));
-        uint32_t u0 = __ldg(p + lane) & 63u;
-        uint32_t u1;
-        if (lane < 16) {
-            u1 = __ldg(p + 32 + lane) & 63u;
+// One 64-dim block of the full 8-bit code inner product, continuing the fp64 chain `acc`
+// in ascending dimension order (every product is exact in fp64). `e` holds the block's 56
+// ex-code bytes (pack_excode.hpp:216-264 layout: bytes 0..47 carry the low 6 bits of dims
+// 0..47 and 2-bit slices of dims 48..63, bytes 48..55 the top bits), w0 / w1 the 1-bit
+// code words of dims 0..31 / 32..63, x the block's 64 rotated query values.
+__device__ __forceinline__ double block_code_ip(const float *__restrict__ x, const uint64_t (&e)[7],
+                                                uint32_t w0, uint32_t w1, double acc) {
+#pragma unroll
+    for (int d = 0; d < 64; ++d) {
+        uint32_t u;
+        if (d < 48) {
+            u = static_cast<uint32_t>(e[d >> 3] >> (8 * (d & 7))) & 63u;
         } else {
-            const int k = lane - 16;
-            u1 = (static_cast<uint32_t>(__ldg(p + k)) >> 6) |
-                 ((static_cast<uint32_t>(__ldg(p + 16 + k)) >> 6) << 2) |
-                 ((static_cast<uint32_t>(__ldg(p + 32 + k)) >> 6) << 4);
+            const int k = d - 48;
+            const uint32_t b0 = static_cast<uint32_t>(e[k >> 3] >> (8 * (k & 7))) & 0xFFu;
+            const uint32_t b1 = static_cast<uint32_t>(e[(16 + k) >> 3] >> (8 * ((16 + k) & 7))) & 0xFFu;
+            const uint32_t b2 = static_cast<uint32_t>(e[(32 + k) >> 3] >> (8 * ((32 + k) & 7))) & 0xFFu;
+            u = (b0 >> 6) | ((b1 >> 6) << 2) | ((b2 >> 6) << 4);
         }
-        u0 |= static_cast<uint32_t>((top >> (8 * (lane & 7) + (lane >> 3))) & 1ull) << 6;
-        u1 |= static_cast<uint32_t>((top >> (8 * (lane & 7) + 4 + (lane >> 3))) & 1ull) << 6;
-        const uint32_t b0 = (w0 >> (31 - lane)) & 1u, b1 = (w1 >> (31 - lane)) & 1u;
-        acc = __fma_rn((double)x[64 * b + lane], (double)(128u * b0 + u0), acc);
-        acc = __fma_rn((double)x[64 * b + 32 + lane], (double)(128u * b1 + u1), acc);
+        u |= static_cast<uint32_t>((e[6] >> (8 * (d & 7) + (d >> 3))) & 1ull) << 6;
+        const uint32_t w = d < 32 ? w0 : w1;
+        const uint32_t bit = (w >> (31 - (d & 31))) & 1u;
+        acc = __fma_rn((double)x[d], (double)(128u * bit + u), acc);
     }
     return acc;
 }
 
-__device__ __forceinline__ double lane_sum(double acc) {
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1)
-        acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
-    return acc;
-}
-
-constexpr int kRefineInFlight = 4;  // candidates per warp whose loads overlap
-
-// One CTA per query; warp per candidate, kRefineInFlight candidates in flight per warp.
-// mode 0 refines the vanguard seeds [0, cnt) and records the seed count; mode 1 refines the
-// main candidates [seed_cnt, cnt). Dynamic shared memory: D floats + nprobe ProbeInfo.
+// One CTA per query, one thread per candidate: every load of a candidate (1-bit code words,
+// ex code, factors, id) is issued before its fp64 chain, so a candidate costs one memory
+// round trip. mode 0 refines the vanguard seeds [0, cnt) and records the seed count; mode 1
+// refines the main candidates [seed_cnt, cnt). Dynamic shared memory: D floats + nprobe
+// ProbeInfo.
 __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, SearchView sv,
                                                                 int mode) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float *x = reinterpret_cast<float *>(smem_raw);
     ProbeInfo *pinfo = reinterpret_cast<ProbeInfo *>(x + ix.D);
     const int q = blockIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    constexpr int kWarps = kRefineThreads / 32;
     const uint32_t cnt = sv.cand_cnt[q];
     const uint32_t cap = static_cast<uint32_t>(sv.cap);
     uint32_t from, to;
@@ -98,32 +83,30 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
     const float kb = sv.scal[q].kb;
     const int nblocks = ix.D / 64;
     const size_t planes_per = static_cast<size_t>(ix.G16 + 1);
-    for (uint32_t i0 = from + warp; i0 < to; i0 += kRefineInFlight * kWarps) {
-        uint32_t idx[kRefineInFlight], gid[kRefineInFlight];
-        ProbeInfo pi[kRefineInFlight];
-        double part[kRefineInFlight];
+    for (uint32_t i = from + threadIdx.x; i < to; i += blockDim.x) {
+        const uint64_t rec = sv.cand_rec[(size_t)q * sv.cap + i];
+        const uint32_t gid = static_cast<uint32_t>(rec & 0xFFFFFFFFu);
+        const ProbeInfo p = pinfo[rec >> 32];
+        const uint4 *cb = ix.scan4 + planes_per * p.start + (gid - p.start);
+        const uint64_t *eb = reinterpret_cast<const uint64_t *>(ix.long_codes + (size_t)gid * ix.LC);
+        const float2 f = __ldg(ix.ex_factors + gid);
+        const uint32_t id = __ldg(ix.ids + gid);
+        double acc = 0.0;
+        for (int g = 0; 2 * g < nblocks; ++g) {
+            const uint4 cw = __ldg(cb + (size_t)g * p.size);
+            uint64_t e[7];
 #pragma unroll
-        for (int t = 0; t < kRefineInFlight; ++t) {
-            idx[t] = min(i0 + t * kWarps, to - 1);  // duplicates of the last one are not stored
-            const uint64_t rec = sv.cand_rec[(size_t)q * sv.cap + idx[t]];
-            gid[t] = static_cast<uint32_t>(rec & 0xFFFFFFFFu);
-            pi[t] = pinfo[rec >> 32];
-        }
+            for (int t = 0; t < 7; ++t) e[t] = __ldg(eb + 14 * g + t);
+            acc = block_code_ip(x + 128 * g, e, cw.x, cw.y, acc);
+            if (2 * g + 1 < nblocks) {
 #pragma unroll
-        for (int t = 0; t < kRefineInFlight; ++t)
-            part[t] = code_ip_partial(x, ix.scan4 + planes_per * pi[t].start + (gid[t] - pi[t].start),
-                                      pi[t].size, ix.long_codes + (size_t)gid[t] * ix.LC, nblocks,
-                                      lane);
-#pragma unroll
-        for (int t = 0; t < kRefineInFlight; ++t) {
-            const double ip = lane_sum(part[t]);
-            if (lane == 0 && i0 + t * kWarps < to) {
-                const float2 f = ix.ex_factors[gid[t]];
-                const float ex_d = __fadd_rn(__fadd_rn(f.x, pi[t].g),
-                                             __fmul_rn(f.y, __fadd_rn(__double2float_rn(ip), kb)));
-                sv.cand_key[(size_t)q * sv.cap + idx[t]] = make_key(ex_d, ix.ids[gid[t]]);
+                for (int t = 0; t < 7; ++t) e[t] = __ldg(eb + 14 * g + 7 + t);
+                acc = block_code_ip(x + 128 * g + 64, e, cw.z, cw.w, acc);
             }
         }
+        const float ex_d = __fadd_rn(__fadd_rn(f.x, p.g),
+                                     __fmul_rn(f.y, __fadd_rn(__double2float_rn(acc), kb)));
+        sv.cand_key[(size_t)q * sv.cap + i] = make_key(ex_d, id);
     }
 }
 

@@ -72,6 +72,7 @@ struct SearchView {
     uint64_t *vg_off;            // nq x veff + 1 offsets into lows
     uint64_t lows_cap;           // capacity of lows (floats)
     int *err;
+    int warp_select_limit;       // keys a warp may collect before queueing a block selection
 };
 
 // ---- per-cluster query grouping (CSR of (query, probe rank) pairs by cluster) --------
@@ -400,14 +401,35 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
 // One CTA per vanguard pair: seeds are the best `keep` keys among low < T0. The pair's lows
 // are staged in shared memory when they fit (kSelectStage floats), so the radix passes
 // read them from there. Dynamic shared memory: next_pow2(keep) keys + kSelectStage floats.
+// With `list` the CTAs serve the pairs queued there (list[0] pairs at list[1..]) in a
+// grid-stride loop; without it CTA i serves vanguard pair i.
 constexpr uint32_t kSelectStage = 8192;
+__device__ void select_pair_block(const IndexView &ix, const SearchView &sv,
+                                  const uint8_t *owned, int pi, uint64_t *s_keys, int *scratch,
+                                  int *s_total, uint32_t *s_base);
 __global__ void __launch_bounds__(256) vanguard_select_kernel(IndexView ix, SearchView sv,
-                                                              const uint8_t *__restrict__ owned) {
+                                                              const uint8_t *__restrict__ owned,
+                                                              const uint32_t *__restrict__ list) {
     extern __shared__ uint64_t s_keys[];
     __shared__ int scratch[256 + 3];
     __shared__ int s_total;
     __shared__ uint32_t s_base;
-    const int pi = blockIdx.x;
+    if (!list) {
+        select_pair_block(ix, sv, owned, blockIdx.x, s_keys, scratch, &s_total, &s_base);
+        return;
+    }
+    const uint32_t count = list[0];
+    for (uint32_t j = blockIdx.x; j < count; j += gridDim.x) {
+        select_pair_block(ix, sv, owned, static_cast<int>(list[1 + j]), s_keys, scratch, &s_total,
+                          &s_base);
+        __syncthreads();
+    }
+}
+
+__device__ void select_pair_block(const IndexView &ix, const SearchView &sv,
+                                  const uint8_t *owned, int pi, uint64_t *s_keys, int *scratch,
+                                  int *s_total_p, uint32_t *s_base_p) {
+    int &s_total = *s_total_p;
     const int q = pi / sv.veff, r = pi % sv.veff;
     const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
     if (owned && !owned[c]) return;
@@ -433,13 +455,16 @@ __global__ void __launch_bounds__(256) vanguard_select_kernel(IndexView ix, Sear
         return l < T0 ? make_key(l, s + i) : kKeyMax;
     };
     block_select_smallest(key_at, n, sv.keep, s_keys, scratch);
-    write_seeds(sv, q, r, s_total, s_keys, &s_base);
+    write_seeds(sv, q, r, s_total, s_keys, s_base_p);
 }
 
-// One CTA per vanguard pair: candidates low < T1 that are not seeds (key > boundary).
+// One warp per vanguard pair (8 per CTA): candidates low < T1 that are not seeds
+// (key > boundary), read from the pair's stored lows.
 __global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, SearchView sv,
                                                               const uint8_t *__restrict__ owned) {
-    const int pi = blockIdx.x;
+    const int lane = threadIdx.x & 31;
+    const int pi = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (pi >= sv.nq * sv.veff) return;  // warp-uniform
     const int q = pi / sv.veff, r = pi % sv.veff;
     const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
     if (owned && !owned[c]) return;
@@ -448,15 +473,127 @@ __global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, Sear
     const float *L = sv.lows + sv.vg_off[pi];
     const float T1 = sv.T1[q];
     const uint64_t bnd = sv.bound[(size_t)q * sv.veff + r];
-    const int lane = threadIdx.x & 31;
-    for (uint32_t base = 0; base < n; base += blockDim.x) {
-        const uint32_t i = base + threadIdx.x;
+    for (uint32_t base = 0; base < n; base += 32) {
+        const uint32_t i = base + lane;
         bool cand = false;
         if (i < n) {
             const float l = L[i];
             cand = (l < T1) && (make_key(l, s + i) > bnd);
         }
         emit_candidate(sv, cand, q, (s + i) | (static_cast<uint64_t>(r) << 32), lane);
+    }
+}
+
+// ---- warp-level seed selection for keep <= 32 -----------------------------------------
+constexpr int kWarpSelectMax = 32;   // largest `keep` handled one warp per pair
+constexpr int kWarpSelectBuf = 256;  // keys at or below the first threshold a warp may hold
+
+__device__ __forceinline__ uint64_t warp_sort_lane_keys(uint64_t v, int lane) {
+    // bitonic sort of one key per lane, ascending by lane index
+    for (int k = 2; k <= 32; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const uint64_t o = __shfl_xor_sync(0xffffffffu, v, j);
+            const bool up = (lane & k) == 0, lower = (lane & j) == 0;
+            v = (lower == up) ? (v < o ? v : o) : (v < o ? o : v);
+        }
+    }
+    return v;
+}
+
+__device__ __forceinline__ void warp_sort_smem(uint64_t *a, int n, int lane) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = lane; i < n; i += 32) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const uint64_t x = a[i], y = a[ixj];
+                    if ((x > y) == ((i & k) == 0)) {
+                        a[i] = y;
+                        a[ixj] = x;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+// One warp per vanguard pair (8 per CTA), keep <= 32. The keep-th smallest of the 32 lane
+// minima bounds the keep-th smallest key from above, so every seed is among the keys at or
+// below it; those (normally a few dozen) are collected and sorted. A pair whose collection
+// exceeds kWarpSelectBuf is queued in fallback[1..] (count in fallback[0]) for
+// vanguard_select_kernel.
+__global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
+    IndexView ix, SearchView sv, const uint8_t *__restrict__ owned,
+    uint32_t *__restrict__ fallback) {
+    __shared__ uint64_t buf[8][kWarpSelectBuf];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int pi = blockIdx.x * 8 + w;
+    if (pi >= sv.nq * sv.veff) return;  // warp-uniform
+    const int q = pi / sv.veff, r = pi % sv.veff;
+    const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
+    if (owned && !owned[c]) return;
+    const uint32_t s = ix.cl_start[c];
+    const uint32_t n = ix.cl_size[c];
+    const float *L = sv.lows + sv.vg_off[pi];
+    const float T0 = sv.T0[q];
+    const int S = sv.keep;
+    uint32_t cnt = 0;
+    uint64_t mn = kKeyMax;
+    for (uint32_t i = lane; i < n; i += 32) {
+        const float l = L[i];
+        if (l < T0) {
+            ++cnt;
+            const uint64_t key = make_key(l, s + i);
+            mn = key < mn ? key : mn;
+        }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
+    const uint32_t total = cnt;
+    uint64_t tau = kKeyMax;
+    if (total > static_cast<uint32_t>(S)) tau = __shfl_sync(0xffffffffu, warp_sort_lane_keys(mn, lane), S - 1);
+    uint64_t *b = buf[w];
+    uint32_t m = 0;
+    for (uint32_t base = 0; base < n; base += 32) {
+        const uint32_t i = base + lane;
+        uint64_t key = kKeyMax;
+        bool take = false;
+        if (i < n) {
+            const float l = L[i];
+            if (l < T0) {
+                key = make_key(l, s + i);
+                take = key <= tau;
+            }
+        }
+        const uint32_t mask = __ballot_sync(0xffffffffu, take);
+        const uint32_t pos = m + __popc(mask & ((1u << lane) - 1u));
+        if (take && pos < static_cast<uint32_t>(kWarpSelectBuf)) b[pos] = key;
+        m += __popc(mask);
+    }
+    if (m > static_cast<uint32_t>(sv.warp_select_limit)) {
+        if (lane == 0) fallback[1 + atomicAdd(fallback, 1u)] = static_cast<uint32_t>(pi);
+        return;
+    }
+    int sort_n = 32;
+    while (sort_n < static_cast<int>(m)) sort_n <<= 1;
+    for (int i = m + lane; i < sort_n; i += 32) b[i] = kKeyMax;
+    __syncwarp();
+    warp_sort_smem(b, sort_n, lane);
+    const int nkeep = min(static_cast<int>(total), S);
+    uint32_t slot0 = 0;
+    if (lane == 0) {
+        slot0 = nkeep ? atomicAdd(sv.cand_cnt + q, static_cast<uint32_t>(nkeep)) : 0u;
+        sv.bound[(size_t)q * sv.veff + r] = total <= static_cast<uint32_t>(S) ? kKeyMax : b[S - 1];
+    }
+    slot0 = __shfl_sync(0xffffffffu, slot0, 0);
+    for (int i = lane; i < nkeep; i += 32) {
+        const uint32_t slot = slot0 + i;
+        const uint32_t gid = static_cast<uint32_t>(b[i] & 0xFFFFFFFFu);
+        if (slot < static_cast<uint32_t>(sv.cap))
+            sv.cand_rec[(size_t)q * sv.cap + slot] = gid | (static_cast<uint64_t>(r) << 32);
+        else
+            atomicOr(sv.err, kDevCandidateOverflow);
     }
 }
 

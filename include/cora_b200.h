@@ -158,6 +158,12 @@ int cora_stage_reset(cora_engine *engine);
  * (every query probing the largest clusters); above the budget the vanguard clusters are
  * rescanned instead (same results). 0 forces rescanning. Set before prepare_workspace. */
 int cora_set_vanguard_lows_budget(cora_engine *engine, uint64_t bytes);
+/* Tuning knobs that never change results (the tests sweep them to cover every code path):
+ *  "vanguard_lows_budget"  same as cora_set_vanguard_lows_budget;
+ *  "warp_select_limit"     keys (0..256) one warp may collect while selecting the seeds of
+ *                          a vanguard pair before it hands the pair to a block-wide
+ *                          selection (0 sends every pair to the block selection). */
+int cora_set_tuning(cora_engine *engine, const char *key, int64_t value);
 /* 1 when the prepared workspace keeps vanguard lower bounds, 0 when it rescans, -1 on NULL. */
 int cora_get_vanguard_mode(const cora_engine *engine);
 /* Candidate capacity per query of the current workspace (array 7 above is nq x cap). */

@@ -188,33 +188,21 @@ void cora_oracle_decode_ex7(const uint8_t *code, uint64_t D, uint8_t *u) {
 }
 
 /* Refinement inner product of the full (1 + ex_bits)-bit code with the rotated query:
- * ipT = sum_i q'_i * (2^ex_bits * b_i + u_i), b the 1-bit code (bit 31-(i%32) of word i/32),
+ * ipT = sum_d q'_d * (2^ex_bits * b_d + u_d), b the 1-bit code (bit 31-(d%32) of word d/32),
  * u the decoded 7-bit ex code. The reference forms the same quantity as
  * 2^ex_bits * ip1 + ip2 (cpu_refinement.cpp:183-191) with ip1 taken from its fp16-LUT or
- * 8-bit-query scan; here it is one fp64 accumulation (all products exact): lane l of 32
- * accumulates dims 64b+l then 64b+32+l for ascending blocks b, then an xor butterfly
- * (offsets 16, 8, 4, 2, 1) combines the lanes, and the sum is rounded once to fp32. */
+ * 8-bit-query scan; here it is one fp64 accumulation in ascending dimension order (every
+ * product is exact in fp64), rounded once to fp32. */
 float cora_oracle_ip_total(const float *qr, const uint32_t *bits, const uint8_t *code,
                            uint64_t D) {
     uint8_t u[4096];
-    double part[32], next[32];
     cora_oracle_decode_ex7(code, D, u);
-    for (int l = 0; l < 32; ++l) {
-        double acc = 0.0;
-        for (uint64_t b = 0; b < D / 64; ++b) {
-            for (int h = 0; h < 2; ++h) {
-                const uint64_t d = 64 * b + 32 * h + l;
-                const uint32_t bit = (bits[d / 32] >> (31 - (d % 32))) & 1u;
-                acc += (double)qr[d] * (double)(128u * bit + u[d]);
-            }
-        }
-        part[l] = acc;
+    double acc = 0.0;
+    for (uint64_t d = 0; d < D; ++d) {
+        const uint32_t bit = (bits[d / 32] >> (31 - (d % 32))) & 1u;
+        acc += (double)qr[d] * (double)(128u * bit + u[d]);
     }
-    for (int off = 16; off >= 1; off >>= 1) {
-        for (int l = 0; l < 32; ++l) next[l] = part[l] + part[l ^ off];
-        memcpy(part, next, sizeof(part));
-    }
-    return (float)part[0];
+    return (float)acc;
 }
 
 /* cpu_refinement.cpp:189-191: ex = f_add_ex + g + f_rescale_ex * (ipT + kb), where

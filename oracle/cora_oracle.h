@@ -25,9 +25,8 @@
  *  - ip_int is exact integer arithmetic; ip1 = width * (float)ip_int;
  *  - low / ex follow the reference's expression trees in fp32, round-to-nearest, with no
  *    contraction (built with -ffp-contract=off);
- *  - the refinement inner product of the full 8-bit code, ipT = <q', 128 b + u>, is
- *    accumulated in fp64 by 32 "lanes" (lane l owns dims 64b+l and 64b+32+l of every
- *    64-dim block b, ascending b) and combined by an xor butterfly (16,8,4,2,1); the
+ *  - the refinement inner product of the full 8-bit code, ipT = <q', 128 b + u>, is one
+ *    fp64 accumulation in ascending dimension order (exact products), rounded once; the
  *    reference adds 128 * ip1 from its scan instead, which with the 8-bit query planes
  *    loses accuracy (ip1's quantisation error is multiplied by 128);
  *  - coarse probes are ordered by (g_add, cluster id); results by (ex, original id);

@@ -26,6 +26,10 @@ def _engine(cb, path=None, sd=None, nq=1, k=10, nprobe=1, vanguard=5, mode="lows
     e.set_vanguard_size(vanguard)
     if mode == "rescan":
         e.set_vanguard_lows_budget(0)
+    if mode == "blocksel":  # every vanguard pair through the block-wide seed selection
+        e.set_tuning("warp_select_limit", 0)
+    if mode == "tightsel":  # the warp selection hands most pairs over
+        e.set_tuning("warp_select_limit", 8)
     if path is not None:
         e.load_index_file(path)
     else:
@@ -53,7 +57,8 @@ def _check_stages(e, q, k, nprobe, ref, tag):
         f"{tag}: candidate counts"
 
 
-@pytest.mark.parametrize("loader,mode", [("file", "lows"), ("raw", "lows"), ("file", "rescan")])
+@pytest.mark.parametrize("loader,mode", [("file", "lows"), ("raw", "lows"), ("file", "rescan"),
+                                         ("file", "blocksel"), ("raw", "tightsel")])
 @pytest.mark.parametrize("name", GOLDEN_NAMES)
 def test_golden_parity(cb, golden, name, loader, mode):
     path, z = golden[name]
@@ -65,7 +70,7 @@ def test_golden_parity(cb, golden, name, loader, mode):
     else:
         e = _engine(cb, sd=po.search_data(po.read_ivf_file(path)), nq=len(q), k=kmax,
                     nprobe=npmax, mode=mode)
-    assert e.get_vanguard_mode() == (1 if mode == "lows" else 0)
+    assert e.get_vanguard_mode() == (0 if mode == "rescan" else 1)
     for k, nprobe, van in grid:
         k, nprobe, van = int(k), int(nprobe), int(van)
         tag = f"{name}/{loader} k{k}_np{nprobe}_v{van}"
@@ -97,6 +102,7 @@ def _synthetic(n, dim, nlist, nq, seed, sigma=0.25):
 @pytest.mark.parametrize("n,dim,nlist,nq,k,nprobe,van,mode", [
     (200_000, 96, 256, 256, 10, 16, 5, "lows"),
     (200_000, 96, 256, 256, 10, 16, 5, "rescan"),
+    (200_000, 96, 256, 256, 10, 16, 5, "tightsel"),
     (200_000, 96, 256, 64, 100, 24, 5, "lows"),
     (60_000, 768, 64, 48, 10, 8, 5, "lows"),
     (60_000, 768, 64, 48, 10, 8, 3, "rescan"),
