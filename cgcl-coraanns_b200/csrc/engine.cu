@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cfloat>
 #include <climits>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -96,7 +97,8 @@ struct Engine {
     bool loaded = false;
     uint64_t N = 0, dim = 0, D = 0, nlist = 0, ex_bits = 0, max_cluster = 0;
     int G16 = 0, W4 = 0, LC = 0;
-    DevBuf<float> centroids, rotator;
+    DevBuf<float> centroids, rotator, cnorm2;  // cnorm2: ||c'||^2 per centroid
+    float cmax = 0.0f;                          // max ||c'|| (rounded up)
     DevBuf<uint4> scan4;
     DevBuf<uint8_t> long_codes;
     DevBuf<float2> ex_factors;
@@ -117,7 +119,7 @@ struct Engine {
     // workspace
     bool ws_ready = false;
     uint64_t ws_q = 0, ws_k = 0, ws_np = 0, ws_vg = 0, cap = 0;
-    DevBuf<float> raw_q, qr, gmat, probe_g, T0, T1, Tcap, out_d;
+    DevBuf<float> raw_q, qr, qnorm2, gmat, probe_g, T0, T1, Tcap, out_d;
     DevBuf<QueryScalars> scal;
     DevBuf<uint32_t> planes, cand_cnt, seed_cnt, pair_cnt, pair_off, pair_cur, item_off, pairs,
         n_items, out_i;
@@ -195,6 +197,20 @@ struct Engine {
         centroids.alloc(nlist * D);
         rotator.alloc(dim * D);
         CUDA_TRY(cudaMemcpy(centroids.p, h_centroids, nlist * D * 4, cudaMemcpyHostToDevice));
+        {
+            std::vector<float> cn(nlist);
+            double mx = 0.0;
+            for (uint64_t c = 0; c < nlist; ++c) {
+                double s2 = 0.0;
+                for (uint64_t j = 0; j < D; ++j)
+                    s2 += (double)h_centroids[c * D + j] * (double)h_centroids[c * D + j];
+                cn[c] = static_cast<float>(s2);
+                mx = std::max(mx, std::sqrt(s2));
+            }
+            cmax = std::nextafter(static_cast<float>(mx), FLT_MAX);
+            cnorm2.alloc(nlist);
+            CUDA_TRY(cudaMemcpy(cnorm2.p, cn.data(), nlist * 4, cudaMemcpyHostToDevice));
+        }
         CUDA_TRY(cudaMemcpy(rotator.p, h_rotator, dim * D * 4, cudaMemcpyHostToDevice));
         cl_start.alloc(nlist);
         cl_size.alloc(nlist);
@@ -248,6 +264,7 @@ struct Engine {
         scal.alloc(max_q);
         planes.alloc(max_q * 8 * W4);
         gmat.alloc(max_q * nlist);
+        qnorm2.alloc(max_q);
         probe_ids.alloc(max_q * max_np);
         probe_g.alloc(max_q * max_np);
         T0.alloc(max_q);
@@ -291,7 +308,8 @@ struct Engine {
     void free_workspace() noexcept {
         ws_ready = false;
         ws_q = ws_k = ws_np = ws_vg = cap = 0;
-        for (auto *b : {&raw_q, &qr, &gmat, &probe_g, &T0, &T1, &Tcap, &out_d}) b->release();
+        for (auto *b : {&raw_q, &qr, &qnorm2, &gmat, &probe_g, &T0, &T1, &Tcap, &out_d})
+            b->release();
         scal.release();
         for (auto *b : {&planes, &cand_cnt, &seed_cnt, &pair_cnt, &pair_off, &pair_cur, &item_off,
                         &pairs, &n_items, &out_i})
@@ -567,23 +585,28 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
         const float c_b = -static_cast<float>((1u << (ex_bits + 1)) - 1u) / 2.0f;
         rotate_prep_kernel<<<static_cast<unsigned>((nq + kRotQueries - 1) / kRotQueries), 256, sm, st>>>(
             d_q, inq, static_cast<int>(dim), static_cast<int>(D), W4, rotator.p, c_b, qr.p, scal.p,
-            planes.p);
+            planes.p, qnorm2.p);
         CUDA_TRY(cudaGetLastError());
     }
     mark(1, st);
-    // 2. coarse distances + top-nprobe
+    // 2. coarse probing: approximate distances for every (query, centroid), then the exact
+    //    top-nprobe among the guarded candidates
     {
         dim3 grid(static_cast<unsigned>((nlist + kDistTile - 1) / kDistTile),
                   static_cast<unsigned>((nq + kDistTile - 1) / kDistTile));
-        centroid_dist_kernel<<<grid, 256, 0, st>>>(qr.p, inq, centroids.p, static_cast<int>(nlist),
-                                                   static_cast<int>(D), gmat.p);
+        approx_dist_f32_kernel<<<grid, 256, 0, st>>>(qr.p, qnorm2.p, inq, centroids.p, cnorm2.p,
+                                                     static_cast<int>(nlist), static_cast<int>(D),
+                                                     gmat.p);
         CUDA_TRY(cudaGetLastError());
         mark(2, st);
-        const size_t sm = (size_t)next_pow2(inp) * 8;
-        CUDA_TRY(cudaFuncSetAttribute(select_probes_kernel,
+        const int ccap = guarded_select_cap(inp);
+        const size_t sm = guarded_select_smem(inp, ccap, static_cast<int>(D));
+        CUDA_TRY(cudaFuncSetAttribute(guarded_select_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        select_probes_kernel<<<inq, 256, sm, st>>>(gmat.p, static_cast<int>(nlist), inp,
-                                                   probe_ids.p, probe_g.p);
+        guarded_select_kernel<<<inq, 256, sm, st>>>(gmat.p, static_cast<int>(nlist), inp, ccap, qr.p,
+                                                    qnorm2.p, centroids.p, cmax,
+                                                    static_cast<int>(D), kApproxEpsF32,
+                                                    probe_ids.p, probe_g.p);
         CUDA_TRY(cudaGetLastError());
     }
     mark(3, st);

@@ -25,7 +25,8 @@ struct QueryScalars {  // per query, 16 bytes
 __global__ void __launch_bounds__(256) rotate_prep_kernel(
     const float *__restrict__ raw_q, int nq, int dim, int D, int W4,
     const float *__restrict__ rotator, float c_b, float *__restrict__ qr_out,
-    QueryScalars *__restrict__ scal_out, uint32_t *__restrict__ planes_out) {
+    QueryScalars *__restrict__ scal_out, uint32_t *__restrict__ planes_out,
+    float *__restrict__ qnorm2_out) {
     extern __shared__ float smem_f[];
     float *sq = smem_f;                       // [kRotQueries][dim]
     float *sr = smem_f + kRotQueries * dim;   // [kRotQueries][D]
@@ -73,6 +74,11 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
     const float sf = (float)part;
     const float width = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
     const float inv = __fdiv_rn(1.0f, width);
+    // ||q'||^2 for the approximate coarse distances (any order: it only feeds the filter)
+    double nrm = 0.0;
+    for (int j = lane; j < D; j += 32) nrm = __fma_rn((double)x[j], (double)x[j], nrm);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) nrm += __shfl_xor_sync(0xffffffffu, nrm, off);
     if (lane == 0) {
         QueryScalars s;
         s.width = width;
@@ -80,6 +86,7 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
         s.kb = __fmul_rn(sf, c_b);
         s.sumq = sf;
         scal_out[q] = s;
+        qnorm2_out[q] = (float)nrm;
     }
     uint32_t *pl = planes_out + (size_t)q * 8 * W4;
     for (int w = 0; w < W4; ++w) {
@@ -98,21 +105,36 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
     }
 }
 
-// Exact coarse distances: g[q][c] = fp32( sum_j fma((q'_j - c_j), (q'_j - c_j)) ) in fp64,
-// ascending j. 64 x 64 output tile per CTA, 256 threads with 4 x 4 outputs each.
+// Exact coarse distance of the search contract: g(q, c) = fp32( sum_j fma(d_j, d_j) ) with
+// d_j = q'_j - c_j in fp64, ascending j (reference: hybrid.cu:465-477 forms the same
+// ||q'||^2 + ||c||^2 - 2 q'.c in fp32).
+__device__ __forceinline__ float exact_centroid_dist(const float *__restrict__ x,
+                                                     const float *__restrict__ c, int D) {
+    double acc = 0.0;
+    for (int j = 0; j < D; ++j) {
+        const double d = __dsub_rn((double)x[j], (double)__ldg(c + j));
+        acc = __fma_rn(d, d, acc);
+    }
+    return (float)acc;
+}
+
+// Approximate coarse distances on CUDA cores (fp32): approx(q, c) = ||q'||^2 + ||c||^2 -
+// 2 <q', c>, 64 x 64 output tile per CTA, 256 threads with 4 x 4 outputs each. Its error
+// bound is kApproxEpsF32 (see guarded_select_kernel).
 constexpr int kDistTile = 64, kDistK = 32;
-__global__ void __launch_bounds__(256) centroid_dist_kernel(
-    const float *__restrict__ qr, int nq, const float *__restrict__ cent, int nlist, int D,
-    float *__restrict__ g_out) {
+__global__ void __launch_bounds__(256) approx_dist_f32_kernel(
+    const float *__restrict__ qr, const float *__restrict__ qnorm2, int nq,
+    const float *__restrict__ cent, const float *__restrict__ cnorm2, int nlist, int D,
+    float *__restrict__ out) {
     __shared__ float sq[kDistK][kDistTile + 1];
     __shared__ float sc[kDistK][kDistTile + 1];
     const int qbase = blockIdx.y * kDistTile, cbase = blockIdx.x * kDistTile;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    double acc[4][4];
+    float acc[4][4];
 #pragma unroll
     for (int a = 0; a < 4; ++a)
 #pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = 0.0;
+        for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
     for (int k0 = 0; k0 < D; k0 += kDistK) {
         for (int i = threadIdx.x; i < kDistK * kDistTile; i += blockDim.x) {
             const int row = i / kDistK, kk = i % kDistK;
@@ -121,20 +143,17 @@ __global__ void __launch_bounds__(256) centroid_dist_kernel(
             sc[kk][row] = ci < nlist ? cent[(size_t)ci * D + k0 + kk] : 0.0f;
         }
         __syncthreads();
-#pragma unroll 4
+#pragma unroll 8
         for (int kk = 0; kk < kDistK; ++kk) {
-            double qv[4], cv[4];
+            float qv[4], cv[4];
 #pragma unroll
-            for (int a = 0; a < 4; ++a) qv[a] = (double)sq[kk][ty * 4 + a];
+            for (int a = 0; a < 4; ++a) qv[a] = sq[kk][ty * 4 + a];
 #pragma unroll
-            for (int b = 0; b < 4; ++b) cv[b] = (double)sc[kk][tx * 4 + b];
+            for (int b = 0; b < 4; ++b) cv[b] = sc[kk][tx * 4 + b];
 #pragma unroll
             for (int a = 0; a < 4; ++a)
 #pragma unroll
-                for (int b = 0; b < 4; ++b) {
-                    const double d = __dsub_rn(qv[a], cv[b]);
-                    acc[a][b] = __fma_rn(d, d, acc[a][b]);
-                }
+                for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(qv[a], cv[b], acc[a][b]);
         }
         __syncthreads();
     }
@@ -145,28 +164,80 @@ __global__ void __launch_bounds__(256) centroid_dist_kernel(
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
             const int ci = cbase + tx * 4 + b;
-            if (ci < nlist) g_out[(size_t)qi * nlist + ci] = (float)acc[a][b];
+            if (ci < nlist)
+                out[(size_t)qi * nlist + ci] = (qnorm2[qi] + cnorm2[ci]) - 2.0f * acc[a][b];
         }
     }
 }
 
-// One CTA per query: the nprobe smallest (g, c) keys, ascending, by block radix selection
-// over the query's row of distances. Dynamic shared memory: next_pow2(nprobe) keys.
-__global__ void __launch_bounds__(256) select_probes_kernel(const float *__restrict__ g,
-                                                            int nlist, int nprobe,
-                                                            int *__restrict__ probe_ids,
-                                                            float *__restrict__ probe_g) {
-    extern __shared__ uint64_t smem_k[];
+// Error bounds |approx - g| <= eps * (||q'|| + max ||c||)^2 of the approximate distance
+// kernels, with slack. fp32 (u = 2^-24, D <= 1024 accumulation terms): the dot product is
+// within gamma_D * ||q'|| ||c||, the norms within gamma_D of theirs, the two final additions
+// and g's own rounding add a few u; 2 * (2 gamma_1032 + 9 u) < 2^-11.
+constexpr double kApproxEpsF32 = 1.0 / 2048.0;
+
+// One CTA per query: the nprobe probes of the contract (smallest exact g, ties by cluster
+// id) from approximate distances. tau = nprobe-th smallest approx; every exact top-nprobe
+// centroid has approx <= tau + 2E (E the approx error bound), so only those candidates are
+// recomputed exactly (fp64) and selected. More candidates than the shared buffer holds (a
+// pathological tie band) fall back to exact distances for every centroid of the query,
+// written over its approximate row. Dynamic shared memory: see guarded_select_smem().
+__global__ void __launch_bounds__(256) guarded_select_kernel(
+    float *__restrict__ approx, int nlist, int nprobe, int cand_cap, const float *__restrict__ qr,
+    const float *__restrict__ qnorm2, const float *__restrict__ cent, float cmax, int D,
+    double eps, int *__restrict__ probe_ids, float *__restrict__ probe_g) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int S2 = next_pow2(nprobe);
+    uint64_t *sel = reinterpret_cast<uint64_t *>(smem_raw);          // S2
+    uint64_t *ckeys = sel + S2;                                       // cand_cap
+    uint32_t *cidx = reinterpret_cast<uint32_t *>(ckeys + cand_cap);  // cand_cap
+    float *x = reinterpret_cast<float *>(cidx + cand_cap);            // D
     __shared__ int scratch[256 + 3];
+    __shared__ int s_ncand;
     const int q = blockIdx.x;
-    const float *row = g + (size_t)q * nlist;
-    auto key_at = [&](uint32_t c) -> uint64_t { return make_key(row[c], c); };
-    block_select_smallest(key_at, static_cast<uint32_t>(nlist), nprobe, smem_k, scratch);
-    for (int r = threadIdx.x; r < nprobe; r += blockDim.x) {
-        const uint64_t key = smem_k[r];
-        probe_ids[(size_t)q * nprobe + r] = static_cast<int>(key & 0xFFFFFFFFu);
-        probe_g[(size_t)q * nprobe + r] = unord_f32(static_cast<uint32_t>(key >> 32));
+    float *row = approx + (size_t)q * nlist;
+    for (int j = threadIdx.x; j < D; j += blockDim.x) x[j] = qr[(size_t)q * D + j];
+    if (threadIdx.x == 0) s_ncand = 0;
+    auto approx_key = [&](uint32_t c) -> uint64_t { return make_key(row[c], c); };
+    block_select_smallest(approx_key, static_cast<uint32_t>(nlist), nprobe, sel, scratch);
+    const double tau = (double)unord_f32(static_cast<uint32_t>(sel[nprobe - 1] >> 32));
+    const double r = sqrt((double)qnorm2[q]) + (double)cmax;
+    const double bound = tau + 2.0 * (eps * r * r + 1e-30);
+    for (int c = threadIdx.x; c < nlist; c += blockDim.x) {
+        if ((double)row[c] <= bound) {
+            const int pos = atomicAdd(&s_ncand, 1);
+            if (pos < cand_cap) cidx[pos] = static_cast<uint32_t>(c);
+        }
     }
+    __syncthreads();
+    const int ncand = s_ncand;
+    if (ncand <= cand_cap) {
+        for (int i = threadIdx.x; i < ncand; i += blockDim.x) {
+            const uint32_t c = cidx[i];
+            ckeys[i] = make_key(exact_centroid_dist(x, cent + (size_t)c * D, D), c);
+        }
+        __syncthreads();
+        auto exact_key = [&](uint32_t i) -> uint64_t { return ckeys[i]; };
+        block_select_smallest(exact_key, static_cast<uint32_t>(ncand), nprobe, sel, scratch);
+    } else {
+        for (int c = threadIdx.x; c < nlist; c += blockDim.x)
+            row[c] = exact_centroid_dist(x, cent + (size_t)c * D, D);
+        __syncthreads();
+        block_select_smallest(approx_key, static_cast<uint32_t>(nlist), nprobe, sel, scratch);
+    }
+    for (int rr = threadIdx.x; rr < nprobe; rr += blockDim.x) {
+        const uint64_t key = sel[rr];
+        probe_ids[(size_t)q * nprobe + rr] = static_cast<int>(key & 0xFFFFFFFFu);
+        probe_g[(size_t)q * nprobe + rr] = unord_f32(static_cast<uint32_t>(key >> 32));
+    }
+}
+
+__host__ __device__ inline size_t guarded_select_smem(int nprobe, int cand_cap, int D) {
+    return (size_t)next_pow2(nprobe) * 8 + (size_t)cand_cap * 12 + (size_t)D * 4;
+}
+__host__ __device__ inline int guarded_select_cap(int nprobe) {
+    const int c = 2 * nprobe > 1024 ? 2 * nprobe : 1024;
+    return c < 8192 ? c : 8192;
 }
 
 }  // namespace cora

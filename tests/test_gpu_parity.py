@@ -124,6 +124,27 @@ def test_live_oracle_parity_larger(cb, n, dim, nlist, nq, k, nprobe, van, mode):
     e.close()
 
 
+def test_probe_ties_take_the_exact_fallback(cb):
+    """Every centroid equidistant from every query: the guarded selection's candidate band
+    holds all 2048 centroids (more than its buffer), so the exact path over every centroid
+    runs; probes must still be the smallest cluster ids, bit for bit as the oracle."""
+    from coraanns_b200 import builder
+    rng = np.random.default_rng(11)
+    nlist, dim, n, nq = 2048, 64, 16384, 16
+    centres = np.repeat(rng.normal(size=(1, dim)).astype(np.float32), nlist, 0)
+    lab = np.arange(n) % nlist
+    data = (centres[lab] + 0.3 * rng.normal(size=(n, dim))).astype(np.float32)
+    q = (centres[:nq] + 0.3 * rng.normal(size=(nq, dim))).astype(np.float32)
+    sd = builder.build_index(data, centres, lab, seed=3)
+    ref = po.OracleIndex(sd).search(q, 10, 16, vanguard=5, with_details=True)
+    e = _engine(cb, sd=sd, nq=nq, k=10, nprobe=16)
+    e.reset_buffer(q)
+    d, i = e.search(q, 10, 16)
+    _check_stages(e, q, 10, 16, ref, "ties")
+    assert np.array_equal(i, ref["ids"]) and d.tobytes() == ref["dist"].tobytes()
+    e.close()
+
+
 def test_candidate_sets_identical(cb, golden):
     """L3: with fixed thresholds the candidate set {v : low(v) < T} is identical."""
     path, z = golden["demo"]
