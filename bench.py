@@ -47,6 +47,9 @@ CONFIGS = {
                  nprobes=[4, 8, 16], seed=20261201),
     "small": dict(n=1_000_000, dim=96, nlist=1024, nq=10_000, sigma=0.25, qnoise=0.05, k=10,
                   nprobes=[8, 16, 32, 64], seed=20261205),
+    # profiling case: codes (5M x 32 B) larger than L2, a few GB on the device in total
+    "medium": dict(n=5_000_000, dim=96, nlist=2048, nq=10_000, sigma=0.25, qnoise=0.05, k=10,
+                   nprobes=[8], seed=20261206),
 }
 TARGET_RECALL = 0.95
 
