@@ -215,26 +215,87 @@ __device__ __forceinline__ void issue_tile(uint4 *stage_buf, uint64_t *bar, cons
                  bar);
 }
 
+// ---- exact 1-bit x 8-bit inner product ---------------------------------------------
+// With offset-binary query planes p'_j (bit j of qint + 128, i.e. the two's-complement
+// planes with plane 7 inverted), sum_i b_i qint_i = sum_j 2^j popc(x & p'_j) - 128 popc(x),
+// an integer identity, so the result equals the reference's
+// sum_{j<7} popc(x & p_j) << j - popc(x & p_7) << 7 (filter_kernels.cuh:79-104) bit for
+// bit. The weighted popcount sum of one 128-bit group (8 planes x 4 words) is formed by a
+// carry-save adder tree: words of equal weight are combined three at a time into a sum
+// word and a carry word of twice the weight, leaving one word per weight 2^0..2^9, so 10
+// POPC replace 32 (POPC issues at a quarter of the logic-op rate on this SM).
+__device__ __forceinline__ void full_add(uint32_t &s, uint32_t &c, uint32_t a, uint32_t b,
+                                         uint32_t d) {
+    s = a ^ b ^ d;
+    c = (a & b) | (d & (a ^ b));
+}
+__device__ __forceinline__ void half_add(uint32_t &s, uint32_t &c, uint32_t a, uint32_t b) {
+    s = a ^ b;
+    c = a & b;
+}
+
+// sum_j 2^j sum_t popc(x_t & p'_{j,t}) for one group; P points at the group's plane words
+// (plane j at P + j * W4, 4 consecutive words).
+template <int W4>
+__device__ __forceinline__ int group_weighted_popc(uint4 x, const uint32_t *__restrict__ P) {
+    uint32_t a[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint4 p = *reinterpret_cast<const uint4 *>(P + j * W4);
+        a[j][0] = x.x & p.x;
+        a[j][1] = x.y & p.y;
+        a[j][2] = x.z & p.z;
+        a[j][3] = x.w & p.w;
+    }
+    uint32_t s, t, cA, cB, cC, nA, nB, nC;
+    int total;
+    // weight 2^0: 4 words
+    full_add(s, cA, a[0][0], a[0][1], a[0][2]);
+    half_add(s, cB, s, a[0][3]);
+    total = __popc(s);
+    // weight 2^1: 4 words + 2 carries
+    full_add(s, nA, a[1][0], a[1][1], a[1][2]);
+    full_add(t, nB, a[1][3], cA, cB);
+    half_add(s, nC, s, t);
+    total += __popc(s) << 1;
+    cA = nA;
+    cB = nB;
+    cC = nC;
+    // weights 2^2 .. 2^7: 4 words + 3 carries each
+#pragma unroll
+    for (int j = 2; j < 8; ++j) {
+        full_add(s, nA, a[j][0], a[j][1], a[j][2]);
+        full_add(t, nB, a[j][3], cA, cB);
+        full_add(s, nC, s, t, cC);
+        total += __popc(s) << j;
+        cA = nA;
+        cB = nB;
+        cC = nC;
+    }
+    // weights 2^8, 2^9: the remaining carries
+    full_add(s, nA, cA, cB, cC);
+    total += __popc(s) << 8;
+    total += __popc(nA) << 9;
+    return total;
+}
+
 template <int G16>
 __device__ __forceinline__ int ip_int_from_planes(const uint4 (&code)[G16],
                                                   const uint32_t *__restrict__ P) {
     constexpr int W4 = ScanShape<G16>::W4;
-    int acc[8];
-#pragma unroll
-    for (int p = 0; p < 8; ++p) acc[p] = 0;
+    int t = 0, px = 0;
 #pragma unroll
     for (int g = 0; g < G16; ++g) {
-#pragma unroll
-        for (int p = 0; p < 8; ++p) {
-            const uint4 qw = *reinterpret_cast<const uint4 *>(P + p * W4 + 4 * g);
-            acc[p] += __popc(code[g].x & qw.x) + __popc(code[g].y & qw.y) +
-                      __popc(code[g].z & qw.z) + __popc(code[g].w & qw.w);
-        }
+        t += group_weighted_popc<W4>(code[g], P + 4 * g);
+        px += __popc(code[g].x) + __popc(code[g].y) + __popc(code[g].z) + __popc(code[g].w);
     }
-    int ip = -(acc[7] << 7);
-#pragma unroll
-    for (int p = 0; p < 7; ++p) ip += acc[p] << p;
-    return ip;
+    return t - (px << 7);
+}
+
+// Copies a query's two's-complement bit-planes into shared memory as offset-binary planes
+// (plane 7 inverted), the form ip_int_from_planes consumes.
+__device__ __forceinline__ uint32_t offset_binary_word(uint32_t w, int word_index, int W4) {
+    return word_index >= 7 * W4 ? ~w : w;
 }
 
 __device__ __forceinline__ float lower_bound_dist(float4 f, float ip1, float g, float k1,
@@ -351,7 +412,8 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
         __syncthreads();
         for (int i = threadIdx.x; i < pc * 8 * W4; i += blockDim.x) {
             const int j = i / (8 * W4);
-            s_planes[i] = sv.planes[(size_t)s_q[j] * 8 * W4 + (i - j * 8 * W4)];
+            s_planes[i] = offset_binary_word(sv.planes[(size_t)s_q[j] * 8 * W4 + (i - j * 8 * W4)],
+                                             i - j * 8 * W4, W4);
         }
         __syncthreads();
         for (int t = 0; t < ntiles; ++t) {
@@ -458,6 +520,8 @@ __device__ void select_pair_block(const IndexView &ix, const SearchView &sv,
     write_seeds(sv, q, r, s_total, s_keys, s_base_p);
 }
 
+constexpr int kLowsUnroll = 4;  // lows loaded per lane before they are processed
+
 // One warp per vanguard pair (8 per CTA): candidates low < T1 that are not seeds
 // (key > boundary), read from the pair's stored lows.
 __global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, SearchView sv,
@@ -473,14 +537,19 @@ __global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, Sear
     const float *L = sv.lows + sv.vg_off[pi];
     const float T1 = sv.T1[q];
     const uint64_t bnd = sv.bound[(size_t)q * sv.veff + r];
-    for (uint32_t base = 0; base < n; base += 32) {
-        const uint32_t i = base + lane;
-        bool cand = false;
-        if (i < n) {
-            const float l = L[i];
-            cand = (l < T1) && (make_key(l, s + i) > bnd);
+    for (uint32_t base = 0; base < n; base += 32 * kLowsUnroll) {
+        float l[kLowsUnroll];
+#pragma unroll
+        for (int t = 0; t < kLowsUnroll; ++t) {  // all loads first: one round trip per batch
+            const uint32_t i = base + 32 * t + lane;
+            l[t] = i < n ? __ldg(L + i) : T1;
         }
-        emit_candidate(sv, cand, q, (s + i) | (static_cast<uint64_t>(r) << 32), lane);
+#pragma unroll
+        for (int t = 0; t < kLowsUnroll; ++t) {
+            const uint32_t i = base + 32 * t + lane;
+            const bool cand = (l[t] < T1) && (make_key(l[t], s + i) > bnd);
+            emit_candidate(sv, cand, q, (s + i) | (static_cast<uint64_t>(r) << 32), lane);
+        }
     }
 }
 
@@ -540,8 +609,9 @@ __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
     const int S = sv.keep;
     uint32_t cnt = 0;
     uint64_t mn = kKeyMax;
+#pragma unroll 4
     for (uint32_t i = lane; i < n; i += 32) {
-        const float l = L[i];
+        const float l = __ldg(L + i);
         if (l < T0) {
             ++cnt;
             const uint64_t key = make_key(l, s + i);
@@ -555,21 +625,23 @@ __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
     if (total > static_cast<uint32_t>(S)) tau = __shfl_sync(0xffffffffu, warp_sort_lane_keys(mn, lane), S - 1);
     uint64_t *b = buf[w];
     uint32_t m = 0;
-    for (uint32_t base = 0; base < n; base += 32) {
-        const uint32_t i = base + lane;
-        uint64_t key = kKeyMax;
-        bool take = false;
-        if (i < n) {
-            const float l = L[i];
-            if (l < T0) {
-                key = make_key(l, s + i);
-                take = key <= tau;
-            }
+    for (uint32_t base = 0; base < n; base += 32 * kLowsUnroll) {
+        float l[kLowsUnroll];
+#pragma unroll
+        for (int t = 0; t < kLowsUnroll; ++t) {
+            const uint32_t i = base + 32 * t + lane;
+            l[t] = i < n ? __ldg(L + i) : T0;
         }
-        const uint32_t mask = __ballot_sync(0xffffffffu, take);
-        const uint32_t pos = m + __popc(mask & ((1u << lane) - 1u));
-        if (take && pos < static_cast<uint32_t>(kWarpSelectBuf)) b[pos] = key;
-        m += __popc(mask);
+#pragma unroll
+        for (int t = 0; t < kLowsUnroll; ++t) {
+            const uint32_t i = base + 32 * t + lane;
+            const uint64_t key = make_key(l[t], s + i);
+            const bool take = (l[t] < T0) && key <= tau;
+            const uint32_t mask = __ballot_sync(0xffffffffu, take);
+            const uint32_t pos = m + __popc(mask & ((1u << lane) - 1u));
+            if (take && pos < static_cast<uint32_t>(kWarpSelectBuf)) b[pos] = key;
+            m += __popc(mask);
+        }
     }
     if (m > static_cast<uint32_t>(sv.warp_select_limit)) {
         if (lane == 0) fallback[1 + atomicAdd(fallback, 1u)] = static_cast<uint32_t>(pi);
@@ -625,7 +697,7 @@ __global__ void __launch_bounds__(kScanThreads) vanguard_rescan_kernel(
     const size_t cbase = (size_t)(G16 + 1) * s;
 
     for (int i = threadIdx.x; i < 8 * W4; i += blockDim.x)
-        s_planes[i] = sv.planes[(size_t)q * 8 * W4 + i];
+        s_planes[i] = offset_binary_word(sv.planes[(size_t)q * 8 * W4 + i], i, W4);
     if (threadIdx.x == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
