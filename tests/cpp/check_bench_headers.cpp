@@ -1,0 +1,136 @@
+// Unit checks of the CLI's option parser, vector-file readers and recall evaluator
+// (host code only; no GPU). Built and run by tests/test_cli.py. Exits non-zero on failure.
+#include <cstdio>
+#include <fstream>
+#include <functional>
+#include <string>
+#include <vector>
+
+#include "coraanns/benchmark/options.hpp"
+#include "coraanns/benchmark/recall.hpp"
+#include "coraanns/benchmark/vectors.hpp"
+
+using namespace coraanns::bench;
+
+static int failures = 0;
+#define CHECK(c)                                                      \
+    do {                                                              \
+        if (!(c)) {                                                   \
+            std::fprintf(stderr, "FAIL %s:%d %s\n", __FILE__, __LINE__, #c); \
+            ++failures;                                               \
+        }                                                             \
+    } while (0)
+
+static bool throws(const std::function<void()> &f) {
+    try {
+        f();
+    } catch (const std::exception &) {
+        return true;
+    }
+    return false;
+}
+
+static CliOptions parse(std::vector<std::string> args) {
+    std::vector<char *> argv;
+    for (auto &a : args) argv.push_back(a.data());
+    argv.push_back(nullptr);
+    return CliOptions(static_cast<int>(args.size()), argv.data(), 0);
+}
+
+int main(int argc, char **argv) {
+    const std::string dir = argc > 1 ? argv[1] : ".";
+    // options
+    auto o = parse({"--topk", "10", "--nprobes=4,8", "--profile", "on"});
+    CHECK(o.get_size("topk", 0) == 10);
+    CHECK(o.get("nprobes", "") == "4,8");
+    CHECK(o.get_bool("profile", false));
+    CHECK(!o.get_bool("absent", false));
+    CHECK(!throws([&] { o.require_known({"topk", "nprobes", "profile"}); }));
+    CHECK(throws([&] { o.require_known({"topk", "nprobes"}); }));
+    CHECK(throws([] { parse({"--topk", "1", "--topk", "2"}); }));
+    CHECK(throws([] { parse({"--topk"}); }));
+    CHECK(throws([] { parse({"--topk", "--rounds", "2"}); }));
+    CHECK(throws([] { parse({"positional"}); }));
+    CHECK(throws([] { parse({"--topk", "-1"}).get_size("topk", 0); }));
+    CHECK(throws([] { parse({"--topk", "12x"}).get_size("topk", 0); }));
+    CHECK(throws([] { parse({"--profile", "maybe"}).get_bool("profile", false); }));
+    CHECK(parse_nprobes("4,8", 16) == (std::vector<std::size_t>{4, 8}));
+    CHECK(parse_nprobes("", 16) == (std::vector<std::size_t>{16}));
+    CHECK(parse_nprobes("", 100) == (std::vector<std::size_t>{40, 50, 60, 75, 95}));
+    CHECK(throws([] { parse_nprobes("0", 16); }));
+    CHECK(throws([] { parse_nprobes("17", 16); }));
+    CHECK(throws([] { parse_nprobes("4,4", 16); }));
+    CHECK(throws([] { parse_nprobes("4,,8", 16); }));
+    CHECK(throws([] { parse_nprobes("+4", 16); }));
+    CHECK(join_values({4, 8, 16}) == "4,8,16");
+    CHECK(throws([] { validate_benchmark_shape(10, 8, 9, 10, 8, 10, 1); }));
+    CHECK(throws([] { validate_benchmark_shape(10, 8, 10, 5, 8, 10, 1); }));
+    CHECK(throws([] { validate_benchmark_shape(10, 8, 10, 10, 9, 10, 1); }));
+    CHECK(!throws([] { validate_benchmark_shape(10, 8, 10, 10, 8, 10, 1); }));
+    {
+        std::vector<std::string> a = {"prog", "i", "--recall-base=base.fbin", "q", "g", "--topk", "3"};
+        std::vector<char *> v;
+        for (auto &s : a) v.push_back(s.data());
+        v.push_back(nullptr);
+        int n = static_cast<int>(a.size());
+        CHECK(take_recall_base(n, v.data()) == "base.fbin");
+        CHECK(n == 6 && std::string(v[3]) == "g" && v[6] == nullptr);
+    }
+
+    // vector files: 3 rows x 2 dims, .fvecs and .fbin
+    const float rows[3][2] = {{0.f, 0.f}, {1.f, 0.f}, {0.f, 3.f}};
+    {
+        std::ofstream f(dir + "/b.fvecs", std::ios::binary);
+        for (auto &r : rows) {
+            const uint32_t d = 2;
+            f.write(reinterpret_cast<const char *>(&d), 4);
+            f.write(reinterpret_cast<const char *>(r), 8);
+        }
+        std::ofstream g(dir + "/b.fbin", std::ios::binary);
+        const uint32_t hdr[2] = {3, 2};
+        g.write(reinterpret_cast<const char *>(hdr), 8);
+        g.write(reinterpret_cast<const char *>(rows), sizeof(rows));
+        std::ofstream t(dir + "/trunc.fbin", std::ios::binary);
+        t.write(reinterpret_cast<const char *>(hdr), 8);
+        t.write(reinterpret_cast<const char *>(rows), 12);
+    }
+    for (const char *name : {"/b.fvecs", "/b.fbin"}) {
+        auto m = load_vectors<float>(dir + name);
+        CHECK(m.rows == 3 && m.cols == 2 && m(2, 1) == 3.f && m(1, 0) == 1.f);
+        MappedVectors mv(dir + name);
+        CHECK(mv.rows() == 3 && mv.dim() == 2 && mv.row(2)[1] == 3.f);
+    }
+    CHECK(throws([&] { load_vectors<float>(dir + "/trunc.fbin"); }));
+    CHECK(throws([&] { MappedVectors m(dir + "/trunc.fbin"); }));
+    CHECK(throws([&] { load_vectors<float>(dir + "/missing.fbin"); }));
+
+    // recall: one query at the origin, GT top-2 = {0, 1}; id 2 is farther than rank 2
+    const float q[2] = {0.f, 0.f};
+    Matrix<uint32_t> gt;
+    gt.rows = 1;
+    gt.cols = 2;
+    gt.data = {0, 1};
+    RecallEvaluator ids_only(q, 1, 2, gt, 2, "");
+    CHECK(ids_only.evaluate({1, 0}) == 1.0);
+    CHECK(ids_only.evaluate({1, 1}) == 0.5);       // a repeated id counts once
+    CHECK(ids_only.evaluate({2, UINT32_MAX}) == 0.0);
+    // distance-aware: a row equal in distance to the GT radius counts as a hit
+    {
+        std::ofstream g(dir + "/d.fbin", std::ios::binary);
+        const uint32_t hdr[2] = {4, 2};
+        const float r4[4][2] = {{0.f, 0.f}, {1.f, 0.f}, {0.f, 3.f}, {0.f, -1.f}};
+        g.write(reinterpret_cast<const char *>(hdr), 8);
+        g.write(reinterpret_cast<const char *>(r4), sizeof(r4));
+    }
+    RecallEvaluator dist(q, 1, 2, gt, 2, dir + "/d.fbin");
+    CHECK(dist.evaluate({0, 3}) == 1.0);   // id 3 is at distance 1 == radius
+    CHECK(dist.evaluate({0, 2}) == 0.5);   // id 2 is at distance 9 > radius
+    CHECK(dist.evaluate({0, 7}) == 0.5);   // out of range id is a miss
+    Matrix<uint32_t> dup;
+    dup.rows = 1;
+    dup.cols = 2;
+    dup.data = {1, 1};
+    CHECK(throws([&] { RecallEvaluator e(q, 1, 2, dup, 2, ""); }));
+    if (failures == 0) std::printf("bench headers: all checks passed\n");
+    return failures == 0 ? 0 : 1;
+}
