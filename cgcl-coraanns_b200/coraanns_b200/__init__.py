@@ -40,7 +40,7 @@ EXPORTS = [
     "cora_get_last_refined_count", "cora_get_last_spilled_count", "cora_get_last_gpu_filter_ms",
     "cora_debug_copy", "cora_get_last_stage_ms", "cora_stage_totals", "cora_stage_reset",
     "cora_set_vanguard_lows_budget", "cora_set_tuning", "cora_get_vanguard_mode",
-    "cora_get_candidate_capacity",
+    "cora_get_candidate_capacity", "cora_probe_noalloc", "cora_probe_noalloc_scratch_limit",
 ]
 
 _p = C.c_void_p
@@ -89,6 +89,8 @@ _sig("cora_stage_reset", C.c_int, _p)
 _sig("cora_set_vanguard_lows_budget", C.c_int, _p, _u64)
 _sig("cora_get_vanguard_mode", C.c_int, _p)
 _sig("cora_set_tuning", C.c_int, _p, C.c_char_p, C.c_int64)
+_sig("cora_probe_noalloc", C.c_int, _p, _p, _u64, _u64, _p, _p, _p)
+_sig("cora_probe_noalloc_scratch_limit", _u64)
 
 STAGES = ("rotate_prep", "centroid_dist", "select_probes", "vanguard_grouping",
           "vanguard_scan", "vanguard_select", "seed_refine", "threshold", "main_grouping",
@@ -122,6 +124,11 @@ def _check(rc):
 
 def _ptr(a):
     return None if a is None else C.c_void_p(a.ctypes.data)
+
+
+def probe_noalloc_scratch_limit() -> int:
+    """Bytes of the static per-device scratch block behind HybridIndex.probe_noalloc."""
+    return int(_lib.cora_probe_noalloc_scratch_limit())
 
 
 class KernelType:
@@ -206,6 +213,15 @@ class HybridIndex:
         """Enqueue a search on device pointers (e.g. torch tensors' data_ptr())."""
         _check(_lib.cora_search_device(self._h, C.c_void_p(d_queries), num_queries, topk, nprobe,
                                        C.c_void_p(d_dists), C.c_void_p(d_ids),
+                                       C.c_void_p(stream) if stream else None))
+
+    def probe_noalloc(self, d_queries: int, num_queries, nprobe, d_probe_ids: int,
+                      d_probe_dists: int, stream: int = 0):
+        """Coarse probing into caller-provided device buffers; allocates nothing (static
+        per-device scratch, limit probe_noalloc_scratch_limit()). Calls that overlap in
+        time race on the scratch; the first call on a device must precede stream capture."""
+        _check(_lib.cora_probe_noalloc(self._h, C.c_void_p(d_queries), num_queries, nprobe,
+                                       C.c_void_p(d_probe_ids), C.c_void_p(d_probe_dists),
                                        C.c_void_p(stream) if stream else None))
 
     def check_device(self):

@@ -12,6 +12,7 @@
 #include <cstring>
 #include <fstream>
 #include <memory>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -1120,6 +1121,136 @@ int cora_get_vanguard_mode(const cora_engine *engine) {
 
 uint64_t cora_get_candidate_capacity(const cora_engine *engine) {
     return engine && engine->e ? engine->e->cap : 0;
+}
+
+}  // extern "C"
+
+// ======================================================================================
+// Coarse probing without allocation (cora_probe_noalloc)
+//
+// Some callers cannot allocate device memory at the point where they need the probe list:
+// a router that decides which GPU or shard owns a query's clusters before the search is
+// dispatched, running next to searches it must not stall (cudaMalloc/cudaFree synchronise
+// the device), or a process that cannot afford the multi-GB search workspace that
+// prepare_workspace reserves. For them this entry point runs the same rotation, approximate
+// distance and guarded top-nprobe kernels as a search, but keeps every intermediate in one
+// fixed block of device memory that is part of the loaded module, so the call itself never
+// allocates: no cudaMalloc/cudaFree, no library routine that allocates, no host buffer on
+// the success path (a rejected call only builds its error message).
+//
+// Limits and rules:
+//  * the scratch block is kNoallocScratchBytes (16 MiB) per device; a call needing more
+//    (num_queries * per-query bytes, see noalloc_scratch_bytes) is rejected with
+//    CORA_EINVAL and a message giving both sizes;
+//  * nothing in the block has to start at zero: every kernel writes each scratch element
+//    before any kernel reads it;
+//  * the first call on a device, with that device current, looks the block's address up
+//    (cudaGetSymbolAddress) and caches it; make that first call before any stream capture;
+//  * there is ONE block per device, shared by every engine on that device: calls that
+//    overlap in time (two streams, two host threads) race on it and corrupt each other's
+//    results. Serialise them, e.g. issue them all on one stream.
+// ======================================================================================
+namespace cora {
+namespace {
+
+constexpr size_t kNoallocScratchBytes = size_t{16} << 20;
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
+
+constexpr int kNoallocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+unsigned char *g_noalloc_ptr[kNoallocMaxDevices] = {};
+
+inline size_t align256(size_t b) { return (b + 255) & ~size_t{255}; }
+
+struct NoallocLayout {
+    size_t qr, qnorm2, scal, planes, approx, total;
+};
+
+NoallocLayout noalloc_layout(uint64_t nq, uint64_t D, uint64_t W4, uint64_t nlist) {
+    NoallocLayout l{};
+    l.qr = 0;
+    l.qnorm2 = l.qr + align256(nq * D * sizeof(float));
+    l.scal = l.qnorm2 + align256(nq * sizeof(float));
+    l.planes = l.scal + align256(nq * sizeof(QueryScalars));
+    l.approx = l.planes + align256(nq * 8 * W4 * sizeof(uint32_t));
+    l.total = l.approx + align256(nq * nlist * sizeof(float));
+    return l;
+}
+
+// Address of this device's scratch block; the device must be current.
+unsigned char *noalloc_scratch(int device) {
+    if (device < 0 || device >= kNoallocMaxDevices) fail(CORA_EINVAL, "device ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_ptr[device]) {
+        void *p = nullptr;
+        const cudaError_t rc = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (rc != cudaSuccess || !p)
+            fail(CORA_ERUNTIME, std::string("cudaGetSymbolAddress for the probe scratch failed: ") +
+                                    cudaGetErrorString(rc));
+        g_noalloc_ptr[device] = static_cast<unsigned char *>(p);
+    }
+    return g_noalloc_ptr[device];
+}
+
+}  // namespace
+}  // namespace cora
+
+extern "C" {
+
+uint64_t cora_probe_noalloc_scratch_limit(void) { return cora::kNoallocScratchBytes; }
+
+int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num_queries,
+                       uint64_t nprobe, int32_t *d_probe_ids, float *d_probe_dists, void *stream) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        if (!e.loaded) cora::fail(CORA_ESTATE, "load an index before probing");
+        if (!d_queries || !d_probe_ids || !d_probe_dists)
+            cora::fail(CORA_EINVAL, "invalid device probe buffers");
+        if (num_queries == 0 || num_queries > cora::kMaxQueryChunk)
+            cora::fail(CORA_EINVAL, "query count must be in [1, 65535]");
+        if (nprobe == 0 || nprobe > e.nlist || nprobe > cora::kMaxProbeFast)
+            cora::fail(CORA_EINVAL, "nprobe must be in [1, min(nlist, 4096)]");
+        const cora::NoallocLayout l = cora::noalloc_layout(num_queries, e.D, e.W4, e.nlist);
+        if (l.total > cora::kNoallocScratchBytes)
+            cora::fail(CORA_EINVAL, "probe needs " + std::to_string(l.total) +
+                                        " bytes of scratch; the static limit is " +
+                                        std::to_string(cora::kNoallocScratchBytes) +
+                                        " bytes: split the queries into smaller calls");
+        CUDA_TRY(cudaSetDevice(e.device));
+        unsigned char *s = cora::noalloc_scratch(e.device);
+        float *qr = reinterpret_cast<float *>(s + l.qr);
+        float *qnorm2 = reinterpret_cast<float *>(s + l.qnorm2);
+        auto *scal = reinterpret_cast<cora::QueryScalars *>(s + l.scal);
+        uint32_t *planes = reinterpret_cast<uint32_t *>(s + l.planes);
+        float *approx = reinterpret_cast<float *>(s + l.approx);
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e.stream;
+        const int inq = static_cast<int>(num_queries), inp = static_cast<int>(nprobe);
+
+        const size_t rsm = (size_t)cora::kRotQueries * (e.dim + e.D) * 4;
+        CUDA_TRY(cudaFuncSetAttribute(cora::rotate_prep_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm));
+        const float c_b = -static_cast<float>((1u << (e.ex_bits + 1)) - 1u) / 2.0f;
+        cora::rotate_prep_kernel<<<static_cast<unsigned>((num_queries + cora::kRotQueries - 1) /
+                                                         cora::kRotQueries),
+                                   256, rsm, st>>>(d_queries, inq, static_cast<int>(e.dim),
+                                                   static_cast<int>(e.D), e.W4, e.rotator.p, c_b,
+                                                   qr, scal, planes, qnorm2);
+        CUDA_TRY(cudaGetLastError());
+        dim3 grid(static_cast<unsigned>((e.nlist + cora::kDistTile - 1) / cora::kDistTile),
+                  static_cast<unsigned>((num_queries + cora::kDistTile - 1) / cora::kDistTile));
+        cora::approx_dist_f32_kernel<<<grid, 256, 0, st>>>(qr, qnorm2, inq, e.centroids.p,
+                                                           e.cnorm2.p, static_cast<int>(e.nlist),
+                                                           static_cast<int>(e.D), approx);
+        CUDA_TRY(cudaGetLastError());
+        const int ccap = cora::guarded_select_cap(inp);
+        const size_t gsm = cora::guarded_select_smem(inp, ccap, static_cast<int>(e.D));
+        CUDA_TRY(cudaFuncSetAttribute(cora::guarded_select_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm));
+        cora::guarded_select_kernel<<<inq, 256, gsm, st>>>(
+            approx, static_cast<int>(e.nlist), inp, ccap, qr, qnorm2, e.centroids.p, e.cmax,
+            static_cast<int>(e.D), cora::kApproxEpsF32, d_probe_ids, d_probe_dists);
+        CUDA_TRY(cudaGetLastError());
+    });
 }
 
 }  // extern "C"

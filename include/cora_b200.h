@@ -169,6 +169,27 @@ int cora_get_vanguard_mode(const cora_engine *engine);
 /* Candidate capacity per query of the current workspace (array 7 above is nq x cap). */
 uint64_t cora_get_candidate_capacity(const cora_engine *engine);
 
+/* Coarse probing that allocates nothing (no counterpart in the reference). For callers
+ * that need a query's probe list where they cannot allocate device memory: e.g. a router
+ * choosing the GPU or shard that owns a query's clusters while searches run beside it
+ * (cudaMalloc/cudaFree would synchronise the device), or a process that cannot afford the
+ * search workspace. Runs the search's own rotation, approximate-distance and guarded
+ * top-nprobe kernels on `stream` (NULL: the engine's stream) and returns without
+ * synchronising; needs a loaded index, not a workspace. Results equal what cora_search
+ * probes for the same queries (cora_debug_copy arrays 1 and 2).
+ *   d_queries      device, num_queries x dim f32
+ *   d_probe_ids    device, num_queries x nprobe i32 (per query ascending by (distance, id))
+ *   d_probe_dists  device, num_queries x nprobe f32 (exact squared distance to the centroid)
+ * Intermediates live in one static device block of cora_probe_noalloc_scratch_limit()
+ * bytes (16 MiB) per device; a call needing more is rejected with CORA_EINVAL (split the
+ * queries). Nothing in the block needs to start at zero. The first call on each device
+ * looks the block up (cudaGetSymbolAddress): make it before any stream capture. The block
+ * is shared by all engines of a device, so calls that overlap in time race on it:
+ * serialise them (e.g. one stream). */
+int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num_queries,
+                       uint64_t nprobe, int32_t *d_probe_ids, float *d_probe_dists, void *stream);
+uint64_t cora_probe_noalloc_scratch_limit(void);
+
 #ifdef __cplusplus
 }
 #endif
