@@ -17,9 +17,12 @@ public host API (cora_search: pinned host queries -> HBM -> results back to host
 compiled from the reference source into oracle/_ref) on the same index with every host
 thread, on a bounded query sample per step.
 
-Multi-GPU (torchrun, one process per GPU): the index is sharded by IVF cluster; every rank
-probes all centroids, scans the clusters it owns and the per-shard top-k lists are merged
-after an NCCL all-gather.
+Multi-GPU (torchrun, one process per GPU): the index is sharded by IVF cluster
+(coraanns_b200.shard); every rank probes all centroids and scans the clusters it owns; the
+shards' vanguard seed keys (-> the global pruning threshold) and then their top-k keys are
+exchanged by NCCL all-gathers and merged on every rank. All ranks answer the same 10K queries
+together, so the total work is fixed as N grows (strong scaling) and `value` is queries/s of
+the whole job.
 """
 from __future__ import annotations
 
@@ -272,10 +275,14 @@ def main():
     t0 = time.time()
     centres, base, q = make_data(cfg, dev)
     cent, lab = kmeans(base, centres)
+    if world > 1:
+        # every shard must cut the same partition: take rank 0's
+        dist.broadcast(cent, 0)
+        dist.broadcast(lab, 0)
     log(f"[bench] data + partition {time.time() - t0:.1f}s")
     from coraanns_b200 import builder
     import coraanns_b200 as cb
-    need_file = (args.impl == "reference") or (rank == 0 and not args.no_cpu_baseline)
+    need_file = (args.impl == "reference") or (rank == 0 and world == 1 and not args.no_cpu_baseline)
     t1 = time.time()
     sd = builder.build_index(base, cent, lab, seed=cfg["seed"], device=dev, keep_bits=need_file)
     log(f"[bench] index build {time.time() - t1:.1f}s")
@@ -316,27 +323,42 @@ def main():
             dist.destroy_process_group()
         return
 
-    eng = cb.HybridIndex(local)
-    eng.load_search_data(sd)
     nq = cfg["nq"]
     nprobes = [args.nprobe] if args.nprobe else cfg["nprobes"]
-    eng.prepare_workspace(nq, k, max(nprobes))
     # A dedicated (non-default) stream: the engine enqueues every kernel of a search on it and
     # the timing events are recorded on it too. torch's default stream is the legacy NULL
     # stream, which the engine's non-blocking streams do not order against.
     stream = torch.cuda.Stream(dev)
-    torch.cuda.synchronize()
     out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
     out_i = torch.empty((nq, k), dtype=torch.int32, device=dev)
+    if world > 1:
+        # cluster-sharded: this rank keeps the clusters the shard plan gives it
+        from coraanns_b200.shard import ShardedIndex, shard_plan
+        six = ShardedIndex(local)
+        six.load_search_data(sd)
+        six.prepare_workspace(nq, k, max(nprobes))
+        eng = six.engine
+        owner = shard_plan(sd["sizes"], world)
 
-    def search_dev(nprobe):
-        eng.search_device(q.data_ptr(), nq, k, nprobe, out_d.data_ptr(), out_i.data_ptr(),
-                          stream.cuda_stream)
+        def search_dev(nprobe):
+            with torch.cuda.stream(stream):
+                six.search_device(q, k, nprobe, out_d, out_i)
+    else:
+        eng = cb.HybridIndex(local)
+        eng.load_search_data(sd)
+        eng.prepare_workspace(nq, k, max(nprobes))
+        owner = None
+
+        def search_dev(nprobe):
+            eng.search_device(q.data_ptr(), nq, k, nprobe, out_d.data_ptr(), out_i.data_ptr(),
+                              stream.cuda_stream)
+    torch.cuda.synchronize()
 
     sweep = {}
     chosen = None
     for npb in nprobes:
         search_dev(npb)
+        torch.cuda.synchronize()
         eng.check_device()
         r = recall_at_k(base, q, gt_ids, gt_d, out_i.cpu().numpy().view(np.uint32), k)
         sweep[npb] = round(r, 4)
@@ -348,10 +370,18 @@ def main():
 
     # algorithmic bytes of one main-scan launch: sum over (query, probe) of n_c * (D/8 + 12)
     search_dev(chosen)
+    torch.cuda.synchronize()
     eng.check_device()
     probes = eng.debug("probe_ids", nq, chosen)
-    cand_per_query = eng.get_last_submitted_count() / nq
+    submitted = eng.get_last_submitted_count()
+    if world > 1:
+        t = torch.tensor([submitted], dtype=torch.int64, device=dev)
+        dist.all_reduce(t)
+        submitted = int(t.item())
+    cand_per_query = submitted / nq
     sizes = sd["sizes"].astype(np.int64)
+    if owner is not None:  # this rank scans only the clusters it owns
+        sizes = np.where(owner == rank, sizes, 0)
     D = int(sd["D"])
     scan_bytes = int(sizes[probes].sum()) * (D // 8 + 12)
 
@@ -380,20 +410,31 @@ def main():
     count, stage_tot = eng.stage_totals()
     stage_avg = {s: v / max(count, 1) for s, v in stage_tot.items()}
     eng.set_profiling(False)
-    qps = nq * world / (ms / 1e3)
+    # every rank answers the same nq queries together (each scans its own clusters)
+    qps = nq / (ms / 1e3)
 
     # ---- e2e through the public host API (pinned host queries, results to host) ----
     qh = torch.empty((nq, cfg["dim"]), dtype=torch.float32, pin_memory=True)
     qh.copy_(q.cpu())
     qh_np = qh.numpy()
-    eng.reset_buffer(qh_np)
+    if world > 1:
+        host_search = lambda: six.search(qh_np, k, chosen)  # noqa: E731
+    else:
+        eng.reset_buffer(qh_np)
+        host_search = lambda: eng.search(qh_np, k, chosen)  # noqa: E731
     for _ in range(args.warmup):
-        eng.search(qh_np, k, chosen)
+        host_search()
+    if world > 1:
+        dist.barrier()
     t = time.perf_counter()
     for _ in range(args.steps):
-        eng.search(qh_np, k, chosen)
+        host_search()
     e2e_s = (time.perf_counter() - t) / args.steps
-    e2e_qps = nq * world / e2e_s
+    if world > 1:
+        t = torch.tensor([e2e_s], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_qps = nq / e2e_s
 
     peak, peak_src = measured_peaks()
     # The 1-bit scan of one search is two passes of scan_kernel (vanguard pairs, then the
@@ -410,17 +451,19 @@ def main():
                          "of codes touched; cross-query reuse lets this exceed the physical DRAM "
                          "traffic)")
     mode = eng.get_vanguard_mode()
-    launches = (21 if mode == 1 else 13) * args.steps
+    # kernels per search: 21 with stored vanguard lows, 13 rescanning; +2 exchange steps
+    # (gather_threshold_kernel, gather_merge_kernel) when sharded
+    launches = ((21 if mode == 1 else 13) + (2 if world > 1 else 0)) * args.steps
 
     cpu_base = None
-    if rank == 0 and not args.no_cpu_baseline and index_path is not None:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and index_path is not None:
         cpu_base, _ = cpu_reference_qps(index_path, q_np, k, chosen, target_seconds=15.0)
 
     if rank == 0:
         line = dict(
             metric="QPS at recall@10>=0.95 (IVF-RaBitQ search)", value=qps, unit="queries/s",
             n_gpus=world, steps=args.steps, warmup=args.warmup, ms_per_step=ms,
-            higher_is_better=True, scaling="weak" if world > 1 else "strong", vs_baseline=None,
+            higher_is_better=True, scaling="strong", vs_baseline=None,
             dtype="u32+f32", data="synthetic (seeded Gaussian mixture, BASELINE config 2 shape)",
             config=dict(workload=f"{args.config}: {cfg['n']} x d{cfg['dim']} L2, nlist {cfg['nlist']}, "
                                  f"8-bit RaBitQ, {nq} queries, topk {k}",
@@ -428,7 +471,9 @@ def main():
                         candidates_per_query=cand_per_query,
                         vanguard_mode="lows" if mode == 1 else "rescan",
                         l2_flush="inputs exceed L2 (index codes > 126 MB)",
-                        stage_ms=stage_avg, parallelism=f"replicas x{world}" if world > 1 else "single"),
+                        stage_ms=stage_avg,
+                        parallelism=(f"cluster-sharded x{world} (NCCL all-gather of seed and "
+                                     f"top-k keys)") if world > 1 else "single"),
             roofline=roofline, cpu_baseline=cpu_base,
             e2e=dict(value=e2e_qps, unit="queries/s", h2d_bytes_per_step=nq * cfg["dim"] * 4,
                      d2h_bytes_per_step=nq * k * 8),

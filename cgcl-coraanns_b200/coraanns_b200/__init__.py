@@ -41,6 +41,8 @@ EXPORTS = [
     "cora_debug_copy", "cora_get_last_stage_ms", "cora_stage_totals", "cora_stage_reset",
     "cora_set_vanguard_lows_budget", "cora_set_tuning", "cora_get_vanguard_mode",
     "cora_get_candidate_capacity", "cora_probe_noalloc", "cora_probe_noalloc_scratch_limit",
+    "cora_shard_plan", "cora_shard_configure", "cora_shard_info", "cora_shard_exchange_words",
+    "cora_shard_search_begin", "cora_shard_search_resume", "cora_shard_search_end",
 ]
 
 _p = C.c_void_p
@@ -91,6 +93,13 @@ _sig("cora_get_vanguard_mode", C.c_int, _p)
 _sig("cora_set_tuning", C.c_int, _p, C.c_char_p, C.c_int64)
 _sig("cora_probe_noalloc", C.c_int, _p, _p, _u64, _u64, _p, _p, _p)
 _sig("cora_probe_noalloc_scratch_limit", _u64)
+_sig("cora_shard_plan", C.c_int, _p, _u64, C.c_uint32, _p)
+_sig("cora_shard_configure", C.c_int, _p, C.c_uint32, C.c_uint32)
+_sig("cora_shard_info", C.c_int, _p, _p)
+_sig("cora_shard_exchange_words", _u64, _u64, _u64)
+_sig("cora_shard_search_begin", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p)
+_sig("cora_shard_search_resume", C.c_int, _p, _p, _p)
+_sig("cora_shard_search_end", C.c_int, _p, _p, _p, _p)
 
 STAGES = ("rotate_prep", "centroid_dist", "select_probes", "vanguard_grouping",
           "vanguard_scan", "vanguard_select", "seed_refine", "threshold", "main_grouping",
@@ -223,6 +232,28 @@ class HybridIndex:
         _check(_lib.cora_probe_noalloc(self._h, C.c_void_p(d_queries), num_queries, nprobe,
                                        C.c_void_p(d_probe_ids), C.c_void_p(d_probe_dists),
                                        C.c_void_p(stream) if stream else None))
+
+    # ---- cluster sharding (see coraanns_b200.shard) ----
+    def shard_configure(self, rank: int, world: int):
+        _check(_lib.cora_shard_configure(self._h, rank, world))
+
+    def shard_info(self) -> dict:
+        out = np.zeros(4, np.uint64)
+        _check(_lib.cora_shard_info(self._h, _ptr(out)))
+        return dict(rank=int(out[0]), world=int(out[1]), vectors=int(out[2]), clusters=int(out[3]))
+
+    def shard_search_begin(self, d_queries: int, num_queries, topk, nprobe, d_send: int,
+                           stream: int = 0):
+        _check(_lib.cora_shard_search_begin(self._h, C.c_void_p(d_queries), num_queries, topk,
+                                            nprobe, C.c_void_p(d_send),
+                                            C.c_void_p(stream) if stream else None))
+
+    def shard_search_resume(self, d_recv: int, d_send: int):
+        _check(_lib.cora_shard_search_resume(self._h, C.c_void_p(d_recv), C.c_void_p(d_send)))
+
+    def shard_search_end(self, d_recv: int, d_dists: int, d_ids: int):
+        _check(_lib.cora_shard_search_end(self._h, C.c_void_p(d_recv), C.c_void_p(d_dists),
+                                          C.c_void_p(d_ids)))
 
     def check_device(self):
         _check(_lib.cora_check_device(self._h))

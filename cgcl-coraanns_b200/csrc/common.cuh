@@ -42,7 +42,8 @@ enum DeviceError : int {
     kDevBadInput = 4,
 };
 
-// ---- TMA bulk copies (cp.async.bulk, no multicast) with bounded mbarrier waits -------
+// ---- TMA bulk copies (cp.async.bulk into this CTA's shared memory only) with bounded
+// mbarrier waits ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

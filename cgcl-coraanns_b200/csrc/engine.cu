@@ -46,6 +46,7 @@ constexpr uint64_t kDefaultVanguard = 5, kMaxQueryChunk = 65535, kMaxProbeCount 
 constexpr uint64_t kDefaultQueueCapacity = 1ull << 26, kDefaultSpillCapacity = 1ull << 24;
 constexpr uint64_t kMaxTopk = 4096, kMaxProbeFast = 4096, kMaxPaddedDim = 1024;
 constexpr int kVanguardMinKeep = 20;
+constexpr uint32_t kMaxShards = 256;
 
 // parameters.hpp:15-25
 void validate_search_shape(uint64_t queries, uint64_t topk, uint64_t nprobe, uint64_t centroids,
@@ -79,6 +80,40 @@ struct DevBuf {
 };
 
 }  // namespace
+
+enum class ScanPhase { kRescanVanguard, kWriteLows, kMain };
+
+struct ScanLaunch {
+    IndexView ix;
+    SearchView sv;
+    int rescan_sort_n;
+    uint64_t n_van;
+    const ScanItem *items;
+    const uint32_t *n_items;
+    const uint32_t *pairs;
+    int *item_counter;
+    const uint8_t *owned;
+    int num_sms;
+    cudaStream_t st;
+};
+
+// Cluster-to-shard plan: longest-processing-time greedy on cluster sizes (every vector of an
+// index costs the same bytes), largest cluster first (ties: lower cluster id) onto the least
+// loaded shard (ties: lower rank). Deterministic, so every rank derives the same plan.
+inline void plan_shards(const uint64_t *sizes, uint64_t nlist, uint32_t world, int32_t *owner) {
+    std::vector<uint32_t> order(nlist);
+    for (uint64_t c = 0; c < nlist; ++c) order[c] = static_cast<uint32_t>(c);
+    std::stable_sort(order.begin(), order.end(),
+                     [&](uint32_t a, uint32_t b) { return sizes[a] > sizes[b]; });
+    std::vector<uint64_t> load(world, 0);
+    for (uint32_t c : order) {
+        uint32_t best = 0;
+        for (uint32_t r = 1; r < world; ++r)
+            if (load[r] < load[best]) best = r;
+        owner[c] = static_cast<int32_t>(best);
+        load[best] += sizes[c];
+    }
+}
 
 struct Engine {
     int device = 0;
@@ -134,7 +169,14 @@ struct Engine {
     std::vector<float> h_T0;  // host mirror kept for capture/seed without device syncs
 
     // last-search state
-    uint64_t last_nq = 0, last_np = 0, last_submitted = 0, last_refined = 0;
+    uint64_t last_nq = 0, last_k = 0, last_np = 0, last_submitted = 0, last_refined = 0;
+
+    // cluster sharding (set before loading): this engine keeps the clusters plan_shards()
+    // gives `shard_rank` of `shard_world`; split_phase tracks a sharded search in progress
+    // (0 none, 1 after begin, 2 after resume).
+    uint32_t shard_rank = 0, shard_world = 1;
+    uint64_t shard_clusters = 0;
+    int split_phase = 0;
     float last_filter_ms = 0.0f;
 
     explicit Engine(int dev) : device(dev) {
@@ -234,6 +276,71 @@ struct Engine {
         repack_scan_planes(tmp_short.p, tmp_fac.p);
         CUDA_TRY(cudaStreamSynchronize(stream));
         loaded = true;
+    }
+
+    // Loads the whole index, or (shard_world > 1) only the clusters plan_shards() gives this
+    // shard: the others keep their centroids, since every shard probes all of them, but no
+    // vectors, and the `owned` mask makes the grouping and vanguard kernels skip them. Each
+    // kept cluster's vectors stay in their order, so ties between equal lower bounds break
+    // the same way as on an unsharded index.
+    void load_any(uint64_t num_vecs, uint64_t d, uint64_t p_d, uint64_t n_centroids,
+                  uint64_t ex_b, const float *h_centroids, const float *h_rotator,
+                  const uint32_t *h_short, const float *h_sf, const uint8_t *h_long,
+                  const float *h_exf, const uint32_t *h_ids, const uint64_t *h_sizes) {
+        const bool valid = h_centroids && h_rotator && h_short && h_sf && h_long && h_exf &&
+                           h_ids && h_sizes && n_centroids && ex_b == 7 && p_d >= d && d &&
+                           p_d % 64 == 0 && p_d <= kMaxPaddedDim;
+        if (shard_world <= 1 || !valid) {  // invalid arguments: load() reports them
+            load(num_vecs, d, p_d, n_centroids, ex_b, h_centroids, h_rotator, h_short, h_sf,
+                 h_long, h_exf, h_ids, h_sizes);
+            shard_clusters = n_centroids;
+            return;
+        }
+        if (loaded) fail(CORA_ESTATE, "index already loaded");
+        uint64_t total = 0;
+        for (uint64_t c = 0; c < n_centroids; ++c) {
+            if (h_sizes[c] > num_vecs - total) fail(CORA_EINVAL, "cluster sizes exceed index size");
+            total += h_sizes[c];
+        }
+        if (total != num_vecs) fail(CORA_EINVAL, "cluster sizes differ from index size");
+        std::vector<int32_t> owner(n_centroids);
+        plan_shards(h_sizes, n_centroids, shard_world, owner.data());
+        const uint64_t W = p_d / 32, lc = p_d * ex_b / 8;
+        uint64_t local = 0, kept = 0;
+        for (uint64_t c = 0; c < n_centroids; ++c)
+            if (owner[c] == static_cast<int32_t>(shard_rank)) {
+                local += h_sizes[c];
+                ++kept;
+            }
+        if (local == 0)
+            fail(CORA_EINVAL, "shard " + std::to_string(shard_rank) + " of " +
+                                  std::to_string(shard_world) +
+                                  " owns no vectors; use fewer shards for this index");
+        std::vector<uint32_t> s_short(local * W), s_ids(local);
+        std::vector<float> s_sf(local * 3), s_exf(local * 2);
+        std::vector<uint8_t> s_long(local * lc), mask(n_centroids, 0);
+        std::vector<uint64_t> s_sizes(n_centroids, 0);
+        uint64_t src = 0, dst = 0;
+        for (uint64_t c = 0; c < n_centroids; ++c) {
+            const uint64_t n = h_sizes[c];
+            if (owner[c] == static_cast<int32_t>(shard_rank)) {
+                // a cluster's 1-bit block is contiguous (word-major within the cluster)
+                std::memcpy(s_short.data() + dst * W, h_short + src * W, n * W * 4);
+                std::memcpy(s_sf.data() + dst * 3, h_sf + src * 3, n * 12);
+                std::memcpy(s_long.data() + dst * lc, h_long + src * lc, n * lc);
+                std::memcpy(s_exf.data() + dst * 2, h_exf + src * 2, n * 8);
+                std::memcpy(s_ids.data() + dst, h_ids + src, n * 4);
+                s_sizes[c] = n;
+                mask[c] = 1;
+                dst += n;
+            }
+            src += n;
+        }
+        load(local, d, p_d, n_centroids, ex_b, h_centroids, h_rotator, s_short.data(),
+             s_sf.data(), s_long.data(), s_exf.data(), s_ids.data(), s_sizes.data());
+        owned.alloc(n_centroids);
+        CUDA_TRY(cudaMemcpy(owned.p, mask.data(), n_centroids, cudaMemcpyHostToDevice));
+        shard_clusters = kept;
     }
 
     void repack_scan_planes(const uint32_t *d_short, const float *d_fac);
@@ -375,6 +482,17 @@ struct Engine {
     // ---------------------------------------------------------------- search
     void enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, float *d_od,
                         uint32_t *d_oi, cudaStream_t st);
+    void enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, cudaStream_t st,
+                       uint64_t *seed_keys_out);
+    void enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uint32_t *d_oi,
+                      uint64_t *topk_keys_out);
+    void enqueue_final(const uint64_t *topk_recv, int world, float *d_od, uint32_t *d_oi);
+    IndexView index_view() const;
+    SearchView search_view() const;
+    ScanLaunch scan_launch(const IndexView &ix, const SearchView &sv, cudaStream_t st) const;
+    void group_pairs(int r_lo, int r_hi, cudaStream_t st);
+    // u64 words per shard in an exchange buffer: k keys per query + one status word.
+    static uint64_t exchange_stride(uint64_t nq, uint64_t k) { return nq * k + 1; }
     void finish(cudaStream_t st) {
         int h_err = 0;
         unsigned long long h_stats[2] = {0, 0};
@@ -392,9 +510,16 @@ struct Engine {
         if (h_err) fail(CORA_ERUNTIME, "device reported an error");
     }
 
+    void require_whole_index() const {
+        if (shard_world > 1)
+            fail(CORA_ESTATE, "this engine holds one shard of the index: search it with the "
+                              "shard search calls (begin / resume / end) on every shard");
+    }
+
     void search_host(const float *h_q, uint64_t nq, uint64_t k, uint64_t np, float *h_d,
                      uint32_t *h_i, int batch_q) {
         validate_ws(nq, k, np);
+        require_whole_index();
         if (!h_q || !h_d || !h_i || batch_q < 1 || batch_q > 6)
             fail(CORA_EINVAL, "invalid search buffers or batch-q (expected 1..6)");
         CUDA_TRY(cudaSetDevice(device));
@@ -499,22 +624,6 @@ size_t scan_smem() {
     return 2 * Sh::kStageEntries * 16 + (size_t)kMaxPairsPerItem * 8 * Sh::W4 * 4;
 }
 
-enum class ScanPhase { kRescanVanguard, kWriteLows, kMain };
-
-struct ScanLaunch {
-    IndexView ix;
-    SearchView sv;
-    int rescan_sort_n;
-    uint64_t n_van;
-    const ScanItem *items;
-    const uint32_t *n_items;
-    const uint32_t *pairs;
-    int *item_counter;
-    const uint8_t *owned;
-    int num_sms;
-    cudaStream_t st;
-};
-
 template <int G16, bool kLows>
 void launch_grouped(const ScanLaunch &L) {
     const size_t sm = scan_smem<G16>();
@@ -563,10 +672,35 @@ void dispatch_scan(int G16, const ScanLaunch &L, ScanPhase phase) {
 }
 }  // namespace
 
+IndexView Engine::index_view() const {
+    return IndexView{scan4.p, cl_start.p, cl_size.p, long_codes.p, ex_factors.p, ids.p,
+                     static_cast<int>(nlist), static_cast<int>(D), G16, LC};
+}
+
+SearchView Engine::search_view() const {
+    const uint64_t veff = vanguard_depth(last_np);
+    const uint64_t keep = std::max<uint64_t>(last_k, kVanguardMinKeep);
+    return SearchView{static_cast<int>(last_nq), static_cast<int>(last_k), static_cast<int>(last_np),
+                      static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
+                      scal.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p,
+                      cand_cnt.p, seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n,
+                      err.p, warp_select_limit};
+}
+
 void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, float *d_od,
                             uint32_t *d_oi, cudaStream_t st) {
+    enqueue_front(d_q, nq, k, np, st, nullptr);
+    enqueue_back(nullptr, 0, d_od, d_oi, nullptr);
+    mark(13, st);
+}
+
+// Stages 0..7: rotation, probing, vanguard seeding and seed refinement, then the threshold
+// (T1) or, for a sharded search, this shard's k smallest seed keys into seed_keys_out.
+void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t np,
+                           cudaStream_t st, uint64_t *seed_keys_out) {
     last_stream = st;
     last_nq = nq;
+    last_k = k;
     last_np = np;
     const int inq = static_cast<int>(nq), inp = static_cast<int>(np), ik = static_cast<int>(k);
     const uint64_t veff = vanguard_depth(np);
@@ -612,40 +746,16 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     }
     mark(3, st);
     const bool lows_mode = lows.n > 0;
-    IndexView ix{scan4.p, cl_start.p, cl_size.p, long_codes.p, ex_factors.p, ids.p,
-                 static_cast<int>(nlist), static_cast<int>(D), G16, LC};
-    SearchView sv{inq, ik, inp, static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
-                  scal.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p, cand_cnt.p,
-                  seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n, err.p,
-                  warp_select_limit};
+    const IndexView ix = index_view();
+    const SearchView sv = search_view();
     const uint8_t *own = owned.n ? owned.p : nullptr;
-    const int rescan_sort_n = next_pow2(static_cast<int>(keep) + (G16 <= 2 ? 512 : 256));
-    ScanLaunch L{ix, sv, rescan_sort_n, nq * veff, items.p, n_items.p, pairs.p, item_counter.p,
-                 own, num_sms, st};
-    // Per-cluster grouping of the (query, probe rank) pairs with rank in [r_lo, r_hi):
-    // cross-query reuse serves up to kMaxPairsPerItem queries from one cluster read.
-    auto group_pairs = [&](int r_lo, int r_hi) {
-        const size_t total = nq * np;
-        const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
-        CUDA_TRY(cudaMemsetAsync(pair_cnt.p, 0, nlist * 4, st));
-        CUDA_TRY(cudaMemsetAsync(pair_cur.p, 0, nlist * 4, st));
-        CUDA_TRY(cudaMemsetAsync(item_counter.p, 0, 4, st));
-        const int ppi = cross_query_reuse ? kMaxPairsPerItem : 1;
-        count_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own,
-                                                   pair_cnt.p);
-        scan_pairs_kernel<<<1, 1024, 0, st>>>(pair_cnt.p, static_cast<int>(nlist), ppi,
-                                               pair_off.p, item_off.p, n_items.p);
-        scatter_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own,
-                                                     pair_off.p, pair_cur.p, pairs.p);
-        emit_items_kernel<<<static_cast<unsigned>((nlist + 255) / 256), 256, 0, st>>>(
-            pair_cnt.p, pair_off.p, item_off.p, static_cast<int>(nlist), ppi, items.p);
-        CUDA_TRY(cudaGetLastError());
-    };
+    const ScanLaunch L = scan_launch(ix, sv, st);
+    (void)ik;
     const int iveff = static_cast<int>(veff);
     const unsigned n_van = static_cast<unsigned>(nq * veff);
     // 3. vanguard pairs: seeds (best `keep` keys per pair among low < T0)
     if (lows_mode) {
-        group_pairs(0, iveff);
+        group_pairs(0, iveff, st);
         vanguard_offsets_kernel<<<1, 1024, 0, st>>>(probe_ids.p, cl_size.p, own, inq, inp, iveff,
                                                     lows.n, vg_off.p, err.p);
         CUDA_TRY(cudaGetLastError());
@@ -682,15 +792,67 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 0);
     CUDA_TRY(cudaGetLastError());
     mark(7, st);
-    const size_t sel_sm = (size_t)next_pow2(ik) * 8;
+    const size_t sel_sm = (size_t)next_pow2(static_cast<int>(k)) * 8;
     CUDA_TRY(cudaFuncSetAttribute(threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)sel_sm));
-    threshold_kernel<<<inq, 256, sel_sm, st>>>(sv);
+    threshold_kernel<<<inq, 256, sel_sm, st>>>(sv, seed_keys_out);
     CUDA_TRY(cudaGetLastError());
+}
+
+ScanLaunch Engine::scan_launch(const IndexView &ix, const SearchView &sv, cudaStream_t st) const {
+    const uint64_t keep = std::max<uint64_t>(last_k, kVanguardMinKeep);
+    const int rescan_sort_n = next_pow2(static_cast<int>(keep) + (G16 <= 2 ? 512 : 256));
+    return ScanLaunch{ix, sv, rescan_sort_n, last_nq * vanguard_depth(last_np), items.p, n_items.p,
+                      pairs.p, item_counter.p, owned.n ? owned.p : nullptr, num_sms, st};
+}
+
+// Per-cluster grouping of the (query, probe rank) pairs with rank in [r_lo, r_hi): cross-query
+// reuse serves up to kMaxPairsPerItem queries from one cluster read.
+void Engine::group_pairs(int r_lo, int r_hi, cudaStream_t st) {
+    const int inq = static_cast<int>(last_nq), inp = static_cast<int>(last_np);
+    const uint8_t *own = owned.n ? owned.p : nullptr;
+    const size_t total = last_nq * last_np;
+    const unsigned blocks = static_cast<unsigned>((total + 255) / 256);
+    CUDA_TRY(cudaMemsetAsync(pair_cnt.p, 0, nlist * 4, st));
+    CUDA_TRY(cudaMemsetAsync(pair_cur.p, 0, nlist * 4, st));
+    CUDA_TRY(cudaMemsetAsync(item_counter.p, 0, 4, st));
+    const int ppi = cross_query_reuse ? kMaxPairsPerItem : 1;
+    count_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own, pair_cnt.p);
+    scan_pairs_kernel<<<1, 1024, 0, st>>>(pair_cnt.p, static_cast<int>(nlist), ppi, pair_off.p,
+                                           item_off.p, n_items.p);
+    scatter_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own,
+                                                 pair_off.p, pair_cur.p, pairs.p);
+    emit_items_kernel<<<static_cast<unsigned>((nlist + 255) / 256), 256, 0, st>>>(
+        pair_cnt.p, pair_off.p, item_off.p, static_cast<int>(nlist), ppi, items.p);
+    CUDA_TRY(cudaGetLastError());
+}
+
+// Stages 8..12 on last_stream: (sharded: T1 from every shard's seed keys in seed_recv) the
+// main pass against T1, refinement and the top-k, written as the result or, sharded, as this
+// shard's k best keys (+ its error word) into topk_keys_out.
+void Engine::enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uint32_t *d_oi,
+                          uint64_t *topk_keys_out) {
+    cudaStream_t st = last_stream;
+    const int inq = static_cast<int>(last_nq), inp = static_cast<int>(last_np);
+    const int iveff = static_cast<int>(vanguard_depth(last_np));
+    const unsigned n_van = static_cast<unsigned>(last_nq * vanguard_depth(last_np));
+    const bool lows_mode = lows.n > 0;
+    const IndexView ix = index_view();
+    const SearchView sv = search_view();
+    const uint8_t *own = owned.n ? owned.p : nullptr;
+    const ScanLaunch L = scan_launch(ix, sv, st);
+    const size_t sel_sm = (size_t)next_pow2(static_cast<int>(last_k)) * 8;
+    if (seed_recv) {
+        CUDA_TRY(cudaFuncSetAttribute(gather_threshold_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sel_sm));
+        gather_threshold_kernel<<<inq, 256, sel_sm, st>>>(seed_recv, world,
+                                                          exchange_stride(last_nq, last_k), sv);
+        CUDA_TRY(cudaGetLastError());
+    }
     mark(8, st);
     // 4. main pass against T1: the other probes are scanned; the vanguard probes are either
     //    filtered from their stored lows or rescanned, skipping their seeds in both cases.
-    group_pairs(lows_mode ? iveff : 0, inp);
+    group_pairs(lows_mode ? iveff : 0, inp, st);
     mark(9, st);
     dispatch_scan(G16, L, ScanPhase::kMain);
     mark(10, st);
@@ -700,13 +862,26 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     }
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));
     mark(11, st);
+    const size_t refine_sm = (size_t)D * 4 + last_np * sizeof(ProbeInfo);
     refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 1);
     CUDA_TRY(cudaGetLastError());
     mark(12, st);
     // 5. final top-k
     CUDA_TRY(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)sel_sm));
-    merge_kernel<<<inq, 256, sel_sm, st>>>(sv, d_od, d_oi, stats.p);
+    merge_kernel<<<inq, 256, sel_sm, st>>>(sv, d_od, d_oi, stats.p, topk_keys_out);
+    CUDA_TRY(cudaGetLastError());
+}
+
+// Sharded search, last step: the top-k over every shard's k best keys in topk_recv.
+void Engine::enqueue_final(const uint64_t *topk_recv, int world, float *d_od, uint32_t *d_oi) {
+    cudaStream_t st = last_stream;
+    const SearchView sv = search_view();
+    const size_t sel_sm = (size_t)next_pow2(static_cast<int>(last_k)) * 8;
+    CUDA_TRY(cudaFuncSetAttribute(gather_merge_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sel_sm));
+    gather_merge_kernel<<<static_cast<unsigned>(last_nq), 256, sel_sm, st>>>(
+        topk_recv, world, exchange_stride(last_nq, last_k), sv, d_od, d_oi);
     CUDA_TRY(cudaGetLastError());
     mark(13, st);
 }
@@ -919,8 +1094,9 @@ int cora_load_from_raw_pointers(cora_engine *engine, uint64_t num_vecs, uint64_t
                                 const float *h_ex_factors, const uint32_t *h_ids,
                                 const uint64_t *h_cluster_sizes) {
     return guarded([&] {
-        eng(engine).load(num_vecs, d, p_d, n_centroids, ex_b, h_centroids, h_rotator, h_short_data,
-                         h_short_factors, h_long_code, h_ex_factors, h_ids, h_cluster_sizes);
+        eng(engine).load_any(num_vecs, d, p_d, n_centroids, ex_b, h_centroids, h_rotator,
+                             h_short_data, h_short_factors, h_long_code, h_ex_factors, h_ids,
+                             h_cluster_sizes);
     });
 }
 
@@ -930,7 +1106,7 @@ int cora_load_index_file(cora_engine *engine, const char *path) {
         if (e.loaded) cora::fail(CORA_ESTATE, "index already loaded");
         if (!path) cora::fail(CORA_EINVAL, "null index path");
         cora::FileIndex f = cora::read_index_file(path);
-        e.load(f.num, f.dim, f.D, f.nlist, f.ex_bits, f.centroids.data(), f.rotator.data(),
+        e.load_any(f.num, f.dim, f.D, f.nlist, f.ex_bits, f.centroids.data(), f.rotator.data(),
                f.short_data.data(), f.short_factors.data(), f.long_codes.data(), f.ex_factors.data(),
                f.ids.data(), f.sizes.data());
     });
@@ -973,11 +1149,86 @@ int cora_search_device(cora_engine *engine, const float *d_queries, uint64_t num
     return guarded([&] {
         Engine &e = eng(engine);
         e.validate_ws(num_queries, topk, nprobe);
+        e.require_whole_index();
         if (!d_queries || !d_final_dists || !d_final_pids)
             cora::fail(CORA_EINVAL, "invalid device search buffers");
         CUDA_TRY(cudaSetDevice(e.device));
         cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e.stream;
         e.enqueue_search(d_queries, num_queries, topk, nprobe, d_final_dists, d_final_pids, st);
+    });
+}
+
+// ---- cluster-sharded search ---------------------------------------------------------------
+int cora_shard_plan(const uint64_t *sizes, uint64_t nlist, uint32_t world, int32_t *owner_out) {
+    return guarded([&] {
+        if (!sizes || !owner_out || nlist == 0 || world == 0 || world > cora::kMaxShards)
+            cora::fail(CORA_EINVAL, "invalid shard plan arguments");
+        cora::plan_shards(sizes, nlist, world, owner_out);
+    });
+}
+
+int cora_shard_configure(cora_engine *engine, uint32_t rank, uint32_t world) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        if (e.loaded) cora::fail(CORA_ESTATE, "configure sharding before loading the index");
+        if (world == 0 || world > cora::kMaxShards || rank >= world)
+            cora::fail(CORA_EINVAL, "shard rank must be in [0, world) and world in [1, 256]");
+        e.shard_rank = rank;
+        e.shard_world = world;
+    });
+}
+
+int cora_shard_info(const cora_engine *engine, uint64_t *out4) {
+    return guarded([&] {
+        const Engine &e = eng(engine);
+        if (!out4) cora::fail(CORA_EINVAL, "null output");
+        out4[0] = e.shard_rank;
+        out4[1] = e.shard_world;
+        out4[2] = e.loaded ? e.N : 0;
+        out4[3] = e.loaded ? e.shard_clusters : 0;
+    });
+}
+
+uint64_t cora_shard_exchange_words(uint64_t num_queries, uint64_t topk) {
+    return Engine::exchange_stride(num_queries, topk);
+}
+
+int cora_shard_search_begin(cora_engine *engine, const float *d_queries, uint64_t num_queries,
+                            uint64_t topk, uint64_t nprobe, uint64_t *d_send, void *stream) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        e.validate_ws(num_queries, topk, nprobe);
+        if (!d_queries || !d_send) cora::fail(CORA_EINVAL, "invalid device search buffers");
+        CUDA_TRY(cudaSetDevice(e.device));
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e.stream;
+        e.split_phase = 0;
+        e.enqueue_front(d_queries, num_queries, topk, nprobe, st, d_send);
+        e.split_phase = 1;
+    });
+}
+
+int cora_shard_search_resume(cora_engine *engine, const uint64_t *d_recv, uint64_t *d_send) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        if (e.split_phase != 1) cora::fail(CORA_ESTATE, "shard search: begin must come first");
+        if (!d_recv || !d_send) cora::fail(CORA_EINVAL, "invalid exchange buffers");
+        CUDA_TRY(cudaSetDevice(e.device));
+        e.split_phase = 0;
+        e.enqueue_back(d_recv, static_cast<int>(e.shard_world), nullptr, nullptr, d_send);
+        e.split_phase = 2;
+    });
+}
+
+int cora_shard_search_end(cora_engine *engine, const uint64_t *d_recv, float *d_final_dists,
+                          uint32_t *d_final_pids) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        if (e.split_phase != 2) cora::fail(CORA_ESTATE, "shard search: resume must come first");
+        if (!d_recv || !d_final_dists || !d_final_pids)
+            cora::fail(CORA_EINVAL, "invalid exchange or result buffers");
+        CUDA_TRY(cudaSetDevice(e.device));
+        e.split_phase = 0;
+        e.enqueue_final(d_recv, static_cast<int>(e.shard_world), d_final_dists, d_final_pids);
     });
 }
 

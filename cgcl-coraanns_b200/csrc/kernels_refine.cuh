@@ -110,9 +110,34 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
     }
 }
 
+__device__ __forceinline__ float threshold_from_kth(uint64_t kth, float T0) {
+    return kth == kKeyMax ? T0 : fminf(T0, unord_f32(static_cast<uint32_t>(kth >> 32)));
+}
+
+// Writes a query's k selected keys as its final result: distances / ids padded with
+// (FLT_MAX, 0), and the threshold after the search (k-th distance when k results exist,
+// else T0; what capture_thresholds() reports).
+__device__ __forceinline__ void write_topk(const uint64_t *s_keys, int q, int k, float T0,
+                                           float *out_d, uint32_t *out_i, float *Tcap) {
+    for (int j = threadIdx.x; j < k; j += blockDim.x) {
+        const uint64_t key = s_keys[j];
+        const bool ok = key != kKeyMax;
+        out_d[(size_t)q * k + j] = ok ? unord_f32(static_cast<uint32_t>(key >> 32)) : FLT_MAX;
+        out_i[(size_t)q * k + j] = ok ? static_cast<uint32_t>(key & 0xFFFFFFFFu) : 0u;
+    }
+    if (threadIdx.x == 0) {
+        const uint64_t kth = s_keys[k - 1];
+        Tcap[q] = kth != kKeyMax ? unord_f32(static_cast<uint32_t>(kth >> 32)) : T0;
+    }
+}
+
 // One CTA per query: T1 = min(T0, k-th smallest seed distance below T0) when at least k
-// seeds are below T0, else T0. Dynamic shared memory: next_pow2(k) keys.
-__global__ void __launch_bounds__(256) threshold_kernel(SearchView sv) {
+// seeds are below T0, else T0. Sharded search (keys_out != nullptr): writes this shard's k
+// smallest seed keys (padded with kKeyMax) to keys_out[q * k ..] instead, for the exchange;
+// gather_threshold_kernel then derives T1 from every shard's keys. Dynamic shared memory:
+// next_pow2(k) keys.
+__global__ void __launch_bounds__(256) threshold_kernel(SearchView sv,
+                                                        uint64_t *__restrict__ keys_out) {
     extern __shared__ uint64_t s_keys[];
     __shared__ int scratch[256 + 3];
     const int q = blockIdx.x;
@@ -124,19 +149,23 @@ __global__ void __launch_bounds__(256) threshold_kernel(SearchView sv) {
         return unord_f32(static_cast<uint32_t>(key >> 32)) < T0 ? key : kKeyMax;
     };
     block_select_smallest(key_at, n, sv.k, s_keys, scratch);
-    if (threadIdx.x == 0) {
-        const uint64_t kth = s_keys[sv.k - 1];
-        sv.T1[q] = kth == kKeyMax ? T0 : fminf(T0, unord_f32(static_cast<uint32_t>(kth >> 32)));
+    if (keys_out) {
+        for (int j = threadIdx.x; j < sv.k; j += blockDim.x)
+            keys_out[(size_t)q * sv.k + j] = s_keys[j];
+    } else if (threadIdx.x == 0) {
+        sv.T1[q] = threshold_from_kth(s_keys[sv.k - 1], T0);
     }
 }
 
-// One CTA per query: final top-k by (ex, id) among all refined candidates with ex < T0.
-// Writes distances / ids (padded with FLT_MAX / 0), records the query's threshold after the
-// search (its k-th distance when k results exist, else T0; what capture_thresholds()
-// reports) and adds the candidate count to stats[0]. Dynamic shared memory: next_pow2(k).
+// One CTA per query: final top-k by (ex, id) among all refined candidates with ex < T0, and
+// the candidate count added to stats[0]. keys_out == nullptr: writes the result
+// (write_topk). Sharded search: writes this shard's k best keys to keys_out[q * k ..] and,
+// from block 0, the shard's device error word to keys_out[nq * k], for the exchange that
+// gather_merge_kernel completes. Dynamic shared memory: next_pow2(k).
 __global__ void __launch_bounds__(256) merge_kernel(SearchView sv, float *__restrict__ out_d,
                                                     uint32_t *__restrict__ out_i,
-                                                    unsigned long long *__restrict__ stats) {
+                                                    unsigned long long *__restrict__ stats,
+                                                    uint64_t *__restrict__ keys_out) {
     extern __shared__ uint64_t s_keys[];
     __shared__ int scratch[256 + 3];
     const int q = blockIdx.x;
@@ -149,16 +178,59 @@ __global__ void __launch_bounds__(256) merge_kernel(SearchView sv, float *__rest
         return unord_f32(static_cast<uint32_t>(key >> 32)) < T0 ? key : kKeyMax;
     };
     block_select_smallest(key_at, n, sv.k, s_keys, scratch);
-    for (int j = threadIdx.x; j < sv.k; j += blockDim.x) {
-        const uint64_t key = s_keys[j];
-        const bool ok = key != kKeyMax;
-        out_d[(size_t)q * sv.k + j] = ok ? unord_f32(static_cast<uint32_t>(key >> 32)) : FLT_MAX;
-        out_i[(size_t)q * sv.k + j] = ok ? static_cast<uint32_t>(key & 0xFFFFFFFFu) : 0u;
+    if (keys_out) {
+        for (int j = threadIdx.x; j < sv.k; j += blockDim.x)
+            keys_out[(size_t)q * sv.k + j] = s_keys[j];
+        if (q == 0 && threadIdx.x == 0)
+            keys_out[(size_t)sv.nq * sv.k] = static_cast<uint32_t>(*sv.err);
+    } else {
+        write_topk(s_keys, q, sv.k, T0, out_d, out_i, sv.Tcap);
     }
-    if (threadIdx.x == 0) {
-        const uint64_t kth = s_keys[sv.k - 1];
-        sv.Tcap[q] = kth != kKeyMax ? unord_f32(static_cast<uint32_t>(kth >> 32)) : T0;
-        atomicAdd(stats, static_cast<unsigned long long>(cnt));
+    if (threadIdx.x == 0) atomicAdd(stats, static_cast<unsigned long long>(cnt));
+}
+
+// ---- shard exchange (cluster-sharded search) -----------------------------------------
+// `recv` holds `world` blocks of `stride` u64 (stride = nq * k + 1), block r = shard r's
+// exchange buffer: k keys per query, then one word (a device error word in the final
+// exchange). One CTA per query; dynamic shared memory: next_pow2(k) keys.
+
+// T1 = min(T0, k-th smallest seed key over every shard) (the single-GPU threshold_kernel
+// over the union of the shards' seeds, which contains the k smallest).
+__global__ void __launch_bounds__(256) gather_threshold_kernel(const uint64_t *__restrict__ recv,
+                                                               int world, size_t stride,
+                                                               SearchView sv) {
+    extern __shared__ uint64_t s_keys[];
+    __shared__ int scratch[256 + 3];
+    const int q = blockIdx.x;
+    const int k = sv.k;
+    auto key_at = [&](uint32_t i) -> uint64_t {
+        const uint32_t r = i / static_cast<uint32_t>(k), j = i - r * static_cast<uint32_t>(k);
+        return recv[r * stride + (size_t)q * k + j];
+    };
+    block_select_smallest(key_at, static_cast<uint32_t>(world * k), k, s_keys, scratch);
+    if (threadIdx.x == 0) sv.T1[q] = threshold_from_kth(s_keys[k - 1], sv.T0[q]);
+}
+
+// Final top-k over every shard's k best keys; ORs every shard's error word into sv.err so
+// that each rank reports a failure on any shard.
+__global__ void __launch_bounds__(256) gather_merge_kernel(const uint64_t *__restrict__ recv,
+                                                           int world, size_t stride,
+                                                           SearchView sv, float *__restrict__ out_d,
+                                                           uint32_t *__restrict__ out_i) {
+    extern __shared__ uint64_t s_keys[];
+    __shared__ int scratch[256 + 3];
+    const int q = blockIdx.x;
+    const int k = sv.k;
+    auto key_at = [&](uint32_t i) -> uint64_t {
+        const uint32_t r = i / static_cast<uint32_t>(k), j = i - r * static_cast<uint32_t>(k);
+        return recv[r * stride + (size_t)q * k + j];
+    };
+    block_select_smallest(key_at, static_cast<uint32_t>(world * k), k, s_keys, scratch);
+    write_topk(s_keys, q, k, sv.T0[q], out_d, out_i, sv.Tcap);
+    if (q == 0 && threadIdx.x == 0) {
+        uint32_t e = 0;
+        for (int r = 0; r < world; ++r) e |= static_cast<uint32_t>(recv[r * stride + stride - 1]);
+        if (e) atomicOr(sv.err, static_cast<int>(e));
     }
 }
 

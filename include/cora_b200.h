@@ -169,6 +169,36 @@ int cora_get_vanguard_mode(const cora_engine *engine);
 /* Candidate capacity per query of the current workspace (array 7 above is nq x cap). */
 uint64_t cora_get_candidate_capacity(const cora_engine *engine);
 
+/* ---- Cluster-sharded search over several GPUs (no counterpart in the reference, which
+ * searches on one GPU). One engine per GPU holds one shard: the clusters that
+ * cora_shard_plan() gives its rank, with every centroid (each shard probes all of them).
+ * A search runs on every shard with the same queries and arguments, in three calls with two
+ * all-gathers in between, done by the caller (e.g. NCCL through torch.distributed) on the
+ * same stream order:
+ *   begin  (queries -> send)      all-gather send -> recv
+ *   resume (recv -> send)         all-gather send -> recv
+ *   end    (recv -> results)
+ * send holds cora_shard_exchange_words(nq, k) u64; recv holds world of them, in rank order.
+ * The first exchange carries each shard's k smallest vanguard seed distances (the global
+ * pruning threshold is the k-th smallest of all), the second each shard's top-k (the result
+ * is the top-k of all) plus its device error word, so that every rank reports a failure on
+ * any shard. Results equal an unsharded search of the whole index, bit for bit. */
+
+/* Longest-processing-time plan over cluster sizes: owner_out[c] = shard of cluster c. */
+int cora_shard_plan(const uint64_t *sizes, uint64_t nlist, uint32_t world, int32_t *owner_out);
+/* Makes the engine load only shard `rank` of `world` (call before loading; world 1 = whole
+ * index). CORA_ESTATE after a load. cora_search / cora_search_device are then rejected. */
+int cora_shard_configure(cora_engine *engine, uint32_t rank, uint32_t world);
+/* out[0..3] = rank, world, vectors held, clusters held. */
+int cora_shard_info(const cora_engine *engine, uint64_t *out4);
+uint64_t cora_shard_exchange_words(uint64_t num_queries, uint64_t topk);
+/* Enqueue on `stream` (NULL: the engine's stream); return without synchronising. */
+int cora_shard_search_begin(cora_engine *engine, const float *d_queries, uint64_t num_queries,
+                            uint64_t topk, uint64_t nprobe, uint64_t *d_send, void *stream);
+int cora_shard_search_resume(cora_engine *engine, const uint64_t *d_recv, uint64_t *d_send);
+int cora_shard_search_end(cora_engine *engine, const uint64_t *d_recv, float *d_final_dists,
+                          uint32_t *d_final_pids);
+
 /* Coarse probing that allocates nothing (no counterpart in the reference). For callers
  * that need a query's probe list where they cannot allocate device memory: e.g. a router
  * choosing the GPU or shard that owns a query's clusters while searches run beside it

@@ -33,6 +33,10 @@ static int cmp_u32(const void *a, const void *b) {
     const uint32_t x = *(const uint32_t *)a, y = *(const uint32_t *)b;
     return (x > y) - (x < y);
 }
+static int cmp_u64(const void *a, const void *b) {
+    const uint64_t x = *(const uint64_t *)a, y = *(const uint64_t *)b;
+    return (x > y) - (x < y);
+}
 
 /* hybrid.cu:436-440 (cuBLAS SGEMM q' = q*P) restated with fp64 accumulation in ascending
  * input-dimension order. fp32*fp32 products are exact in fp64, so a fused or unfused
@@ -236,11 +240,25 @@ static void push(entry_t **v, uint64_t *n, uint64_t *cap, entry_t e) {
     (*v)[(*n)++] = e;
 }
 
-int cora_oracle_search(const cora_oracle_index *ix, const float *q, uint64_t nq, uint64_t k,
+/* k smallest keys of res[] with value < T0, ascending, padded with UINT64_MAX. */
+static void smallest_keys(const entry_t *res, uint64_t nres, float T0, uint64_t k,
+                          uint64_t *out) {
+    uint64_t *tmp = (uint64_t *)malloc((nres ? nres : 1) * sizeof(uint64_t));
+    uint64_t m = 0;
+    for (uint64_t i = 0; i < nres; ++i)
+        if (res[i].value < T0) tmp[m++] = res[i].key;
+    qsort(tmp, m, sizeof(uint64_t), cmp_u64);
+    for (uint64_t i = 0; i < k; ++i) out[i] = i < m ? tmp[i] : UINT64_MAX;
+    free(tmp);
+}
+
+static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq, uint64_t k,
                        uint64_t nprobe, uint64_t vanguard, const float *thresholds0,
                        float *out_dist, uint32_t *out_ids, uint64_t *cand_count,
                        float *thresholds1, int32_t *probe_ids_out, float *probe_g_out,
-                       uint32_t *cand_gids, uint64_t cand_cap, int threads) {
+                       uint32_t *cand_gids, uint64_t cand_cap, int threads,
+                       const float *thresholds1_in, uint64_t *seed_keys_out,
+                       uint64_t *topk_keys_out) {
     if (!ix || !q || !out_dist || !out_ids || k == 0 || k > CORA_ORACLE_VANGUARD_MAX_KEEP ||
         nprobe == 0 || nprobe > ix->nlist ||
         ix->padded_dim % 64 || ix->padded_dim > 4096 || ix->ex_bits != 7)
@@ -304,9 +322,13 @@ int cora_oracle_search(const cora_oracle_index *ix, const float *q, uint64_t nq,
                 push(&res, &nres, &cres, e);
             }
         }
-        /* T1 = k-th smallest seed distance below T0, when at least k exist. */
+        /* T1 = k-th smallest seed distance below T0, when at least k exist (over every
+         * shard's seeds when the caller passes it in). */
+        if (seed_keys_out) smallest_keys(res, nres, T0, k, seed_keys_out + n * k);
         float T1 = T0;
-        {
+        if (thresholds1_in) {
+            T1 = thresholds1_in[n];
+        } else {
             uint64_t nv = 0;
             for (uint64_t i = 0; i < nres; ++i)
                 if (res[i].value < T0) ++nv;
@@ -356,6 +378,7 @@ int cora_oracle_search(const cora_oracle_index *ix, const float *q, uint64_t nq,
         /* Output: ascending (ex, id) among ex < T0, padded with (FLT_MAX, 0)
          * (cpu_refinement.cpp:197-230,269-283). */
         qsort(res, nres, sizeof(entry_t), cmp_entry);
+        if (topk_keys_out) smallest_keys(res, nres, T0, k, topk_keys_out + n * k);
         uint64_t o = 0;
         for (uint64_t i = 0; i < nres && o < k; ++i) {
             if (!(res[i].value < T0)) continue;
@@ -372,4 +395,24 @@ int cora_oracle_search(const cora_oracle_index *ix, const float *q, uint64_t nq,
     }
     free(starts);
     return 0;
+}
+
+int cora_oracle_search(const cora_oracle_index *ix, const float *q, uint64_t nq, uint64_t k,
+                       uint64_t nprobe, uint64_t vanguard, const float *thresholds0,
+                       float *out_dist, uint32_t *out_ids, uint64_t *cand_count,
+                       float *thresholds1, int32_t *probe_ids_out, float *probe_g_out,
+                       uint32_t *cand_gids, uint64_t cand_cap, int threads) {
+    return search_impl(ix, q, nq, k, nprobe, vanguard, thresholds0, out_dist, out_ids,
+                       cand_count, thresholds1, probe_ids_out, probe_g_out, cand_gids, cand_cap,
+                       threads, NULL, NULL, NULL);
+}
+
+int cora_oracle_search_shard(const cora_oracle_index *ix, const float *q, uint64_t nq,
+                             uint64_t k, uint64_t nprobe, uint64_t vanguard,
+                             const float *thresholds0, const float *thresholds1_in,
+                             uint64_t *seed_keys_out, uint64_t *topk_keys_out, float *out_dist,
+                             uint32_t *out_ids, uint64_t *cand_count, int threads) {
+    return search_impl(ix, q, nq, k, nprobe, vanguard, thresholds0, out_dist, out_ids,
+                       cand_count, NULL, NULL, NULL, NULL, 0, threads, thresholds1_in,
+                       seed_keys_out, topk_keys_out);
 }

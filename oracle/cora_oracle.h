@@ -90,6 +90,22 @@ int cora_oracle_search(const cora_oracle_index *ix, const float *q, uint64_t nq,
                        float *thresholds1, int32_t *probe_ids, float *probe_g,
                        uint32_t *cand_gids, uint64_t cand_cap, int threads);
 
+/* One shard's part of a cluster-sharded search (the index holds only the shard's clusters;
+ * the others have size 0). Same as cora_oracle_search, plus:
+ *   seed_keys_out  [nq x k] (NULL to skip): the shard's k smallest seed keys
+ *                  (ord(ex) << 32 | id) with ex < T0, ascending, padded with UINT64_MAX;
+ *   thresholds1_in [nq]     (NULL: computed from the shard's own seeds): the threshold of
+ *                  the main pass, i.e. min(T0, k-th smallest key over every shard's
+ *                  seed_keys_out) when at least k exist, else T0;
+ *   topk_keys_out  [nq x k] (NULL to skip): the shard's top-k keys, padded as above.
+ * Merging the shards' topk_keys_out (k smallest of the union) gives cora_oracle_search's
+ * result on the whole index. */
+int cora_oracle_search_shard(const cora_oracle_index *ix, const float *q, uint64_t nq,
+                             uint64_t k, uint64_t nprobe, uint64_t vanguard,
+                             const float *thresholds0, const float *thresholds1_in,
+                             uint64_t *seed_keys_out, uint64_t *topk_keys_out, float *out_dist,
+                             uint32_t *out_ids, uint64_t *cand_count, int threads);
+
 #ifdef __cplusplus
 }
 #endif

@@ -150,6 +150,11 @@ def lib():
                                          C.c_uint64, C.c_uint64, C.c_void_p, _f32p, _u32p,
                                          C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_void_p, C.c_uint64, C.c_int]
+        L.cora_oracle_search_shard.restype = C.c_int
+        L.cora_oracle_search_shard.argtypes = [C.POINTER(_Index), _f32p, C.c_uint64,
+                                               C.c_uint64, C.c_uint64, C.c_uint64, C.c_void_p,
+                                               C.c_void_p, C.c_void_p, C.c_void_p, _f32p, _u32p,
+                                               C.c_void_p, C.c_int]
         L.cora_oracle_rotate.argtypes = [C.POINTER(_Index), _f32p, C.c_uint64, _f32p]
         L.cora_oracle_query_prep.argtypes = [C.c_uint64, C.c_uint64, _f32p, C.c_uint64, _f32p,
                                              _f32p, _f32p, _f32p, _i32p, _u32p]
@@ -212,6 +217,26 @@ class OracleIndex:
             return dist, ids
         return dict(dist=dist, ids=ids, cand_count=cnt, thresholds1=t1, probe_ids=pids,
                     probe_g=pg, cand_gids=cg)
+
+    def search_shard(self, q, k, nprobe, vanguard=5, thresholds=None, thresholds1=None,
+                     threads=None):
+        """One shard's part of a sharded search (cora_oracle_search_shard): returns
+        (seed_keys, topk_keys, dist, ids), keys as uint64 (nq, k) padded with UINT64_MAX."""
+        q = np.ascontiguousarray(q, np.float32)
+        nq = q.shape[0]
+        seeds = np.empty((nq, k), np.uint64)
+        topk = np.empty((nq, k), np.uint64)
+        dist = np.empty((nq, k), np.float32)
+        ids = np.empty((nq, k), np.uint32)
+        t0 = None if thresholds is None else np.ascontiguousarray(thresholds, np.float32)
+        t1 = None if thresholds1 is None else np.ascontiguousarray(thresholds1, np.float32)
+        threads = threads or min(8, os.cpu_count() or 1)
+        rc = lib().cora_oracle_search_shard(C.byref(self.c), q, nq, k, nprobe, vanguard,
+                                            _ptr(t0), _ptr(t1), _ptr(seeds), _ptr(topk), dist,
+                                            ids, None, threads)
+        if rc != 0:
+            raise ValueError("oracle rejected the search arguments")
+        return seeds, topk, dist, ids
 
     def rotate(self, q):
         q = np.ascontiguousarray(q, np.float32)
@@ -389,3 +414,66 @@ def distance_recall(base, queries, gt_ids, results, k):
             if x in truth or ((b[x] - q) ** 2).sum() <= kth:
                 hits += 1
     return hits / (len(queries) * k)
+
+
+# --------------------------------------------------------------------------------------
+# Cluster-sharded search on the CPU: one shard's oracle behind the begin / resume / end
+# protocol of coraanns_b200.shard.run_sharded_search, exchanging through torch CPU tensors
+# (gloo). The threshold and merge steps restate gather_threshold_kernel and
+# gather_merge_kernel in numpy.
+# --------------------------------------------------------------------------------------
+_KEY_MAX = np.uint64(0xFFFFFFFFFFFFFFFF)
+
+
+def unord_f32(o):
+    """Inverse of the key's order-preserving float map (ord_f32)."""
+    o = np.asarray(o, np.uint32)
+    u = np.where(o & np.uint32(0x80000000), o & np.uint32(0x7FFFFFFF), ~o).astype(np.uint32)
+    return u.view(np.float32)
+
+
+def smallest_keys_per_query(recv, world, nq, k):
+    """(nq, k) smallest keys of every shard's block in an all-gathered buffer."""
+    stride = nq * k + 1
+    blocks = np.asarray(recv).view(np.uint64).reshape(world, stride)[:, :nq * k]
+    allk = blocks.reshape(world, nq, k).transpose(1, 0, 2).reshape(nq, world * k)
+    return np.sort(allk, axis=1)[:, :k]
+
+
+class OracleShard:
+    def __init__(self, sd_shard: dict, world: int, vanguard=5, thresholds=None, threads=None):
+        self.o = OracleIndex(sd_shard)
+        self.world, self.vanguard, self.T0, self.threads = world, vanguard, thresholds, threads
+
+    def buffers(self, nq, k):
+        import torch
+        w = nq * k + 1
+        return torch.zeros(w, dtype=torch.int64), torch.zeros(self.world * w, dtype=torch.int64)
+
+    def begin(self, q, nq, k, nprobe, send):
+        self.args = (np.asarray(q, np.float32), nq, k, nprobe)
+        seeds, _, _, _ = self.o.search_shard(self.args[0], k, nprobe, self.vanguard, self.T0,
+                                             threads=self.threads)
+        send.numpy().view(np.uint64)[:nq * k] = seeds.ravel()
+
+    def resume(self, recv, send):
+        q, nq, k, nprobe = self.args
+        kth = smallest_keys_per_query(recv.numpy(), self.world, nq, k)[:, k - 1]
+        T0 = np.full(nq, np.finfo(np.float32).max, np.float32) if self.T0 is None else \
+            np.asarray(self.T0, np.float32)
+        T1 = np.where(kth == _KEY_MAX, T0,
+                      np.minimum(T0, unord_f32((kth >> np.uint64(32)).astype(np.uint32))))
+        self.T1 = T1.astype(np.float32)
+        _, topk, _, _ = self.o.search_shard(q, k, nprobe, self.vanguard, self.T0, self.T1,
+                                            threads=self.threads)
+        buf = send.numpy().view(np.uint64)
+        buf[:nq * k] = topk.ravel()
+        buf[nq * k] = 0
+
+    def end(self, recv, out_d, out_i):
+        _, nq, k, _ = self.args
+        keys = smallest_keys_per_query(recv.numpy(), self.world, nq, k)
+        ok = keys != _KEY_MAX
+        out_d[...] = np.where(ok, unord_f32((keys >> np.uint64(32)).astype(np.uint32)),
+                              np.finfo(np.float32).max)
+        out_i[...] = np.where(ok, (keys & np.uint64(0xFFFFFFFF)).astype(np.uint32), 0)

@@ -1,0 +1,191 @@
+"""Cluster-sharded search on the GPU: the shard kernels and the exchange protocol.
+
+On one GPU, `world` sharded engines of one index run in one process and exchange through
+device copies (the all-gather a multi-GPU run does with NCCL): the merged result must equal
+the oracle's committed result, and the unsharded engine's, bit for bit. With two or more
+GPUs, two torch.distributed ranks over NCCL run the same check through ShardedIndex.
+"""
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def cb():
+    import coraanns_b200
+    return coraanns_b200
+
+
+class LocalShards:
+    """`world` shard engines of one index on this GPU, exchanging by device copies."""
+
+    def __init__(self, cb, load, world, nq, k, nprobe, vanguard=5, lows=True):
+        self.engines = []
+        for r in range(world):
+            e = cb.HybridIndex(0)
+            e.shard_configure(r, world)
+            e.set_vanguard_size(vanguard)
+            if not lows:
+                e.set_vanguard_lows_budget(0)
+            load(e)
+            e.prepare_workspace(nq, k, nprobe)
+            self.engines.append(e)
+
+    def search(self, q, k, nprobe):
+        import torch
+        from coraanns_b200.shard import exchange_words
+        nq, world = q.shape[0], len(self.engines)
+        w = exchange_words(nq, k)
+        st = torch.cuda.Stream()
+        with torch.cuda.stream(st):
+            dq = torch.from_numpy(np.ascontiguousarray(q)).cuda()
+            sends = [torch.empty(w, dtype=torch.int64, device="cuda") for _ in range(world)]
+            recv = torch.empty(world * w, dtype=torch.int64, device="cuda")
+            outs = [(torch.empty((nq, k), dtype=torch.float32, device="cuda"),
+                     torch.empty((nq, k), dtype=torch.int32, device="cuda")) for _ in range(world)]
+            for e, s in zip(self.engines, sends):
+                e.shard_search_begin(dq.data_ptr(), nq, k, nprobe, s.data_ptr(), st.cuda_stream)
+            torch.cat(sends, out=recv)
+            for e, s in zip(self.engines, sends):
+                e.shard_search_resume(recv.data_ptr(), s.data_ptr())
+            torch.cat(sends, out=recv)
+            for e, (d, i) in zip(self.engines, outs):
+                e.shard_search_end(recv.data_ptr(), d.data_ptr(), i.data_ptr())
+        st.synchronize()
+        for e in self.engines:
+            e.check_device()
+        return [(d.cpu().numpy(), i.cpu().numpy().view(np.uint32)) for d, i in outs]
+
+    def close(self):
+        for e in self.engines:
+            e.close()
+
+
+CASES = [("demo", 10, 8, 5), ("demo", 50, 8, 2), ("demo", 10, 16, 0), ("d96", 100, 8, 5),
+         ("d200", 10, 8, 2), ("d150", 20, 8, 1)]
+
+
+@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("lows", [True, False])
+@pytest.mark.parametrize("name,k,nprobe,van", CASES)
+def test_local_shards_match_oracle(cb, name, k, nprobe, van, world, lows):
+    z = np.load(GOLDEN / f"{name}.npz")
+    q = z["queries"]
+    path = str(GOLDEN / f"{name}.index")
+    ls = LocalShards(cb, lambda e: e.load_index_file(path), world, len(q), k, nprobe, van, lows)
+    outs = ls.search(q, k, nprobe)
+    want_d, want_i = z[f"dist_k{k}_np{nprobe}_v{van}"], z[f"ids_k{k}_np{nprobe}_v{van}"]
+    for d, i in outs:
+        assert np.array_equal(i, want_i)
+        assert d.tobytes() == want_d.tobytes()
+    # every shard applied the global threshold; the shards' candidates add up to the
+    # unsharded candidate count (each candidate lives on exactly one shard)
+    t1 = [e.debug("thresholds1", len(q)) for e in ls.engines]
+    for t in t1:
+        assert t.tobytes() == z[f"t1_k{k}_np{nprobe}_v{van}"].tobytes()
+    cand = sum(e.debug("cand_count", len(q)).astype(np.int64) for e in ls.engines)
+    assert np.array_equal(cand, z[f"cand_k{k}_np{nprobe}_v{van}"].astype(np.int64))
+    info = [e.shard_info() for e in ls.engines]
+    assert sum(x["clusters"] for x in info) == int(z["meta"][2])
+    ls.close()
+
+
+def test_local_shards_synthetic_match_unsharded(cb):
+    """World 4 over a larger index (heavier clusters, several tiles per cluster)."""
+    from coraanns_b200 import builder
+    rng = np.random.default_rng(17)
+    n, dim, nlist, nq, k, nprobe = 200_000, 96, 256, 512, 10, 16
+    centres = rng.normal(size=(nlist, dim)).astype(np.float32)
+    lab = rng.integers(0, nlist, n)
+    data = (centres[lab] + 0.25 * rng.normal(size=(n, dim))).astype(np.float32)
+    q = (centres[rng.integers(0, nlist, nq)] + 0.25 * rng.normal(size=(nq, dim))).astype(np.float32)
+    sd = builder.build_index(data, centres, lab, seed=17)
+    full = cb.HybridIndex(0)
+    full.load_search_data(sd)
+    full.prepare_workspace(nq, k, nprobe)
+    full.reset_buffer(q)
+    want_d, want_i = full.search(q, k, nprobe)
+    full.close()
+    ls = LocalShards(cb, lambda e: e.load_search_data(sd), 4, nq, k, nprobe)
+    for d, i in ls.search(q, k, nprobe):
+        assert np.array_equal(i, want_i) and d.tobytes() == want_d.tobytes()
+    ls.close()
+
+
+def test_sharded_engine_rules(cb):
+    path = str(GOLDEN / "demo.index")
+    e = cb.HybridIndex(0)
+    with pytest.raises(cb.InvalidArgument):
+        e.shard_configure(2, 2)
+    e.shard_configure(1, 2)
+    e.load_index_file(path)
+    with pytest.raises(cb.LogicError):
+        e.shard_configure(0, 2)  # after loading
+    e.prepare_workspace(8, 10, 4)
+    q = np.load(GOLDEN / "demo.npz")["queries"][:8]
+    with pytest.raises(cb.LogicError, match="shard"):
+        e.search(q, 10, 4)  # a shard alone cannot answer
+    with pytest.raises(cb.LogicError):
+        e.shard_search_resume(1, 1)  # before begin
+    info = e.shard_info()
+    assert info["rank"] == 1 and info["world"] == 2 and 0 < info["vectors"] < 4096
+    e.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, out_q):
+    import sys
+    root = GOLDEN.parent.parent
+    sys.path[:0] = [str(root / "cgcl-coraanns_b200"), str(root / "tests")]
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from coraanns_b200.shard import ShardedIndex
+        z = np.load(GOLDEN / "d96.npz")
+        q = z["queries"]
+        ix = ShardedIndex(rank)
+        ix.load_index_file(str(GOLDEN / "d96.index"))
+        ix.prepare_workspace(len(q), 100, 8)
+        d, i = ix.search(q, 100, 8)
+        ok = np.array_equal(i, z["ids_k100_np8_v5"]) and d.tobytes() == z["dist_k100_np8_v5"].tobytes()
+        ix.close()
+        out_q.put((rank, ok))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_over_nccl():
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get() for _ in range(2))
+    for p in procs:
+        p.join(timeout=180)
+        assert p.exitcode == 0
+    assert res == [(0, True), (1, True)]
