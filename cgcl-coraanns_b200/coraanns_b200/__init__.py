@@ -41,6 +41,7 @@ EXPORTS = [
     "cora_debug_copy", "cora_get_last_stage_ms", "cora_stage_totals", "cora_stage_reset",
     "cora_set_vanguard_lows_budget", "cora_set_tuning", "cora_get_vanguard_mode",
     "cora_get_candidate_capacity", "cora_probe_noalloc", "cora_probe_noalloc_scratch_limit",
+    "cora_probe_noalloc_status",
     "cora_shard_plan", "cora_shard_configure", "cora_shard_info", "cora_shard_exchange_words",
     "cora_shard_search_begin", "cora_shard_search_resume", "cora_shard_search_end",
 ]
@@ -93,6 +94,7 @@ _sig("cora_get_vanguard_mode", C.c_int, _p)
 _sig("cora_set_tuning", C.c_int, _p, C.c_char_p, C.c_int64)
 _sig("cora_probe_noalloc", C.c_int, _p, _p, _u64, _u64, _p, _p, _p)
 _sig("cora_probe_noalloc_scratch_limit", _u64)
+_sig("cora_probe_noalloc_status", C.c_int, _p, _p)
 _sig("cora_shard_plan", C.c_int, _p, _u64, C.c_uint32, _p)
 _sig("cora_shard_configure", C.c_int, _p, C.c_uint32, C.c_uint32)
 _sig("cora_shard_info", C.c_int, _p, _p)
@@ -233,6 +235,10 @@ class HybridIndex:
                                        C.c_void_p(d_probe_ids), C.c_void_p(d_probe_dists),
                                        C.c_void_p(stream) if stream else None))
 
+    def probe_noalloc_status(self, stream: int = 0):
+        """Synchronise and raise if the last probe_noalloc failed on the device."""
+        _check(_lib.cora_probe_noalloc_status(self._h, C.c_void_p(stream) if stream else None))
+
     # ---- cluster sharding (see coraanns_b200.shard) ----
     def shard_configure(self, rank: int, world: int):
         _check(_lib.cora_shard_configure(self._h, rank, world))
@@ -339,6 +345,7 @@ class HybridIndex:
             "planes": (5, np.uint32, (nq, 8, W4)),
             "scalars": (6, np.float32, (nq, 4)),
             "cand_gids": (7, np.uint32, (nq, self.candidate_capacity())),
+            "approx": (8, np.float32, (nq, (info["nlist"] + 3) // 4 * 4)),
         }[what]
         out = np.empty(spec[2], spec[1])
         _check(_lib.cora_debug_copy(self._h, spec[0], _ptr(out), out.nbytes))

@@ -19,6 +19,7 @@
 
 #include "../../include/cora_b200.h"
 #include "common.cuh"
+#include "kernels_probe.cuh"
 #include "kernels_query.cuh"
 #include "kernels_refine.cuh"
 #include "kernels_scan.cuh"
@@ -96,6 +97,68 @@ struct ScanLaunch {
     int num_sms;
     cudaStream_t st;
 };
+
+// ---- tensor maps for the probe GEMM (driver entry point, no libcuda link) ----------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_tiled() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    if (!fn) fail(CORA_ECUDA, "the driver does not provide cuTensorMapEncodeTiled");
+    return fn;
+}
+
+// 2-D fp32 tensor map over `rows` rows of `cols` floats, `ld` floats apart (ld % 4 == 0,
+// 16-byte aligned base); box of box_cols x box_rows with 128-byte swizzle (box_cols * 4 <=
+// 128); reads past the edges return zeros, stores past them are dropped.
+inline CUtensorMap map_f32_2d(const float *base, uint64_t cols, uint64_t rows, uint64_t ld,
+                              uint32_t box_cols, uint32_t box_rows) {
+    CUtensorMap m;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {ld * 4};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = encode_tiled()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                                      const_cast<float *>(base), dims, strides, box, estr,
+                                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        fail(CORA_ECUDA, "cuTensorMapEncodeTiled failed with status " + std::to_string(int(r)));
+    return m;
+}
+
+inline uint64_t approx_ld(uint64_t nlist) { return (nlist + 3) & ~uint64_t(3); }
+
+// approx[q * ld + c] = ||q'||^2 + ||c||^2 - 2 <q', c> for every query and centroid, on the
+// tensor cores (probe_gemm_kernel; persistent, one CTA per SM at most).
+inline void launch_probe_gemm(const float *qr, const float *qnorm2, uint64_t nq, uint64_t D,
+                              const float *cent, const float *cnorm2, uint64_t nlist,
+                              float *approx, int num_sms, cudaStream_t st, int *err) {
+    const CUtensorMap tq = map_f32_2d(qr, D, nq, D, kPgBK, kPgBM);
+    const CUtensorMap tc = map_f32_2d(cent, D, nlist, D, kPgBK, kPgBN);
+    const CUtensorMap to = map_f32_2d(approx, nlist, nq, approx_ld(nlist), 32, kPgBM);
+    const size_t sm = probe_gemm_smem();
+    CUDA_TRY(cudaFuncSetAttribute(probe_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)sm));
+    const uint64_t tiles = ((nq + kPgBM - 1) / kPgBM) * ((nlist + kPgBN - 1) / kPgBN);
+    const unsigned grid = static_cast<unsigned>(std::min<uint64_t>(tiles, (uint64_t)num_sms));
+    probe_gemm_kernel<<<grid, kPgThreads, sm, st>>>(tq, tc, to, qnorm2, cnorm2,
+                                                    static_cast<int>(nq), static_cast<int>(nlist),
+                                                    static_cast<int>(D), err);
+    CUDA_TRY(cudaGetLastError());
+}
 
 // Cluster-to-shard plan: longest-processing-time greedy on cluster sizes (every vector of an
 // index costs the same bytes), largest cluster first (ties: lower cluster id) onto the least
@@ -371,7 +434,7 @@ struct Engine {
         qr.alloc(max_q * D);
         scal.alloc(max_q);
         planes.alloc(max_q * 8 * W4);
-        gmat.alloc(max_q * nlist);
+        gmat.alloc(max_q * approx_ld(nlist));
         qnorm2.alloc(max_q);
         probe_ids.alloc(max_q * max_np);
         probe_g.alloc(max_q * max_np);
@@ -727,21 +790,17 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
     // 2. coarse probing: approximate distances for every (query, centroid), then the exact
     //    top-nprobe among the guarded candidates
     {
-        dim3 grid(static_cast<unsigned>((nlist + kDistTile - 1) / kDistTile),
-                  static_cast<unsigned>((nq + kDistTile - 1) / kDistTile));
-        approx_dist_f32_kernel<<<grid, 256, 0, st>>>(qr.p, qnorm2.p, inq, centroids.p, cnorm2.p,
-                                                     static_cast<int>(nlist), static_cast<int>(D),
-                                                     gmat.p);
-        CUDA_TRY(cudaGetLastError());
+        launch_probe_gemm(qr.p, qnorm2.p, nq, D, centroids.p, cnorm2.p, nlist, gmat.p, num_sms,
+                          st, err.p);
         mark(2, st);
         const int ccap = guarded_select_cap(inp);
         const size_t sm = guarded_select_smem(inp, ccap, static_cast<int>(D));
         CUDA_TRY(cudaFuncSetAttribute(guarded_select_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        guarded_select_kernel<<<inq, 256, sm, st>>>(gmat.p, static_cast<int>(nlist), inp, ccap, qr.p,
-                                                    qnorm2.p, centroids.p, cmax,
-                                                    static_cast<int>(D), kApproxEpsF32,
-                                                    probe_ids.p, probe_g.p);
+        guarded_select_kernel<<<inq, 256, sm, st>>>(gmat.p, static_cast<int>(nlist),
+                                                    approx_ld(nlist), inp, ccap, qr.p, qnorm2.p,
+                                                    centroids.p, cmax, static_cast<int>(D),
+                                                    kApproxEpsTF32, probe_ids.p, probe_g.p);
         CUDA_TRY(cudaGetLastError());
     }
     mark(3, st);
@@ -906,6 +965,7 @@ void Engine::debug_copy(int what, void *out, uint64_t bytes) {
         case 4: copy(T1.p, nq * 4); break;
         case 5: copy(planes.p, nq * 8 * W4 * 4); break;
         case 6: copy(scal.p, nq * 16); break;
+        case 8: copy(gmat.p, nq * approx_ld(nlist) * 4); break;
         case 7: {
             if (bytes != nq * cap * 4) fail(CORA_EINVAL, "debug_copy: byte count does not match");
             std::vector<uint64_t> rec(nq * cap);
@@ -1414,17 +1474,18 @@ unsigned char *g_noalloc_ptr[kNoallocMaxDevices] = {};
 inline size_t align256(size_t b) { return (b + 255) & ~size_t{255}; }
 
 struct NoallocLayout {
-    size_t qr, qnorm2, scal, planes, approx, total;
+    size_t status, qr, qnorm2, scal, planes, approx, total;
 };
 
 NoallocLayout noalloc_layout(uint64_t nq, uint64_t D, uint64_t W4, uint64_t nlist) {
     NoallocLayout l{};
-    l.qr = 0;
+    l.status = 0;  // device error word of the last call (zeroed by each call)
+    l.qr = 256;
     l.qnorm2 = l.qr + align256(nq * D * sizeof(float));
     l.scal = l.qnorm2 + align256(nq * sizeof(float));
     l.planes = l.scal + align256(nq * sizeof(QueryScalars));
     l.approx = l.planes + align256(nq * 8 * W4 * sizeof(uint32_t));
-    l.total = l.approx + align256(nq * nlist * sizeof(float));
+    l.total = l.approx + align256(nq * approx_ld(nlist) * sizeof(float));
     return l;
 }
 
@@ -1474,8 +1535,10 @@ int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num
         auto *scal = reinterpret_cast<cora::QueryScalars *>(s + l.scal);
         uint32_t *planes = reinterpret_cast<uint32_t *>(s + l.planes);
         float *approx = reinterpret_cast<float *>(s + l.approx);
+        int *status = reinterpret_cast<int *>(s + l.status);
         cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e.stream;
         const int inq = static_cast<int>(num_queries), inp = static_cast<int>(nprobe);
+        CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), st));
 
         const size_t rsm = (size_t)cora::kRotQueries * (e.dim + e.D) * 4;
         CUDA_TRY(cudaFuncSetAttribute(cora::rotate_prep_kernel,
@@ -1487,20 +1550,31 @@ int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num
                                                    static_cast<int>(e.D), e.W4, e.rotator.p, c_b,
                                                    qr, scal, planes, qnorm2);
         CUDA_TRY(cudaGetLastError());
-        dim3 grid(static_cast<unsigned>((e.nlist + cora::kDistTile - 1) / cora::kDistTile),
-                  static_cast<unsigned>((num_queries + cora::kDistTile - 1) / cora::kDistTile));
-        cora::approx_dist_f32_kernel<<<grid, 256, 0, st>>>(qr, qnorm2, inq, e.centroids.p,
-                                                           e.cnorm2.p, static_cast<int>(e.nlist),
-                                                           static_cast<int>(e.D), approx);
-        CUDA_TRY(cudaGetLastError());
+        cora::launch_probe_gemm(qr, qnorm2, num_queries, e.D, e.centroids.p, e.cnorm2.p, e.nlist,
+                                approx, e.num_sms, st, status);
         const int ccap = cora::guarded_select_cap(inp);
         const size_t gsm = cora::guarded_select_smem(inp, ccap, static_cast<int>(e.D));
         CUDA_TRY(cudaFuncSetAttribute(cora::guarded_select_kernel,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm));
         cora::guarded_select_kernel<<<inq, 256, gsm, st>>>(
-            approx, static_cast<int>(e.nlist), inp, ccap, qr, qnorm2, e.centroids.p, e.cmax,
-            static_cast<int>(e.D), cora::kApproxEpsF32, d_probe_ids, d_probe_dists);
+            approx, static_cast<int>(e.nlist), cora::approx_ld(e.nlist), inp, ccap, qr, qnorm2,
+            e.centroids.p, e.cmax, static_cast<int>(e.D), cora::kApproxEpsTF32, d_probe_ids,
+            d_probe_dists);
         CUDA_TRY(cudaGetLastError());
+    });
+}
+
+int cora_probe_noalloc_status(cora_engine *engine, void *stream) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        CUDA_TRY(cudaSetDevice(e.device));
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e.stream;
+        unsigned char *s = cora::noalloc_scratch(e.device);
+        int h = 0;
+        CUDA_TRY(cudaMemcpyAsync(&h, s, sizeof(int), cudaMemcpyDeviceToHost, st));
+        CUDA_TRY(cudaStreamSynchronize(st));
+        if (h & cora::kDevWaitTimeout) cora::fail(CORA_ERUNTIME, "a device-side wait timed out");
+        if (h) cora::fail(CORA_ERUNTIME, "device reported an error");
     });
 }
 

@@ -118,63 +118,8 @@ __device__ __forceinline__ float exact_centroid_dist(const float *__restrict__ x
     return (float)acc;
 }
 
-// Approximate coarse distances on CUDA cores (fp32): approx(q, c) = ||q'||^2 + ||c||^2 -
-// 2 <q', c>, 64 x 64 output tile per CTA, 256 threads with 4 x 4 outputs each. Its error
-// bound is kApproxEpsF32 (see guarded_select_kernel).
-constexpr int kDistTile = 64, kDistK = 32;
-__global__ void __launch_bounds__(256) approx_dist_f32_kernel(
-    const float *__restrict__ qr, const float *__restrict__ qnorm2, int nq,
-    const float *__restrict__ cent, const float *__restrict__ cnorm2, int nlist, int D,
-    float *__restrict__ out) {
-    __shared__ float sq[kDistK][kDistTile + 1];
-    __shared__ float sc[kDistK][kDistTile + 1];
-    const int qbase = blockIdx.y * kDistTile, cbase = blockIdx.x * kDistTile;
-    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
-    float acc[4][4];
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
-    for (int k0 = 0; k0 < D; k0 += kDistK) {
-        for (int i = threadIdx.x; i < kDistK * kDistTile; i += blockDim.x) {
-            const int row = i / kDistK, kk = i % kDistK;
-            const int qi = qbase + row, ci = cbase + row;
-            sq[kk][row] = qi < nq ? qr[(size_t)qi * D + k0 + kk] : 0.0f;
-            sc[kk][row] = ci < nlist ? cent[(size_t)ci * D + k0 + kk] : 0.0f;
-        }
-        __syncthreads();
-#pragma unroll 8
-        for (int kk = 0; kk < kDistK; ++kk) {
-            float qv[4], cv[4];
-#pragma unroll
-            for (int a = 0; a < 4; ++a) qv[a] = sq[kk][ty * 4 + a];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) cv[b] = sc[kk][tx * 4 + b];
-#pragma unroll
-            for (int a = 0; a < 4; ++a)
-#pragma unroll
-                for (int b = 0; b < 4; ++b) acc[a][b] = fmaf(qv[a], cv[b], acc[a][b]);
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int a = 0; a < 4; ++a) {
-        const int qi = qbase + ty * 4 + a;
-        if (qi >= nq) continue;
-#pragma unroll
-        for (int b = 0; b < 4; ++b) {
-            const int ci = cbase + tx * 4 + b;
-            if (ci < nlist)
-                out[(size_t)qi * nlist + ci] = (qnorm2[qi] + cnorm2[ci]) - 2.0f * acc[a][b];
-        }
-    }
-}
-
-// Error bounds |approx - g| <= eps * (||q'|| + max ||c||)^2 of the approximate distance
-// kernels, with slack. fp32 (u = 2^-24, D <= 1024 accumulation terms): the dot product is
-// within gamma_D * ||q'|| ||c||, the norms within gamma_D of theirs, the two final additions
-// and g's own rounding add a few u; 2 * (2 gamma_1032 + 9 u) < 2^-11.
-constexpr double kApproxEpsF32 = 1.0 / 2048.0;
+// The approximate distances come from probe_gemm_kernel (tensor cores, kernels_probe.cuh),
+// with |approx - g| <= kApproxEpsTF32 * (||q'|| + max ||c||)^2.
 
 // One CTA per query: the nprobe probes of the contract (smallest exact g, ties by cluster
 // id) from approximate distances. tau = nprobe-th smallest approx; every exact top-nprobe
@@ -183,9 +128,9 @@ constexpr double kApproxEpsF32 = 1.0 / 2048.0;
 // pathological tie band) fall back to exact distances for every centroid of the query,
 // written over its approximate row. Dynamic shared memory: see guarded_select_smem().
 __global__ void __launch_bounds__(256) guarded_select_kernel(
-    float *__restrict__ approx, int nlist, int nprobe, int cand_cap, const float *__restrict__ qr,
-    const float *__restrict__ qnorm2, const float *__restrict__ cent, float cmax, int D,
-    double eps, int *__restrict__ probe_ids, float *__restrict__ probe_g) {
+    float *__restrict__ approx, int nlist, size_t ld, int nprobe, int cand_cap,
+    const float *__restrict__ qr, const float *__restrict__ qnorm2, const float *__restrict__ cent,
+    float cmax, int D, double eps, int *__restrict__ probe_ids, float *__restrict__ probe_g) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int S2 = next_pow2(nprobe);
     uint64_t *sel = reinterpret_cast<uint64_t *>(smem_raw);          // S2
@@ -195,7 +140,7 @@ __global__ void __launch_bounds__(256) guarded_select_kernel(
     __shared__ int scratch[256 + 3];
     __shared__ int s_ncand;
     const int q = blockIdx.x;
-    float *row = approx + (size_t)q * nlist;
+    float *row = approx + (size_t)q * ld;  // ld: row stride (nlist rounded up to 4 floats)
     for (int j = threadIdx.x; j < D; j += blockDim.x) x[j] = qr[(size_t)q * D + j];
     if (threadIdx.x == 0) s_ncand = 0;
     auto approx_key = [&](uint32_t c) -> uint64_t { return make_key(row[c], c); };

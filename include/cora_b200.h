@@ -137,7 +137,9 @@ float cora_get_last_gpu_filter_ms(const cora_engine *engine);
  * (nq x nprobe i32), 2 probe distances (nq x nprobe f32), 3 per-query candidate counts
  * (nq u32), 4 thresholds after seeding (nq f32), 5 query bit-planes
  * (nq x 8 x W4 u32, W4 = 4 * ceil(D / 128)), 6 query scalars (nq x {width, k1, kb, sumq}),
- * 7 candidate gids (nq x cap u32, per query sorted ascending, unused slots 0xFFFFFFFF).
+ * 7 candidate gids (nq x cap u32, per query sorted ascending, unused slots 0xFFFFFFFF),
+ * 8 approximate coarse distances of the tensor-core probe GEMM (nq x ld f32, ld = nlist
+ * rounded up to a multiple of 4; rows the exact fallback recomputed hold exact values).
  * `bytes` must equal the size of the requested array. */
 int cora_debug_copy(cora_engine *engine, int what, void *h_out, uint64_t bytes);
 /* Per-stage device times (ms) of the last search run with profiling enabled, from CUDA
@@ -219,6 +221,9 @@ int cora_shard_search_end(cora_engine *engine, const uint64_t *d_recv, float *d_
 int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num_queries,
                        uint64_t nprobe, int32_t *d_probe_ids, float *d_probe_dists, void *stream);
 uint64_t cora_probe_noalloc_scratch_limit(void);
+/* Synchronises `stream` and reports a device-side failure of the last cora_probe_noalloc
+ * on this device (a bounded wait in the tensor-core kernel that expired): CORA_ERUNTIME. */
+int cora_probe_noalloc_status(cora_engine *engine, void *stream);
 
 #ifdef __cplusplus
 }

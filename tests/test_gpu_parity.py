@@ -124,6 +124,33 @@ def test_live_oracle_parity_larger(cb, n, dim, nlist, nq, k, nprobe, van, mode):
     e.close()
 
 
+@pytest.mark.parametrize("n,dim,nlist,nq", [
+    (60_000, 96, 998, 300),    # ld = 1000, ragged row and column tiles
+    (40_000, 768, 300, 131),   # 24 K chunks
+    (20_000, 64, 16, 5),       # one tile, mostly out of bounds
+])
+def test_probe_gemm_error_within_guard(cb, n, dim, nlist, nq):
+    """The tensor-core approximate distances stay inside the error bound the guarded
+    selection assumes (|approx - exact| <= eps * (|q'| + max |c|)^2, eps = 2^-9), and the
+    probe lists and distances equal the oracle's exact selection bit for bit."""
+    sd, q = _synthetic(n, dim, nlist, nq, seed=nlist + dim)
+    nprobe = min(8, nlist)
+    e = _engine(cb, sd=sd, nq=nq, k=10, nprobe=nprobe)
+    e.reset_buffer(q)
+    e.search(q, 10, nprobe)
+    approx = e.debug("approx", nq)[:, :nlist].astype(np.float64)
+    qr = e.debug("rotated", nq).astype(np.float64)
+    cent = np.asarray(sd["centroids"], np.float64)
+    exact = ((qr[:, None, :] - cent[None, :, :]) ** 2).sum(2)
+    r = np.sqrt((qr ** 2).sum(1))[:, None] + np.sqrt((cent ** 2).sum(1)).max()
+    ratio = np.abs(approx - exact) / r ** 2
+    assert ratio.max() <= 2.0 ** -9, ratio.max()
+    ref = po.OracleIndex(sd).search(q, 10, nprobe, with_details=True)
+    assert np.array_equal(e.debug("probe_ids", nq, nprobe), ref["probe_ids"])
+    assert e.debug("probe_g", nq, nprobe).tobytes() == ref["probe_g"].tobytes()
+    e.close()
+
+
 def test_probe_ties_take_the_exact_fallback(cb):
     """Every centroid equidistant from every query: the guarded selection's candidate band
     holds all 2048 centroids (more than its buffer), so the exact path over every centroid
