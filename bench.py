@@ -451,9 +451,15 @@ def main():
                          "of codes touched; cross-query reuse lets this exceed the physical DRAM "
                          "traffic)")
     mode = eng.get_vanguard_mode()
-    # kernels per search: 21 with stored vanguard lows, 13 rescanning; +2 exchange steps
-    # (gather_threshold_kernel, gather_merge_kernel) when sharded
-    launches = ((21 if mode == 1 else 13) + (2 if world > 1 else 0)) * args.steps
+    # Kernels per search: rotation, probe GEMM, probe selection (warp kernel + its block
+    # fallback when nprobe <= 32), seed refine, threshold, main grouping (4), main scan,
+    # refine, merge; with stored vanguard lows also vanguard grouping (4), lows offsets, lows
+    # scan, seed selection (warp + block fallback when keep <= 32) and the lows filter, else
+    # one vanguard rescan; +2 exchange steps (gather_threshold / gather_merge) when sharded.
+    sel = 2 if chosen <= 32 else 1
+    vsel = 2 if max(k, 20) <= 32 else 1
+    per_search = 11 + sel + ((7 + vsel) if mode == 1 else 1) + (2 if world > 1 else 0)
+    launches = per_search * args.steps
 
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and index_path is not None:

@@ -120,6 +120,38 @@ __device__ __forceinline__ void block_bitonic_sort(uint64_t *a, int n) {
     }
 }
 
+// ---- warp-wide bitonic sorts of uint64 keys -----------------------------------------------
+// One key per lane, returned ascending by lane index.
+__device__ __forceinline__ uint64_t warp_sort_lane_keys(uint64_t v, int lane) {
+    for (int k = 2; k <= 32; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const uint64_t o = __shfl_xor_sync(0xffffffffu, v, j);
+            const bool up = (lane & k) == 0, lower = (lane & j) == 0;
+            v = (lower == up) ? (v < o ? v : o) : (v < o ? o : v);
+        }
+    }
+    return v;
+}
+
+// n (a power of two) keys in shared memory, sorted ascending by the calling warp.
+__device__ __forceinline__ void warp_sort_smem(uint64_t *a, int n, int lane) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = lane; i < n; i += 32) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const uint64_t x = a[i], y = a[ixj];
+                    if ((x > y) == ((i & k) == 0)) {
+                        a[i] = y;
+                        a[ixj] = x;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
 __host__ __device__ __forceinline__ int next_pow2(int x) {
     int p = 1;
     while (p < x) p <<= 1;

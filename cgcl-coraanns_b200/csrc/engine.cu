@@ -160,6 +160,40 @@ inline void launch_probe_gemm(const float *qr, const float *qnorm2, uint64_t nq,
     CUDA_TRY(cudaGetLastError());
 }
 
+// Exact top-nprobe from the approximate distances: one warp per query when nprobe <= 32
+// (queries whose candidate set overflows go on to the block kernel through `fallback`,
+// 1 + nq words), else one CTA per query.
+inline void launch_guarded_select(float *approx, uint64_t nlist, uint64_t nq, uint64_t nprobe,
+                                  const float *qr, const float *qnorm2, const float *cent,
+                                  float cmax, uint64_t D, int *probe_ids, float *probe_g,
+                                  uint32_t *fallback, int num_sms, cudaStream_t st) {
+    const int inq = static_cast<int>(nq), inp = static_cast<int>(nprobe), iD = static_cast<int>(D);
+    const int ccap = guarded_select_cap(inp);
+    const size_t bsm = guarded_select_smem(inp, ccap, iD);
+    CUDA_TRY(cudaFuncSetAttribute(guarded_select_kernel,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm));
+    if (nprobe <= 32) {
+        const size_t wsm = guarded_select_warp_smem(iD);
+        CUDA_TRY(cudaFuncSetAttribute(guarded_select_warp_kernel,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wsm));
+        CUDA_TRY(cudaMemsetAsync(fallback, 0, 4, st));
+        guarded_select_warp_kernel<<<static_cast<unsigned>((nq + kGuardWarps - 1) / kGuardWarps),
+                                     32 * kGuardWarps, wsm, st>>>(
+            approx, static_cast<int>(nlist), approx_ld(nlist), inq, inp, qr, qnorm2, cent, cmax,
+            iD, kApproxEpsTF32, probe_ids, probe_g, fallback);
+        CUDA_TRY(cudaGetLastError());
+        guarded_select_kernel<<<static_cast<unsigned>(2 * num_sms), 256, bsm, st>>>(
+            approx, static_cast<int>(nlist), approx_ld(nlist), inp, ccap, qr, qnorm2, cent, cmax,
+            iD, kApproxEpsTF32, probe_ids, probe_g, fallback);
+    } else {
+        guarded_select_kernel<<<inq, 256, bsm, st>>>(approx, static_cast<int>(nlist),
+                                                     approx_ld(nlist), inp, ccap, qr, qnorm2, cent,
+                                                     cmax, iD, kApproxEpsTF32, probe_ids, probe_g,
+                                                     nullptr);
+    }
+    CUDA_TRY(cudaGetLastError());
+}
+
 // Cluster-to-shard plan: longest-processing-time greedy on cluster sizes (every vector of an
 // index costs the same bytes), largest cluster first (ties: lower cluster id) onto the least
 // loaded shard (ties: lower rank). Deterministic, so every rank derives the same plan.
@@ -793,15 +827,9 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
         launch_probe_gemm(qr.p, qnorm2.p, nq, D, centroids.p, cnorm2.p, nlist, gmat.p, num_sms,
                           st, err.p);
         mark(2, st);
-        const int ccap = guarded_select_cap(inp);
-        const size_t sm = guarded_select_smem(inp, ccap, static_cast<int>(D));
-        CUDA_TRY(cudaFuncSetAttribute(guarded_select_kernel,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        guarded_select_kernel<<<inq, 256, sm, st>>>(gmat.p, static_cast<int>(nlist),
-                                                    approx_ld(nlist), inp, ccap, qr.p, qnorm2.p,
-                                                    centroids.p, cmax, static_cast<int>(D),
-                                                    kApproxEpsTF32, probe_ids.p, probe_g.p);
-        CUDA_TRY(cudaGetLastError());
+        // select_fallback (>= 1 + nq words) is free until the vanguard stage
+        launch_guarded_select(gmat.p, nlist, nq, np, qr.p, qnorm2.p, centroids.p, cmax, D,
+                              probe_ids.p, probe_g.p, select_fallback.p, num_sms, st);
     }
     mark(3, st);
     const bool lows_mode = lows.n > 0;
@@ -1474,7 +1502,7 @@ unsigned char *g_noalloc_ptr[kNoallocMaxDevices] = {};
 inline size_t align256(size_t b) { return (b + 255) & ~size_t{255}; }
 
 struct NoallocLayout {
-    size_t status, qr, qnorm2, scal, planes, approx, total;
+    size_t status, qr, qnorm2, scal, planes, approx, fallback, total;
 };
 
 NoallocLayout noalloc_layout(uint64_t nq, uint64_t D, uint64_t W4, uint64_t nlist) {
@@ -1485,7 +1513,8 @@ NoallocLayout noalloc_layout(uint64_t nq, uint64_t D, uint64_t W4, uint64_t nlis
     l.scal = l.qnorm2 + align256(nq * sizeof(float));
     l.planes = l.scal + align256(nq * sizeof(QueryScalars));
     l.approx = l.planes + align256(nq * 8 * W4 * sizeof(uint32_t));
-    l.total = l.approx + align256(nq * approx_ld(nlist) * sizeof(float));
+    l.fallback = l.approx + align256(nq * approx_ld(nlist) * sizeof(float));
+    l.total = l.fallback + align256((nq + 1) * sizeof(uint32_t));
     return l;
 }
 
@@ -1552,15 +1581,10 @@ int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num
         CUDA_TRY(cudaGetLastError());
         cora::launch_probe_gemm(qr, qnorm2, num_queries, e.D, e.centroids.p, e.cnorm2.p, e.nlist,
                                 approx, e.num_sms, st, status);
-        const int ccap = cora::guarded_select_cap(inp);
-        const size_t gsm = cora::guarded_select_smem(inp, ccap, static_cast<int>(e.D));
-        CUDA_TRY(cudaFuncSetAttribute(cora::guarded_select_kernel,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gsm));
-        cora::guarded_select_kernel<<<inq, 256, gsm, st>>>(
-            approx, static_cast<int>(e.nlist), cora::approx_ld(e.nlist), inp, ccap, qr, qnorm2,
-            e.centroids.p, e.cmax, static_cast<int>(e.D), cora::kApproxEpsTF32, d_probe_ids,
-            d_probe_dists);
-        CUDA_TRY(cudaGetLastError());
+        cora::launch_guarded_select(approx, e.nlist, num_queries, nprobe, qr, qnorm2,
+                                    e.centroids.p, e.cmax, e.D, d_probe_ids, d_probe_dists,
+                                    reinterpret_cast<uint32_t *>(s + l.fallback), e.num_sms, st);
+        (void)inp;
     });
 }
 

@@ -127,10 +127,37 @@ __device__ __forceinline__ float exact_centroid_dist(const float *__restrict__ x
 // recomputed exactly (fp64) and selected. More candidates than the shared buffer holds (a
 // pathological tie band) fall back to exact distances for every centroid of the query,
 // written over its approximate row. Dynamic shared memory: see guarded_select_smem().
+// list == nullptr: query blockIdx.x; otherwise the queries list[1 .. list[0]] (grid-stride),
+// the ones guarded_select_warp_kernel handed over.
+__device__ void guarded_select_block(int q, float *__restrict__ approx, int nlist, size_t ld,
+                                     int nprobe, int cand_cap, const float *__restrict__ qr,
+                                     const float *__restrict__ qnorm2,
+                                     const float *__restrict__ cent, float cmax, int D, double eps,
+                                     int *__restrict__ probe_ids, float *__restrict__ probe_g);
+
 __global__ void __launch_bounds__(256) guarded_select_kernel(
     float *__restrict__ approx, int nlist, size_t ld, int nprobe, int cand_cap,
     const float *__restrict__ qr, const float *__restrict__ qnorm2, const float *__restrict__ cent,
-    float cmax, int D, double eps, int *__restrict__ probe_ids, float *__restrict__ probe_g) {
+    float cmax, int D, double eps, int *__restrict__ probe_ids, float *__restrict__ probe_g,
+    const uint32_t *__restrict__ list) {
+    if (!list) {
+        guarded_select_block(blockIdx.x, approx, nlist, ld, nprobe, cand_cap, qr, qnorm2, cent,
+                             cmax, D, eps, probe_ids, probe_g);
+        return;
+    }
+    const uint32_t n = list[0];
+    for (uint32_t j = blockIdx.x; j < n; j += gridDim.x) {
+        guarded_select_block(static_cast<int>(list[1 + j]), approx, nlist, ld, nprobe, cand_cap,
+                             qr, qnorm2, cent, cmax, D, eps, probe_ids, probe_g);
+        __syncthreads();  // shared memory is reused by the next query
+    }
+}
+
+__device__ void guarded_select_block(int q, float *__restrict__ approx, int nlist, size_t ld,
+                                     int nprobe, int cand_cap, const float *__restrict__ qr,
+                                     const float *__restrict__ qnorm2,
+                                     const float *__restrict__ cent, float cmax, int D, double eps,
+                                     int *__restrict__ probe_ids, float *__restrict__ probe_g) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int S2 = next_pow2(nprobe);
     uint64_t *sel = reinterpret_cast<uint64_t *>(smem_raw);          // S2
@@ -139,7 +166,6 @@ __global__ void __launch_bounds__(256) guarded_select_kernel(
     float *x = reinterpret_cast<float *>(cidx + cand_cap);            // D
     __shared__ int scratch[256 + 3];
     __shared__ int s_ncand;
-    const int q = blockIdx.x;
     float *row = approx + (size_t)q * ld;  // ld: row stride (nlist rounded up to 4 floats)
     for (int j = threadIdx.x; j < D; j += blockDim.x) x[j] = qr[(size_t)q * D + j];
     if (threadIdx.x == 0) s_ncand = 0;
@@ -179,6 +205,95 @@ __global__ void __launch_bounds__(256) guarded_select_kernel(
 
 __host__ __device__ inline size_t guarded_select_smem(int nprobe, int cand_cap, int D) {
     return (size_t)next_pow2(nprobe) * 8 + (size_t)cand_cap * 12 + (size_t)D * 4;
+}
+
+// One warp per query (8 per CTA), nprobe <= 32: the same selection without block-wide radix
+// passes. The nprobe-th smallest of the 32 lane minima, tau_ub, is >= tau (nprobe values lie
+// at or below it), so {approx <= tau_ub + 2E} contains the guard band {approx <= tau + 2E},
+// and recomputing that superset exactly selects the same probes (a centroid outside the band
+// can never beat one of the true top-nprobe). It is normally a few dozen centroids; a query
+// whose set exceeds kGuardWarpBand is queued in fallback[1..] (count in fallback[0]) for
+// guarded_select_kernel. Dynamic shared memory: guarded_select_warp_smem(D).
+constexpr int kGuardWarpBand = 256;
+constexpr int kGuardWarps = 8;
+__host__ __device__ inline size_t guarded_select_warp_slice(int D) {
+    return (size_t)D * 4 + (size_t)kGuardWarpBand * 12;
+}
+__host__ __device__ inline size_t guarded_select_warp_smem(int D) {
+    return kGuardWarps * guarded_select_warp_slice(D);
+}
+
+__global__ void __launch_bounds__(256) guarded_select_warp_kernel(
+    const float *__restrict__ approx, int nlist, size_t ld, int nq, int nprobe,
+    const float *__restrict__ qr, const float *__restrict__ qnorm2, const float *__restrict__ cent,
+    float cmax, int D, double eps, int *__restrict__ probe_ids, float *__restrict__ probe_g,
+    uint32_t *__restrict__ fallback) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int w = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int q = blockIdx.x * kGuardWarps + w;
+    if (q >= nq) return;  // whole warp
+    float *x = reinterpret_cast<float *>(smem_raw + w * guarded_select_warp_slice(D));
+    uint64_t *keys = reinterpret_cast<uint64_t *>(x + D);  // D % 64 == 0: 8-byte aligned
+    uint32_t *cidx = reinterpret_cast<uint32_t *>(keys + kGuardWarpBand);
+    const float *row = approx + (size_t)q * ld;  // ld % 4 == 0: rows are 16-byte aligned
+    for (int j = lane; j < D; j += 32) x[j] = qr[(size_t)q * D + j];
+
+    float mn = FLT_MAX;
+    for (int c0 = lane * 4; c0 < nlist; c0 += 128) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(row + c0));
+        mn = fminf(mn, v.x);
+        if (c0 + 1 < nlist) mn = fminf(mn, v.y);
+        if (c0 + 2 < nlist) mn = fminf(mn, v.z);
+        if (c0 + 3 < nlist) mn = fminf(mn, v.w);
+    }
+    const uint64_t kth = __shfl_sync(0xffffffffu,
+                                     warp_sort_lane_keys(make_key(mn, lane), lane), nprobe - 1);
+    const double tau_ub = (double)unord_f32(static_cast<uint32_t>(kth >> 32));
+    const double r = sqrt((double)qnorm2[q]) + (double)cmax;
+    const double bound = tau_ub + 2.0 * (eps * r * r + 1e-30);
+
+    uint32_t cnt = 0;
+    for (int base = 0; base < nlist; base += 128) {
+        const int c0 = base + lane * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c0 < nlist) v = __ldg(reinterpret_cast<const float4 *>(row + c0));
+        const float ve[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const bool take = c0 + e < nlist && (double)ve[e] <= bound;
+            const uint32_t m = __ballot_sync(0xffffffffu, take);
+            const uint32_t pos = cnt + __popc(m & ((1u << lane) - 1u));
+            if (take && pos < kGuardWarpBand) cidx[pos] = static_cast<uint32_t>(c0 + e);
+            cnt += __popc(m);
+        }
+    }
+    if (cnt > kGuardWarpBand) {
+        if (lane == 0) fallback[1 + atomicAdd(fallback, 1u)] = static_cast<uint32_t>(q);
+        return;
+    }
+    __syncwarp();
+    for (uint32_t i = lane; i < cnt; i += 32) {
+        const uint32_t c = cidx[i];
+        keys[i] = make_key(exact_centroid_dist(x, cent + (size_t)c * D, D), c);
+    }
+    __syncwarp();
+    if (cnt <= 32) {
+        const uint64_t key = warp_sort_lane_keys(lane < (int)cnt ? keys[lane] : kKeyMax, lane);
+        if (lane < nprobe) {
+            probe_ids[(size_t)q * nprobe + lane] = static_cast<int>(key & 0xFFFFFFFFu);
+            probe_g[(size_t)q * nprobe + lane] = unord_f32(static_cast<uint32_t>(key >> 32));
+        }
+    } else {
+        const int n2 = next_pow2(static_cast<int>(cnt));
+        for (int i = static_cast<int>(cnt) + lane; i < n2; i += 32) keys[i] = kKeyMax;
+        __syncwarp();
+        warp_sort_smem(keys, n2, lane);
+        for (int j = lane; j < nprobe; j += 32) {
+            const uint64_t key = keys[j];
+            probe_ids[(size_t)q * nprobe + j] = static_cast<int>(key & 0xFFFFFFFFu);
+            probe_g[(size_t)q * nprobe + j] = unord_f32(static_cast<uint32_t>(key >> 32));
+        }
+    }
 }
 __host__ __device__ inline int guarded_select_cap(int nprobe) {
     const int c = 2 * nprobe > 1024 ? 2 * nprobe : 1024;

@@ -557,36 +557,6 @@ __global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, Sear
 constexpr int kWarpSelectMax = 32;   // largest `keep` handled one warp per pair
 constexpr int kWarpSelectBuf = 256;  // keys at or below the first threshold a warp may hold
 
-__device__ __forceinline__ uint64_t warp_sort_lane_keys(uint64_t v, int lane) {
-    // bitonic sort of one key per lane, ascending by lane index
-    for (int k = 2; k <= 32; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            const uint64_t o = __shfl_xor_sync(0xffffffffu, v, j);
-            const bool up = (lane & k) == 0, lower = (lane & j) == 0;
-            v = (lower == up) ? (v < o ? v : o) : (v < o ? o : v);
-        }
-    }
-    return v;
-}
-
-__device__ __forceinline__ void warp_sort_smem(uint64_t *a, int n, int lane) {
-    for (int k = 2; k <= n; k <<= 1) {
-        for (int j = k >> 1; j > 0; j >>= 1) {
-            for (int i = lane; i < n; i += 32) {
-                const int ixj = i ^ j;
-                if (ixj > i) {
-                    const uint64_t x = a[i], y = a[ixj];
-                    if ((x > y) == ((i & k) == 0)) {
-                        a[i] = y;
-                        a[ixj] = x;
-                    }
-                }
-            }
-            __syncwarp();
-        }
-    }
-}
-
 // One warp per vanguard pair (8 per CTA), keep <= 32. The keep-th smallest of the 32 lane
 // minima bounds the keep-th smallest key from above, so every seed is among the keys at or
 // below it; those (normally a few dozen) are collected and sorted. A pair whose collection
