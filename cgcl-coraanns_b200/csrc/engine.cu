@@ -259,6 +259,7 @@ struct Engine {
     DevBuf<int> probe_ids, item_counter, err;
     DevBuf<uint32_t> select_fallback;  // [0] count, [1..] vanguard pairs for block selection
     DevBuf<uint64_t> bound, cand_rec, cand_key, vg_off;
+    DevBuf<unsigned long long> lows_top;
     DevBuf<float> lows;
     std::vector<uint32_t> h_sizes_sorted;  // cluster sizes, descending (lows worst case)
     DevBuf<ScanItem> items;
@@ -482,13 +483,14 @@ struct Engine {
             // worst case of the lows buffer: every query probes the ws_vg largest clusters
             uint64_t worst = 0;
             for (uint64_t r = 0; r < ws_vg && r < h_sizes_sorted.size(); ++r)
-                worst += h_sizes_sorted[r];
+                worst += lows_slice(h_sizes_sorted[r]);  // slices padded to 4 floats
             worst *= max_q;
             size_t free_b = 0, total_b = 0;
             CUDA_TRY(cudaMemGetInfo(&free_b, &total_b));
             const uint64_t limit = std::min<uint64_t>(lows_budget, free_b / 4);
             if (worst > 0 && worst * 4 <= limit) lows.alloc(worst);
         }
+        lows_top.alloc(1);
         cand_cnt.alloc(max_q);
         seed_cnt.alloc(max_q);
         cand_rec.alloc(max_q * cap);
@@ -524,6 +526,7 @@ struct Engine {
         err.release();
         bound.release();
         vg_off.release();
+        lows_top.release();
         select_fallback.release();
         lows.release();
         cand_rec.release();
@@ -781,7 +784,7 @@ SearchView Engine::search_view() const {
                       static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
                       scal.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p,
                       cand_cnt.p, seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n,
-                      err.p, warp_select_limit};
+                      lows_top.p, err.p, warp_select_limit};
 }
 
 void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, float *d_od,
@@ -799,7 +802,7 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
     last_nq = nq;
     last_k = k;
     last_np = np;
-    const int inq = static_cast<int>(nq), inp = static_cast<int>(np), ik = static_cast<int>(k);
+    const int inq = static_cast<int>(nq), ik = static_cast<int>(k);
     const uint64_t veff = vanguard_depth(np);
     const uint64_t keep = std::max<uint64_t>(k, kVanguardMinKeep);
 
@@ -843,9 +846,8 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
     // 3. vanguard pairs: seeds (best `keep` keys per pair among low < T0)
     if (lows_mode) {
         group_pairs(0, iveff, st);
-        vanguard_offsets_kernel<<<1, 1024, 0, st>>>(probe_ids.p, cl_size.p, own, inq, inp, iveff,
-                                                    lows.n, vg_off.p, err.p);
-        CUDA_TRY(cudaGetLastError());
+        // the lows pass bump-allocates the pairs' slices
+        CUDA_TRY(cudaMemsetAsync(lows_top.p, 0, sizeof(unsigned long long), st));
     }
     mark(4, st);
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter0, st));

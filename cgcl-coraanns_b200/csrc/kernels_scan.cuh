@@ -69,8 +69,9 @@ struct SearchView {
     uint64_t *cand_rec;          // nq x cap : gid | (probe rank << 32)
     uint64_t *cand_key;          // nq x cap : ord(ex) << 32 | id
     float *lows;                 // vanguard lower bounds (lows mode), see vg_off
-    uint64_t *vg_off;            // nq x veff + 1 offsets into lows
+    uint64_t *vg_off;            // nq x veff: each vanguard pair's slice offset in lows
     uint64_t lows_cap;           // capacity of lows (floats)
+    unsigned long long *lows_top;  // bump allocator of lows slices (zeroed per search)
     int *err;
     int warp_select_limit;       // keys a warp may collect before queueing a block selection
 };
@@ -165,43 +166,11 @@ __global__ void emit_items_kernel(const uint32_t *__restrict__ cnt,
     }
 }
 
-// Offsets of every vanguard pair's slice of the lows buffer: one CTA, pairs in
-// (query, rank) order. Non-owned clusters (sharded search) get empty slices. Sets
-// kDevCandidateOverflow if the total exceeds the buffer (sized for the worst case).
-__global__ void __launch_bounds__(1024) vanguard_offsets_kernel(
-    const int *__restrict__ probe_ids, const uint32_t *__restrict__ cl_size,
-    const uint8_t *__restrict__ owned, int nq, int nprobe, int veff, uint64_t cap,
-    uint64_t *__restrict__ vg_off, int *__restrict__ err) {
-    __shared__ uint64_t s_sum[1024];
-    const int t = threadIdx.x;
-    const int per = (nq + 1023) / 1024;
-    const int b = t * per, e = min(nq, b + per);
-    uint64_t sum = 0;
-    for (int q = b; q < e; ++q)
-        for (int r = 0; r < veff; ++r) {
-            const int c = probe_ids[(size_t)q * nprobe + r];
-            if (!owned || owned[c]) sum += cl_size[c];
-        }
-    s_sum[t] = sum;
-    __syncthreads();
-    for (int d = 1; d < 1024; d <<= 1) {
-        const uint64_t v = t >= d ? s_sum[t - d] : 0;
-        __syncthreads();
-        s_sum[t] += v;
-        __syncthreads();
-    }
-    uint64_t run = s_sum[t] - sum;
-    for (int q = b; q < e; ++q)
-        for (int r = 0; r < veff; ++r) {
-            vg_off[(size_t)q * veff + r] = run;
-            const int c = probe_ids[(size_t)q * nprobe + r];
-            if (!owned || owned[c]) run += cl_size[c];
-        }
-    if (t == 1023) {
-        vg_off[(size_t)nq * veff] = s_sum[1023];
-        if (s_sum[1023] > cap) atomicOr(err, kDevCandidateOverflow);
-    }
-}
+// Lows slices: each vanguard pair gets round_up(n_c, 4) floats (16-byte aligned slices, so
+// the select and filter kernels read them as float4), bump-allocated per item by the lows
+// pass of scan_kernel; the worst case (every query probing the largest clusters) is what
+// prepare_workspace reserves.
+__host__ __device__ __forceinline__ uint32_t lows_slice(uint32_t n) { return (n + 3u) & ~3u; }
 
 // ---- shared pieces ------------------------------------------------------------------
 template <int G16>
@@ -221,9 +190,11 @@ __device__ __forceinline__ void issue_tile(uint4 *stage_buf, uint64_t *bar, cons
 // an integer identity, so the result equals the reference's
 // sum_{j<7} popc(x & p_j) << j - popc(x & p_7) << 7 (filter_kernels.cuh:79-104) bit for
 // bit. The weighted popcount sum of one 128-bit group (8 planes x 4 words) is formed by a
-// carry-save adder tree: words of equal weight are combined three at a time into a sum
-// word and a carry word of twice the weight, leaving one word per weight 2^0..2^9, so 10
-// POPC replace 32 (POPC issues at a quarter of the logic-op rate on this SM).
+// carry-save adder tree over the low weights: words of equal weight are combined three at a
+// time into a sum word and a carry word of twice the weight. POPC issues at a quarter of the
+// logic-op rate on this SM, and a full tree (10 POPC) left the logic pipe the bottleneck, so
+// the tree stops at weight 2^4 and the words of weights 2^5..2^7 (plus the carries into
+// 2^5) are counted directly: 5 + 15 POPC, about 20 fewer logic ops, both pipes near balance.
 __device__ __forceinline__ void full_add(uint32_t &s, uint32_t &c, uint32_t a, uint32_t b,
                                          uint32_t d) {
     s = a ^ b ^ d;
@@ -233,6 +204,19 @@ __device__ __forceinline__ void half_add(uint32_t &s, uint32_t &c, uint32_t a, u
     s = a ^ b;
     c = a & b;
 }
+
+// Weights combined by the adder tree (2^0 .. 2^(kCsaLevels-1)); 8 = the full tree. Measured
+// on config 2 (both scan passes): 4 -> 1.35 ms, 5 -> 1.25, 6 -> 1.27, 7 -> 1.36, 8 -> 1.41;
+// two vectors per thread (CORA_SCAN_VPT 2) raised registers from 72 to 94 and lost 13%.
+#ifndef CORA_CSA_LEVELS
+#define CORA_CSA_LEVELS 5
+#endif
+constexpr int kCsaLevels = CORA_CSA_LEVELS;
+static_assert(kCsaLevels >= 2 && kCsaLevels <= 8, "adder tree depth");
+// Vectors each scan thread evaluates per pass over a tile's queries.
+#ifndef CORA_SCAN_VPT
+#define CORA_SCAN_VPT 1
+#endif
 
 // sum_j 2^j sum_t popc(x_t & p'_{j,t}) for one group; P points at the group's plane words
 // (plane j at P + j * W4, 4 consecutive words).
@@ -261,9 +245,9 @@ __device__ __forceinline__ int group_weighted_popc(uint4 x, const uint32_t *__re
     cA = nA;
     cB = nB;
     cC = nC;
-    // weights 2^2 .. 2^7: 4 words + 3 carries each
+    // weights 2^2 .. 2^(L-1): 4 words + 3 carries each
 #pragma unroll
-    for (int j = 2; j < 8; ++j) {
+    for (int j = 2; j < kCsaLevels; ++j) {
         full_add(s, nA, a[j][0], a[j][1], a[j][2]);
         full_add(t, nB, a[j][3], cA, cB);
         full_add(s, nC, s, t, cC);
@@ -272,24 +256,38 @@ __device__ __forceinline__ int group_weighted_popc(uint4 x, const uint32_t *__re
         cB = nB;
         cC = nC;
     }
-    // weights 2^8, 2^9: the remaining carries
-    full_add(s, nA, cA, cB, cC);
-    total += __popc(s) << 8;
-    total += __popc(nA) << 9;
+    if (kCsaLevels == 8) {  // full tree: the carries of weight 2^8 and their carry (2^9)
+        full_add(s, nA, cA, cB, cC);
+        return total + (__popc(s) << 8) + (__popc(nA) << 9);
+    }
+    // weights 2^L .. 2^7 counted directly (the 3 carries into 2^L as well)
+    total += (__popc(cA) + __popc(cB) + __popc(cC)) << kCsaLevels;
+#pragma unroll
+    for (int j = kCsaLevels; j < 8; ++j)
+        total += (__popc(a[j][0]) + __popc(a[j][1]) + __popc(a[j][2]) + __popc(a[j][3])) << j;
     return total;
 }
 
+// popc of the whole code times 128: the query-independent part of the identity.
+template <int G16>
+__device__ __forceinline__ int code_bias(const uint4 (&code)[G16]) {
+    int px = 0;
+#pragma unroll
+    for (int g = 0; g < G16; ++g)
+        px += __popc(code[g].x) + __popc(code[g].y) + __popc(code[g].z) + __popc(code[g].w);
+    return px << 7;
+}
+
+// sum_i b_i qint_i of one code against one query's offset-binary planes; `bias` is
+// code_bias(code), computed once per vector.
 template <int G16>
 __device__ __forceinline__ int ip_int_from_planes(const uint4 (&code)[G16],
-                                                  const uint32_t *__restrict__ P) {
+                                                  const uint32_t *__restrict__ P, int bias) {
     constexpr int W4 = ScanShape<G16>::W4;
-    int t = 0, px = 0;
+    int t = 0;
 #pragma unroll
-    for (int g = 0; g < G16; ++g) {
-        t += group_weighted_popc<W4>(code[g], P + 4 * g);
-        px += __popc(code[g].x) + __popc(code[g].y) + __popc(code[g].z) + __popc(code[g].w);
-    }
-    return t - (px << 7);
+    for (int g = 0; g < G16; ++g) t += group_weighted_popc<W4>(code[g], P + 4 * g);
+    return t - bias;
 }
 
 // Copies a query's two's-complement bit-planes into shared memory as offset-binary planes
@@ -365,6 +363,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
         s_w[kMaxPairsPerItem], s_gerr[kMaxPairsPerItem];
     __shared__ int s_q[kMaxPairsPerItem], s_r[kMaxPairsPerItem];
     __shared__ int s_item, s_abort;
+    __shared__ unsigned long long s_lbase;  // lows pass: this item's slices (~0ull: no room)
 
     if (threadIdx.x == 0) {
         mbar_init(&bars[0], 1);
@@ -390,6 +389,19 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
         const int ntiles = (n + TV - 1) / TV;
         if (threadIdx.x == 0 && ntiles > 0)
             issue_tile<G16>(stage, &bars[0], ix.scan4, cbase, n, 0, min(TV, n));
+        if (kWriteLows) {
+            if (threadIdx.x == 0) {
+                const unsigned long long need =
+                    (unsigned long long)pc * lows_slice(static_cast<uint32_t>(n));
+                unsigned long long b = atomicAdd(sv.lows_top, need);
+                if (b + need > sv.lows_cap) {
+                    atomicOr(sv.err, kDevCandidateOverflow);
+                    b = ~0ull;
+                }
+                s_lbase = b;
+            }
+            __syncthreads();
+        }
         if (threadIdx.x < pc) {
             const uint32_t pr = pairs[item.pair_begin + threadIdx.x];
             const int q = static_cast<int>(pr >> 16), r = static_cast<int>(pr & 0xFFFFu);
@@ -402,8 +414,13 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
             s_w[threadIdx.x] = qs.width;
             s_gerr[threadIdx.x] = __fsqrt_rn(fmaxf(g, 0.0f));
             if (kWriteLows) {
-                // slice offset of this vanguard pair, carried in s_bnd
-                s_bnd[threadIdx.x] = sv.vg_off[(size_t)q * sv.veff + r];
+                // slice offset of this vanguard pair, carried in s_bnd (~0: not stored)
+                const unsigned long long b = s_lbase;
+                const uint64_t off =
+                    b == ~0ull ? 0ull
+                               : b + (uint64_t)threadIdx.x * lows_slice(static_cast<uint32_t>(n));
+                sv.vg_off[(size_t)q * sv.veff + r] = off;
+                s_bnd[threadIdx.x] = b == ~0ull ? ~0ull : off;
             } else {
                 s_T1[threadIdx.x] = sv.T1[q];
                 s_bnd[threadIdx.x] = r < sv.veff ? sv.bound[(size_t)q * sv.veff + r] : 0ull;
@@ -427,30 +444,47 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
                 issue_tile<G16>(stage + (b ^ 1) * Sh::kStageEntries, &bars[b ^ 1], ix.scan4, cbase,
                                 n, v0 + TV, min(TV, n - v0 - TV));
             const uint4 *sb = stage + b * Sh::kStageEntries;
-            for (int base = 0; base < tv; base += kScanThreads) {
-                const int i = base + threadIdx.x;
-                const bool valid = i < tv;
-                uint4 code[G16];
-                float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+            // every thread evaluates V vectors of the tile against each query in turn, so a
+            // query's planes are read from shared memory once per V vectors
+            constexpr int V = CORA_SCAN_VPT < TV / kScanThreads ? CORA_SCAN_VPT : TV / kScanThreads;
+            for (int vb = 0; vb < tv; vb += V * kScanThreads) {
+                uint4 code[V][G16];
+                float4 f[V];
+                int bias[V];
+                bool valid[V];
 #pragma unroll
-                for (int gg = 0; gg < G16; ++gg)
-                    code[gg] = valid ? sb[gg * TV + i] : make_uint4(0, 0, 0, 0);
-                if (valid) {
-                    const uint4 fr = sb[G16 * TV + i];
-                    f = make_float4(__uint_as_float(fr.x), __uint_as_float(fr.y),
-                                    __uint_as_float(fr.z), 0.0f);
+                for (int v = 0; v < V; ++v) {
+                    const int i = vb + v * kScanThreads + threadIdx.x;
+                    valid[v] = i < tv;
+                    f[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int gg = 0; gg < G16; ++gg)
+                        code[v][gg] = valid[v] ? sb[gg * TV + i] : make_uint4(0, 0, 0, 0);
+                    if (valid[v]) {
+                        const uint4 fr = sb[G16 * TV + i];
+                        f[v] = make_float4(__uint_as_float(fr.x), __uint_as_float(fr.y),
+                                           __uint_as_float(fr.z), 0.0f);
+                    }
+                    bias[v] = code_bias<G16>(code[v]);
                 }
-                const uint32_t gid = s + static_cast<uint32_t>(v0 + i);
                 for (int j = 0; j < pc; ++j) {
-                    const int ip = ip_int_from_planes<G16>(code, s_planes + j * 8 * W4);
-                    const float ip1 = __fadd_rn(__fmul_rn(s_w[j], (float)ip), 0.0f);
-                    const float low = lower_bound_dist(f, ip1, s_g[j], s_k1[j], s_gerr[j]);
-                    if (kWriteLows) {
-                        if (valid) sv.lows[s_bnd[j] + v0 + i] = low;
-                    } else {
-                        const bool cand = valid && (low < s_T1[j]) && (make_key(low, gid) > s_bnd[j]);
-                        emit_candidate(sv, cand, s_q[j], gid | (static_cast<uint64_t>(s_r[j]) << 32),
-                                       lane);
+                    const uint32_t *P = s_planes + j * 8 * W4;
+#pragma unroll
+                    for (int v = 0; v < V; ++v) {
+                        const int i = vb + v * kScanThreads + threadIdx.x;
+                        const int ip = ip_int_from_planes<G16>(code[v], P, bias[v]);
+                        const float ip1 = __fadd_rn(__fmul_rn(s_w[j], (float)ip), 0.0f);
+                        const float low =
+                            lower_bound_dist(f[v], ip1, s_g[j], s_k1[j], s_gerr[j]);
+                        if (kWriteLows) {
+                            if (valid[v] && s_bnd[j] != ~0ull) sv.lows[s_bnd[j] + v0 + i] = low;
+                        } else {
+                            const uint32_t gid = s + static_cast<uint32_t>(v0 + i);
+                            const bool cand =
+                                valid[v] && (low < s_T1[j]) && (make_key(low, gid) > s_bnd[j]);
+                            emit_candidate(sv, cand, s_q[j],
+                                           gid | (static_cast<uint64_t>(s_r[j]) << 32), lane);
+                        }
                     }
                 }
             }
@@ -520,7 +554,23 @@ __device__ void select_pair_block(const IndexView &ix, const SearchView &sv,
     write_seeds(sv, q, r, s_total, s_keys, s_base_p);
 }
 
-constexpr int kLowsUnroll = 4;  // lows loaded per lane before they are processed
+constexpr int kLowsUnroll = 2;  // float4 lows loaded per lane before they are processed
+
+// Loads lows 4 * (i4 .. i4 + 32 * (kLowsUnroll - 1)) of a slice as float4 (slices are
+// 16-byte aligned and padded to a multiple of 4); entries at or past n read as `fill`.
+__device__ __forceinline__ void load_lows4(const float4 *__restrict__ L4, uint32_t n,
+                                           uint32_t i4, float fill, float (&l)[4 * kLowsUnroll]) {
+#pragma unroll
+    for (int t = 0; t < kLowsUnroll; ++t) {  // all loads first: one round trip per batch
+        const uint32_t j4 = i4 + 32 * t;
+        float4 v = make_float4(fill, fill, fill, fill);
+        if (4 * j4 < n) v = __ldg(L4 + j4);
+        l[4 * t + 0] = v.x;
+        l[4 * t + 1] = 4 * j4 + 1 < n ? v.y : fill;
+        l[4 * t + 2] = 4 * j4 + 2 < n ? v.z : fill;
+        l[4 * t + 3] = 4 * j4 + 3 < n ? v.w : fill;
+    }
+}
 
 // One warp per vanguard pair (8 per CTA): candidates low < T1 that are not seeds
 // (key > boundary), read from the pair's stored lows.
@@ -534,22 +584,21 @@ __global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, Sear
     if (owned && !owned[c]) return;
     const uint32_t s = ix.cl_start[c];
     const uint32_t n = ix.cl_size[c];
-    const float *L = sv.lows + sv.vg_off[pi];
+    const float4 *L4 = reinterpret_cast<const float4 *>(sv.lows + sv.vg_off[pi]);
     const float T1 = sv.T1[q];
     const uint64_t bnd = sv.bound[(size_t)q * sv.veff + r];
-    for (uint32_t base = 0; base < n; base += 32 * kLowsUnroll) {
-        float l[kLowsUnroll];
+    for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
+        float l[4 * kLowsUnroll];
+        load_lows4(L4, n, b4 + lane, T1, l);
 #pragma unroll
-        for (int t = 0; t < kLowsUnroll; ++t) {  // all loads first: one round trip per batch
-            const uint32_t i = base + 32 * t + lane;
-            l[t] = i < n ? __ldg(L + i) : T1;
-        }
+        for (int t = 0; t < kLowsUnroll; ++t)
 #pragma unroll
-        for (int t = 0; t < kLowsUnroll; ++t) {
-            const uint32_t i = base + 32 * t + lane;
-            const bool cand = (l[t] < T1) && (make_key(l[t], s + i) > bnd);
-            emit_candidate(sv, cand, q, (s + i) | (static_cast<uint64_t>(r) << 32), lane);
-        }
+            for (int e = 0; e < 4; ++e) {
+                const uint32_t i = 4 * (b4 + lane + 32 * t) + e;
+                const float lv = l[4 * t + e];
+                const bool cand = (lv < T1) && (make_key(lv, s + i) > bnd);
+                emit_candidate(sv, cand, q, (s + i) | (static_cast<uint64_t>(r) << 32), lane);
+            }
     }
 }
 
@@ -574,19 +623,25 @@ __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
     if (owned && !owned[c]) return;
     const uint32_t s = ix.cl_start[c];
     const uint32_t n = ix.cl_size[c];
-    const float *L = sv.lows + sv.vg_off[pi];
+    const float4 *L4 = reinterpret_cast<const float4 *>(sv.lows + sv.vg_off[pi]);
     const float T0 = sv.T0[q];
     const int S = sv.keep;
     uint32_t cnt = 0;
     uint64_t mn = kKeyMax;
-#pragma unroll 4
-    for (uint32_t i = lane; i < n; i += 32) {
-        const float l = __ldg(L + i);
-        if (l < T0) {
-            ++cnt;
-            const uint64_t key = make_key(l, s + i);
-            mn = key < mn ? key : mn;
-        }
+    for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
+        float l[4 * kLowsUnroll];
+        load_lows4(L4, n, b4 + lane, T0, l);
+#pragma unroll
+        for (int t = 0; t < kLowsUnroll; ++t)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float lv = l[4 * t + e];
+                if (lv < T0) {
+                    ++cnt;
+                    const uint64_t key = make_key(lv, s + 4 * (b4 + lane + 32 * t) + e);
+                    mn = key < mn ? key : mn;
+                }
+            }
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
@@ -595,23 +650,21 @@ __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
     if (total > static_cast<uint32_t>(S)) tau = __shfl_sync(0xffffffffu, warp_sort_lane_keys(mn, lane), S - 1);
     uint64_t *b = buf[w];
     uint32_t m = 0;
-    for (uint32_t base = 0; base < n; base += 32 * kLowsUnroll) {
-        float l[kLowsUnroll];
+    for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
+        float l[4 * kLowsUnroll];
+        load_lows4(L4, n, b4 + lane, T0, l);
 #pragma unroll
-        for (int t = 0; t < kLowsUnroll; ++t) {
-            const uint32_t i = base + 32 * t + lane;
-            l[t] = i < n ? __ldg(L + i) : T0;
-        }
+        for (int t = 0; t < kLowsUnroll; ++t)
 #pragma unroll
-        for (int t = 0; t < kLowsUnroll; ++t) {
-            const uint32_t i = base + 32 * t + lane;
-            const uint64_t key = make_key(l[t], s + i);
-            const bool take = (l[t] < T0) && key <= tau;
-            const uint32_t mask = __ballot_sync(0xffffffffu, take);
-            const uint32_t pos = m + __popc(mask & ((1u << lane) - 1u));
-            if (take && pos < static_cast<uint32_t>(kWarpSelectBuf)) b[pos] = key;
-            m += __popc(mask);
-        }
+            for (int e = 0; e < 4; ++e) {
+                const float lv = l[4 * t + e];
+                const uint64_t key = make_key(lv, s + 4 * (b4 + lane + 32 * t) + e);
+                const bool take = (lv < T0) && key <= tau;
+                const uint32_t mask = __ballot_sync(0xffffffffu, take);
+                const uint32_t pos = m + __popc(mask & ((1u << lane) - 1u));
+                if (take && pos < static_cast<uint32_t>(kWarpSelectBuf)) b[pos] = key;
+                m += __popc(mask);
+            }
     }
     if (m > static_cast<uint32_t>(sv.warp_select_limit)) {
         if (lane == 0) fallback[1 + atomicAdd(fallback, 1u)] = static_cast<uint32_t>(pi);
@@ -698,7 +751,7 @@ __global__ void __launch_bounds__(kScanThreads) vanguard_rescan_kernel(
             const uint4 fr = sb[G16 * TV + i];
             const float4 f = make_float4(__uint_as_float(fr.x), __uint_as_float(fr.y),
                                          __uint_as_float(fr.z), 0.0f);
-            const int ip = ip_int_from_planes<G16>(code, s_planes);
+            const int ip = ip_int_from_planes<G16>(code, s_planes, code_bias<G16>(code));
             const float ip1 = __fadd_rn(__fmul_rn(qs.width, (float)ip), 0.0f);
             const float low = lower_bound_dist(f, ip1, g, qs.k1, gerr);
             if (low < T0) {
