@@ -456,9 +456,11 @@ def main():
     # refine, merge; with stored vanguard lows also vanguard grouping (4), lows offsets, lows
     # scan, seed selection (warp + block fallback when keep <= 32) and the lows filter, else
     # one vanguard rescan; +2 exchange steps (gather_threshold / gather_merge) when sharded.
+    # (threshold and final top-k: warp kernel + block fallback each when k <= 32)
     sel = 2 if chosen <= 32 else 1
     vsel = 2 if max(k, 20) <= 32 else 1
-    per_search = 11 + sel + ((7 + vsel) if mode == 1 else 1) + (2 if world > 1 else 0)
+    topk = 2 if k <= 32 else 1
+    per_search = 9 + sel + 2 * topk + ((7 + vsel) if mode == 1 else 1) + (2 if world > 1 else 0)
     launches = per_search * args.steps
 
     cpu_base = None

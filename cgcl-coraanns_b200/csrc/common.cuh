@@ -120,6 +120,16 @@ __device__ __forceinline__ void block_bitonic_sort(uint64_t *a, int n) {
     }
 }
 
+// Inclusive prefix sum over the lanes of a full warp.
+__device__ __forceinline__ uint32_t warp_inclusive_sum(uint32_t v, int lane) {
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const uint32_t o = __shfl_up_sync(0xffffffffu, v, off);
+        if (lane >= off) v += o;
+    }
+    return v;
+}
+
 // ---- warp-wide bitonic sorts of uint64 keys -----------------------------------------------
 // One key per lane, returned ascending by lane index.
 __device__ __forceinline__ uint64_t warp_sort_lane_keys(uint64_t v, int lane) {

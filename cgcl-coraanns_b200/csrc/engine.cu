@@ -248,6 +248,7 @@ struct Engine {
     // worst cases fall back to rescanning the vanguard clusters.
     uint64_t lows_budget = 16ull << 30;
     int warp_select_limit = kWarpSelectBuf;  // see vanguard_select_warp_kernel
+    int topk_warp_limit = kWarpTopBuf;       // see topk_warp_kernel
 
     // workspace
     bool ws_ready = false;
@@ -587,6 +588,7 @@ struct Engine {
     void enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uint32_t *d_oi,
                       uint64_t *topk_keys_out);
     void enqueue_final(const uint64_t *topk_recv, int world, float *d_od, uint32_t *d_oi);
+    void launch_topk(int mode, float *d_od, uint32_t *d_oi, uint64_t *keys_out, cudaStream_t st);
     IndexView index_view() const;
     SearchView search_view() const;
     ScanLaunch scan_launch(const IndexView &ix, const SearchView &sv, cudaStream_t st) const;
@@ -784,7 +786,7 @@ SearchView Engine::search_view() const {
                       static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
                       scal.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p,
                       cand_cnt.p, seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n,
-                      lows_top.p, err.p, warp_select_limit};
+                      lows_top.p, err.p, warp_select_limit, topk_warp_limit};
 }
 
 void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, float *d_od,
@@ -875,16 +877,43 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
         CUDA_TRY(cudaGetLastError());
     }
     mark(6, st);
-    const size_t refine_sm = (size_t)D * 4 + np * sizeof(ProbeInfo);
+    const size_t refine_sm = (size_t)D * 8 + np * sizeof(ProbeInfo);  // query as doubles
     CUDA_TRY(cudaFuncSetAttribute(refine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)refine_sm));
     refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 0);
     CUDA_TRY(cudaGetLastError());
     mark(7, st);
-    const size_t sel_sm = (size_t)next_pow2(static_cast<int>(k)) * 8;
+    launch_topk(0, nullptr, nullptr, seed_keys_out, st);
+}
+
+// Threshold (mode 0) or final top-k (mode 1): one warp per query for k <= 32 (the queries
+// whose candidate collection overflows go on to the block kernel through select_fallback,
+// free at this point), else one CTA per query.
+void Engine::launch_topk(int mode, float *d_od, uint32_t *d_oi, uint64_t *keys_out,
+                         cudaStream_t st) {
+    const SearchView sv = search_view();
+    const unsigned inq = static_cast<unsigned>(last_nq);
+    const size_t sel_sm = (size_t)next_pow2(static_cast<int>(last_k)) * 8;
     CUDA_TRY(cudaFuncSetAttribute(threshold_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)sel_sm));
-    threshold_kernel<<<inq, 256, sel_sm, st>>>(sv, seed_keys_out);
+    CUDA_TRY(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)sel_sm));
+    if (last_k <= 32) {
+        CUDA_TRY(cudaMemsetAsync(select_fallback.p, 0, 4, st));
+        topk_warp_kernel<<<(inq + 7) / 8, 256, 0, st>>>(sv, mode, d_od, d_oi, stats.p, keys_out,
+                                                          select_fallback.p);
+        CUDA_TRY(cudaGetLastError());
+        const unsigned grid = static_cast<unsigned>(2 * num_sms);
+        if (mode == 0)
+            threshold_kernel<<<grid, 256, sel_sm, st>>>(sv, keys_out, select_fallback.p);
+        else
+            merge_kernel<<<grid, 256, sel_sm, st>>>(sv, d_od, d_oi, nullptr, keys_out,
+                                                     select_fallback.p);
+    } else if (mode == 0) {
+        threshold_kernel<<<inq, 256, sel_sm, st>>>(sv, keys_out, nullptr);
+    } else {
+        merge_kernel<<<inq, 256, sel_sm, st>>>(sv, d_od, d_oi, stats.p, keys_out, nullptr);
+    }
     CUDA_TRY(cudaGetLastError());
 }
 
@@ -951,15 +980,12 @@ void Engine::enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uin
     }
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));
     mark(11, st);
-    const size_t refine_sm = (size_t)D * 4 + last_np * sizeof(ProbeInfo);
+    const size_t refine_sm = (size_t)D * 8 + last_np * sizeof(ProbeInfo);  // query as doubles
     refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 1);
     CUDA_TRY(cudaGetLastError());
     mark(12, st);
     // 5. final top-k
-    CUDA_TRY(cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)sel_sm));
-    merge_kernel<<<inq, 256, sel_sm, st>>>(sv, d_od, d_oi, stats.p, topk_keys_out);
-    CUDA_TRY(cudaGetLastError());
+    launch_topk(1, d_od, d_oi, topk_keys_out, st);
 }
 
 // Sharded search, last step: the top-k over every shard's k best keys in topk_recv.
@@ -1446,6 +1472,10 @@ int cora_set_tuning(cora_engine *engine, const char *key, int64_t value) {
             if (value < 0 || value > cora::kWarpSelectBuf)
                 cora::fail(CORA_EINVAL, "warp_select_limit must be in [0, 256]");
             e.warp_select_limit = static_cast<int>(value);
+        } else if (k == "topk_warp_limit") {
+            if (value < 0 || value > cora::kWarpTopBuf)
+                cora::fail(CORA_EINVAL, "topk_warp_limit must be in [0, 256]");
+            e.topk_warp_limit = static_cast<int>(value);
         } else if (k == "vanguard_lows_budget") {
             if (value < 0) cora::fail(CORA_EINVAL, "vanguard_lows_budget must be >= 0");
             if (e.ws_ready) cora::fail(CORA_ESTATE, "set the lows budget before prepare_workspace");

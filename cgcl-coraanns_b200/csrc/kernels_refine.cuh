@@ -28,24 +28,50 @@ struct ProbeInfo {  // per (query, probe rank), staged in shared memory by refin
 // ex-code bytes (pack_excode.hpp:216-264 layout: bytes 0..47 carry the low 6 bits of dims
 // 0..47 and 2-bit slices of dims 48..63, bytes 48..55 the top bits), w0 / w1 the 1-bit
 // code words of dims 0..31 / 32..63, x the block's 64 rotated query values.
-__device__ __forceinline__ double block_code_ip(const float *__restrict__ x, const uint64_t (&e)[7],
-                                                uint32_t w0, uint32_t w1, double acc) {
+//
+// The 8-bit codes c = 128 b + u are decoded four dimensions at a time into the bytes of a
+// word (SWAR), and each byte becomes the double c exactly as (2^52 + c) - 2^52 from its bit
+// pattern, so the loop runs no int or float conversion instructions; x holds the query as
+// doubles (exact widening of the fp32 values).
+__device__ __forceinline__ uint32_t code4(const uint32_t (&ew)[14], uint32_t rbits, int d0) {
+    uint32_t low;
+    if (d0 < 48) {
+        low = ew[d0 / 4] & 0x3F3F3F3Fu;  // low 6 bits of dims d0..d0+3 = bytes d0..d0+3
+    } else {                             // dims 48 + k: top 2 bits of bytes k, 16 + k, 32 + k
+        const int t = (d0 - 48) / 4;
+        low = ((ew[t] >> 6) & 0x03030303u) | ((ew[4 + t] >> 4) & 0x0C0C0C0Cu) |
+              ((ew[8 + t] >> 2) & 0x30303030u);
+    }
+    // bit 6: dim 8k + m sits at bit 8m + k of bytes 48..55 (word 12 for m < 4, else 13)
+    const int k = d0 >> 3;
+    const uint32_t top = ((ew[12 + ((d0 & 7) >> 2)] >> k) & 0x01010101u) << 6;
+    // bit 7: the 1-bit code, dim d at bit (d & 31) of the bit-reversed word; spread the four
+    // bits of dims d0..d0+3 to bit 7 of bytes 0..3 (the shifted copies do not overlap)
+    const uint32_t nib = (rbits >> (d0 & 31)) & 0xFu;
+    const uint32_t msb = (nib * 0x10204080u) & 0x80808080u;
+    return low | top | msb;
+}
+
+__device__ __forceinline__ double block_code_ip(const double *__restrict__ x,
+                                                const uint64_t (&e)[7], uint32_t w0, uint32_t w1,
+                                                double acc) {
+    uint32_t ew[14];
 #pragma unroll
-    for (int d = 0; d < 64; ++d) {
-        uint32_t u;
-        if (d < 48) {
-            u = static_cast<uint32_t>(e[d >> 3] >> (8 * (d & 7))) & 63u;
-        } else {
-            const int k = d - 48;
-            const uint32_t b0 = static_cast<uint32_t>(e[k >> 3] >> (8 * (k & 7))) & 0xFFu;
-            const uint32_t b1 = static_cast<uint32_t>(e[(16 + k) >> 3] >> (8 * ((16 + k) & 7))) & 0xFFu;
-            const uint32_t b2 = static_cast<uint32_t>(e[(32 + k) >> 3] >> (8 * ((32 + k) & 7))) & 0xFFu;
-            u = (b0 >> 6) | ((b1 >> 6) << 2) | ((b2 >> 6) << 4);
+    for (int t = 0; t < 7; ++t) {
+        ew[2 * t] = static_cast<uint32_t>(e[t]);
+        ew[2 * t + 1] = static_cast<uint32_t>(e[t] >> 32);
+    }
+    const uint32_t r0 = __brev(w0), r1 = __brev(w1);
+#pragma unroll
+    for (int d0 = 0; d0 < 64; d0 += 4) {
+        const uint32_t c4 = code4(ew, d0 < 32 ? r0 : r1, d0);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t c = __byte_perm(c4, 0u, 0x4440u | i);
+            const double cd = __dsub_rn(__hiloint2double(0x43300000, static_cast<int>(c)),
+                                        4503599627370496.0);
+            acc = __fma_rn(x[d0 + i], cd, acc);
         }
-        u |= static_cast<uint32_t>((e[6] >> (8 * (d & 7) + (d >> 3))) & 1ull) << 6;
-        const uint32_t w = d < 32 ? w0 : w1;
-        const uint32_t bit = (w >> (31 - (d & 31))) & 1u;
-        acc = __fma_rn((double)x[d], (double)(128u * bit + u), acc);
     }
     return acc;
 }
@@ -58,7 +84,7 @@ __device__ __forceinline__ double block_code_ip(const float *__restrict__ x, con
 __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, SearchView sv,
                                                                 int mode) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    float *x = reinterpret_cast<float *>(smem_raw);
+    double *x = reinterpret_cast<double *>(smem_raw);
     ProbeInfo *pinfo = reinterpret_cast<ProbeInfo *>(x + ix.D);
     const int q = blockIdx.x;
     const uint32_t cnt = sv.cand_cnt[q];
@@ -73,7 +99,8 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
         to = min(cnt, cap);
     }
     if (from >= to) return;  // uniform across the block
-    for (int j = threadIdx.x; j < ix.D; j += blockDim.x) x[j] = sv.qr[(size_t)q * ix.D + j];
+    for (int j = threadIdx.x; j < ix.D; j += blockDim.x)
+        x[j] = static_cast<double>(sv.qr[(size_t)q * ix.D + j]);
     const int np = mode == 0 ? sv.veff : sv.nprobe;
     for (int r = threadIdx.x; r < np; r += blockDim.x) {
         const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
@@ -136,11 +163,26 @@ __device__ __forceinline__ void write_topk(const uint64_t *s_keys, int q, int k,
 // smallest seed keys (padded with kKeyMax) to keys_out[q * k ..] instead, for the exchange;
 // gather_threshold_kernel then derives T1 from every shard's keys. Dynamic shared memory:
 // next_pow2(k) keys.
+// With `list`, the CTAs serve the queries list[1 .. list[0]] (grid-stride) that
+// topk_warp_kernel handed over.
+__device__ void threshold_block(int q, const SearchView &sv, uint64_t *__restrict__ keys_out,
+                                uint64_t *s_keys, int *scratch);
 __global__ void __launch_bounds__(256) threshold_kernel(SearchView sv,
-                                                        uint64_t *__restrict__ keys_out) {
+                                                        uint64_t *__restrict__ keys_out,
+                                                        const uint32_t *__restrict__ list) {
     extern __shared__ uint64_t s_keys[];
     __shared__ int scratch[256 + 3];
-    const int q = blockIdx.x;
+    if (!list) {
+        threshold_block(blockIdx.x, sv, keys_out, s_keys, scratch);
+        return;
+    }
+    for (uint32_t j = blockIdx.x; j < list[0]; j += gridDim.x) {
+        threshold_block(static_cast<int>(list[1 + j]), sv, keys_out, s_keys, scratch);
+        __syncthreads();
+    }
+}
+__device__ void threshold_block(int q, const SearchView &sv, uint64_t *__restrict__ keys_out,
+                                uint64_t *s_keys, int *scratch) {
     const float T0 = sv.T0[q];
     const uint32_t n = sv.seed_cnt[q];
     const uint64_t *keys = sv.cand_key + (size_t)q * sv.cap;
@@ -162,13 +204,30 @@ __global__ void __launch_bounds__(256) threshold_kernel(SearchView sv,
 // (write_topk). Sharded search: writes this shard's k best keys to keys_out[q * k ..] and,
 // from block 0, the shard's device error word to keys_out[nq * k], for the exchange that
 // gather_merge_kernel completes. Dynamic shared memory: next_pow2(k).
+// With `list`, as threshold_kernel; stats == nullptr skips the count (already added).
+__device__ void merge_block(int q, const SearchView &sv, float *__restrict__ out_d,
+                            uint32_t *__restrict__ out_i, unsigned long long *__restrict__ stats,
+                            uint64_t *__restrict__ keys_out, uint64_t *s_keys, int *scratch);
 __global__ void __launch_bounds__(256) merge_kernel(SearchView sv, float *__restrict__ out_d,
                                                     uint32_t *__restrict__ out_i,
                                                     unsigned long long *__restrict__ stats,
-                                                    uint64_t *__restrict__ keys_out) {
+                                                    uint64_t *__restrict__ keys_out,
+                                                    const uint32_t *__restrict__ list) {
     extern __shared__ uint64_t s_keys[];
     __shared__ int scratch[256 + 3];
-    const int q = blockIdx.x;
+    if (!list) {
+        merge_block(blockIdx.x, sv, out_d, out_i, stats, keys_out, s_keys, scratch);
+        return;
+    }
+    for (uint32_t j = blockIdx.x; j < list[0]; j += gridDim.x) {
+        merge_block(static_cast<int>(list[1 + j]), sv, out_d, out_i, stats, keys_out, s_keys,
+                    scratch);
+        __syncthreads();
+    }
+}
+__device__ void merge_block(int q, const SearchView &sv, float *__restrict__ out_d,
+                            uint32_t *__restrict__ out_i, unsigned long long *__restrict__ stats,
+                            uint64_t *__restrict__ keys_out, uint64_t *s_keys, int *scratch) {
     const float T0 = sv.T0[q];
     const uint32_t cnt = sv.cand_cnt[q];
     const uint32_t n = min(cnt, static_cast<uint32_t>(sv.cap));
@@ -186,7 +245,78 @@ __global__ void __launch_bounds__(256) merge_kernel(SearchView sv, float *__rest
     } else {
         write_topk(s_keys, q, sv.k, T0, out_d, out_i, sv.Tcap);
     }
-    if (threadIdx.x == 0) atomicAdd(stats, static_cast<unsigned long long>(cnt));
+    if (threadIdx.x == 0 && stats) atomicAdd(stats, static_cast<unsigned long long>(cnt));
+}
+
+// ---- warp-level threshold (mode 0) and merge (mode 1) for k <= 32 ----------------------
+// One warp per query (8 per CTA). The k-th smallest of the 32 lane minima bounds the k-th
+// smallest key from above, so the k smallest keys are among those at or below it (normally
+// a few dozen), which are collected and sorted. A query whose collection exceeds
+// kWarpTopBuf is queued in fallback[1..] (count in fallback[0]) for the block kernel.
+constexpr int kWarpTopBuf = 256;
+__global__ void __launch_bounds__(256) topk_warp_kernel(SearchView sv, int mode,
+                                                        float *__restrict__ out_d,
+                                                        uint32_t *__restrict__ out_i,
+                                                        unsigned long long *__restrict__ stats,
+                                                        uint64_t *__restrict__ keys_out,
+                                                        uint32_t *__restrict__ fallback) {
+    __shared__ uint64_t buf[8][kWarpTopBuf];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int q = blockIdx.x * 8 + w;
+    if (q >= sv.nq) return;  // whole warp
+    const float T0 = sv.T0[q];
+    const uint32_t cnt = sv.cand_cnt[q];
+    const uint32_t n = mode == 0 ? sv.seed_cnt[q] : min(cnt, static_cast<uint32_t>(sv.cap));
+    const uint64_t *keys = sv.cand_key + (size_t)q * sv.cap;
+    const int k = sv.k;
+    if (mode == 1 && lane == 0) atomicAdd(stats, static_cast<unsigned long long>(cnt));
+    auto key_at = [&](uint32_t i) -> uint64_t {
+        const uint64_t key = keys[i];
+        return unord_f32(static_cast<uint32_t>(key >> 32)) < T0 ? key : kKeyMax;
+    };
+    uint64_t mn = kKeyMax;
+    for (uint32_t i = lane; i < n; i += 32) {
+        const uint64_t key = key_at(i);
+        mn = key < mn ? key : mn;
+    }
+    const uint64_t tau = __shfl_sync(0xffffffffu, warp_sort_lane_keys(mn, lane), k - 1);
+    uint64_t *b = buf[w];
+    uint32_t m = 0;
+    for (uint32_t base = 0; base < n; base += 32) {
+        const uint32_t i = base + lane;
+        const uint64_t key = i < n ? key_at(i) : kKeyMax;
+        const bool take = key != kKeyMax && key <= tau;
+        const uint32_t mask = __ballot_sync(0xffffffffu, take);
+        const uint32_t pos = m + __popc(mask & ((1u << lane) - 1u));
+        if (take && pos < static_cast<uint32_t>(kWarpTopBuf)) b[pos] = key;
+        m += __popc(mask);
+    }
+    if (m > static_cast<uint32_t>(sv.topk_warp_limit)) {
+        if (lane == 0) fallback[1 + atomicAdd(fallback, 1u)] = static_cast<uint32_t>(q);
+        return;
+    }
+    int sort_n = 32;
+    while (sort_n < static_cast<int>(m)) sort_n <<= 1;
+    for (int i = m + lane; i < sort_n; i += 32) b[i] = kKeyMax;
+    __syncwarp();
+    warp_sort_smem(b, sort_n, lane);
+    const uint64_t kth = b[k - 1];
+    if (keys_out) {
+        for (int j = lane; j < k; j += 32) keys_out[(size_t)q * k + j] = b[j];
+        if (mode == 1 && q == 0 && lane == 0)
+            keys_out[(size_t)sv.nq * k] = static_cast<uint32_t>(*sv.err);
+    } else if (mode == 0) {
+        if (lane == 0) sv.T1[q] = threshold_from_kth(kth, T0);
+    } else {
+        for (int j = lane; j < k; j += 32) {
+            const uint64_t key = b[j];
+            const bool ok = key != kKeyMax;
+            out_d[(size_t)q * k + j] = ok ? unord_f32(static_cast<uint32_t>(key >> 32)) : FLT_MAX;
+            out_i[(size_t)q * k + j] = ok ? static_cast<uint32_t>(key & 0xFFFFFFFFu) : 0u;
+        }
+        if (lane == 0)
+            sv.Tcap[q] = kth != kKeyMax ? unord_f32(static_cast<uint32_t>(kth >> 32)) : T0;
+    }
 }
 
 // ---- shard exchange (cluster-sharded search) -----------------------------------------

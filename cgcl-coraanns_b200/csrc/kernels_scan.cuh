@@ -74,6 +74,7 @@ struct SearchView {
     unsigned long long *lows_top;  // bump allocator of lows slices (zeroed per search)
     int *err;
     int warp_select_limit;       // keys a warp may collect before queueing a block selection
+    int topk_warp_limit;         // the same for the threshold / final top-k (topk_warp_kernel)
 };
 
 // ---- per-cluster query grouping (CSR of (query, probe rank) pairs by cluster) --------
@@ -421,6 +422,9 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
                                : b + (uint64_t)threadIdx.x * lows_slice(static_cast<uint32_t>(n));
                 sv.vg_off[(size_t)q * sv.veff + r] = off;
                 s_bnd[threadIdx.x] = b == ~0ull ? ~0ull : off;
+                if (b != ~0ull)  // the slice's padding reads as +inf (never below a threshold)
+                    for (uint32_t p = n; p < lows_slice(static_cast<uint32_t>(n)); ++p)
+                        sv.lows[off + p] = __int_as_float(0x7f800000);
             } else {
                 s_T1[threadIdx.x] = sv.T1[q];
                 s_bnd[threadIdx.x] = r < sv.veff ? sv.bound[(size_t)q * sv.veff + r] : 0ull;
@@ -554,22 +558,28 @@ __device__ void select_pair_block(const IndexView &ix, const SearchView &sv,
     write_seeds(sv, q, r, s_total, s_keys, s_base_p);
 }
 
-constexpr int kLowsUnroll = 2;  // float4 lows loaded per lane before they are processed
+constexpr int kLowsUnroll = 4;  // float4 lows loaded per lane before they are processed
 
 // Loads lows 4 * (i4 .. i4 + 32 * (kLowsUnroll - 1)) of a slice as float4 (slices are
-// 16-byte aligned and padded to a multiple of 4); entries at or past n read as `fill`.
+// 16-byte aligned and padded with +inf to a multiple of 4); float4s past the slice read as
+// +inf.
 __device__ __forceinline__ void load_lows4(const float4 *__restrict__ L4, uint32_t n,
-                                           uint32_t i4, float fill, float (&l)[4 * kLowsUnroll]) {
+                                           uint32_t i4, float (&l)[4 * kLowsUnroll]) {
+    const float inf = __int_as_float(0x7f800000);
 #pragma unroll
     for (int t = 0; t < kLowsUnroll; ++t) {  // all loads first: one round trip per batch
         const uint32_t j4 = i4 + 32 * t;
-        float4 v = make_float4(fill, fill, fill, fill);
+        float4 v = make_float4(inf, inf, inf, inf);
         if (4 * j4 < n) v = __ldg(L4 + j4);
         l[4 * t + 0] = v.x;
-        l[4 * t + 1] = 4 * j4 + 1 < n ? v.y : fill;
-        l[4 * t + 2] = 4 * j4 + 2 < n ? v.z : fill;
-        l[4 * t + 3] = 4 * j4 + 3 < n ? v.w : fill;
+        l[4 * t + 1] = v.y;
+        l[4 * t + 2] = v.z;
+        l[4 * t + 3] = v.w;
     }
+}
+// Slice index of bit e of a lane's batch mask (element e of load_lows4's array).
+__device__ __forceinline__ uint32_t lows_index(uint32_t b4, int lane, int e) {
+    return 4 * (b4 + lane + 32 * (e >> 2)) + (e & 3);
 }
 
 // One warp per vanguard pair (8 per CTA): candidates low < T1 that are not seeds
@@ -587,18 +597,35 @@ __global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, Sear
     const float4 *L4 = reinterpret_cast<const float4 *>(sv.lows + sv.vg_off[pi]);
     const float T1 = sv.T1[q];
     const uint64_t bnd = sv.bound[(size_t)q * sv.veff + r];
+    const float *L = sv.lows + sv.vg_off[pi];
+    const uint64_t rtag = static_cast<uint64_t>(r) << 32;
     for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
         float l[4 * kLowsUnroll];
-        load_lows4(L4, n, b4 + lane, T1, l);
+        load_lows4(L4, n, b4 + lane, l);
+        uint32_t take = 0;  // bit e: element e of this lane's batch is below T1
 #pragma unroll
-        for (int t = 0; t < kLowsUnroll; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const uint32_t i = 4 * (b4 + lane + 32 * t) + e;
-                const float lv = l[4 * t + e];
-                const bool cand = (lv < T1) && (make_key(lv, s + i) > bnd);
-                emit_candidate(sv, cand, q, (s + i) | (static_cast<uint64_t>(r) << 32), lane);
-            }
+        for (int e = 0; e < 4 * kLowsUnroll; ++e) take |= (l[e] < T1 ? 1u : 0u) << e;
+        // the few elements below T1: drop the seeds (key at or below the boundary)
+        for (uint32_t m = take; m; m &= m - 1) {
+            const int e = __ffs(m) - 1;
+            const uint32_t i = lows_index(b4, lane, e);
+            if (make_key(L[i], s + i) <= bnd) take &= ~(1u << e);
+        }
+        // one warp prefix sum and one slot reservation per batch
+        const uint32_t mine = __popc(take);
+        const uint32_t incl = warp_inclusive_sum(mine, lane);
+        const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+        if (total == 0) continue;
+        uint32_t base = 0;
+        if (lane == 31) base = atomicAdd(sv.cand_cnt + q, total);
+        uint32_t slot = __shfl_sync(0xffffffffu, base, 31) + incl - mine;
+        for (uint32_t m = take; m; m &= m - 1, ++slot) {
+            const uint32_t i = lows_index(b4, lane, __ffs(m) - 1);
+            if (slot < static_cast<uint32_t>(sv.cap))
+                sv.cand_rec[(size_t)q * sv.cap + slot] = (s + i) | rtag;
+            else
+                atomicOr(sv.err, kDevCandidateOverflow);
+        }
     }
 }
 
@@ -626,45 +653,49 @@ __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
     const float4 *L4 = reinterpret_cast<const float4 *>(sv.lows + sv.vg_off[pi]);
     const float T0 = sv.T0[q];
     const int S = sv.keep;
+    // Pass 1: count of lows < T0 and each lane's smallest low. S lanes hold a low <= tau_f
+    // (the S-th smallest lane minimum), so the S smallest keys all have low <= tau_f.
+    const float inf = __int_as_float(0x7f800000);
     uint32_t cnt = 0;
-    uint64_t mn = kKeyMax;
+    float mn = inf;
     for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
         float l[4 * kLowsUnroll];
-        load_lows4(L4, n, b4 + lane, T0, l);
+        load_lows4(L4, n, b4 + lane, l);
 #pragma unroll
-        for (int t = 0; t < kLowsUnroll; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float lv = l[4 * t + e];
-                if (lv < T0) {
-                    ++cnt;
-                    const uint64_t key = make_key(lv, s + 4 * (b4 + lane + 32 * t) + e);
-                    mn = key < mn ? key : mn;
-                }
-            }
+        for (int e = 0; e < 4 * kLowsUnroll; ++e) {
+            const bool below = l[e] < T0;
+            cnt += below ? 1u : 0u;
+            mn = fminf(mn, below ? l[e] : inf);
+        }
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
     const uint32_t total = cnt;
-    uint64_t tau = kKeyMax;
-    if (total > static_cast<uint32_t>(S)) tau = __shfl_sync(0xffffffffu, warp_sort_lane_keys(mn, lane), S - 1);
+    float tau_f = inf;  // every low < T0 is a seed when there are at most S
+    if (total > static_cast<uint32_t>(S))
+        tau_f = unord_f32(static_cast<uint32_t>(
+            __shfl_sync(0xffffffffu, warp_sort_lane_keys(make_key(mn, lane), lane), S - 1) >> 32));
+    // Pass 2: collect every key with low < T0 and low <= tau_f (-0 and +0 compare equal
+    // here, so the set contains every key the exact bound would take)
+    const float *L = sv.lows + sv.vg_off[pi];
     uint64_t *b = buf[w];
     uint32_t m = 0;
     for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
         float l[4 * kLowsUnroll];
-        load_lows4(L4, n, b4 + lane, T0, l);
+        load_lows4(L4, n, b4 + lane, l);
+        uint32_t take = 0;
 #pragma unroll
-        for (int t = 0; t < kLowsUnroll; ++t)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float lv = l[4 * t + e];
-                const uint64_t key = make_key(lv, s + 4 * (b4 + lane + 32 * t) + e);
-                const bool take = (lv < T0) && key <= tau;
-                const uint32_t mask = __ballot_sync(0xffffffffu, take);
-                const uint32_t pos = m + __popc(mask & ((1u << lane) - 1u));
-                if (take && pos < static_cast<uint32_t>(kWarpSelectBuf)) b[pos] = key;
-                m += __popc(mask);
-            }
+        for (int e = 0; e < 4 * kLowsUnroll; ++e)
+            take |= (l[e] < T0 && l[e] <= tau_f ? 1u : 0u) << e;
+        const uint32_t mine = __popc(take);
+        const uint32_t incl = warp_inclusive_sum(mine, lane);
+        const uint32_t got = __shfl_sync(0xffffffffu, incl, 31);
+        uint32_t pos = m + incl - mine;
+        for (uint32_t mm = take; mm; mm &= mm - 1, ++pos) {
+            const uint32_t i = lows_index(b4, lane, __ffs(mm) - 1);
+            if (pos < static_cast<uint32_t>(kWarpSelectBuf)) b[pos] = make_key(L[i], s + i);
+        }
+        m += got;
     }
     if (m > static_cast<uint32_t>(sv.warp_select_limit)) {
         if (lane == 0) fallback[1 + atomicAdd(fallback, 1u)] = static_cast<uint32_t>(pi);

@@ -164,7 +164,8 @@ int cora_set_vanguard_lows_budget(cora_engine *engine, uint64_t bytes);
  *  "vanguard_lows_budget"  same as cora_set_vanguard_lows_budget;
  *  "warp_select_limit"     keys (0..256) one warp may collect while selecting the seeds of
  *                          a vanguard pair before it hands the pair to a block-wide
- *                          selection (0 sends every pair to the block selection). */
+ *                          selection (0 sends every pair to the block selection);
+ *  "topk_warp_limit"       the same for the threshold and final top-k of a query (k <= 32). */
 int cora_set_tuning(cora_engine *engine, const char *key, int64_t value);
 /* 1 when the prepared workspace keeps vanguard lower bounds, 0 when it rescans, -1 on NULL. */
 int cora_get_vanguard_mode(const cora_engine *engine);

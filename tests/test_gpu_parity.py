@@ -26,10 +26,12 @@ def _engine(cb, path=None, sd=None, nq=1, k=10, nprobe=1, vanguard=5, mode="lows
     e.set_vanguard_size(vanguard)
     if mode == "rescan":
         e.set_vanguard_lows_budget(0)
-    if mode == "blocksel":  # every vanguard pair through the block-wide seed selection
+    if mode == "blocksel":  # every pair / query through the block-wide selections
         e.set_tuning("warp_select_limit", 0)
-    if mode == "tightsel":  # the warp selection hands most pairs over
+        e.set_tuning("topk_warp_limit", 0)
+    if mode == "tightsel":  # the warp selections hand most pairs / queries over
         e.set_tuning("warp_select_limit", 8)
+        e.set_tuning("topk_warp_limit", 4)
     if path is not None:
         e.load_index_file(path)
     else:
