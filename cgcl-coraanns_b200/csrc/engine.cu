@@ -981,6 +981,8 @@ void Engine::enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uin
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));
     mark(11, st);
     const size_t refine_sm = (size_t)D * 8 + last_np * sizeof(ProbeInfo);  // query as doubles
+    CUDA_TRY(cudaFuncSetAttribute(refine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)refine_sm));
     refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 1);
     CUDA_TRY(cudaGetLastError());
     mark(12, st);

@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
     const float kb = sv.scal[q].kb;
     const int nblocks = ix.D / 64;
     const size_t planes_per = static_cast<size_t>(ix.G16 + 1);
+    const bool v16 = (ix.LC & 15) == 0;  // ex-code rows 16-byte aligned (D % 128 == 0)
     for (uint32_t i = from + threadIdx.x; i < to; i += blockDim.x) {
         const uint64_t rec = sv.cand_rec[(size_t)q * sv.cap + i];
         const uint32_t gid = static_cast<uint32_t>(rec & 0xFFFFFFFFu);
@@ -121,15 +122,29 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
         double acc = 0.0;
         for (int g = 0; 2 * g < nblocks; ++g) {
             const uint4 cw = __ldg(cb + (size_t)g * p.size);
-            uint64_t e[7];
+            uint64_t e[14];
+            if (v16 && 2 * g + 1 < nblocks) {
+                // a full 128-dim group is 112 bytes: seven 16-byte loads (rows 16-byte aligned)
+                const uint4 *e4 = reinterpret_cast<const uint4 *>(eb + 14 * g);
 #pragma unroll
-            for (int t = 0; t < 7; ++t) e[t] = __ldg(eb + 14 * g + t);
-            acc = block_code_ip(x + 128 * g, e, cw.x, cw.y, acc);
-            if (2 * g + 1 < nblocks) {
+                for (int t = 0; t < 7; ++t) {
+                    const uint4 v = __ldg(e4 + t);
+                    e[2 * t] = (uint64_t(v.y) << 32) | v.x;
+                    e[2 * t + 1] = (uint64_t(v.w) << 32) | v.z;
+                }
+            } else {
 #pragma unroll
-                for (int t = 0; t < 7; ++t) e[t] = __ldg(eb + 14 * g + 7 + t);
-                acc = block_code_ip(x + 128 * g + 64, e, cw.z, cw.w, acc);
+                for (int t = 0; t < 14; ++t)
+                    e[t] = (t < 7 || 2 * g + 1 < nblocks) ? __ldg(eb + 14 * g + t) : 0ull;
             }
+            uint64_t lo[7], hi[7];
+#pragma unroll
+            for (int t = 0; t < 7; ++t) {
+                lo[t] = e[t];
+                hi[t] = e[7 + t];
+            }
+            acc = block_code_ip(x + 128 * g, lo, cw.x, cw.y, acc);
+            if (2 * g + 1 < nblocks) acc = block_code_ip(x + 128 * g + 64, hi, cw.z, cw.w, acc);
         }
         const float ex_d = __fadd_rn(__fadd_rn(f.x, p.g),
                                      __fmul_rn(f.y, __fadd_rn(__double2float_rn(acc), kb)));
