@@ -17,12 +17,14 @@ public host API (cora_search: pinned host queries -> HBM -> results back to host
 compiled from the reference source into oracle/_ref) on the same index with every host
 thread, on a bounded query sample per step.
 
-Multi-GPU (torchrun, one process per GPU): the index is sharded by IVF cluster
-(coraanns_b200.shard); every rank probes all centroids and scans the clusters it owns; the
-shards' vanguard seed keys (-> the global pruning threshold) and then their top-k keys are
-exchanged by NCCL all-gathers and merged on every rank. All ranks answer the same 10K queries
-together, so the total work is fixed as N grows (strong scaling) and `value` is queries/s of
-the whole job.
+Multi-GPU (torchrun, one process per GPU): N GPUs form N / S copies of the index, each copy
+cluster-sharded over S GPUs (coraanns_b200.shard: every shard probes all centroids and scans
+the clusters it owns; the shards' vanguard seed keys, which give the global pruning
+threshold, and then their top-k keys are exchanged by NCCL all-gathers and merged). The
+copies answer disjoint slices of the 10K-query batch. S defaults to the fewest GPUs whose
+memory holds the index (1 for config 2: every GPU holds a full copy and no collective runs on
+the data path); `--shards S` forces cluster sharding. The batch is fixed as N grows (strong
+scaling) and `value` is queries/s of the whole job.
 """
 from __future__ import annotations
 
@@ -237,6 +239,40 @@ def cpu_reference_qps(index_path, q_np, k, nprobe, target_seconds=15.0, threads=
                        f"{dt:.1f} s"), run
 
 
+_OUT_FD = None
+
+
+def redirect_stdout():
+    """Route everything libraries print to stdout (e.g. NCCL's version banner) to stderr,
+    so that the result line is the only thing on stdout."""
+    global _OUT_FD
+    sys.stdout.flush()
+    _OUT_FD = os.dup(1)
+    os.dup2(2, 1)
+
+
+def emit(line: dict):
+    data = (json.dumps(line) + "\n").encode()
+    if _OUT_FD is None:
+        sys.stdout.write(data.decode())
+        sys.stdout.flush()
+    else:
+        os.write(_OUT_FD, data)
+
+
+def auto_shards(sd, world, dev) -> int:
+    """Fewest GPUs per copy of the index that keep a copy under half of one GPU's memory
+    (the rest is workspace); 1 when the index fits, so every GPU holds a full copy."""
+    import torch
+    n, D = int(sd["num"]), int(sd["D"])
+    index_bytes = n * (D // 8 + 12 + D * 7 // 8 + 8 + 4) + int(sd["nlist"]) * D * 4
+    budget = torch.cuda.get_device_properties(dev).total_memory // 2
+    for s in range(1, world + 1):
+        if world % s == 0 and index_bytes // s <= budget:
+            return s
+    return world
+
+
 # ------------------------------------------------------------------------------------
 # main
 # ------------------------------------------------------------------------------------
@@ -249,7 +285,10 @@ def main():
     ap.add_argument("--config", choices=sorted(CONFIGS), default="cfg2")
     ap.add_argument("--nprobe", type=int, default=0, help="fix nprobe instead of sweeping")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--shards", type=int, default=0,
+                    help="GPUs per copy of the index (cluster shards); 0 = as memory requires")
     args = ap.parse_args()
+    redirect_stdout()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
 
@@ -318,41 +357,63 @@ def main():
                                 nprobe=nprobe, recall_at_10=rec, sample_queries=m),
                     cpu_baseline=dict(base_info, value=v),
                     e2e=dict(value=v, unit="queries/s", h2d_bytes_per_step=0, d2h_bytes_per_step=0))
-        print(json.dumps(line), flush=True)
+        emit(line)
         if world > 1:
             dist.destroy_process_group()
         return
 
-    nq = cfg["nq"]
+    nq_total = cfg["nq"]
     nprobes = [args.nprobe] if args.nprobe else cfg["nprobes"]
+    # Multi-GPU layout: `shards` GPUs hold one copy of the index (cluster-sharded when > 1)
+    # and world // shards such copies answer disjoint slices of the query batch. By default
+    # the index is sharded only as far as memory requires (config 2 fits one GPU many times
+    # over, so every GPU holds a full copy).
+    shards = args.shards or auto_shards(sd, world, dev)
+    if world % shards:
+        raise SystemExit(f"--shards {shards} does not divide {world} GPUs")
+    replicas = world // shards
+    rep, srank = rank // shards, rank % shards
+    lo, hi = nq_total * rep // replicas, nq_total * (rep + 1) // replicas
+    nq = hi - lo
+    qs = q[lo:hi].contiguous()
     # A dedicated (non-default) stream: the engine enqueues every kernel of a search on it and
     # the timing events are recorded on it too. torch's default stream is the legacy NULL
     # stream, which the engine's non-blocking streams do not order against.
     stream = torch.cuda.Stream(dev)
     out_d = torch.empty((nq, k), dtype=torch.float32, device=dev)
     out_i = torch.empty((nq, k), dtype=torch.int32, device=dev)
-    if world > 1:
+    owner = None
+    if shards > 1:
         # cluster-sharded: this rank keeps the clusters the shard plan gives it
         from coraanns_b200.shard import ShardedIndex, shard_plan
-        six = ShardedIndex(local)
+        groups = [dist.new_group(list(range(g * shards, (g + 1) * shards)))
+                  for g in range(replicas)]
+        six = ShardedIndex(local, group=groups[rep])
         six.load_search_data(sd)
         six.prepare_workspace(nq, k, max(nprobes))
         eng = six.engine
-        owner = shard_plan(sd["sizes"], world)
+        owner = shard_plan(sd["sizes"], shards)
 
         def search_dev(nprobe):
             with torch.cuda.stream(stream):
-                six.search_device(q, k, nprobe, out_d, out_i)
+                six.search_device(qs, k, nprobe, out_d, out_i)
     else:
         eng = cb.HybridIndex(local)
         eng.load_search_data(sd)
         eng.prepare_workspace(nq, k, max(nprobes))
-        owner = None
 
         def search_dev(nprobe):
-            eng.search_device(q.data_ptr(), nq, k, nprobe, out_d.data_ptr(), out_i.data_ptr(),
+            eng.search_device(qs.data_ptr(), nq, k, nprobe, out_d.data_ptr(), out_i.data_ptr(),
                               stream.cuda_stream)
     torch.cuda.synchronize()
+
+    def total(x, op=None):
+        """Sum (or max) of a scalar over every rank."""
+        if world == 1:
+            return x
+        t = torch.tensor([float(x)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=op or dist.ReduceOp.SUM)
+        return float(t.item())
 
     sweep = {}
     chosen = None
@@ -360,7 +421,10 @@ def main():
         search_dev(npb)
         torch.cuda.synchronize()
         eng.check_device()
-        r = recall_at_k(base, q, gt_ids, gt_d, out_i.cpu().numpy().view(np.uint32), k)
+        r = recall_at_k(base, qs, gt_ids[lo:hi], gt_d[lo:hi],
+                        out_i.cpu().numpy().view(np.uint32), k)
+        # every shard of a replica holds the same result: count each replica once
+        r = total(r * nq if srank == 0 else 0.0) / nq_total
         sweep[npb] = round(r, 4)
         if chosen is None and r >= TARGET_RECALL:
             chosen = npb
@@ -373,15 +437,10 @@ def main():
     torch.cuda.synchronize()
     eng.check_device()
     probes = eng.debug("probe_ids", nq, chosen)
-    submitted = eng.get_last_submitted_count()
-    if world > 1:
-        t = torch.tensor([submitted], dtype=torch.int64, device=dev)
-        dist.all_reduce(t)
-        submitted = int(t.item())
-    cand_per_query = submitted / nq
+    cand_per_query = total(eng.get_last_submitted_count()) / nq_total
     sizes = sd["sizes"].astype(np.int64)
     if owner is not None:  # this rank scans only the clusters it owns
-        sizes = np.where(owner == rank, sizes, 0)
+        sizes = np.where(owner == srank, sizes, 0)
     D = int(sd["D"])
     scan_bytes = int(sizes[probes].sum()) * (D // 8 + 12)
 
@@ -402,22 +461,17 @@ def main():
         ev1.record(stream)
         torch.cuda.synchronize()
     eng.check_device()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    ms = total(ev0.elapsed_time(ev1) / args.steps, dist.ReduceOp.MAX if world > 1 else None)
     count, stage_tot = eng.stage_totals()
     stage_avg = {s: v / max(count, 1) for s, v in stage_tot.items()}
     eng.set_profiling(False)
-    # every rank answers the same nq queries together (each scans its own clusters)
-    qps = nq / (ms / 1e3)
+    qps = nq_total / (ms / 1e3)  # the whole batch, answered by all replicas together
 
     # ---- e2e through the public host API (pinned host queries, results to host) ----
     qh = torch.empty((nq, cfg["dim"]), dtype=torch.float32, pin_memory=True)
-    qh.copy_(q.cpu())
+    qh.copy_(qs.cpu())
     qh_np = qh.numpy()
-    if world > 1:
+    if shards > 1:
         host_search = lambda: six.search(qh_np, k, chosen)  # noqa: E731
     else:
         eng.reset_buffer(qh_np)
@@ -429,12 +483,9 @@ def main():
     t = time.perf_counter()
     for _ in range(args.steps):
         host_search()
-    e2e_s = (time.perf_counter() - t) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_s], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e_qps = nq / e2e_s
+    e2e_s = total((time.perf_counter() - t) / args.steps,
+                  dist.ReduceOp.MAX if world > 1 else None)
+    e2e_qps = nq_total / e2e_s
 
     peak, peak_src = measured_peaks()
     # The 1-bit scan of one search is two passes of scan_kernel (vanguard pairs, then the
@@ -442,31 +493,40 @@ def main():
     # is every probed (query, cluster) pair once.
     scan_ms = stage_avg["vanguard_scan"] + stage_avg["main_scan"]
     achieved = scan_bytes / (scan_ms / 1e3) / 1e9 if scan_ms > 0 else None
-    traffic = profiled_traffic()
+    traffic = profiled_traffic() if world == 1 else None
     roofline = dict(bound="hbm", kernel="scan_kernel (vanguard + main passes)", achieved=achieved,
                     peak=peak, unit="GB/s", frac=(achieved / peak) if achieved else None,
                     traffic=traffic, peak_source=peak_src,
                     algorithmic_bytes_per_launch=scan_bytes, launch_ms=scan_ms,
                     note="bytes = sum over (query, probe) of n_c*(D/8+12) (per-query accounting "
                          "of codes touched; cross-query reuse lets this exceed the physical DRAM "
-                         "traffic)")
+                         "traffic); rank 0's launches")
     mode = eng.get_vanguard_mode()
     # Kernels per search: rotation, probe GEMM, probe selection (warp kernel + its block
     # fallback when nprobe <= 32), seed refine, threshold, main grouping (4), main scan,
-    # refine, merge; with stored vanguard lows also vanguard grouping (4), lows offsets, lows
-    # scan, seed selection (warp + block fallback when keep <= 32) and the lows filter, else
-    # one vanguard rescan; +2 exchange steps (gather_threshold / gather_merge) when sharded.
-    # (threshold and final top-k: warp kernel + block fallback each when k <= 32)
+    # refine, merge (threshold and final top-k: warp kernel + block fallback each when
+    # k <= 32); with stored vanguard lows also vanguard grouping (4), lows scan, seed
+    # selection (warp + block fallback when keep <= 32) and the lows filter, else one vanguard
+    # rescan; +2 exchange steps (gather_threshold / gather_merge) when sharded.
     sel = 2 if chosen <= 32 else 1
     vsel = 2 if max(k, 20) <= 32 else 1
     topk = 2 if k <= 32 else 1
-    per_search = 9 + sel + 2 * topk + ((7 + vsel) if mode == 1 else 1) + (2 if world > 1 else 0)
+    per_search = (9 + sel + 2 * topk + ((6 + vsel) if mode == 1 else 1)
+                  + (2 if shards > 1 else 0))
     launches = per_search * args.steps
 
     cpu_base = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and index_path is not None:
         cpu_base, _ = cpu_reference_qps(index_path, q_np, k, chosen, target_seconds=15.0)
 
+    if world == 1:
+        parallelism = "single"
+    elif shards == 1:
+        parallelism = (f"query-parallel x{replicas} (each GPU holds the whole index and answers "
+                       f"{nq} of the {nq_total} queries; no collective on the data path)")
+    else:
+        parallelism = (f"{replicas} replica(s) x {shards} cluster shards (NCCL all-gather of "
+                       f"seed and top-k keys within each replica)")
     if rank == 0:
         line = dict(
             metric="QPS at recall@10>=0.95 (IVF-RaBitQ search)", value=qps, unit="queries/s",
@@ -474,19 +534,18 @@ def main():
             higher_is_better=True, scaling="strong", vs_baseline=None,
             dtype="u32+f32", data="synthetic (seeded Gaussian mixture, BASELINE config 2 shape)",
             config=dict(workload=f"{args.config}: {cfg['n']} x d{cfg['dim']} L2, nlist {cfg['nlist']}, "
-                                 f"8-bit RaBitQ, {nq} queries, topk {k}",
+                                 f"8-bit RaBitQ, {nq_total} queries, topk {k}",
                         nprobe=chosen, recall_at_10=sweep.get(chosen), recall_sweep=sweep,
                         candidates_per_query=cand_per_query,
                         vanguard_mode="lows" if mode == 1 else "rescan",
                         l2_flush="inputs exceed L2 (index codes > 126 MB)",
-                        stage_ms=stage_avg,
-                        parallelism=(f"cluster-sharded x{world} (NCCL all-gather of seed and "
-                                     f"top-k keys)") if world > 1 else "single"),
+                        stage_ms=stage_avg, shards=shards, replicas=replicas,
+                        parallelism=parallelism),
             roofline=roofline, cpu_baseline=cpu_base,
             e2e=dict(value=e2e_qps, unit="queries/s", h2d_bytes_per_step=nq * cfg["dim"] * 4,
                      d2h_bytes_per_step=nq * k * 8),
             gpu_launches=launches, clocks=clk.summary())
-        print(json.dumps(line), flush=True)
+        emit(line)
     eng.close()
     if index_path is not None and index_path.exists():
         index_path.unlink()

@@ -723,7 +723,7 @@ size_t rescan_smem(int sort_n) {
 template <int G16>
 size_t scan_smem() {
     using Sh = ScanShape<G16>;
-    return 2 * Sh::kStageEntries * 16 + (size_t)kMaxPairsPerItem * 8 * Sh::W4 * 4;
+    return (size_t)Sh::kStages * Sh::kStageEntries * 16 + (size_t)kMaxPairsPerItem * 8 * Sh::W4 * 4;
 }
 
 template <int G16, bool kLows>
@@ -919,7 +919,7 @@ void Engine::launch_topk(int mode, float *d_od, uint32_t *d_oi, uint64_t *keys_o
 
 ScanLaunch Engine::scan_launch(const IndexView &ix, const SearchView &sv, cudaStream_t st) const {
     const uint64_t keep = std::max<uint64_t>(last_k, kVanguardMinKeep);
-    const int rescan_sort_n = next_pow2(static_cast<int>(keep) + (G16 <= 2 ? 512 : 256));
+    const int rescan_sort_n = next_pow2(static_cast<int>(keep) + 256 /* ScanShape::TV */);
     return ScanLaunch{ix, sv, rescan_sort_n, last_nq * vanguard_depth(last_np), items.p, n_items.p,
                       pairs.p, item_counter.p, owned.n ? owned.p : nullptr, num_sms, st};
 }

@@ -34,7 +34,10 @@ constexpr int kMaxPairsPerItem = 32;
 
 template <int G16>
 struct ScanShape {
-    static constexpr int TV = G16 <= 2 ? 512 : 256;   // vectors per staged tile
+    static constexpr int TV = 256;                     // vectors per staged tile
+    // tiles in flight in scan_kernel (its shared memory: kStages x kStageEntries x 16 B);
+    // deep enough to hide the TMA latency when an item serves few queries
+    static constexpr int kStages = G16 <= 2 ? 4 : 2;
     static constexpr int W4 = 4 * G16;                 // 32-bit code words per vector
     static constexpr int kStageEntries = (G16 + 1) * TV;
 };
@@ -354,11 +357,11 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
     const uint32_t *__restrict__ n_items_ptr, const uint32_t *__restrict__ pairs,
     int *__restrict__ item_counter) {
     using Sh = ScanShape<G16>;
-    constexpr int TV = Sh::TV, W4 = Sh::W4;
+    constexpr int TV = Sh::TV, W4 = Sh::W4, S = Sh::kStages;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint4 *stage = reinterpret_cast<uint4 *>(smem_raw);
-    uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + 2 * Sh::kStageEntries);
-    __shared__ __align__(8) uint64_t bars[2];
+    uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + S * Sh::kStageEntries);
+    __shared__ __align__(8) uint64_t bars[S];
     __shared__ uint64_t s_bnd[kMaxPairsPerItem];
     __shared__ float s_T1[kMaxPairsPerItem], s_g[kMaxPairsPerItem], s_k1[kMaxPairsPerItem],
         s_w[kMaxPairsPerItem], s_gerr[kMaxPairsPerItem];
@@ -367,15 +370,14 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
     __shared__ unsigned long long s_lbase;  // lows pass: this item's slices (~0ull: no room)
 
     if (threadIdx.x == 0) {
-        mbar_init(&bars[0], 1);
-        mbar_init(&bars[1], 1);
+        for (int i = 0; i < S; ++i) mbar_init(&bars[i], 1);
         fence_barrier_init();
         s_abort = 0;
     }
     __syncthreads();
     const uint32_t n_items = *n_items_ptr;
     const int lane = threadIdx.x & 31;
-    uint32_t phase[2] = {0, 0};
+    uint32_t phase = 0;  // bit i: parity of the next phase of bars[i]
     while (true) {
         if (threadIdx.x == 0) s_item = atomicAdd(item_counter, 1);
         __syncthreads();
@@ -388,8 +390,10 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
         const int pc = static_cast<int>(item.pair_count);
         const size_t cbase = (size_t)(G16 + 1) * s;
         const int ntiles = (n + TV - 1) / TV;
-        if (threadIdx.x == 0 && ntiles > 0)
-            issue_tile<G16>(stage, &bars[0], ix.scan4, cbase, n, 0, min(TV, n));
+        if (threadIdx.x == 0)  // the first S - 1 tiles go out at once
+            for (int u = 0; u < S - 1 && u < ntiles; ++u)
+                issue_tile<G16>(stage + u * Sh::kStageEntries, &bars[u], ix.scan4, cbase, n,
+                                u * TV, min(TV, n - u * TV));
         if (kWriteLows) {
             if (threadIdx.x == 0) {
                 const unsigned long long need =
@@ -438,15 +442,24 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
         }
         __syncthreads();
         for (int t = 0; t < ntiles; ++t) {
-            const int b = t & 1;
+            const int b = t % S;
             const int v0 = t * TV, tv = min(TV, n - v0);
-            if (!mbar_wait_bounded(&bars[b], phase[b], sv.err)) s_abort = 1;
-            phase[b] ^= 1;
+            if (!mbar_wait_bounded(&bars[b], (phase >> b) & 1u, sv.err)) s_abort = 1;
+            phase ^= 1u << b;
             __syncthreads();
-            if (s_abort) return;
-            if (threadIdx.x == 0 && t + 1 < ntiles)
-                issue_tile<G16>(stage + (b ^ 1) * Sh::kStageEntries, &bars[b ^ 1], ix.scan4, cbase,
-                                n, v0 + TV, min(TV, n - v0 - TV));
+            if (s_abort) {
+                // let the copies still in flight (tiles t .. t + S - 2) land before exiting
+                if (threadIdx.x == 0)
+                    for (int u = t; u < t + S - 1 && u < ntiles; ++u)
+                        mbar_wait_bounded(&bars[u % S], ((phase >> (u % S)) & 1u) ^ (u == t),
+                                          sv.err);
+                return;
+            }
+            if (threadIdx.x == 0 && t + S - 1 < ntiles) {  // into the slot tile t - 1 freed
+                const int u = t + S - 1;
+                issue_tile<G16>(stage + (u % S) * Sh::kStageEntries, &bars[u % S], ix.scan4,
+                                cbase, n, u * TV, min(TV, n - u * TV));
+            }
             const uint4 *sb = stage + b * Sh::kStageEntries;
             // every thread evaluates V vectors of the tile against each query in turn, so a
             // query's planes are read from shared memory once per V vectors
