@@ -287,6 +287,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shards", type=int, default=0,
                     help="GPUs per copy of the index (cluster shards); 0 = as memory requires")
+    ap.add_argument("--queries", type=int, default=0,
+                    help="search only the first N queries of the batch (profiling a GPU's "
+                         "slice of a multi-GPU run); 0 = the whole batch")
     args = ap.parse_args()
     redirect_stdout()
     if args.warmup < 3 and args.impl == "ours":
@@ -313,6 +316,9 @@ def main():
 
     t0 = time.time()
     centres, base, q = make_data(cfg, dev)
+    if args.queries:
+        cfg = dict(cfg, nq=min(args.queries, cfg["nq"]))
+        q = q[:cfg["nq"]].contiguous()
     cent, lab = kmeans(base, centres)
     if world > 1:
         # every shard must cut the same partition: take rank 0's
