@@ -198,14 +198,15 @@ def measured_peaks():
     return 6650.0, "fallback (6.65 TB/s)"
 
 
-def profiled_traffic():
-    """Per-launch DRAM bytes of the main scan kernel from the committed ncu summary."""
-    p = ROOT / "profiles" / "scan_main_cfg2.json"
-    if p.exists():
-        try:
-            return json.loads(p.read_text()).get("dram_bytes_per_launch_full_size")
-        except ValueError:
-            return None
+def profiled_traffic(config):
+    """DRAM bytes (read + write) of the two scan launches of one search, from the committed
+    ncu summary of the full-size config-2 workload (None for other configs)."""
+    p = ROOT / "profiles" / "scan_kernel_cfg2_dram.md"
+    if config != "cfg2" or not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_search_full_size:"):
+            return int(line.split(":")[1])
     return None
 
 
@@ -343,7 +344,19 @@ def main():
         log(f"[bench] index file {index_path.stat().st_size / 1e9:.2f} GB in {time.time() - t2:.1f}s")
 
     if args.impl == "reference":
-        nprobe = args.nprobe or 32
+        # the reference's own operating point: the smallest nprobe of the sweep whose
+        # recall@10 on a 1000-query sample reaches the target (the rule the GPU arm uses)
+        nprobe = args.nprobe
+        if not nprobe:
+            import py_oracle as po
+            ivf = po.RefIVF(index_path) if po.ref_available() else po.oracle_from_file(index_path)
+            ms = min(1000, len(q_np))
+            for npb in cfg["nprobes"]:
+                ids = ivf.search(q_np[:ms], k, npb, threads=os.cpu_count())
+                ids = ids[1] if isinstance(ids, tuple) else ids
+                nprobe = npb
+                if recall_at_k(base, q[:ms], gt_ids[:ms], gt_d[:ms], ids, k) >= TARGET_RECALL:
+                    break
         base_info, run = cpu_reference_qps(index_path, q_np, k, nprobe, target_seconds=4.0)
         m = int(base_info["sample"].split()[0])
         for _ in range(args.warmup):
@@ -499,7 +512,7 @@ def main():
     # is every probed (query, cluster) pair once.
     scan_ms = stage_avg["vanguard_scan"] + stage_avg["main_scan"]
     achieved = scan_bytes / (scan_ms / 1e3) / 1e9 if scan_ms > 0 else None
-    traffic = profiled_traffic() if world == 1 else None
+    traffic = profiled_traffic(args.config) if world == 1 else None
     roofline = dict(bound="hbm", kernel="scan_kernel (vanguard + main passes)", achieved=achieved,
                     peak=peak, unit="GB/s", frac=(achieved / peak) if achieved else None,
                     traffic=traffic, peak_source=peak_src,
