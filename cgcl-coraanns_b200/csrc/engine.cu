@@ -143,9 +143,12 @@ inline uint64_t approx_ld(uint64_t nlist) { return (nlist + 3) & ~uint64_t(3); }
 
 // approx[q * ld + c] = ||q'||^2 + ||c||^2 - 2 <q', c> for every query and centroid, on the
 // tensor cores (probe_gemm_kernel; persistent, one CTA per SM at most).
+inline uint64_t chunk_count(uint64_t nlist) { return (nlist + 31) / 32; }
+
 inline void launch_probe_gemm(const float *qr, const float *qnorm2, uint64_t nq, uint64_t D,
                               const float *cent, const float *cnorm2, uint64_t nlist,
-                              float *approx, int num_sms, cudaStream_t st, int *err) {
+                              float *approx, float *chunk_min, int num_sms, cudaStream_t st,
+                              int *err) {
     const CUtensorMap tq = map_f32_2d(qr, D, nq, D, kPgBK, kPgBM);
     const CUtensorMap tc = map_f32_2d(cent, D, nlist, D, kPgBK, kPgBN);
     const CUtensorMap to = map_f32_2d(approx, nlist, nq, approx_ld(nlist), 32, kPgBM);
@@ -156,17 +159,18 @@ inline void launch_probe_gemm(const float *qr, const float *qnorm2, uint64_t nq,
     const unsigned grid = static_cast<unsigned>(std::min<uint64_t>(tiles, (uint64_t)num_sms));
     probe_gemm_kernel<<<grid, kPgThreads, sm, st>>>(tq, tc, to, qnorm2, cnorm2,
                                                     static_cast<int>(nq), static_cast<int>(nlist),
-                                                    static_cast<int>(D), err);
+                                                    static_cast<int>(D), chunk_min, err);
     CUDA_TRY(cudaGetLastError());
 }
 
 // Exact top-nprobe from the approximate distances: one warp per query when nprobe <= 32
 // (queries whose candidate set overflows go on to the block kernel through `fallback`,
 // 1 + nq words), else one CTA per query.
-inline void launch_guarded_select(float *approx, uint64_t nlist, uint64_t nq, uint64_t nprobe,
-                                  const float *qr, const float *qnorm2, const float *cent,
-                                  float cmax, uint64_t D, int *probe_ids, float *probe_g,
-                                  uint32_t *fallback, int num_sms, cudaStream_t st) {
+inline void launch_guarded_select(float *approx, const float *chunk_min, uint64_t nlist,
+                                  uint64_t nq, uint64_t nprobe, const float *qr,
+                                  const float *qnorm2, const float *cent, float cmax, uint64_t D,
+                                  int *probe_ids, float *probe_g, uint32_t *fallback, int num_sms,
+                                  cudaStream_t st) {
     const int inq = static_cast<int>(nq), inp = static_cast<int>(nprobe), iD = static_cast<int>(D);
     const int ccap = guarded_select_cap(inp);
     const size_t bsm = guarded_select_smem(inp, ccap, iD);
@@ -179,8 +183,8 @@ inline void launch_guarded_select(float *approx, uint64_t nlist, uint64_t nq, ui
         CUDA_TRY(cudaMemsetAsync(fallback, 0, 4, st));
         guarded_select_warp_kernel<<<static_cast<unsigned>((nq + kGuardWarps - 1) / kGuardWarps),
                                      32 * kGuardWarps, wsm, st>>>(
-            approx, static_cast<int>(nlist), approx_ld(nlist), inq, inp, qr, qnorm2, cent, cmax,
-            iD, kApproxEpsTF32, probe_ids, probe_g, fallback);
+            approx, chunk_min, static_cast<int>(nlist), approx_ld(nlist), inq, inp, qr, qnorm2,
+            cent, cmax, iD, kApproxEpsTF32, probe_ids, probe_g, fallback);
         CUDA_TRY(cudaGetLastError());
         guarded_select_kernel<<<static_cast<unsigned>(2 * num_sms), 256, bsm, st>>>(
             approx, static_cast<int>(nlist), approx_ld(nlist), inp, ccap, qr, qnorm2, cent, cmax,
@@ -253,7 +257,7 @@ struct Engine {
     // workspace
     bool ws_ready = false;
     uint64_t ws_q = 0, ws_k = 0, ws_np = 0, ws_vg = 0, cap = 0;
-    DevBuf<float> raw_q, qr, qnorm2, gmat, probe_g, T0, T1, Tcap, out_d;
+    DevBuf<float> raw_q, qr, qnorm2, gmat, cmin, probe_g, T0, T1, Tcap, out_d;
     DevBuf<QueryScalars> scal;
     DevBuf<uint32_t> planes, cand_cnt, seed_cnt, pair_cnt, pair_off, pair_cur, item_off, pairs,
         n_items, out_i;
@@ -350,8 +354,11 @@ struct Engine {
                 mx = std::max(mx, std::sqrt(s2));
             }
             cmax = std::nextafter(static_cast<float>(mx), FLT_MAX);
-            cnorm2.alloc(nlist);
-            CUDA_TRY(cudaMemcpy(cnorm2.p, cn.data(), nlist * 4, cudaMemcpyHostToDevice));
+            // zero-padded to a multiple of the probe GEMM's 256-column tile (its epilogue reads
+            // whole 32-column chunks as float4)
+            cn.resize((nlist + 255) / 256 * 256, 0.0f);
+            cnorm2.alloc(cn.size());
+            CUDA_TRY(cudaMemcpy(cnorm2.p, cn.data(), cn.size() * 4, cudaMemcpyHostToDevice));
         }
         CUDA_TRY(cudaMemcpy(rotator.p, h_rotator, dim * D * 4, cudaMemcpyHostToDevice));
         cl_start.alloc(nlist);
@@ -471,6 +478,7 @@ struct Engine {
         scal.alloc(max_q);
         planes.alloc(max_q * 8 * W4);
         gmat.alloc(max_q * approx_ld(nlist));
+        cmin.alloc(max_q * chunk_count(nlist));
         qnorm2.alloc(max_q);
         probe_ids.alloc(max_q * max_np);
         probe_g.alloc(max_q * max_np);
@@ -516,7 +524,7 @@ struct Engine {
     void free_workspace() noexcept {
         ws_ready = false;
         ws_q = ws_k = ws_np = ws_vg = cap = 0;
-        for (auto *b : {&raw_q, &qr, &qnorm2, &gmat, &probe_g, &T0, &T1, &Tcap, &out_d})
+        for (auto *b : {&raw_q, &qr, &qnorm2, &gmat, &cmin, &probe_g, &T0, &T1, &Tcap, &out_d})
             b->release();
         scal.release();
         for (auto *b : {&planes, &cand_cnt, &seed_cnt, &pair_cnt, &pair_off, &pair_cur, &item_off,
@@ -829,12 +837,12 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
     // 2. coarse probing: approximate distances for every (query, centroid), then the exact
     //    top-nprobe among the guarded candidates
     {
-        launch_probe_gemm(qr.p, qnorm2.p, nq, D, centroids.p, cnorm2.p, nlist, gmat.p, num_sms,
-                          st, err.p);
+        launch_probe_gemm(qr.p, qnorm2.p, nq, D, centroids.p, cnorm2.p, nlist, gmat.p, cmin.p,
+                          num_sms, st, err.p);
         mark(2, st);
         // select_fallback (>= 1 + nq words) is free until the vanguard stage
-        launch_guarded_select(gmat.p, nlist, nq, np, qr.p, qnorm2.p, centroids.p, cmax, D,
-                              probe_ids.p, probe_g.p, select_fallback.p, num_sms, st);
+        launch_guarded_select(gmat.p, cmin.p, nlist, nq, np, qr.p, qnorm2.p, centroids.p, cmax,
+                              D, probe_ids.p, probe_g.p, select_fallback.p, num_sms, st);
     }
     mark(3, st);
     const bool lows_mode = lows.n > 0;
@@ -1536,7 +1544,7 @@ unsigned char *g_noalloc_ptr[kNoallocMaxDevices] = {};
 inline size_t align256(size_t b) { return (b + 255) & ~size_t{255}; }
 
 struct NoallocLayout {
-    size_t status, qr, qnorm2, scal, planes, approx, fallback, total;
+    size_t status, qr, qnorm2, scal, planes, approx, chunk_min, fallback, total;
 };
 
 NoallocLayout noalloc_layout(uint64_t nq, uint64_t D, uint64_t W4, uint64_t nlist) {
@@ -1547,7 +1555,8 @@ NoallocLayout noalloc_layout(uint64_t nq, uint64_t D, uint64_t W4, uint64_t nlis
     l.scal = l.qnorm2 + align256(nq * sizeof(float));
     l.planes = l.scal + align256(nq * sizeof(QueryScalars));
     l.approx = l.planes + align256(nq * 8 * W4 * sizeof(uint32_t));
-    l.fallback = l.approx + align256(nq * approx_ld(nlist) * sizeof(float));
+    l.chunk_min = l.approx + align256(nq * approx_ld(nlist) * sizeof(float));
+    l.fallback = l.chunk_min + align256(nq * chunk_count(nlist) * sizeof(float));
     l.total = l.fallback + align256((nq + 1) * sizeof(uint32_t));
     return l;
 }
@@ -1613,9 +1622,10 @@ int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num
                                                    static_cast<int>(e.D), e.W4, e.rotator.p, c_b,
                                                    qr, scal, planes, qnorm2);
         CUDA_TRY(cudaGetLastError());
+        float *cmin = reinterpret_cast<float *>(s + l.chunk_min);
         cora::launch_probe_gemm(qr, qnorm2, num_queries, e.D, e.centroids.p, e.cnorm2.p, e.nlist,
-                                approx, e.num_sms, st, status);
-        cora::launch_guarded_select(approx, e.nlist, num_queries, nprobe, qr, qnorm2,
+                                approx, cmin, e.num_sms, st, status);
+        cora::launch_guarded_select(approx, cmin, e.nlist, num_queries, nprobe, qr, qnorm2,
                                     e.centroids.p, e.cmax, e.D, d_probe_ids, d_probe_dists,
                                     reinterpret_cast<uint32_t *>(s + l.fallback), e.num_sms, st);
         (void)inp;

@@ -20,7 +20,10 @@
 //              MMAs (M 128, N 256, K 8) from one lane; tcgen05.commit frees stages and
 //              publishes accumulators;
 //   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, apply the norms, stage the
-//              128 x 32 block in shared memory (128-byte swizzle) and TMA-store it.
+//              128 x 32 block in shared memory (128-byte swizzle) and TMA-store it; with
+//              chunk_min, also each row's minimum over every 32-column chunk
+//              (chunk_min[(c / 32) * nq + q]), which lets the selection read only the
+//              chunks that can hold a probe.
 // Every wait is bounded (kDevWaitTimeout on expiry) and the CTA always drains its copies and
 // MMAs and frees its TMEM before it exits.
 #pragma once
@@ -148,7 +151,8 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
 __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_c,
     const __grid_constant__ CUtensorMap tm_out, const float *__restrict__ qnorm2,
-    const float *__restrict__ cnorm2, int nq, int nlist, int D, int *err) {
+    const float *__restrict__ cnorm2, int nq, int nlist, int D, float *__restrict__ chunk_min,
+    int *err) {
     extern __shared__ unsigned char pg_smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(pg_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -268,18 +272,31 @@ __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
                 if (et == 0) bulk_wait_group_read1();  // this buffer's previous store is read
                 named_barrier_sync(1, 128);
                 unsigned char *ob = sOut + obuf * kPgOutBuf + row * 128;
+                // cnorm2 is zero-padded to a multiple of 256: whole-chunk vector loads are safe
+                const float4 *cn4 = reinterpret_cast<const float4 *>(cnorm2 + c0);
+                float cmin = __int_as_float(0x7f800000);  // min over the chunk's columns
+                const bool full = c0 + 32 <= nlist;
 #pragma unroll
                 for (int ch = 0; ch < 8; ++ch) {
+                    const float4 cn = __ldg(cn4 + ch);
                     float4 o;
-                    float *po = reinterpret_cast<float *>(&o);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int c = c0 + ch * 4 + e;
-                        const float cn = c < nlist ? __ldg(cnorm2 + c) : 0.0f;
-                        po[e] = __fsub_rn(__fadd_rn(qn, cn), __fmul_rn(2.0f, v[ch * 4 + e]));
+                    o.x = __fsub_rn(__fadd_rn(qn, cn.x), __fmul_rn(2.0f, v[ch * 4 + 0]));
+                    o.y = __fsub_rn(__fadd_rn(qn, cn.y), __fmul_rn(2.0f, v[ch * 4 + 1]));
+                    o.z = __fsub_rn(__fadd_rn(qn, cn.z), __fmul_rn(2.0f, v[ch * 4 + 2]));
+                    o.w = __fsub_rn(__fadd_rn(qn, cn.w), __fmul_rn(2.0f, v[ch * 4 + 3]));
+                    if (full) {
+                        cmin = fminf(cmin, fminf(fminf(o.x, o.y), fminf(o.z, o.w)));
+                    } else {  // the row's last, partial chunk: padded columns stay out
+                        const int c = c0 + ch * 4;
+                        if (c < nlist) cmin = fminf(cmin, o.x);
+                        if (c + 1 < nlist) cmin = fminf(cmin, o.y);
+                        if (c + 2 < nlist) cmin = fminf(cmin, o.z);
+                        if (c + 3 < nlist) cmin = fminf(cmin, o.w);
                     }
                     *reinterpret_cast<float4 *>(ob + ((ch ^ (row & 7)) << 4)) = o;
                 }
+                if (chunk_min && ok && q < nq && c0 < nlist)  // chunk-major: coalesced over q
+                    chunk_min[(size_t)(c0 / 32) * nq + q] = cmin;
                 fence_proxy_async_smem();
                 named_barrier_sync(1, 128);
                 if (et == 0 && ok) {

@@ -1,12 +1,13 @@
-// Query preparation and coarse probing kernels.
+// Query preparation and exact probe selection.
 //
-//  rotate_prep_kernel   q' = q * P, sumq / k1 / kb, 8-bit symmetric query bit-planes
-//                       (reference: src/search/hybrid.cu:436-458,
-//                        src/search/query_kernels.cuh:73-94,117-189)
-//  centroid_dist_kernel g_add(q, c) = ||q' - c'||^2 for every (query, centroid)
-//                       (reference: hybrid.cu:465-477, query_kernels.cuh:10-64)
-//  select_probes_kernel top-nprobe by (g_add, cluster id)
-//                       (reference: raft::matrix::select_k, hybrid.cu:485-493)
+//  rotate_prep_kernel          q' = q * P, sumq / k1 / kb, 8-bit symmetric query bit-planes
+//                              (reference: src/search/hybrid.cu:436-458,
+//                               src/search/query_kernels.cuh:73-94,117-189)
+//  guarded_select_warp_kernel  top-nprobe by (g_add, cluster id) from the tensor-core
+//  guarded_select_kernel       approximate distances (kernels_probe.cuh) plus an exact fp64
+//                              recompute of the error band (reference: g_add of
+//                              hybrid.cu:465-477 / query_kernels.cuh:10-64, selected by
+//                              raft::matrix::select_k, hybrid.cu:485-493)
 #pragma once
 #include "common.cuh"
 
@@ -223,11 +224,16 @@ __host__ __device__ inline size_t guarded_select_warp_smem(int D) {
     return kGuardWarps * guarded_select_warp_slice(D);
 }
 
+//
+// The bound and the band come from the per-chunk minima the probe GEMM writes
+// (chunk_min[j * nq + q] = min of columns 32j .. 32j + 31 of row q): lane l's group is
+// its chunks l, l + 32, ..., and only the chunks whose minimum is inside the band are read
+// from the distance row (128 coalesced bytes each), so a row is not read in full.
 __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
-    const float *__restrict__ approx, int nlist, size_t ld, int nq, int nprobe,
-    const float *__restrict__ qr, const float *__restrict__ qnorm2, const float *__restrict__ cent,
-    float cmax, int D, double eps, int *__restrict__ probe_ids, float *__restrict__ probe_g,
-    uint32_t *__restrict__ fallback) {
+    const float *__restrict__ approx, const float *__restrict__ chunk_min, int nlist, size_t ld,
+    int nq, int nprobe, const float *__restrict__ qr, const float *__restrict__ qnorm2,
+    const float *__restrict__ cent, float cmax, int D, double eps, int *__restrict__ probe_ids,
+    float *__restrict__ probe_g, uint32_t *__restrict__ fallback) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int w = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int q = blockIdx.x * kGuardWarps + w;
@@ -235,17 +241,13 @@ __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
     float *x = reinterpret_cast<float *>(smem_raw + w * guarded_select_warp_slice(D));
     uint64_t *keys = reinterpret_cast<uint64_t *>(x + D);  // D % 64 == 0: 8-byte aligned
     uint32_t *cidx = reinterpret_cast<uint32_t *>(keys + kGuardWarpBand);
-    const float *row = approx + (size_t)q * ld;  // ld % 4 == 0: rows are 16-byte aligned
+    const float *row = approx + (size_t)q * ld;
+    const int nchunk = (nlist + 31) / 32;
+    const float *cm = chunk_min + q;  // chunk j at cm[j * nq]
     for (int j = lane; j < D; j += 32) x[j] = qr[(size_t)q * D + j];
 
     float mn = FLT_MAX;
-    for (int c0 = lane * 4; c0 < nlist; c0 += 128) {
-        const float4 v = __ldg(reinterpret_cast<const float4 *>(row + c0));
-        mn = fminf(mn, v.x);
-        if (c0 + 1 < nlist) mn = fminf(mn, v.y);
-        if (c0 + 2 < nlist) mn = fminf(mn, v.z);
-        if (c0 + 3 < nlist) mn = fminf(mn, v.w);
-    }
+    for (int c = lane; c < nchunk; c += 32) mn = fminf(mn, __ldg(cm + (size_t)c * nq));
     const uint64_t kth = __shfl_sync(0xffffffffu,
                                      warp_sort_lane_keys(make_key(mn, lane), lane), nprobe - 1);
     const double tau_ub = (double)unord_f32(static_cast<uint32_t>(kth >> 32));
@@ -253,17 +255,17 @@ __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
     const double bound = tau_ub + 2.0 * (eps * r * r + 1e-30);
 
     uint32_t cnt = 0;
-    for (int base = 0; base < nlist; base += 128) {
-        const int c0 = base + lane * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (c0 < nlist) v = __ldg(reinterpret_cast<const float4 *>(row + c0));
-        const float ve[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const bool take = c0 + e < nlist && (double)ve[e] <= bound;
+    for (int cb = 0; cb < nchunk; cb += 32) {
+        const int c = cb + lane;
+        uint32_t chunks = __ballot_sync(
+            0xffffffffu, c < nchunk && (double)__ldg(cm + (size_t)c * nq) <= bound);
+        while (chunks) {  // warp-uniform: the chunks that can hold a band member
+            const int col = 32 * (cb + __ffs(chunks) - 1) + lane;
+            chunks &= chunks - 1;
+            const bool take = col < nlist && (double)__ldg(row + col) <= bound;
             const uint32_t m = __ballot_sync(0xffffffffu, take);
             const uint32_t pos = cnt + __popc(m & ((1u << lane) - 1u));
-            if (take && pos < kGuardWarpBand) cidx[pos] = static_cast<uint32_t>(c0 + e);
+            if (take && pos < kGuardWarpBand) cidx[pos] = static_cast<uint32_t>(col);
             cnt += __popc(m);
         }
     }
