@@ -120,6 +120,10 @@ __device__ __forceinline__ void block_bitonic_sort(uint64_t *a, int n) {
     }
 }
 
+// Row stride (floats) of the probe GEMM's per-chunk row minima: ceil(nlist / 32) rounded up
+// to a multiple of 8 (8 chunks of 32 columns per 256-column tile).
+__host__ __device__ __forceinline__ int chunk_stride(int nlist) { return (nlist + 255) / 256 * 8; }
+
 // Inclusive prefix sum over the lanes of a full warp.
 __device__ __forceinline__ uint32_t warp_inclusive_sum(uint32_t v, int lane) {
 #pragma unroll

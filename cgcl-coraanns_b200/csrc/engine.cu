@@ -143,8 +143,6 @@ inline uint64_t approx_ld(uint64_t nlist) { return (nlist + 3) & ~uint64_t(3); }
 
 // approx[q * ld + c] = ||q'||^2 + ||c||^2 - 2 <q', c> for every query and centroid, on the
 // tensor cores (probe_gemm_kernel; persistent, one CTA per SM at most).
-inline uint64_t chunk_count(uint64_t nlist) { return (nlist + 31) / 32; }
-
 inline void launch_probe_gemm(const float *qr, const float *qnorm2, uint64_t nq, uint64_t D,
                               const float *cent, const float *cnorm2, uint64_t nlist,
                               float *approx, float *chunk_min, int num_sms, cudaStream_t st,
@@ -478,7 +476,7 @@ struct Engine {
         scal.alloc(max_q);
         planes.alloc(max_q * 8 * W4);
         gmat.alloc(max_q * approx_ld(nlist));
-        cmin.alloc(max_q * chunk_count(nlist));
+        cmin.alloc(max_q * chunk_stride(static_cast<int>(nlist)));
         qnorm2.alloc(max_q);
         probe_ids.alloc(max_q * max_np);
         probe_g.alloc(max_q * max_np);
@@ -1556,7 +1554,7 @@ NoallocLayout noalloc_layout(uint64_t nq, uint64_t D, uint64_t W4, uint64_t nlis
     l.planes = l.scal + align256(nq * sizeof(QueryScalars));
     l.approx = l.planes + align256(nq * 8 * W4 * sizeof(uint32_t));
     l.chunk_min = l.approx + align256(nq * approx_ld(nlist) * sizeof(float));
-    l.fallback = l.chunk_min + align256(nq * chunk_count(nlist) * sizeof(float));
+    l.fallback = l.chunk_min + align256(nq * chunk_stride(static_cast<int>(nlist)) * sizeof(float));
     l.total = l.fallback + align256((nq + 1) * sizeof(uint32_t));
     return l;
 }

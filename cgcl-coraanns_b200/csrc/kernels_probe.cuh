@@ -22,8 +22,8 @@
 //   warps 2-5  epilogue: tcgen05.ld 32 columns at a time, apply the norms, stage the
 //              128 x 32 block in shared memory (128-byte swizzle) and TMA-store it; with
 //              chunk_min, also each row's minimum over every 32-column chunk
-//              (chunk_min[(c / 32) * nq + q]), which lets the selection read only the
-//              chunks that can hold a probe.
+//              (chunk_min[q * chunk_stride(nlist) + c / 32], +inf past nlist), which lets
+//              the selection read only the chunks that can hold a probe.
 // Every wait is bounded (kDevWaitTimeout on expiry) and the CTA always drains its copies and
 // MMAs and frees its TMEM before it exits.
 #pragma once
@@ -260,6 +260,8 @@ __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
             tc_fence_after();
             const int q = m0 + row;
             const float qn = (ok && q < nq) ? __ldg(qnorm2 + q) : 0.0f;
+            float cm8[kPgBN / 32];  // this row's minima of the tile's eight 32-column chunks
+#pragma unroll
             for (int j = 0; j < kPgBN / 32; ++j) {
                 float v[32];
                 if (ok) {
@@ -295,8 +297,7 @@ __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
                     }
                     *reinterpret_cast<float4 *>(ob + ((ch ^ (row & 7)) << 4)) = o;
                 }
-                if (chunk_min && ok && q < nq && c0 < nlist)  // chunk-major: coalesced over q
-                    chunk_min[(size_t)(c0 / 32) * nq + q] = cmin;
+                cm8[j] = cmin;  // +inf for chunks past nlist
                 fence_proxy_async_smem();
                 named_barrier_sync(1, 128);
                 if (et == 0 && ok) {
@@ -304,6 +305,12 @@ __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
                     bulk_commit_group();
                 }
                 obuf ^= 1;
+            }
+            if (chunk_min && ok && q < nq) {  // one full 32-byte sector per row and tile
+                float4 *dst = reinterpret_cast<float4 *>(
+                    chunk_min + (size_t)q * chunk_stride(nlist) + n0 / 32);
+                dst[0] = make_float4(cm8[0], cm8[1], cm8[2], cm8[3]);
+                dst[1] = make_float4(cm8[4], cm8[5], cm8[6], cm8[7]);
             }
             tc_fence_before();
             __syncwarp();

@@ -226,9 +226,9 @@ __host__ __device__ inline size_t guarded_select_warp_smem(int D) {
 
 //
 // The bound and the band come from the per-chunk minima the probe GEMM writes
-// (chunk_min[j * nq + q] = min of columns 32j .. 32j + 31 of row q): lane l's group is
-// its chunks l, l + 32, ..., and only the chunks whose minimum is inside the band are read
-// from the distance row (128 coalesced bytes each), so a row is not read in full.
+// (chunk_min[q * chunk_stride(nlist) + j] = min of row q's columns 32j .. 32j + 31): lane l's
+// group is its chunks l, l + 32, ..., and only the chunks whose minimum is inside the band
+// are read from the distance row (128 coalesced bytes each), so a row is not read in full.
 __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
     const float *__restrict__ approx, const float *__restrict__ chunk_min, int nlist, size_t ld,
     int nq, int nprobe, const float *__restrict__ qr, const float *__restrict__ qnorm2,
@@ -243,11 +243,11 @@ __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
     uint32_t *cidx = reinterpret_cast<uint32_t *>(keys + kGuardWarpBand);
     const float *row = approx + (size_t)q * ld;
     const int nchunk = (nlist + 31) / 32;
-    const float *cm = chunk_min + q;  // chunk j at cm[j * nq]
+    const float *cm = chunk_min + (size_t)q * chunk_stride(nlist);
     for (int j = lane; j < D; j += 32) x[j] = qr[(size_t)q * D + j];
 
     float mn = FLT_MAX;
-    for (int c = lane; c < nchunk; c += 32) mn = fminf(mn, __ldg(cm + (size_t)c * nq));
+    for (int c = lane; c < nchunk; c += 32) mn = fminf(mn, __ldg(cm + c));
     const uint64_t kth = __shfl_sync(0xffffffffu,
                                      warp_sort_lane_keys(make_key(mn, lane), lane), nprobe - 1);
     const double tau_ub = (double)unord_f32(static_cast<uint32_t>(kth >> 32));
@@ -257,8 +257,7 @@ __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
     uint32_t cnt = 0;
     for (int cb = 0; cb < nchunk; cb += 32) {
         const int c = cb + lane;
-        uint32_t chunks = __ballot_sync(
-            0xffffffffu, c < nchunk && (double)__ldg(cm + (size_t)c * nq) <= bound);
+        uint32_t chunks = __ballot_sync(0xffffffffu, c < nchunk && (double)__ldg(cm + c) <= bound);
         while (chunks) {  // warp-uniform: the chunks that can hold a band member
             const int col = 32 * (cb + __ffs(chunks) - 1) + lane;
             chunks &= chunks - 1;
