@@ -294,6 +294,61 @@ __device__ __forceinline__ int ip_int_from_planes(const uint4 (&code)[G16],
     return t - bias;
 }
 
+// ---- the same inner product through byte dot products -------------------------------
+// Code word x_w (dims 32w .. 32w + 31, dim 32w + b at bit 31 - b) is split into eight words
+// of 0/1 bytes, e_{w,s} = (x_w >> s) & 0x01010101: byte m is the bit of dim
+// 32w + 31 - s - 8m. The query word Q_{w,s} holds qint of those four dims as signed bytes,
+// so sum_{w,s} dp4a(e_{w,s}, Q_{w,s}) = sum_i b_i qint_i exactly (int32 accumulation,
+// |sum| <= 128 D). The split is done once per vector and serves every query of the item.
+#ifndef CORA_SCAN_DP4A
+#define CORA_SCAN_DP4A 1
+#endif
+constexpr bool kScanDp4a = CORA_SCAN_DP4A != 0;
+
+// Q_{w,s} of one query from its two's-complement bit-planes (plane j word w at pl[j*W4+w]):
+// bit s + 8m of plane j is bit j of byte m.
+__device__ __forceinline__ uint32_t query_byte_word(const uint32_t *__restrict__ pl, int w,
+                                                    int s, int W4) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v |= ((__ldg(pl + j * W4 + w) >> s) & 0x01010101u) << j;
+    return v;
+}
+
+template <int G16>
+__device__ __forceinline__ void split_code_bytes(const uint4 (&code)[G16],
+                                                 uint32_t (&e)[32 * G16]) {
+#pragma unroll
+    for (int g = 0; g < G16; ++g) {
+        const uint32_t x[4] = {code[g].x, code[g].y, code[g].z, code[g].w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+            for (int s = 0; s < 8; ++s) e[(4 * g + t) * 8 + s] = (x[t] >> s) & 0x01010101u;
+    }
+}
+
+// sum_i b_i qint_i from the split code and one query's byte words Q (Q_{w,s} at Q[8w + s]).
+template <int G16>
+__device__ __forceinline__ int ip_int_from_bytes(const uint32_t (&e)[32 * G16],
+                                                 const uint32_t *__restrict__ Q) {
+    int acc = 0;
+#pragma unroll
+    for (int w = 0; w < 4 * G16; ++w) {
+        const uint4 a = *reinterpret_cast<const uint4 *>(Q + 8 * w);
+        const uint4 b = *reinterpret_cast<const uint4 *>(Q + 8 * w + 4);
+        acc = __dp4a(static_cast<int>(e[8 * w + 0]), static_cast<int>(a.x), acc);
+        acc = __dp4a(static_cast<int>(e[8 * w + 1]), static_cast<int>(a.y), acc);
+        acc = __dp4a(static_cast<int>(e[8 * w + 2]), static_cast<int>(a.z), acc);
+        acc = __dp4a(static_cast<int>(e[8 * w + 3]), static_cast<int>(a.w), acc);
+        acc = __dp4a(static_cast<int>(e[8 * w + 4]), static_cast<int>(b.x), acc);
+        acc = __dp4a(static_cast<int>(e[8 * w + 5]), static_cast<int>(b.y), acc);
+        acc = __dp4a(static_cast<int>(e[8 * w + 6]), static_cast<int>(b.z), acc);
+        acc = __dp4a(static_cast<int>(e[8 * w + 7]), static_cast<int>(b.w), acc);
+    }
+    return acc;
+}
+
 // Copies a query's two's-complement bit-planes into shared memory as offset-binary planes
 // (plane 7 inverted), the form ip_int_from_planes consumes.
 __device__ __forceinline__ uint32_t offset_binary_word(uint32_t w, int word_index, int W4) {
@@ -358,6 +413,9 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
     int *__restrict__ item_counter) {
     using Sh = ScanShape<G16>;
     constexpr int TV = Sh::TV, W4 = Sh::W4, S = Sh::kStages;
+    // query words: byte words for dp4a (the split code is 32 * G16 registers, so only for
+    // D <= 128), offset-binary bit-planes otherwise; both are 8 * W4 words per query
+    constexpr bool kBytes = kScanDp4a && G16 == 1;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint4 *stage = reinterpret_cast<uint4 *>(smem_raw);
     uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + S * Sh::kStageEntries);
@@ -436,9 +494,10 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
         }
         __syncthreads();
         for (int i = threadIdx.x; i < pc * 8 * W4; i += blockDim.x) {
-            const int j = i / (8 * W4);
-            s_planes[i] = offset_binary_word(sv.planes[(size_t)s_q[j] * 8 * W4 + (i - j * 8 * W4)],
-                                             i - j * 8 * W4, W4);
+            const int j = i / (8 * W4), r = i - j * 8 * W4;
+            const uint32_t *pl = sv.planes + (size_t)s_q[j] * 8 * W4;
+            s_planes[i] = kBytes ? query_byte_word(pl, r >> 3, r & 7, W4)
+                                 : offset_binary_word(pl[r], r, W4);
         }
         __syncthreads();
         for (int t = 0; t < ntiles; ++t) {
@@ -468,6 +527,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
                 uint4 code[V][G16];
                 float4 f[V];
                 int bias[V];
+                uint32_t e[V][kBytes ? 32 * G16 : 1];
                 bool valid[V];
 #pragma unroll
                 for (int v = 0; v < V; ++v) {
@@ -482,14 +542,21 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
                         f[v] = make_float4(__uint_as_float(fr.x), __uint_as_float(fr.y),
                                            __uint_as_float(fr.z), 0.0f);
                     }
-                    bias[v] = code_bias<G16>(code[v]);
+                    if constexpr (kBytes)
+                        split_code_bytes<G16>(code[v], e[v]);
+                    else
+                        bias[v] = code_bias<G16>(code[v]);
                 }
                 for (int j = 0; j < pc; ++j) {
                     const uint32_t *P = s_planes + j * 8 * W4;
 #pragma unroll
                     for (int v = 0; v < V; ++v) {
                         const int i = vb + v * kScanThreads + threadIdx.x;
-                        const int ip = ip_int_from_planes<G16>(code[v], P, bias[v]);
+                        int ip;
+                        if constexpr (kBytes)
+                            ip = ip_int_from_bytes<G16>(e[v], P);
+                        else
+                            ip = ip_int_from_planes<G16>(code[v], P, bias[v]);
                         const float ip1 = __fadd_rn(__fmul_rn(s_w[j], (float)ip), 0.0f);
                         const float low =
                             lower_bound_dist(f[v], ip1, s_g[j], s_k1[j], s_gerr[j]);
