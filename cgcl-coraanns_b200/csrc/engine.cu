@@ -238,6 +238,8 @@ struct Engine {
     DevBuf<uint8_t> long_codes;
     DevBuf<float2> ex_factors;
     DevBuf<uint32_t> ids, cl_start, cl_size;
+    DevBuf<uint32_t> cl_chunk;              // first 32-vector chunk of each cluster (nlist + 1)
+    DevBuf<float4> chunk_range, cl_range;   // factor ranges per chunk / per cluster
     DevBuf<uint8_t> owned;  // optional shard ownership mask (all clusters when empty)
 
     // options (hybrid.cuh:66-113)
@@ -257,6 +259,7 @@ struct Engine {
     uint64_t ws_q = 0, ws_k = 0, ws_np = 0, ws_vg = 0, cap = 0;
     DevBuf<float> raw_q, qr, qnorm2, gmat, cmin, probe_g, T0, T1, Tcap, out_d;
     DevBuf<QueryScalars> scal;
+    DevBuf<int2> qrange;
     DevBuf<uint32_t> planes, cand_cnt, seed_cnt, pair_cnt, pair_off, pair_cur, item_off, pairs,
         n_items, out_i;
     DevBuf<int> probe_ids, item_counter, err;
@@ -378,6 +381,17 @@ struct Engine {
         CUDA_TRY(cudaMemcpy(tmp_fac.p, h_short_factors, N * 12, cudaMemcpyHostToDevice));
         scan4.alloc(N * (G16 + 1));
         repack_scan_planes(tmp_short.p, tmp_fac.p);
+        {
+            std::vector<uint32_t> chunk(nlist + 1, 0);
+            for (uint64_t c = 0; c < nlist; ++c) chunk[c + 1] = chunk[c] + (sizes[c] + 31) / 32;
+            cl_chunk.alloc(nlist + 1);
+            CUDA_TRY(cudaMemcpy(cl_chunk.p, chunk.data(), (nlist + 1) * 4, cudaMemcpyHostToDevice));
+            chunk_range.alloc(std::max<uint32_t>(chunk[nlist], 1));
+            cl_range.alloc(nlist);
+            chunk_ranges_kernel<<<static_cast<unsigned>(nlist), 256, 0, stream>>>(
+                scan4.p, cl_start.p, cl_size.p, cl_chunk.p, G16, chunk_range.p, cl_range.p);
+            CUDA_TRY(cudaGetLastError());
+        }
         CUDA_TRY(cudaStreamSynchronize(stream));
         loaded = true;
     }
@@ -474,6 +488,7 @@ struct Engine {
         raw_q.alloc(max_q * dim);
         qr.alloc(max_q * D);
         scal.alloc(max_q);
+        qrange.alloc(max_q);
         planes.alloc(max_q * 8 * W4);
         gmat.alloc(max_q * approx_ld(nlist));
         cmin.alloc(max_q * chunk_stride(static_cast<int>(nlist)));
@@ -525,6 +540,7 @@ struct Engine {
         for (auto *b : {&raw_q, &qr, &qnorm2, &gmat, &cmin, &probe_g, &T0, &T1, &Tcap, &out_d})
             b->release();
         scal.release();
+        qrange.release();
         for (auto *b : {&planes, &cand_cnt, &seed_cnt, &pair_cnt, &pair_off, &pair_cur, &item_off,
                         &pairs, &n_items, &out_i})
             b->release();
@@ -781,7 +797,8 @@ void dispatch_scan(int G16, const ScanLaunch &L, ScanPhase phase) {
 }  // namespace
 
 IndexView Engine::index_view() const {
-    return IndexView{scan4.p, cl_start.p, cl_size.p, long_codes.p, ex_factors.p, ids.p,
+    return IndexView{scan4.p, cl_start.p, cl_size.p, chunk_range.p, cl_chunk.p, cl_range.p,
+                     long_codes.p, ex_factors.p, ids.p,
                      static_cast<int>(nlist), static_cast<int>(D), G16, LC};
 }
 
@@ -790,7 +807,7 @@ SearchView Engine::search_view() const {
     const uint64_t keep = std::max<uint64_t>(last_k, kVanguardMinKeep);
     return SearchView{static_cast<int>(last_nq), static_cast<int>(last_k), static_cast<int>(last_np),
                       static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
-                      scal.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p,
+                      scal.p, qrange.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p,
                       cand_cnt.p, seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n,
                       lows_top.p, err.p, warp_select_limit, topk_warp_limit};
 }
@@ -828,7 +845,7 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
         const float c_b = -static_cast<float>((1u << (ex_bits + 1)) - 1u) / 2.0f;
         rotate_prep_kernel<<<static_cast<unsigned>((nq + kRotQueries - 1) / kRotQueries), 256, sm, st>>>(
             d_q, inq, static_cast<int>(dim), static_cast<int>(D), W4, rotator.p, c_b, qr.p, scal.p,
-            planes.p, qnorm2.p);
+            planes.p, qnorm2.p, qrange.p);
         CUDA_TRY(cudaGetLastError());
     }
     mark(1, st);
@@ -1618,7 +1635,7 @@ int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num
                                                          cora::kRotQueries),
                                    256, rsm, st>>>(d_queries, inq, static_cast<int>(e.dim),
                                                    static_cast<int>(e.D), e.W4, e.rotator.p, c_b,
-                                                   qr, scal, planes, qnorm2);
+                                                   qr, scal, planes, qnorm2, nullptr);
         CUDA_TRY(cudaGetLastError());
         float *cmin = reinterpret_cast<float *>(s + l.chunk_min);
         cora::launch_probe_gemm(qr, qnorm2, num_queries, e.D, e.centroids.p, e.cnorm2.p, e.nlist,

@@ -27,7 +27,7 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
     const float *__restrict__ raw_q, int nq, int dim, int D, int W4,
     const float *__restrict__ rotator, float c_b, float *__restrict__ qr_out,
     QueryScalars *__restrict__ scal_out, uint32_t *__restrict__ planes_out,
-    float *__restrict__ qnorm2_out) {
+    float *__restrict__ qnorm2_out, int2 *__restrict__ qrange_out) {
     extern __shared__ float smem_f[];
     float *sq = smem_f;                       // [kRotQueries][dim]
     float *sr = smem_f + kRotQueries * dim;   // [kRotQueries][D]
@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
         qnorm2_out[q] = (float)nrm;
     }
     uint32_t *pl = planes_out + (size_t)q * 8 * W4;
+    int pos = 0, neg = 0;  // sums of the positive and of the negative qint
     for (int w = 0; w < W4; ++w) {
         const int j = w * 32 + lane;
         int v = 0;
@@ -97,6 +98,8 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
             v = __float2int_rn(__fmul_rn(x[j], inv));
             v = max(-128, min(127, v));
         }
+        pos += max(v, 0);
+        neg += min(v, 0);
         const uint32_t bits = static_cast<uint32_t>(v) & 0xFFu;
 #pragma unroll
         for (int b = 0; b < 8; ++b) {
@@ -104,6 +107,10 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
             if (lane == 0) pl[b * W4 + w] = m;
         }
     }
+    // [neg, pos] is the range of sum_i b_i qint_i over every 1-bit code (the scan's bound)
+    pos = __reduce_add_sync(0xffffffffu, pos);
+    neg = __reduce_add_sync(0xffffffffu, neg);
+    if (qrange_out && lane == 0) qrange_out[q] = make_int2(pos, neg);
 }
 
 // Exact coarse distance of the search contract: g(q, c) = fp32( sum_j fma(d_j, d_j) ) with

@@ -50,6 +50,11 @@ struct IndexView {
     const uint4 *scan4;          // scan planes
     const uint32_t *cl_start;    // nlist
     const uint32_t *cl_size;     // nlist
+    // factor ranges (FactorRange) of every 32-vector chunk of every cluster (cluster c's
+    // chunk j at cl_chunk[c] + j) and of whole clusters (cl_range[c]); see chunk_ranges_kernel
+    const float4 *chunk_range;
+    const uint32_t *cl_chunk;    // nlist + 1
+    const float4 *cl_range;      // nlist
     const uint8_t *long_codes;   // N x LC
     const float2 *ex_factors;    // N
     const uint32_t *ids;         // N
@@ -59,6 +64,7 @@ struct IndexView {
 struct SearchView {
     int nq, k, nprobe, veff, keep, cap;
     const QueryScalars *scal;    // nq
+    const int2 *qrange;          // nq: {sum of positive qint, sum of negative qint}
     const uint32_t *planes;      // nq x 8 x W4
     const float *qr;             // nq x D
     const int *probe_ids;        // nq x nprobe
@@ -176,6 +182,76 @@ __global__ void emit_items_kernel(const uint32_t *__restrict__ cnt,
 // prepare_workspace reserves.
 __host__ __device__ __forceinline__ uint32_t lows_slice(uint32_t n) { return (n + 3u) & ~3u; }
 
+// ---- factor ranges and the lower-bound test that skips whole chunks -------------------
+// A factor range {min f_add, max |f_add|, max |f_rescale|, max |f_error|} over a set of
+// vectors bounds every lower bound the scan computes for them against one pair:
+//   low = fl(fl(fl(f_add + g) + fl(f_rescale * t)) - fl(f_error * gerr)),  |t| <= M,
+// where t = fl(fl(width * ip) + k1) is monotone in ip, so M (its largest magnitude over the
+// reachable ip in [neg, pos]) is taken at an end of that range. Each of the five roundings
+// errs by at most 2^-24 of a magnitude below S = max|f_add| + |g| + max|f_rescale| M +
+// max|f_error| gerr, so low >= L - 2^-20 S with L = min f_add + g - max|f_rescale| M -
+// max|f_error| gerr. When that is >= T, no vector of the set has low < T: skipping it
+// leaves the candidate set unchanged. NaN factors fall out of the min/max (fminf/fmaxf
+// ignore NaN) and their lows (NaN) are never below T either.
+__device__ __forceinline__ bool range_at_least(float4 fr, float g, float M, float gerr,
+                                               float T) {
+    const double r = (double)fr.z * M, e = (double)fr.w * gerr;
+    const double L = ((double)fr.x + g) - r - e;
+    const double S = (double)fr.y + fabs((double)g) + r + e;
+    return L - 0x1p-20 * S >= (double)T;
+}
+
+// M of one pair: the largest |fl(fl(width * ip) + k1)| over ip in [neg, pos] (the scan's
+// evaluation of ip1 + k1, see scan_kernel).
+__device__ __forceinline__ float ip_term_bound(int2 range, float width, float k1) {
+    const float hi = __fadd_rn(__fadd_rn(__fmul_rn(width, (float)range.x), 0.0f), k1);
+    const float lo = __fadd_rn(__fadd_rn(__fmul_rn(width, (float)range.y), 0.0f), k1);
+    return fmaxf(fabsf(hi), fabsf(lo));
+}
+
+// One CTA per cluster: the factor range of each 32-vector chunk (warp-wide reductions) and
+// of the whole cluster. Built once when the index is loaded.
+__global__ void __launch_bounds__(256) chunk_ranges_kernel(const uint4 *__restrict__ scan4,
+                                                           const uint32_t *__restrict__ cl_start,
+                                                           const uint32_t *__restrict__ cl_size,
+                                                           const uint32_t *__restrict__ cl_chunk,
+                                                           int G16, float4 *__restrict__ chunk_range,
+                                                           float4 *__restrict__ cl_range) {
+    __shared__ float4 s_red[8];
+    const int c = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t s = cl_start[c], n = cl_size[c];
+    const float inf = __int_as_float(0x7f800000);
+    float4 acc = make_float4(inf, 0.0f, 0.0f, 0.0f);
+    for (uint32_t k = warp; k * 32 < n; k += 8) {
+        const uint32_t i = k * 32 + lane;
+        float4 v = make_float4(inf, 0.0f, 0.0f, 0.0f);
+        if (i < n) {
+            const uint4 f = scan4[(size_t)(G16 + 1) * s + (size_t)G16 * n + i];
+            const float fa = __uint_as_float(f.x);
+            v = make_float4(fa, fabsf(fa), fabsf(__uint_as_float(f.y)),
+                            fabsf(__uint_as_float(f.z)));
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            v.x = fminf(v.x, __shfl_xor_sync(0xffffffffu, v.x, off));
+            v.y = fmaxf(v.y, __shfl_xor_sync(0xffffffffu, v.y, off));
+            v.z = fmaxf(v.z, __shfl_xor_sync(0xffffffffu, v.z, off));
+            v.w = fmaxf(v.w, __shfl_xor_sync(0xffffffffu, v.w, off));
+        }
+        if (lane == 0) chunk_range[cl_chunk[c] + k] = v;
+        acc = make_float4(fminf(acc.x, v.x), fmaxf(acc.y, v.y), fmaxf(acc.z, v.z),
+                          fmaxf(acc.w, v.w));
+    }
+    if (lane == 0) s_red[warp] = acc;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; ++w)
+            acc = make_float4(fminf(acc.x, s_red[w].x), fmaxf(acc.y, s_red[w].y),
+                              fmaxf(acc.z, s_red[w].z), fmaxf(acc.w, s_red[w].w));
+        cl_range[c] = acc;
+    }
+}
+
 // ---- shared pieces ------------------------------------------------------------------
 template <int G16>
 __device__ __forceinline__ void issue_tile(uint4 *stage_buf, uint64_t *bar, const uint4 *scan4,
@@ -217,6 +293,11 @@ __device__ __forceinline__ void half_add(uint32_t &s, uint32_t &c, uint32_t a, u
 #endif
 constexpr int kCsaLevels = CORA_CSA_LEVELS;
 static_assert(kCsaLevels >= 2 && kCsaLevels <= 8, "adder tree depth");
+// Resident CTAs per SM that scan_kernel's register budget is sized for: 4 (<= 64 registers)
+// for D <= 128, where it was measured 3% faster than 2 or 3 on config 2; 2 above.
+#ifndef CORA_SCAN_MINB
+#define CORA_SCAN_MINB(G16) ((G16) == 1 ? 4 : 2)
+#endif
 // Vectors each scan thread evaluates per pass over a tile's queries.
 #ifndef CORA_SCAN_VPT
 #define CORA_SCAN_VPT 1
@@ -332,21 +413,21 @@ __device__ __forceinline__ void split_code_bytes(const uint4 (&code)[G16],
 template <int G16>
 __device__ __forceinline__ int ip_int_from_bytes(const uint32_t (&e)[32 * G16],
                                                  const uint32_t *__restrict__ Q) {
-    int acc = 0;
+    int acc[4] = {0, 0, 0, 0};  // four independent chains (dp4a latency)
 #pragma unroll
     for (int w = 0; w < 4 * G16; ++w) {
         const uint4 a = *reinterpret_cast<const uint4 *>(Q + 8 * w);
         const uint4 b = *reinterpret_cast<const uint4 *>(Q + 8 * w + 4);
-        acc = __dp4a(static_cast<int>(e[8 * w + 0]), static_cast<int>(a.x), acc);
-        acc = __dp4a(static_cast<int>(e[8 * w + 1]), static_cast<int>(a.y), acc);
-        acc = __dp4a(static_cast<int>(e[8 * w + 2]), static_cast<int>(a.z), acc);
-        acc = __dp4a(static_cast<int>(e[8 * w + 3]), static_cast<int>(a.w), acc);
-        acc = __dp4a(static_cast<int>(e[8 * w + 4]), static_cast<int>(b.x), acc);
-        acc = __dp4a(static_cast<int>(e[8 * w + 5]), static_cast<int>(b.y), acc);
-        acc = __dp4a(static_cast<int>(e[8 * w + 6]), static_cast<int>(b.z), acc);
-        acc = __dp4a(static_cast<int>(e[8 * w + 7]), static_cast<int>(b.w), acc);
+        acc[0] = __dp4a(static_cast<int>(e[8 * w + 0]), static_cast<int>(a.x), acc[0]);
+        acc[1] = __dp4a(static_cast<int>(e[8 * w + 1]), static_cast<int>(a.y), acc[1]);
+        acc[2] = __dp4a(static_cast<int>(e[8 * w + 2]), static_cast<int>(a.z), acc[2]);
+        acc[3] = __dp4a(static_cast<int>(e[8 * w + 3]), static_cast<int>(a.w), acc[3]);
+        acc[0] = __dp4a(static_cast<int>(e[8 * w + 4]), static_cast<int>(b.x), acc[0]);
+        acc[1] = __dp4a(static_cast<int>(e[8 * w + 5]), static_cast<int>(b.y), acc[1]);
+        acc[2] = __dp4a(static_cast<int>(e[8 * w + 6]), static_cast<int>(b.z), acc[2]);
+        acc[3] = __dp4a(static_cast<int>(e[8 * w + 7]), static_cast<int>(b.w), acc[3]);
     }
-    return acc;
+    return (acc[0] + acc[1]) + (acc[2] + acc[3]);
 }
 
 // Copies a query's two's-complement bit-planes into shared memory as offset-binary planes
@@ -405,9 +486,12 @@ __device__ __forceinline__ void write_seeds(const SearchView &sv, int q, int r, 
 // ---- grouped scan: persistent CTAs over (cluster, <= 32 pairs) items -----------------
 // kWriteLows: store every low in the pair's slice of sv.lows (vanguard pass).
 // otherwise:  emit candidates low < T1 (main pass; vanguard seeds are skipped through the
-//             boundary key when vanguard pairs are rescanned).
+//             boundary key when vanguard pairs are rescanned). A pair is dropped from an
+//             item, and from each 32-vector chunk (one warp of a tile), whose factor range
+//             proves every low >= T1 (range_at_least): no tile is loaded for an item that
+//             keeps no pair, and a warp evaluates only the pairs its chunk keeps.
 template <int G16, bool kWriteLows>
-__global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
+__global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel(
     IndexView ix, SearchView sv, const ScanItem *__restrict__ items,
     const uint32_t *__restrict__ n_items_ptr, const uint32_t *__restrict__ pairs,
     int *__restrict__ item_counter) {
@@ -421,10 +505,12 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
     uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + S * Sh::kStageEntries);
     __shared__ __align__(8) uint64_t bars[S];
     __shared__ uint64_t s_bnd[kMaxPairsPerItem];
-    __shared__ float s_T1[kMaxPairsPerItem], s_g[kMaxPairsPerItem], s_k1[kMaxPairsPerItem],
-        s_w[kMaxPairsPerItem], s_gerr[kMaxPairsPerItem];
+    // per pair: {width, g, k1, sqrt(max(g, 0))} (one 16-byte read per evaluation)
+    __shared__ float4 s_par[kMaxPairsPerItem];
+    __shared__ float s_T1[kMaxPairsPerItem], s_M[kMaxPairsPerItem];
     __shared__ int s_q[kMaxPairsPerItem], s_r[kMaxPairsPerItem];
     __shared__ int s_item, s_abort;
+    __shared__ uint32_t s_keep;  // main pass: the item's pairs that some vector may need
     __shared__ unsigned long long s_lbase;  // lows pass: this item's slices (~0ull: no room)
 
     if (threadIdx.x == 0) {
@@ -434,7 +520,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
     }
     __syncthreads();
     const uint32_t n_items = *n_items_ptr;
-    const int lane = threadIdx.x & 31;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t phase = 0;  // bit i: parity of the next phase of bars[i]
     while (true) {
         if (threadIdx.x == 0) s_item = atomicAdd(item_counter, 1);
@@ -448,7 +534,8 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
         const int pc = static_cast<int>(item.pair_count);
         const size_t cbase = (size_t)(G16 + 1) * s;
         const int ntiles = (n + TV - 1) / TV;
-        if (threadIdx.x == 0)  // the first S - 1 tiles go out at once
+        const uint32_t chunk0 = kWriteLows ? 0u : ix.cl_chunk[c];
+        if (kWriteLows && threadIdx.x == 0)  // the first S - 1 tiles go out at once
             for (int u = 0; u < S - 1 && u < ntiles; ++u)
                 issue_tile<G16>(stage + u * Sh::kStageEntries, &bars[u], ix.scan4, cbase, n,
                                 u * TV, min(TV, n - u * TV));
@@ -472,10 +559,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
             const QueryScalars qs = sv.scal[q];
             s_q[threadIdx.x] = q;
             s_r[threadIdx.x] = r;
-            s_g[threadIdx.x] = g;
-            s_k1[threadIdx.x] = qs.k1;
-            s_w[threadIdx.x] = qs.width;
-            s_gerr[threadIdx.x] = __fsqrt_rn(fmaxf(g, 0.0f));
+            s_par[threadIdx.x] = make_float4(qs.width, g, qs.k1, __fsqrt_rn(fmaxf(g, 0.0f)));
             if (kWriteLows) {
                 // slice offset of this vanguard pair, carried in s_bnd (~0: not stored)
                 const unsigned long long b = s_lbase;
@@ -489,10 +573,30 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
                         sv.lows[off + p] = __int_as_float(0x7f800000);
             } else {
                 s_T1[threadIdx.x] = sv.T1[q];
+                s_M[threadIdx.x] = ip_term_bound(sv.qrange[q], qs.width, qs.k1);
                 s_bnd[threadIdx.x] = r < sv.veff ? sv.bound[(size_t)q * sv.veff + r] : 0ull;
             }
         }
         __syncthreads();
+        uint32_t keep = pc == 32 ? ~0u : (1u << pc) - 1u;
+        if (!kWriteLows) {
+            if (warp == 0) {
+                bool need = false;
+                if (lane < pc) {
+                    const float4 pj = s_par[lane];
+                    need = !range_at_least(ix.cl_range[c], pj.y, s_M[lane], pj.w, s_T1[lane]);
+                }
+                const uint32_t m = __ballot_sync(0xffffffffu, need);
+                if (lane == 0) s_keep = m;
+            }
+            __syncthreads();
+            keep = s_keep;
+            if (keep == 0) continue;  // no vector of the cluster can be a candidate
+            if (threadIdx.x == 0)
+                for (int u = 0; u < S - 1 && u < ntiles; ++u)
+                    issue_tile<G16>(stage + u * Sh::kStageEntries, &bars[u], ix.scan4, cbase, n,
+                                    u * TV, min(TV, n - u * TV));
+        }
         for (int i = threadIdx.x; i < pc * 8 * W4; i += blockDim.x) {
             const int j = i / (8 * W4), r = i - j * 8 * W4;
             const uint32_t *pl = sv.planes + (size_t)s_q[j] * 8 * W4;
@@ -520,6 +624,19 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
                                 cbase, n, u * TV, min(TV, n - u * TV));
             }
             const uint4 *sb = stage + b * Sh::kStageEntries;
+            // the pairs this warp's chunk (vectors v0 + 32 warp ..) keeps
+            uint32_t wkeep = keep;
+            if (!kWriteLows) {
+                static_assert(TV == kScanThreads, "one vector per thread: warp w = chunk w");
+                const int k = v0 / 32 + warp;
+                bool need = false;
+                if (k * 32 < n && lane < pc && ((keep >> lane) & 1u)) {
+                    const float4 pj = s_par[lane];
+                    need = !range_at_least(__ldg(ix.chunk_range + chunk0 + k), pj.y, s_M[lane],
+                                           pj.w, s_T1[lane]);
+                }
+                wkeep = __ballot_sync(0xffffffffu, need);
+            }
             // every thread evaluates V vectors of the tile against each query in turn, so a
             // query's planes are read from shared memory once per V vectors
             constexpr int V = CORA_SCAN_VPT < TV / kScanThreads ? CORA_SCAN_VPT : TV / kScanThreads;
@@ -547,7 +664,8 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
                     else
                         bias[v] = code_bias<G16>(code[v]);
                 }
-                for (int j = 0; j < pc; ++j) {
+                for (uint32_t mj = wkeep; mj; mj &= mj - 1u) {
+                    const int j = __ffs(mj) - 1;
                     const uint32_t *P = s_planes + j * 8 * W4;
 #pragma unroll
                     for (int v = 0; v < V; ++v) {
@@ -557,9 +675,9 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_kernel(
                             ip = ip_int_from_bytes<G16>(e[v], P);
                         else
                             ip = ip_int_from_planes<G16>(code[v], P, bias[v]);
-                        const float ip1 = __fadd_rn(__fmul_rn(s_w[j], (float)ip), 0.0f);
-                        const float low =
-                            lower_bound_dist(f[v], ip1, s_g[j], s_k1[j], s_gerr[j]);
+                        const float4 pj = s_par[j];
+                        const float ip1 = __fadd_rn(__fmul_rn(pj.x, (float)ip), 0.0f);
+                        const float low = lower_bound_dist(f[v], ip1, pj.y, pj.z, pj.w);
                         if (kWriteLows) {
                             if (valid[v] && s_bnd[j] != ~0ull) sv.lows[s_bnd[j] + v0 + i] = low;
                         } else {
