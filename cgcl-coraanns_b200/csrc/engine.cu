@@ -745,7 +745,8 @@ size_t rescan_smem(int sort_n) {
 template <int G16>
 size_t scan_smem() {
     using Sh = ScanShape<G16>;
-    return (size_t)Sh::kStages * Sh::kStageEntries * 16 + (size_t)kMaxPairsPerItem * 8 * Sh::W4 * 4;
+    return (size_t)Sh::kStages * Sh::kScanStageEntries * 16 +
+           (size_t)kMaxPairsPerItem * 8 * Sh::W4 * 4;
 }
 
 template <int G16, bool kLows>

@@ -114,7 +114,14 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
     for (uint32_t i = from + threadIdx.x; i < to; i += blockDim.x) {
         const uint64_t rec = sv.cand_rec[(size_t)q * sv.cap + i];
         const uint32_t gid = static_cast<uint32_t>(rec & 0xFFFFFFFFu);
-        const ProbeInfo p = pinfo[rec >> 32];
+        const uint32_t pr = static_cast<uint32_t>(rec >> 32);
+        // a record outside its probe's cluster is reported, never dereferenced
+        if (pr >= static_cast<uint32_t>(np) || gid - pinfo[pr].start >= pinfo[pr].size) {
+            atomicOr(sv.err, kDevBadInput);
+            sv.cand_key[(size_t)q * sv.cap + i] = kKeyMax;
+            continue;
+        }
+        const ProbeInfo p = pinfo[pr];
         const uint4 *cb = ix.scan4 + planes_per * p.start + (gid - p.start);
         const uint64_t *eb = reinterpret_cast<const uint64_t *>(ix.long_codes + (size_t)gid * ix.LC);
         const float2 f = __ldg(ix.ex_factors + gid);

@@ -32,14 +32,24 @@ namespace cora {
 constexpr int kScanThreads = 256;
 constexpr int kMaxPairsPerItem = 32;
 
+// Vectors each scan_kernel thread evaluates per pass over an item's pairs (D <= 128 only):
+// the query words read from shared memory then serve that many vectors.
+#ifndef CORA_SCAN_VPT
+#define CORA_SCAN_VPT 1
+#endif
+
 template <int G16>
 struct ScanShape {
-    static constexpr int TV = 256;                     // vectors per staged tile
+    static constexpr int TV = 256;                     // vectors per staged tile (rescan)
     // tiles in flight in scan_kernel (its shared memory: kStages x kStageEntries x 16 B);
     // deep enough to hide the TMA latency when an item serves few queries
     static constexpr int kStages = G16 <= 2 ? 4 : 2;
     static constexpr int W4 = 4 * G16;                 // 32-bit code words per vector
     static constexpr int kStageEntries = (G16 + 1) * TV;
+    // scan_kernel's tiles: kScanThreads x VPT vectors
+    static constexpr int VPT = G16 == 1 ? CORA_SCAN_VPT : 1;
+    static constexpr int kScanTV = 256 * VPT;
+    static constexpr int kScanStageEntries = (G16 + 1) * kScanTV;
 };
 
 struct ScanItem {
@@ -253,14 +263,14 @@ __global__ void __launch_bounds__(256) chunk_ranges_kernel(const uint4 *__restri
 }
 
 // ---- shared pieces ------------------------------------------------------------------
-template <int G16>
+template <int G16, int TVT = ScanShape<G16>::TV>
 __device__ __forceinline__ void issue_tile(uint4 *stage_buf, uint64_t *bar, const uint4 *scan4,
                                            size_t cbase, int n, int v0, int tv) {
     const uint32_t bytes = static_cast<uint32_t>(tv) * 16u;
     mbar_arrive_expect_tx(bar, bytes * (G16 + 1));
 #pragma unroll
     for (int g = 0; g <= G16; ++g)
-        bulk_g2s(stage_buf + g * ScanShape<G16>::TV, scan4 + cbase + (size_t)g * n + v0, bytes,
+        bulk_g2s(stage_buf + g * TVT, scan4 + cbase + (size_t)g * n + v0, bytes,
                  bar);
 }
 
@@ -297,10 +307,6 @@ static_assert(kCsaLevels >= 2 && kCsaLevels <= 8, "adder tree depth");
 // for D <= 128, where it was measured 3% faster than 2 or 3 on config 2; 2 above.
 #ifndef CORA_SCAN_MINB
 #define CORA_SCAN_MINB(G16) ((G16) == 1 ? 4 : 2)
-#endif
-// Vectors each scan thread evaluates per pass over a tile's queries.
-#ifndef CORA_SCAN_VPT
-#define CORA_SCAN_VPT 1
 #endif
 
 // sum_j 2^j sum_t popc(x_t & p'_{j,t}) for one group; P points at the group's plane words
@@ -496,13 +502,13 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
     const uint32_t *__restrict__ n_items_ptr, const uint32_t *__restrict__ pairs,
     int *__restrict__ item_counter) {
     using Sh = ScanShape<G16>;
-    constexpr int TV = Sh::TV, W4 = Sh::W4, S = Sh::kStages;
+    constexpr int TV = Sh::kScanTV, W4 = Sh::W4, S = Sh::kStages, SE = Sh::kScanStageEntries;
     // query words: byte words for dp4a (the split code is 32 * G16 registers, so only for
     // D <= 128), offset-binary bit-planes otherwise; both are 8 * W4 words per query
     constexpr bool kBytes = kScanDp4a && G16 == 1;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint4 *stage = reinterpret_cast<uint4 *>(smem_raw);
-    uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + S * Sh::kStageEntries);
+    uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + S * SE);
     __shared__ __align__(8) uint64_t bars[S];
     __shared__ uint64_t s_bnd[kMaxPairsPerItem];
     // per pair: {width, g, k1, sqrt(max(g, 0))} (one 16-byte read per evaluation)
@@ -537,8 +543,8 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
         const uint32_t chunk0 = kWriteLows ? 0u : ix.cl_chunk[c];
         if (kWriteLows && threadIdx.x == 0)  // the first S - 1 tiles go out at once
             for (int u = 0; u < S - 1 && u < ntiles; ++u)
-                issue_tile<G16>(stage + u * Sh::kStageEntries, &bars[u], ix.scan4, cbase, n,
-                                u * TV, min(TV, n - u * TV));
+                issue_tile<G16, TV>(stage + u * SE, &bars[u], ix.scan4, cbase, n, u * TV,
+                                    min(TV, n - u * TV));
         if (kWriteLows) {
             if (threadIdx.x == 0) {
                 const unsigned long long need =
@@ -594,8 +600,8 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
             if (keep == 0) continue;  // no vector of the cluster can be a candidate
             if (threadIdx.x == 0)
                 for (int u = 0; u < S - 1 && u < ntiles; ++u)
-                    issue_tile<G16>(stage + u * Sh::kStageEntries, &bars[u], ix.scan4, cbase, n,
-                                    u * TV, min(TV, n - u * TV));
+                    issue_tile<G16, TV>(stage + u * SE, &bars[u], ix.scan4, cbase, n, u * TV,
+                                        min(TV, n - u * TV));
         }
         for (int i = threadIdx.x; i < pc * 8 * W4; i += blockDim.x) {
             const int j = i / (8 * W4), r = i - j * 8 * W4;
@@ -620,26 +626,30 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
             }
             if (threadIdx.x == 0 && t + S - 1 < ntiles) {  // into the slot tile t - 1 freed
                 const int u = t + S - 1;
-                issue_tile<G16>(stage + (u % S) * Sh::kStageEntries, &bars[u % S], ix.scan4,
-                                cbase, n, u * TV, min(TV, n - u * TV));
+                issue_tile<G16, TV>(stage + (u % S) * SE, &bars[u % S], ix.scan4, cbase, n,
+                                    u * TV, min(TV, n - u * TV));
             }
-            const uint4 *sb = stage + b * Sh::kStageEntries;
-            // the pairs this warp's chunk (vectors v0 + 32 warp ..) keeps
+            const uint4 *sb = stage + b * SE;
+            constexpr int V = Sh::VPT;
+            // the pairs this warp's chunks (vectors v0 + 256 v + 32 warp ..) keep
             uint32_t wkeep = keep;
             if (!kWriteLows) {
-                static_assert(TV == kScanThreads, "one vector per thread: warp w = chunk w");
-                const int k = v0 / 32 + warp;
-                bool need = false;
-                if (k * 32 < n && lane < pc && ((keep >> lane) & 1u)) {
-                    const float4 pj = s_par[lane];
-                    need = !range_at_least(__ldg(ix.chunk_range + chunk0 + k), pj.y, s_M[lane],
-                                           pj.w, s_T1[lane]);
+                static_assert(TV == kScanThreads * V, "thread t evaluates vectors t + 256 v");
+                wkeep = 0;
+#pragma unroll
+                for (int v = 0; v < V; ++v) {
+                    const int k = (v0 + v * kScanThreads) / 32 + warp;
+                    bool need = false;
+                    if (k * 32 < n && lane < pc && ((keep >> lane) & 1u)) {
+                        const float4 pj = s_par[lane];
+                        need = !range_at_least(__ldg(ix.chunk_range + chunk0 + k), pj.y,
+                                               s_M[lane], pj.w, s_T1[lane]);
+                    }
+                    wkeep |= __ballot_sync(0xffffffffu, need);
                 }
-                wkeep = __ballot_sync(0xffffffffu, need);
             }
             // every thread evaluates V vectors of the tile against each query in turn, so a
-            // query's planes are read from shared memory once per V vectors
-            constexpr int V = CORA_SCAN_VPT < TV / kScanThreads ? CORA_SCAN_VPT : TV / kScanThreads;
+            // query's words are read from shared memory once per V vectors
             for (int vb = 0; vb < tv; vb += V * kScanThreads) {
                 uint4 code[V][G16];
                 float4 f[V];
@@ -781,7 +791,8 @@ __device__ __forceinline__ uint32_t lows_index(uint32_t b4, int lane, int e) {
 }
 
 // One warp per vanguard pair (8 per CTA): candidates low < T1 that are not seeds
-// (key > boundary), read from the pair's stored lows.
+// (key > boundary), read from the pair's stored lows. A pair whose cluster's factor range
+// proves every low >= T1 (range_at_least) has none and reads nothing.
 __global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, SearchView sv,
                                                               const uint8_t *__restrict__ owned) {
     const int lane = threadIdx.x & 31;
@@ -792,8 +803,15 @@ __global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, Sear
     if (owned && !owned[c]) return;
     const uint32_t s = ix.cl_start[c];
     const uint32_t n = ix.cl_size[c];
-    const float4 *L4 = reinterpret_cast<const float4 *>(sv.lows + sv.vg_off[pi]);
     const float T1 = sv.T1[q];
+    {
+        const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
+        const QueryScalars qs = sv.scal[q];
+        if (range_at_least(ix.cl_range[c], g, ip_term_bound(sv.qrange[q], qs.width, qs.k1),
+                           __fsqrt_rn(fmaxf(g, 0.0f)), T1))
+            return;  // warp-uniform
+    }
+    const float4 *L4 = reinterpret_cast<const float4 *>(sv.lows + sv.vg_off[pi]);
     const uint64_t bnd = sv.bound[(size_t)q * sv.veff + r];
     const float *L = sv.lows + sv.vg_off[pi];
     const uint64_t rtag = static_cast<uint64_t>(r) << 32;
