@@ -164,6 +164,29 @@ inline void launch_probe_gemm(const float *qr, const float *qnorm2, uint64_t nq,
 // Exact top-nprobe from the approximate distances: one warp per query when nprobe <= 32
 // (queries whose candidate set overflows go on to the block kernel through `fallback`,
 // 1 + nq words), else one CTA per query.
+// rotate_prep_kernel with kRotQueriesWide queries per CTA when D <= 128, else kRotQueries.
+inline void launch_rotate_prep(const float *raw_q, uint64_t nq, uint64_t dim, uint64_t D, int W4,
+                               const double *rotator, float c_b, float *qr, QueryScalars *scal,
+                               uint32_t *planes, float *qnorm2, int2 *qrange, cudaStream_t st) {
+    const bool wide = D <= 128;
+    const int qpc = wide ? kRotQueriesWide : kRotQueries;
+    const size_t sm = (size_t)qpc * (2 * dim + D) * 4;
+    const unsigned grid = static_cast<unsigned>((nq + qpc - 1) / qpc);
+    const int inq = static_cast<int>(nq), idim = static_cast<int>(dim), iD = static_cast<int>(D);
+    if (wide) {
+        CUDA_TRY(cudaFuncSetAttribute(rotate_prep_kernel<kRotQueriesWide>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        rotate_prep_kernel<kRotQueriesWide><<<grid, 256, sm, st>>>(
+            raw_q, inq, idim, iD, W4, rotator, c_b, qr, scal, planes, qnorm2, qrange);
+    } else {
+        CUDA_TRY(cudaFuncSetAttribute(rotate_prep_kernel<kRotQueries>,
+                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        rotate_prep_kernel<kRotQueries><<<grid, 256, sm, st>>>(
+            raw_q, inq, idim, iD, W4, rotator, c_b, qr, scal, planes, qnorm2, qrange);
+    }
+    CUDA_TRY(cudaGetLastError());
+}
+
 inline void launch_guarded_select(float *approx, const float *chunk_min, uint64_t nlist,
                                   uint64_t nq, uint64_t nprobe, const float *qr,
                                   const float *qnorm2, const float *cent, float cmax, uint64_t D,
@@ -232,12 +255,12 @@ struct Engine {
     bool loaded = false;
     uint64_t N = 0, dim = 0, D = 0, nlist = 0, ex_bits = 0, max_cluster = 0;
     int G16 = 0, W4 = 0, LC = 0;
-    DevBuf<float> centroids, rotator, cnorm2;  // cnorm2: ||c'||^2 per centroid
+    DevBuf<float> centroids, cnorm2;  // cnorm2: ||c'||^2 per centroid
+    DevBuf<double> rotator;            // dim x D, held in fp64 for the rotation chains
     float cmax = 0.0f;                          // max ||c'|| (rounded up)
     DevBuf<uint4> scan4;
-    DevBuf<uint8_t> long_codes;
-    DevBuf<float2> ex_factors;
-    DevBuf<uint32_t> ids, cl_start, cl_size;
+    DevBuf<uint4> rows, meta;  // refine rows (N x D bytes) and meta words (see IndexView)
+    DevBuf<uint32_t> cl_start, cl_size;
     DevBuf<uint32_t> cl_chunk;              // first 32-vector chunk of each cluster (nlist + 1)
     DevBuf<float4> chunk_range, cl_range;   // factor ranges per chunk / per cluster
     DevBuf<uint8_t> owned;  // optional shard ownership mask (all clusters when empty)
@@ -361,17 +384,23 @@ struct Engine {
             cnorm2.alloc(cn.size());
             CUDA_TRY(cudaMemcpy(cnorm2.p, cn.data(), cn.size() * 4, cudaMemcpyHostToDevice));
         }
-        CUDA_TRY(cudaMemcpy(rotator.p, h_rotator, dim * D * 4, cudaMemcpyHostToDevice));
+        {
+            const std::vector<double> rd(h_rotator, h_rotator + dim * D);  // exact widening
+            CUDA_TRY(cudaMemcpy(rotator.p, rd.data(), dim * D * 8, cudaMemcpyHostToDevice));
+        }
         cl_start.alloc(nlist);
         cl_size.alloc(nlist);
         CUDA_TRY(cudaMemcpy(cl_start.p, starts.data(), nlist * 4, cudaMemcpyHostToDevice));
         CUDA_TRY(cudaMemcpy(cl_size.p, sizes.data(), nlist * 4, cudaMemcpyHostToDevice));
-        long_codes.alloc(N * LC);
-        ex_factors.alloc(N);
-        ids.alloc(N);
-        CUDA_TRY(cudaMemcpy(long_codes.p, h_long, N * LC, cudaMemcpyHostToDevice));
-        CUDA_TRY(cudaMemcpy(ex_factors.p, h_exf, N * 8, cudaMemcpyHostToDevice));
-        CUDA_TRY(cudaMemcpy(ids.p, h_ids, N * 4, cudaMemcpyHostToDevice));
+        DevBuf<uint8_t> tmp_long;
+        DevBuf<float2> tmp_exf;
+        DevBuf<uint32_t> tmp_ids;
+        tmp_long.alloc(N * LC);
+        tmp_exf.alloc(N);
+        tmp_ids.alloc(N);
+        CUDA_TRY(cudaMemcpy(tmp_long.p, h_long, N * LC, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(tmp_exf.p, h_exf, N * 8, cudaMemcpyHostToDevice));
+        CUDA_TRY(cudaMemcpy(tmp_ids.p, h_ids, N * 4, cudaMemcpyHostToDevice));
         // Repack the adapter's word-major 1-bit codes + float[N][3] factors into scan planes.
         DevBuf<uint32_t> tmp_short;
         DevBuf<float> tmp_fac;
@@ -392,6 +421,12 @@ struct Engine {
                 scan4.p, cl_start.p, cl_size.p, cl_chunk.p, G16, chunk_range.p, cl_range.p);
             CUDA_TRY(cudaGetLastError());
         }
+        rows.alloc(std::max<uint64_t>(N * D / 16, 1));
+        meta.alloc(std::max<uint64_t>(N, 1));
+        build_refine_rows_kernel<<<static_cast<unsigned>(nlist), 256, 0, stream>>>(
+            tmp_long.p, tmp_exf.p, tmp_ids.p, scan4.p, cl_start.p, cl_size.p, static_cast<int>(D),
+            G16, LC, reinterpret_cast<uint8_t *>(rows.p), meta.p);
+        CUDA_TRY(cudaGetLastError());
         CUDA_TRY(cudaStreamSynchronize(stream));
         loaded = true;
     }
@@ -799,7 +834,7 @@ void dispatch_scan(int G16, const ScanLaunch &L, ScanPhase phase) {
 
 IndexView Engine::index_view() const {
     return IndexView{scan4.p, cl_start.p, cl_size.p, chunk_range.p, cl_chunk.p, cl_range.p,
-                     long_codes.p, ex_factors.p, ids.p,
+                     rows.p, meta.p,
                      static_cast<int>(nlist), static_cast<int>(D), G16, LC};
 }
 
@@ -840,14 +875,9 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
 
     // 1. rotation + query factors + bit-planes
     {
-        const size_t sm = (size_t)kRotQueries * (dim + D) * 4;
-        CUDA_TRY(cudaFuncSetAttribute(rotate_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)sm));
         const float c_b = -static_cast<float>((1u << (ex_bits + 1)) - 1u) / 2.0f;
-        rotate_prep_kernel<<<static_cast<unsigned>((nq + kRotQueries - 1) / kRotQueries), 256, sm, st>>>(
-            d_q, inq, static_cast<int>(dim), static_cast<int>(D), W4, rotator.p, c_b, qr.p, scal.p,
-            planes.p, qnorm2.p, qrange.p);
-        CUDA_TRY(cudaGetLastError());
+        launch_rotate_prep(d_q, nq, dim, D, W4, rotator.p, c_b, qr.p, scal.p, planes.p, qnorm2.p,
+                           qrange.p, st);
     }
     mark(1, st);
     // 2. coarse probing: approximate distances for every (query, centroid), then the exact
@@ -1625,19 +1655,12 @@ int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num
         float *approx = reinterpret_cast<float *>(s + l.approx);
         int *status = reinterpret_cast<int *>(s + l.status);
         cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e.stream;
-        const int inq = static_cast<int>(num_queries), inp = static_cast<int>(nprobe);
+        const int inp = static_cast<int>(nprobe);
         CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), st));
 
-        const size_t rsm = (size_t)cora::kRotQueries * (e.dim + e.D) * 4;
-        CUDA_TRY(cudaFuncSetAttribute(cora::rotate_prep_kernel,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)rsm));
         const float c_b = -static_cast<float>((1u << (e.ex_bits + 1)) - 1u) / 2.0f;
-        cora::rotate_prep_kernel<<<static_cast<unsigned>((num_queries + cora::kRotQueries - 1) /
-                                                         cora::kRotQueries),
-                                   256, rsm, st>>>(d_queries, inq, static_cast<int>(e.dim),
-                                                   static_cast<int>(e.D), e.W4, e.rotator.p, c_b,
-                                                   qr, scal, planes, qnorm2, nullptr);
-        CUDA_TRY(cudaGetLastError());
+        cora::launch_rotate_prep(d_queries, num_queries, e.dim, e.D, e.W4, e.rotator.p, c_b, qr,
+                                 scal, planes, qnorm2, nullptr, st);
         float *cmin = reinterpret_cast<float *>(s + l.chunk_min);
         cora::launch_probe_gemm(qr, qnorm2, num_queries, e.D, e.centroids.p, e.cnorm2.p, e.nlist,
                                 approx, cmin, e.num_sms, st, status);

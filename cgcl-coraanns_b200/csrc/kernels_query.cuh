@@ -13,115 +13,139 @@
 
 namespace cora {
 
-constexpr int kRotQueries = 8;  // queries per CTA in rotate_prep_kernel
+// queries per CTA of rotate_prep_kernel: kRotQueriesWide when D <= 128 (two groups of
+// kRotQueries share the CTA's 256 threads), else kRotQueries
+constexpr int kRotQueries = 8;
+constexpr int kRotQueriesWide = 16;
 
 struct QueryScalars {  // per query, 16 bytes
     float width, k1, kb, sumq;
 };
 
-// One CTA handles kRotQueries queries. Each output dim j of q' is an fp64 chain over the
-// input dims in ascending order (fp32 x fp32 products are exact in fp64, so the fused
-// multiply-add rounds exactly like the oracle's add). Warp w then prepares query w.
-// Dynamic shared memory: kRotQueries * (dim + D) floats.
+// One CTA handles kQ queries, in kQ / 8 groups of 8 that split the CTA's threads. Each output
+// dim j of q' is an fp64 chain over the input dims in ascending order (fp32 x fp32 products
+// are exact in fp64, so the fused multiply-add rounds exactly like the oracle's add); the
+// queries are widened to fp64 once in shared memory and the rotator is held in fp64.
+// Warp w then prepares queries w, w + 8, ... Dynamic shared memory: kQ * (2 dim + D) floats.
+template <int kQ>
 __global__ void __launch_bounds__(256) rotate_prep_kernel(
     const float *__restrict__ raw_q, int nq, int dim, int D, int W4,
-    const float *__restrict__ rotator, float c_b, float *__restrict__ qr_out,
+    const double *__restrict__ rotator, float c_b, float *__restrict__ qr_out,
     QueryScalars *__restrict__ scal_out, uint32_t *__restrict__ planes_out,
     float *__restrict__ qnorm2_out, int2 *__restrict__ qrange_out) {
-    extern __shared__ float smem_f[];
-    float *sq = smem_f;                       // [kRotQueries][dim]
-    float *sr = smem_f + kRotQueries * dim;   // [kRotQueries][D]
-    const int q0 = blockIdx.x * kRotQueries;
-    const int nqb = min(kRotQueries, nq - q0);
-    for (int i = threadIdx.x; i < kRotQueries * dim; i += blockDim.x) {
+    constexpr int kGroups = kQ / kRotQueries;
+    extern __shared__ double smem_d[];
+    double *sq = smem_d;                                        // [kQ][dim]
+    float *sr = reinterpret_cast<float *>(smem_d + kQ * dim);   // [kQ][D]
+    const int q0 = blockIdx.x * kQ;
+    const int nqb = min(kQ, nq - q0);
+    for (int i = threadIdx.x; i < kQ * dim; i += blockDim.x) {
         const int qq = i / dim;
-        sq[i] = qq < nqb ? raw_q[(size_t)(q0 + qq) * dim + (i - qq * dim)] : 0.0f;
+        sq[i] = qq < nqb ? (double)raw_q[(size_t)(q0 + qq) * dim + (i - qq * dim)] : 0.0;
     }
     __syncthreads();
-    for (int j = threadIdx.x; j < D; j += blockDim.x) {
+    constexpr int kTpg = 256 / kGroups;  // threads per group
+    const int grp = threadIdx.x / kTpg;
+    const double *sqg = sq + grp * kRotQueries * dim;
+    for (int j = threadIdx.x % kTpg; j < D; j += kTpg) {
         double acc[kRotQueries];
 #pragma unroll
         for (int qq = 0; qq < kRotQueries; ++qq) acc[qq] = 0.0;
         for (int i = 0; i < dim; ++i) {
-            const double p = (double)__ldg(rotator + (size_t)i * D + j);
+            const double p = __ldg(rotator + (size_t)i * D + j);
 #pragma unroll
             for (int qq = 0; qq < kRotQueries; ++qq)
-                acc[qq] = __fma_rn((double)sq[qq * dim + i], p, acc[qq]);
+                acc[qq] = __fma_rn(sqg[qq * dim + i], p, acc[qq]);
         }
 #pragma unroll
         for (int qq = 0; qq < kRotQueries; ++qq) {
+            const int qa = grp * kRotQueries + qq;
             const float v = (float)acc[qq];
-            sr[qq * D + j] = v;
-            if (qq < nqb) qr_out[(size_t)(q0 + qq) * D + j] = v;
+            sr[qa * D + j] = v;
+            if (qa < nqb) qr_out[(size_t)(q0 + qa) * D + j] = v;
         }
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (warp >= nqb) return;
-    const int q = q0 + warp;
-    const float *x = sr + warp * D;
-    // sumq: lane-strided fp64 partial sums, xor butterfly (identical on every lane)
-    double part = 0.0;
-    float amax = 0.0f;
-    for (int j = lane; j < D; j += 32) {
-        part = __dadd_rn(part, (double)x[j]);
-        amax = fmaxf(amax, fabsf(x[j]));
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-        part = __dadd_rn(part, __shfl_xor_sync(0xffffffffu, part, off));
-        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-    }
-    const float sf = (float)part;
-    const float width = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
-    const float inv = __fdiv_rn(1.0f, width);
-    // ||q'||^2 for the approximate coarse distances (any order: it only feeds the filter)
-    double nrm = 0.0;
-    for (int j = lane; j < D; j += 32) nrm = __fma_rn((double)x[j], (double)x[j], nrm);
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) nrm += __shfl_xor_sync(0xffffffffu, nrm, off);
-    if (lane == 0) {
-        QueryScalars s;
-        s.width = width;
-        s.k1 = __fmul_rn(sf, -0.5f);
-        s.kb = __fmul_rn(sf, c_b);
-        s.sumq = sf;
-        scal_out[q] = s;
-        qnorm2_out[q] = (float)nrm;
-    }
-    uint32_t *pl = planes_out + (size_t)q * 8 * W4;
-    int pos = 0, neg = 0;  // sums of the positive and of the negative qint
-    for (int w = 0; w < W4; ++w) {
-        const int j = w * 32 + lane;
-        int v = 0;
-        if (j < D) {
-            v = __float2int_rn(__fmul_rn(x[j], inv));
-            v = max(-128, min(127, v));
+    for (int qw = warp; qw < nqb; qw += 8) {
+        const int q = q0 + qw;
+        const float *x = sr + qw * D;
+        // sumq: lane-strided fp64 partial sums, xor butterfly (identical on every lane)
+        double part = 0.0;
+        float amax = 0.0f;
+        for (int j = lane; j < D; j += 32) {
+            part = __dadd_rn(part, (double)x[j]);
+            amax = fmaxf(amax, fabsf(x[j]));
         }
-        pos += max(v, 0);
-        neg += min(v, 0);
-        const uint32_t bits = static_cast<uint32_t>(v) & 0xFFu;
 #pragma unroll
-        for (int b = 0; b < 8; ++b) {
-            const uint32_t m = __brev(__ballot_sync(0xffffffffu, (bits >> b) & 1u));
-            if (lane == 0) pl[b * W4 + w] = m;
+        for (int off = 16; off >= 1; off >>= 1) {
+            part = __dadd_rn(part, __shfl_xor_sync(0xffffffffu, part, off));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
         }
+        const float sf = (float)part;
+        const float width = fmaxf(__fdiv_rn(amax, 127.0f), 1e-30f);
+        const float inv = __fdiv_rn(1.0f, width);
+        // ||q'||^2 for the approximate coarse distances (any order: it only feeds the filter)
+        double nrm = 0.0;
+        for (int j = lane; j < D; j += 32) nrm = __fma_rn((double)x[j], (double)x[j], nrm);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) nrm += __shfl_xor_sync(0xffffffffu, nrm, off);
+        if (lane == 0) {
+            QueryScalars s;
+            s.width = width;
+            s.k1 = __fmul_rn(sf, -0.5f);
+            s.kb = __fmul_rn(sf, c_b);
+            s.sumq = sf;
+            scal_out[q] = s;
+            qnorm2_out[q] = (float)nrm;
+        }
+        uint32_t *pl = planes_out + (size_t)q * 8 * W4;
+        int pos = 0, neg = 0;  // sums of the positive and of the negative qint
+        for (int w = 0; w < W4; ++w) {
+            const int j = w * 32 + lane;
+            int v = 0;
+            if (j < D) {
+                v = __float2int_rn(__fmul_rn(x[j], inv));
+                v = max(-128, min(127, v));
+            }
+            pos += max(v, 0);
+            neg += min(v, 0);
+            const uint32_t bits = static_cast<uint32_t>(v) & 0xFFu;
+#pragma unroll
+            for (int b = 0; b < 8; ++b) {
+                const uint32_t m = __brev(__ballot_sync(0xffffffffu, (bits >> b) & 1u));
+                if (lane == 0) pl[b * W4 + w] = m;
+            }
+        }
+        // [neg, pos] is the range of sum_i b_i qint_i over every 1-bit code (the scan's bound)
+        pos = __reduce_add_sync(0xffffffffu, pos);
+        neg = __reduce_add_sync(0xffffffffu, neg);
+        if (qrange_out && lane == 0) qrange_out[q] = make_int2(pos, neg);
     }
-    // [neg, pos] is the range of sum_i b_i qint_i over every 1-bit code (the scan's bound)
-    pos = __reduce_add_sync(0xffffffffu, pos);
-    neg = __reduce_add_sync(0xffffffffu, neg);
-    if (qrange_out && lane == 0) qrange_out[q] = make_int2(pos, neg);
 }
 
 // Exact coarse distance of the search contract: g(q, c) = fp32( sum_j fma(d_j, d_j) ) with
 // d_j = q'_j - c_j in fp64, ascending j (reference: hybrid.cu:465-477 forms the same
 // ||q'||^2 + ||c||^2 - 2 q'.c in fp32).
+// The centroid row is loaded 32 dims at a time (eight 16-byte loads in flight; rows are
+// 16-byte aligned since D % 64 == 0) ahead of the chain, which stays in ascending order.
 __device__ __forceinline__ float exact_centroid_dist(const float *__restrict__ x,
                                                      const float *__restrict__ c, int D) {
     double acc = 0.0;
-    for (int j = 0; j < D; ++j) {
-        const double d = __dsub_rn((double)x[j], (double)__ldg(c + j));
-        acc = __fma_rn(d, d, acc);
+    const float4 *c4 = reinterpret_cast<const float4 *>(c);
+    for (int j0 = 0; j0 < D; j0 += 32) {
+        float4 v[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) v[t] = __ldg(c4 + j0 / 4 + t);
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const float cv[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const double d = __dsub_rn((double)x[j0 + 4 * t + u], (double)cv[u]);
+                acc = __fma_rn(d, d, acc);
+            }
+        }
     }
     return (float)acc;
 }

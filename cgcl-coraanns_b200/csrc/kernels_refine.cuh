@@ -76,9 +76,9 @@ __device__ __forceinline__ double block_code_ip(const double *__restrict__ x,
     return acc;
 }
 
-// One CTA per query, one thread per candidate: every load of a candidate (1-bit code words,
-// ex code, factors, id) is issued before its fp64 chain, so a candidate costs one memory
-// round trip. mode 0 refines the vanguard seeds [0, cnt) and records the seed count; mode 1
+// One CTA per query, one thread per candidate: a candidate's refine row (ex code and 1-bit
+// code, D bytes, 32-byte sectors used whole) and its meta word are loaded before its fp64
+// chain, so a candidate costs one memory round trip. mode 0 refines the vanguard seeds [0, cnt) and records the seed count; mode 1
 // refines the main candidates [seed_cnt, cnt). Dynamic shared memory: D floats + nprobe
 // ProbeInfo.
 __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, SearchView sv,
@@ -109,8 +109,7 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
     __syncthreads();
     const float kb = sv.scal[q].kb;
     const int nblocks = ix.D / 64;
-    const size_t planes_per = static_cast<size_t>(ix.G16 + 1);
-    const bool v16 = (ix.LC & 15) == 0;  // ex-code rows 16-byte aligned (D % 128 == 0)
+    const int row4 = ix.D / 16;  // uint4 per refine row
     for (uint32_t i = from + threadIdx.x; i < to; i += blockDim.x) {
         const uint64_t rec = sv.cand_rec[(size_t)q * sv.cap + i];
         const uint32_t gid = static_cast<uint32_t>(rec & 0xFFFFFFFFu);
@@ -122,36 +121,45 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
             continue;
         }
         const ProbeInfo p = pinfo[pr];
-        const uint4 *cb = ix.scan4 + planes_per * p.start + (gid - p.start);
-        const uint64_t *eb = reinterpret_cast<const uint64_t *>(ix.long_codes + (size_t)gid * ix.LC);
-        const float2 f = __ldg(ix.ex_factors + gid);
-        const uint32_t id = __ldg(ix.ids + gid);
+        const uint4 *row = ix.rows + (size_t)gid * row4;
+        const uint4 mt = __ldg(ix.meta + gid);  // {f_add_ex, f_rescale_ex, id, 0}
+        const float2 f = make_float2(__uint_as_float(mt.x), __uint_as_float(mt.y));
+        const uint32_t id = mt.z;
         double acc = 0.0;
         for (int g = 0; 2 * g < nblocks; ++g) {
-            const uint4 cw = __ldg(cb + (size_t)g * p.size);
-            uint64_t e[14];
-            if (v16 && 2 * g + 1 < nblocks) {
-                // a full 128-dim group is 112 bytes: seven 16-byte loads (rows 16-byte aligned)
-                const uint4 *e4 = reinterpret_cast<const uint4 *>(eb + 14 * g);
+            const uint4 *gr = row + 8 * g;
+            uint64_t lo[7], hi[7];
+            if (2 * g + 1 < nblocks) {
+                // a full 128-dim group: 112 ex-code bytes then the 4 code words (128 bytes)
+                uint4 v[8];
+#pragma unroll
+                for (int t = 0; t < 8; ++t) v[t] = __ldg(gr + t);
+                uint64_t e[14];
 #pragma unroll
                 for (int t = 0; t < 7; ++t) {
-                    const uint4 v = __ldg(e4 + t);
-                    e[2 * t] = (uint64_t(v.y) << 32) | v.x;
-                    e[2 * t + 1] = (uint64_t(v.w) << 32) | v.z;
+                    e[2 * t] = (uint64_t(v[t].y) << 32) | v[t].x;
+                    e[2 * t + 1] = (uint64_t(v[t].w) << 32) | v[t].z;
                 }
+#pragma unroll
+                for (int t = 0; t < 7; ++t) {
+                    lo[t] = e[t];
+                    hi[t] = e[7 + t];
+                }
+                acc = block_code_ip(x + 128 * g, lo, v[7].x, v[7].y, acc);
+                acc = block_code_ip(x + 128 * g + 64, hi, v[7].z, v[7].w, acc);
             } else {
+                // a last 64-dim block: 56 ex-code bytes then its 2 code words (64 bytes)
+                uint4 v[4];
 #pragma unroll
-                for (int t = 0; t < 14; ++t)
-                    e[t] = (t < 7 || 2 * g + 1 < nblocks) ? __ldg(eb + 14 * g + t) : 0ull;
-            }
-            uint64_t lo[7], hi[7];
+                for (int t = 0; t < 4; ++t) v[t] = __ldg(gr + t);
 #pragma unroll
-            for (int t = 0; t < 7; ++t) {
-                lo[t] = e[t];
-                hi[t] = e[7 + t];
+                for (int t = 0; t < 3; ++t) {
+                    lo[2 * t] = (uint64_t(v[t].y) << 32) | v[t].x;
+                    lo[2 * t + 1] = (uint64_t(v[t].w) << 32) | v[t].z;
+                }
+                lo[6] = (uint64_t(v[3].y) << 32) | v[3].x;
+                acc = block_code_ip(x + 128 * g, lo, v[3].z, v[3].w, acc);
             }
-            acc = block_code_ip(x + 128 * g, lo, cw.x, cw.y, acc);
-            if (2 * g + 1 < nblocks) acc = block_code_ip(x + 128 * g + 64, hi, cw.z, cw.w, acc);
         }
         const float ex_d = __fadd_rn(__fadd_rn(f.x, p.g),
                                      __fmul_rn(f.y, __fadd_rn(__double2float_rn(acc), kb)));

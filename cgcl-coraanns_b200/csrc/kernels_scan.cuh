@@ -65,9 +65,10 @@ struct IndexView {
     const float4 *chunk_range;
     const uint32_t *cl_chunk;    // nlist + 1
     const float4 *cl_range;      // nlist
-    const uint8_t *long_codes;   // N x LC
-    const float2 *ex_factors;    // N
-    const uint32_t *ids;         // N
+    // refine rows (build_refine_rows_kernel): per vector D bytes, for each 128-dim group
+    // its 112 ex-code bytes then its 4 code words (a last 64-dim block: 56 + 8 bytes)
+    const uint4 *rows;           // N x D / 16
+    const uint4 *meta;           // N: {f_add_ex, f_rescale_ex, id, 0}
     int nlist, D, G16, LC;
 };
 
@@ -259,6 +260,38 @@ __global__ void __launch_bounds__(256) chunk_ranges_kernel(const uint4 *__restri
             acc = make_float4(fminf(acc.x, s_red[w].x), fmaxf(acc.y, s_red[w].y),
                               fmaxf(acc.z, s_red[w].z), fmaxf(acc.w, s_red[w].w));
         cl_range[c] = acc;
+    }
+}
+
+// One CTA per cluster: the refine rows and meta words of its vectors, from the ex codes
+// (LC = 7 D / 8 bytes per vector, 56 per 64-dim block), the 1-bit code words in the scan
+// planes, the ex factors and the ids. Built once when the index is loaded.
+__global__ void __launch_bounds__(256) build_refine_rows_kernel(
+    const uint8_t *__restrict__ long_codes, const float2 *__restrict__ exf,
+    const uint32_t *__restrict__ ids, const uint4 *__restrict__ scan4,
+    const uint32_t *__restrict__ cl_start, const uint32_t *__restrict__ cl_size, int D, int G16,
+    int LC, uint8_t *__restrict__ rows, uint4 *__restrict__ meta) {
+    const int c = blockIdx.x;
+    const uint32_t s = cl_start[c], n = cl_size[c];
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const size_t gid = (size_t)s + i;
+        const uint8_t *ex = long_codes + gid * LC;
+        uint8_t *row = rows + gid * D;
+        for (int g = 0; g < G16; ++g) {
+            const bool full = 128 * g + 128 <= D;
+            const int exb = full ? 112 : 56;
+            for (int b = 0; b < exb; ++b) row[128 * g + b] = ex[112 * g + b];
+            const uint4 cw = scan4[(size_t)(G16 + 1) * s + (size_t)g * n + i];
+            uint32_t *w = reinterpret_cast<uint32_t *>(row + 128 * g + exb);
+            w[0] = cw.x;
+            w[1] = cw.y;
+            if (full) {
+                w[2] = cw.z;
+                w[3] = cw.w;
+            }
+        }
+        const float2 f = exf[gid];
+        meta[gid] = make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), ids[gid], 0u);
     }
 }
 
