@@ -649,7 +649,7 @@ struct Engine {
     IndexView index_view() const;
     SearchView search_view() const;
     ScanLaunch scan_launch(const IndexView &ix, const SearchView &sv, cudaStream_t st) const;
-    void group_pairs(int r_lo, int r_hi, cudaStream_t st);
+    void group_pairs(int r_lo, int r_hi, bool prune, cudaStream_t st);
     // u64 words per shard in an exchange buffer: k keys per query + one status word.
     static uint64_t exchange_stride(uint64_t nq, uint64_t k) { return nq * k + 1; }
     void finish(cudaStream_t st) {
@@ -901,7 +901,7 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
     const unsigned n_van = static_cast<unsigned>(nq * veff);
     // 3. vanguard pairs: seeds (best `keep` keys per pair among low < T0)
     if (lows_mode) {
-        group_pairs(0, iveff, st);
+        group_pairs(0, iveff, false, st);
         // the lows pass bump-allocates the pairs' slices
         CUDA_TRY(cudaMemsetAsync(lows_top.p, 0, sizeof(unsigned long long), st));
     }
@@ -980,7 +980,8 @@ ScanLaunch Engine::scan_launch(const IndexView &ix, const SearchView &sv, cudaSt
 
 // Per-cluster grouping of the (query, probe rank) pairs with rank in [r_lo, r_hi): cross-query
 // reuse serves up to kMaxPairsPerItem queries from one cluster read.
-void Engine::group_pairs(int r_lo, int r_hi, cudaStream_t st) {
+// prune: leave out the pairs that pair_pruned proves candidate-free against T1 (main pass).
+void Engine::group_pairs(int r_lo, int r_hi, bool prune, cudaStream_t st) {
     const int inq = static_cast<int>(last_nq), inp = static_cast<int>(last_np);
     const uint8_t *own = owned.n ? owned.p : nullptr;
     const size_t total = last_nq * last_np;
@@ -989,10 +990,13 @@ void Engine::group_pairs(int r_lo, int r_hi, cudaStream_t st) {
     CUDA_TRY(cudaMemsetAsync(pair_cur.p, 0, nlist * 4, st));
     CUDA_TRY(cudaMemsetAsync(item_counter.p, 0, 4, st));
     const int ppi = cross_query_reuse ? kMaxPairsPerItem : 1;
-    count_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own, pair_cnt.p);
+    PairPrune pp{};
+    if (prune) pp = PairPrune{cl_range.p, probe_g.p, qrange.p, scal.p, T1.p};
+    count_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own, pp,
+                                               pair_cnt.p);
     scan_pairs_kernel<<<1, 1024, 0, st>>>(pair_cnt.p, static_cast<int>(nlist), ppi, pair_off.p,
                                            item_off.p, n_items.p);
-    scatter_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own,
+    scatter_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own, pp,
                                                  pair_off.p, pair_cur.p, pairs.p);
     emit_items_kernel<<<static_cast<unsigned>((nlist + 255) / 256), 256, 0, st>>>(
         pair_cnt.p, pair_off.p, item_off.p, static_cast<int>(nlist), ppi, items.p);
@@ -1024,7 +1028,7 @@ void Engine::enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uin
     mark(8, st);
     // 4. main pass against T1: the other probes are scanned; the vanguard probes are either
     //    filtered from their stored lows or rescanned, skipping their seeds in both cases.
-    group_pairs(lows_mode ? iveff : 0, inp, st);
+    group_pairs(lows_mode ? iveff : 0, inp, true, st);
     mark(9, st);
     dispatch_scan(G16, L, ScanPhase::kMain);
     mark(10, st);

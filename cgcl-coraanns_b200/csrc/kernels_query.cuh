@@ -51,11 +51,21 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
         double acc[kRotQueries];
 #pragma unroll
         for (int qq = 0; qq < kRotQueries; ++qq) acc[qq] = 0.0;
-        for (int i = 0; i < dim; ++i) {
-            const double p = __ldg(rotator + (size_t)i * D + j);
+        // rotator values are loaded eight rows ahead of their use (dim % 8 == 0 is not
+        // assumed: the tail rows read as 0 and are not accumulated)
+        for (int i0 = 0; i0 < dim; i0 += 8) {
+            double p[8];
 #pragma unroll
-            for (int qq = 0; qq < kRotQueries; ++qq)
-                acc[qq] = __fma_rn(sqg[qq * dim + i], p, acc[qq]);
+            for (int u = 0; u < 8; ++u)
+                p[u] = i0 + u < dim ? __ldg(rotator + (size_t)(i0 + u) * D + j) : 0.0;
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                if (i0 + u < dim) {
+#pragma unroll
+                    for (int qq = 0; qq < kRotQueries; ++qq)
+                        acc[qq] = __fma_rn(sqg[qq * dim + i0 + u], p[u], acc[qq]);
+                }
+            }
         }
 #pragma unroll
         for (int qq = 0; qq < kRotQueries; ++qq) {

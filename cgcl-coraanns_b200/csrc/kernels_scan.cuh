@@ -97,18 +97,65 @@ struct SearchView {
     int topk_warp_limit;         // the same for the threshold / final top-k (topk_warp_kernel)
 };
 
+// ---- factor ranges and the lower-bound test that skips whole chunks -------------------
+// A factor range {min f_add, max |f_add|, max |f_rescale|, max |f_error|} over a set of
+// vectors bounds every lower bound the scan computes for them against one pair:
+//   low = fl(fl(fl(f_add + g) + fl(f_rescale * t)) - fl(f_error * gerr)),  |t| <= M,
+// where t = fl(fl(width * ip) + k1) is monotone in ip, so M (its largest magnitude over the
+// reachable ip in [neg, pos]) is taken at an end of that range. Each of the five roundings
+// errs by at most 2^-24 of a magnitude below S = max|f_add| + |g| + max|f_rescale| M +
+// max|f_error| gerr, so low >= L - 2^-20 S with L = min f_add + g - max|f_rescale| M -
+// max|f_error| gerr. When that is >= T, no vector of the set has low < T: skipping it
+// leaves the candidate set unchanged. NaN factors fall out of the min/max (fminf/fmaxf
+// ignore NaN) and their lows (NaN) are never below T either.
+__device__ __forceinline__ bool range_at_least(float4 fr, float g, float M, float gerr,
+                                               float T) {
+    const double r = (double)fr.z * M, e = (double)fr.w * gerr;
+    const double L = ((double)fr.x + g) - r - e;
+    const double S = (double)fr.y + fabs((double)g) + r + e;
+    return L - 0x1p-20 * S >= (double)T;
+}
+
+// M of one pair: the largest |fl(fl(width * ip) + k1)| over ip in [neg, pos] (the scan's
+// evaluation of ip1 + k1, see scan_kernel).
+__device__ __forceinline__ float ip_term_bound(int2 range, float width, float k1) {
+    const float hi = __fadd_rn(__fadd_rn(__fmul_rn(width, (float)range.x), 0.0f), k1);
+    const float lo = __fadd_rn(__fadd_rn(__fmul_rn(width, (float)range.y), 0.0f), k1);
+    return fmaxf(fabsf(hi), fabsf(lo));
+}
+
+// Pair pruning of the main pass's grouping (cl_range == nullptr: none): a (query, probe)
+// pair is left out when its cluster's factor range proves every low >= T1 of the query, the
+// test scan_kernel also applies per item and per chunk.
+struct PairPrune {
+    const float4 *cl_range;      // nlist
+    const float *probe_g;        // nq x nprobe
+    const int2 *qrange;          // nq
+    const QueryScalars *scal;    // nq
+    const float *T1;             // nq
+};
+__device__ __forceinline__ bool pair_pruned(const PairPrune &pp, int q, int r, int c,
+                                            int nprobe) {
+    if (!pp.cl_range) return false;
+    const float g = pp.probe_g[(size_t)q * nprobe + r];
+    const QueryScalars qs = pp.scal[q];
+    return range_at_least(pp.cl_range[c], g, ip_term_bound(pp.qrange[q], qs.width, qs.k1),
+                          __fsqrt_rn(fmaxf(g, 0.0f)), pp.T1[q]);
+}
+
 // ---- per-cluster query grouping (CSR of (query, probe rank) pairs by cluster) --------
 // Pairs with probe rank in [r_lo, r_hi) whose cluster is owned by this shard (owned ==
-// nullptr: all) are grouped; a pair is packed as (q << 16) | r.
+// nullptr: all) and that pair_pruned keeps are grouped; a pair is packed as (q << 16) | r.
 __global__ void count_pairs_kernel(const int *__restrict__ probe_ids, int nq, int nprobe,
                                    int r_lo, int r_hi, const uint8_t *__restrict__ owned,
-                                   uint32_t *__restrict__ cnt) {
+                                   PairPrune pp, uint32_t *__restrict__ cnt) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (size_t)nq * nprobe) return;
     const int r = static_cast<int>(i % nprobe);
     if (r < r_lo || r >= r_hi) return;
     const int c = probe_ids[i];
     if (owned && !owned[c]) return;
+    if (pair_pruned(pp, static_cast<int>(i / nprobe), r, c, nprobe)) return;
     atomicAdd(cnt + c, 1u);
 }
 
@@ -154,7 +201,7 @@ __global__ void __launch_bounds__(1024) scan_pairs_kernel(const uint32_t *__rest
 
 __global__ void scatter_pairs_kernel(const int *__restrict__ probe_ids, int nq, int nprobe,
                                      int r_lo, int r_hi, const uint8_t *__restrict__ owned,
-                                     const uint32_t *__restrict__ off,
+                                     PairPrune pp, const uint32_t *__restrict__ off,
                                      uint32_t *__restrict__ cursor,
                                      uint32_t *__restrict__ pairs) {
     const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -164,6 +211,7 @@ __global__ void scatter_pairs_kernel(const int *__restrict__ probe_ids, int nq, 
     const int c = probe_ids[i];
     if (owned && !owned[c]) return;
     const int q = static_cast<int>(i / nprobe);
+    if (pair_pruned(pp, q, r, c, nprobe)) return;
     const uint32_t pos = atomicAdd(cursor + c, 1u);
     pairs[off[c] + pos] = (static_cast<uint32_t>(q) << 16) | static_cast<uint32_t>(r);
 }
@@ -192,33 +240,6 @@ __global__ void emit_items_kernel(const uint32_t *__restrict__ cnt,
 // pass of scan_kernel; the worst case (every query probing the largest clusters) is what
 // prepare_workspace reserves.
 __host__ __device__ __forceinline__ uint32_t lows_slice(uint32_t n) { return (n + 3u) & ~3u; }
-
-// ---- factor ranges and the lower-bound test that skips whole chunks -------------------
-// A factor range {min f_add, max |f_add|, max |f_rescale|, max |f_error|} over a set of
-// vectors bounds every lower bound the scan computes for them against one pair:
-//   low = fl(fl(fl(f_add + g) + fl(f_rescale * t)) - fl(f_error * gerr)),  |t| <= M,
-// where t = fl(fl(width * ip) + k1) is monotone in ip, so M (its largest magnitude over the
-// reachable ip in [neg, pos]) is taken at an end of that range. Each of the five roundings
-// errs by at most 2^-24 of a magnitude below S = max|f_add| + |g| + max|f_rescale| M +
-// max|f_error| gerr, so low >= L - 2^-20 S with L = min f_add + g - max|f_rescale| M -
-// max|f_error| gerr. When that is >= T, no vector of the set has low < T: skipping it
-// leaves the candidate set unchanged. NaN factors fall out of the min/max (fminf/fmaxf
-// ignore NaN) and their lows (NaN) are never below T either.
-__device__ __forceinline__ bool range_at_least(float4 fr, float g, float M, float gerr,
-                                               float T) {
-    const double r = (double)fr.z * M, e = (double)fr.w * gerr;
-    const double L = ((double)fr.x + g) - r - e;
-    const double S = (double)fr.y + fabs((double)g) + r + e;
-    return L - 0x1p-20 * S >= (double)T;
-}
-
-// M of one pair: the largest |fl(fl(width * ip) + k1)| over ip in [neg, pos] (the scan's
-// evaluation of ip1 + k1, see scan_kernel).
-__device__ __forceinline__ float ip_term_bound(int2 range, float width, float k1) {
-    const float hi = __fadd_rn(__fadd_rn(__fmul_rn(width, (float)range.x), 0.0f), k1);
-    const float lo = __fadd_rn(__fadd_rn(__fmul_rn(width, (float)range.y), 0.0f), k1);
-    return fmaxf(fabsf(hi), fabsf(lo));
-}
 
 // One CTA per cluster: the factor range of each 32-vector chunk (warp-wide reductions) and
 // of the whole cluster. Built once when the index is loaded.
