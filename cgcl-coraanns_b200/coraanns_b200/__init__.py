@@ -210,11 +210,22 @@ class HybridIndex:
         _check(_lib.cora_reset_buffer(self._h, _ptr(q), n))
 
     # -- search ----------------------------------------------------------------------
-    def search(self, h_queries, topk, nprobe, batch_q=4, num_queries=None):
+    def search(self, h_queries, topk, nprobe, batch_q=4, num_queries=None, out=None):
+        """Search host queries; results go to new arrays, or into `out` = (dists, ids), C
+        arrays of shape (n, topk), float32 / uint32 (e.g. views of pinned host memory, which
+        the device writes directly)."""
         q = np.ascontiguousarray(h_queries, np.float32)
         n = q.shape[0] if num_queries is None else num_queries
-        dists = np.empty((n, topk), np.float32)
-        ids = np.empty((n, topk), np.uint32)
+        if out is None:
+            dists = np.empty((n, topk), np.float32)
+            ids = np.empty((n, topk), np.uint32)
+        else:
+            dists, ids = out
+            if (dists.dtype != np.float32 or ids.dtype != np.uint32
+                    or dists.shape != (n, topk) or ids.shape != (n, topk)
+                    or not dists.flags.c_contiguous or not ids.flags.c_contiguous):
+                raise ValueError("out must be C-contiguous float32 / uint32 arrays of shape "
+                                 "(num_queries, topk)")
         _check(_lib.cora_search(self._h, _ptr(q), n, topk, nprobe, _ptr(dists), _ptr(ids),
                                 int(batch_q)))
         return dists, ids

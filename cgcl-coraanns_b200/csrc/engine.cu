@@ -269,6 +269,7 @@ struct Engine {
     uint64_t vanguard = kDefaultVanguard;
     uint64_t queue_capacity = kDefaultQueueCapacity, spill_capacity = kDefaultSpillCapacity;
     bool profiling = false, candidate_stats = false, gpu_filter_timing = false;
+    bool search_graphs = true;  // replay whole searches from a captured CUDA graph
     bool cross_query_reuse = true, cpu_secondary_filter = true;
     int ip_kernel_type = 0;
     // Upper bound on the HBM buffer holding the vanguard pairs' lower bounds; larger
@@ -306,6 +307,33 @@ struct Engine {
     int split_phase = 0;
     float last_filter_ms = 0.0f;
 
+    // ---- CUDA graph of a whole search (search_host / search_device) ----------------------
+    // A search is ~30 dependent launches plus their host-side set-up (function attributes,
+    // tensor-map encoding); replaying a captured graph costs one launch. The graph is
+    // rebuilt when anything it baked in changes: buffers, shape, stream, or configuration
+    // (ws_gen counts loads and workspace changes).
+    struct GraphKey {
+        const float *d_q = nullptr;
+        uint64_t nq = 0, k = 0, np = 0, ws_gen = 0, vanguard = 0;
+        float *d_od = nullptr;
+        uint32_t *d_oi = nullptr;
+        cudaStream_t st = nullptr;
+        int wsl = 0, twl = 0;
+        bool reuse = false;
+        bool same(const GraphKey &o) const {
+            return d_q == o.d_q && nq == o.nq && k == o.k && np == o.np && ws_gen == o.ws_gen &&
+                   vanguard == o.vanguard && d_od == o.d_od && d_oi == o.d_oi && st == o.st &&
+                   wsl == o.wsl && twl == o.twl && reuse == o.reuse;
+        }
+    };
+    GraphKey graph_key;
+    cudaGraphExec_t graph_exec = nullptr;
+    uint64_t ws_gen = 0;
+    void drop_graph() noexcept {
+        if (graph_exec) cudaGraphExecDestroy(graph_exec);
+        graph_exec = nullptr;
+    }
+
     explicit Engine(int dev) : device(dev) {
         CUDA_TRY(cudaSetDevice(device));
         CUDA_TRY(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
@@ -319,6 +347,7 @@ struct Engine {
     ~Engine() {
         cudaSetDevice(device);
         if (stream) cudaStreamSynchronize(stream);
+        drop_graph();
         free_workspace();
         if (ev_filter0) cudaEventDestroy(ev_filter0);
         if (ev_filter1) cudaEventDestroy(ev_filter1);
@@ -429,6 +458,7 @@ struct Engine {
         CUDA_TRY(cudaGetLastError());
         CUDA_TRY(cudaStreamSynchronize(stream));
         loaded = true;
+        ++ws_gen;
     }
 
     // Loads the whole index, or (shard_world > 1) only the clusters plan_shards() gives this
@@ -570,6 +600,8 @@ struct Engine {
     }
 
     void free_workspace() noexcept {
+        drop_graph();
+        ++ws_gen;
         ws_ready = false;
         ws_q = ws_k = ws_np = ws_vg = cap = 0;
         for (auto *b : {&raw_q, &qr, &qnorm2, &gmat, &cmin, &probe_g, &T0, &T1, &Tcap, &out_d})
@@ -850,9 +882,55 @@ SearchView Engine::search_view() const {
 
 void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, float *d_od,
                             uint32_t *d_oi, cudaStream_t st) {
-    enqueue_front(d_q, nq, k, np, st, nullptr);
-    enqueue_back(nullptr, 0, d_od, d_oi, nullptr);
-    mark(13, st);
+    // graphs need a capturable stream, and stage events / filter timing stay eager
+    const bool special = st == nullptr || st == cudaStreamLegacy || st == cudaStreamPerThread;
+    if (!search_graphs || profiling || gpu_filter_timing || special) {
+        enqueue_front(d_q, nq, k, np, st, nullptr);
+        enqueue_back(nullptr, 0, d_od, d_oi, nullptr);
+        mark(13, st);
+        return;
+    }
+    GraphKey key;
+    key.d_q = d_q;
+    key.nq = nq;
+    key.k = k;
+    key.np = np;
+    key.ws_gen = ws_gen;
+    key.vanguard = vanguard;
+    key.d_od = d_od;
+    key.d_oi = d_oi;
+    key.st = st;
+    key.wsl = warp_select_limit;
+    key.twl = topk_warp_limit;
+    key.reuse = cross_query_reuse;
+    if (!graph_exec || !graph_key.same(key)) {
+        drop_graph();
+        CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
+        try {
+            enqueue_front(d_q, nq, k, np, st, nullptr);
+            enqueue_back(nullptr, 0, d_od, d_oi, nullptr);
+        } catch (...) {
+            cudaGraph_t broken = nullptr;
+            cudaStreamEndCapture(st, &broken);
+            if (broken) cudaGraphDestroy(broken);
+            throw;
+        }
+        cudaGraph_t g = nullptr;
+        CUDA_TRY(cudaStreamEndCapture(st, &g));
+        const cudaError_t ie = cudaGraphInstantiate(&graph_exec, g, 0);
+        cudaGraphDestroy(g);
+        if (ie != cudaSuccess) {
+            graph_exec = nullptr;
+            CUDA_TRY(ie);
+        }
+        graph_key = key;
+    }
+    // the host-side record of the search that the eager path keeps
+    last_stream = st;
+    last_nq = nq;
+    last_k = k;
+    last_np = np;
+    CUDA_TRY(cudaGraphLaunch(graph_exec, st));
 }
 
 // Stages 0..7: rotation, probing, vanguard seeding and seed refinement, then the threshold
@@ -1540,6 +1618,10 @@ int cora_set_tuning(cora_engine *engine, const char *key, int64_t value) {
             if (value < 0) cora::fail(CORA_EINVAL, "vanguard_lows_budget must be >= 0");
             if (e.ws_ready) cora::fail(CORA_ESTATE, "set the lows budget before prepare_workspace");
             e.lows_budget = static_cast<uint64_t>(value);
+        } else if (k == "search_graphs") {
+            if (value != 0 && value != 1) cora::fail(CORA_EINVAL, "search_graphs must be 0 or 1");
+            e.search_graphs = value != 0;
+            if (!e.search_graphs) e.drop_graph();
         } else {
             cora::fail(CORA_EINVAL, "unknown tuning key: " + k);
         }

@@ -165,7 +165,12 @@ int cora_set_vanguard_lows_budget(cora_engine *engine, uint64_t bytes);
  *  "warp_select_limit"     keys (0..256) one warp may collect while selecting the seeds of
  *                          a vanguard pair before it hands the pair to a block-wide
  *                          selection (0 sends every pair to the block selection);
- *  "topk_warp_limit"       the same for the threshold and final top-k of a query (k <= 32). */
+ *  "topk_warp_limit"       the same for the threshold and final top-k of a query (k <= 32);
+ *  "search_graphs"         1 (default): cora_search / cora_search_device replay a captured
+ *                          CUDA graph of the whole search (rebuilt when the buffers, shape,
+ *                          stream or configuration change; not used while profiling or
+ *                          filter timing is on, nor on the legacy default stream); 0: every
+ *                          search launches its kernels one by one. */
 int cora_set_tuning(cora_engine *engine, const char *key, int64_t value);
 /* 1 when the prepared workspace keeps vanguard lower bounds, 0 when it rescans, -1 on NULL. */
 int cora_get_vanguard_mode(const cora_engine *engine);

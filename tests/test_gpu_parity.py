@@ -209,3 +209,34 @@ def test_device_entry_point_matches_host(cb, golden):
     assert dd.cpu().numpy().tobytes() == d_h.tobytes()
     assert np.array_equal(di.cpu().numpy().view(np.uint32), i_h)
     e.close()
+
+
+def test_search_graph_replay_matches_eager(cb, golden):
+    """A search replayed from the captured CUDA graph returns what launching its kernels one
+    by one returns, across shape, threshold and configuration changes (which rebuild or
+    reuse the graph)."""
+    path, z = golden["d96"]
+    q = z["queries"]
+    n = len(q)
+    e = _engine(cb, path=path, nq=n, k=10, nprobe=8)
+    results = {}
+    for graphs in (1, 0):
+        e.set_tuning("search_graphs", graphs)
+        out = []
+        for nq, k, npb in ((n, 10, 8), (n // 2, 5, 4), (n, 10, 8)):
+            for _ in range(2):  # the second call replays the graph of the first
+                e.reset_buffer(q[:nq])
+                d, i = e.search(q[:nq], k, npb)
+                out.append((d.tobytes(), i.tobytes()))
+        e.reset_buffer(q)
+        e.seed_thresholds(np.full(n, 30.0, np.float32))
+        d, i = e.search(q, 10, 8)
+        out.append((d.tobytes(), i.tobytes()))
+        e.set_tuning("warp_select_limit", 8)
+        e.reset_buffer(q)
+        d, i = e.search(q, 10, 8)
+        out.append((d.tobytes(), i.tobytes()))
+        e.set_tuning("warp_select_limit", 256)
+        results[graphs] = out
+    assert results[1] == results[0]
+    e.close()
