@@ -23,16 +23,11 @@ struct ProbeInfo {  // per (query, probe rank), staged in shared memory by refin
     float g;
 };
 
-// One 64-dim block of the full 8-bit code inner product, continuing the fp64 chain `acc`
-// in ascending dimension order (every product is exact in fp64). `e` holds the block's 56
-// ex-code bytes (pack_excode.hpp:216-264 layout: bytes 0..47 carry the low 6 bits of dims
-// 0..47 and 2-bit slices of dims 48..63, bytes 48..55 the top bits), w0 / w1 the 1-bit
-// code words of dims 0..31 / 32..63, x the block's 64 rotated query values.
-//
-// The 8-bit codes c = 128 b + u are decoded four dimensions at a time into the bytes of a
-// word (SWAR), and each byte becomes the double c exactly as (2^52 + c) - 2^52 from its bit
-// pattern, so the loop runs no int or float conversion instructions; x holds the query as
-// doubles (exact widening of the fp32 values).
+// The 8-bit codes c = 128 b + u of dims d0 .. d0 + 3 of one 64-dim block, as the bytes of a
+// word (SWAR). `ew` holds the block's 56 ex-code bytes (pack_excode.hpp:216-264 layout:
+// bytes 0..47 carry the low 6 bits of dims 0..47 and 2-bit slices of dims 48..63, bytes
+// 48..55 the top bits), rbits the bit-reversed 1-bit code word of the block's half that
+// holds d0.
 __device__ __forceinline__ uint32_t code4(const uint32_t (&ew)[14], uint32_t rbits, int d0) {
     uint32_t low;
     if (d0 < 48) {
@@ -52,33 +47,61 @@ __device__ __forceinline__ uint32_t code4(const uint32_t (&ew)[14], uint32_t rbi
     return low | top | msb;
 }
 
-__device__ __forceinline__ double block_code_ip(const double *__restrict__ x,
-                                                const uint64_t (&e)[7], uint32_t w0, uint32_t w1,
-                                                double acc) {
-    uint32_t ew[14];
-#pragma unroll
-    for (int t = 0; t < 7; ++t) {
-        ew[2 * t] = static_cast<uint32_t>(e[t]);
-        ew[2 * t + 1] = static_cast<uint32_t>(e[t] >> 32);
+// One CTA per cluster, at load: the refine rows (the 8-bit codes c = 128 b + u of every
+// dimension, decoded by code4 from the ex codes and the 1-bit code words in the scan planes)
+// and the meta words {f_add_ex, f_rescale_ex, id, 0} of its vectors.
+__global__ void __launch_bounds__(256) build_refine_rows_kernel(
+    const uint8_t *__restrict__ long_codes, const float2 *__restrict__ exf,
+    const uint32_t *__restrict__ ids, const uint4 *__restrict__ scan4,
+    const uint32_t *__restrict__ cl_start, const uint32_t *__restrict__ cl_size, int D, int G16,
+    int LC, uint8_t *__restrict__ rows, uint4 *__restrict__ meta) {
+    const int c = blockIdx.x;
+    const uint32_t s = cl_start[c], n = cl_size[c];
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const size_t gid = (size_t)s + i;
+        uint32_t *row = reinterpret_cast<uint32_t *>(rows + gid * D);
+        for (int blk = 0; blk < D / 64; ++blk) {
+            // 56 ex-code bytes of the block (rows of LC = 7 D / 8 bytes: 8-byte aligned)
+            const uint32_t *eb =
+                reinterpret_cast<const uint32_t *>(long_codes + gid * LC + 56 * blk);
+            uint32_t ew[14];
+            for (int t = 0; t < 14; ++t) ew[t] = eb[t];
+            const uint4 cw = scan4[(size_t)(G16 + 1) * s + (size_t)(blk / 2) * n + i];
+            const uint32_t w0 = (blk & 1) ? cw.z : cw.x, w1 = (blk & 1) ? cw.w : cw.y;
+            const uint32_t r0 = __brev(w0), r1 = __brev(w1);
+            for (int d0 = 0; d0 < 64; d0 += 4)
+                row[(64 * blk + d0) / 4] = code4(ew, d0 < 32 ? r0 : r1, d0);
+        }
+        const float2 f = exf[gid];
+        meta[gid] = make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), ids[gid], 0u);
     }
-    const uint32_t r0 = __brev(w0), r1 = __brev(w1);
+}
+
+// One 64-dim block of the 8-bit code inner product, continuing the fp64 chain `acc` in
+// ascending dimension order (every product is exact in fp64); v holds the block's 64 codes,
+// x its 64 rotated query values. Each byte becomes the double c exactly as
+// (2^52 + c) - 2^52 from its bit pattern, so the loop runs no conversion instructions.
+__device__ __forceinline__ double block_code8_ip(const double *__restrict__ x, const uint4 (&v)[4],
+                                                 double acc) {
 #pragma unroll
-    for (int d0 = 0; d0 < 64; d0 += 4) {
-        const uint32_t c4 = code4(ew, d0 < 32 ? r0 : r1, d0);
+    for (int t = 0; t < 4; ++t) {
+        const uint32_t w4[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t c = __byte_perm(c4, 0u, 0x4440u | i);
-            const double cd = __dsub_rn(__hiloint2double(0x43300000, static_cast<int>(c)),
-                                        4503599627370496.0);
-            acc = __fma_rn(x[d0 + i], cd, acc);
+        for (int h = 0; h < 4; ++h) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t c = __byte_perm(w4[h], 0u, 0x4440u | i);
+                const double cd = __dsub_rn(__hiloint2double(0x43300000, static_cast<int>(c)),
+                                            4503599627370496.0);
+                acc = __fma_rn(x[16 * t + 4 * h + i], cd, acc);
+            }
         }
     }
     return acc;
 }
 
-// One CTA per query, one thread per candidate: a candidate's refine row (ex code and 1-bit
-// code, D bytes, 32-byte sectors used whole) and its meta word are loaded before its fp64
-// chain, so a candidate costs one memory round trip. mode 0 refines the vanguard seeds [0, cnt) and records the seed count; mode 1
+// One CTA per query, one thread per candidate: a candidate's refine row (its 8-bit codes, D
+// bytes, 32-byte sectors used whole) and its meta word are loaded before its fp64 chain. mode 0 refines the vanguard seeds [0, cnt) and records the seed count; mode 1
 // refines the main candidates [seed_cnt, cnt). Dynamic shared memory: D floats + nprobe
 // ProbeInfo.
 __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, SearchView sv,
@@ -126,40 +149,11 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
         const float2 f = make_float2(__uint_as_float(mt.x), __uint_as_float(mt.y));
         const uint32_t id = mt.z;
         double acc = 0.0;
-        for (int g = 0; 2 * g < nblocks; ++g) {
-            const uint4 *gr = row + 8 * g;
-            uint64_t lo[7], hi[7];
-            if (2 * g + 1 < nblocks) {
-                // a full 128-dim group: 112 ex-code bytes then the 4 code words (128 bytes)
-                uint4 v[8];
+        for (int blk = 0; blk < nblocks; ++blk) {
+            uint4 v[4];
 #pragma unroll
-                for (int t = 0; t < 8; ++t) v[t] = __ldg(gr + t);
-                uint64_t e[14];
-#pragma unroll
-                for (int t = 0; t < 7; ++t) {
-                    e[2 * t] = (uint64_t(v[t].y) << 32) | v[t].x;
-                    e[2 * t + 1] = (uint64_t(v[t].w) << 32) | v[t].z;
-                }
-#pragma unroll
-                for (int t = 0; t < 7; ++t) {
-                    lo[t] = e[t];
-                    hi[t] = e[7 + t];
-                }
-                acc = block_code_ip(x + 128 * g, lo, v[7].x, v[7].y, acc);
-                acc = block_code_ip(x + 128 * g + 64, hi, v[7].z, v[7].w, acc);
-            } else {
-                // a last 64-dim block: 56 ex-code bytes then its 2 code words (64 bytes)
-                uint4 v[4];
-#pragma unroll
-                for (int t = 0; t < 4; ++t) v[t] = __ldg(gr + t);
-#pragma unroll
-                for (int t = 0; t < 3; ++t) {
-                    lo[2 * t] = (uint64_t(v[t].y) << 32) | v[t].x;
-                    lo[2 * t + 1] = (uint64_t(v[t].w) << 32) | v[t].z;
-                }
-                lo[6] = (uint64_t(v[3].y) << 32) | v[3].x;
-                acc = block_code_ip(x + 128 * g, lo, v[3].z, v[3].w, acc);
-            }
+            for (int t = 0; t < 4; ++t) v[t] = __ldg(row + 4 * blk + t);
+            acc = block_code8_ip(x + 64 * blk, v, acc);
         }
         const float ex_d = __fadd_rn(__fadd_rn(f.x, p.g),
                                      __fmul_rn(f.y, __fadd_rn(__double2float_rn(acc), kb)));

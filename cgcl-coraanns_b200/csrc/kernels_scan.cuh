@@ -65,8 +65,8 @@ struct IndexView {
     const float4 *chunk_range;
     const uint32_t *cl_chunk;    // nlist + 1
     const float4 *cl_range;      // nlist
-    // refine rows (build_refine_rows_kernel): per vector D bytes, for each 128-dim group
-    // its 112 ex-code bytes then its 4 code words (a last 64-dim block: 56 + 8 bytes)
+    // refine rows (build_refine_rows_kernel): per vector its D 8-bit codes c = 128 b + u
+    // (b the 1-bit code, u the 7-bit ex code), one byte per dimension
     const uint4 *rows;           // N x D / 16
     const uint4 *meta;           // N: {f_add_ex, f_rescale_ex, id, 0}
     int nlist, D, G16, LC;
@@ -281,38 +281,6 @@ __global__ void __launch_bounds__(256) chunk_ranges_kernel(const uint4 *__restri
             acc = make_float4(fminf(acc.x, s_red[w].x), fmaxf(acc.y, s_red[w].y),
                               fmaxf(acc.z, s_red[w].z), fmaxf(acc.w, s_red[w].w));
         cl_range[c] = acc;
-    }
-}
-
-// One CTA per cluster: the refine rows and meta words of its vectors, from the ex codes
-// (LC = 7 D / 8 bytes per vector, 56 per 64-dim block), the 1-bit code words in the scan
-// planes, the ex factors and the ids. Built once when the index is loaded.
-__global__ void __launch_bounds__(256) build_refine_rows_kernel(
-    const uint8_t *__restrict__ long_codes, const float2 *__restrict__ exf,
-    const uint32_t *__restrict__ ids, const uint4 *__restrict__ scan4,
-    const uint32_t *__restrict__ cl_start, const uint32_t *__restrict__ cl_size, int D, int G16,
-    int LC, uint8_t *__restrict__ rows, uint4 *__restrict__ meta) {
-    const int c = blockIdx.x;
-    const uint32_t s = cl_start[c], n = cl_size[c];
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-        const size_t gid = (size_t)s + i;
-        const uint8_t *ex = long_codes + gid * LC;
-        uint8_t *row = rows + gid * D;
-        for (int g = 0; g < G16; ++g) {
-            const bool full = 128 * g + 128 <= D;
-            const int exb = full ? 112 : 56;
-            for (int b = 0; b < exb; ++b) row[128 * g + b] = ex[112 * g + b];
-            const uint4 cw = scan4[(size_t)(G16 + 1) * s + (size_t)g * n + i];
-            uint32_t *w = reinterpret_cast<uint32_t *>(row + 128 * g + exb);
-            w[0] = cw.x;
-            w[1] = cw.y;
-            if (full) {
-                w[2] = cw.z;
-                w[3] = cw.w;
-            }
-        }
-        const float2 f = exf[gid];
-        meta[gid] = make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), ids[gid], 0u);
     }
 }
 
@@ -740,7 +708,10 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
                         else
                             ip = ip_int_from_planes<G16>(code[v], P, bias[v]);
                         const float4 pj = s_par[j];
-                        const float ip1 = __fadd_rn(__fmul_rn(pj.x, (float)ip), 0.0f);
+                        // ip1 = width * ip_int (+ 0 in the reference: width >= 1e-30 and
+                        // |ip_int| >= 1 or ip_int = 0 give a normal or +0 product, which the
+                        // addition of 0 leaves unchanged)
+                        const float ip1 = __fmul_rn(pj.x, (float)ip);
                         const float low = lower_bound_dist(f[v], ip1, pj.y, pj.z, pj.w);
                         if (kWriteLows) {
                             if (valid[v] && s_bnd[j] != ~0ull) sv.lows[s_bnd[j] + v0 + i] = low;
@@ -923,40 +894,35 @@ __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
     const float4 *L4 = reinterpret_cast<const float4 *>(sv.lows + sv.vg_off[pi]);
     const float T0 = sv.T0[q];
     const int S = sv.keep;
-    // Pass 1: count of lows < T0 and each lane's smallest low. S lanes hold a low <= tau_f
-    // (the S-th smallest lane minimum), so the S smallest keys all have low <= tau_f.
+    // Pass 1: each lane's smallest low (NaN lows drop out of fminf). tau_f, the S-th
+    // smallest lane minimum, bounds the seeds: when tau_f < T0 the S lanes at or below it
+    // hold S lows <= tau_f below T0, so the S smallest keys all have low <= tau_f; when
+    // tau_f >= T0 every low < T0 is collected.
     const float inf = __int_as_float(0x7f800000);
-    uint32_t cnt = 0;
     float mn = inf;
     for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
         float l[4 * kLowsUnroll];
         load_lows4(L4, n, b4 + lane, l);
 #pragma unroll
-        for (int e = 0; e < 4 * kLowsUnroll; ++e) {
-            const bool below = l[e] < T0;
-            cnt += below ? 1u : 0u;
-            mn = fminf(mn, below ? l[e] : inf);
-        }
+        for (int e = 0; e < 4 * kLowsUnroll; ++e) mn = fminf(mn, l[e]);
     }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, off);
-    const uint32_t total = cnt;
-    float tau_f = inf;  // every low < T0 is a seed when there are at most S
-    if (total > static_cast<uint32_t>(S))
-        tau_f = unord_f32(static_cast<uint32_t>(
-            __shfl_sync(0xffffffffu, warp_sort_lane_keys(make_key(mn, lane), lane), S - 1) >> 32));
-    // Pass 2: collect every key with low < T0 and low <= tau_f (-0 and +0 compare equal
-    // here, so the set contains every key the exact bound would take)
+    const float tau_f = unord_f32(static_cast<uint32_t>(
+        __shfl_sync(0xffffffffu, warp_sort_lane_keys(make_key(mn, lane), lane), S - 1) >> 32));
+    // Pass 2: count the lows < T0 and collect every key with low < T0 and low <= tau_f (-0
+    // and +0 compare equal here, so the set contains every key the exact bound would take)
     const float *L = sv.lows + sv.vg_off[pi];
     uint64_t *b = buf[w];
-    uint32_t m = 0;
+    uint32_t m = 0, cnt = 0;
     for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
         float l[4 * kLowsUnroll];
         load_lows4(L4, n, b4 + lane, l);
         uint32_t take = 0;
 #pragma unroll
-        for (int e = 0; e < 4 * kLowsUnroll; ++e)
-            take |= (l[e] < T0 && l[e] <= tau_f ? 1u : 0u) << e;
+        for (int e = 0; e < 4 * kLowsUnroll; ++e) {
+            const bool below = l[e] < T0;
+            cnt += below ? 1u : 0u;
+            take |= (below && l[e] <= tau_f ? 1u : 0u) << e;
+        }
         const uint32_t mine = __popc(take);
         const uint32_t incl = warp_inclusive_sum(mine, lane);
         const uint32_t got = __shfl_sync(0xffffffffu, incl, 31);
@@ -967,6 +933,7 @@ __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
         }
         m += got;
     }
+    const uint32_t total = __reduce_add_sync(0xffffffffu, cnt);
     if (m > static_cast<uint32_t>(sv.warp_select_limit)) {
         if (lane == 0) fallback[1 + atomicAdd(fallback, 1u)] = static_cast<uint32_t>(pi);
         return;
@@ -976,7 +943,13 @@ __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
     for (int i = m + lane; i < sort_n; i += 32) b[i] = kKeyMax;
     __syncwarp();
     warp_sort_smem(b, sort_n, lane);
-    const int nkeep = min(static_cast<int>(total), S);
+    // the collection holds every seed (at least min(total, S) keys); a shortfall would mean
+    // a broken bound, reported instead of emitting ids that are not in the index
+    int nkeep = min(static_cast<int>(total), S);
+    if (static_cast<int>(m) < nkeep) {
+        if (lane == 0) atomicOr(sv.err, kDevBadInput);
+        nkeep = static_cast<int>(m);
+    }
     uint32_t slot0 = 0;
     if (lane == 0) {
         slot0 = nkeep ? atomicAdd(sv.cand_cnt + q, static_cast<uint32_t>(nkeep)) : 0u;
