@@ -288,6 +288,7 @@ struct Engine {
         n_items, out_i;
     DevBuf<int> probe_ids, item_counter, err;
     DevBuf<uint32_t> select_fallback;  // [0] count, [1..] vanguard pairs for block selection
+    DevBuf<uint32_t> filt_list;        // [0] count, [1..] vanguard pairs the lows filter reads
     DevBuf<uint64_t> bound, cand_rec, cand_key, vg_off;
     DevBuf<unsigned long long> lows_top;
     DevBuf<float> lows;
@@ -566,6 +567,7 @@ struct Engine {
         bound.alloc(max_q * std::max<uint64_t>(ws_vg, 1));
         vg_off.alloc(max_q * std::max<uint64_t>(ws_vg, 1) + 1);
         select_fallback.alloc(max_q * std::max<uint64_t>(ws_vg, 1) + 1);
+        filt_list.alloc(max_q * std::max<uint64_t>(ws_vg, 1) + 1);
         {
             // worst case of the lows buffer: every query probes the ws_vg largest clusters
             uint64_t worst = 0;
@@ -618,6 +620,7 @@ struct Engine {
         vg_off.release();
         lows_top.release();
         select_fallback.release();
+        filt_list.release();
         lows.release();
         cand_rec.release();
         cand_key.release();
@@ -1111,7 +1114,9 @@ void Engine::enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uin
     dispatch_scan(G16, L, ScanPhase::kMain);
     mark(10, st);
     if (lows_mode) {
-        vanguard_filter_kernel<<<(n_van + 7) / 8, 256, 0, st>>>(ix, sv, own);
+        CUDA_TRY(cudaMemsetAsync(filt_list.p, 0, 4, st));
+        filter_list_kernel<<<(n_van + 255) / 256, 256, 0, st>>>(ix, sv, own, filt_list.p);
+        vanguard_filter_kernel<<<(n_van + 7) / 8, 256, 0, st>>>(ix, sv, filt_list.p);
         CUDA_TRY(cudaGetLastError());
     }
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));

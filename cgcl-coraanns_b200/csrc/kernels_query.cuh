@@ -299,14 +299,23 @@ __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
     for (int cb = 0; cb < nchunk; cb += 32) {
         const int c = cb + lane;
         uint32_t chunks = __ballot_sync(0xffffffffu, c < nchunk && (double)__ldg(cm + c) <= bound);
-        while (chunks) {  // warp-uniform: the chunks that can hold a band member
-            const int col = 32 * (cb + __ffs(chunks) - 1) + lane;
-            chunks &= chunks - 1;
-            const bool take = col < nlist && (double)__ldg(row + col) <= bound;
-            const uint32_t m = __ballot_sync(0xffffffffu, take);
-            const uint32_t pos = cnt + __popc(m & ((1u << lane) - 1u));
-            if (take && pos < kGuardWarpBand) cidx[pos] = static_cast<uint32_t>(col);
-            cnt += __popc(m);
+        while (chunks) {  // warp-uniform: the chunks that can hold a band member, 4 at a time
+            int col[4];
+            float v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {  // every load first: one round trip per 4 chunks
+                col[u] = chunks ? 32 * (cb + __ffs(chunks) - 1) + lane : nlist;
+                chunks &= chunks - 1;
+                v[u] = col[u] < nlist ? __ldg(row + col[u]) : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const bool take = col[u] < nlist && (double)v[u] <= bound;
+                const uint32_t m = __ballot_sync(0xffffffffu, take);
+                const uint32_t pos = cnt + __popc(m & ((1u << lane) - 1u));
+                if (take && pos < kGuardWarpBand) cidx[pos] = static_cast<uint32_t>(col[u]);
+                cnt += __popc(m);
+            }
         }
     }
     if (cnt > kGuardWarpBand) {

@@ -287,13 +287,17 @@ __global__ void __launch_bounds__(256) topk_warp_kernel(SearchView sv, int mode,
     __shared__ uint64_t buf[8][kWarpTopBuf];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int q = blockIdx.x * 8 + w;
+    if (mode == 1 && threadIdx.x == 0) {  // candidates submitted: one atomic per CTA
+        unsigned long long sum = 0;
+        for (int j = blockIdx.x * 8; j < min(sv.nq, blockIdx.x * 8 + 8); ++j) sum += sv.cand_cnt[j];
+        atomicAdd(stats, sum);
+    }
     if (q >= sv.nq) return;  // whole warp
     const float T0 = sv.T0[q];
     const uint32_t cnt = sv.cand_cnt[q];
     const uint32_t n = mode == 0 ? sv.seed_cnt[q] : min(cnt, static_cast<uint32_t>(sv.cap));
     const uint64_t *keys = sv.cand_key + (size_t)q * sv.cap;
     const int k = sv.k;
-    if (mode == 1 && lane == 0) atomicAdd(stats, static_cast<unsigned long long>(cnt));
     auto key_at = [&](uint32_t i) -> uint64_t {
         const uint64_t key = keys[i];
         return unord_f32(static_cast<uint32_t>(key >> 32)) < T0 ? key : kKeyMax;

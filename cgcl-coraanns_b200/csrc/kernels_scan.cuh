@@ -815,43 +815,60 @@ __device__ __forceinline__ uint32_t lows_index(uint32_t b4, int lane, int e) {
     return 4 * (b4 + lane + 32 * (e >> 2)) + (e & 3);
 }
 
-// One warp per vanguard pair (8 per CTA): candidates low < T1 that are not seeds
-// (key > boundary), read from the pair's stored lows. A pair whose cluster's factor range
-// proves every low >= T1 (range_at_least) has none and reads nothing.
-__global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, SearchView sv,
-                                                              const uint8_t *__restrict__ owned) {
+// The vanguard pairs the lows filter must read: owned by this shard and not proven
+// candidate-free against T1 by their cluster's factor range (range_at_least). Appended to
+// list[1..] (count in list[0], zeroed by the caller) with one atomic per warp.
+__global__ void __launch_bounds__(256) filter_list_kernel(IndexView ix, SearchView sv,
+                                                          const uint8_t *__restrict__ owned,
+                                                          uint32_t *__restrict__ list) {
+    const int pi = blockIdx.x * blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & 31;
-    const int pi = blockIdx.x * 8 + (threadIdx.x >> 5);
-    if (pi >= sv.nq * sv.veff) return;  // warp-uniform
+    bool keep = false;
+    if (pi < sv.nq * sv.veff) {
+        const int q = pi / sv.veff, r = pi % sv.veff;
+        const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
+        if (!owned || owned[c]) {
+            const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
+            const QueryScalars qs = sv.scal[q];
+            keep = !range_at_least(ix.cl_range[c], g,
+                                   ip_term_bound(sv.qrange[q], qs.width, qs.k1),
+                                   __fsqrt_rn(fmaxf(g, 0.0f)), sv.T1[q]);
+        }
+    }
+    const uint32_t mask = __ballot_sync(0xffffffffu, keep);
+    if (!mask) return;
+    uint32_t base = 0;
+    if (lane == 0) base = atomicAdd(list, __popc(mask));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    if (keep) list[1 + base + __popc(mask & ((1u << lane) - 1u))] = static_cast<uint32_t>(pi);
+}
+
+// One warp per listed vanguard pair (filter_list_kernel; 8 per CTA, warps past the list's
+// count exit): candidates low < T1 that are not seeds (key > boundary), read from the
+// pair's stored lows.
+__global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, SearchView sv,
+                                                              const uint32_t *__restrict__ list) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t li = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (li >= list[0]) return;  // warp-uniform
+    const int pi = static_cast<int>(list[1 + li]);
     const int q = pi / sv.veff, r = pi % sv.veff;
     const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
-    if (owned && !owned[c]) return;
     const uint32_t s = ix.cl_start[c];
     const uint32_t n = ix.cl_size[c];
     const float T1 = sv.T1[q];
-    {
-        const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
-        const QueryScalars qs = sv.scal[q];
-        if (range_at_least(ix.cl_range[c], g, ip_term_bound(sv.qrange[q], qs.width, qs.k1),
-                           __fsqrt_rn(fmaxf(g, 0.0f)), T1))
-            return;  // warp-uniform
-    }
     const float4 *L4 = reinterpret_cast<const float4 *>(sv.lows + sv.vg_off[pi]);
     const uint64_t bnd = sv.bound[(size_t)q * sv.veff + r];
-    const float *L = sv.lows + sv.vg_off[pi];
     const uint64_t rtag = static_cast<uint64_t>(r) << 32;
     for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
         float l[4 * kLowsUnroll];
         load_lows4(L4, n, b4 + lane, l);
-        uint32_t take = 0;  // bit e: element e of this lane's batch is below T1
+        // bit e: element e of this lane's batch is below T1 and not a seed (key above the
+        // boundary; the padding reads as +inf)
+        uint32_t take = 0;
 #pragma unroll
-        for (int e = 0; e < 4 * kLowsUnroll; ++e) take |= (l[e] < T1 ? 1u : 0u) << e;
-        // the few elements below T1: drop the seeds (key at or below the boundary)
-        for (uint32_t m = take; m; m &= m - 1) {
-            const int e = __ffs(m) - 1;
-            const uint32_t i = lows_index(b4, lane, e);
-            if (make_key(L[i], s + i) <= bnd) take &= ~(1u << e);
-        }
+        for (int e = 0; e < 4 * kLowsUnroll; ++e)
+            if (l[e] < T1 && make_key(l[e], s + lows_index(b4, lane, e)) > bnd) take |= 1u << e;
         // one warp prefix sum and one slot reservation per batch
         const uint32_t mine = __popc(take);
         const uint32_t incl = warp_inclusive_sum(mine, lane);
