@@ -532,7 +532,8 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
     uint4 *stage = reinterpret_cast<uint4 *>(smem_raw);
     uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + S * SE);
     __shared__ __align__(8) uint64_t bars[S];
-    __shared__ uint64_t s_bnd[kMaxPairsPerItem];
+    __shared__ uint64_t s_bnd[kMaxPairsPerItem];  // main pass: each pair's seed boundary key
+    __shared__ float *s_lp[kMaxPairsPerItem];     // lows pass: each pair's lows slice
     // per pair: {width, g, k1, sqrt(max(g, 0))} (one 16-byte read per evaluation)
     __shared__ float4 s_par[kMaxPairsPerItem];
     __shared__ float s_T1[kMaxPairsPerItem], s_M[kMaxPairsPerItem];
@@ -563,10 +564,6 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
         const size_t cbase = (size_t)(G16 + 1) * s;
         const int ntiles = (n + TV - 1) / TV;
         const uint32_t chunk0 = kWriteLows ? 0u : ix.cl_chunk[c];
-        if (kWriteLows && threadIdx.x == 0)  // the first S - 1 tiles go out at once
-            for (int u = 0; u < S - 1 && u < ntiles; ++u)
-                issue_tile<G16, TV>(stage + u * SE, &bars[u], ix.scan4, cbase, n, u * TV,
-                                    min(TV, n - u * TV));
         if (kWriteLows) {
             if (threadIdx.x == 0) {
                 const unsigned long long need =
@@ -589,13 +586,14 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
             s_r[threadIdx.x] = r;
             s_par[threadIdx.x] = make_float4(qs.width, g, qs.k1, __fsqrt_rn(fmaxf(g, 0.0f)));
             if (kWriteLows) {
-                // slice offset of this vanguard pair, carried in s_bnd (~0: not stored)
+                // slice of this vanguard pair (offset 0 when the buffer is full: the search
+                // reports the overflow, and the readers of the slice stay in bounds)
                 const unsigned long long b = s_lbase;
                 const uint64_t off =
                     b == ~0ull ? 0ull
                                : b + (uint64_t)threadIdx.x * lows_slice(static_cast<uint32_t>(n));
                 sv.vg_off[(size_t)q * sv.veff + r] = off;
-                s_bnd[threadIdx.x] = b == ~0ull ? ~0ull : off;
+                s_lp[threadIdx.x] = sv.lows + off;
                 if (b != ~0ull)  // the slice's padding reads as +inf (never below a threshold)
                     for (uint32_t p = n; p < lows_slice(static_cast<uint32_t>(n)); ++p)
                         sv.lows[off + p] = __int_as_float(0x7f800000);
@@ -607,7 +605,13 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
         }
         __syncthreads();
         uint32_t keep = pc == 32 ? ~0u : (1u << pc) - 1u;
-        if (!kWriteLows) {
+        if (kWriteLows) {
+            if (s_lbase == ~0ull) continue;  // no room for the lows: the search fails anyway
+            if (threadIdx.x == 0)  // the first S - 1 tiles go out at once
+                for (int u = 0; u < S - 1 && u < ntiles; ++u)
+                    issue_tile<G16, TV>(stage + u * SE, &bars[u], ix.scan4, cbase, n, u * TV,
+                                        min(TV, n - u * TV));
+        } else {
             if (warp == 0) {
                 bool need = false;
                 if (lane < pc) {
@@ -696,8 +700,10 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
                     else
                         bias[v] = code_bias<G16>(code[v]);
                 }
-                for (uint32_t mj = wkeep; mj; mj &= mj - 1u) {
-                    const int j = __ffs(mj) - 1;
+                // lows pass: every pair in order; main pass: the pairs this warp's chunk keeps
+                for (uint32_t mj = wkeep, jj = 0; kWriteLows ? jj < static_cast<uint32_t>(pc) : mj != 0;
+                     mj &= mj - 1u, ++jj) {
+                    const int j = kWriteLows ? static_cast<int>(jj) : __ffs(mj) - 1;
                     const uint32_t *P = s_planes + j * 8 * W4;
 #pragma unroll
                     for (int v = 0; v < V; ++v) {
@@ -714,7 +720,7 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
                         const float ip1 = __fmul_rn(pj.x, (float)ip);
                         const float low = lower_bound_dist(f[v], ip1, pj.y, pj.z, pj.w);
                         if (kWriteLows) {
-                            if (valid[v] && s_bnd[j] != ~0ull) sv.lows[s_bnd[j] + v0 + i] = low;
+                            if (valid[v]) s_lp[j][v0 + i] = low;
                         } else {
                             const uint32_t gid = s + static_cast<uint32_t>(v0 + i);
                             const bool cand =
