@@ -83,8 +83,6 @@ int main(int argc, char **argv) {
         const std::size_t scap = opt.get_size("queue-spill-capacity", coraanns::queue::default_spill_capacity);
         if (qcap == 0 || (qcap & (qcap - 1)) != 0)
             throw std::invalid_argument("queue-capacity must be a positive power of two");
-        if (!opt.get("exact-base", "").empty())
-            throw std::invalid_argument("--exact-base (FP32 diagnostic refine) is not implemented by this engine");
 
         std::cout << "Loading queries and groundtruth..." << std::endl;
         const Matrix<float> query = load_vectors<float>(query_file);
@@ -99,6 +97,24 @@ int main(int argc, char **argv) {
         coraanns::HybridIndex index;
         index.load_index_file(index_file);
         const auto shape = index.index_info();
+        // --exact-base: FP32 diagnostic refine against a mapped base (apps/search.cpp:126-146,
+        // 171-175); exact distances are squared L2, the metric of the hybrid search path
+        std::unique_ptr<MappedVectors> exact_base;
+        const std::string exact_base_file = opt.get("exact-base", "");
+        if (!exact_base_file.empty()) {
+            exact_base = std::make_unique<MappedVectors>(exact_base_file);
+            if (exact_base->rows() != shape.num_vectors || exact_base->dim() != shape.dim) {
+                std::cerr << "Exact-refine base shape mismatch: file=" << exact_base->rows() << 'x'
+                          << exact_base->dim() << ", index=" << shape.num_vectors << 'x'
+                          << shape.dim << '\n';
+                return 1;
+            }
+            std::cout << "Exact FP32 refine enabled with mmap base: " << exact_base_file << " ("
+                      << exact_base->rows() << 'x' << exact_base->dim() << ")\n";
+            index.enable_exact_refine(exact_base->mapping(), exact_base->rows(), exact_base->dim(),
+                                      exact_base->row_stride_bytes(),
+                                      exact_base->data_offset_bytes());
+        }
         std::unique_ptr<RecallEvaluator> evaluator;
         if (!recall_once)
             evaluator = std::make_unique<RecallEvaluator>(query.data.data(), nq, dim, gt, topk, recall_base);

@@ -31,7 +31,8 @@ CORA_OK, CORA_EINVAL, CORA_ESTATE, CORA_ERUNTIME, CORA_ECUDA, CORA_ENOMEM = rang
 EXPORTS = [
     "cora_last_error", "cora_create", "cora_destroy", "cora_load_from_raw_pointers",
     "cora_load_index_file", "cora_index_info", "cora_prepare_workspace", "cora_free_workspace",
-    "cora_reset_buffer", "cora_search", "cora_search_device", "cora_check_device",
+    "cora_reset_buffer", "cora_enable_exact_refine", "cora_search", "cora_search_device",
+    "cora_check_device",
     "cora_seed_thresholds", "cora_capture_thresholds", "cora_set_vanguard_size",
     "cora_get_vanguard_size", "cora_set_queue_capacity", "cora_set_queue_spill_capacity",
     "cora_get_queue_capacity", "cora_set_profiling", "cora_set_candidate_stats",
@@ -66,6 +67,7 @@ _sig("cora_index_info", C.c_int, _p, _p)
 _sig("cora_prepare_workspace", C.c_int, _p, _u64, _u64, _u64)
 _sig("cora_free_workspace", None, _p)
 _sig("cora_reset_buffer", C.c_int, _p, _p, _u64)
+_sig("cora_enable_exact_refine", C.c_int, _p, _p, _u64, _u64, _u64, _u64)
 _sig("cora_search", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p, C.c_int)
 _sig("cora_search_device", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p, _p)
 _sig("cora_check_device", C.c_int, _p)
@@ -203,6 +205,24 @@ class HybridIndex:
 
     def free_workspace(self):
         _lib.cora_free_workspace(self._h)
+
+    def enable_exact_refine(self, base=None, base_rows=None, base_dim=None,
+                            row_stride_bytes=None, data_offset_bytes=0):
+        """enable_exact_refine (hybrid.cuh:171-178). `base`: a float32 (rows, dim) array
+        whose row i is the vector with original id i (its rows are copied into HBM by this
+        call, or at load), or a raw pointer with the four sizes as in the C ABI; None turns
+        exact refinement off."""
+        if base is None:
+            _check(_lib.cora_enable_exact_refine(self._h, None, 0, 0, 0, 0))
+            return
+        if isinstance(base, np.ndarray):
+            b = np.ascontiguousarray(base, np.float32)
+            self._exact_base = b  # borrowed until the rows are in HBM
+            _check(_lib.cora_enable_exact_refine(self._h, _ptr(b), b.shape[0], b.shape[1],
+                                                 b.shape[1] * 4, 0))
+            return
+        _check(_lib.cora_enable_exact_refine(self._h, C.c_void_p(base), base_rows, base_dim,
+                                             row_stride_bytes, data_offset_bytes))
 
     def reset_buffer(self, h_queries, num_queries=None):
         q = np.ascontiguousarray(h_queries, np.float32)

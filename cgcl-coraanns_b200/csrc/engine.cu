@@ -260,6 +260,13 @@ struct Engine {
     float cmax = 0.0f;                          // max ||c'|| (rounded up)
     DevBuf<uint4> scan4;
     DevBuf<uint4> rows, meta;  // refine rows (N x D bytes) and meta words (see IndexView)
+    std::vector<uint32_t> h_ids;  // original id of every loaded vector (exact refinement)
+    // exact FP32 refinement (hybrid.cuh:171-178): the caller's base, borrowed like the
+    // reference's mapping, and its rows gathered into HBM in this engine's vector order
+    const uint8_t *xb_map = nullptr;
+    uint64_t xb_rows = 0, xb_dim = 0, xb_stride = 0, xb_offset = 0;
+    DevBuf<float> exact_base;
+    DevBuf<uint8_t> exact_ok;
     DevBuf<uint32_t> cl_start, cl_size;
     DevBuf<uint32_t> cl_chunk;              // first 32-vector chunk of each cluster (nlist + 1)
     DevBuf<float4> chunk_range, cl_range;   // factor ranges per chunk / per cluster
@@ -299,6 +306,7 @@ struct Engine {
 
     // last-search state
     uint64_t last_nq = 0, last_k = 0, last_np = 0, last_submitted = 0, last_refined = 0;
+    const float *last_dq = nullptr;  // device queries of the search in progress
 
     // cluster sharding (set before loading): this engine keeps the clusters plan_shards()
     // gives `shard_rank` of `shard_world`; split_phase tracks a sharded search in progress
@@ -431,6 +439,7 @@ struct Engine {
         CUDA_TRY(cudaMemcpy(tmp_long.p, h_long, N * LC, cudaMemcpyHostToDevice));
         CUDA_TRY(cudaMemcpy(tmp_exf.p, h_exf, N * 8, cudaMemcpyHostToDevice));
         CUDA_TRY(cudaMemcpy(tmp_ids.p, h_ids, N * 4, cudaMemcpyHostToDevice));
+        this->h_ids.assign(h_ids, h_ids + N);
         // Repack the adapter's word-major 1-bit codes + float[N][3] factors into scan planes.
         DevBuf<uint32_t> tmp_short;
         DevBuf<float> tmp_fac;
@@ -460,6 +469,55 @@ struct Engine {
         CUDA_TRY(cudaStreamSynchronize(stream));
         loaded = true;
         ++ws_gen;
+        if (xb_map) build_exact_base();
+    }
+
+    // enable_exact_refine (hybrid.cuh:171-178): nullptr turns it off. The reference keeps
+    // the host mapping and reads rows during its CPU refinement; here the rows this engine
+    // needs are copied into HBM (now, or when the index is loaded), in vector order.
+    void enable_exact_refine(const uint8_t *mapping, uint64_t rows, uint64_t bdim,
+                             uint64_t stride, uint64_t offset) {
+        if (mapping && bdim == dim && rows && stride < bdim * 4)
+            fail(CORA_EINVAL, "exact base row stride is shorter than a row");
+        xb_map = mapping;
+        xb_rows = rows;
+        xb_dim = bdim;
+        xb_stride = stride;
+        xb_offset = offset;
+        drop_graph();
+        ++ws_gen;
+        if (!mapping) {
+            exact_base.release();
+            exact_ok.release();
+            return;
+        }
+        if (loaded) build_exact_base();
+    }
+    void build_exact_base() {
+        const bool same_dim = xb_dim == dim;
+        exact_base.alloc(std::max<uint64_t>(N * dim, 1));
+        exact_ok.alloc(std::max<uint64_t>(N, 1));
+        // rows whose id lies outside the base (or every row when the dimension differs)
+        // are marked missing and their candidates dropped, as the reference skips them
+        // (cpu_refinement.cpp:169-172)
+        const uint64_t chunk = 1 << 16;
+        std::vector<float> stage(chunk * dim);
+        std::vector<uint8_t> ok(chunk);
+        for (uint64_t g0 = 0; g0 < N; g0 += chunk) {
+            const uint64_t m = std::min(chunk, N - g0);
+            for (uint64_t i = 0; i < m; ++i) {
+                const uint64_t pid = h_ids[g0 + i];
+                ok[i] = same_dim && pid < xb_rows;
+                if (ok[i])
+                    std::memcpy(stage.data() + i * dim, xb_map + xb_offset + pid * xb_stride,
+                                dim * 4);
+                else
+                    std::memset(stage.data() + i * dim, 0, dim * 4);
+            }
+            CUDA_TRY(cudaMemcpy(exact_base.p + g0 * dim, stage.data(), m * dim * 4,
+                                cudaMemcpyHostToDevice));
+            CUDA_TRY(cudaMemcpy(exact_ok.p + g0, ok.data(), m, cudaMemcpyHostToDevice));
+        }
     }
 
     // Loads the whole index, or (shard_world > 1) only the clusters plan_shards() gives this
@@ -869,8 +927,8 @@ void dispatch_scan(int G16, const ScanLaunch &L, ScanPhase phase) {
 
 IndexView Engine::index_view() const {
     return IndexView{scan4.p, cl_start.p, cl_size.p, chunk_range.p, cl_chunk.p, cl_range.p,
-                     rows.p, meta.p,
-                     static_cast<int>(nlist), static_cast<int>(D), G16, LC};
+                     rows.p, meta.p, exact_base.n ? exact_base.p : nullptr, exact_ok.p,
+                     static_cast<int>(nlist), static_cast<int>(D), G16, LC, static_cast<int>(dim)};
 }
 
 SearchView Engine::search_view() const {
@@ -878,7 +936,7 @@ SearchView Engine::search_view() const {
     const uint64_t keep = std::max<uint64_t>(last_k, kVanguardMinKeep);
     return SearchView{static_cast<int>(last_nq), static_cast<int>(last_k), static_cast<int>(last_np),
                       static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
-                      scal.p, qrange.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p,
+                      last_dq, scal.p, qrange.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p,
                       cand_cnt.p, seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n,
                       lows_top.p, err.p, warp_select_limit, topk_warp_limit};
 }
@@ -933,6 +991,7 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     last_nq = nq;
     last_k = k;
     last_np = np;
+    last_dq = d_q;
     CUDA_TRY(cudaGraphLaunch(graph_exec, st));
 }
 
@@ -944,6 +1003,7 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
     last_nq = nq;
     last_k = k;
     last_np = np;
+    last_dq = d_q;
     const int inq = static_cast<int>(nq), ik = static_cast<int>(k);
     const uint64_t veff = vanguard_depth(np);
     const uint64_t keep = std::max<uint64_t>(k, kVanguardMinKeep);
@@ -1392,6 +1452,17 @@ void cora_free_workspace(cora_engine *engine) {
 
 int cora_reset_buffer(cora_engine *engine, const float *h_queries, uint64_t num_queries) {
     return guarded([&] { eng(engine).reset_buffer(h_queries, num_queries); });
+}
+
+int cora_enable_exact_refine(cora_engine *engine, const uint8_t *base_mapping,
+                             uint64_t base_rows, uint64_t base_dim, uint64_t row_stride_bytes,
+                             uint64_t data_offset_bytes) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        CUDA_TRY(cudaSetDevice(e.device));
+        e.enable_exact_refine(base_mapping, base_rows, base_dim, row_stride_bytes,
+                              data_offset_bytes);
+    });
 }
 
 int cora_search(cora_engine *engine, const float *h_queries, uint64_t num_queries, uint64_t topk,

@@ -122,8 +122,15 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
         to = min(cnt, cap);
     }
     if (from >= to) return;  // uniform across the block
-    for (int j = threadIdx.x; j < ix.D; j += blockDim.x)
-        x[j] = static_cast<double>(sv.qr[(size_t)q * ix.D + j]);
+    const bool exact = ix.exact_base != nullptr;
+    // x: the rotated query (ex-code estimate), or the raw query (exact refinement)
+    if (exact) {
+        for (int j = threadIdx.x; j < ix.dim; j += blockDim.x)
+            x[j] = static_cast<double>(sv.raw_q[(size_t)q * ix.dim + j]);
+    } else {
+        for (int j = threadIdx.x; j < ix.D; j += blockDim.x)
+            x[j] = static_cast<double>(sv.qr[(size_t)q * ix.D + j]);
+    }
     const int np = mode == 0 ? sv.veff : sv.nprobe;
     for (int r = threadIdx.x; r < np; r += blockDim.x) {
         const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
@@ -144,8 +151,33 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
             continue;
         }
         const ProbeInfo p = pinfo[pr];
-        const uint4 *row = ix.rows + (size_t)gid * row4;
         const uint4 mt = __ldg(ix.meta + gid);  // {f_add_ex, f_rescale_ex, id, 0}
+        if (exact) {
+            // exact squared L2 distance to the base row, the fp64 fma chain over the raw
+            // dimensions ascending, rounded once (cpu_refinement.cpp:168-181); a vector whose
+            // row is missing is dropped (its key never ranks or sets a threshold)
+            uint64_t key = kKeyMax;
+            if (__ldg(ix.exact_ok + gid)) {
+                const float *b = ix.exact_base + (size_t)gid * ix.dim;
+                double acc = 0.0;
+                for (int j0 = 0; j0 < ix.dim; j0 += 8) {
+                    float bv[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) bv[u] = j0 + u < ix.dim ? __ldg(b + j0 + u) : 0.0f;
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        if (j0 + u < ix.dim) {
+                            const double d = __dsub_rn(x[j0 + u], static_cast<double>(bv[u]));
+                            acc = __fma_rn(d, d, acc);
+                        }
+                    }
+                }
+                key = make_key(__double2float_rn(acc), mt.z);
+            }
+            sv.cand_key[(size_t)q * sv.cap + i] = key;
+            continue;
+        }
+        const uint4 *row = ix.rows + (size_t)gid * row4;
         const float2 f = make_float2(__uint_as_float(mt.x), __uint_as_float(mt.y));
         const uint32_t id = mt.z;
         double acc = 0.0;

@@ -69,11 +69,16 @@ struct IndexView {
     // (b the 1-bit code, u the 7-bit ex code), one byte per dimension
     const uint4 *rows;           // N x D / 16
     const uint4 *meta;           // N: {f_add_ex, f_rescale_ex, id, 0}
-    int nlist, D, G16, LC;
+    // exact FP32 refinement (nullptr: off): base row of every vector (N x dim, its original
+    // id's row of the caller's base) and whether that row exists (N)
+    const float *exact_base;
+    const uint8_t *exact_ok;
+    int nlist, D, G16, LC, dim;
 };
 
 struct SearchView {
     int nq, k, nprobe, veff, keep, cap;
+    const float *raw_q;          // nq x dim, the search's input queries (exact refinement)
     const QueryScalars *scal;    // nq
     const int2 *qrange;          // nq: {sum of positive qint, sum of negative qint}
     const uint32_t *planes;      // nq x 8 x W4

@@ -115,6 +115,9 @@ class MappedVectors {
     }
     std::size_t rows() const { return rows_; }
     std::size_t dim() const { return dim_; }
+    const uint8_t *mapping() const { return base_; }
+    std::size_t row_stride_bytes() const { return stride_; }
+    std::size_t data_offset_bytes() const { return offset_; }
     const float *row(std::size_t i) const {
         return reinterpret_cast<const float *>(base_ + offset_ + i * stride_);
     }

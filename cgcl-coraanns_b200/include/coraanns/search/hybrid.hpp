@@ -98,11 +98,14 @@ class HybridIndex {
         detail::check(cora_reset_buffer(engine_, h_queries, num_queries));
     }
 
-    // The diagnostic FP32 refinement against a mapped base (hybrid.cuh:171-178) is not
-    // implemented by this engine; calling it is rejected instead of silently ignored.
-    void enable_exact_refine(const std::uint8_t *, std::size_t, std::size_t, std::size_t,
-                             std::size_t) {
-        throw std::logic_error("exact-base refinement is not implemented by this engine");
+    // The diagnostic FP32 refinement against a mapped base (hybrid.cuh:171-178): candidates
+    // are ranked by their exact squared L2 distance to base row `original id`; the rows the
+    // engine holds are copied into HBM by this call (or when the index is loaded).
+    void enable_exact_refine(const std::uint8_t *base_mapping, std::size_t base_rows,
+                             std::size_t base_dim, std::size_t row_stride_bytes,
+                             std::size_t data_offset_bytes) {
+        detail::check(cora_enable_exact_refine(engine_, base_mapping, base_rows, base_dim,
+                                               row_stride_bytes, data_offset_bytes));
     }
 
     // Unlike the reference, the extended codes, factors and ids are copied to HBM: the host

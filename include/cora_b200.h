@@ -80,6 +80,19 @@ void cora_free_workspace(cora_engine *engine);
  * CORA_ESTATE without a workspace, CORA_EINVAL if num_queries exceeds it. */
 int cora_reset_buffer(cora_engine *engine, const float *h_queries, uint64_t num_queries);
 
+/* enable_exact_refine (hybrid.cuh:171-178): refine candidates with the exact squared L2
+ * distance between the raw query and base row `id` (the vector's original id), row id at
+ * base_mapping + data_offset_bytes + id * row_stride_bytes, base_dim fp32 values; the
+ * distance is the fp32 rounding of the fp64 fma chain over the dimensions ascending.
+ * Candidates whose id >= base_rows, or every candidate when base_dim differs from the
+ * index dimension, are dropped (cpu_refinement.cpp:168-181). The rows this engine holds are
+ * copied into HBM now (or when the index is loaded), so the mapping must stay valid until
+ * then. base_mapping == NULL turns exact refinement off. CORA_EINVAL when the stride is
+ * shorter than a row. */
+int cora_enable_exact_refine(cora_engine *engine, const uint8_t *base_mapping,
+                             uint64_t base_rows, uint64_t base_dim, uint64_t row_stride_bytes,
+                             uint64_t data_offset_bytes);
+
 /* search (hybrid.cuh:195-196): blocking; CORA_EINVAL unless 1 <= batch_q <= 6 or if the
  * shape exceeds the workspace; CORA_ERUNTIME with "spill capacity exhausted" when the
  * per-query candidate capacity ((queue + spill capacity) / max_queries) overflows. */

@@ -223,10 +223,24 @@ static void vector_bits(const cora_oracle_index *ix, uint64_t start, uint64_t n,
     for (uint64_t w = 0; w < W; ++w) out[w] = ix->short_data[start * W + w * n + i];
 }
 
-static float refine(const cora_oracle_index *ix, const float *x, uint64_t start, uint64_t n,
-                    uint64_t i, float g, float kb) {
+/* Exact FP32 refinement of gid against the raw query qraw (see cora_oracle_index). */
+static float exact_refine(const cora_oracle_index *ix, const float *qraw, uint64_t gid) {
+    const uint64_t pid = ix->ids[gid];
+    if (ix->exact_dim != ix->dim || pid >= ix->exact_rows) return NAN;
+    const float *b = ix->exact_base + pid * ix->exact_stride;
+    double acc = 0.0;
+    for (uint64_t d = 0; d < ix->dim; ++d) {
+        const double diff = (double)qraw[d] - (double)b[d];
+        acc = fma(diff, diff, acc);
+    }
+    return (float)acc;
+}
+
+static float refine(const cora_oracle_index *ix, const float *qraw, const float *x,
+                    uint64_t start, uint64_t n, uint64_t i, float g, float kb) {
     uint32_t bits[128];
     const uint64_t D = ix->padded_dim, LC = D * ix->ex_bits / 8, gid = start + i;
+    if (ix->exact_base) return exact_refine(ix, qraw, gid);
     vector_bits(ix, start, n, i, bits);
     const float ipt = cora_oracle_ip_total(x, bits, ix->long_codes + gid * LC, D);
     return cora_oracle_ex(ix, gid, ipt, g, kb);
@@ -316,7 +330,7 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
             const uint64_t ns = take_all[r] ? npair : keep;
             for (uint64_t i = 0; i < ns; ++i) {
                 const uint32_t gid = pair[i].gid;
-                const float ex = refine(ix, x, s, nc, gid - s, g, kb);
+                const float ex = refine(ix, q + n * ix->dim, x, s, nc, gid - s, g, kb);
                 entry_t e = {((uint64_t)ord_f32(ex) << 32) | ix->ids[gid], ex, pair[i].ip1, gid,
                              (uint32_t)r};
                 push(&res, &nres, &cres, e);
@@ -359,7 +373,7 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
                     if (key <= bound[r]) continue;
                 }
                 const uint32_t gid = (uint32_t)(s + i);
-                const float ex = refine(ix, x, s, nc, i, g, kb);
+                const float ex = refine(ix, q + n * ix->dim, x, s, nc, i, g, kb);
                 entry_t e = {((uint64_t)ord_f32(ex) << 32) | ix->ids[gid], ex, ip1, gid,
                              (uint32_t)r};
                 push(&res, &nres, &cres, e);

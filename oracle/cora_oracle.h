@@ -59,6 +59,14 @@ typedef struct {
     const float *ex_factors;       /* N x 2: f_add_ex, f_rescale_ex */
     const uint32_t *ids;           /* N original ids, cluster order */
     const uint64_t *cluster_sizes; /* nlist */
+    /* Optional exact FP32 refinement (hybrid.cuh:171-178, cpu_refinement.cpp:168-181):
+     * when exact_base is set, a candidate's distance is the exact squared L2 distance
+     * between the raw query and base row ids[gid] (row pid at exact_base + pid *
+     * exact_stride floats), the fp32 rounding of the fp64 fma chain over d ascending;
+     * candidates whose pid >= exact_rows, or all of them when exact_dim != dim, are
+     * dropped (value NaN: never a result, never below a threshold; still counted). */
+    const float *exact_base;
+    uint64_t exact_rows, exact_dim, exact_stride;
 } cora_oracle_index;
 
 #define CORA_ORACLE_VANGUARD_MIN_KEEP 20

@@ -133,7 +133,9 @@ class _Index(C.Structure):
                 ("centroids", C.c_void_p), ("rotator", C.c_void_p),
                 ("short_data", C.c_void_p), ("short_factors", C.c_void_p),
                 ("long_codes", C.c_void_p), ("ex_factors", C.c_void_p),
-                ("ids", C.c_void_p), ("cluster_sizes", C.c_void_p)]
+                ("ids", C.c_void_p), ("cluster_sizes", C.c_void_p),
+                ("exact_base", C.c_void_p), ("exact_rows", C.c_uint64),
+                ("exact_dim", C.c_uint64), ("exact_stride", C.c_uint64)]
 
 
 _lib = None
@@ -174,9 +176,12 @@ def _ptr(a):
 
 
 class OracleIndex:
-    """Holds SearchData-layout arrays (contiguous, right dtypes) for the C oracle."""
+    """Holds SearchData-layout arrays (contiguous, right dtypes) for the C oracle.
+    exact_base: optional float32 (rows, dim) base vectors indexed by original id; when set,
+    candidates are refined with exact squared L2 distances (HybridIndex::enable_exact_refine,
+    hybrid.cuh:171-178)."""
 
-    def __init__(self, sd: dict):
+    def __init__(self, sd: dict, exact_base=None):
         self.sd = {
             "centroids": np.ascontiguousarray(sd["centroids"], np.float32),
             "rotator": np.ascontiguousarray(sd["rotator"], np.float32),
@@ -193,7 +198,20 @@ class OracleIndex:
         self.c = _Index(self.num, self.dim, self.D, self.nlist, self.ex_bits,
                         _ptr(s["centroids"]), _ptr(s["rotator"]), _ptr(s["short_data"]),
                         _ptr(s["short_factors"]), _ptr(s["long_codes"]), _ptr(s["ex_factors"]),
-                        _ptr(s["ids"]), _ptr(s["sizes"]))
+                        _ptr(s["ids"]), _ptr(s["sizes"]), None, 0, 0, 0)
+        self.set_exact_base(exact_base)
+
+    def set_exact_base(self, base):
+        """Exact refinement against `base` (float32 (rows, dim), row = original id), or off."""
+        if base is None:
+            self.exact = None
+            self.c.exact_base, self.c.exact_rows, self.c.exact_dim, self.c.exact_stride = \
+                None, 0, 0, 0
+            return
+        self.exact = np.ascontiguousarray(base, np.float32)
+        self.c.exact_base = _ptr(self.exact)
+        self.c.exact_rows, self.c.exact_dim = self.exact.shape
+        self.c.exact_stride = self.exact.shape[1]
 
     def search(self, q, k, nprobe, vanguard=5, thresholds=None, with_details=False,
                cand_cap=0, threads=None):

@@ -122,3 +122,22 @@ def test_cli_search_matches_oracle_recall(tmp_path):
     assert "mode=distance-aware" in r.stdout and "recall=deferred" in r.stdout
     want = _expected_recall(z["ids_k10_np4_v5"], gt, 10, radius, base, q)
     assert _final_table(r.stdout)[4][1] == pytest.approx(want, abs=1e-6)
+
+    # --exact-base: FP32 diagnostic refine; the ids are the oracle's exact-refine ids
+    import py_oracle as po
+    o = po.oracle_from_file(GOLDEN / "demo.index")
+    o.set_exact_base(base)
+    _, ids_exact = o.search(q, 10, 4)
+    cmd = [str(CLI), str(GOLDEN / "demo.index"), str(tmp_path / "q.fvecs"), str(tmp_path / "gt.ivecs"),
+           "--topk", "10", "--nprobes", "4", "--rounds", "1", "--warmup", "0",
+           "--exact-base", str(tmp_path / "base.fbin")]
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr + r.stdout
+    assert "Exact FP32 refine enabled with mmap base:" in r.stdout
+    assert _final_table(r.stdout)[4][1] == pytest.approx(_expected_recall(ids_exact, gt, 10),
+                                                         abs=1e-6)
+    # a base of another shape is rejected before searching
+    _write_bin(tmp_path / "short.fbin", base[:100])
+    cmd[-1] = str(tmp_path / "short.fbin")
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 1 and "Exact-refine base shape mismatch" in r.stderr
