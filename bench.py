@@ -557,12 +557,13 @@ def main():
     # fallback when nprobe <= 32), seed refine, threshold, main grouping (4), main scan,
     # refine, merge (threshold and final top-k: warp kernel + block fallback each when
     # k <= 32); with stored vanguard lows also vanguard grouping (4), lows scan, seed
-    # selection (warp + block fallback when keep <= 32) and the lows filter, else one vanguard
-    # rescan; +2 exchange steps (gather_threshold / gather_merge) when sharded.
+    # selection (warp + block fallback when keep <= 32) and the lows filter (pair list +
+    # filter), else one vanguard rescan; +2 exchange steps (gather_threshold / gather_merge)
+    # when sharded.
     sel = 2 if chosen <= 32 else 1
     vsel = 2 if max(k, 20) <= 32 else 1
     topk = 2 if k <= 32 else 1
-    per_search = (9 + sel + 2 * topk + ((6 + vsel) if mode == 1 else 1)
+    per_search = (9 + sel + 2 * topk + ((7 + vsel) if mode == 1 else 1)
                   + (2 if shards > 1 else 0))
     launches = per_search * args.steps
 
