@@ -11,6 +11,8 @@
 //
 // Estimator (reference src/search/filter_kernels.cuh:79-114, 693-696):
 //   ip_int = sum_{j<7} popc(x & plane_j) << j  -  popc(x & plane_7) << 7      (exact)
+//          = sum_i b_i qint_i, evaluated as byte dot products (dp4a) for D <= 128 and as
+//            bit-plane popcounts above (both exact in int32)
 //   ip1    = width * ip_int
 //   low    = (f_add + g) + f_rescale * (ip1 + k1) - f_error * sqrt(max(g, 0))
 //
@@ -22,7 +24,9 @@
 //  4. the remaining pairs (r >= veff) are grouped by cluster and scanned against T1, and the
 //     stored lows of the vanguard pairs are filtered against T1 (skipping their seeds).
 // When the lows buffer would not fit its budget, step 1-2 run as one kernel per vanguard
-// pair instead (vanguard_rescan_kernel) and step 4 rescans the vanguard clusters.
+// pair instead (vanguard_rescan_kernel) and step 4 rescans the vanguard clusters. Step 4
+// leaves out every (pair, cluster), (pair, item) and (pair, 32-vector chunk) whose factor
+// range proves all its lows >= T1 (range_at_least): the candidate set is unchanged.
 #pragma once
 #include "common.cuh"
 #include "kernels_query.cuh"
@@ -323,8 +327,8 @@ __device__ __forceinline__ void half_add(uint32_t &s, uint32_t &c, uint32_t a, u
 }
 
 // Weights combined by the adder tree (2^0 .. 2^(kCsaLevels-1)); 8 = the full tree. Measured
-// on config 2 (both scan passes): 4 -> 1.35 ms, 5 -> 1.25, 6 -> 1.27, 7 -> 1.36, 8 -> 1.41;
-// two vectors per thread (CORA_SCAN_VPT 2) raised registers from 72 to 94 and lost 13%.
+// on config 2 with this form in both scan passes (before the byte dot products replaced it
+// for D <= 128): 4 -> 1.35 ms, 5 -> 1.25, 6 -> 1.27, 7 -> 1.36, 8 -> 1.41.
 #ifndef CORA_CSA_LEVELS
 #define CORA_CSA_LEVELS 5
 #endif
