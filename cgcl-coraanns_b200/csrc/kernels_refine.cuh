@@ -16,7 +16,12 @@
 
 namespace cora {
 
-constexpr int kRefineThreads = 128;
+#ifndef CORA_REFINE_THREADS
+#define CORA_REFINE_THREADS 128
+#endif
+// threads per query in refine_kernel; measured on config 2 (candidate refine): 64 -> 0.202
+// ms, 128 -> 0.192, 256 -> 0.188 (seed refine 0.080 / 0.072 / 0.075)
+constexpr int kRefineThreads = CORA_REFINE_THREADS;
 
 struct ProbeInfo {  // per (query, probe rank), staged in shared memory by refine_kernel
     uint32_t start, size;
