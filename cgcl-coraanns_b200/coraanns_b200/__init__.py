@@ -31,6 +31,7 @@ CORA_OK, CORA_EINVAL, CORA_ESTATE, CORA_ERUNTIME, CORA_ECUDA, CORA_ENOMEM = rang
 EXPORTS = [
     "cora_last_error", "cora_create", "cora_destroy", "cora_load_from_raw_pointers",
     "cora_load_index_file", "cora_index_info", "cora_prepare_workspace", "cora_free_workspace",
+    "cora_index_file_shard_info",
     "cora_reset_buffer", "cora_enable_exact_refine", "cora_search", "cora_search_device",
     "cora_check_device",
     "cora_seed_thresholds", "cora_capture_thresholds", "cora_set_vanguard_size",
@@ -68,6 +69,7 @@ _sig("cora_prepare_workspace", C.c_int, _p, _u64, _u64, _u64)
 _sig("cora_free_workspace", None, _p)
 _sig("cora_reset_buffer", C.c_int, _p, _p, _u64)
 _sig("cora_enable_exact_refine", C.c_int, _p, _p, _u64, _u64, _u64, _u64)
+_sig("cora_index_file_shard_info", C.c_int, C.c_char_p, C.c_uint32, C.c_uint32, _p)
 _sig("cora_search", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p, C.c_int)
 _sig("cora_search_device", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p, _p)
 _sig("cora_check_device", C.c_int, _p)
@@ -142,6 +144,15 @@ def _ptr(a):
 def probe_noalloc_scratch_limit() -> int:
     """Bytes of the static per-device scratch block behind HybridIndex.probe_noalloc."""
     return int(_lib.cora_probe_noalloc_scratch_limit())
+
+
+def index_file_shard_info(path, rank: int, world: int) -> dict:
+    """The share of an index file that shard `rank` of `world` holds and reads (no GPU):
+    vectors, clusters, payload bytes, and the file's total vectors."""
+    out = np.zeros(4, np.uint64)
+    _check(_lib.cora_index_file_shard_info(str(path).encode(), rank, world, _ptr(out)))
+    return dict(vectors=int(out[0]), clusters=int(out[1]), payload_bytes=int(out[2]),
+                total_vectors=int(out[3]))
 
 
 class KernelType:

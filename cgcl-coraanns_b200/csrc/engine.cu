@@ -554,10 +554,6 @@ struct Engine {
                 local += h_sizes[c];
                 ++kept;
             }
-        if (local == 0)
-            fail(CORA_EINVAL, "shard " + std::to_string(shard_rank) + " of " +
-                                  std::to_string(shard_world) +
-                                  " owns no vectors; use fewer shards for this index");
         std::vector<uint32_t> s_short(local * W), s_ids(local);
         std::vector<float> s_sf(local * 3), s_exf(local * 2);
         std::vector<uint8_t> s_long(local * lc), mask(n_centroids, 0);
@@ -578,8 +574,24 @@ struct Engine {
             }
             src += n;
         }
-        load(local, d, p_d, n_centroids, ex_b, h_centroids, h_rotator, s_short.data(),
-             s_sf.data(), s_long.data(), s_exf.data(), s_ids.data(), s_sizes.data());
+        load_shard_local(local, d, p_d, n_centroids, ex_b, h_centroids, h_rotator, s_short.data(),
+                         s_sf.data(), s_long.data(), s_exf.data(), s_ids.data(), s_sizes.data(),
+                         mask, kept);
+    }
+
+    // A shard's part of an index, already sliced (sizes 0 outside the shard, `mask` 1 on its
+    // clusters): loaded like a whole index, plus the ownership mask.
+    void load_shard_local(uint64_t local, uint64_t d, uint64_t p_d, uint64_t n_centroids,
+                          uint64_t ex_b, const float *h_centroids, const float *h_rotator,
+                          const uint32_t *h_short, const float *h_sf, const uint8_t *h_long,
+                          const float *h_exf, const uint32_t *h_ids, const uint64_t *h_sizes,
+                          const std::vector<uint8_t> &mask, uint64_t kept) {
+        if (local == 0)
+            fail(CORA_EINVAL, "shard " + std::to_string(shard_rank) + " of " +
+                                  std::to_string(shard_world) +
+                                  " owns no vectors; use fewer shards for this index");
+        load(local, d, p_d, n_centroids, ex_b, h_centroids, h_rotator, h_short, h_sf, h_long,
+             h_exf, h_ids, h_sizes);
         owned.alloc(n_centroids);
         CUDA_TRY(cudaMemcpy(owned.p, mask.data(), n_centroids, cudaMemcpyHostToDevice));
         shard_clusters = kept;
@@ -1249,15 +1261,24 @@ void Engine::debug_copy(int what, void *out, uint64_t bytes) {
 // index file -> adapter arrays (ivf.hpp:447-539 + search_data.cpp:45-123)
 // ------------------------------------------------------------------------------------
 namespace {
+// An index file read whole, or (world > 1) only the clusters plan_shards() gives `rank`:
+// then num and sizes count this shard's vectors (sizes 0 elsewhere), `owned` marks its
+// clusters, and every centroid is kept (each shard probes all of them).
 struct FileIndex {
     uint64_t num = 0, dim = 0, nlist = 0, ex_bits = 0, D = 0;
+    uint64_t full_num = 0, kept = 0, bytes_read = 0;
     std::vector<uint64_t> sizes;
+    std::vector<uint8_t> owned;
     std::vector<float> rotator, centroids, short_factors, ex_factors;
     std::vector<uint32_t> short_data, ids;
     std::vector<uint8_t> long_codes;
 };
 
-FileIndex read_index_file(const char *path) {
+// Reads an IVF index file (ivf.hpp:403-445; flat centroids). The payload sections (FastScan
+// batches, ex codes, ids) are laid out by cluster, so a shard seeks to its own clusters and
+// reads each run of consecutive owned clusters in one piece: a shard's host memory and file
+// traffic are its share of the index, not the whole file.
+FileIndex read_index_file(const char *path, uint32_t rank = 0, uint32_t world = 1) {
     std::ifstream in(path, std::ios::binary);
     if (!in) fail(CORA_EINVAL, std::string("Cannot open IVF index: ") + path);
     FileIndex f;
@@ -1266,22 +1287,24 @@ FileIndex read_index_file(const char *path) {
     in.read(reinterpret_cast<char *>(hdr), sizeof(hdr));
     in.read(reinterpret_cast<char *>(types), 2);
     if (!in) fail(CORA_EINVAL, "truncated IVF index header");
-    f.num = hdr[0];
+    f.full_num = hdr[0];
     f.dim = hdr[1];
     f.nlist = hdr[2];
     f.ex_bits = hdr[3];
     if (types[0] != 0) fail(CORA_EINVAL, "only matrix-rotator indexes are supported");
-    if (!f.num || !f.dim || !f.nlist || f.ex_bits > 8) fail(CORA_EINVAL, "invalid IVF index header");
+    if (!f.full_num || !f.dim || !f.nlist || f.ex_bits > 8)
+        fail(CORA_EINVAL, "invalid IVF index header");
     f.D = (f.dim + 63) / 64 * 64;
     const uint64_t D = f.D, W = D / 32;
-    f.sizes.resize(f.nlist);
-    in.read(reinterpret_cast<char *>(f.sizes.data()), 8 * f.nlist);
+    std::vector<uint64_t> full_sizes(f.nlist);
+    in.read(reinterpret_cast<char *>(full_sizes.data()), 8 * f.nlist);
     uint64_t total = 0, blocks = 0;
-    for (auto s : f.sizes) {
-        total += s;
-        blocks += (s + 31) / 32;
+    for (auto sz : full_sizes) {
+        total += sz;
+        blocks += (sz + 31) / 32;
     }
-    if (!in || total != f.num) fail(CORA_EINVAL, "The sum of cluster num != total number of points");
+    if (!in || total != f.full_num)
+        fail(CORA_EINVAL, "The sum of cluster num != total number of points");
     f.rotator.resize(f.dim * D);
     in.read(reinterpret_cast<char *>(f.rotator.data()), 4 * f.dim * D);
     const std::streampos begin = in.tellg();
@@ -1290,20 +1313,41 @@ FileIndex read_index_file(const char *path) {
     in.seekg(begin);
     const uint64_t rec = D * 4 + 32 * 12;
     const uint64_t ex_stride = f.ex_bits ? D * f.ex_bits / 8 + 8 : 0;
-    const uint64_t payload = blocks * rec + f.num * ex_stride + 4 * f.num;
+    const uint64_t payload = blocks * rec + f.full_num * ex_stride + 4 * f.full_num;
     if (remaining == payload)
         fail(CORA_EINVAL, "HNSW-sidecar centroid storage (nlist >= 20000 indexes) is not supported");
     if (remaining != payload + 4 * D * f.nlist)
         fail(CORA_EINVAL, "IVF index size does not match a supported centroid layout");
     f.centroids.resize(f.nlist * D);
     in.read(reinterpret_cast<char *>(f.centroids.data()), 4 * D * f.nlist);
-    std::vector<uint8_t> batch(blocks * rec);
-    in.read(reinterpret_cast<char *>(batch.data()), batch.size());
-    std::vector<uint8_t> ex(f.num * ex_stride);
-    in.read(reinterpret_cast<char *>(ex.data()), ex.size());
-    f.ids.resize(f.num);
-    in.read(reinterpret_cast<char *>(f.ids.data()), 4 * f.num);
     if (!in) fail(CORA_EINVAL, "Failed to read IVF index payload");
+    const uint64_t batch_at = static_cast<uint64_t>(begin) + 4 * D * f.nlist;
+    const uint64_t ex_at = batch_at + blocks * rec;
+    const uint64_t ids_at = ex_at + f.full_num * ex_stride;
+
+    // the clusters this reader keeps, and their local layout
+    f.owned.assign(f.nlist, 1);
+    if (world > 1) {
+        std::vector<int32_t> owner(f.nlist);
+        plan_shards(full_sizes.data(), f.nlist, world, owner.data());
+        for (uint64_t c = 0; c < f.nlist; ++c) f.owned[c] = owner[c] == static_cast<int32_t>(rank);
+    }
+    f.sizes.assign(f.nlist, 0);
+    std::vector<uint64_t> cstart(f.nlist + 1, 0), bstart(f.nlist + 1, 0), lstart(f.nlist + 1, 0);
+    for (uint64_t c = 0; c < f.nlist; ++c) {
+        cstart[c + 1] = cstart[c] + full_sizes[c];
+        bstart[c + 1] = bstart[c] + (full_sizes[c] + 31) / 32;
+        f.sizes[c] = f.owned[c] ? full_sizes[c] : 0;
+        lstart[c + 1] = lstart[c] + f.sizes[c];
+        f.kept += f.owned[c];
+    }
+    f.num = lstart[f.nlist];
+    const uint64_t lc = D * f.ex_bits / 8;
+    f.short_data.assign(f.num * W, 0u);
+    f.short_factors.assign(f.num * 3, 0.0f);
+    f.long_codes.resize(f.num * lc);
+    f.ex_factors.resize(f.num * 2);
+    f.ids.resize(f.num);
 
     // FastScan batches of 32 vectors -> word-major 1-bit codes per cluster. In a batch,
     // dims 8i..8i+7 occupy 32 bytes; dims with (dim % 8) < 4 sit in the first 16, the
@@ -1312,42 +1356,57 @@ FileIndex read_index_file(const char *path) {
     static const int perm[16] = {0, 8, 1, 9, 2, 10, 3, 11, 4, 12, 5, 13, 6, 14, 7, 15};
     int inv_perm[16];
     for (int j = 0; j < 16; ++j) inv_perm[perm[j]] = j;
-    f.short_data.assign(f.num * W, 0u);
-    f.short_factors.assign(f.num * 3, 0.0f);
-    std::vector<uint64_t> cstart(f.nlist + 1, 0), bstart(f.nlist + 1, 0);
-    for (uint64_t c = 0; c < f.nlist; ++c) {
-        cstart[c + 1] = cstart[c] + f.sizes[c];
-        bstart[c + 1] = bstart[c] + (f.sizes[c] + 31) / 32;
-    }
+    std::vector<uint8_t> batch, ex;
+    auto read_at = [&](uint64_t at, void *dst, uint64_t bytes) {
+        in.seekg(static_cast<std::streamoff>(at));
+        in.read(reinterpret_cast<char *>(dst), static_cast<std::streamsize>(bytes));
+        if (!in) fail(CORA_EINVAL, "Failed to read IVF index payload");
+        f.bytes_read += bytes;
+    };
+    for (uint64_t c0 = 0; c0 < f.nlist;) {
+        if (!f.owned[c0]) {
+            ++c0;
+            continue;
+        }
+        uint64_t c1 = c0;  // run [c0, c1) of consecutive owned clusters
+        while (c1 < f.nlist && f.owned[c1]) ++c1;
+        batch.resize((bstart[c1] - bstart[c0]) * rec);
+        read_at(batch_at + bstart[c0] * rec, batch.data(), batch.size());
+        const uint64_t rn = cstart[c1] - cstart[c0];
+        ex.resize(rn * ex_stride);
+        read_at(ex_at + cstart[c0] * ex_stride, ex.data(), ex.size());
+        read_at(ids_at + cstart[c0] * 4, f.ids.data() + lstart[c0], rn * 4);
 #pragma omp parallel for schedule(dynamic, 16)
-    for (int64_t c = 0; c < static_cast<int64_t>(f.nlist); ++c) {
-        const uint64_t n = f.sizes[c], s = cstart[c];
-        for (uint64_t i = 0; i < n; i += 32) {
-            const uint8_t *blk = batch.data() + (bstart[c] + i / 32) * rec;
-            const float *fa = reinterpret_cast<const float *>(blk + D * 4);
-            const uint64_t len = std::min<uint64_t>(32, n - i);
-            for (uint64_t v = 0; v < len; ++v) {
-                for (uint64_t w = 0; w < W; ++w) {
-                    uint32_t word = 0;
-                    for (int b = 0; b < 32; ++b) {
-                        const uint64_t d = w * 32 + b;
-                        const uint8_t byte =
-                            blk[(d / 8) * 32 + ((d % 8) < 4 ? 0 : 16) + inv_perm[v % 16]];
-                        const uint8_t nib = v < 16 ? (byte & 0x0F) : (byte >> 4);
-                        word |= static_cast<uint32_t>((nib >> (3 - (d % 4))) & 1u) << (31 - b);
+        for (int64_t c = static_cast<int64_t>(c0); c < static_cast<int64_t>(c1); ++c) {
+            const uint64_t n = full_sizes[c], s = lstart[c];
+            for (uint64_t i = 0; i < n; i += 32) {
+                const uint8_t *blk = batch.data() + (bstart[c] - bstart[c0] + i / 32) * rec;
+                const float *fa = reinterpret_cast<const float *>(blk + D * 4);
+                const uint64_t len = std::min<uint64_t>(32, n - i);
+                for (uint64_t v = 0; v < len; ++v) {
+                    for (uint64_t w = 0; w < W; ++w) {
+                        uint32_t word = 0;
+                        for (int b = 0; b < 32; ++b) {
+                            const uint64_t d = w * 32 + b;
+                            const uint8_t byte =
+                                blk[(d / 8) * 32 + ((d % 8) < 4 ? 0 : 16) + inv_perm[v % 16]];
+                            const uint8_t nib = v < 16 ? (byte & 0x0F) : (byte >> 4);
+                            word |= static_cast<uint32_t>((nib >> (3 - (d % 4))) & 1u) << (31 - b);
+                        }
+                        f.short_data[s * W + w * n + i + v] = word;
                     }
-                    f.short_data[s * W + w * n + i + v] = word;
+                    for (int t = 0; t < 3; ++t)
+                        f.short_factors[(s + i + v) * 3 + t] = fa[t * 32 + v];
                 }
-                for (int t = 0; t < 3; ++t) f.short_factors[(s + i + v) * 3 + t] = fa[t * 32 + v];
+            }
+            const uint64_t e0 = cstart[c] - cstart[c0];
+            for (uint64_t i = 0; i < n; ++i) {
+                std::memcpy(f.long_codes.data() + (s + i) * lc, ex.data() + (e0 + i) * ex_stride, lc);
+                std::memcpy(f.ex_factors.data() + (s + i) * 2,
+                            ex.data() + (e0 + i) * ex_stride + lc, 8);
             }
         }
-    }
-    const uint64_t lc = D * f.ex_bits / 8;
-    f.long_codes.resize(f.num * lc);
-    f.ex_factors.resize(f.num * 2);
-    for (uint64_t i = 0; i < f.num; ++i) {
-        std::memcpy(f.long_codes.data() + i * lc, ex.data() + i * ex_stride, lc);
-        std::memcpy(f.ex_factors.data() + i * 2, ex.data() + i * ex_stride + lc, 8);
+        c0 = c1;
     }
     return f;
 }
@@ -1424,10 +1483,52 @@ int cora_load_index_file(cora_engine *engine, const char *path) {
         Engine &e = eng(engine);
         if (e.loaded) cora::fail(CORA_ESTATE, "index already loaded");
         if (!path) cora::fail(CORA_EINVAL, "null index path");
+        if (e.shard_world > 1) {  // read this shard's clusters only
+            cora::FileIndex f = cora::read_index_file(path, e.shard_rank, e.shard_world);
+            e.load_shard_local(f.num, f.dim, f.D, f.nlist, f.ex_bits, f.centroids.data(),
+                               f.rotator.data(), f.short_data.data(), f.short_factors.data(),
+                               f.long_codes.data(), f.ex_factors.data(), f.ids.data(),
+                               f.sizes.data(), f.owned, f.kept);
+            return;
+        }
         cora::FileIndex f = cora::read_index_file(path);
         e.load_any(f.num, f.dim, f.D, f.nlist, f.ex_bits, f.centroids.data(), f.rotator.data(),
                f.short_data.data(), f.short_factors.data(), f.long_codes.data(), f.ex_factors.data(),
                f.ids.data(), f.sizes.data());
+    });
+}
+
+int cora_index_file_shard_info(const char *path, uint32_t rank, uint32_t world,
+                               uint64_t *out4) {
+    return guarded([&] {
+        if (!path || !out4) cora::fail(CORA_EINVAL, "null argument");
+        if (world == 0 || world > cora::kMaxShards || rank >= world)
+            cora::fail(CORA_EINVAL, "invalid shard rank / world");
+        std::ifstream in(path, std::ios::binary);
+        if (!in) cora::fail(CORA_EINVAL, std::string("Cannot open IVF index: ") + path);
+        uint64_t hdr[4];
+        uint8_t types[2];
+        in.read(reinterpret_cast<char *>(hdr), sizeof(hdr));
+        in.read(reinterpret_cast<char *>(types), 2);
+        if (!in || !hdr[2] || !hdr[1]) cora::fail(CORA_EINVAL, "truncated IVF index header");
+        const uint64_t nlist = hdr[2], D = (hdr[1] + 63) / 64 * 64;
+        std::vector<uint64_t> sizes(nlist);
+        in.read(reinterpret_cast<char *>(sizes.data()), 8 * nlist);
+        if (!in) cora::fail(CORA_EINVAL, "truncated IVF index header");
+        std::vector<int32_t> owner(nlist, 0);
+        if (world > 1) cora::plan_shards(sizes.data(), nlist, world, owner.data());
+        const uint64_t rec = D * 4 + 32 * 12, ex_stride = hdr[3] ? D * hdr[3] / 8 + 8 : 0;
+        uint64_t vecs = 0, clusters = 0, bytes = 0;
+        for (uint64_t c = 0; c < nlist; ++c)
+            if (owner[c] == static_cast<int32_t>(rank)) {
+                vecs += sizes[c];
+                ++clusters;
+                bytes += (sizes[c] + 31) / 32 * rec + sizes[c] * (ex_stride + 4);
+            }
+        out4[0] = vecs;
+        out4[1] = clusters;
+        out4[2] = bytes;
+        out4[3] = hdr[0];
     });
 }
 

@@ -69,6 +69,11 @@ int cora_load_index_file(cora_engine *engine, const char *path);
 /* Index shape after loading: out[0..5] = num, dim, padded_dim, nlist, ex_bits,
  * largest cluster size. */
 int cora_index_info(const cora_engine *engine, uint64_t *out6);
+/* A shard's share of an index file (no GPU needed): out4 = {vectors, clusters, payload
+ * bytes, the file's total vectors} that shard `rank` of `world` (cora_shard_plan) holds and
+ * reads. A shard engine's cora_load_index_file reads only those payload bytes (plus the
+ * header, rotator and every centroid). */
+int cora_index_file_shard_info(const char *path, uint32_t rank, uint32_t world, uint64_t *out4);
 
 /* prepare_workspace (hybrid.cuh:167): validate_search_shape (parameters.hpp:15-25),
  * CORA_ESTATE without an index; frees and reallocates. */

@@ -138,3 +138,21 @@ def test_plan_balances_and_is_deterministic():
         assert set(np.unique(a)) == set(range(world))
     with pytest.raises(ValueError):
         shard_plan(sizes, 0)
+
+
+def test_index_file_shard_info_partitions_the_file():
+    """A shard engine reads only its clusters' payload from an index file: the shards'
+    shares partition the vectors, clusters and payload bytes (no GPU needed)."""
+    import coraanns_b200 as cb
+    import py_oracle as po
+    path = GOLDEN / "d96.index"
+    whole = cb.index_file_shard_info(path, 0, 1)
+    ivf = po.read_ivf_file(path)
+    assert whole["vectors"] == whole["total_vectors"] == int(ivf["num"])
+    assert whole["clusters"] == int(ivf["nlist"])
+    for world in (2, 3, 4):
+        parts = [cb.index_file_shard_info(path, r, world) for r in range(world)]
+        assert sum(p["vectors"] for p in parts) == whole["vectors"]
+        assert sum(p["clusters"] for p in parts) == whole["clusters"]
+        assert sum(p["payload_bytes"] for p in parts) == whole["payload_bytes"]
+        assert max(p["payload_bytes"] for p in parts) < whole["payload_bytes"]
