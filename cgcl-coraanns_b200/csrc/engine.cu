@@ -1274,7 +1274,48 @@ struct FileIndex {
     std::vector<uint8_t> long_codes;
 };
 
-// Reads an IVF index file (ivf.hpp:403-445; flat centroids). The payload sections (FastScan
+// Centroids of an HNSW-initialised index (nlist >= 20000) from its hnswlib sidecar
+// `<index>.hnsw`, written by hnswlib's saveIndex (third_party/.../hnswlib/hnswalg.h:685-713):
+// a header of offsetLevel0, max_elements, cur_element_count, size_data_per_element,
+// label_offset, offsetData (u64), maxlevel (i32), enterpoint_node (u32), maxM, maxM0, M
+// (u64), mult (f64), ef_construction (u64), then cur_element_count level-0 records whose
+// vector (D floats) sits at offsetData and label (u64, the cluster id) at label_offset
+// (initializer.hpp:207-214). The upper-level links that follow are not needed.
+void read_hnsw_centroids(const char *path, uint64_t nlist, uint64_t D, float *out) {
+    std::ifstream in(path, std::ios::binary);
+    if (!in) fail(CORA_EINVAL, std::string("Cannot open HNSW centroid sidecar: ") + path);
+    uint64_t h6[6];
+    int32_t maxlevel;
+    uint32_t enterpoint;
+    uint64_t h3[3];
+    double mult;
+    uint64_t efc;
+    in.read(reinterpret_cast<char *>(h6), sizeof h6);
+    in.read(reinterpret_cast<char *>(&maxlevel), 4);
+    in.read(reinterpret_cast<char *>(&enterpoint), 4);
+    in.read(reinterpret_cast<char *>(h3), sizeof h3);
+    in.read(reinterpret_cast<char *>(&mult), 8);
+    in.read(reinterpret_cast<char *>(&efc), 8);
+    if (!in) fail(CORA_EINVAL, "truncated HNSW centroid sidecar");
+    const uint64_t count = h6[2], per = h6[3], label_off = h6[4], data_off = h6[5];
+    if (h6[0] != 0 || count != nlist || data_off + 4 * D > per || label_off + 8 > per)
+        fail(CORA_EINVAL, "HNSW centroid sidecar does not match the index's clusters");
+    std::vector<uint8_t> rec(per);
+    std::vector<uint8_t> seen(nlist, 0);
+    for (uint64_t i = 0; i < count; ++i) {
+        in.read(reinterpret_cast<char *>(rec.data()), static_cast<std::streamsize>(per));
+        if (!in) fail(CORA_EINVAL, "truncated HNSW centroid sidecar");
+        uint64_t label;
+        std::memcpy(&label, rec.data() + label_off, 8);
+        if (label >= nlist || seen[label])
+            fail(CORA_EINVAL, "HNSW centroid sidecar labels are not the cluster ids");
+        seen[label] = 1;
+        std::memcpy(out + label * D, rec.data() + data_off, 4 * D);
+    }
+}
+
+// Reads an IVF index file (ivf.hpp:403-445; centroids embedded, or in the hnswlib sidecar
+// for nlist >= 20000). The payload sections (FastScan
 // batches, ex codes, ids) are laid out by cluster, so a shard seeks to its own clusters and
 // reads each run of consecutive owned clusters in one piece: a shard's host memory and file
 // traffic are its share of the index, not the whole file.
@@ -1314,14 +1355,17 @@ FileIndex read_index_file(const char *path, uint32_t rank = 0, uint32_t world = 
     const uint64_t rec = D * 4 + 32 * 12;
     const uint64_t ex_stride = f.ex_bits ? D * f.ex_bits / 8 + 8 : 0;
     const uint64_t payload = blocks * rec + f.full_num * ex_stride + 4 * f.full_num;
-    if (remaining == payload)
-        fail(CORA_EINVAL, "HNSW-sidecar centroid storage (nlist >= 20000 indexes) is not supported");
-    if (remaining != payload + 4 * D * f.nlist)
+    const bool sidecar = remaining == payload;  // nlist >= 20000: hnswlib sidecar centroids
+    if (!sidecar && remaining != payload + 4 * D * f.nlist)
         fail(CORA_EINVAL, "IVF index size does not match a supported centroid layout");
     f.centroids.resize(f.nlist * D);
-    in.read(reinterpret_cast<char *>(f.centroids.data()), 4 * D * f.nlist);
-    if (!in) fail(CORA_EINVAL, "Failed to read IVF index payload");
-    const uint64_t batch_at = static_cast<uint64_t>(begin) + 4 * D * f.nlist;
+    if (sidecar) {
+        read_hnsw_centroids((std::string(path) + ".hnsw").c_str(), f.nlist, D, f.centroids.data());
+    } else {
+        in.read(reinterpret_cast<char *>(f.centroids.data()), 4 * D * f.nlist);
+        if (!in) fail(CORA_EINVAL, "Failed to read IVF index payload");
+    }
+    const uint64_t batch_at = static_cast<uint64_t>(begin) + (sidecar ? 0 : 4 * D * f.nlist);
     const uint64_t ex_at = batch_at + blocks * rec;
     const uint64_t ids_at = ex_at + f.full_num * ex_stride;
 

@@ -62,8 +62,8 @@ def read_ivf_file(path) -> dict:
     if remaining == payload + 4 * D * nlist:
         centroids = np.frombuffer(raw, np.float32, nlist * D, off).reshape(nlist, D).copy()
         off += 4 * D * nlist
-    elif remaining == payload:
-        raise ValueError("HNSW-sidecar centroid storage is not supported by this reader")
+    elif remaining == payload:  # nlist >= 20000: centroids in the hnswlib sidecar
+        centroids = read_hnsw_centroids(str(path) + ".hnsw", nlist, D)
     else:
         raise ValueError("index size does not match a supported centroid layout")
     batch = np.frombuffer(raw, np.uint8, batch_bytes, off)
@@ -73,6 +73,35 @@ def read_ivf_file(path) -> dict:
     ids = np.frombuffer(raw, np.uint32, num, off).copy()
     return dict(num=num, dim=dim, D=D, nlist=nlist, ex_bits=ex_bits, metric=metric,
                 sizes=sizes, rotator=rotator, centroids=centroids, batch=batch, ex=ex, ids=ids)
+
+
+# hnswlib's saveIndex header (third_party/.../hnswlib/hnswalg.h:685-713): offsetLevel0,
+# max_elements, cur_element_count, size_data_per_element, label_offset, offsetData (u64),
+# maxlevel (i32), enterpoint_node (u32), maxM, maxM0, M (u64), mult (f64),
+# ef_construction (u64); then cur_element_count level-0 records of size_data_per_element
+# bytes (the vector at offsetData, its u64 label at label_offset), then the upper-level
+# link lists.
+_HNSW_HDR = struct.Struct("<6Q iI 3Q d Q")
+
+
+def read_hnsw_centroids(path, nlist, D) -> np.ndarray:
+    """Rotated centroids (nlist x D) of an HNSW-initialised IVF index: element labels are
+    cluster ids (initializer.hpp:207-214, :252-279)."""
+    raw = Path(path).read_bytes()
+    (off0, _maxel, count, per, label_off, data_off, _lvl, _ep, _mm, _mm0, _m, _mult,
+     _efc) = _HNSW_HDR.unpack_from(raw, 0)
+    if count != nlist or data_off + 4 * D > per or label_off + 8 > per or off0 != 0:
+        raise ValueError("HNSW sidecar does not match the index's clusters")
+    base = _HNSW_HDR.size
+    if len(raw) < base + count * per:
+        raise ValueError("truncated HNSW sidecar")
+    level0 = np.frombuffer(raw, np.uint8, count * per, base).reshape(count, per)
+    labels = level0[:, label_off:label_off + 8].copy().view(np.uint64).reshape(count)
+    if labels.max(initial=0) >= nlist or len(np.unique(labels)) != nlist:
+        raise ValueError("HNSW sidecar labels are not the cluster ids")
+    cent = np.empty((nlist, D), np.float32)
+    cent[labels.astype(np.int64)] = level0[:, data_off:data_off + 4 * D].copy().view(np.float32)
+    return cent
 
 
 _KPERM0 = [0, 8, 1, 9, 2, 10, 3, 11, 4, 12, 5, 13, 6, 14, 7, 15]
