@@ -20,11 +20,12 @@ thread, on a bounded query sample per step.
 Multi-GPU (torchrun, one process per GPU): N GPUs form N / S copies of the index, each copy
 cluster-sharded over S GPUs (coraanns_b200.shard: every shard probes all centroids and scans
 the clusters it owns; the shards' vanguard seed keys, which give the global pruning
-threshold, and then their top-k keys are exchanged by NCCL all-gathers and merged). The
-copies answer disjoint slices of the 10K-query batch. S defaults to the fewest GPUs whose
-memory holds the index (1 for config 2: every GPU holds a full copy and no collective runs on
-the data path); `--shards S` forces cluster sharding. The batch is fixed as N grows (strong
-scaling) and `value` is queries/s of the whole job.
+threshold, and then their top-k keys are exchanged by NCCL all-gathers and merged). Each
+copy answers its own 10K-query batch (queries are independent units: no collective between
+copies), so the per-GPU work is fixed as N grows (weak scaling; strong only when a single
+copy spans every GPU). S defaults to the fewest GPUs whose memory holds the index (1 for
+config 2: every GPU holds a full copy and no collective runs on the data path); `--shards S`
+forces cluster sharding. `value` is queries/s of the whole job.
 """
 from __future__ import annotations
 
@@ -80,6 +81,16 @@ def make_data(cfg, dev):
     q = (centres[qlab] + cfg["sigma"] * torch.randn(cfg["nq"], cfg["dim"], generator=g, device=dev)
          + cfg["qnoise"] * torch.randn(cfg["nq"], cfg["dim"], generator=g, device=dev))
     return centres, base, q.contiguous()
+
+
+def make_queries(centres, cfg, n, seed, dev):
+    """Another batch of n queries from the same mixture (a replica's own batch)."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    qlab = torch.randint(0, cfg["nlist"], (n,), generator=g, device=dev)
+    q = (centres[qlab] + cfg["sigma"] * torch.randn(n, cfg["dim"], generator=g, device=dev)
+         + cfg["qnoise"] * torch.randn(n, cfg["dim"], generator=g, device=dev))
+    return q.contiguous()
 
 
 def assign(base, cent):
@@ -382,20 +393,27 @@ def main():
             dist.destroy_process_group()
         return
 
-    nq_total = cfg["nq"]
     nprobes = [args.nprobe] if args.nprobe else cfg["nprobes"]
     # Multi-GPU layout: `shards` GPUs hold one copy of the index (cluster-sharded when > 1)
-    # and world // shards such copies answer disjoint slices of the query batch. By default
-    # the index is sharded only as far as memory requires (config 2 fits one GPU many times
-    # over, so every GPU holds a full copy).
+    # and world // shards such copies (replicas) each answer their own batch of the
+    # config's queries (independent units, no collective between replicas): weak scaling
+    # over replicas, the per-GPU work fixed as N grows. By default the index is sharded only
+    # as far as memory requires (config 2 fits one GPU many times over, so every GPU holds a
+    # full copy). Replica 0's batch is the N = 1 batch; replica r draws another batch from
+    # the same mixture (the same seed on every shard of the replica) with its own ground
+    # truth.
     shards = args.shards or auto_shards(sd, world, dev)
     if world % shards:
         raise SystemExit(f"--shards {shards} does not divide {world} GPUs")
     replicas = world // shards
     rep, srank = rank // shards, rank % shards
-    lo, hi = nq_total * rep // replicas, nq_total * (rep + 1) // replicas
-    nq = hi - lo
-    qs = q[lo:hi].contiguous()
+    nq = cfg["nq"]
+    nq_total = nq * replicas
+    if rep == 0:
+        qs, gts = q, (gt_ids, gt_d)
+    else:
+        qs = make_queries(centres, cfg, nq, cfg["seed"] + 7919 * rep, dev)
+        gts = ground_truth(base, qs, k)
     # A dedicated (non-default) stream: the engine enqueues every kernel of a search on it and
     # the timing events are recorded on it too. torch's default stream is the legacy NULL
     # stream, which the engine's non-blocking streams do not order against.
@@ -441,7 +459,7 @@ def main():
         search_dev(npb)
         torch.cuda.synchronize()
         eng.check_device()
-        r = recall_at_k(base, qs, gt_ids[lo:hi], gt_d[lo:hi],
+        r = recall_at_k(base, qs, gts[0], gts[1],
                         out_i.cpu().numpy().view(np.uint32), k)
         # every shard of a replica holds the same result: count each replica once
         r = total(r * nq if srank == 0 else 0.0) / nq_total
@@ -484,7 +502,7 @@ def main():
         torch.cuda.synchronize()
     eng.check_device()
     ms = total(ev0.elapsed_time(ev1) / args.steps, dist.ReduceOp.MAX if world > 1 else None)
-    qps = nq_total / (ms / 1e3)  # the whole batch, answered by all replicas together
+    qps = nq_total / (ms / 1e3)  # every replica's batch, answered side by side
 
     # ---- stage times: the same searches again with stage events (kernels launched one by
     # one), for the per-stage breakdown and the dominant kernel's duration
@@ -575,15 +593,17 @@ def main():
         parallelism = "single"
     elif shards == 1:
         parallelism = (f"query-parallel x{replicas} (each GPU holds the whole index and answers "
-                       f"{nq} of the {nq_total} queries; no collective on the data path)")
+                       f"its own batch of {nq} queries; no collective on the data path)")
     else:
-        parallelism = (f"{replicas} replica(s) x {shards} cluster shards (NCCL all-gather of "
-                       f"seed and top-k keys within each replica)")
+        parallelism = (f"{replicas} replica(s) x {shards} cluster shards, {nq} queries per "
+                       f"replica (NCCL all-gather of seed and top-k keys within each replica)")
+    # weak over replicas (each answers its own batch); strong when one replica is sharded
+    scaling = "strong" if (replicas == 1 and world > 1) else "weak"
     if rank == 0:
         line = dict(
             metric="QPS at recall@10>=0.95 (IVF-RaBitQ search)", value=qps, unit="queries/s",
             n_gpus=world, steps=args.steps, warmup=args.warmup, ms_per_step=ms,
-            higher_is_better=True, scaling="strong", vs_baseline=None,
+            higher_is_better=True, scaling=scaling, vs_baseline=None,
             dtype="u32+f32", data="synthetic (seeded Gaussian mixture, BASELINE config 2 shape)",
             config=dict(workload=f"{args.config}: {cfg['n']} x d{cfg['dim']} L2, nlist {cfg['nlist']}, "
                                  f"8-bit RaBitQ, {nq_total} queries, topk {k}",
