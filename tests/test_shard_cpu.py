@@ -156,3 +156,13 @@ def test_index_file_shard_info_partitions_the_file():
         assert sum(p["clusters"] for p in parts) == whole["clusters"]
         assert sum(p["payload_bytes"] for p in parts) == whole["payload_bytes"]
         assert max(p["payload_bytes"] for p in parts) < whole["payload_bytes"]
+
+
+def test_index_file_shard_info_rejects_bad_arguments(tmp_path):
+    import coraanns_b200 as cb
+    path = GOLDEN / "d96.index"
+    for rank, world in ((2, 2), (0, 0), (0, 1000)):
+        with pytest.raises(ValueError):
+            cb.index_file_shard_info(path, rank, world)
+    with pytest.raises(ValueError):
+        cb.index_file_shard_info(tmp_path / "missing.index", 0, 1)
