@@ -604,7 +604,7 @@ def main():
             metric="QPS at recall@10>=0.95 (IVF-RaBitQ search)", value=qps, unit="queries/s",
             n_gpus=world, steps=args.steps, warmup=args.warmup, ms_per_step=ms,
             higher_is_better=True, scaling=scaling, vs_baseline=None,
-            dtype="u32+f32", data="synthetic (seeded Gaussian mixture, BASELINE config 2 shape)",
+            dtype="i8+f32", data="synthetic (seeded Gaussian mixture, BASELINE config 2 shape)",
             config=dict(workload=f"{args.config}: {cfg['n']} x d{cfg['dim']} L2, nlist {cfg['nlist']}, "
                                  f"8-bit RaBitQ, {nq_total} queries, topk {k}",
                         nprobe=chosen, recall_at_10=sweep.get(chosen), recall_sweep=sweep,
