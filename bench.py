@@ -338,8 +338,9 @@ def main():
         dist.broadcast(cent, 0)
         dist.broadcast(lab, 0)
     log(f"[bench] data + partition {time.time() - t0:.1f}s")
+    # the builder is torch-only tooling; importing it does not map the search library, so
+    # the reference arm below never loads libcoraanns_b200.so
     from coraanns_b200 import builder
-    import coraanns_b200 as cb
     need_file = (args.impl == "reference") or (rank == 0 and world == 1 and not args.no_cpu_baseline)
     t1 = time.time()
     sd = builder.build_index(base, cent, lab, seed=cfg["seed"], device=dev, keep_bits=need_file)
@@ -393,6 +394,7 @@ def main():
             dist.destroy_process_group()
         return
 
+    import coraanns_b200 as cb
     nprobes = [args.nprobe] if args.nprobe else cfg["nprobes"]
     # Multi-GPU layout: `shards` GPUs hold one copy of the index (cluster-sharded when > 1)
     # and world // shards such copies (replicas) each answer their own batch of the

@@ -57,30 +57,44 @@ int main(int argc, char **argv) {
     try {
         const std::string recall_base = take_recall_base(argc, argv);
         const std::string index_file = argv[1], query_file = argv[2], gt_file = argv[3];
-        CliOptions opt(argc, argv, 4);
-        opt.require_known({"topk", "nprobes", "rounds", "warmup", "batch-q", "threads", "query-chunk",
-                           "vanguard-size", "cpu-secondary-filter", "profile", "cross-query-reuse",
-                           "candidate-stats", "gpu-filter-timing", "exact-base", "recall-once",
-                           "queue-capacity", "queue-spill-capacity"});
-        const std::size_t topk = opt.get_size("topk", 100);
-        const std::size_t rounds = opt.get_size("rounds", 5);
-        const std::size_t warmup = opt.get_size("warmup", 1);
-        const bool recall_once = opt.get_bool("recall-once", false);
-        const std::size_t batch_q = opt.get_size("batch-q", coraanns::default_batch_q);
+        // the reference CLI's options (apps/search.cpp:26-318), in the order they are read
+        OptionTable opt{{"topk", OptionKind::kSize},
+                        {"rounds", OptionKind::kSize},
+                        {"warmup", OptionKind::kSize},
+                        {"recall-once", OptionKind::kBool},
+                        {"batch-q", OptionKind::kSize},
+                        {"threads", OptionKind::kSize},
+                        {"vanguard-size", OptionKind::kSize},
+                        {"profile", OptionKind::kBool},
+                        {"candidate-stats", OptionKind::kBool},
+                        {"gpu-filter-timing", OptionKind::kBool},
+                        {"cross-query-reuse", OptionKind::kBool},
+                        {"cpu-secondary-filter", OptionKind::kBool},
+                        {"queue-capacity", OptionKind::kSize},
+                        {"queue-spill-capacity", OptionKind::kSize},
+                        {"query-chunk", OptionKind::kSize},
+                        {"exact-base", OptionKind::kText},
+                        {"nprobes", OptionKind::kText}};
+        opt.parse(argc, argv, 4);
+        const std::size_t topk = opt.size("topk", 100);
+        const std::size_t rounds = opt.size("rounds", 5);
+        const std::size_t warmup = opt.size("warmup", 1);
+        const bool recall_once = opt.flag("recall-once", false);
+        const std::size_t batch_q = opt.size("batch-q", coraanns::default_batch_q);
         if (batch_q < 1 || batch_q > 6) throw std::invalid_argument("batch-q must be in [1, 6]");
-        const std::size_t threads = opt.get_size("threads", static_cast<std::size_t>(omp_get_max_threads()));
+        const std::size_t threads = opt.size("threads", static_cast<std::size_t>(omp_get_max_threads()));
         if (threads == 0 || threads > static_cast<std::size_t>(std::numeric_limits<int>::max()))
             throw std::invalid_argument("threads must be a positive int");
         omp_set_dynamic(0);
         omp_set_num_threads(static_cast<int>(threads));
-        const std::size_t vanguard = opt.get_size("vanguard-size", coraanns::default_vanguard_size);
-        const bool profile = opt.get_bool("profile", false);
-        const bool candidate_stats = opt.get_bool("candidate-stats", false);
-        const bool filter_timing = opt.get_bool("gpu-filter-timing", false);
-        const bool reuse = opt.get_bool("cross-query-reuse", true);
-        const bool secondary = opt.get_bool("cpu-secondary-filter", true);
-        const std::size_t qcap = opt.get_size("queue-capacity", coraanns::queue::default_capacity);
-        const std::size_t scap = opt.get_size("queue-spill-capacity", coraanns::queue::default_spill_capacity);
+        const std::size_t vanguard = opt.size("vanguard-size", coraanns::default_vanguard_size);
+        const bool profile = opt.flag("profile", false);
+        const bool candidate_stats = opt.flag("candidate-stats", false);
+        const bool filter_timing = opt.flag("gpu-filter-timing", false);
+        const bool reuse = opt.flag("cross-query-reuse", true);
+        const bool secondary = opt.flag("cpu-secondary-filter", true);
+        const std::size_t qcap = opt.size("queue-capacity", coraanns::queue::default_capacity);
+        const std::size_t scap = opt.size("queue-spill-capacity", coraanns::queue::default_spill_capacity);
         if (qcap == 0 || (qcap & (qcap - 1)) != 0)
             throw std::invalid_argument("queue-capacity must be a positive power of two");
 
@@ -89,7 +103,7 @@ int main(int argc, char **argv) {
         const Matrix<uint32_t> gt = load_vectors<uint32_t>(gt_file);
         const std::size_t nq = query.rows, dim = query.cols;
         std::cout << "Loaded " << nq << " queries with dimension " << dim << std::endl;
-        const std::size_t chunk_req = opt.get_size("query-chunk", nq);
+        const std::size_t chunk_req = opt.size("query-chunk", nq);
         if (chunk_req == 0) throw std::invalid_argument("query-chunk must be positive");
         const std::size_t chunk = std::min({chunk_req, nq, coraanns::max_query_chunk});
 
@@ -100,7 +114,7 @@ int main(int argc, char **argv) {
         // --exact-base: FP32 diagnostic refine against a mapped base (apps/search.cpp:126-146,
         // 171-175); exact distances are squared L2, the metric of the hybrid search path
         std::unique_ptr<MappedVectors> exact_base;
-        const std::string exact_base_file = opt.get("exact-base", "");
+        const std::string exact_base_file = opt.text("exact-base", "");
         if (!exact_base_file.empty()) {
             exact_base = std::make_unique<MappedVectors>(exact_base_file);
             if (exact_base->rows() != shape.num_vectors || exact_base->dim() != shape.dim) {
@@ -119,7 +133,7 @@ int main(int argc, char **argv) {
         if (!recall_once)
             evaluator = std::make_unique<RecallEvaluator>(query.data.data(), nq, dim, gt, topk, recall_base);
         validate_benchmark_shape(nq, dim, gt.rows, gt.cols, shape.dim, topk, rounds);
-        const auto nprobes = parse_nprobes(opt.get("nprobes", ""), shape.num_clusters);
+        const auto nprobes = parse_nprobes(opt.text("nprobes", ""), shape.num_clusters);
         const std::size_t max_nprobe = *std::max_element(nprobes.begin(), nprobes.end());
         coraanns::validate_search_shape(chunk, topk, max_nprobe, shape.num_clusters, shape.padded_dim);
 

@@ -6,7 +6,10 @@ argument meaning and error behaviour, with the C++ exception types mapped to
 ``InvalidArgument`` (std::invalid_argument, a ``LogicError``), ``LogicError``
 (std::logic_error) and ``RuntimeError`` (std::runtime_error).
 
-There is no CPU fallback: importing this module fails if the CUDA library was not built.
+There is no CPU fallback: the first call into the library (creating a HybridIndex, or
+``load_library()``) raises ImportError if the CUDA library was not built. The library is
+mapped on that first call, not at import, so that tooling in this package that needs no GPU
+engine (``coraanns_b200.builder``) can be imported without it.
 """
 from __future__ import annotations
 
@@ -18,12 +21,6 @@ import numpy as np
 PKG_ROOT = Path(__file__).resolve().parent.parent
 LIB_PATH = PKG_ROOT / "_build" / "libcoraanns_b200.so"
 HEADER = PKG_ROOT.parent / "include" / "cora_b200.h"
-
-if not LIB_PATH.exists():
-    raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {PKG_ROOT}` "
-                      "(or __graft_entry__.build()); there is no CPU fallback")
-
-_lib = C.CDLL(str(LIB_PATH))
 
 CORA_OK, CORA_EINVAL, CORA_ESTATE, CORA_ERUNTIME, CORA_ECUDA, CORA_ENOMEM = range(6)
 
@@ -52,60 +49,88 @@ _p = C.c_void_p
 _u64 = C.c_uint64
 
 
-def _sig(name, res, *args):
-    f = getattr(_lib, name)
+def _sig(L, name, res, *args):
+    f = getattr(L, name)
     f.restype = res
     f.argtypes = list(args)
 
 
-_sig("cora_last_error", C.c_char_p)
-_sig("cora_create", C.c_int, C.POINTER(_p), C.c_int)
-_sig("cora_destroy", None, _p)
-_sig("cora_load_from_raw_pointers", C.c_int, _p, _u64, _u64, _u64, _u64, _u64, _p, _p, _p, _p,
-     _p, _p, _p, _p)
-_sig("cora_load_index_file", C.c_int, _p, C.c_char_p)
-_sig("cora_index_info", C.c_int, _p, _p)
-_sig("cora_prepare_workspace", C.c_int, _p, _u64, _u64, _u64)
-_sig("cora_free_workspace", None, _p)
-_sig("cora_reset_buffer", C.c_int, _p, _p, _u64)
-_sig("cora_enable_exact_refine", C.c_int, _p, _p, _u64, _u64, _u64, _u64)
-_sig("cora_index_file_shard_info", C.c_int, C.c_char_p, C.c_uint32, C.c_uint32, _p)
-_sig("cora_search", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p, C.c_int)
-_sig("cora_search_device", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p, _p)
-_sig("cora_check_device", C.c_int, _p)
-_sig("cora_seed_thresholds", C.c_int, _p, _p, _u64)
-_sig("cora_capture_thresholds", C.c_int, _p, _p, _u64)
-_sig("cora_set_vanguard_size", C.c_int, _p, _u64)
-_sig("cora_get_vanguard_size", _u64, _p)
-_sig("cora_set_queue_capacity", C.c_int, _p, _u64)
-_sig("cora_set_queue_spill_capacity", C.c_int, _p, _u64)
-_sig("cora_get_queue_capacity", _u64, _p)
-for _n in ("cora_set_profiling", "cora_set_candidate_stats", "cora_set_gpu_filter_timing",
-           "cora_set_cross_query_reuse", "cora_set_cpu_secondary_filter", "cora_set_ip_kernel_type"):
-    _sig(_n, None, _p, C.c_int)
-_sig("cora_get_ip_kernel_type", C.c_int, _p)
-_sig("cora_get_last_submitted_count", _u64, _p)
-_sig("cora_get_last_refined_count", _u64, _p)
-_sig("cora_get_last_spilled_count", _u64, _p)
-_sig("cora_get_last_gpu_filter_ms", C.c_float, _p)
-_sig("cora_debug_copy", C.c_int, _p, C.c_int, _p, _u64)
-_sig("cora_get_candidate_capacity", _u64, _p)
-_sig("cora_get_last_stage_ms", C.c_int, _p, _p, _u64)
-_sig("cora_stage_totals", C.c_int, _p, _p, _u64, _p)
-_sig("cora_stage_reset", C.c_int, _p)
-_sig("cora_set_vanguard_lows_budget", C.c_int, _p, _u64)
-_sig("cora_get_vanguard_mode", C.c_int, _p)
-_sig("cora_set_tuning", C.c_int, _p, C.c_char_p, C.c_int64)
-_sig("cora_probe_noalloc", C.c_int, _p, _p, _u64, _u64, _p, _p, _p)
-_sig("cora_probe_noalloc_scratch_limit", _u64)
-_sig("cora_probe_noalloc_status", C.c_int, _p, _p)
-_sig("cora_shard_plan", C.c_int, _p, _u64, C.c_uint32, _p)
-_sig("cora_shard_configure", C.c_int, _p, C.c_uint32, C.c_uint32)
-_sig("cora_shard_info", C.c_int, _p, _p)
-_sig("cora_shard_exchange_words", _u64, _u64, _u64)
-_sig("cora_shard_search_begin", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p)
-_sig("cora_shard_search_resume", C.c_int, _p, _p, _p)
-_sig("cora_shard_search_end", C.c_int, _p, _p, _p, _p)
+def _bind(L):
+    """Declares the C signatures on a freshly mapped library."""
+    _sig(L, "cora_last_error", C.c_char_p)
+    _sig(L, "cora_create", C.c_int, C.POINTER(_p), C.c_int)
+    _sig(L, "cora_destroy", None, _p)
+    _sig(L, "cora_load_from_raw_pointers", C.c_int, _p, _u64, _u64, _u64, _u64, _u64, _p, _p, _p, _p,
+         _p, _p, _p, _p)
+    _sig(L, "cora_load_index_file", C.c_int, _p, C.c_char_p)
+    _sig(L, "cora_index_info", C.c_int, _p, _p)
+    _sig(L, "cora_prepare_workspace", C.c_int, _p, _u64, _u64, _u64)
+    _sig(L, "cora_free_workspace", None, _p)
+    _sig(L, "cora_reset_buffer", C.c_int, _p, _p, _u64)
+    _sig(L, "cora_enable_exact_refine", C.c_int, _p, _p, _u64, _u64, _u64, _u64)
+    _sig(L, "cora_index_file_shard_info", C.c_int, C.c_char_p, C.c_uint32, C.c_uint32, _p)
+    _sig(L, "cora_search", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p, C.c_int)
+    _sig(L, "cora_search_device", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p, _p)
+    _sig(L, "cora_check_device", C.c_int, _p)
+    _sig(L, "cora_seed_thresholds", C.c_int, _p, _p, _u64)
+    _sig(L, "cora_capture_thresholds", C.c_int, _p, _p, _u64)
+    _sig(L, "cora_set_vanguard_size", C.c_int, _p, _u64)
+    _sig(L, "cora_get_vanguard_size", _u64, _p)
+    _sig(L, "cora_set_queue_capacity", C.c_int, _p, _u64)
+    _sig(L, "cora_set_queue_spill_capacity", C.c_int, _p, _u64)
+    _sig(L, "cora_get_queue_capacity", _u64, _p)
+    for _n in ("cora_set_profiling", "cora_set_candidate_stats", "cora_set_gpu_filter_timing",
+               "cora_set_cross_query_reuse", "cora_set_cpu_secondary_filter", "cora_set_ip_kernel_type"):
+        _sig(L, _n, None, _p, C.c_int)
+    _sig(L, "cora_get_ip_kernel_type", C.c_int, _p)
+    _sig(L, "cora_get_last_submitted_count", _u64, _p)
+    _sig(L, "cora_get_last_refined_count", _u64, _p)
+    _sig(L, "cora_get_last_spilled_count", _u64, _p)
+    _sig(L, "cora_get_last_gpu_filter_ms", C.c_float, _p)
+    _sig(L, "cora_debug_copy", C.c_int, _p, C.c_int, _p, _u64)
+    _sig(L, "cora_get_candidate_capacity", _u64, _p)
+    _sig(L, "cora_get_last_stage_ms", C.c_int, _p, _p, _u64)
+    _sig(L, "cora_stage_totals", C.c_int, _p, _p, _u64, _p)
+    _sig(L, "cora_stage_reset", C.c_int, _p)
+    _sig(L, "cora_set_vanguard_lows_budget", C.c_int, _p, _u64)
+    _sig(L, "cora_get_vanguard_mode", C.c_int, _p)
+    _sig(L, "cora_set_tuning", C.c_int, _p, C.c_char_p, C.c_int64)
+    _sig(L, "cora_probe_noalloc", C.c_int, _p, _p, _u64, _u64, _p, _p, _p)
+    _sig(L, "cora_probe_noalloc_scratch_limit", _u64)
+    _sig(L, "cora_probe_noalloc_status", C.c_int, _p, _p)
+    _sig(L, "cora_shard_plan", C.c_int, _p, _u64, C.c_uint32, _p)
+    _sig(L, "cora_shard_configure", C.c_int, _p, C.c_uint32, C.c_uint32)
+    _sig(L, "cora_shard_info", C.c_int, _p, _p)
+    _sig(L, "cora_shard_exchange_words", _u64, _u64, _u64)
+    _sig(L, "cora_shard_search_begin", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p)
+    _sig(L, "cora_shard_search_resume", C.c_int, _p, _p, _p)
+    _sig(L, "cora_shard_search_end", C.c_int, _p, _p, _p, _p)
+
+
+_cdll = None
+
+
+def load_library():
+    """Maps libcoraanns_b200.so (once) and returns it; ImportError when it was not built."""
+    global _cdll
+    if _cdll is None:
+        if not LIB_PATH.exists():
+            raise ImportError(f"{LIB_PATH} is missing: build it with `make -C {PKG_ROOT}` "
+                              "(or __graft_entry__.build()); there is no CPU fallback")
+        L = C.CDLL(str(LIB_PATH))
+        _bind(L)
+        _cdll = L
+    return _cdll
+
+
+class _LazyLib:
+    """Forwards attribute access to the library, mapping it on first use."""
+
+    def __getattr__(self, name):
+        return getattr(load_library(), name)
+
+
+_lib = _LazyLib()
 
 STAGES = ("rotate_prep", "centroid_dist", "select_probes", "vanguard_grouping",
           "vanguard_scan", "vanguard_select", "seed_refine", "threshold", "main_grouping",

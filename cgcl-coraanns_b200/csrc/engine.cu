@@ -1879,7 +1879,10 @@ uint64_t cora_get_candidate_capacity(const cora_engine *engine) {
 //  * nothing in the block has to start at zero: every kernel writes each scratch element
 //    before any kernel reads it;
 //  * the first call on a device, with that device current, looks the block's address up
-//    (cudaGetSymbolAddress) and caches it; make that first call before any stream capture;
+//    (cudaGetSymbolAddress) and caches it with the device's current context; make that first
+//    call before any stream capture. After the context is torn down and created again
+//    (cudaDeviceReset), the next call looks the address up again, so it too must come before
+//    any capture;
 //  * there is ONE block per device, shared by every engine on that device: calls that
 //    overlap in time (two streams, two host threads) race on it and corrupt each other's
 //    results. Serialise them, e.g. issue them all on one stream.
@@ -1892,7 +1895,32 @@ __device__ __align__(256) unsigned char g_noalloc_scratch[kNoallocScratchBytes];
 
 constexpr int kNoallocMaxDevices = 64;
 std::mutex g_noalloc_mutex;
-unsigned char *g_noalloc_ptr[kNoallocMaxDevices] = {};
+// Per device: the context the address was looked up in, and the address. A context that is
+// torn down and created again (cudaDeviceReset) loads the module anew, so the address is
+// looked up again whenever the device's current context differs from the cached one.
+struct NoallocSlot {
+    void *ctx = nullptr;
+    unsigned char *ptr = nullptr;
+};
+NoallocSlot g_noalloc_slot[kNoallocMaxDevices];
+
+using CtxGetCurrentFn = int (*)(void **);
+inline void *current_context() {
+    static CtxGetCurrentFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    });
+    if (!fn) fail(CORA_ECUDA, "the driver does not provide cuCtxGetCurrent");
+    void *ctx = nullptr;
+    if (fn(&ctx) != 0 || !ctx) fail(CORA_ECUDA, "no current CUDA context");
+    return ctx;
+}
 
 inline size_t align256(size_t b) { return (b + 255) & ~size_t{255}; }
 
@@ -1914,19 +1942,22 @@ NoallocLayout noalloc_layout(uint64_t nq, uint64_t D, uint64_t W4, uint64_t nlis
     return l;
 }
 
-// Address of this device's scratch block; the device must be current.
+// Address of this device's scratch block in its current context; the device must be current.
 unsigned char *noalloc_scratch(int device) {
     if (device < 0 || device >= kNoallocMaxDevices) fail(CORA_EINVAL, "device ordinal out of range");
+    void *ctx = current_context();
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (!g_noalloc_ptr[device]) {
+    NoallocSlot &slot = g_noalloc_slot[device];
+    if (!slot.ptr || slot.ctx != ctx) {
         void *p = nullptr;
         const cudaError_t rc = cudaGetSymbolAddress(&p, g_noalloc_scratch);
         if (rc != cudaSuccess || !p)
             fail(CORA_ERUNTIME, std::string("cudaGetSymbolAddress for the probe scratch failed: ") +
                                     cudaGetErrorString(rc));
-        g_noalloc_ptr[device] = static_cast<unsigned char *>(p);
+        slot.ctx = ctx;
+        slot.ptr = static_cast<unsigned char *>(p);
     }
-    return g_noalloc_ptr[device];
+    return slot.ptr;
 }
 
 }  // namespace
@@ -1962,7 +1993,6 @@ int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num
         float *approx = reinterpret_cast<float *>(s + l.approx);
         int *status = reinterpret_cast<int *>(s + l.status);
         cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e.stream;
-        const int inp = static_cast<int>(nprobe);
         CUDA_TRY(cudaMemsetAsync(status, 0, sizeof(int), st));
 
         const float c_b = -static_cast<float>((1u << (e.ex_bits + 1)) - 1u) / 2.0f;
@@ -1974,7 +2004,6 @@ int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num
         cora::launch_guarded_select(approx, cmin, e.nlist, num_queries, nprobe, qr, qnorm2,
                                     e.centroids.p, e.cmax, e.D, d_probe_ids, d_probe_dists,
                                     reinterpret_cast<uint32_t *>(s + l.fallback), e.num_sms, st);
-        (void)inp;
     });
 }
 

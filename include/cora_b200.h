@@ -239,7 +239,8 @@ int cora_shard_search_end(cora_engine *engine, const uint64_t *d_recv, float *d_
  * Intermediates live in one static device block of cora_probe_noalloc_scratch_limit()
  * bytes (16 MiB) per device; a call needing more is rejected with CORA_EINVAL (split the
  * queries). Nothing in the block needs to start at zero. The first call on each device
- * looks the block up (cudaGetSymbolAddress): make it before any stream capture. The block
+ * looks the block up (cudaGetSymbolAddress): make it before any stream capture (and again
+ * the first call after the device's context was reset, which looks it up anew). The block
  * is shared by all engines of a device, so calls that overlap in time race on it:
  * serialise them (e.g. one stream). */
 int cora_probe_noalloc(cora_engine *engine, const float *d_queries, uint64_t num_queries,

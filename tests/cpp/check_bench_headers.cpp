@@ -30,30 +30,53 @@ static bool throws(const std::function<void()> &f) {
     return false;
 }
 
-static CliOptions parse(std::vector<std::string> args) {
+static OptionTable parse(std::vector<std::string> args) {
     std::vector<char *> argv;
     for (auto &a : args) argv.push_back(a.data());
     argv.push_back(nullptr);
-    return CliOptions(static_cast<int>(args.size()), argv.data(), 0);
+    OptionTable t{{"topk", OptionKind::kSize},
+                  {"rounds", OptionKind::kSize},
+                  {"nprobes", OptionKind::kText},
+                  {"profile", OptionKind::kBool},
+                  {"absent", OptionKind::kBool}};
+    t.parse(static_cast<int>(args.size()), argv.data(), 0);
+    return t;
+}
+
+static std::string message_of(const std::function<void()> &f) {
+    try {
+        f();
+    } catch (const std::exception &e) {
+        return e.what();
+    }
+    return "";
 }
 
 int main(int argc, char **argv) {
     const std::string dir = argc > 1 ? argv[1] : ".";
-    // options
+    // options: the reference's syntax and messages
     auto o = parse({"--topk", "10", "--nprobes=4,8", "--profile", "on"});
-    CHECK(o.get_size("topk", 0) == 10);
-    CHECK(o.get("nprobes", "") == "4,8");
-    CHECK(o.get_bool("profile", false));
-    CHECK(!o.get_bool("absent", false));
-    CHECK(!throws([&] { o.require_known({"topk", "nprobes", "profile"}); }));
-    CHECK(throws([&] { o.require_known({"topk", "nprobes"}); }));
-    CHECK(throws([] { parse({"--topk", "1", "--topk", "2"}); }));
-    CHECK(throws([] { parse({"--topk"}); }));
-    CHECK(throws([] { parse({"--topk", "--rounds", "2"}); }));
-    CHECK(throws([] { parse({"positional"}); }));
-    CHECK(throws([] { parse({"--topk", "-1"}).get_size("topk", 0); }));
-    CHECK(throws([] { parse({"--topk", "12x"}).get_size("topk", 0); }));
-    CHECK(throws([] { parse({"--profile", "maybe"}).get_bool("profile", false); }));
+    CHECK(o.size("topk", 0) == 10);
+    CHECK(o.size("rounds", 5) == 5);
+    CHECK(o.text("nprobes", "") == "4,8");
+    CHECK(o.flag("profile", false));
+    CHECK(!o.flag("absent", false));
+    CHECK(o.given("topk") && !o.given("rounds"));
+    CHECK(parse({"--topk="}).size("topk", 7) == 7);  // empty value: not given
+    CHECK(message_of([] { parse({"--bogus", "1"}); }) == "Unknown option --bogus");
+    CHECK(message_of([] { parse({"--topk", "1", "--topk", "2"}); }) ==
+          "Invalid or duplicate option --topk");
+    CHECK(message_of([] { parse({"--topk"}); }) == "Missing value for --topk");
+    CHECK(message_of([] { parse({"--topk", "--rounds", "2"}); }) == "Missing value for --topk");
+    CHECK(message_of([] { parse({"positional"}); }) == "Unexpected positional argument: positional");
+    CHECK(message_of([] { parse({"--topk", "-1"}); }) == "Invalid integer for --topk: -1");
+    CHECK(message_of([] { parse({"--topk", "12x"}); }) == "Invalid integer for --topk: 12x");
+    CHECK(message_of([] { parse({"--topk", "99999999999999999999999"}); }) ==
+          "Invalid integer for --topk: 99999999999999999999999");
+    CHECK(message_of([] { parse({"--profile", "maybe"}); }) == "Invalid boolean for --profile: maybe");
+    CHECK(!parse({"--profile=off"}).flag("profile", true));
+    CHECK(throws([] { parse({}).size("profile", 0); }));   // read as the wrong kind
+    CHECK(throws([] { parse({}).flag("undeclared", 0); }));
     CHECK(parse_nprobes("4,8", 16) == (std::vector<std::size_t>{4, 8}));
     CHECK(parse_nprobes("", 16) == (std::vector<std::size_t>{16}));
     CHECK(parse_nprobes("", 100) == (std::vector<std::size_t>{40, 50, 60, 75, 95}));
@@ -62,6 +85,9 @@ int main(int argc, char **argv) {
     CHECK(throws([] { parse_nprobes("4,4", 16); }));
     CHECK(throws([] { parse_nprobes("4,,8", 16); }));
     CHECK(throws([] { parse_nprobes("+4", 16); }));
+    CHECK(throws([] { parse_nprobes("4,", 16); }));
+    CHECK(message_of([] { parse_nprobes("4,4", 16); }) == "Duplicate nprobe value: 4");
+    CHECK(message_of([] { parse_nprobes("17", 16); }) == "Each nprobe must be in [1, nlist]; got: 17");
     CHECK(join_values({4, 8, 16}) == "4,8,16");
     CHECK(throws([] { validate_benchmark_shape(10, 8, 9, 10, 8, 10, 1); }));
     CHECK(throws([] { validate_benchmark_shape(10, 8, 10, 5, 8, 10, 1); }));
