@@ -35,7 +35,8 @@ EXPORTS = [
     "cora_get_vanguard_size", "cora_set_queue_capacity", "cora_set_queue_spill_capacity",
     "cora_get_queue_capacity", "cora_set_profiling", "cora_set_candidate_stats",
     "cora_set_gpu_filter_timing", "cora_set_cross_query_reuse", "cora_set_cpu_secondary_filter",
-    "cora_set_ip_kernel_type", "cora_get_ip_kernel_type", "cora_get_last_submitted_count",
+    "cora_set_ip_kernel_type", "cora_get_ip_kernel_type", "cora_set_refine_full_code",
+    "cora_get_refine_full_code", "cora_get_last_submitted_count",
     "cora_get_last_refined_count", "cora_get_last_spilled_count", "cora_get_last_gpu_filter_ms",
     "cora_debug_copy", "cora_get_last_stage_ms", "cora_stage_totals", "cora_stage_reset",
     "cora_set_vanguard_lows_budget", "cora_set_tuning", "cora_get_vanguard_mode",
@@ -83,6 +84,8 @@ def _bind(L):
                "cora_set_cross_query_reuse", "cora_set_cpu_secondary_filter", "cora_set_ip_kernel_type"):
         _sig(L, _n, None, _p, C.c_int)
     _sig(L, "cora_get_ip_kernel_type", C.c_int, _p)
+    _sig(L, "cora_set_refine_full_code", None, _p, C.c_int)
+    _sig(L, "cora_get_refine_full_code", C.c_int, _p)
     _sig(L, "cora_get_last_submitted_count", _u64, _p)
     _sig(L, "cora_get_last_refined_count", _u64, _p)
     _sig(L, "cora_get_last_spilled_count", _u64, _p)
@@ -363,6 +366,12 @@ class HybridIndex:
     def set_cpu_secondary_filter(self, on): _lib.cora_set_cpu_secondary_filter(self._h, int(bool(on)))
     def set_ip_kernel_type(self, t): _lib.cora_set_ip_kernel_type(self._h, int(t))
     def get_ip_kernel_type(self): return int(_lib.cora_get_ip_kernel_type(self._h))
+
+    def set_refine_full_code(self, on):
+        """Refine with <q', 128 b + u> instead of the reference's 128 ip1 + ip2 (opt-in)."""
+        _lib.cora_set_refine_full_code(self._h, int(bool(on)))
+
+    def get_refine_full_code(self): return bool(_lib.cora_get_refine_full_code(self._h))
 
     def get_last_submitted_count(self): return int(_lib.cora_get_last_submitted_count(self._h))
     def get_last_refined_count(self): return int(_lib.cora_get_last_refined_count(self._h))

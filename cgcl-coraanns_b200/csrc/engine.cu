@@ -278,6 +278,8 @@ struct Engine {
     bool profiling = false, candidate_stats = false, gpu_filter_timing = false;
     bool search_graphs = true;  // replay whole searches from a captured CUDA graph
     bool cross_query_reuse = true, cpu_secondary_filter = true;
+    // refinement form: false (default) the reference's 128 ip1 + ip2, true <q', 128 b + u>
+    bool refine_full_code = false;
     int ip_kernel_type = 0;
     // Upper bound on the HBM buffer holding the vanguard pairs' lower bounds; larger
     // worst cases fall back to rescanning the vanguard clusters.
@@ -328,11 +330,11 @@ struct Engine {
         uint32_t *d_oi = nullptr;
         cudaStream_t st = nullptr;
         int wsl = 0, twl = 0;
-        bool reuse = false;
+        bool reuse = false, full_code = false;
         bool same(const GraphKey &o) const {
             return d_q == o.d_q && nq == o.nq && k == o.k && np == o.np && ws_gen == o.ws_gen &&
                    vanguard == o.vanguard && d_od == o.d_od && d_oi == o.d_oi && st == o.st &&
-                   wsl == o.wsl && twl == o.twl && reuse == o.reuse;
+                   wsl == o.wsl && twl == o.twl && reuse == o.reuse && full_code == o.full_code;
         }
     };
     GraphKey graph_key;
@@ -950,7 +952,8 @@ SearchView Engine::search_view() const {
                       static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
                       last_dq, scal.p, qrange.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p,
                       cand_cnt.p, seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n,
-                      lows_top.p, err.p, warp_select_limit, topk_warp_limit};
+                      lows_top.p, err.p, warp_select_limit, topk_warp_limit,
+                      refine_full_code ? 1 : 0};
 }
 
 void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, float *d_od,
@@ -976,6 +979,7 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     key.wsl = warp_select_limit;
     key.twl = topk_warp_limit;
     key.reuse = cross_query_reuse;
+    key.full_code = refine_full_code;
     if (!graph_exec || !graph_key.same(key)) {
         drop_graph();
         CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
@@ -1084,7 +1088,7 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
         CUDA_TRY(cudaGetLastError());
     }
     mark(6, st);
-    const size_t refine_sm = (size_t)D * 8 + np * sizeof(ProbeInfo);  // query as doubles
+    const size_t refine_sm = refine_smem(static_cast<int>(D), static_cast<int>(np));
     CUDA_TRY(cudaFuncSetAttribute(refine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)refine_sm));
     refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 0);
@@ -1193,7 +1197,7 @@ void Engine::enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uin
     }
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));
     mark(11, st);
-    const size_t refine_sm = (size_t)D * 8 + last_np * sizeof(ProbeInfo);  // query as doubles
+    const size_t refine_sm = refine_smem(static_cast<int>(D), static_cast<int>(last_np));
     CUDA_TRY(cudaFuncSetAttribute(refine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)refine_sm));
     refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 1);
@@ -1773,6 +1777,12 @@ void cora_set_ip_kernel_type(cora_engine *engine, int kernel_type) {
 }
 int cora_get_ip_kernel_type(const cora_engine *engine) {
     return engine && engine->e ? engine->e->ip_kernel_type : 0;
+}
+void cora_set_refine_full_code(cora_engine *engine, int enabled) {
+    if (engine && engine->e) engine->e->refine_full_code = enabled != 0;
+}
+int cora_get_refine_full_code(const cora_engine *engine) {
+    return engine && engine->e ? (engine->e->refine_full_code ? 1 : 0) : 0;
 }
 
 uint64_t cora_get_last_submitted_count(const cora_engine *engine) {

@@ -1,9 +1,12 @@
 // Ex-code refinement, vanguard threshold and final top-k kernels.
 //
-//  refine_kernel     ex = f_add_ex + g + f_rescale_ex * (<q', 128 b + u> + kb)
-//                    (reference: src/search/cpu_refinement.cpp:183-191 with the 7-bit code
-//                     layout of third_party/rabitq/.../quantization/pack_excode.hpp:216-264,
-//                     decoded as utils/space.hpp:677-762 does)
+//  refine_kernel     ex = (f_add_ex + g) + f_rescale_ex * ((128 ip1 + ip2) + kb), with
+//                    ip1 = width * ip_int the scan's integer estimate of <q', b> and
+//                    ip2 = <q', u> (reference: src/search/cpu_refinement.cpp:183-191 =
+//                    split_distance_boosting, third_party/rabitq/.../index/estimator.hpp:
+//                    86-103, with the 7-bit code layout of quantization/pack_excode.hpp:
+//                    216-264, decoded as utils/space.hpp:677-762 does); opt-in full-code
+//                    form: (f_add_ex + g) + f_rescale_ex * (<q', 128 b + u> + kb)
 //  threshold_kernel  T1 = min(T0, k-th smallest seed distance)  (reference: vanguard seeds
 //                    set thresholds, src/search/filter_kernels.cuh:308-468)
 //  merge_kernel      best k by (ex, id) among ex < T0, padded with (FLT_MAX, 0)
@@ -82,38 +85,53 @@ __global__ void __launch_bounds__(256) build_refine_rows_kernel(
     }
 }
 
-// One 64-dim block of the 8-bit code inner product, continuing the fp64 chain `acc` in
-// ascending dimension order (every product is exact in fp64); v holds the block's 64 codes,
-// x its 64 rotated query values. Each byte becomes the double c exactly as
-// (2^52 + c) - 2^52 from its bit pattern, so the loop runs no conversion instructions.
-__device__ __forceinline__ double block_code8_ip(const double *__restrict__ x, const uint4 (&v)[4],
-                                                 double acc) {
+// One 64-dim block of a refine row (v: its 64 codes c = 128 b + u, 4 per word, dimension
+// order) against the rotated query x (fp64, shared memory), continuing the fp64 chain `acc`
+// in ascending dimension order (every product is exact in fp64). Each byte becomes the
+// double c (or u = c & 127) exactly as (2^52 + c) - 2^52 from its bit pattern, so the loop
+// runs no conversion instructions.
+//   kSplit (the reference form): acc accumulates <x, u>, and ip accumulates
+//     sum_i b_i qint_i with dp4a over the code words' top bits and the query's qint bytes
+//     (qw: qint of dims 4t .. 4t + 3 as the signed bytes of word t), exact in int32;
+//   otherwise: acc accumulates <x, 128 b + u>.
+template <bool kSplit>
+__device__ __forceinline__ void block_code8_ip(const double *__restrict__ x,
+                                               const uint32_t *__restrict__ qw,
+                                               const uint4 (&v)[4], double &acc, int &ip) {
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
         const uint32_t w4[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
+            const uint32_t w = kSplit ? (w4[h] & 0x7F7F7F7Fu) : w4[h];
+            if (kSplit)
+                ip = __dp4a(static_cast<int>((w4[h] >> 7) & 0x01010101u),
+                            static_cast<int>(qw[4 * t + h]), ip);
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
-                const uint32_t c = __byte_perm(w4[h], 0u, 0x4440u | i);
+                const uint32_t c = __byte_perm(w, 0u, 0x4440u | i);
                 const double cd = __dsub_rn(__hiloint2double(0x43300000, static_cast<int>(c)),
                                             4503599627370496.0);
                 acc = __fma_rn(x[16 * t + 4 * h + i], cd, acc);
             }
         }
     }
-    return acc;
 }
 
 // One CTA per query, one thread per candidate: a candidate's refine row (its 8-bit codes, D
-// bytes, 32-byte sectors used whole) and its meta word are loaded before its fp64 chain. mode 0 refines the vanguard seeds [0, cnt) and records the seed count; mode 1
-// refines the main candidates [seed_cnt, cnt). Dynamic shared memory: D floats + nprobe
-// ProbeInfo.
+// bytes, 32-byte sectors used whole) and its meta word are loaded before its fp64 chain.
+// mode 0 refines the vanguard seeds [0, cnt) and records the seed count; mode 1 refines the
+// main candidates [seed_cnt, cnt). Dynamic shared memory (refine_smem): the query as D
+// doubles, its qint as D / 4 words of signed bytes, nprobe ProbeInfo.
+__host__ __device__ __forceinline__ size_t refine_smem(int D, int nprobe) {
+    return (size_t)D * 8 + (size_t)D + (size_t)nprobe * sizeof(ProbeInfo);
+}
 __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, SearchView sv,
                                                                 int mode) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     double *x = reinterpret_cast<double *>(smem_raw);
-    ProbeInfo *pinfo = reinterpret_cast<ProbeInfo *>(x + ix.D);
+    uint32_t *qw = reinterpret_cast<uint32_t *>(x + ix.D);
+    ProbeInfo *pinfo = reinterpret_cast<ProbeInfo *>(qw + ix.D / 4);
     const int q = blockIdx.x;
     const uint32_t cnt = sv.cand_cnt[q];
     const uint32_t cap = static_cast<uint32_t>(sv.cap);
@@ -135,6 +153,22 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
     } else {
         for (int j = threadIdx.x; j < ix.D; j += blockDim.x)
             x[j] = static_cast<double>(sv.qr[(size_t)q * ix.D + j]);
+        // qint of dims 4t .. 4t + 3 from the query's two's-complement bit-planes (plane b,
+        // word j / 32, bit 31 - j % 32 holds bit b of qint_j & 0xFF): byte i of word t
+        const int W4 = 4 * ix.G16;
+        const uint32_t *pl = sv.planes + (size_t)q * 8 * W4;
+        for (int t = threadIdx.x; t < ix.D / 4; t += blockDim.x) {
+            uint32_t word = 0;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const int j = 4 * t + i;
+                uint32_t byte = 0;
+#pragma unroll
+                for (int b = 0; b < 8; ++b) byte |= ((pl[b * W4 + j / 32] >> (31 - j % 32)) & 1u) << b;
+                word |= byte << (8 * i);
+            }
+            qw[t] = word;
+        }
     }
     const int np = mode == 0 ? sv.veff : sv.nprobe;
     for (int r = threadIdx.x; r < np; r += blockDim.x) {
@@ -142,7 +176,7 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
         pinfo[r] = ProbeInfo{ix.cl_start[c], ix.cl_size[c], sv.probe_g[(size_t)q * sv.nprobe + r]};
     }
     __syncthreads();
-    const float kb = sv.scal[q].kb;
+    const float kb = sv.scal[q].kb, width = sv.scal[q].width;
     const int nblocks = ix.D / 64;
     const int row4 = ix.D / 16;  // uint4 per refine row
     for (uint32_t i = from + threadIdx.x; i < to; i += blockDim.x) {
@@ -186,14 +220,28 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
         const float2 f = make_float2(__uint_as_float(mt.x), __uint_as_float(mt.y));
         const uint32_t id = mt.z;
         double acc = 0.0;
-        for (int blk = 0; blk < nblocks; ++blk) {
-            uint4 v[4];
+        int ip = 0;
+        float t;  // the factor of f_rescale_ex
+        if (sv.refine_full_code) {
+            for (int blk = 0; blk < nblocks; ++blk) {
+                uint4 v[4];
 #pragma unroll
-            for (int t = 0; t < 4; ++t) v[t] = __ldg(row + 4 * blk + t);
-            acc = block_code8_ip(x + 64 * blk, v, acc);
+                for (int u = 0; u < 4; ++u) v[u] = __ldg(row + 4 * blk + u);
+                block_code8_ip<false>(x + 64 * blk, qw + 16 * blk, v, acc, ip);
+            }
+            t = __fadd_rn(__double2float_rn(acc), kb);
+        } else {
+            for (int blk = 0; blk < nblocks; ++blk) {
+                uint4 v[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) v[u] = __ldg(row + 4 * blk + u);
+                block_code8_ip<true>(x + 64 * blk, qw + 16 * blk, v, acc, ip);
+            }
+            // ip1 exactly as the scan forms it; 128 * ip1 is exact
+            const float ip1 = __fmul_rn(width, static_cast<float>(ip));
+            t = __fadd_rn(__fadd_rn(__fmul_rn(128.0f, ip1), __double2float_rn(acc)), kb);
         }
-        const float ex_d = __fadd_rn(__fadd_rn(f.x, p.g),
-                                     __fmul_rn(f.y, __fadd_rn(__double2float_rn(acc), kb)));
+        const float ex_d = __fadd_rn(__fadd_rn(f.x, p.g), __fmul_rn(f.y, t));
         sv.cand_key[(size_t)q * sv.cap + i] = make_key(ex_d, id);
     }
 }

@@ -89,6 +89,9 @@ class HybridIndex {
     KernelType get_ip_kernel_type() const {
         return static_cast<KernelType>(cora_get_ip_kernel_type(engine_));
     }
+    // Refinement form (this engine's addition): false = the reference's 128 ip1 + ip2.
+    void set_refine_full_code(bool enabled) { cora_set_refine_full_code(engine_, enabled ? 1 : 0); }
+    bool get_refine_full_code() const { return cora_get_refine_full_code(engine_) != 0; }
 
     void prepare_workspace(std::size_t max_queries, std::size_t max_topk, std::size_t max_nprobe) {
         detail::check(cora_prepare_workspace(engine_, max_queries, max_topk, max_nprobe));

@@ -142,6 +142,15 @@ void cora_set_cpu_secondary_filter(cora_engine *engine, int enabled);
 void cora_set_ip_kernel_type(cora_engine *engine, int kernel_type);
 int cora_get_ip_kernel_type(const cora_engine *engine);
 
+/* Refinement form (no reference counterpart; the reference always uses its default).
+ * 0 (default): the reference's expression, ex = (f_add_ex + g) + f_rescale_ex *
+ * ((128 ip1 + ip2) + kb), ip1 = width * ip_int the scan's integer estimate of <q', b>
+ * (cpu_refinement.cpp:183-191). 1: the full 8-bit code inner product <q', 128 b + u> in place
+ * of 128 ip1 + ip2, which removes the query-quantisation error of ip1 (better recall; results
+ * then differ from the reference's). Takes effect from the next search. */
+void cora_set_refine_full_code(cora_engine *engine, int enabled);
+int cora_get_refine_full_code(const cora_engine *engine);
+
 /* Counters of the last search (hybrid.cuh:137-153). submitted = candidates that passed
  * the 1-bit lower bound (seeds included); refined = candidates refined with ex codes;
  * spilled is always 0 (no host ring). */

@@ -209,12 +209,33 @@ float cora_oracle_ip_total(const float *qr, const uint32_t *bits, const uint8_t 
     return (float)acc;
 }
 
-/* cpu_refinement.cpp:189-191: ex = f_add_ex + g + f_rescale_ex * (ipT + kb), where
- * ipT = 2^ex_bits * ip1 + ip2 is the full-code inner product above. */
+/* Full-code form (opt-in): ex = (f_add_ex + g) + f_rescale_ex * (ipT + kb), ipT the
+ * full-code inner product above in place of the reference's 2^ex_bits * ip1 + ip2. */
 float cora_oracle_ex(const cora_oracle_index *ix, uint64_t gid, float ip_total, float g,
                      float kb) {
     const float *f = ix->ex_factors + gid * 2;
     return (f[0] + g) + (f[1] * (ip_total + kb));
+}
+
+/* ip2 of cpu_refinement.cpp:183-185: <q', u> over the decoded 7-bit ex code, the quantity
+ * ip64_fxu7_avx (utils/space.hpp:677-762) computes; here one fp64 accumulation in
+ * ascending dimension order (products exact), rounded once. */
+float cora_oracle_ip_ex(const float *qr, const uint8_t *code, uint64_t D) {
+    uint8_t u[4096];
+    cora_oracle_decode_ex7(code, D, u);
+    double acc = 0.0;
+    for (uint64_t d = 0; d < D; ++d) acc += (double)qr[d] * (double)u[d];
+    return (float)acc;
+}
+
+/* cpu_refinement.cpp:186-191 (= split_distance_boosting, estimator.hpp:86-103):
+ * ex = (f_add_ex + g) + f_rescale_ex * ((2^ex_bits * ip1 + ip2) + kb), evaluated in that
+ * order in fp32 (2^7 * ip1 is exact). */
+float cora_oracle_ex_split(const cora_oracle_index *ix, uint64_t gid, float ip1, float ip2,
+                           float g, float kb) {
+    const float *f = ix->ex_factors + gid * 2;
+    const float t = ((128.0f * ip1) + ip2) + kb;
+    return (f[0] + g) + (f[1] * t);
 }
 
 static void vector_bits(const cora_oracle_index *ix, uint64_t start, uint64_t n, uint64_t i,
@@ -236,14 +257,17 @@ static float exact_refine(const cora_oracle_index *ix, const float *qraw, uint64
     return (float)acc;
 }
 
+/* Refinement of vector i of the cluster at `start` (size n); ip1 is the scan's estimate. */
 static float refine(const cora_oracle_index *ix, const float *qraw, const float *x,
-                    uint64_t start, uint64_t n, uint64_t i, float g, float kb) {
+                    uint64_t start, uint64_t n, uint64_t i, float ip1, float g, float kb) {
     uint32_t bits[128];
     const uint64_t D = ix->padded_dim, LC = D * ix->ex_bits / 8, gid = start + i;
+    const uint8_t *code = ix->long_codes + gid * LC;
     if (ix->exact_base) return exact_refine(ix, qraw, gid);
+    if (!ix->refine_full_code)
+        return cora_oracle_ex_split(ix, gid, ip1, cora_oracle_ip_ex(x, code, D), g, kb);
     vector_bits(ix, start, n, i, bits);
-    const float ipt = cora_oracle_ip_total(x, bits, ix->long_codes + gid * LC, D);
-    return cora_oracle_ex(ix, gid, ipt, g, kb);
+    return cora_oracle_ex(ix, gid, cora_oracle_ip_total(x, bits, code, D), g, kb);
 }
 
 static void push(entry_t **v, uint64_t *n, uint64_t *cap, entry_t e) {
@@ -330,7 +354,7 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
             const uint64_t ns = take_all[r] ? npair : keep;
             for (uint64_t i = 0; i < ns; ++i) {
                 const uint32_t gid = pair[i].gid;
-                const float ex = refine(ix, q + n * ix->dim, x, s, nc, gid - s, g, kb);
+                const float ex = refine(ix, q + n * ix->dim, x, s, nc, gid - s, pair[i].ip1, g, kb);
                 entry_t e = {((uint64_t)ord_f32(ex) << 32) | ix->ids[gid], ex, pair[i].ip1, gid,
                              (uint32_t)r};
                 push(&res, &nres, &cres, e);
@@ -373,7 +397,7 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
                     if (key <= bound[r]) continue;
                 }
                 const uint32_t gid = (uint32_t)(s + i);
-                const float ex = refine(ix, q + n * ix->dim, x, s, nc, i, g, kb);
+                const float ex = refine(ix, q + n * ix->dim, x, s, nc, i, ip1, g, kb);
                 entry_t e = {((uint64_t)ord_f32(ex) << 32) | ix->ids[gid], ex, ip1, gid,
                              (uint32_t)r};
                 push(&res, &nres, &cres, e);

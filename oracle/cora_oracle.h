@@ -25,10 +25,16 @@
  *  - ip_int is exact integer arithmetic; ip1 = width * (float)ip_int;
  *  - low / ex follow the reference's expression trees in fp32, round-to-nearest, with no
  *    contraction (built with -ffp-contract=off);
- *  - the refinement inner product of the full 8-bit code, ipT = <q', 128 b + u>, is one
- *    fp64 accumulation in ascending dimension order (exact products), rounded once; the
- *    reference adds 128 * ip1 from its scan instead, which with the 8-bit query planes
- *    loses accuracy (ip1's quantisation error is multiplied by 128);
+ *  - refinement follows the reference's expression (cpu_refinement.cpp:183-191,
+ *    estimator.hpp:86-103): ex = (f_add_ex + g) + f_rescale_ex * ((2^ex_bits * ip1 + ip2)
+ *    + kb), with ip1 = width * ip_int the scan's integer estimate of <q', b> (the exact_ip
+ *    the reference's producers publish, filter_kernels.cuh:106) and ip2 = <q', u> over the
+ *    decoded ex code u, one fp64 accumulation in ascending dimension order (exact
+ *    products) rounded once (the reference sums in fp32 with AVX FMAs: ip2 agrees within
+ *    1e-4 relative, tests/test_oracle.py);
+ *  - opt-in (refine_full_code = 1): the full 8-bit code inner product ipT = <q', 128 b + u>
+ *    in place of 128 * ip1 + ip2, one fp64 accumulation rounded once; it removes ip1's
+ *    query-quantisation error, which the reference form multiplies by 128;
  *  - coarse probes are ordered by (g_add, cluster id); results by (ex, original id);
  *  - thresholds are static per phase (seeded T0, then T1 from the vanguard seeds), so the
  *    candidate set {v : low(v) < T} is a pure function of the inputs. The first
@@ -67,6 +73,8 @@ typedef struct {
      * dropped (value NaN: never a result, never below a threshold; still counted). */
     const float *exact_base;
     uint64_t exact_rows, exact_dim, exact_stride;
+    /* 0 (default): the reference's 2^ex * ip1 + ip2 refinement; 1: the full-code ipT. */
+    int refine_full_code;
 } cora_oracle_index;
 
 #define CORA_ORACLE_VANGUARD_MIN_KEEP 20
@@ -86,6 +94,11 @@ float cora_oracle_ip_total(const float *qr, const uint32_t *bits, const uint8_t 
                            uint64_t D);
 float cora_oracle_ex(const cora_oracle_index *ix, uint64_t gid, float ip_total, float g,
                      float kb);
+/* ip2 = <q', u>, u the decoded 7-bit ex code (what ip64_fxu7_avx computes). */
+float cora_oracle_ip_ex(const float *qr, const uint8_t *code, uint64_t D);
+/* The reference's refinement: (f_add_ex + g) + f_rescale_ex * ((128 * ip1 + ip2) + kb). */
+float cora_oracle_ex_split(const cora_oracle_index *ix, uint64_t gid, float ip1, float ip2,
+                           float g, float kb);
 
 /* Full search. Outputs are row-major nq x k. thresholds0 may be NULL (FLT_MAX).
  * Optional outputs (NULL to skip): cand_count[nq] (= seeds + main candidates),

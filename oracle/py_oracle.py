@@ -164,7 +164,8 @@ class _Index(C.Structure):
                 ("long_codes", C.c_void_p), ("ex_factors", C.c_void_p),
                 ("ids", C.c_void_p), ("cluster_sizes", C.c_void_p),
                 ("exact_base", C.c_void_p), ("exact_rows", C.c_uint64),
-                ("exact_dim", C.c_uint64), ("exact_stride", C.c_uint64)]
+                ("exact_dim", C.c_uint64), ("exact_stride", C.c_uint64),
+                ("refine_full_code", C.c_int)]
 
 
 _lib = None
@@ -191,9 +192,16 @@ def lib():
                                              _f32p, _f32p, _f32p, _i32p, _u32p]
         L.cora_oracle_probe.argtypes = [C.POINTER(_Index), _f32p, C.c_uint64, C.c_uint64,
                                         _i32p, _f32p]
+        L.cora_oracle_ip_ex.restype = C.c_float
+        L.cora_oracle_ip_ex.argtypes = [_f32p, _u8p, C.c_uint64]
+        L.cora_oracle_ex_split.restype = C.c_float
+        L.cora_oracle_ex_split.argtypes = [C.POINTER(_Index), C.c_uint64, C.c_float, C.c_float,
+                                           C.c_float, C.c_float]
         L.cora_oracle_ip_total.restype = C.c_float
         L.cora_oracle_ip_total.argtypes = [_f32p, _u32p, _u8p, C.c_uint64]
         L.cora_oracle_decode_ex7.argtypes = [_u8p, C.c_uint64, _u8p]
+        L.cora_oracle_ip_int.restype = C.c_int32
+        L.cora_oracle_ip_int.argtypes = [C.POINTER(_Index), C.c_uint64, _u32p]
         L.cora_oracle_centroid_dist.restype = C.c_float
         L.cora_oracle_centroid_dist.argtypes = [_f32p, _f32p, C.c_uint64]
         _lib = L
@@ -208,9 +216,10 @@ class OracleIndex:
     """Holds SearchData-layout arrays (contiguous, right dtypes) for the C oracle.
     exact_base: optional float32 (rows, dim) base vectors indexed by original id; when set,
     candidates are refined with exact squared L2 distances (HybridIndex::enable_exact_refine,
-    hybrid.cuh:171-178)."""
+    hybrid.cuh:171-178). full_code: refine with the full 8-bit code inner product instead
+    of the reference's 128 * ip1 + ip2 (cora_oracle.h)."""
 
-    def __init__(self, sd: dict, exact_base=None):
+    def __init__(self, sd: dict, exact_base=None, full_code=False):
         self.sd = {
             "centroids": np.ascontiguousarray(sd["centroids"], np.float32),
             "rotator": np.ascontiguousarray(sd["rotator"], np.float32),
@@ -227,8 +236,16 @@ class OracleIndex:
         self.c = _Index(self.num, self.dim, self.D, self.nlist, self.ex_bits,
                         _ptr(s["centroids"]), _ptr(s["rotator"]), _ptr(s["short_data"]),
                         _ptr(s["short_factors"]), _ptr(s["long_codes"]), _ptr(s["ex_factors"]),
-                        _ptr(s["ids"]), _ptr(s["sizes"]), None, 0, 0, 0)
+                        _ptr(s["ids"]), _ptr(s["sizes"]), None, 0, 0, 0, int(bool(full_code)))
         self.set_exact_base(exact_base)
+
+    @property
+    def full_code(self) -> bool:
+        return bool(self.c.refine_full_code)
+
+    @full_code.setter
+    def full_code(self, on):
+        self.c.refine_full_code = int(bool(on))
 
     def set_exact_base(self, base):
         """Exact refinement against `base` (float32 (rows, dim), row = original id), or off."""
@@ -308,8 +325,8 @@ class OracleIndex:
         return ids, g
 
 
-def oracle_from_file(path) -> OracleIndex:
-    return OracleIndex(search_data(read_ivf_file(path)))
+def oracle_from_file(path, full_code=False) -> OracleIndex:
+    return OracleIndex(search_data(read_ivf_file(path)), full_code=full_code)
 
 
 # --------------------------------------------------------------------------------------
@@ -488,8 +505,9 @@ def smallest_keys_per_query(recv, world, nq, k):
 
 
 class OracleShard:
-    def __init__(self, sd_shard: dict, world: int, vanguard=5, thresholds=None, threads=None):
-        self.o = OracleIndex(sd_shard)
+    def __init__(self, sd_shard: dict, world: int, vanguard=5, thresholds=None, threads=None,
+                 full_code=False):
+        self.o = OracleIndex(sd_shard, full_code=full_code)
         self.world, self.vanguard, self.T0, self.threads = world, vanguard, thresholds, threads
 
     def buffers(self, nq, k):

@@ -14,9 +14,14 @@ oracle/_ref/libcora_ref_*.so, i.e. the reference's own CPU code). For each fixtu
    reference SearchData adapter, its 7-bit ex-code inner products (ip64_fxu7_avx) on sampled
    (query, vector) pairs, and the reference CPU search (rabitq_cpu loop) result ids;
 5. records exact ground truth (fp64, ties by id) and the oracle's search outputs for a grid
-   of (topk, nprobe, vanguard).
+   of (topk, nprobe, vanguard), in the default refinement form (the reference's
+   128 * ip1 + ip2: keys dist_/ids_/cand_/t1_/probe_/probeg_) and in the full-code form
+   (keys with a "T" suffix on the prefix: distT_/idsT_/candT_/t1T_).
 
-Usage: python tests/golden/make_golden.py  (writes tests/golden/*.index, *.npz)
+Usage: python tests/golden/make_golden.py [names]   (writes tests/golden/*.index, *.npz)
+       python tests/golden/make_golden.py --outputs-only [names]
+           recomputes step 5 only, from the committed index files (the reference builder
+           draws a fresh random rotation on every run, so rebuilding changes the indexes)
 """
 from __future__ import annotations
 
@@ -71,6 +76,34 @@ def sha(a) -> str:
     return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
 
 
+def oracle_outputs(oracle, queries, grid, out):
+    """The oracle's search outputs over the grid, in both refinement forms, into `out`."""
+    for full_code, sfx in ((False, ""), (True, "T")):
+        oracle.full_code = full_code
+        for k, nprobe, van in grid:
+            k, nprobe, van = int(k), int(nprobe), int(van)
+            det = oracle.search(queries, k, nprobe, vanguard=van, with_details=True)
+            tag = f"k{k}_np{nprobe}_v{van}"
+            out[f"dist{sfx}_{tag}"] = det["dist"]
+            out[f"ids{sfx}_{tag}"] = det["ids"]
+            out[f"cand{sfx}_{tag}"] = det["cand_count"]
+            out[f"t1{sfx}_{tag}"] = det["thresholds1"]
+            if not full_code:
+                out[f"probe_{tag}"] = det["probe_ids"]
+                out[f"probeg_{tag}"] = det["probe_g"]
+    oracle.full_code = False
+
+
+def refresh_outputs(name):
+    """Recompute the oracle outputs of a committed fixture in place (index unchanged)."""
+    with np.load(HERE / f"{name}.npz") as z:
+        out = {k: z[k] for k in z.files}
+    oracle = po.oracle_from_file(HERE / f"{name}.index")
+    oracle_outputs(oracle, out["queries"], out["grid"], out)
+    np.savez_compressed(HERE / f"{name}.npz", **out)
+    print(f"{name}: outputs refreshed")
+
+
 def build_fixture(name):
     n, dim, nlist, nq, sigma, qnoise, seed, grid = FIXTURES[name]
     centres, base, queries = make_data(n, dim, nlist, nq, sigma, qnoise, seed)
@@ -106,16 +139,7 @@ def build_fixture(name):
         key = f"refcpu_k{k}_np{nprobe}"
         if key not in out:
             out[key] = ref.search(queries, k, nprobe, threads=4)
-    # oracle outputs
-    for k, nprobe, van in grid:
-        det = oracle.search(queries, k, nprobe, vanguard=van, with_details=True)
-        tag = f"k{k}_np{nprobe}_v{van}"
-        out[f"dist_{tag}"] = det["dist"]
-        out[f"ids_{tag}"] = det["ids"]
-        out[f"cand_{tag}"] = det["cand_count"]
-        out[f"t1_{tag}"] = det["thresholds1"]
-        out[f"probe_{tag}"] = det["probe_ids"]
-        out[f"probeg_{tag}"] = det["probe_g"]
+    oracle_outputs(oracle, queries, grid, out)
     prep = oracle.query_prep(qr)
     out["qr"] = qr
     out["planes"] = prep["planes"]
@@ -129,10 +153,15 @@ def build_fixture(name):
 
 
 def main():
+    args = sys.argv[1:]
+    if args and args[0] == "--outputs-only":
+        for name in (args[1:] or FIXTURES):
+            refresh_outputs(name)
+        return
     if not po.ref_available():
         sys.exit("oracle/_ref is missing: build it with `make -C oracle ref` where the "
                  "reference tree exists")
-    for name in (sys.argv[1:] or FIXTURES):
+    for name in (args or FIXTURES):
         build_fixture(name)
 
 

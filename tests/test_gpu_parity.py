@@ -21,9 +21,11 @@ def cb():
     return coraanns_b200
 
 
-def _engine(cb, path=None, sd=None, nq=1, k=10, nprobe=1, vanguard=5, mode="lows"):
+def _engine(cb, path=None, sd=None, nq=1, k=10, nprobe=1, vanguard=5, mode="lows",
+            full_code=False):
     e = cb.HybridIndex(0)
     e.set_vanguard_size(vanguard)
+    e.set_refine_full_code(full_code)
     if mode == "rescan":
         e.set_vanguard_lows_budget(0)
     if mode == "blocksel":  # every pair / query through the block-wide selections
@@ -59,19 +61,25 @@ def _check_stages(e, q, k, nprobe, ref, tag):
         f"{tag}: candidate counts"
 
 
-@pytest.mark.parametrize("loader,mode", [("file", "lows"), ("raw", "lows"), ("file", "rescan"),
-                                         ("file", "blocksel"), ("raw", "tightsel")])
+@pytest.mark.parametrize("loader,mode,full_code", [
+    ("file", "lows", False), ("raw", "lows", False), ("file", "rescan", False),
+    ("file", "blocksel", False), ("raw", "tightsel", False),
+    ("file", "lows", True), ("raw", "rescan", True)])
 @pytest.mark.parametrize("name", GOLDEN_NAMES)
-def test_golden_parity(cb, golden, name, loader, mode):
+def test_golden_parity(cb, golden, name, loader, mode, full_code):
+    """Every stage and the results against the committed oracle outputs, in the default
+    (reference) refinement form and in the full-code form."""
     path, z = golden[name]
     q = z["queries"]
     grid = z["grid"]
+    sfx = "T" if full_code else ""
     kmax, npmax = int(grid[:, 0].max()), int(grid[:, 1].max())
     if loader == "file":
-        e = _engine(cb, path=path, nq=len(q), k=kmax, nprobe=npmax, mode=mode)
+        e = _engine(cb, path=path, nq=len(q), k=kmax, nprobe=npmax, mode=mode,
+                    full_code=full_code)
     else:
         e = _engine(cb, sd=po.search_data(po.read_ivf_file(path)), nq=len(q), k=kmax,
-                    nprobe=npmax, mode=mode)
+                    nprobe=npmax, mode=mode, full_code=full_code)
     assert e.get_vanguard_mode() == (0 if mode == "rescan" else 1)
     for k, nprobe, van in grid:
         k, nprobe, van = int(k), int(nprobe), int(van)
@@ -82,11 +90,11 @@ def test_golden_parity(cb, golden, name, loader, mode):
         key = f"k{k}_np{nprobe}_v{van}"
         ref = dict(qr=z["qr"], scalars=z["scalars"], planes=z["planes"],
                    probe_ids=z[f"probe_{key}"], probe_g=z[f"probeg_{key}"],
-                   thresholds1=z[f"t1_{key}"], cand_count=z[f"cand_{key}"])
+                   thresholds1=z[f"t1{sfx}_{key}"], cand_count=z[f"cand{sfx}_{key}"])
         _check_stages(e, q, k, nprobe, ref, tag)
-        assert np.array_equal(i, z[f"ids_{key}"]), f"{tag}: ids"
-        assert d.tobytes() == z[f"dist_{key}"].tobytes(), f"{tag}: distances"
-        assert e.get_last_submitted_count() == int(z[f"cand_{key}"].sum())
+        assert np.array_equal(i, z[f"ids{sfx}_{key}"]), f"{tag}: ids"
+        assert d.tobytes() == z[f"dist{sfx}_{key}"].tobytes(), f"{tag}: distances"
+        assert e.get_last_submitted_count() == int(z[f"cand{sfx}_{key}"].sum())
     e.close()
 
 
@@ -101,23 +109,27 @@ def _synthetic(n, dim, nlist, nq, seed, sigma=0.25):
     return sd, q
 
 
-@pytest.mark.parametrize("n,dim,nlist,nq,k,nprobe,van,mode", [
-    (200_000, 96, 256, 256, 10, 16, 5, "lows"),
-    (200_000, 96, 256, 256, 10, 16, 5, "rescan"),
-    (200_000, 96, 256, 256, 10, 16, 5, "tightsel"),
-    (200_000, 96, 256, 64, 100, 24, 5, "lows"),
-    (60_000, 768, 64, 48, 10, 8, 5, "lows"),
-    (60_000, 768, 64, 48, 10, 8, 3, "rescan"),
-    (100_000, 128, 128, 300, 10, 32, 0, "lows"),
+@pytest.mark.parametrize("n,dim,nlist,nq,k,nprobe,van,mode,full_code", [
+    (200_000, 96, 256, 256, 10, 16, 5, "lows", False),
+    (200_000, 96, 256, 256, 10, 16, 5, "rescan", False),
+    (200_000, 96, 256, 256, 10, 16, 5, "tightsel", False),
+    (200_000, 96, 256, 64, 100, 24, 5, "lows", False),
+    (200_000, 96, 256, 64, 100, 24, 5, "lows", True),
+    (60_000, 768, 64, 48, 10, 8, 5, "lows", False),
+    (60_000, 768, 64, 48, 10, 8, 3, "rescan", False),
+    (60_000, 768, 64, 48, 10, 8, 5, "lows", True),
+    (100_000, 128, 128, 300, 10, 32, 0, "lows", False),
 ])
-def test_live_oracle_parity_larger(cb, n, dim, nlist, nq, k, nprobe, van, mode):
+def test_live_oracle_parity_larger(cb, n, dim, nlist, nq, k, nprobe, van, mode, full_code):
     """Bit-exact parity with the oracle on indexes larger than the fixtures (more tiles per
-    cluster, more pairs per item, D = 768), in both vanguard modes."""
+    cluster, more pairs per item, D = 768), in both vanguard modes and both refinement
+    forms."""
     sd, q = _synthetic(n, dim, nlist, nq, seed=n + dim)
-    o = po.OracleIndex(sd)
+    o = po.OracleIndex(sd, full_code=full_code)
     ref = o.search(q, k, nprobe, vanguard=van, with_details=True,
                    cand_cap=0)
-    e = _engine(cb, sd=sd, nq=nq, k=k, nprobe=nprobe, vanguard=van, mode=mode)
+    e = _engine(cb, sd=sd, nq=nq, k=k, nprobe=nprobe, vanguard=van, mode=mode,
+                full_code=full_code)
     e.reset_buffer(q)
     d, i = e.search(q, k, nprobe)
     _check_stages(e, q, k, nprobe, ref, f"synthetic n{n} d{dim}")
@@ -237,6 +249,15 @@ def test_search_graph_replay_matches_eager(cb, golden):
         d, i = e.search(q, 10, 8)
         out.append((d.tobytes(), i.tobytes()))
         e.set_tuning("warp_select_limit", 256)
+        e.set_refine_full_code(True)  # a configuration change: the graph is rebuilt
+        e.reset_buffer(q)
+        d, i = e.search(q, 10, 8)
+        out.append((d.tobytes(), i.tobytes()))
+        e.set_refine_full_code(False)
+        e.reset_buffer(q)
+        d, i = e.search(q, 10, 8)
+        out.append((d.tobytes(), i.tobytes()))
         results[graphs] = out
+    assert results[1][-2] != results[1][-1]  # the two forms rank differently here
     assert results[1] == results[0]
     e.close()
