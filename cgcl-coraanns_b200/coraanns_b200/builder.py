@@ -105,20 +105,31 @@ def _words(bits: torch.Tensor) -> torch.Tensor:
 
 
 def build_index(data, centroids, assign, seed: int = 7, device="cpu", chunk: int = 1 << 20,
-                keep_bits: bool = False) -> dict:
+                keep_bits: bool = False, rotator=None, rotated_centroids=None,
+                t_const: float | None = None) -> dict:
     """Build an 8-bit (1 + 7 ex bits) L2 index. data n x dim, centroids nlist x dim,
     assign n cluster ids. Returns the adapter layout dict (see oracle/py_oracle.py keys),
-    plus 'bits' (n x D bool, cluster order) when keep_bits."""
+    plus 'bits' (n x D bool, cluster order) when keep_bits.
+
+    The random pieces are seeded from `seed`; to quantise against another builder's choices
+    (e.g. the reference's, which draws them unseeded) pass them in: `rotator` (dim x D),
+    `rotated_centroids` (nlist x D, used as given) and `t_const` (the ex-code rescale
+    constant of the "faster" mode)."""
     dev = torch.device(device)
     data = torch.as_tensor(np.asarray(data) if not torch.is_tensor(data) else data)
     n, dim = data.shape
     D = padded_dim(dim)
     nlist = int(centroids.shape[0])
-    P = torch.as_tensor(random_rotation(dim, seed), device=dev)
-    cent = torch.as_tensor(np.asarray(centroids, np.float32) if not torch.is_tensor(centroids)
-                           else centroids, device=dev).float()
-    crot = (cent.double() @ P.double()).float()
-    t_const = const_scaling_factor(D, 7, seed + 1)
+    P = torch.as_tensor(np.asarray(rotator, np.float32) if rotator is not None
+                        else random_rotation(dim, seed), device=dev)
+    if rotated_centroids is not None:
+        crot = torch.as_tensor(np.asarray(rotated_centroids, np.float32), device=dev)
+    else:
+        cent = torch.as_tensor(np.asarray(centroids, np.float32) if not torch.is_tensor(centroids)
+                               else centroids, device=dev).float()
+        crot = (cent.double() @ P.double()).float()
+    if t_const is None:
+        t_const = const_scaling_factor(D, 7, seed + 1)
     a = torch.as_tensor(np.asarray(assign) if not torch.is_tensor(assign) else assign,
                         device=dev).long()
     order = torch.argsort(a, stable=True)
