@@ -422,6 +422,7 @@ class HybridIndex:
             "scalars": (6, np.float32, (nq, 4)),
             "cand_gids": (7, np.uint32, (nq, self.candidate_capacity())),
             "approx": (8, np.float32, (nq, (info["nlist"] + 3) // 4 * 4)),
+            "lut": (9, np.uint16, (nq, D // 4, 16)),
         }[what]
         out = np.empty(spec[2], spec[1])
         _check(_lib.cora_debug_copy(self._h, spec[0], _ptr(out), out.nbytes))

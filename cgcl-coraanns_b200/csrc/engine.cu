@@ -167,7 +167,7 @@ inline void launch_probe_gemm(const float *qr, const float *qnorm2, uint64_t nq,
 // rotate_prep_kernel with kRotQueriesWide queries per CTA when D <= 128, else kRotQueries.
 inline void launch_rotate_prep(const float *raw_q, uint64_t nq, uint64_t dim, uint64_t D, int W4,
                                const double *rotator, float c_b, float *qr, QueryScalars *scal,
-                               uint32_t *planes, float *qnorm2, int2 *qrange, cudaStream_t st) {
+                               uint32_t *planes, float *qnorm2, float *ipm, cudaStream_t st) {
     const bool wide = D <= 128;
     const int qpc = wide ? kRotQueriesWide : kRotQueries;
     const size_t sm = (size_t)qpc * (2 * dim + D) * 4;
@@ -177,12 +177,12 @@ inline void launch_rotate_prep(const float *raw_q, uint64_t nq, uint64_t dim, ui
         CUDA_TRY(cudaFuncSetAttribute(rotate_prep_kernel<kRotQueriesWide>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
         rotate_prep_kernel<kRotQueriesWide><<<grid, 256, sm, st>>>(
-            raw_q, inq, idim, iD, W4, rotator, c_b, qr, scal, planes, qnorm2, qrange);
+            raw_q, inq, idim, iD, W4, rotator, c_b, qr, scal, planes, qnorm2, ipm);
     } else {
         CUDA_TRY(cudaFuncSetAttribute(rotate_prep_kernel<kRotQueries>,
                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
         rotate_prep_kernel<kRotQueries><<<grid, 256, sm, st>>>(
-            raw_q, inq, idim, iD, W4, rotator, c_b, qr, scal, planes, qnorm2, qrange);
+            raw_q, inq, idim, iD, W4, rotator, c_b, qr, scal, planes, qnorm2, ipm);
     }
     CUDA_TRY(cudaGetLastError());
 }
@@ -280,7 +280,10 @@ struct Engine {
     bool cross_query_reuse = true, cpu_secondary_filter = true;
     // refinement form: false (default) the reference's 128 ip1 + ip2, true <q', 128 b + u>
     bool refine_full_code = false;
-    int ip_kernel_type = 0;
+    // estimator of the scan (hybrid.cuh:12 KernelType): 0 Lut4Bit (the fp16-LUT estimator,
+    // the reference's default), 1 Bitwise (the integer estimator, this engine's default)
+    int ip_kernel_type = 1;
+    bool lut_mode() const { return ip_kernel_type == 0; }
     // Upper bound on the HBM buffer holding the vanguard pairs' lower bounds; larger
     // worst cases fall back to rescanning the vanguard clusters.
     uint64_t lows_budget = 16ull << 30;
@@ -292,7 +295,8 @@ struct Engine {
     uint64_t ws_q = 0, ws_k = 0, ws_np = 0, ws_vg = 0, cap = 0;
     DevBuf<float> raw_q, qr, qnorm2, gmat, cmin, probe_g, T0, T1, Tcap, out_d;
     DevBuf<QueryScalars> scal;
-    DevBuf<int2> qrange;
+    DevBuf<float> ipm;   // per query: bound on |fl(ip1 + k1)| for the pruning test
+    DevBuf<__half> lut;  // per query: LUT estimator tables (D / 4 groups x 16)
     DevBuf<uint32_t> planes, cand_cnt, seed_cnt, pair_cnt, pair_off, pair_cur, item_off, pairs,
         n_items, out_i;
     DevBuf<int> probe_ids, item_counter, err;
@@ -330,11 +334,12 @@ struct Engine {
         uint32_t *d_oi = nullptr;
         cudaStream_t st = nullptr;
         int wsl = 0, twl = 0;
-        bool reuse = false, full_code = false;
+        bool reuse = false, full_code = false, lut = false;
         bool same(const GraphKey &o) const {
             return d_q == o.d_q && nq == o.nq && k == o.k && np == o.np && ws_gen == o.ws_gen &&
                    vanguard == o.vanguard && d_od == o.d_od && d_oi == o.d_oi && st == o.st &&
-                   wsl == o.wsl && twl == o.twl && reuse == o.reuse && full_code == o.full_code;
+                   wsl == o.wsl && twl == o.twl && reuse == o.reuse &&
+                   full_code == o.full_code && lut == o.lut;
         }
     };
     GraphKey graph_key;
@@ -626,7 +631,8 @@ struct Engine {
         raw_q.alloc(max_q * dim);
         qr.alloc(max_q * D);
         scal.alloc(max_q);
-        qrange.alloc(max_q);
+        ipm.alloc(max_q);
+        lut.alloc(max_q * 4 * D);
         planes.alloc(max_q * 8 * W4);
         gmat.alloc(max_q * approx_ld(nlist));
         cmin.alloc(max_q * chunk_stride(static_cast<int>(nlist)));
@@ -681,7 +687,8 @@ struct Engine {
         for (auto *b : {&raw_q, &qr, &qnorm2, &gmat, &cmin, &probe_g, &T0, &T1, &Tcap, &out_d})
             b->release();
         scal.release();
-        qrange.release();
+        ipm.release();
+        lut.release();
         for (auto *b : {&planes, &cand_cnt, &seed_cnt, &pair_cnt, &pair_off, &pair_cur, &item_off,
                         &pairs, &n_items, &out_i})
             b->release();
@@ -879,51 +886,62 @@ void Engine::repack_scan_planes(const uint32_t *d_short, const float *d_fac) {
 // search pipeline
 // ------------------------------------------------------------------------------------
 namespace {
-template <int G16>
+// Query words per pair in the scan kernels' shared memory (bytes): integer estimator 8 W4
+// words, LUT estimator kLutFloats table entries.
+template <int G16, bool kLut>
+constexpr size_t query_block_bytes() {
+    return kLut ? (size_t)ScanShape<G16>::kLutFloats * 4 : (size_t)8 * ScanShape<G16>::W4 * 4;
+}
+template <int G16, bool kLut>
 size_t rescan_smem(int sort_n) {
     using Sh = ScanShape<G16>;
-    return 2 * Sh::kStageEntries * 16 + 8 * Sh::W4 * 4 + (size_t)sort_n * 8;
+    return 2 * Sh::kStageEntries * 16 + query_block_bytes<G16, kLut>() + (size_t)sort_n * 8;
 }
-template <int G16>
+template <int G16, bool kLut>
 size_t scan_smem() {
     using Sh = ScanShape<G16>;
+    const int ppi = kLut ? Sh::kLutPairs : kMaxPairsPerItem;
     return (size_t)Sh::kStages * Sh::kScanStageEntries * 16 +
-           (size_t)kMaxPairsPerItem * 8 * Sh::W4 * 4;
+           (size_t)ppi * query_block_bytes<G16, kLut>();
 }
 
-template <int G16, bool kLows>
+template <int G16, bool kLows, bool kLut>
 void launch_grouped(const ScanLaunch &L) {
-    const size_t sm = scan_smem<G16>();
-    CUDA_TRY(cudaFuncSetAttribute(scan_kernel<G16, kLows>,
-                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    const size_t sm = scan_smem<G16, kLut>();
+    auto *kern = scan_kernel<G16, kLows, kLut>;
+    CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
     int per_sm = 0;
-    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, scan_kernel<G16, kLows>,
-                                                           kScanThreads, sm));
+    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kScanThreads, sm));
     const int grid = std::max(1, per_sm) * L.num_sms;
-    scan_kernel<G16, kLows><<<grid, kScanThreads, sm, L.st>>>(L.ix, L.sv, L.items, L.n_items,
-                                                            L.pairs, L.item_counter);
+    kern<<<grid, kScanThreads, sm, L.st>>>(L.ix, L.sv, L.items, L.n_items, L.pairs,
+                                           L.item_counter);
     CUDA_TRY(cudaGetLastError());
 }
 
-template <int G16>
+template <int G16, bool kLut>
 void launch_scan(const ScanLaunch &L, ScanPhase phase) {
     if (phase == ScanPhase::kRescanVanguard) {
-        const size_t sm = rescan_smem<G16>(L.rescan_sort_n);
-        CUDA_TRY(cudaFuncSetAttribute(vanguard_rescan_kernel<G16>,
-                                      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
-        vanguard_rescan_kernel<G16><<<static_cast<unsigned>(L.n_van), kScanThreads, sm, L.st>>>(
-            L.ix, L.sv, L.rescan_sort_n, L.owned);
+        const size_t sm = rescan_smem<G16, kLut>(L.rescan_sort_n);
+        auto *kern = vanguard_rescan_kernel<G16, kLut>;
+        CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+        kern<<<static_cast<unsigned>(L.n_van), kScanThreads, sm, L.st>>>(L.ix, L.sv,
+                                                                         L.rescan_sort_n, L.owned);
         CUDA_TRY(cudaGetLastError());
     } else if (phase == ScanPhase::kWriteLows) {
-        launch_grouped<G16, true>(L);
+        launch_grouped<G16, true, kLut>(L);
     } else {
-        launch_grouped<G16, false>(L);
+        launch_grouped<G16, false, kLut>(L);
     }
 }
 
-void dispatch_scan(int G16, const ScanLaunch &L, ScanPhase phase) {
-#define CORA_SCAN_CASE(G) \
-    case G: launch_scan<G>(L, phase); break;
+void dispatch_scan(int G16, bool lut, const ScanLaunch &L, ScanPhase phase) {
+#define CORA_SCAN_CASE(G)                    \
+    case G:                                  \
+        if (lut)                             \
+            launch_scan<G, true>(L, phase);  \
+        else                                 \
+            launch_scan<G, false>(L, phase); \
+        break;
     switch (G16) {
         CORA_SCAN_CASE(1)
         CORA_SCAN_CASE(2)
@@ -937,6 +955,9 @@ void dispatch_scan(int G16, const ScanLaunch &L, ScanPhase phase) {
     }
 #undef CORA_SCAN_CASE
 }
+
+// Pairs per grouped item with the LUT estimator (ScanShape::kLutPairs).
+int lut_pairs_per_item(int G16) { return G16 == 1 ? 32 : (G16 == 2 ? 16 : 8); }
 }  // namespace
 
 IndexView Engine::index_view() const {
@@ -950,7 +971,8 @@ SearchView Engine::search_view() const {
     const uint64_t keep = std::max<uint64_t>(last_k, kVanguardMinKeep);
     return SearchView{static_cast<int>(last_nq), static_cast<int>(last_k), static_cast<int>(last_np),
                       static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
-                      last_dq, scal.p, qrange.p, planes.p, qr.p, probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p,
+                      last_dq, scal.p, ipm.p, planes.p, lut.p, lut_mode() ? 1 : 0, qr.p,
+                      probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p,
                       cand_cnt.p, seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n,
                       lows_top.p, err.p, warp_select_limit, topk_warp_limit,
                       refine_full_code ? 1 : 0};
@@ -980,6 +1002,7 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     key.twl = topk_warp_limit;
     key.reuse = cross_query_reuse;
     key.full_code = refine_full_code;
+    key.lut = lut_mode();
     if (!graph_exec || !graph_key.same(key)) {
         drop_graph();
         CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
@@ -1034,7 +1057,13 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
     {
         const float c_b = -static_cast<float>((1u << (ex_bits + 1)) - 1u) / 2.0f;
         launch_rotate_prep(d_q, nq, dim, D, W4, rotator.p, c_b, qr.p, scal.p, planes.p, qnorm2.p,
-                           qrange.p, st);
+                           ipm.p, st);
+        if (lut_mode()) {  // the LUT estimator's tables (and its pruning bound, over ipm)
+            lut_build_kernel<<<static_cast<unsigned>((nq + kLutWarps - 1) / kLutWarps),
+                               32 * kLutWarps, 0, st>>>(qr.p, scal.p, static_cast<int>(nq),
+                                                        static_cast<int>(D), lut.p, ipm.p);
+            CUDA_TRY(cudaGetLastError());
+        }
     }
     mark(1, st);
     // 2. coarse probing: approximate distances for every (query, centroid), then the exact
@@ -1065,9 +1094,9 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
     mark(4, st);
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter0, st));
     if (lows_mode)
-        dispatch_scan(G16, L, ScanPhase::kWriteLows);
+        dispatch_scan(G16, lut_mode(), L, ScanPhase::kWriteLows);
     else
-        dispatch_scan(G16, L, ScanPhase::kRescanVanguard);
+        dispatch_scan(G16, lut_mode(), L, ScanPhase::kRescanVanguard);
     mark(5, st);
     if (lows_mode) {
         const size_t sm = (size_t)next_pow2(static_cast<int>(keep)) * 8 + kSelectStage * 4;
@@ -1146,9 +1175,9 @@ void Engine::group_pairs(int r_lo, int r_hi, bool prune, cudaStream_t st) {
     CUDA_TRY(cudaMemsetAsync(pair_cnt.p, 0, nlist * 4, st));
     CUDA_TRY(cudaMemsetAsync(pair_cur.p, 0, nlist * 4, st));
     CUDA_TRY(cudaMemsetAsync(item_counter.p, 0, 4, st));
-    const int ppi = cross_query_reuse ? kMaxPairsPerItem : 1;
+    const int ppi = !cross_query_reuse ? 1 : (lut_mode() ? lut_pairs_per_item(G16) : kMaxPairsPerItem);
     PairPrune pp{};
-    if (prune) pp = PairPrune{cl_range.p, probe_g.p, qrange.p, scal.p, T1.p};
+    if (prune) pp = PairPrune{cl_range.p, probe_g.p, ipm.p, T1.p};
     count_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own, pp,
                                                pair_cnt.p);
     scan_pairs_kernel<<<1, 1024, 0, st>>>(pair_cnt.p, static_cast<int>(nlist), ppi, pair_off.p,
@@ -1187,7 +1216,7 @@ void Engine::enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uin
     //    filtered from their stored lows or rescanned, skipping their seeds in both cases.
     group_pairs(lows_mode ? iveff : 0, inp, true, st);
     mark(9, st);
-    dispatch_scan(G16, L, ScanPhase::kMain);
+    dispatch_scan(G16, lut_mode(), L, ScanPhase::kMain);
     mark(10, st);
     if (lows_mode) {
         CUDA_TRY(cudaMemsetAsync(filt_list.p, 0, 4, st));
@@ -1241,6 +1270,7 @@ void Engine::debug_copy(int what, void *out, uint64_t bytes) {
         case 5: copy(planes.p, nq * 8 * W4 * 4); break;
         case 6: copy(scal.p, nq * 16); break;
         case 8: copy(gmat.p, nq * approx_ld(nlist) * 4); break;
+        case 9: copy(lut.p, nq * 4 * D * 2); break;
         case 7: {
             if (bytes != nq * cap * 4) fail(CORA_EINVAL, "debug_copy: byte count does not match");
             std::vector<uint64_t> rec(nq * cap);
@@ -1773,7 +1803,7 @@ void cora_set_cpu_secondary_filter(cora_engine *engine, int enabled) {
     if (engine && engine->e) engine->e->cpu_secondary_filter = enabled != 0;
 }
 void cora_set_ip_kernel_type(cora_engine *engine, int kernel_type) {
-    if (engine && engine->e) engine->e->ip_kernel_type = kernel_type;
+    if (engine && engine->e) engine->e->ip_kernel_type = kernel_type == 0 ? 0 : 1;
 }
 int cora_get_ip_kernel_type(const cora_engine *engine) {
     return engine && engine->e ? engine->e->ip_kernel_type : 0;

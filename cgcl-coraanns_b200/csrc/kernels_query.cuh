@@ -3,12 +3,16 @@
 //  rotate_prep_kernel          q' = q * P, sumq / k1 / kb, 8-bit symmetric query bit-planes
 //                              (reference: src/search/hybrid.cu:436-458,
 //                               src/search/query_kernels.cuh:73-94,117-189)
+//  lut_build_kernel            fp16 lookup tables of the LUT estimator (reference:
+//                              src/search/query_kernels.cuh:199-221)
 //  guarded_select_warp_kernel  top-nprobe by (g_add, cluster id) from the tensor-core
 //  guarded_select_kernel       approximate distances (kernels_probe.cuh) plus an exact fp64
 //                              recompute of the error band (reference: g_add of
 //                              hybrid.cu:465-477 / query_kernels.cuh:10-64, selected by
 //                              raft::matrix::select_k, hybrid.cu:485-493)
 #pragma once
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace cora {
@@ -22,6 +26,16 @@ struct QueryScalars {  // per query, 16 bytes
     float width, k1, kb, sumq;
 };
 
+// The pruning test (range_at_least, kernels_scan.cuh) needs, per query, a bound M on the
+// magnitude of the scan's fl(ip1 + k1) over every possible 1-bit code. Integer estimator:
+// fl(fl(width * ip) + k1) is monotone in ip, so M is taken at the ends of the reachable
+// ip_int range [neg, pos] (the sums of the negative and of the positive qint).
+__device__ __forceinline__ float ip_term_bound(int pos, int neg, float width, float k1) {
+    const float hi = __fadd_rn(__fadd_rn(__fmul_rn(width, (float)pos), 0.0f), k1);
+    const float lo = __fadd_rn(__fadd_rn(__fmul_rn(width, (float)neg), 0.0f), k1);
+    return fmaxf(fabsf(hi), fabsf(lo));
+}
+
 // One CTA handles kQ queries, in kQ / 8 groups of 8 that split the CTA's threads. Each output
 // dim j of q' is an fp64 chain over the input dims in ascending order (fp32 x fp32 products
 // are exact in fp64, so the fused multiply-add rounds exactly like the oracle's add); the
@@ -32,7 +46,7 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
     const float *__restrict__ raw_q, int nq, int dim, int D, int W4,
     const double *__restrict__ rotator, float c_b, float *__restrict__ qr_out,
     QueryScalars *__restrict__ scal_out, uint32_t *__restrict__ planes_out,
-    float *__restrict__ qnorm2_out, int2 *__restrict__ qrange_out) {
+    float *__restrict__ qnorm2_out, float *__restrict__ ipm_out) {
     constexpr int kGroups = kQ / kRotQueries;
     extern __shared__ double smem_d[];
     double *sq = smem_d;                                        // [kQ][dim]
@@ -130,7 +144,55 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
         // [neg, pos] is the range of sum_i b_i qint_i over every 1-bit code (the scan's bound)
         pos = __reduce_add_sync(0xffffffffu, pos);
         neg = __reduce_add_sync(0xffffffffu, neg);
-        if (qrange_out && lane == 0) qrange_out[q] = make_int2(pos, neg);
+        if (ipm_out && lane == 0) ipm_out[q] = ip_term_bound(pos, neg, width, __fmul_rn(sf, -0.5f));
+    }
+}
+
+// ---- LUT estimator tables -----------------------------------------------------------
+// The reference's default estimator (KernelType::Lut4Bit) forms ip1 = <q', b> from fp16
+// tables: entry (g, p) of nibble group g (dims 4g .. 4g + 3) and 4-bit pattern p (bit 3 =
+// dim 4g, ..., bit 0 = dim 4g + 3) is half(s), s the fp32 sum, starting from 0, of the
+// selected q' in dimension order (query_kernels.cuh:199-221). Tables are stored as
+// lut[q][g][p], 16 halves (32 bytes) per group. One warp per query, 8 queries per CTA.
+//
+// The bound M of the pruning test: ip1 = acc0 + acc1 where acc0 / acc1 are fp32 sums of at
+// most D / 8 table entries each, so |ip1| <= A (1 + 2^-24)^(D / 4) <= A (1 + 2^-16) for
+// A = sum_g max_p |entry(g, p)| and D <= 1024; M = (A (1 + 2^-16) + |k1|) (1 + 2^-23) bounds
+// |fl(ip1 + k1)| (every step rounded upwards).
+constexpr int kLutWarps = 8;
+__global__ void __launch_bounds__(32 * kLutWarps) lut_build_kernel(
+    const float *__restrict__ qr, const QueryScalars *__restrict__ scal, int nq, int D,
+    __half *__restrict__ lut, float *__restrict__ ipm) {
+    const int lane = threadIdx.x & 31;
+    const int q = blockIdx.x * kLutWarps + (threadIdx.x >> 5);
+    if (q >= nq) return;  // whole warp
+    const float4 *x4 = reinterpret_cast<const float4 *>(qr + (size_t)q * D);
+    double A = 0.0;
+    for (int g = lane; g < D / 4; g += 32) {
+        const float4 v = __ldg(x4 + g);
+        __align__(16) __half h[16];
+        double hm = 0.0;
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+            float sum = 0.0f;
+            if (p & 8) sum = __fadd_rn(sum, v.x);
+            if (p & 4) sum = __fadd_rn(sum, v.y);
+            if (p & 2) sum = __fadd_rn(sum, v.z);
+            if (p & 1) sum = __fadd_rn(sum, v.w);
+            h[p] = __float2half_rn(sum);
+            hm = fmax(hm, fabs((double)__half2float(h[p])));
+        }
+        uint4 *dst = reinterpret_cast<uint4 *>(lut + ((size_t)q * (D / 4) + g) * 16);
+        dst[0] = *reinterpret_cast<const uint4 *>(h);
+        dst[1] = *reinterpret_cast<const uint4 *>(h + 8);
+        A = __dadd_ru(A, hm);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) A = __dadd_ru(A, __shfl_xor_sync(0xffffffffu, A, off));
+    if (lane == 0) {
+        const double grown = __dmul_ru(A, 1.0 + 0x1p-16);
+        const double m = __dmul_ru(__dadd_ru(grown, fabs((double)scal[q].k1)), 1.0 + 0x1p-23);
+        ipm[q] = __double2float_ru(m);
     }
 }
 

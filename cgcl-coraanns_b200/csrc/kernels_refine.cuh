@@ -85,28 +85,48 @@ __global__ void __launch_bounds__(256) build_refine_rows_kernel(
     }
 }
 
-// One 64-dim block of a refine row (v: its 64 codes c = 128 b + u, 4 per word, dimension
-// order) against the rotated query x (fp64, shared memory), continuing the fp64 chain `acc`
-// in ascending dimension order (every product is exact in fp64). Each byte becomes the
-// double c (or u = c & 127) exactly as (2^52 + c) - 2^52 from its bit pattern, so the loop
-// runs no conversion instructions.
-//   kSplit (the reference form): acc accumulates <x, u>, and ip accumulates
-//     sum_i b_i qint_i with dp4a over the code words' top bits and the query's qint bytes
-//     (qw: qint of dims 4t .. 4t + 3 as the signed bytes of word t), exact in int32;
-//   otherwise: acc accumulates <x, 128 b + u>.
-template <bool kSplit>
+// Refinement forms: the reference's expression with ip1 from the integer estimator (the
+// default) or from the LUT estimator (with the scan's estimator), or the full-code inner
+// product (opt-in).
+enum RefineForm : int { kRefineSplitInt = 0, kRefineSplitLut = 1, kRefineFullCode = 2 };
+
+// One 64-dim block (index blk) of a refine row (v: its 64 codes c = 128 b + u, 4 per word,
+// dimension order) against the rotated query x (fp64, shared memory), continuing the fp64
+// chain `acc` in ascending dimension order (every product is exact in fp64). Each byte
+// becomes the double c (or u = c & 127) exactly as (2^52 + c) - 2^52 from its bit pattern,
+// so the loop runs no conversion instructions.
+//   kRefineSplitInt: acc accumulates <x, u>, and ip accumulates sum_i b_i qint_i with dp4a
+//     over the code words' top bits and the query's qint bytes (qw: qint of dims 4t .. 4t + 3
+//     as the signed bytes of word t), exact in int32;
+//   kRefineSplitLut: acc accumulates <x, u>, and la0 / la1 the LUT estimator's sums: row
+//     word t (dims 4t .. 4t + 3) is nibble group t, whose pattern is the four code bits (dim
+//     4t at bit 3); even groups go to la0, odd ones to la1, in ascending order (the scan's
+//     order, ip_from_lut), from the fp32 tables T (16 per group);
+//   kRefineFullCode: acc accumulates <x, 128 b + u>.
+template <int kForm>
 __device__ __forceinline__ void block_code8_ip(const double *__restrict__ x,
                                                const uint32_t *__restrict__ qw,
-                                               const uint4 (&v)[4], double &acc, int &ip) {
+                                               const float *__restrict__ T, int blk,
+                                               const uint4 (&v)[4], double &acc, int &ip,
+                                               float &la0, float &la1) {
 #pragma unroll
     for (int t = 0; t < 4; ++t) {
         const uint32_t w4[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
-            const uint32_t w = kSplit ? (w4[h] & 0x7F7F7F7Fu) : w4[h];
-            if (kSplit)
+            const uint32_t w = kForm == kRefineFullCode ? w4[h] : (w4[h] & 0x7F7F7F7Fu);
+            if (kForm == kRefineSplitInt)
                 ip = __dp4a(static_cast<int>((w4[h] >> 7) & 0x01010101u),
-                            static_cast<int>(qw[4 * t + h]), ip);
+                            static_cast<int>(qw[16 * blk + 4 * t + h]), ip);
+            if (kForm == kRefineSplitLut) {
+                const uint32_t pat = ((w4[h] >> 4) & 8u) | ((w4[h] >> 13) & 4u) |
+                                     ((w4[h] >> 22) & 2u) | (w4[h] >> 31);
+                const float e = T[(16 * blk + 4 * t + h) * 16 + pat];
+                if (h & 1)
+                    la1 = __fadd_rn(la1, e);
+                else
+                    la0 = __fadd_rn(la0, e);
+            }
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const uint32_t c = __byte_perm(w, 0u, 0x4440u | i);
@@ -118,20 +138,45 @@ __device__ __forceinline__ void block_code8_ip(const double *__restrict__ x,
     }
 }
 
+// The refinement of one candidate row: the factor t of f_rescale_ex.
+template <int kForm>
+__device__ __forceinline__ float refine_row_term(const uint4 *__restrict__ row, int nblocks,
+                                                 const double *__restrict__ x,
+                                                 const uint32_t *__restrict__ qw,
+                                                 const float *__restrict__ T, float width,
+                                                 float kb) {
+    double acc = 0.0;
+    int ip = 0;
+    float la0 = 0.0f, la1 = 0.0f;
+    for (int blk = 0; blk < nblocks; ++blk) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) v[u] = __ldg(row + 4 * blk + u);
+        block_code8_ip<kForm>(x + 64 * blk, qw, T, blk, v, acc, ip, la0, la1);
+    }
+    if (kForm == kRefineFullCode) return __fadd_rn(__double2float_rn(acc), kb);
+    // ip1 exactly as the scan forms it; 128 * ip1 is exact
+    const float ip1 = kForm == kRefineSplitInt ? __fmul_rn(width, static_cast<float>(ip))
+                                               : __fadd_rn(la0, la1);
+    return __fadd_rn(__fadd_rn(__fmul_rn(128.0f, ip1), __double2float_rn(acc)), kb);
+}
+
 // One CTA per query, one thread per candidate: a candidate's refine row (its 8-bit codes, D
 // bytes, 32-byte sectors used whole) and its meta word are loaded before its fp64 chain.
 // mode 0 refines the vanguard seeds [0, cnt) and records the seed count; mode 1 refines the
 // main candidates [seed_cnt, cnt). Dynamic shared memory (refine_smem): the query as D
-// doubles, its qint as D / 4 words of signed bytes, nprobe ProbeInfo.
+// doubles, its qint as D / 4 words of signed bytes, its LUT tables as 4 D floats, nprobe
+// ProbeInfo.
 __host__ __device__ __forceinline__ size_t refine_smem(int D, int nprobe) {
-    return (size_t)D * 8 + (size_t)D + (size_t)nprobe * sizeof(ProbeInfo);
+    return (size_t)D * 8 + (size_t)D + (size_t)D * 16 + (size_t)nprobe * sizeof(ProbeInfo);
 }
 __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, SearchView sv,
                                                                 int mode) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     double *x = reinterpret_cast<double *>(smem_raw);
     uint32_t *qw = reinterpret_cast<uint32_t *>(x + ix.D);
-    ProbeInfo *pinfo = reinterpret_cast<ProbeInfo *>(qw + ix.D / 4);
+    float *T = reinterpret_cast<float *>(qw + ix.D / 4);
+    ProbeInfo *pinfo = reinterpret_cast<ProbeInfo *>(T + 4 * ix.D);
     const int q = blockIdx.x;
     const uint32_t cnt = sv.cand_cnt[q];
     const uint32_t cap = static_cast<uint32_t>(sv.cap);
@@ -153,6 +198,10 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
     } else {
         for (int j = threadIdx.x; j < ix.D; j += blockDim.x)
             x[j] = static_cast<double>(sv.qr[(size_t)q * ix.D + j]);
+        // the LUT estimator's tables, widened to fp32
+        if (sv.lut_mode)
+            for (int i = threadIdx.x; i < 4 * ix.D; i += blockDim.x)
+                T[i] = __half2float(sv.lut[(size_t)q * 4 * ix.D + i]);
         // qint of dims 4t .. 4t + 3 from the query's two's-complement bit-planes (plane b,
         // word j / 32, bit 31 - j % 32 holds bit b of qint_j & 0xFF): byte i of word t
         const int W4 = 4 * ix.G16;
@@ -177,6 +226,8 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
     }
     __syncthreads();
     const float kb = sv.scal[q].kb, width = sv.scal[q].width;
+    const int form = sv.refine_full_code ? kRefineFullCode
+                                         : (sv.lut_mode ? kRefineSplitLut : kRefineSplitInt);
     const int nblocks = ix.D / 64;
     const int row4 = ix.D / 16;  // uint4 per refine row
     for (uint32_t i = from + threadIdx.x; i < to; i += blockDim.x) {
@@ -219,28 +270,13 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
         const uint4 *row = ix.rows + (size_t)gid * row4;
         const float2 f = make_float2(__uint_as_float(mt.x), __uint_as_float(mt.y));
         const uint32_t id = mt.z;
-        double acc = 0.0;
-        int ip = 0;
         float t;  // the factor of f_rescale_ex
-        if (sv.refine_full_code) {
-            for (int blk = 0; blk < nblocks; ++blk) {
-                uint4 v[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) v[u] = __ldg(row + 4 * blk + u);
-                block_code8_ip<false>(x + 64 * blk, qw + 16 * blk, v, acc, ip);
-            }
-            t = __fadd_rn(__double2float_rn(acc), kb);
-        } else {
-            for (int blk = 0; blk < nblocks; ++blk) {
-                uint4 v[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) v[u] = __ldg(row + 4 * blk + u);
-                block_code8_ip<true>(x + 64 * blk, qw + 16 * blk, v, acc, ip);
-            }
-            // ip1 exactly as the scan forms it; 128 * ip1 is exact
-            const float ip1 = __fmul_rn(width, static_cast<float>(ip));
-            t = __fadd_rn(__fadd_rn(__fmul_rn(128.0f, ip1), __double2float_rn(acc)), kb);
-        }
+        if (form == kRefineSplitInt)
+            t = refine_row_term<kRefineSplitInt>(row, nblocks, x, qw, T, width, kb);
+        else if (form == kRefineSplitLut)
+            t = refine_row_term<kRefineSplitLut>(row, nblocks, x, qw, T, width, kb);
+        else
+            t = refine_row_term<kRefineFullCode>(row, nblocks, x, qw, T, width, kb);
         const float ex_d = __fadd_rn(__fadd_rn(f.x, p.g), __fmul_rn(f.y, t));
         sv.cand_key[(size_t)q * sv.cap + i] = make_key(ex_d, id);
     }

@@ -15,6 +15,10 @@
 //            bit-plane popcounts above (both exact in int32)
 //   ip1    = width * ip_int
 //   low    = (f_add + g) + f_rescale * (ip1 + k1) - f_error * sqrt(max(g, 0))
+// or, with the LUT estimator (the reference's default kernel type, filter_kernels.cuh:
+// 283-306, 655-696), ip1 = acc0 + acc1 from the query's fp16 tables (lut_build_kernel):
+// nibble n of code word w (bits 31 - 4n .. 28 - 4n, dims 32w + 4n ..) looks up entry
+// (8w + n, nibble) and is added, in fp32 and in order, to acc0 for even n, acc1 for odd n.
 //
 // Search phases (all on one stream):
 //  1. vanguard pairs (probe rank r < veff) are grouped by cluster and scanned once; their
@@ -45,6 +49,11 @@ constexpr int kMaxPairsPerItem = 32;
 template <int G16>
 struct ScanShape {
     static constexpr int TV = 256;                     // vectors per staged tile (rescan)
+    // LUT estimator: floats per pair of the tables staged in shared memory (32 G16 nibble
+    // groups x 16; groups past D / 4 hold zeros, which leave the sums unchanged) and the
+    // pairs per grouped item that keep them within the shared-memory budget
+    static constexpr int kLutFloats = 512 * G16;
+    static constexpr int kLutPairs = G16 == 1 ? 32 : (G16 == 2 ? 16 : 8);
     // tiles in flight in scan_kernel (its shared memory: kStages x kStageEntries x 16 B);
     // deep enough to hide the TMA latency when an item serves few queries
     static constexpr int kStages = G16 <= 2 ? 4 : 2;
@@ -84,8 +93,10 @@ struct SearchView {
     int nq, k, nprobe, veff, keep, cap;
     const float *raw_q;          // nq x dim, the search's input queries (exact refinement)
     const QueryScalars *scal;    // nq
-    const int2 *qrange;          // nq: {sum of positive qint, sum of negative qint}
+    const float *ipm;            // nq: bound on |fl(ip1 + k1)| (ip_term_bound / lut_build_kernel)
     const uint32_t *planes;      // nq x 8 x W4
+    const __half *lut;           // nq x (D / 4) x 16: LUT estimator tables (lut_mode only)
+    int lut_mode;                // 1: the scan's ip1 comes from the LUT estimator
     const float *qr;             // nq x D
     const int *probe_ids;        // nq x nprobe
     const float *probe_g;        // nq x nprobe
@@ -126,31 +137,20 @@ __device__ __forceinline__ bool range_at_least(float4 fr, float g, float M, floa
     return L - 0x1p-20 * S >= (double)T;
 }
 
-// M of one pair: the largest |fl(fl(width * ip) + k1)| over ip in [neg, pos] (the scan's
-// evaluation of ip1 + k1, see scan_kernel).
-__device__ __forceinline__ float ip_term_bound(int2 range, float width, float k1) {
-    const float hi = __fadd_rn(__fadd_rn(__fmul_rn(width, (float)range.x), 0.0f), k1);
-    const float lo = __fadd_rn(__fadd_rn(__fmul_rn(width, (float)range.y), 0.0f), k1);
-    return fmaxf(fabsf(hi), fabsf(lo));
-}
-
 // Pair pruning of the main pass's grouping (cl_range == nullptr: none): a (query, probe)
 // pair is left out when its cluster's factor range proves every low >= T1 of the query, the
 // test scan_kernel also applies per item and per chunk.
 struct PairPrune {
     const float4 *cl_range;      // nlist
     const float *probe_g;        // nq x nprobe
-    const int2 *qrange;          // nq
-    const QueryScalars *scal;    // nq
+    const float *ipm;            // nq
     const float *T1;             // nq
 };
 __device__ __forceinline__ bool pair_pruned(const PairPrune &pp, int q, int r, int c,
                                             int nprobe) {
     if (!pp.cl_range) return false;
     const float g = pp.probe_g[(size_t)q * nprobe + r];
-    const QueryScalars qs = pp.scal[q];
-    return range_at_least(pp.cl_range[c], g, ip_term_bound(pp.qrange[q], qs.width, qs.k1),
-                          __fsqrt_rn(fmaxf(g, 0.0f)), pp.T1[q]);
+    return range_at_least(pp.cl_range[c], g, pp.ipm[q], __fsqrt_rn(fmaxf(g, 0.0f)), pp.T1[q]);
 }
 
 // ---- per-cluster query grouping (CSR of (query, probe rank) pairs by cluster) --------
@@ -474,6 +474,52 @@ __device__ __forceinline__ uint32_t offset_binary_word(uint32_t w, int word_inde
     return word_index >= 7 * W4 ? ~w : w;
 }
 
+// ---- LUT estimator ---------------------------------------------------------------
+// ip1 of one code from a pair's tables T (fp32, 16 per nibble group, shared memory): the
+// reference's order of additions (vanguard_lut_inner_product, filter_kernels.cuh:283-306).
+// Padding words (dims past D) meet zero entries: adding +0 to a sum that started at +0
+// leaves it unchanged, so they need no test.
+template <int G16>
+__device__ __forceinline__ float ip_from_lut(const uint4 (&code)[G16], const float *__restrict__ T) {
+    float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll
+    for (int g = 0; g < G16; ++g) {
+        const uint32_t x[4] = {code[g].x, code[g].y, code[g].z, code[g].w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float *Tw = T + (4 * g + t) * 128;  // word 4g + t: nibble groups 8w .. 8w + 7
+#pragma unroll
+            for (int n = 0; n < 8; n += 2) {
+                acc0 = __fadd_rn(acc0, Tw[n * 16 + ((x[t] >> (28 - 4 * n)) & 0xFu)]);
+                acc1 = __fadd_rn(acc1, Tw[(n + 1) * 16 + ((x[t] >> (24 - 4 * n)) & 0xFu)]);
+            }
+        }
+    }
+    return __fadd_rn(acc0, acc1);
+}
+
+// Widens query q's fp16 tables (4 D halves) into dst (kLutFloats fp32, zero past 4 D), one
+// 16-byte load per thread and step; the calling threads cover [tid0, tid0 + nthreads).
+template <int G16>
+__device__ __forceinline__ void stage_lut(float *__restrict__ dst, const __half *__restrict__ lut,
+                                          int q, int D, int tid0, int nthreads) {
+    constexpr int LT = ScanShape<G16>::kLutFloats;
+    const uint4 *src = reinterpret_cast<const uint4 *>(lut + (size_t)q * 4 * D);
+    for (int i = tid0; i < LT / 8; i += nthreads) {
+        float4 lo = make_float4(0.f, 0.f, 0.f, 0.f), hi = lo;
+        if (8 * i < 4 * D) {
+            const uint4 u = __ldg(src + i);
+            const __half2 *h = reinterpret_cast<const __half2 *>(&u);
+            const float2 a = __half22float2(h[0]), b = __half22float2(h[1]);
+            const float2 c = __half22float2(h[2]), d = __half22float2(h[3]);
+            lo = make_float4(a.x, a.y, b.x, b.y);
+            hi = make_float4(c.x, c.y, d.x, d.y);
+        }
+        reinterpret_cast<float4 *>(dst)[2 * i] = lo;
+        reinterpret_cast<float4 *>(dst)[2 * i + 1] = hi;
+    }
+}
+
 __device__ __forceinline__ float lower_bound_dist(float4 f, float ip1, float g, float k1,
                                                   float gerr) {
     const float a = __fadd_rn(f.x, g);
@@ -528,7 +574,9 @@ __device__ __forceinline__ void write_seeds(const SearchView &sv, int q, int r, 
 //             item, and from each 32-vector chunk (one warp of a tile), whose factor range
 //             proves every low >= T1 (range_at_least): no tile is loaded for an item that
 //             keeps no pair, and a warp evaluates only the pairs its chunk keeps.
-template <int G16, bool kWriteLows>
+// kLut: ip1 from the LUT estimator (each pair's tables staged in shared memory as fp32;
+// items hold at most ScanShape::kLutPairs pairs).
+template <int G16, bool kWriteLows, bool kLut>
 __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel(
     IndexView ix, SearchView sv, const ScanItem *__restrict__ items,
     const uint32_t *__restrict__ n_items_ptr, const uint32_t *__restrict__ pairs,
@@ -536,8 +584,10 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
     using Sh = ScanShape<G16>;
     constexpr int TV = Sh::kScanTV, W4 = Sh::W4, S = Sh::kStages, SE = Sh::kScanStageEntries;
     // query words: byte words for dp4a (the split code is 32 * G16 registers, so only for
-    // D <= 128), offset-binary bit-planes otherwise; both are 8 * W4 words per query
-    constexpr bool kBytes = kScanDp4a && G16 == 1;
+    // D <= 128), offset-binary bit-planes otherwise; both are 8 * W4 words per query. With
+    // the LUT estimator: kLutFloats fp32 table entries per pair.
+    constexpr bool kBytes = kScanDp4a && G16 == 1 && !kLut;
+    constexpr int kQB = kLut ? Sh::kLutFloats : 8 * W4;  // 32-bit words per pair
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint4 *stage = reinterpret_cast<uint4 *>(smem_raw);
     uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + S * SE);
@@ -609,7 +659,7 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
                         sv.lows[off + p] = __int_as_float(0x7f800000);
             } else {
                 s_T1[threadIdx.x] = sv.T1[q];
-                s_M[threadIdx.x] = ip_term_bound(sv.qrange[q], qs.width, qs.k1);
+                s_M[threadIdx.x] = sv.ipm[q];
                 s_bnd[threadIdx.x] = r < sv.veff ? sv.bound[(size_t)q * sv.veff + r] : 0ull;
             }
         }
@@ -639,11 +689,18 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
                     issue_tile<G16, TV>(stage + u * SE, &bars[u], ix.scan4, cbase, n, u * TV,
                                         min(TV, n - u * TV));
         }
-        for (int i = threadIdx.x; i < pc * 8 * W4; i += blockDim.x) {
-            const int j = i / (8 * W4), r = i - j * 8 * W4;
-            const uint32_t *pl = sv.planes + (size_t)s_q[j] * 8 * W4;
-            s_planes[i] = kBytes ? query_byte_word(pl, r >> 3, r & 7, W4)
-                                 : offset_binary_word(pl[r], r, W4);
+        if constexpr (kLut) {
+            // one warp per pair in turn
+            for (int j = warp; j < pc; j += kScanThreads / 32)
+                stage_lut<G16>(reinterpret_cast<float *>(s_planes) + j * kQB, sv.lut, s_q[j],
+                               ix.D, lane, 32);
+        } else {
+            for (int i = threadIdx.x; i < pc * kQB; i += blockDim.x) {
+                const int j = i / kQB, r = i - j * kQB;
+                const uint32_t *pl = sv.planes + (size_t)s_q[j] * 8 * W4;
+                s_planes[i] = kBytes ? query_byte_word(pl, r >> 3, r & 7, W4)
+                                     : offset_binary_word(pl[r], r, W4);
+            }
         }
         __syncthreads();
         for (int t = 0; t < ntiles; ++t) {
@@ -691,6 +748,7 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
                 float4 f[V];
                 int bias[V];
                 uint32_t e[V][kBytes ? 32 * G16 : 1];
+                (void)bias;
                 bool valid[V];
 #pragma unroll
                 for (int v = 0; v < V; ++v) {
@@ -707,27 +765,32 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
                     }
                     if constexpr (kBytes)
                         split_code_bytes<G16>(code[v], e[v]);
-                    else
+                    else if constexpr (!kLut)
                         bias[v] = code_bias<G16>(code[v]);
                 }
                 // lows pass: every pair in order; main pass: the pairs this warp's chunk keeps
                 for (uint32_t mj = wkeep, jj = 0; kWriteLows ? jj < static_cast<uint32_t>(pc) : mj != 0;
                      mj &= mj - 1u, ++jj) {
                     const int j = kWriteLows ? static_cast<int>(jj) : __ffs(mj) - 1;
-                    const uint32_t *P = s_planes + j * 8 * W4;
+                    const uint32_t *P = s_planes + j * kQB;
 #pragma unroll
                     for (int v = 0; v < V; ++v) {
                         const int i = vb + v * kScanThreads + threadIdx.x;
-                        int ip;
-                        if constexpr (kBytes)
-                            ip = ip_int_from_bytes<G16>(e[v], P);
-                        else
-                            ip = ip_int_from_planes<G16>(code[v], P, bias[v]);
                         const float4 pj = s_par[j];
-                        // ip1 = width * ip_int (+ 0 in the reference: width >= 1e-30 and
-                        // |ip_int| >= 1 or ip_int = 0 give a normal or +0 product, which the
-                        // addition of 0 leaves unchanged)
-                        const float ip1 = __fmul_rn(pj.x, (float)ip);
+                        float ip1;
+                        if constexpr (kLut) {
+                            ip1 = ip_from_lut<G16>(code[v], reinterpret_cast<const float *>(P));
+                        } else {
+                            int ip;
+                            if constexpr (kBytes)
+                                ip = ip_int_from_bytes<G16>(e[v], P);
+                            else
+                                ip = ip_int_from_planes<G16>(code[v], P, bias[v]);
+                            // ip1 = width * ip_int (+ 0 in the reference: width >= 1e-30 and
+                            // |ip_int| >= 1 or ip_int = 0 give a normal or +0 product, which
+                            // the addition of 0 leaves unchanged)
+                            ip1 = __fmul_rn(pj.x, (float)ip);
+                        }
                         const float low = lower_bound_dist(f[v], ip1, pj.y, pj.z, pj.w);
                         if (kWriteLows) {
                             if (valid[v]) s_lp[j][v0 + i] = low;
@@ -845,10 +908,8 @@ __global__ void __launch_bounds__(256) filter_list_kernel(IndexView ix, SearchVi
         const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
         if (!owned || owned[c]) {
             const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
-            const QueryScalars qs = sv.scal[q];
-            keep = !range_at_least(ix.cl_range[c], g,
-                                   ip_term_bound(sv.qrange[q], qs.width, qs.k1),
-                                   __fsqrt_rn(fmaxf(g, 0.0f)), sv.T1[q]);
+            keep = !range_at_least(ix.cl_range[c], g, sv.ipm[q], __fsqrt_rn(fmaxf(g, 0.0f)),
+                                   sv.T1[q]);
         }
     }
     const uint32_t mask = __ballot_sync(0xffffffffu, keep);
@@ -1000,15 +1061,16 @@ __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
 }
 
 // ---- rescan mode: one CTA per vanguard pair scans the cluster and keeps its seeds ----
-template <int G16>
+template <int G16, bool kLut>
 __global__ void __launch_bounds__(kScanThreads) vanguard_rescan_kernel(
     IndexView ix, SearchView sv, int sort_n, const uint8_t *__restrict__ owned) {
     using Sh = ScanShape<G16>;
     constexpr int TV = Sh::TV, W4 = Sh::W4;
+    constexpr int kQB = kLut ? Sh::kLutFloats : 8 * W4;  // query words (see scan_kernel)
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint4 *stage = reinterpret_cast<uint4 *>(smem_raw);                      // [2][(G16+1)TV]
     uint32_t *s_planes = reinterpret_cast<uint32_t *>(stage + 2 * Sh::kStageEntries);
-    uint64_t *s_keys = reinterpret_cast<uint64_t *>(s_planes + 8 * W4);     // sort_n
+    uint64_t *s_keys = reinterpret_cast<uint64_t *>(s_planes + kQB);        // sort_n
     __shared__ __align__(8) uint64_t bars[2];
     __shared__ int n_staged, n_total, s_abort;
     __shared__ uint64_t thresh;
@@ -1026,8 +1088,13 @@ __global__ void __launch_bounds__(kScanThreads) vanguard_rescan_kernel(
     const float gerr = __fsqrt_rn(fmaxf(g, 0.0f));
     const size_t cbase = (size_t)(G16 + 1) * s;
 
-    for (int i = threadIdx.x; i < 8 * W4; i += blockDim.x)
-        s_planes[i] = offset_binary_word(sv.planes[(size_t)q * 8 * W4 + i], i, W4);
+    if constexpr (kLut) {
+        stage_lut<G16>(reinterpret_cast<float *>(s_planes), sv.lut, q, ix.D, threadIdx.x,
+                       blockDim.x);
+    } else {
+        for (int i = threadIdx.x; i < 8 * W4; i += blockDim.x)
+            s_planes[i] = offset_binary_word(sv.planes[(size_t)q * 8 * W4 + i], i, W4);
+    }
     if (threadIdx.x == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
@@ -1058,8 +1125,13 @@ __global__ void __launch_bounds__(kScanThreads) vanguard_rescan_kernel(
             const uint4 fr = sb[G16 * TV + i];
             const float4 f = make_float4(__uint_as_float(fr.x), __uint_as_float(fr.y),
                                          __uint_as_float(fr.z), 0.0f);
-            const int ip = ip_int_from_planes<G16>(code, s_planes, code_bias<G16>(code));
-            const float ip1 = __fadd_rn(__fmul_rn(qs.width, (float)ip), 0.0f);
+            float ip1;
+            if constexpr (kLut) {
+                ip1 = ip_from_lut<G16>(code, reinterpret_cast<const float *>(s_planes));
+            } else {
+                const int ip = ip_int_from_planes<G16>(code, s_planes, code_bias<G16>(code));
+                ip1 = __fadd_rn(__fmul_rn(qs.width, (float)ip), 0.0f);
+            }
             const float low = lower_bound_dist(f, ip1, g, qs.k1, gerr);
             if (low < T0) {
                 atomicAdd(&n_total, 1);

@@ -132,8 +132,13 @@ int cora_set_queue_spill_capacity(cora_engine *engine, uint64_t capacity);
 uint64_t cora_get_queue_capacity(const cora_engine *engine);
 
 /* Knobs (hybrid.cuh:121-135,160-165). cross_query_reuse=0 processes one query per
- * cluster work item; cpu_secondary_filter and ip_kernel_type are accepted for drop-in
- * compatibility (refinement runs on the GPU; the scan always uses the integer estimator). */
+ * cluster work item; cpu_secondary_filter is accepted for drop-in compatibility (refinement
+ * runs on the GPU). ip_kernel_type selects the scan's estimator (hybrid.cuh:12):
+ * 0 = Lut4Bit, ip1 from fp16 lookup tables of the rotated query (query_kernels.cuh:199-221,
+ * filter_kernels.cuh:283-306), the reference's default; 1 = Bitwise, ip1 = width * ip_int
+ * from the integer estimator (filter_kernels.cuh:79-114), THIS ENGINE'S DEFAULT (exact
+ * integer arithmetic, the fastest scan). Any other value selects Bitwise. Both feed the same
+ * lower bound and refinement expression. */
 void cora_set_profiling(cora_engine *engine, int enabled);
 void cora_set_candidate_stats(cora_engine *engine, int enabled);
 void cora_set_gpu_filter_timing(cora_engine *engine, int enabled);
@@ -166,7 +171,8 @@ float cora_get_last_gpu_filter_ms(const cora_engine *engine);
  * (nq x 8 x W4 u32, W4 = 4 * ceil(D / 128)), 6 query scalars (nq x {width, k1, kb, sumq}),
  * 7 candidate gids (nq x cap u32, per query sorted ascending, unused slots 0xFFFFFFFF),
  * 8 approximate coarse distances of the tensor-core probe GEMM (nq x ld f32, ld = nlist
- * rounded up to a multiple of 4; rows the exact fallback recomputed hold exact values).
+ * rounded up to a multiple of 4; rows the exact fallback recomputed hold exact values),
+ * 9 LUT estimator tables (nq x D/4 x 16 binary16; written only with kernel type Lut4Bit).
  * `bytes` must equal the size of the requested array. */
 int cora_debug_copy(cora_engine *engine, int what, void *h_out, uint64_t bytes);
 /* Per-stage device times (ms) of the last search run with profiling enabled, from CUDA

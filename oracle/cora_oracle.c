@@ -174,6 +174,81 @@ float cora_oracle_low(const cora_oracle_index *ix, uint64_t gid, float ip1, floa
     return (a + b) - e;
 }
 
+/* IEEE 754 binary32 -> binary16 with round to nearest, ties to even (the rounding of
+ * CUDA's __float2half_rn, which the reference's table kernel uses), from the format's
+ * definition: normal results keep 10 of the 23 fraction bits and round on the 13 dropped
+ * ones; results below 2^-14 are multiples of 2^-24 rounded from the full significand;
+ * magnitudes from 65520 (half-way between the largest half, 65504, and 2^16) up are inf. */
+uint16_t cora_oracle_f32_to_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    const uint16_t sign = (uint16_t)((x >> 16) & 0x8000u);
+    const uint32_t ax = x & 0x7FFFFFFFu;
+    if (ax >= 0x7F800000u) return (uint16_t)(sign | (ax > 0x7F800000u ? 0x7E00u : 0x7C00u));
+    if (ax >= 0x477FF000u) return (uint16_t)(sign | 0x7C00u); /* >= 65520 */
+    if (ax >= 0x38800000u) {                                  /* >= 2^-14: normal half */
+        const uint32_t r = ax - 0x38000000u;                  /* exponent bias 127 -> 15 */
+        uint32_t h = r >> 13;
+        const uint32_t rest = r & 0x1FFFu;
+        if (rest > 0x1000u || (rest == 0x1000u && (h & 1u))) ++h; /* a carry may bump the exponent */
+        return (uint16_t)(sign | h);
+    }
+    const uint32_t e = ax >> 23;
+    if (e < 102) return sign; /* below 2^-25: rounds to zero */
+    const uint32_t m24 = (ax & 0x7FFFFFu) | 0x800000u;
+    const uint32_t shift = 126u - e; /* value / 2^-24 = m24 / 2^shift, shift in [14, 24] */
+    uint32_t k = m24 >> shift;
+    const uint32_t rest = m24 & ((1u << shift) - 1u), halfway = 1u << (shift - 1);
+    if (rest > halfway || (rest == halfway && (k & 1u))) ++k; /* k = 1024: the smallest normal */
+    return (uint16_t)(sign | k);
+}
+
+float cora_oracle_f16_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16, e = (h >> 10) & 31u, m = h & 1023u;
+    uint32_t x;
+    if (e == 0) {
+        const float v = (float)m * 0x1p-24f; /* exact */
+        memcpy(&x, &v, 4);
+        x |= sign;
+    } else if (e == 31) {
+        x = sign | 0x7F800000u | (m << 13);
+    } else {
+        x = sign | ((e + 112u) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &x, 4);
+    return f;
+}
+
+/* query_kernels.cuh:199-221 (precompute_lut_fp16_kernel): entry (g, p) is the fp32 sum,
+ * starting from 0, of q'[4g + i] over the bits 3 - i set in p (i ascending), rounded to
+ * binary16. */
+void cora_oracle_query_lut(const float *qr, uint64_t D, uint16_t *lut) {
+    for (uint64_t g = 0; g < D / 4; ++g)
+        for (int p = 0; p < 16; ++p) {
+            float sum = 0.0f;
+            for (int i = 0; i < 4; ++i)
+                if (p & (8 >> i)) sum += qr[4 * g + (uint64_t)i];
+            lut[g * 16 + (uint64_t)p] = cora_oracle_f32_to_f16(sum);
+        }
+}
+
+/* filter_kernels.cuh:283-306 / 655-694: nibble n of word w (its dims 32w + 4n ..) adds entry
+ * (8w + n, nibble) to acc0 for even n and to acc1 for odd n, in order; ip1 = acc0 + acc1. */
+float cora_oracle_ip_lut(const uint32_t *words, const uint16_t *lut, uint64_t D) {
+    float acc0 = 0.0f, acc1 = 0.0f;
+    for (uint64_t w = 0; w < D / 32; ++w)
+        for (int n = 0; n < 8; ++n) {
+            const uint32_t nib = (words[w] >> (28 - 4 * n)) & 0xFu;
+            const float v = cora_oracle_f16_to_f32(lut[(8 * w + (uint64_t)n) * 16 + nib]);
+            if (n & 1)
+                acc1 += v;
+            else
+                acc0 += v;
+        }
+    return acc0 + acc1;
+}
+
 /* Inverse of pack_excode.hpp:216-264 (packing_7bit_excode), per 64 dims = 56 bytes. */
 void cora_oracle_decode_ex7(const uint8_t *code, uint64_t D, uint8_t *u) {
     for (uint64_t b = 0; b < D / 64; ++b) {
@@ -270,6 +345,18 @@ static float refine(const cora_oracle_index *ix, const float *qraw, const float 
     return cora_oracle_ex(ix, gid, cora_oracle_ip_total(x, bits, code, D), g, kb);
 }
 
+/* The scan's ip1 of vector i of the cluster at `start` (size n): the integer estimator's
+ * width * ip_int (+ 0, filter_kernels.cuh:106), or the LUT estimator's sum (lut != NULL). */
+static float scan_ip1(const cora_oracle_index *ix, uint64_t start, uint64_t n, uint64_t i,
+                      const uint32_t *planes, float width, const uint16_t *lut) {
+    if (lut) {
+        uint32_t words[128];
+        vector_bits(ix, start, n, i, words);
+        return cora_oracle_ip_lut(words, lut, ix->padded_dim);
+    }
+    return width * (float)ip_int_at(ix, start, n, i, planes) + 0.0f;
+}
+
 static void push(entry_t **v, uint64_t *n, uint64_t *cap, entry_t e) {
     if (*n == *cap) {
         *cap = *cap ? *cap * 2 : 256;
@@ -322,9 +409,11 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
         entry_t *res = NULL, *pair = NULL;
         uint64_t nres = 0, cres = 0, npair = 0, cpair = 0;
         float sumq, k1, kb, width;
+        uint16_t *lut = ix->lut_estimator ? (uint16_t *)malloc(4 * D * sizeof(uint16_t)) : NULL;
 
         cora_oracle_rotate(ix, q + n * ix->dim, 1, x);
         cora_oracle_query_prep(D, ix->ex_bits, x, 1, &sumq, &k1, &kb, &width, NULL, planes);
+        if (lut) cora_oracle_query_lut(x, D, lut);
         probe_one(ix, x, nprobe, pid, pg, scratch);
         if (probe_ids_out) memcpy(probe_ids_out + n * nprobe, pid, nprobe * sizeof(int32_t));
         if (probe_g_out) memcpy(probe_g_out + n * nprobe, pg, nprobe * sizeof(float));
@@ -340,7 +429,7 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
             const float g = pg[r];
             npair = 0;
             for (uint64_t i = 0; i < nc; ++i) {
-                const float ip1 = width * (float)ip_int_at(ix, s, nc, i, planes) + 0.0f;
+                const float ip1 = scan_ip1(ix, s, nc, i, planes, width, lut);
                 const float low = cora_oracle_low(ix, s + i, ip1, g, k1);
                 if (low < T0) {
                     entry_t e = {((uint64_t)ord_f32(low) << 32) | (uint32_t)(s + i), low, ip1,
@@ -389,7 +478,7 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
             const float g = pg[r];
             if (r < veff && take_all[r]) continue;
             for (uint64_t i = 0; i < nc; ++i) {
-                const float ip1 = width * (float)ip_int_at(ix, s, nc, i, planes) + 0.0f;
+                const float ip1 = scan_ip1(ix, s, nc, i, planes, width, lut);
                 const float low = cora_oracle_low(ix, s + i, ip1, g, k1);
                 if (!(low < T1)) continue;
                 if (r < veff) {
@@ -429,7 +518,7 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
             out_ids[n * k + o] = 0;
         }
         free(x); free(planes); free(scratch); free(pid); free(pg); free(res); free(pair);
-        free(bound); free(take_all);
+        free(bound); free(take_all); free(lut);
     }
     free(starts);
     return 0;

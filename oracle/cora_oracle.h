@@ -22,7 +22,12 @@
  *  - rotation and centroid distances accumulate in fp64 in ascending index order (fp64
  *    fma; products of two fp32 values are exact in fp64) and round once to fp32; sumq
  *    accumulates in fp64 over 32 strided lanes combined by an xor butterfly;
- *  - ip_int is exact integer arithmetic; ip1 = width * (float)ip_int;
+ *  - ip_int is exact integer arithmetic; ip1 = width * (float)ip_int; or, with the LUT
+ *    estimator (lut_estimator = 1; query_kernels.cuh:199-221, filter_kernels.cuh:283-306),
+ *    ip1 = acc0 + acc1 over fp16 table entries: entry (g, p) = half_rne(fp32 sum from 0 of
+ *    the q' of dims 4g + i with bit 3 - i of p set, i ascending), and nibble n of code word
+ *    w (bits 31 - 4n .. 28 - 4n) adds entry (8w + n, nibble) to acc0 (n even) or acc1 (n
+ *    odd), in ascending (w, n) order, in fp32;
  *  - low / ex follow the reference's expression trees in fp32, round-to-nearest, with no
  *    contraction (built with -ffp-contract=off);
  *  - refinement follows the reference's expression (cpu_refinement.cpp:183-191,
@@ -75,6 +80,9 @@ typedef struct {
     uint64_t exact_rows, exact_dim, exact_stride;
     /* 0 (default): the reference's 2^ex * ip1 + ip2 refinement; 1: the full-code ipT. */
     int refine_full_code;
+    /* 0 (default): ip1 from the integer estimator (KernelType::Bitwise); 1: from the fp16
+     * LUT estimator (KernelType::Lut4Bit, the reference's default kernel type). */
+    int lut_estimator;
 } cora_oracle_index;
 
 #define CORA_ORACLE_VANGUARD_MIN_KEEP 20
@@ -94,6 +102,13 @@ float cora_oracle_ip_total(const float *qr, const uint32_t *bits, const uint8_t 
                            uint64_t D);
 float cora_oracle_ex(const cora_oracle_index *ix, uint64_t gid, float ip_total, float g,
                      float kb);
+/* binary32 -> binary16, round to nearest (ties to even), and binary16 -> binary32. */
+uint16_t cora_oracle_f32_to_f16(float f);
+float cora_oracle_f16_to_f32(uint16_t h);
+/* LUT estimator tables of one rotated query: lut[g * 16 + p], g < D / 4 (binary16 bits). */
+void cora_oracle_query_lut(const float *qr, uint64_t D, uint16_t *lut);
+/* LUT estimator ip1 of one vector's 1-bit code words (D / 32 words, dim 32w + b at bit 31 - b). */
+float cora_oracle_ip_lut(const uint32_t *words, const uint16_t *lut, uint64_t D);
 /* ip2 = <q', u>, u the decoded 7-bit ex code (what ip64_fxu7_avx computes). */
 float cora_oracle_ip_ex(const float *qr, const uint8_t *code, uint64_t D);
 /* The reference's refinement: (f_add_ex + g) + f_rescale_ex * ((128 * ip1 + ip2) + kb). */

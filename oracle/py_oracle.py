@@ -165,7 +165,7 @@ class _Index(C.Structure):
                 ("ids", C.c_void_p), ("cluster_sizes", C.c_void_p),
                 ("exact_base", C.c_void_p), ("exact_rows", C.c_uint64),
                 ("exact_dim", C.c_uint64), ("exact_stride", C.c_uint64),
-                ("refine_full_code", C.c_int)]
+                ("refine_full_code", C.c_int), ("lut_estimator", C.c_int)]
 
 
 _lib = None
@@ -192,6 +192,15 @@ def lib():
                                              _f32p, _f32p, _f32p, _i32p, _u32p]
         L.cora_oracle_probe.argtypes = [C.POINTER(_Index), _f32p, C.c_uint64, C.c_uint64,
                                         _i32p, _f32p]
+        L.cora_oracle_f32_to_f16.restype = C.c_uint16
+        L.cora_oracle_f32_to_f16.argtypes = [C.c_float]
+        L.cora_oracle_f16_to_f32.restype = C.c_float
+        L.cora_oracle_f16_to_f32.argtypes = [C.c_uint16]
+        L.cora_oracle_query_lut.argtypes = [_f32p, C.c_uint64,
+                                            np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")]
+        L.cora_oracle_ip_lut.restype = C.c_float
+        L.cora_oracle_ip_lut.argtypes = [_u32p, np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS"),
+                                         C.c_uint64]
         L.cora_oracle_ip_ex.restype = C.c_float
         L.cora_oracle_ip_ex.argtypes = [_f32p, _u8p, C.c_uint64]
         L.cora_oracle_ex_split.restype = C.c_float
@@ -217,9 +226,10 @@ class OracleIndex:
     exact_base: optional float32 (rows, dim) base vectors indexed by original id; when set,
     candidates are refined with exact squared L2 distances (HybridIndex::enable_exact_refine,
     hybrid.cuh:171-178). full_code: refine with the full 8-bit code inner product instead
-    of the reference's 128 * ip1 + ip2 (cora_oracle.h)."""
+    of the reference's 128 * ip1 + ip2; lut: ip1 from the fp16 LUT estimator instead of the
+    integer one (cora_oracle.h)."""
 
-    def __init__(self, sd: dict, exact_base=None, full_code=False):
+    def __init__(self, sd: dict, exact_base=None, full_code=False, lut=False):
         self.sd = {
             "centroids": np.ascontiguousarray(sd["centroids"], np.float32),
             "rotator": np.ascontiguousarray(sd["rotator"], np.float32),
@@ -236,7 +246,8 @@ class OracleIndex:
         self.c = _Index(self.num, self.dim, self.D, self.nlist, self.ex_bits,
                         _ptr(s["centroids"]), _ptr(s["rotator"]), _ptr(s["short_data"]),
                         _ptr(s["short_factors"]), _ptr(s["long_codes"]), _ptr(s["ex_factors"]),
-                        _ptr(s["ids"]), _ptr(s["sizes"]), None, 0, 0, 0, int(bool(full_code)))
+                        _ptr(s["ids"]), _ptr(s["sizes"]), None, 0, 0, 0, int(bool(full_code)),
+                        int(bool(lut)))
         self.set_exact_base(exact_base)
 
     @property
@@ -246,6 +257,24 @@ class OracleIndex:
     @full_code.setter
     def full_code(self, on):
         self.c.refine_full_code = int(bool(on))
+
+    @property
+    def lut(self) -> bool:
+        return bool(self.c.lut_estimator)
+
+    @lut.setter
+    def lut(self, on):
+        self.c.lut_estimator = int(bool(on))
+
+    def query_lut(self, qr):
+        """LUT estimator tables (nq, D / 4, 16) as binary16 bits (uint16)."""
+        qr = np.ascontiguousarray(qr, np.float32)
+        out = np.empty((qr.shape[0], self.D // 4, 16), np.uint16)
+        for i in range(qr.shape[0]):
+            row = np.empty(self.D * 4, np.uint16)
+            lib().cora_oracle_query_lut(np.ascontiguousarray(qr[i]), self.D, row)
+            out[i] = row.reshape(self.D // 4, 16)
+        return out
 
     def set_exact_base(self, base):
         """Exact refinement against `base` (float32 (rows, dim), row = original id), or off."""
@@ -325,8 +354,8 @@ class OracleIndex:
         return ids, g
 
 
-def oracle_from_file(path, full_code=False) -> OracleIndex:
-    return OracleIndex(search_data(read_ivf_file(path)), full_code=full_code)
+def oracle_from_file(path, full_code=False, lut=False) -> OracleIndex:
+    return OracleIndex(search_data(read_ivf_file(path)), full_code=full_code, lut=lut)
 
 
 # --------------------------------------------------------------------------------------
@@ -506,8 +535,8 @@ def smallest_keys_per_query(recv, world, nq, k):
 
 class OracleShard:
     def __init__(self, sd_shard: dict, world: int, vanguard=5, thresholds=None, threads=None,
-                 full_code=False):
-        self.o = OracleIndex(sd_shard, full_code=full_code)
+                 full_code=False, lut=False):
+        self.o = OracleIndex(sd_shard, full_code=full_code, lut=lut)
         self.world, self.vanguard, self.T0, self.threads = world, vanguard, thresholds, threads
 
     def buffers(self, nq, k):

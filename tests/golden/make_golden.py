@@ -16,7 +16,8 @@ oracle/_ref/libcora_ref_*.so, i.e. the reference's own CPU code). For each fixtu
 5. records exact ground truth (fp64, ties by id) and the oracle's search outputs for a grid
    of (topk, nprobe, vanguard), in the default refinement form (the reference's
    128 * ip1 + ip2: keys dist_/ids_/cand_/t1_/probe_/probeg_) and in the full-code form
-   (keys with a "T" suffix on the prefix: distT_/idsT_/candT_/t1T_).
+   (keys with a "T" suffix on the prefix: distT_/idsT_/candT_/t1T_), and with the fp16-LUT
+   estimator (the reference's default kernel type; "L" suffix: distL_/idsL_/candL_/t1L_).
 
 Usage: python tests/golden/make_golden.py [names]   (writes tests/golden/*.index, *.npz)
        python tests/golden/make_golden.py --outputs-only [names]
@@ -78,8 +79,8 @@ def sha(a) -> str:
 
 def oracle_outputs(oracle, queries, grid, out):
     """The oracle's search outputs over the grid, in both refinement forms, into `out`."""
-    for full_code, sfx in ((False, ""), (True, "T")):
-        oracle.full_code = full_code
+    for full_code, lut, sfx in ((False, False, ""), (True, False, "T"), (False, True, "L")):
+        oracle.full_code, oracle.lut = full_code, lut
         for k, nprobe, van in grid:
             k, nprobe, van = int(k), int(nprobe), int(van)
             det = oracle.search(queries, k, nprobe, vanguard=van, with_details=True)
@@ -88,10 +89,10 @@ def oracle_outputs(oracle, queries, grid, out):
             out[f"ids{sfx}_{tag}"] = det["ids"]
             out[f"cand{sfx}_{tag}"] = det["cand_count"]
             out[f"t1{sfx}_{tag}"] = det["thresholds1"]
-            if not full_code:
+            if not sfx:
                 out[f"probe_{tag}"] = det["probe_ids"]
                 out[f"probeg_{tag}"] = det["probe_g"]
-    oracle.full_code = False
+    oracle.full_code, oracle.lut = False, False
 
 
 def refresh_outputs(name):

@@ -21,11 +21,17 @@ def cb():
     return coraanns_b200
 
 
+# forms of the search contract: "" integer estimator + the reference's refinement (the
+# default), "T" full-code refinement, "L" fp16-LUT estimator (the golden keys' suffixes)
+FORMS = {"": dict(), "T": dict(full_code=True), "L": dict(lut=True)}
+
+
 def _engine(cb, path=None, sd=None, nq=1, k=10, nprobe=1, vanguard=5, mode="lows",
-            full_code=False):
+            full_code=False, lut=False):
     e = cb.HybridIndex(0)
     e.set_vanguard_size(vanguard)
     e.set_refine_full_code(full_code)
+    e.set_ip_kernel_type(cb.KernelType.Lut4Bit if lut else cb.KernelType.Bitwise)
     if mode == "rescan":
         e.set_vanguard_lows_budget(0)
     if mode == "blocksel":  # every pair / query through the block-wide selections
@@ -61,25 +67,25 @@ def _check_stages(e, q, k, nprobe, ref, tag):
         f"{tag}: candidate counts"
 
 
-@pytest.mark.parametrize("loader,mode,full_code", [
-    ("file", "lows", False), ("raw", "lows", False), ("file", "rescan", False),
-    ("file", "blocksel", False), ("raw", "tightsel", False),
-    ("file", "lows", True), ("raw", "rescan", True)])
+@pytest.mark.parametrize("loader,mode,sfx", [
+    ("file", "lows", ""), ("raw", "lows", ""), ("file", "rescan", ""),
+    ("file", "blocksel", ""), ("raw", "tightsel", ""),
+    ("file", "lows", "T"), ("raw", "rescan", "T"),
+    ("file", "lows", "L"), ("raw", "rescan", "L"), ("file", "tightsel", "L")])
 @pytest.mark.parametrize("name", GOLDEN_NAMES)
-def test_golden_parity(cb, golden, name, loader, mode, full_code):
-    """Every stage and the results against the committed oracle outputs, in the default
-    (reference) refinement form and in the full-code form."""
+def test_golden_parity(cb, golden, name, loader, mode, sfx):
+    """Every stage and the results against the committed oracle outputs, in each form of
+    the contract (integer estimator + the reference's refinement, full-code refinement,
+    fp16-LUT estimator)."""
     path, z = golden[name]
     q = z["queries"]
     grid = z["grid"]
-    sfx = "T" if full_code else ""
     kmax, npmax = int(grid[:, 0].max()), int(grid[:, 1].max())
     if loader == "file":
-        e = _engine(cb, path=path, nq=len(q), k=kmax, nprobe=npmax, mode=mode,
-                    full_code=full_code)
+        e = _engine(cb, path=path, nq=len(q), k=kmax, nprobe=npmax, mode=mode, **FORMS[sfx])
     else:
         e = _engine(cb, sd=po.search_data(po.read_ivf_file(path)), nq=len(q), k=kmax,
-                    nprobe=npmax, mode=mode, full_code=full_code)
+                    nprobe=npmax, mode=mode, **FORMS[sfx])
     assert e.get_vanguard_mode() == (0 if mode == "rescan" else 1)
     for k, nprobe, van in grid:
         k, nprobe, van = int(k), int(nprobe), int(van)
@@ -92,6 +98,9 @@ def test_golden_parity(cb, golden, name, loader, mode, full_code):
                    probe_ids=z[f"probe_{key}"], probe_g=z[f"probeg_{key}"],
                    thresholds1=z[f"t1{sfx}_{key}"], cand_count=z[f"cand{sfx}_{key}"])
         _check_stages(e, q, k, nprobe, ref, tag)
+        if sfx == "L":
+            want = po.oracle_from_file(path).query_lut(z["qr"])
+            assert np.array_equal(e.debug("lut", len(q)), want), f"{tag}: LUT tables"
         assert np.array_equal(i, z[f"ids{sfx}_{key}"]), f"{tag}: ids"
         assert d.tobytes() == z[f"dist{sfx}_{key}"].tobytes(), f"{tag}: distances"
         assert e.get_last_submitted_count() == int(z[f"cand{sfx}_{key}"].sum())
@@ -109,27 +118,32 @@ def _synthetic(n, dim, nlist, nq, seed, sigma=0.25):
     return sd, q
 
 
-@pytest.mark.parametrize("n,dim,nlist,nq,k,nprobe,van,mode,full_code", [
-    (200_000, 96, 256, 256, 10, 16, 5, "lows", False),
-    (200_000, 96, 256, 256, 10, 16, 5, "rescan", False),
-    (200_000, 96, 256, 256, 10, 16, 5, "tightsel", False),
-    (200_000, 96, 256, 64, 100, 24, 5, "lows", False),
-    (200_000, 96, 256, 64, 100, 24, 5, "lows", True),
-    (60_000, 768, 64, 48, 10, 8, 5, "lows", False),
-    (60_000, 768, 64, 48, 10, 8, 3, "rescan", False),
-    (60_000, 768, 64, 48, 10, 8, 5, "lows", True),
-    (100_000, 128, 128, 300, 10, 32, 0, "lows", False),
+@pytest.mark.parametrize("n,dim,nlist,nq,k,nprobe,van,mode,sfx", [
+    (200_000, 96, 256, 256, 10, 16, 5, "lows", ""),
+    (200_000, 96, 256, 256, 10, 16, 5, "rescan", ""),
+    (200_000, 96, 256, 256, 10, 16, 5, "tightsel", ""),
+    (200_000, 96, 256, 64, 100, 24, 5, "lows", ""),
+    (200_000, 96, 256, 64, 100, 24, 5, "lows", "T"),
+    (200_000, 96, 256, 256, 10, 16, 5, "lows", "L"),
+    (200_000, 96, 256, 64, 100, 24, 5, "rescan", "L"),
+    (60_000, 768, 64, 48, 10, 8, 5, "lows", ""),
+    (60_000, 768, 64, 48, 10, 8, 3, "rescan", ""),
+    (60_000, 768, 64, 48, 10, 8, 5, "lows", "T"),
+    (60_000, 768, 64, 48, 10, 8, 5, "lows", "L"),
+    (60_000, 768, 64, 48, 10, 8, 3, "rescan", "L"),
+    (40_000, 150, 64, 64, 10, 8, 5, "lows", "L"),
+    (40_000, 150, 64, 64, 10, 8, 5, "rescan", ""),
+    (100_000, 128, 128, 300, 10, 32, 0, "lows", ""),
 ])
-def test_live_oracle_parity_larger(cb, n, dim, nlist, nq, k, nprobe, van, mode, full_code):
+def test_live_oracle_parity_larger(cb, n, dim, nlist, nq, k, nprobe, van, mode, sfx):
     """Bit-exact parity with the oracle on indexes larger than the fixtures (more tiles per
-    cluster, more pairs per item, D = 768), in both vanguard modes and both refinement
-    forms."""
+    cluster, more pairs per item, D = 768, padded code words at D = 192), in both vanguard
+    modes and every form of the contract."""
     sd, q = _synthetic(n, dim, nlist, nq, seed=n + dim)
-    o = po.OracleIndex(sd, full_code=full_code)
+    o = po.OracleIndex(sd, **FORMS[sfx])
     ref = o.search(q, k, nprobe, vanguard=van, with_details=True,
                    cand_cap=0)
-    e = _engine(cb, sd=sd, nq=nq, k=k, nprobe=nprobe, vanguard=van, mode=mode,
-                full_code=full_code)
+    e = _engine(cb, sd=sd, nq=nq, k=k, nprobe=nprobe, vanguard=van, mode=mode, **FORMS[sfx])
     e.reset_buffer(q)
     d, i = e.search(q, k, nprobe)
     _check_stages(e, q, k, nprobe, ref, f"synthetic n{n} d{dim}")
@@ -257,7 +271,12 @@ def test_search_graph_replay_matches_eager(cb, golden):
         e.reset_buffer(q)
         d, i = e.search(q, 10, 8)
         out.append((d.tobytes(), i.tobytes()))
+        e.set_ip_kernel_type(cb.KernelType.Lut4Bit)  # another estimator: rebuilt again
+        e.reset_buffer(q)
+        d, i = e.search(q, 10, 8)
+        out.append((d.tobytes(), i.tobytes()))
+        e.set_ip_kernel_type(cb.KernelType.Bitwise)
         results[graphs] = out
-    assert results[1][-2] != results[1][-1]  # the two forms rank differently here
+    assert results[1][-3] != results[1][-2]  # the two refinement forms rank differently here
     assert results[1] == results[0]
     e.close()

@@ -28,14 +28,17 @@ def test_searchdata_restatement_matches_reference_hashes(golden, name):
     assert got == list(z["sd_sha"])
 
 
-@pytest.mark.parametrize("full_code", [False, True])
+MODES = {"": dict(), "T": dict(full_code=True), "L": dict(lut=True)}
+
+
+@pytest.mark.parametrize("sfx", list(MODES))
 @pytest.mark.parametrize("name", GOLDEN_NAMES)
-def test_oracle_reproduces_golden_outputs(golden, name, full_code):
-    """The oracle is deterministic: rerunning it gives the committed outputs bit for bit, in
-    the default (reference) refinement form and in the full-code form ("T" keys)."""
+def test_oracle_reproduces_golden_outputs(golden, name, sfx):
+    """The oracle is deterministic: rerunning it gives the committed outputs bit for bit, with
+    the integer estimator and the reference's refinement (the default), the full-code
+    refinement ("T" keys) and the fp16-LUT estimator ("L" keys)."""
     path, z = golden[name]
-    o = po.oracle_from_file(path, full_code=full_code)
-    sfx = "T" if full_code else ""
+    o = po.oracle_from_file(path, **MODES[sfx])
     for k, nprobe, van in z["grid"]:
         tag = f"k{k}_np{nprobe}_v{van}"
         det = o.search(z["queries"], int(k), int(nprobe), vanguard=int(van), with_details=True)
@@ -145,13 +148,53 @@ def test_refinement_matches_reference_expression_live(golden, name):
     assert count > 0 and worst <= 1e-4, (count, worst)
 
 
+def test_half_conversion_matches_ieee_round_to_nearest_even():
+    """The oracle's binary32 -> binary16 rounding (the LUT entries; CUDA's __float2half_rn)
+    equals numpy's IEEE conversion on random values across the half range, subnormals, ties
+    and overflow; binary16 -> binary32 is exact for every finite half."""
+    rng = np.random.default_rng(5)
+    v = (rng.normal(size=50000) * 10.0 ** rng.integers(-9, 6, 50000)).astype(np.float32)
+    edges = np.array([0.0, -0.0, 65504, 65519.996, 65520, -65520, 1e9, 2 ** -24, 2 ** -25,
+                      3 * 2 ** -26, 2 ** -14, 2 ** -14 * (1 - 2 ** -11), 1 + 2 ** -11,
+                      1 + 3 * 2 ** -11], np.float32)
+    v = np.concatenate([v, edges])
+    with np.errstate(over="ignore"):
+        want = v.astype(np.float16).view(np.uint16)
+    got = np.array([po.lib().cora_oracle_f32_to_f16(float(x)) for x in v], np.uint16)
+    assert np.array_equal(got, want)
+    h = np.arange(65536, dtype=np.uint16)
+    ref = h.view(np.float16).astype(np.float32)
+    back = np.array([po.lib().cora_oracle_f16_to_f32(int(x)) for x in h], np.float32)
+    fin = np.isfinite(ref)
+    assert np.array_equal(back[fin].view(np.uint32), ref[fin].view(np.uint32))
+
+
+def test_lut_tables_restate_reference_formula(golden):
+    """query_kernels.cuh:199-221: entry (g, p) = half(fp32 sum from 0 of the q'[4g + i]
+    selected by bit 3 - i of p, i ascending), restated here in numpy and compared bitwise."""
+    path, z = golden["d96"]
+    o = po.oracle_from_file(path)
+    qr = z["qr"][:8]
+    got = o.query_lut(qr)
+    D = qr.shape[1]
+    want = np.zeros((len(qr), D // 4, 16), np.float16)
+    for p in range(16):
+        acc = np.zeros((len(qr), D // 4), np.float32)
+        for i in range(4):
+            if p & (8 >> i):
+                acc = (acc + qr[:, i::4]).astype(np.float32)
+        want[:, :, p] = acc.astype(np.float16)
+    assert np.array_equal(got, want.view(np.uint16))
+
+
 @pytest.mark.parametrize("name", GOLDEN_NAMES)
 def test_recall_on_par_with_reference_cpu(golden, name):
     """L5: distance-aware recall@k against the reference CPU search (the rabitq_cpu loop,
-    recorded). The full-code refinement is at least the reference's minus 0.02 at every grid
-    point. The default form reproduces the reference hybrid path's 128 * ip1 + ip2 with the
-    integer estimator's ip1 (its Bitwise kernel type), whose 8-bit query quantisation costs
-    recall against rabitq_cpu's estimator: it is held to 0.06 below it."""
+    recorded). The fp16-LUT estimator (the reference hybrid path's default kernel type) and
+    the full-code refinement are at least the reference's minus 0.02 at every grid point. The
+    default form reproduces the reference hybrid path's 128 * ip1 + ip2 with the integer
+    estimator's ip1 (its Bitwise kernel type), whose 8-bit query quantisation costs recall
+    against rabitq_cpu's estimator: it is held to 0.06 below it."""
     path, z = golden[name]
     base = regen_base(z["meta"], z["gen"])
     gt = z["gt_ids"]
@@ -159,8 +202,9 @@ def test_recall_on_par_with_reference_cpu(golden, name):
     for k, nprobe, van in z["grid"]:
         tag = f"k{k}_np{nprobe}_v{van}"
         ref = po.distance_recall(base, z["queries"], gt, z[f"refcpu_k{k}_np{nprobe}"], int(k))
-        full = po.distance_recall(base, z["queries"], gt, z[f"idsT_{tag}"], int(k))
-        assert full >= ref - 0.02, (tag, full, ref)
+        for sfx in ("T", "L"):
+            other = po.distance_recall(base, z["queries"], gt, z[f"ids{sfx}_{tag}"], int(k))
+            assert other >= ref - 0.02, (tag, sfx, other, ref)
         if int(k) >= 10:
             mine = po.distance_recall(base, z["queries"], gt, z[f"ids_{tag}"], int(k))
             assert mine >= ref - 0.06, (tag, mine, ref)
