@@ -155,10 +155,12 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
 // selected q' in dimension order (query_kernels.cuh:199-221). Tables are stored as
 // lut[q][g][p], 16 halves (32 bytes) per group. One warp per query, 8 queries per CTA.
 //
-// The bound M of the pruning test: ip1 = acc0 + acc1 where acc0 / acc1 are fp32 sums of at
-// most D / 8 table entries each, so |ip1| <= A (1 + 2^-24)^(D / 4) <= A (1 + 2^-16) for
-// A = sum_g max_p |entry(g, p)| and D <= 1024; M = (A (1 + 2^-16) + |k1|) (1 + 2^-23) bounds
-// |fl(ip1 + k1)| (every step rounded upwards).
+// The bound M of the pruning test: the exact sum of a code's entries lies in [Lo, Hi], Lo / Hi
+// the sums over the groups of their smallest / largest entry (sums of halves, exact in
+// fp64). ip1 = acc0 + acc1 sums at most D / 8 entries per accumulator in fp32, so it is
+// within ((D / 8) + 1) 2^-24 A <= 2^-16 A of the exact sum (A = sum_g max_p |entry(g, p)|,
+// D <= 1024), and fl(ip1 + k1) is then within
+// M = (max(|Hi + k1|, |Lo + k1|) + 2^-16 A) (1 + 2^-22) of zero (every step rounded upwards).
 constexpr int kLutWarps = 8;
 __global__ void __launch_bounds__(32 * kLutWarps) lut_build_kernel(
     const float *__restrict__ qr, const QueryScalars *__restrict__ scal, int nq, int D,
@@ -167,11 +169,11 @@ __global__ void __launch_bounds__(32 * kLutWarps) lut_build_kernel(
     const int q = blockIdx.x * kLutWarps + (threadIdx.x >> 5);
     if (q >= nq) return;  // whole warp
     const float4 *x4 = reinterpret_cast<const float4 *>(qr + (size_t)q * D);
-    double A = 0.0;
+    double A = 0.0, Hi = 0.0, Lo = 0.0;  // sums of halves: exact in fp64
     for (int g = lane; g < D / 4; g += 32) {
         const float4 v = __ldg(x4 + g);
         __align__(16) __half h[16];
-        double hm = 0.0;
+        double hmax = 0.0, hmin = 0.0;  // p = 0 gives 0
 #pragma unroll
         for (int p = 0; p < 16; ++p) {
             float sum = 0.0f;
@@ -180,18 +182,29 @@ __global__ void __launch_bounds__(32 * kLutWarps) lut_build_kernel(
             if (p & 2) sum = __fadd_rn(sum, v.z);
             if (p & 1) sum = __fadd_rn(sum, v.w);
             h[p] = __float2half_rn(sum);
-            hm = fmax(hm, fabs((double)__half2float(h[p])));
+            const double e = (double)__half2float(h[p]);
+            hmax = fmax(hmax, e);
+            hmin = fmin(hmin, e);
         }
         uint4 *dst = reinterpret_cast<uint4 *>(lut + ((size_t)q * (D / 4) + g) * 16);
         dst[0] = *reinterpret_cast<const uint4 *>(h);
         dst[1] = *reinterpret_cast<const uint4 *>(h + 8);
-        A = __dadd_ru(A, hm);
+        A += fmax(hmax, -hmin);
+        Hi += hmax;
+        Lo += hmin;
     }
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) A = __dadd_ru(A, __shfl_xor_sync(0xffffffffu, A, off));
+    for (int off = 16; off >= 1; off >>= 1) {
+        A += __shfl_xor_sync(0xffffffffu, A, off);
+        Hi += __shfl_xor_sync(0xffffffffu, Hi, off);
+        Lo += __shfl_xor_sync(0xffffffffu, Lo, off);
+    }
     if (lane == 0) {
-        const double grown = __dmul_ru(A, 1.0 + 0x1p-16);
-        const double m = __dmul_ru(__dadd_ru(grown, fabs((double)scal[q].k1)), 1.0 + 0x1p-23);
+        // max |t| over t in [Lo + k1, Hi + k1] is max(Hi + k1, -(Lo + k1)), each bounded
+        // outwards (k1 may carry bits below the halves' 2^-24 grid)
+        const double k1 = (double)scal[q].k1;
+        const double span = fmax(__dadd_ru(Hi, k1), -__dadd_rd(Lo, k1));
+        const double m = __dmul_ru(__dadd_ru(span, __dmul_ru(A, 0x1p-16)), 1.0 + 0x1p-22);
         ipm[q] = __double2float_ru(m);
     }
 }

@@ -134,3 +134,43 @@ def test_bound_tight_chunks(seed):
                 dropped += 1
                 assert np.all(lows >= T), (trial, T, lows.min())
     assert dropped > 0
+
+
+def lut_bound(lut_f16, k1):
+    """The LUT estimator's bound M (lut_build_kernel): Hi / Lo the sums of each group's
+    largest / smallest entry, A the sum of the largest magnitudes; rounded outwards."""
+    e = lut_f16.astype(np.float64)                       # (D / 4, 16), exact halves
+    hi, lo = e.max(1).sum(), e.min(1).sum()
+    A = np.maximum(e.max(1), -e.min(1)).sum()
+    span = max(np.nextafter(hi + float(k1), np.inf), -np.nextafter(lo + float(k1), -np.inf))
+    m = (span + A * 2.0 ** -16) * (1 + 2.0 ** -22)
+    return np.nextafter(np.float32(m), np.float32(np.inf)) if np.float32(m) < m else np.float32(m)
+
+
+@pytest.mark.parametrize("D", [128, 192, 768])
+def test_lut_bound_covers_every_code(D):
+    """|fl(ip1 + k1)| <= M for the LUT estimator, with ip1 from the oracle's fp32 table sums
+    (cora_oracle_ip_lut), on random codes and on the codes that select each group's largest
+    or smallest entry (the ends of the range), for queries of several scales."""
+    import py_oracle as po
+    rng = np.random.default_rng(D)
+    W = D // 32
+    for trial in range(40):
+        qr = (rng.standard_normal(D) * 10.0 ** rng.uniform(-3, 2)).astype(np.float32)
+        lut = np.empty(D * 4, np.uint16)
+        po.lib().cora_oracle_query_lut(qr, D, lut)
+        tab = lut.view(np.float16).reshape(D // 4, 16)
+        k1 = np.float32(np.float32(qr.astype(np.float64).sum()) * np.float32(-0.5))
+        M = lut_bound(tab, k1)
+        codes = [rng.integers(0, 2 ** 32, W, dtype=np.uint64).astype(np.uint32) for _ in range(30)]
+        for pick in (np.argmax, np.argmin):  # the extreme pattern of every group
+            pats = pick(tab.astype(np.float32), axis=1)
+            words = np.zeros(W, np.uint32)
+            for g, pval in enumerate(pats):
+                w, n = divmod(g, 8)
+                words[w] |= np.uint32(int(pval) << (28 - 4 * n))
+            codes.append(words)
+        for words in codes:
+            ip1 = np.float32(po.lib().cora_oracle_ip_lut(np.ascontiguousarray(words), lut, D))
+            t = np.float32(ip1 + k1)
+            assert abs(t) <= M, (trial, t, M)
