@@ -131,7 +131,8 @@ int main(int argc, char **argv) {
         }
         std::unique_ptr<RecallEvaluator> evaluator;
         if (!recall_once)
-            evaluator = std::make_unique<RecallEvaluator>(query.data.data(), nq, dim, gt, topk, recall_base);
+            evaluator = std::make_unique<RecallEvaluator>(query.data.data(), nq, dim, gt, topk,
+                                                          recall_base, index.get_metric());
         validate_benchmark_shape(nq, dim, gt.rows, gt.cols, shape.dim, topk, rounds);
         const auto nprobes = parse_nprobes(opt.text("nprobes", ""), shape.num_clusters);
         const std::size_t max_nprobe = *std::max_element(nprobes.begin(), nprobes.end());
@@ -223,7 +224,8 @@ int main(int argc, char **argv) {
         }
         if (recall_once) {
             std::cout << "[RecallSchedule] QPS rounds complete; evaluating saved results" << std::endl;
-            evaluator = std::make_unique<RecallEvaluator>(query.data.data(), nq, dim, gt, topk, recall_base);
+            evaluator = std::make_unique<RecallEvaluator>(query.data.data(), nq, dim, gt, topk,
+                                                          recall_base, index.get_metric());
             for (std::size_t l = 0; l < L; ++l) {
                 recall[0][l] = evaluator->evaluate(saved[l]);
                 std::cout << "[RecallPoint] nprobe=" << nprobes[l] << " source_round=1 recall=" << recall[0][l]

@@ -35,7 +35,8 @@ EXPORTS = [
     "cora_get_vanguard_size", "cora_set_queue_capacity", "cora_set_queue_spill_capacity",
     "cora_get_queue_capacity", "cora_set_profiling", "cora_set_candidate_stats",
     "cora_set_gpu_filter_timing", "cora_set_cross_query_reuse", "cora_set_cpu_secondary_filter",
-    "cora_set_ip_kernel_type", "cora_get_ip_kernel_type", "cora_set_refine_full_code",
+    "cora_set_ip_kernel_type", "cora_get_ip_kernel_type", "cora_set_metric", "cora_get_metric",
+    "cora_set_refine_full_code",
     "cora_get_refine_full_code", "cora_get_last_submitted_count",
     "cora_get_last_refined_count", "cora_get_last_spilled_count", "cora_get_last_gpu_filter_ms",
     "cora_debug_copy", "cora_get_last_stage_ms", "cora_stage_totals", "cora_stage_reset",
@@ -84,6 +85,8 @@ def _bind(L):
                "cora_set_cross_query_reuse", "cora_set_cpu_secondary_filter", "cora_set_ip_kernel_type"):
         _sig(L, _n, None, _p, C.c_int)
     _sig(L, "cora_get_ip_kernel_type", C.c_int, _p)
+    _sig(L, "cora_set_metric", C.c_int, _p, C.c_int)
+    _sig(L, "cora_get_metric", C.c_int, _p)
     _sig(L, "cora_set_refine_full_code", None, _p, C.c_int)
     _sig(L, "cora_get_refine_full_code", C.c_int, _p)
     _sig(L, "cora_get_last_submitted_count", _u64, _p)
@@ -223,7 +226,9 @@ class HybridIndex:
                                                 *[_ptr(a) for a in arrs]))
 
     def load_search_data(self, sd: dict):
-        """Load the arrays of a SearchData-layout dict (keys as oracle/py_oracle.py)."""
+        """Load the arrays of a SearchData-layout dict (keys as oracle/py_oracle.py); its
+        optional "metric" (0 L2, 1 inner product) is applied too."""
+        self.set_metric(int(sd.get("metric", 0)))
         self.load_from_raw_pointers(sd["num"], sd["dim"], sd["D"], sd["nlist"], sd["ex_bits"],
                                     sd["centroids"], sd["rotator"], sd["short_data"],
                                     sd["short_factors"], sd["long_codes"], sd["ex_factors"],
@@ -367,6 +372,12 @@ class HybridIndex:
     def set_ip_kernel_type(self, t): _lib.cora_set_ip_kernel_type(self._h, int(t))
     def get_ip_kernel_type(self): return int(_lib.cora_get_ip_kernel_type(self._h))
 
+    def set_metric(self, metric: int):
+        """0 squared L2, 1 inner product (set from the file header by load_index_file)."""
+        _check(_lib.cora_set_metric(self._h, int(metric)))
+
+    def get_metric(self) -> int: return int(_lib.cora_get_metric(self._h))
+
     def set_refine_full_code(self, on):
         """Refine with <q', 128 b + u> instead of the reference's 128 ip1 + ip2 (opt-in)."""
         _lib.cora_set_refine_full_code(self._h, int(bool(on)))
@@ -423,6 +434,7 @@ class HybridIndex:
             "cand_gids": (7, np.uint32, (nq, self.candidate_capacity())),
             "approx": (8, np.float32, (nq, (info["nlist"] + 3) // 4 * 4)),
             "lut": (9, np.uint16, (nq, D // 4, 16)),
+            "probe_gadd": (10, np.float32, (nq, nprobe)),
         }[what]
         out = np.empty(spec[2], spec[1])
         _check(_lib.cora_debug_copy(self._h, spec[0], _ptr(out), out.nbytes))

@@ -106,10 +106,11 @@ def _words(bits: torch.Tensor) -> torch.Tensor:
 
 def build_index(data, centroids, assign, seed: int = 7, device="cpu", chunk: int = 1 << 20,
                 keep_bits: bool = False, rotator=None, rotated_centroids=None,
-                t_const: float | None = None) -> dict:
-    """Build an 8-bit (1 + 7 ex bits) L2 index. data n x dim, centroids nlist x dim,
-    assign n cluster ids. Returns the adapter layout dict (see oracle/py_oracle.py keys),
-    plus 'bits' (n x D bool, cluster order) when keep_bits.
+                t_const: float | None = None, metric: int = 0) -> dict:
+    """Build an 8-bit (1 + 7 ex bits) index, metric 0 (squared L2) or 1 (inner product).
+    data n x dim, centroids nlist x dim, assign n cluster ids. Returns the adapter layout
+    dict (see oracle/py_oracle.py keys), plus 'bits' (n x D bool, cluster order) when
+    keep_bits.
 
     The random pieces are seeded from `seed`; to quantise against another builder's choices
     (e.g. the reference's, which draws them unseeded) pass them in: `rotator` (dim x D),
@@ -149,7 +150,7 @@ def build_index(data, centroids, assign, seed: int = 7, device="cpu", chunk: int
         x = data[idx].to(dev).float()
         xr = (x.double() @ P.double()).float()
         cl = a_sorted[s:e]
-        bits, f, code, ef = _quantize_rows(xr, crot[cl], t_const)
+        bits, f, code, ef = _quantize_rows(xr, crot[cl], t_const, metric=metric)
         fac[s:e], exf[s:e], lcs[s:e] = f, ef, _pack_ex7(code)
         if keep_bits:
             all_bits[s:e] = bits
@@ -164,17 +165,20 @@ def build_index(data, centroids, assign, seed: int = 7, device="cpu", chunk: int
                short_data=short.to(torch.int64).cpu().numpy().astype(np.uint32),
                short_factors=fac.cpu().numpy(), long_codes=lcs.cpu().numpy().reshape(-1),
                ex_factors=exf.cpu().numpy(), ids=order.cpu().numpy().astype(np.uint32),
-               sizes=sizes.cpu().numpy().astype(np.uint64), t_const=t_const)
+               sizes=sizes.cpu().numpy().astype(np.uint64), t_const=t_const, metric=metric)
     if keep_bits:
         out["bits"] = all_bits.cpu().numpy()
     return out
 
 
-def _quantize_rows(xr, crows, t_const, ex_bits=7):
-    """Quantise rotated vectors xr (m x D) against their rotated centroids crows (m x D), L2:
+def _quantize_rows(xr, crows, t_const, ex_bits=7, metric=0):
+    """Quantise rotated vectors xr (m x D) against their rotated centroids crows (m x D):
     one-bit code b = [r > 0] and factors (rabitq_impl.hpp:76-137), ex code with the constant
-    rescale factor and its factors (rabitq_impl.hpp:379-500). Returns bits (m x D bool),
-    factors (m x 3 f32), ex codes (m x D uint8 in [0, 127]) and ex factors (m x 2 f32)."""
+    rescale factor and its factors (rabitq_impl.hpp:379-500), for squared L2 (metric 0) or
+    inner product (metric 1, the METRIC_IP branches: f_add = 1 - <r, c> + |r|^2 <c, xu> /
+    <r, xu>, f_rescale = -|r|^2 / <r, xu>, f_error without the factor 2, f_rescale_ex =
+    -|r| / ipnorm). Returns bits (m x D bool), factors (m x 3 f32), ex codes (m x D uint8 in
+    [0, 127]) and ex factors (m x 2 f32)."""
     r = xr.double() - crows.double()
     c = crows.double()
     D = r.shape[1]
@@ -187,8 +191,13 @@ def _quantize_rows(xr, crows, t_const, ex_bits=7):
     ip_resi = torch.where(ip_resi == 0, torch.full_like(ip_resi, float("inf")), ip_resi)
     xu_sq = (xu * xu).sum(1)
     tmp_err = l2_norm * EPS0 * torch.sqrt(((l2_sqr * xu_sq) / (ip_resi * ip_resi) - 1) / (D - 1))
-    fac = torch.stack([l2_sqr + 2 * l2_sqr * ip_cent / ip_resi, -2 * l2_sqr / ip_resi,
-                       2 * tmp_err], 1).float()
+    ip_rc = (r * c).sum(1)
+    if metric == 1:
+        fac = torch.stack([1 - ip_rc + l2_sqr * ip_cent / ip_resi, -l2_sqr / ip_resi, tmp_err],
+                          1).float()
+    else:
+        fac = torch.stack([l2_sqr + 2 * l2_sqr * ip_cent / ip_resi, -2 * l2_sqr / ip_resi,
+                           2 * tmp_err], 1).float()
     o = (r / l2_norm.clamp_min(1e-300)[:, None]).abs()
     code = torch.clamp((t_const * o + 1e-5).floor(), max=(1 << ex_bits) - 1).to(torch.int64)
     ipnorm = ((code.double() + 0.5) * o).sum(1)
@@ -201,7 +210,11 @@ def _quantize_rows(xr, crows, t_const, ex_bits=7):
     ip_resi_ex = (r * xu_ex).sum(1)
     ip_cent_ex = (c * xu_ex).sum(1)
     ip_resi_ex = torch.where(ip_resi_ex == 0, torch.full_like(ip_resi_ex, float("inf")), ip_resi_ex)
-    exf = torch.stack([l2_sqr + 2 * l2_sqr * ip_cent_ex / ip_resi_ex, inv * -2 * l2_norm], 1).float()
+    if metric == 1:
+        exf = torch.stack([1 - ip_rc + l2_sqr * ip_cent_ex / ip_resi_ex, inv * -l2_norm], 1).float()
+    else:
+        exf = torch.stack([l2_sqr + 2 * l2_sqr * ip_cent_ex / ip_resi_ex, inv * -2 * l2_norm],
+                          1).float()
     return bits, fac, code.to(torch.uint8), exf
 
 
@@ -212,7 +225,7 @@ def write_index_file(path, sd: dict, bits: np.ndarray):
     sizes = sd["sizes"].astype(np.uint64)
     with open(path, "wb") as f:
         f.write(struct.pack("<4Q", n, dim, nlist, 7))
-        f.write(struct.pack("<BB", 0, 0))
+        f.write(struct.pack("<BB", 0, int(sd.get("metric", 0))))  # matrix rotator, metric
         f.write(sizes.tobytes())
         f.write(np.ascontiguousarray(sd["rotator"], np.float32).tobytes())
         f.write(np.ascontiguousarray(sd["centroids"], np.float32).tobytes())

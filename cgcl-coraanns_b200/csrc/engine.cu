@@ -284,6 +284,10 @@ struct Engine {
     // the reference's default), 1 Bitwise (the integer estimator, this engine's default)
     int ip_kernel_type = 1;
     bool lut_mode() const { return ip_kernel_type == 0; }
+    // distance (MetricType of ivf.hpp, defines.hpp:65): 0 squared L2, 1 inner product
+    // (distances 1 - <q, x> as estimated by the reference's IP factors); set by the index
+    // file, or by cora_set_metric for indexes loaded from raw arrays
+    int metric = 0;
     // Upper bound on the HBM buffer holding the vanguard pairs' lower bounds; larger
     // worst cases fall back to rescanning the vanguard clusters.
     uint64_t lows_budget = 16ull << 30;
@@ -293,7 +297,7 @@ struct Engine {
     // workspace
     bool ws_ready = false;
     uint64_t ws_q = 0, ws_k = 0, ws_np = 0, ws_vg = 0, cap = 0;
-    DevBuf<float> raw_q, qr, qnorm2, gmat, cmin, probe_g, T0, T1, Tcap, out_d;
+    DevBuf<float> raw_q, qr, qnorm2, gmat, cmin, probe_g, probe_ga, T0, T1, Tcap, out_d;
     DevBuf<QueryScalars> scal;
     DevBuf<float> ipm;   // per query: bound on |fl(ip1 + k1)| for the pruning test
     DevBuf<__half> lut;  // per query: LUT estimator tables (D / 4 groups x 16)
@@ -335,11 +339,12 @@ struct Engine {
         cudaStream_t st = nullptr;
         int wsl = 0, twl = 0;
         bool reuse = false, full_code = false, lut = false;
+        int metric = 0;
         bool same(const GraphKey &o) const {
             return d_q == o.d_q && nq == o.nq && k == o.k && np == o.np && ws_gen == o.ws_gen &&
                    vanguard == o.vanguard && d_od == o.d_od && d_oi == o.d_oi && st == o.st &&
                    wsl == o.wsl && twl == o.twl && reuse == o.reuse &&
-                   full_code == o.full_code && lut == o.lut;
+                   full_code == o.full_code && lut == o.lut && metric == o.metric;
         }
     };
     GraphKey graph_key;
@@ -486,6 +491,8 @@ struct Engine {
                              uint64_t stride, uint64_t offset) {
         if (mapping && bdim == dim && rows && stride < bdim * 4)
             fail(CORA_EINVAL, "exact base row stride is shorter than a row");
+        if (mapping && metric == 1)
+            fail(CORA_EINVAL, "exact refinement is defined for L2 indexes only");
         xb_map = mapping;
         xb_rows = rows;
         xb_dim = bdim;
@@ -639,6 +646,7 @@ struct Engine {
         qnorm2.alloc(max_q);
         probe_ids.alloc(max_q * max_np);
         probe_g.alloc(max_q * max_np);
+        probe_ga.alloc(max_q * max_np);
         T0.alloc(max_q);
         T1.alloc(max_q);
         Tcap.alloc(max_q);
@@ -684,7 +692,8 @@ struct Engine {
         ++ws_gen;
         ws_ready = false;
         ws_q = ws_k = ws_np = ws_vg = cap = 0;
-        for (auto *b : {&raw_q, &qr, &qnorm2, &gmat, &cmin, &probe_g, &T0, &T1, &Tcap, &out_d})
+        for (auto *b : {&raw_q, &qr, &qnorm2, &gmat, &cmin, &probe_g, &probe_ga, &T0, &T1, &Tcap,
+                        &out_d})
             b->release();
         scal.release();
         ipm.release();
@@ -781,6 +790,13 @@ struct Engine {
                  "--queue-spill-capacity, or reduce --query-chunk.");
         if (h_err & kDevWaitTimeout) fail(CORA_ERUNTIME, "a device-side wait timed out");
         if (h_err) fail(CORA_ERUNTIME, "device reported an error");
+    }
+
+    void set_metric(int m) {
+        if (m != 0 && m != 1) fail(CORA_EINVAL, "metric must be 0 (L2) or 1 (inner product)");
+        if (m == 1 && xb_map)
+            fail(CORA_EINVAL, "exact refinement is defined for L2 indexes only");
+        metric = m;
     }
 
     void require_whole_index() const {
@@ -972,7 +988,8 @@ SearchView Engine::search_view() const {
     return SearchView{static_cast<int>(last_nq), static_cast<int>(last_k), static_cast<int>(last_np),
                       static_cast<int>(veff), static_cast<int>(keep), static_cast<int>(cap),
                       last_dq, scal.p, ipm.p, planes.p, lut.p, lut_mode() ? 1 : 0, qr.p,
-                      probe_ids.p, probe_g.p, T0.p, Tcap.p, T1.p, bound.p,
+                      probe_ids.p, probe_g.p, metric == 1 ? probe_ga.p : probe_g.p, T0.p, Tcap.p,
+                      T1.p, bound.p,
                       cand_cnt.p, seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n,
                       lows_top.p, err.p, warp_select_limit, topk_warp_limit,
                       refine_full_code ? 1 : 0};
@@ -1003,6 +1020,7 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     key.reuse = cross_query_reuse;
     key.full_code = refine_full_code;
     key.lut = lut_mode();
+    key.metric = metric;
     if (!graph_exec || !graph_key.same(key)) {
         drop_graph();
         CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
@@ -1075,6 +1093,12 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
         // select_fallback (>= 1 + nq words) is free until the vanguard stage
         launch_guarded_select(gmat.p, cmin.p, nlist, nq, np, qr.p, qnorm2.p, centroids.p, cmax,
                               D, probe_ids.p, probe_g.p, select_fallback.p, num_sms, st);
+        if (metric == 1) {  // inner product: the additive term -<q', c'> of every probe
+            ip_gadd_kernel<<<static_cast<unsigned>((nq + 7) / 8), 256, 0, st>>>(
+                qr.p, centroids.p, probe_ids.p, static_cast<int>(nq), static_cast<int>(np),
+                static_cast<int>(D), probe_ga.p);
+            CUDA_TRY(cudaGetLastError());
+        }
     }
     mark(3, st);
     const bool lows_mode = lows.n > 0;
@@ -1177,7 +1201,8 @@ void Engine::group_pairs(int r_lo, int r_hi, bool prune, cudaStream_t st) {
     CUDA_TRY(cudaMemsetAsync(item_counter.p, 0, 4, st));
     const int ppi = !cross_query_reuse ? 1 : (lut_mode() ? lut_pairs_per_item(G16) : kMaxPairsPerItem);
     PairPrune pp{};
-    if (prune) pp = PairPrune{cl_range.p, probe_g.p, ipm.p, T1.p};
+    if (prune)
+        pp = PairPrune{cl_range.p, probe_g.p, metric == 1 ? probe_ga.p : probe_g.p, ipm.p, T1.p};
     count_pairs_kernel<<<blocks, 256, 0, st>>>(probe_ids.p, inq, inp, r_lo, r_hi, own, pp,
                                                pair_cnt.p);
     scan_pairs_kernel<<<1, 1024, 0, st>>>(pair_cnt.p, static_cast<int>(nlist), ppi, pair_off.p,
@@ -1271,6 +1296,7 @@ void Engine::debug_copy(int what, void *out, uint64_t bytes) {
         case 6: copy(scal.p, nq * 16); break;
         case 8: copy(gmat.p, nq * approx_ld(nlist) * 4); break;
         case 9: copy(lut.p, nq * 4 * D * 2); break;
+        case 10: copy(metric == 1 ? probe_ga.p : probe_g.p, nq * np * 4); break;
         case 7: {
             if (bytes != nq * cap * 4) fail(CORA_EINVAL, "debug_copy: byte count does not match");
             std::vector<uint64_t> rec(nq * cap);
@@ -1300,6 +1326,7 @@ namespace {
 // clusters, and every centroid is kept (each shard probes all of them).
 struct FileIndex {
     uint64_t num = 0, dim = 0, nlist = 0, ex_bits = 0, D = 0;
+    int metric = 0;  // MetricType byte of the header: 0 L2, 1 IP
     uint64_t full_num = 0, kept = 0, bytes_read = 0;
     std::vector<uint64_t> sizes;
     std::vector<uint8_t> owned;
@@ -1367,6 +1394,8 @@ FileIndex read_index_file(const char *path, uint32_t rank = 0, uint32_t world = 
     f.nlist = hdr[2];
     f.ex_bits = hdr[3];
     if (types[0] != 0) fail(CORA_EINVAL, "only matrix-rotator indexes are supported");
+    if (types[1] > 1) fail(CORA_EINVAL, "unknown metric type in the IVF index header");
+    f.metric = types[1];
     if (!f.full_num || !f.dim || !f.nlist || f.ex_bits > 8)
         fail(CORA_EINVAL, "invalid IVF index header");
     f.D = (f.dim + 63) / 64 * 64;
@@ -1567,9 +1596,11 @@ int cora_load_index_file(cora_engine *engine, const char *path) {
                                f.rotator.data(), f.short_data.data(), f.short_factors.data(),
                                f.long_codes.data(), f.ex_factors.data(), f.ids.data(),
                                f.sizes.data(), f.owned, f.kept);
+            e.set_metric(f.metric);
             return;
         }
         cora::FileIndex f = cora::read_index_file(path);
+        e.set_metric(f.metric);
         e.load_any(f.num, f.dim, f.D, f.nlist, f.ex_bits, f.centroids.data(), f.rotator.data(),
                f.short_data.data(), f.short_factors.data(), f.long_codes.data(), f.ex_factors.data(),
                f.ids.data(), f.sizes.data());
@@ -1807,6 +1838,12 @@ void cora_set_ip_kernel_type(cora_engine *engine, int kernel_type) {
 }
 int cora_get_ip_kernel_type(const cora_engine *engine) {
     return engine && engine->e ? engine->e->ip_kernel_type : 0;
+}
+int cora_set_metric(cora_engine *engine, int metric) {
+    return guarded([&] { eng(engine).set_metric(metric); });
+}
+int cora_get_metric(const cora_engine *engine) {
+    return engine && engine->e ? engine->e->metric : -1;
 }
 void cora_set_refine_full_code(cora_engine *engine, int enabled) {
     if (engine && engine->e) engine->e->refine_full_code = enabled != 0;

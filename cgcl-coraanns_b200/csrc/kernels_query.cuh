@@ -421,6 +421,35 @@ __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
         }
     }
 }
+// Inner-product metric: the estimator's additive term of every (query, probe) pair,
+// g_add = -<q', c'> (index/query.hpp:99-108; the reference CPU path probes by L2 distance and
+// takes the dot product with the probed centroid, ivf/ivf.hpp:681-706), as the fp32 rounding
+// of the fp64 fma chain over the dimensions in ascending order. One warp per query, one
+// lane per probe.
+__global__ void __launch_bounds__(256) ip_gadd_kernel(const float *__restrict__ qr,
+                                                      const float *__restrict__ cent,
+                                                      const int *__restrict__ probe_ids, int nq,
+                                                      int nprobe, int D,
+                                                      float *__restrict__ probe_ga) {
+    const int lane = threadIdx.x & 31;
+    const int q = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (q >= nq) return;
+    const float *x = qr + (size_t)q * D;
+    for (int r = lane; r < nprobe; r += 32) {
+        const float4 *c4 = reinterpret_cast<const float4 *>(
+            cent + (size_t)probe_ids[(size_t)q * nprobe + r] * D);
+        double acc = 0.0;
+        for (int j0 = 0; j0 < D; j0 += 4) {
+            const float4 c = __ldg(c4 + j0 / 4);
+            acc = __fma_rn((double)x[j0], (double)c.x, acc);
+            acc = __fma_rn((double)x[j0 + 1], (double)c.y, acc);
+            acc = __fma_rn((double)x[j0 + 2], (double)c.z, acc);
+            acc = __fma_rn((double)x[j0 + 3], (double)c.w, acc);
+        }
+        probe_ga[(size_t)q * nprobe + r] = -__double2float_rn(acc);
+    }
+}
+
 __host__ __device__ inline int guarded_select_cap(int nprobe) {
     const int c = 2 * nprobe > 1024 ? 2 * nprobe : 1024;
     return c < 8192 ? c : 8192;

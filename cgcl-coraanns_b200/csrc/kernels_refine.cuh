@@ -28,7 +28,7 @@ constexpr int kRefineThreads = CORA_REFINE_THREADS;
 
 struct ProbeInfo {  // per (query, probe rank), staged in shared memory by refine_kernel
     uint32_t start, size;
-    float g;
+    float g;  // the additive query term g_add
 };
 
 // The 8-bit codes c = 128 b + u of dims d0 .. d0 + 3 of one 64-dim block, as the bytes of a
@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
     const int np = mode == 0 ? sv.veff : sv.nprobe;
     for (int r = threadIdx.x; r < np; r += blockDim.x) {
         const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
-        pinfo[r] = ProbeInfo{ix.cl_start[c], ix.cl_size[c], sv.probe_g[(size_t)q * sv.nprobe + r]};
+        pinfo[r] = ProbeInfo{ix.cl_start[c], ix.cl_size[c], sv.probe_ga[(size_t)q * sv.nprobe + r]};
     }
     __syncthreads();
     const float kb = sv.scal[q].kb, width = sv.scal[q].width;

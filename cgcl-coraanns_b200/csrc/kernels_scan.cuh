@@ -14,8 +14,10 @@
 //          = sum_i b_i qint_i, evaluated as byte dot products (dp4a) for D <= 128 and as
 //            bit-plane popcounts above (both exact in int32)
 //   ip1    = width * ip_int
-//   low    = (f_add + g) + f_rescale * (ip1 + k1) - f_error * sqrt(max(g, 0))
-// or, with the LUT estimator (the reference's default kernel type, filter_kernels.cuh:
+//   low    = (f_add + g_add) + f_rescale * (ip1 + k1) - f_error * sqrt(max(g, 0))
+// with g the squared L2 distance to the probed centroid and g_add = g (L2) or -<q', c'>
+// (inner product; the reference CPU path's set_g_add, index/query.hpp:99-108 and
+// ivf/ivf.hpp:699-706); or, with the LUT estimator (the reference's default kernel type, filter_kernels.cuh:
 // 283-306, 655-696), ip1 = acc0 + acc1 from the query's fp16 tables (lut_build_kernel):
 // nibble n of code word w (bits 31 - 4n .. 28 - 4n, dims 32w + 4n ..) looks up entry
 // (8w + n, nibble) and is added, in fp32 and in order, to acc0 for even n, acc1 for odd n.
@@ -99,7 +101,10 @@ struct SearchView {
     int lut_mode;                // 1: the scan's ip1 comes from the LUT estimator
     const float *qr;             // nq x D
     const int *probe_ids;        // nq x nprobe
-    const float *probe_g;        // nq x nprobe
+    const float *probe_g;        // nq x nprobe: squared L2 distance to the probed centroid
+    // nq x nprobe: the estimator's additive query term g_add (L2: probe_g itself; inner
+    // product: -<q', c'>); its error term is always sqrt(probe_g)
+    const float *probe_ga;
     const float *T0;             // nq, seeded thresholds (never modified by a search)
     float *Tcap;                 // nq, thresholds after the search (capture_thresholds)
     float *T1;                   // nq
@@ -142,15 +147,17 @@ __device__ __forceinline__ bool range_at_least(float4 fr, float g, float M, floa
 // test scan_kernel also applies per item and per chunk.
 struct PairPrune {
     const float4 *cl_range;      // nlist
-    const float *probe_g;        // nq x nprobe
+    const float *probe_g;        // nq x nprobe (error term)
+    const float *probe_ga;       // nq x nprobe (additive term)
     const float *ipm;            // nq
     const float *T1;             // nq
 };
 __device__ __forceinline__ bool pair_pruned(const PairPrune &pp, int q, int r, int c,
                                             int nprobe) {
     if (!pp.cl_range) return false;
-    const float g = pp.probe_g[(size_t)q * nprobe + r];
-    return range_at_least(pp.cl_range[c], g, pp.ipm[q], __fsqrt_rn(fmaxf(g, 0.0f)), pp.T1[q]);
+    const size_t at = (size_t)q * nprobe + r;
+    return range_at_least(pp.cl_range[c], pp.probe_ga[at], pp.ipm[q],
+                          __fsqrt_rn(fmaxf(pp.probe_g[at], 0.0f)), pp.T1[q]);
 }
 
 // ---- per-cluster query grouping (CSR of (query, probe rank) pairs by cluster) --------
@@ -641,10 +648,11 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
             const uint32_t pr = pairs[item.pair_begin + threadIdx.x];
             const int q = static_cast<int>(pr >> 16), r = static_cast<int>(pr & 0xFFFFu);
             const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
+            const float ga = sv.probe_ga[(size_t)q * sv.nprobe + r];
             const QueryScalars qs = sv.scal[q];
             s_q[threadIdx.x] = q;
             s_r[threadIdx.x] = r;
-            s_par[threadIdx.x] = make_float4(qs.width, g, qs.k1, __fsqrt_rn(fmaxf(g, 0.0f)));
+            s_par[threadIdx.x] = make_float4(qs.width, ga, qs.k1, __fsqrt_rn(fmaxf(g, 0.0f)));
             if (kWriteLows) {
                 // slice of this vanguard pair (offset 0 when the buffer is full: the search
                 // reports the overflow, and the readers of the slice stay in bounds)
@@ -908,7 +916,8 @@ __global__ void __launch_bounds__(256) filter_list_kernel(IndexView ix, SearchVi
         const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
         if (!owned || owned[c]) {
             const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
-            keep = !range_at_least(ix.cl_range[c], g, sv.ipm[q], __fsqrt_rn(fmaxf(g, 0.0f)),
+            const float ga = sv.probe_ga[(size_t)q * sv.nprobe + r];
+            keep = !range_at_least(ix.cl_range[c], ga, sv.ipm[q], __fsqrt_rn(fmaxf(g, 0.0f)),
                                    sv.T1[q]);
         }
     }
@@ -1081,6 +1090,7 @@ __global__ void __launch_bounds__(kScanThreads) vanguard_rescan_kernel(
     const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
     if (owned && !owned[c]) return;
     const float g = sv.probe_g[(size_t)q * sv.nprobe + r];
+    const float ga = sv.probe_ga[(size_t)q * sv.nprobe + r];
     const uint32_t s = ix.cl_start[c];
     const int n = static_cast<int>(ix.cl_size[c]);
     const QueryScalars qs = sv.scal[q];
@@ -1132,7 +1142,7 @@ __global__ void __launch_bounds__(kScanThreads) vanguard_rescan_kernel(
                 const int ip = ip_int_from_planes<G16>(code, s_planes, code_bias<G16>(code));
                 ip1 = __fadd_rn(__fmul_rn(qs.width, (float)ip), 0.0f);
             }
-            const float low = lower_bound_dist(f, ip1, g, qs.k1, gerr);
+            const float low = lower_bound_dist(f, ip1, ga, qs.k1, gerr);
             if (low < T0) {
                 atomicAdd(&n_total, 1);
                 tk.offer(make_key(low, s + v0 + i));

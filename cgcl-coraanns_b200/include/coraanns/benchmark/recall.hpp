@@ -1,9 +1,9 @@
 // recall@k for the coraanns_search CLI, with the reference evaluator's semantics
 // (include/coraanns/benchmark/recall.hpp:52-275): a returned id counts once; it is a hit if it
 // is among the ground-truth top-k ids, or (distance-aware mode, with a base file) if its exact
-// fp64 squared L2 distance is <= that of the ground truth's rank-k neighbour. Ids that are
-// out of range or equal to UINT32_MAX are misses. Only the L2 metric is searched by this
-// engine, so only L2 is evaluated.
+// fp64 score is as good as the ground truth's rank-k neighbour's: squared L2 distance <= it
+// (metric 0), or inner product >= it (metric 1). Ids that are out of range or equal to
+// UINT32_MAX are misses.
 #pragma once
 
 #include <algorithm>
@@ -28,10 +28,12 @@ struct RecallCounts {
 class RecallEvaluator {
   public:
     RecallEvaluator(const float *queries, std::size_t nq, std::size_t dim,
-                    const Matrix<uint32_t> &gt, std::size_t topk, const std::string &base_file)
-        : queries_(queries), nq_(nq), dim_(dim), topk_(topk) {
+                    const Matrix<uint32_t> &gt, std::size_t topk, const std::string &base_file,
+                    int metric = 0)
+        : queries_(queries), nq_(nq), dim_(dim), topk_(topk), metric_(metric) {
         if (!queries || !nq || !dim || !topk || gt.rows != nq || gt.cols < topk)
             throw std::invalid_argument("Invalid query/GT shape for recall@k");
+        if (metric != 0 && metric != 1) throw std::invalid_argument("Recall metric must be L2 or IP");
         if (!base_file.empty()) {
             base_ = std::make_unique<MappedVectors>(base_file);
             if (base_->dim() != dim) throw std::invalid_argument("Recall base and query dimensions differ");
@@ -46,14 +48,15 @@ class RecallEvaluator {
                     throw std::invalid_argument("Invalid GT ID for recall base");
             }
             if (base_) {
-                radius_[q] = l2(q, t[topk - 1]);
+                radius_[q] = score(q, t[topk - 1]);
                 if (!finite(radius_[q])) throw std::invalid_argument("Non-finite query/GT distance");
             }
             std::sort(t, t + topk);
             if (std::adjacent_find(t, t + topk) != t + topk)
                 throw std::invalid_argument("GT top-k contains duplicate IDs");
         }
-        std::cout << "[Recall] mode=" << (base_ ? "distance-aware" : "id") << " metric=l2 topk=" << topk
+        std::cout << "[Recall] mode=" << (base_ ? "distance-aware" : "id")
+                  << " metric=" << (metric_ == 0 ? "l2" : "ip") << " topk=" << topk
                   << " base=" << (base_ ? base_file : "none (use --recall-base for distance checks)")
                   << "\n";
     }
@@ -71,9 +74,9 @@ class RecallEvaluator {
             if (std::binary_search(t, t + topk_, id)) {
                 ++c.id_hits;
             } else if (base_) {
-                const double s = l2(q, id);
+                const double s = score(q, id);
                 ++c.exact_checks;
-                c.distance_hits += finite(s) && s <= radius_[q];
+                c.distance_hits += finite(s) && (metric_ == 0 ? s <= radius_[q] : s >= radius_[q]);
             }
         }
         return c;
@@ -108,19 +111,25 @@ class RecallEvaluator {
         std::memcpy(&b, &v, 8);
         return (b & 0x7ff0000000000000ULL) != 0x7ff0000000000000ULL;
     }
-    double l2(std::size_t q, uint32_t id) const {
+    // exact fp64 score: squared L2 distance (metric 0) or inner product (metric 1)
+    double score(std::size_t q, uint32_t id) const {
         const float *a = queries_ + q * dim_;
         const float *b = base_->row(id);
         double s = 0.0;
         for (std::size_t d = 0; d < dim_; ++d) {
-            const double e = static_cast<double>(a[d]) - b[d];
-            s += e * e;
+            if (metric_ == 0) {
+                const double e = static_cast<double>(a[d]) - b[d];
+                s += e * e;
+            } else {
+                s += static_cast<double>(a[d]) * b[d];
+            }
         }
         return s;
     }
 
     const float *queries_;
     std::size_t nq_, dim_, topk_;
+    int metric_ = 0;
     std::unique_ptr<MappedVectors> base_;
     std::vector<uint32_t> truth_;
     std::vector<double> radius_;

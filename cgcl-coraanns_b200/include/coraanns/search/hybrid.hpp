@@ -89,6 +89,10 @@ class HybridIndex {
     KernelType get_ip_kernel_type() const {
         return static_cast<KernelType>(cora_get_ip_kernel_type(engine_));
     }
+    // Distance (this engine's addition; the reference's hybrid path is L2 only): 0 squared
+    // L2, 1 inner product. Set from the file header by load_index_file.
+    void set_metric(int metric) { detail::check(cora_set_metric(engine_, metric)); }
+    int get_metric() const { return cora_get_metric(engine_); }
     // Refinement form (this engine's addition): false = the reference's 128 ip1 + ip2.
     void set_refine_full_code(bool enabled) { cora_set_refine_full_code(engine_, enabled ? 1 : 0); }
     bool get_refine_full_code() const { return cora_get_refine_full_code(engine_) != 0; }

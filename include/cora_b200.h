@@ -147,6 +147,17 @@ void cora_set_cpu_secondary_filter(cora_engine *engine, int enabled);
 void cora_set_ip_kernel_type(cora_engine *engine, int kernel_type);
 int cora_get_ip_kernel_type(const cora_engine *engine);
 
+/* Distance of the index (no counterpart in the reference's hybrid path, which is L2 only;
+ * the reference's CPU path supports both, ivf.hpp:681-706): 0 squared L2 (default), 1 inner
+ * product, where distances are the reference IP factors' estimates of 1 - <q, x> and the
+ * additive query term is -<q', c'> (index/query.hpp:99-108; probes stay the nearest centroids
+ * by L2 distance). cora_load_index_file sets it from the file header's MetricType; indexes
+ * loaded from raw arrays must be built for the metric set here. CORA_EINVAL for other values
+ * or for inner product with exact refinement enabled. Takes effect from the next search.
+ * cora_get_metric returns -1 for a NULL engine. */
+int cora_set_metric(cora_engine *engine, int metric);
+int cora_get_metric(const cora_engine *engine);
+
 /* Refinement form (no reference counterpart; the reference always uses its default).
  * 0 (default): the reference's expression, ex = (f_add_ex + g) + f_rescale_ex *
  * ((128 ip1 + ip2) + kb), ip1 = width * ip_int the scan's integer estimate of <q', b>
@@ -172,7 +183,9 @@ float cora_get_last_gpu_filter_ms(const cora_engine *engine);
  * 7 candidate gids (nq x cap u32, per query sorted ascending, unused slots 0xFFFFFFFF),
  * 8 approximate coarse distances of the tensor-core probe GEMM (nq x ld f32, ld = nlist
  * rounded up to a multiple of 4; rows the exact fallback recomputed hold exact values),
- * 9 LUT estimator tables (nq x D/4 x 16 binary16; written only with kernel type Lut4Bit).
+ * 9 LUT estimator tables (nq x D/4 x 16 binary16; written only with kernel type Lut4Bit),
+ * 10 the estimator's additive query term g_add per probe (nq x nprobe f32; = array 2 for L2,
+ * -<q', c'> for inner product).
  * `bytes` must equal the size of the requested array. */
 int cora_debug_copy(cora_engine *engine, int what, void *h_out, uint64_t bytes);
 /* Per-stage device times (ms) of the last search run with profiling enabled, from CUDA

@@ -165,13 +165,25 @@ int32_t cora_oracle_ip_int(const cora_oracle_index *ix, uint64_t gid, const uint
 
 /* filter_kernels.cuh:693-696: low = f_add + g + f_rescale*(ip1 + k1) - f_error*sqrt(g),
  * with sqrt's argument clamped at zero. */
-float cora_oracle_low(const cora_oracle_index *ix, uint64_t gid, float ip1, float g, float k1) {
+float cora_oracle_low2(const cora_oracle_index *ix, uint64_t gid, float ip1, float g_add,
+                       float gerr, float k1) {
     const float *f = ix->short_factors + gid * 3;
-    const float gerr = sqrtf(fmaxf(g, 0.0f));
-    const float a = f[0] + g;
+    const float a = f[0] + g_add;
     const float b = f[1] * (ip1 + k1);
     const float e = f[2] * gerr;
     return (a + b) - e;
+}
+
+float cora_oracle_low(const cora_oracle_index *ix, uint64_t gid, float ip1, float g, float k1) {
+    return cora_oracle_low2(ix, gid, ip1, g, sqrtf(fmaxf(g, 0.0f)), k1);
+}
+
+/* ivf.hpp:699-706 (dot_product of the rotated query and the centroid) negated, as
+ * set_g_add(dist, ip) stores it for METRIC_IP (query.hpp:99-108). */
+float cora_oracle_ip_gadd(const float *qr, const float *c, uint64_t D) {
+    double acc = 0.0;
+    for (uint64_t j = 0; j < D; ++j) acc = fma((double)qr[j], (double)c[j], acc);
+    return -(float)acc;
 }
 
 /* IEEE 754 binary32 -> binary16 with round to nearest, ties to even (the rounding of
@@ -417,6 +429,11 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
         probe_one(ix, x, nprobe, pid, pg, scratch);
         if (probe_ids_out) memcpy(probe_ids_out + n * nprobe, pid, nprobe * sizeof(int32_t));
         if (probe_g_out) memcpy(probe_g_out + n * nprobe, pg, nprobe * sizeof(float));
+        /* the additive term of each probe (the squared distance for L2) */
+        float *pga = (float *)malloc(nprobe * sizeof(float));
+        for (uint64_t r = 0; r < nprobe; ++r)
+            pga[r] = ix->metric == 1 ? cora_oracle_ip_gadd(x, ix->centroids + (uint64_t)pid[r] * D, D)
+                                     : pg[r];
 
         const float T0 = thresholds0 ? thresholds0[n] : FLT_MAX;
         uint64_t *bound = (uint64_t *)malloc((veff ? veff : 1) * sizeof(uint64_t));
@@ -426,11 +443,11 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
          * low < T0 as seeds (filter_kernels.cuh:308-468), refined right away. */
         for (uint64_t r = 0; r < veff; ++r) {
             const uint64_t c = (uint64_t)pid[r], s = starts[c], nc = ix->cluster_sizes[c];
-            const float g = pg[r];
+            const float g = pga[r], gerr = sqrtf(fmaxf(pg[r], 0.0f));
             npair = 0;
             for (uint64_t i = 0; i < nc; ++i) {
                 const float ip1 = scan_ip1(ix, s, nc, i, planes, width, lut);
-                const float low = cora_oracle_low(ix, s + i, ip1, g, k1);
+                const float low = cora_oracle_low2(ix, s + i, ip1, g, gerr, k1);
                 if (low < T0) {
                     entry_t e = {((uint64_t)ord_f32(low) << 32) | (uint32_t)(s + i), low, ip1,
                                  (uint32_t)(s + i), (uint32_t)r};
@@ -475,11 +492,11 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
          * seeds (keys at or below the recorded boundary). */
         for (uint64_t r = 0; r < nprobe; ++r) {
             const uint64_t c = (uint64_t)pid[r], s = starts[c], nc = ix->cluster_sizes[c];
-            const float g = pg[r];
+            const float g = pga[r], gerr = sqrtf(fmaxf(pg[r], 0.0f));
             if (r < veff && take_all[r]) continue;
             for (uint64_t i = 0; i < nc; ++i) {
                 const float ip1 = scan_ip1(ix, s, nc, i, planes, width, lut);
-                const float low = cora_oracle_low(ix, s + i, ip1, g, k1);
+                const float low = cora_oracle_low2(ix, s + i, ip1, g, gerr, k1);
                 if (!(low < T1)) continue;
                 if (r < veff) {
                     const uint64_t key = ((uint64_t)ord_f32(low) << 32) | (uint32_t)(s + i);
@@ -518,7 +535,7 @@ static int search_impl(const cora_oracle_index *ix, const float *q, uint64_t nq,
             out_ids[n * k + o] = 0;
         }
         free(x); free(planes); free(scratch); free(pid); free(pg); free(res); free(pair);
-        free(bound); free(take_all); free(lut);
+        free(bound); free(take_all); free(lut); free(pga);
     }
     free(starts);
     return 0;

@@ -83,6 +83,11 @@ typedef struct {
     /* 0 (default): ip1 from the integer estimator (KernelType::Bitwise); 1: from the fp16
      * LUT estimator (KernelType::Lut4Bit, the reference's default kernel type). */
     int lut_estimator;
+    /* 0 (default): squared L2; 1: inner product (the reference CPU path's METRIC_IP): the
+     * additive query term of a probed cluster is g_add = -<q', c'> (fp64 chain in ascending
+     * order, rounded once; index/query.hpp:99-108, ivf/ivf.hpp:681-706) instead of the
+     * squared distance g; the error term stays sqrt(g); probes stay the nearest by g. */
+    int metric;
 } cora_oracle_index;
 
 #define CORA_ORACLE_VANGUARD_MIN_KEEP 20
@@ -97,6 +102,11 @@ void cora_oracle_probe(const cora_oracle_index *ix, const float *qr, uint64_t nq
                        uint64_t nprobe, int32_t *probe_ids, float *probe_g);
 int32_t cora_oracle_ip_int(const cora_oracle_index *ix, uint64_t gid, const uint32_t *planes);
 float cora_oracle_low(const cora_oracle_index *ix, uint64_t gid, float ip1, float g, float k1);
+/* The same with separate additive and error terms (g_add; gerr = sqrt(max(g, 0))). */
+float cora_oracle_low2(const cora_oracle_index *ix, uint64_t gid, float ip1, float g_add,
+                       float gerr, float k1);
+/* The inner-product metric's additive term: -(fp32 of the fp64 chain sum_j q'_j c_j). */
+float cora_oracle_ip_gadd(const float *qr, const float *c, uint64_t D);
 void cora_oracle_decode_ex7(const uint8_t *code, uint64_t D, uint8_t *u);
 float cora_oracle_ip_total(const float *qr, const uint32_t *bits, const uint8_t *code,
                            uint64_t D);

@@ -150,7 +150,8 @@ def search_data(ivf: dict) -> dict:
     return dict(centroids=ivf["centroids"], rotator=ivf["rotator"], short_data=short,
                 short_factors=factors, long_codes=long_codes.reshape(-1).copy(),
                 ex_factors=ex_factors.copy(), ids=ivf["ids"], sizes=ivf["sizes"].copy(),
-                num=num, dim=ivf["dim"], D=D, nlist=ivf["nlist"], ex_bits=ex_bits)
+                num=num, dim=ivf["dim"], D=D, nlist=ivf["nlist"], ex_bits=ex_bits,
+                metric=int(ivf.get("metric", 0)))
 
 
 # --------------------------------------------------------------------------------------
@@ -165,7 +166,7 @@ class _Index(C.Structure):
                 ("ids", C.c_void_p), ("cluster_sizes", C.c_void_p),
                 ("exact_base", C.c_void_p), ("exact_rows", C.c_uint64),
                 ("exact_dim", C.c_uint64), ("exact_stride", C.c_uint64),
-                ("refine_full_code", C.c_int), ("lut_estimator", C.c_int)]
+                ("refine_full_code", C.c_int), ("lut_estimator", C.c_int), ("metric", C.c_int)]
 
 
 _lib = None
@@ -211,6 +212,8 @@ def lib():
         L.cora_oracle_decode_ex7.argtypes = [_u8p, C.c_uint64, _u8p]
         L.cora_oracle_ip_int.restype = C.c_int32
         L.cora_oracle_ip_int.argtypes = [C.POINTER(_Index), C.c_uint64, _u32p]
+        L.cora_oracle_ip_gadd.restype = C.c_float
+        L.cora_oracle_ip_gadd.argtypes = [_f32p, _f32p, C.c_uint64]
         L.cora_oracle_centroid_dist.restype = C.c_float
         L.cora_oracle_centroid_dist.argtypes = [_f32p, _f32p, C.c_uint64]
         _lib = L
@@ -247,7 +250,8 @@ class OracleIndex:
                         _ptr(s["centroids"]), _ptr(s["rotator"]), _ptr(s["short_data"]),
                         _ptr(s["short_factors"]), _ptr(s["long_codes"]), _ptr(s["ex_factors"]),
                         _ptr(s["ids"]), _ptr(s["sizes"]), None, 0, 0, 0, int(bool(full_code)),
-                        int(bool(lut)))
+                        int(bool(lut)), int(sd.get("metric", 0)))
+        self.metric = int(sd.get("metric", 0))
         self.set_exact_base(exact_base)
 
     @property
@@ -478,33 +482,41 @@ class RefIVF:
 # --------------------------------------------------------------------------------------
 # Small numpy helpers shared by tests and the bench's CPU legs
 # --------------------------------------------------------------------------------------
-def exact_knn(base, queries, k):
-    """Exact L2 top-k by (fp64 distance, id), as tools/data/generate_gt_gpu.py:114-119."""
+def _dist(b, q, metric):
+    """fp64 distance of base rows b to query q: squared L2 (metric 0) or minus the inner
+    product (metric 1, so that smaller is better in both)."""
+    return ((b - q) ** 2).sum(-1) if metric == 0 else -(b @ q)
+
+
+def exact_knn(base, queries, k, metric=0):
+    """Exact top-k by (fp64 distance, id), as tools/data/generate_gt_gpu.py:114-119; for the
+    inner-product metric by largest inner product."""
     b = np.asarray(base, np.float64)
     out_i = np.empty((len(queries), k), np.uint32)
     out_d = np.empty((len(queries), k), np.float64)
     for i, q in enumerate(np.asarray(queries, np.float64)):
-        d = ((b - q) ** 2).sum(1)
+        d = _dist(b, q, metric)
         order = np.lexsort((np.arange(len(b)), d))[:k]
         out_i[i], out_d[i] = order, d[order]
     return out_i, out_d
 
 
-def distance_recall(base, queries, gt_ids, results, k):
+def distance_recall(base, queries, gt_ids, results, k, metric=0):
     """Distance-aware recall@k (recall.hpp:133-190): an id counts if it is in the GT
-    top-k or its exact fp64 distance is <= the GT k-th distance; duplicates count once."""
+    top-k or its exact fp64 score is as good as the GT k-th one's (squared L2 <=, inner
+    product >=); duplicates count once."""
     b = np.asarray(base, np.float64)
     hits = 0
     for i, q in enumerate(np.asarray(queries, np.float64)):
         truth = set(int(x) for x in gt_ids[i, :k])
-        kth = ((b[int(gt_ids[i, k - 1])] - q) ** 2).sum()
+        kth = _dist(b[int(gt_ids[i, k - 1])], q, metric)
         seen = set()
         for x in results[i, :k]:
             x = int(x)
             if x in seen or x >= len(b):
                 continue
             seen.add(x)
-            if x in truth or ((b[x] - q) ** 2).sum() <= kth:
+            if x in truth or _dist(b[x], q, metric) <= kth:
                 hits += 1
     return hits / (len(queries) * k)
 

@@ -13,7 +13,7 @@ sys.path.insert(0, str(ROOT / "oracle"))
 sys.path.insert(0, str(ROOT / "cgcl-coraanns_b200"))
 sys.path.insert(0, str(ROOT))
 
-GOLDEN_NAMES = ["demo", "d96", "d200", "d150"]
+GOLDEN_NAMES = ["demo", "d96", "d200", "d150", "ip128"]
 
 
 def pytest_configure(config):
@@ -39,13 +39,22 @@ def golden():
 
 
 def regen_base(meta, gen):
-    """Regenerate a fixture's base vectors from its recorded seed (make_golden.make_data)."""
+    """Regenerate a fixture's base vectors from its recorded seed (make_golden.make_data);
+    gen[2], when present, marks unit-normalised (inner-product) fixtures."""
     n, dim, nlist, nq, seed = (int(x) for x in meta)
     sigma = float(gen[0])
     rng = np.random.default_rng(seed)
     centres = rng.normal(size=(nlist, dim)).astype(np.float32)
     lab = rng.integers(0, nlist, n)
-    return (centres[lab] + sigma * rng.normal(size=(n, dim))).astype(np.float32)
+    base = (centres[lab] + sigma * rng.normal(size=(n, dim))).astype(np.float32)
+    if len(gen) > 2 and gen[2]:
+        base = (base / np.linalg.norm(base, axis=1, keepdims=True)).astype(np.float32)
+    return base
+
+
+def fixture_metric(z) -> int:
+    """0 squared L2, 1 inner product (fixtures record it; older ones are L2)."""
+    return int(z["metric"]) if "metric" in z else 0
 
 
 # ------------------------------------------------------------------------------------

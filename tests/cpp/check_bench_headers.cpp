@@ -152,6 +152,18 @@ int main(int argc, char **argv) {
     CHECK(dist.evaluate({0, 3}) == 1.0);   // id 3 is at distance 1 == radius
     CHECK(dist.evaluate({0, 2}) == 0.5);   // id 2 is at distance 9 > radius
     CHECK(dist.evaluate({0, 7}) == 0.5);   // out of range id is a miss
+    // inner product: a row whose exact IP reaches the GT radius counts
+    {
+        const float qi[2] = {1.f, 0.f};
+        Matrix<uint32_t> gti;
+        gti.rows = 1;
+        gti.cols = 1;
+        gti.data = {1};  // id 1 = (1, 0): IP 1
+        RecallEvaluator ip(qi, 1, 2, gti, 1, dir + "/d.fbin", 1);
+        CHECK(ip.evaluate({1}) == 1.0);
+        CHECK(ip.evaluate({3}) == 0.0);  // (0, -1): IP 0 < 1
+        CHECK(throws([&] { RecallEvaluator bad(qi, 1, 2, gti, 1, "", 2); }));
+    }
     Matrix<uint32_t> dup;
     dup.rows = 1;
     dup.cols = 2;

@@ -38,17 +38,24 @@ sys.path.insert(0, str(ROOT / "oracle"))
 import py_oracle as po  # noqa: E402
 
 FIXTURES = {
-    # name: (n, dim, nlist, nq, sigma, query_noise, seed, grid)
+    # name: (n, dim, nlist, nq, sigma, query_noise, seed, grid[, metric]); metric 1 = inner
+    # product on unit-normalised vectors
     "demo": (4096, 128, 16, 100, 0.3, 0.05, 20261201,
              [(10, 4, 5), (10, 8, 5), (10, 16, 5), (10, 16, 0), (1, 4, 5), (50, 8, 2)]),
     "d96": (2048, 96, 16, 48, 0.25, 0.05, 20261202,
             [(10, 2, 5), (10, 6, 5), (10, 16, 1), (100, 8, 5), (10, 4, 0)]),
     "d200": (512, 200, 8, 24, 0.3, 0.05, 20261203, [(10, 3, 5), (10, 8, 2), (5, 8, 0)]),
     "d150": (512, 150, 8, 24, 0.3, 0.05, 20261204, [(10, 3, 5), (20, 8, 1)]),
+    "ip128": (4096, 128, 16, 64, 0.3, 0.05, 20261207, [(10, 4, 5), (10, 8, 5), (20, 6, 2)], 1),
 }
 
 
-def make_data(n, dim, nlist, nq, sigma, qnoise, seed):
+def fixture_metric(name) -> int:
+    spec = FIXTURES[name]
+    return spec[8] if len(spec) > 8 else 0
+
+
+def make_data(n, dim, nlist, nq, sigma, qnoise, seed, normalise=False):
     rng = np.random.default_rng(seed)
     centres = rng.normal(size=(nlist, dim)).astype(np.float32)
     lab = rng.integers(0, nlist, n)
@@ -56,6 +63,9 @@ def make_data(n, dim, nlist, nq, sigma, qnoise, seed):
     qlab = rng.integers(0, nlist, nq)
     queries = (centres[qlab] + sigma * rng.normal(size=(nq, dim)) +
                qnoise * rng.normal(size=(nq, dim))).astype(np.float32)
+    if normalise:  # unit vectors (the inner-product configurations)
+        base = (base / np.linalg.norm(base, axis=1, keepdims=True)).astype(np.float32)
+        queries = (queries / np.linalg.norm(queries, axis=1, keepdims=True)).astype(np.float32)
     return centres, base, queries
 
 
@@ -106,11 +116,12 @@ def refresh_outputs(name):
 
 
 def build_fixture(name):
-    n, dim, nlist, nq, sigma, qnoise, seed, grid = FIXTURES[name]
-    centres, base, queries = make_data(n, dim, nlist, nq, sigma, qnoise, seed)
+    n, dim, nlist, nq, sigma, qnoise, seed, grid = FIXTURES[name][:8]
+    metric = fixture_metric(name)
+    centres, base, queries = make_data(n, dim, nlist, nq, sigma, qnoise, seed, metric == 1)
     cents, assign = lloyd(base, centres)
     index_path = HERE / f"{name}.index"
-    po.ref_build_index(index_path, base, cents, assign, total_bits=8)
+    po.ref_build_index(index_path, base, cents, assign, total_bits=8, metric_ip=metric == 1)
     ref = po.RefIVF(index_path)
     rsd = ref.search_data()
     sd = po.search_data(po.read_ivf_file(index_path))
@@ -119,7 +130,7 @@ def build_fixture(name):
         assert np.asarray(sd[key]).tobytes() == np.asarray(rsd[key]).tobytes(), key
     oracle = po.OracleIndex(sd)
     out = {"queries": queries, "gt_ids": None}
-    gt_ids, gt_d = po.exact_knn(base, queries, 100)
+    gt_ids, gt_d = po.exact_knn(base, queries, 100, metric)
     out["gt_ids"], out["gt_dist"] = gt_ids, gt_d
     # reference adapter hashes (L0)
     out["sd_sha"] = np.array([sha(rsd[k]) for k in ("centroids", "rotator", "short_data",
@@ -147,7 +158,8 @@ def build_fixture(name):
     out["scalars"] = np.stack([prep["width"], prep["k1"], prep["kb"], prep["sumq"]], 1)
     out["grid"] = np.array(grid, np.int64)
     out["meta"] = np.array([n, dim, nlist, nq, seed], np.int64)
-    out["gen"] = np.array([sigma, qnoise], np.float64)
+    out["gen"] = np.array([sigma, qnoise, float(metric == 1)], np.float64)
+    out["metric"] = np.array(metric, np.int64)
     ref.close()
     np.savez_compressed(HERE / f"{name}.npz", **out)
     print(f"{name}: index {index_path.stat().st_size} B, npz {(HERE / (name + '.npz')).stat().st_size} B")

@@ -74,12 +74,16 @@ def _decode(sd, n, D):
     return u
 
 
-@pytest.mark.parametrize("n,dim,nlist,seed", [(3000, 96, 16, 41), (1200, 200, 8, 42)])
-def test_builder_matches_reference_faster_quantizer(tmp_path, n, dim, nlist, seed):
+@pytest.mark.parametrize("n,dim,nlist,seed,metric", [(3000, 96, 16, 41, 0), (1200, 200, 8, 42, 0),
+                                                     (2000, 128, 8, 43, 1)])
+def test_builder_matches_reference_faster_quantizer(tmp_path, n, dim, nlist, seed, metric):
     base, centres, lab = _data(n, dim, nlist, seed)
+    if metric == 1:  # inner product on unit vectors
+        base /= np.linalg.norm(base, axis=1, keepdims=True)
     path = tmp_path / "ref.index"
-    po.ref_build_index(path, base, centres, lab, total_bits=8, faster=True)
+    po.ref_build_index(path, base, centres, lab, total_bits=8, faster=True, metric_ip=metric == 1)
     ref = po.search_data(po.read_ivf_file(path))
+    assert ref["metric"] == metric
     D = int(ref["D"])
     ref_bits = _unpack_bits(ref)
     ref_u = _decode(ref, n, D)
@@ -91,7 +95,7 @@ def test_builder_matches_reference_faster_quantizer(tmp_path, n, dim, nlist, see
 
     from coraanns_b200 import builder
     mine = builder.build_index(base, centres, lab, rotator=ref["rotator"],
-                               rotated_centroids=ref["centroids"], t_const=t)
+                               rotated_centroids=ref["centroids"], t_const=t, metric=metric)
     assert np.array_equal(mine["ids"], ref["ids"])
     assert np.array_equal(mine["sizes"], ref["sizes"])
     # 1-bit codes: byte-identical
@@ -110,6 +114,8 @@ def test_builder_matches_reference_faster_quantizer(tmp_path, n, dim, nlist, see
     same = ~diff.any(1)
     assert same.mean() >= 0.995
     l2 = (r * r).sum(1)[:, None]
+    if metric == 1:  # the factors' scale includes the constant 1 of 1 - <q, x>
+        l2 = np.maximum(l2, 1.0)
     for key in ("short_factors", "ex_factors"):
         a, b = mine[key].astype(np.float64), ref[key].astype(np.float64)
         err = np.abs(a - b) / np.maximum(np.abs(b), l2)

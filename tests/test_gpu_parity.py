@@ -101,21 +101,61 @@ def test_golden_parity(cb, golden, name, loader, mode, sfx):
         if sfx == "L":
             want = po.oracle_from_file(path).query_lut(z["qr"])
             assert np.array_equal(e.debug("lut", len(q)), want), f"{tag}: LUT tables"
+        if int(z["metric"]) if "metric" in z else 0:  # inner product: the additive terms
+            cent = po.search_data(po.read_ivf_file(path))["centroids"]
+            pids = z[f"probe_{key}"]
+            want = np.array([[po.lib().cora_oracle_ip_gadd(np.ascontiguousarray(z["qr"][a]),
+                                                           np.ascontiguousarray(cent[c]), cent.shape[1])
+                              for c in pids[a]] for a in range(len(q))], np.float32)
+            assert e.debug("probe_gadd", len(q), nprobe).tobytes() == want.tobytes(), \
+                f"{tag}: -<q', c'>"
         assert np.array_equal(i, z[f"ids{sfx}_{key}"]), f"{tag}: ids"
         assert d.tobytes() == z[f"dist{sfx}_{key}"].tobytes(), f"{tag}: distances"
         assert e.get_last_submitted_count() == int(z[f"cand{sfx}_{key}"].sum())
     e.close()
 
 
-def _synthetic(n, dim, nlist, nq, seed, sigma=0.25):
+def _synthetic(n, dim, nlist, nq, seed, sigma=0.25, metric=0):
     from coraanns_b200 import builder
     rng = np.random.default_rng(seed)
     centres = rng.normal(size=(nlist, dim)).astype(np.float32)
     lab = rng.integers(0, nlist, n)
     data = (centres[lab] + sigma * rng.normal(size=(n, dim))).astype(np.float32)
     q = (centres[rng.integers(0, nlist, nq)] + sigma * rng.normal(size=(nq, dim))).astype(np.float32)
-    sd = builder.build_index(data, centres, lab, seed=seed)
+    if metric == 1:  # inner product on unit vectors
+        data /= np.linalg.norm(data, axis=1, keepdims=True)
+        q /= np.linalg.norm(q, axis=1, keepdims=True)
+    sd = builder.build_index(data, centres, lab, seed=seed, metric=metric)
     return sd, q
+
+
+@pytest.mark.parametrize("n,dim,nlist,nq,k,nprobe,mode,sfx", [
+    (60_000, 768, 64, 48, 100, 8, "lows", ""),
+    (60_000, 768, 64, 48, 10, 8, "rescan", "L"),
+    (200_000, 96, 256, 128, 10, 16, "lows", ""),
+    (200_000, 96, 256, 128, 10, 16, "lows", "T"),
+])
+def test_inner_product_live_parity(cb, n, dim, nlist, nq, k, nprobe, mode, sfx):
+    """Inner-product indexes (unit vectors, the reference quantizer's METRIC_IP factors):
+    every stage, the additive terms -<q', c'>, candidates and results bit-exact to the oracle."""
+    sd, q = _synthetic(n, dim, nlist, nq, seed=n + dim + 1, metric=1)
+    o = po.OracleIndex(sd, **FORMS[sfx])
+    assert o.metric == 1
+    ref = o.search(q, k, nprobe, vanguard=5, with_details=True)
+    e = _engine(cb, sd=sd, nq=nq, k=k, nprobe=nprobe, mode=mode, **FORMS[sfx])
+    assert e.get_metric() == 1
+    e.reset_buffer(q)
+    d, i = e.search(q, k, nprobe)
+    _check_stages(e, q, k, nprobe, ref, f"ip d{dim}")
+    qr = e.debug("rotated", nq)
+    cent = np.asarray(sd["centroids"], np.float32)
+    want = np.array([[po.lib().cora_oracle_ip_gadd(np.ascontiguousarray(qr[a]),
+                                                   np.ascontiguousarray(cent[c]), cent.shape[1])
+                      for c in ref["probe_ids"][a]] for a in range(nq)], np.float32)
+    assert e.debug("probe_gadd", nq, nprobe).tobytes() == want.tobytes()
+    assert np.array_equal(i, ref["ids"])
+    assert d.tobytes() == ref["dist"].tobytes()
+    e.close()
 
 
 @pytest.mark.parametrize("n,dim,nlist,nq,k,nprobe,van,mode,sfx", [

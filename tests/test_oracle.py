@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 
 import py_oracle as po
-from conftest import GOLDEN_NAMES, kat_fixture, regen_base
+from conftest import GOLDEN_NAMES, fixture_metric, kat_fixture, regen_base
 
 SD_KEYS = ("centroids", "rotator", "short_data", "short_factors", "long_codes", "ex_factors",
            "ids", "sizes")
@@ -63,9 +63,17 @@ def _pair_terms(sd, z, o):
                                              np.ascontiguousarray(prep["planes"][qi]))
         ip1 = np.float32(prep["width"][qi]) * np.float32(ip_int)
         x = np.ascontiguousarray(z["qr"][qi])
-        g = po.lib().cora_oracle_centroid_dist(x, np.ascontiguousarray(sd["centroids"][c]), D)
-        out.append((qi, gid, np.float32(ip1), np.float32(g), np.float32(prep["kb"][qi])))
+        out.append((qi, gid, np.float32(ip1), _g_add(sd, x, c), np.float32(prep["kb"][qi])))
     return out
+
+
+def _g_add(sd, x, c):
+    """The additive query term of cluster c: the squared distance (L2) or -<q', c'> (IP)."""
+    cent = np.ascontiguousarray(sd["centroids"][c])
+    D = int(sd["D"])
+    if int(sd.get("metric", 0)) == 1:
+        return np.float32(po.lib().cora_oracle_ip_gadd(x, cent, D))
+    return np.float32(po.lib().cora_oracle_centroid_dist(x, cent, D))
 
 
 @pytest.mark.parametrize("name", GOLDEN_NAMES)
@@ -132,7 +140,7 @@ def test_refinement_matches_reference_expression_live(golden, name):
                 break
             gid = int(gid)
             c = int(np.searchsorted(starts, gid, side="right") - 1)
-            g = f32(po.lib().cora_oracle_centroid_dist(x, np.ascontiguousarray(sd["centroids"][c]), D))
+            g = _g_add(sd, x, c)
             ip_int = po.lib().cora_oracle_ip_int(C.byref(o.c), gid,
                                                  np.ascontiguousarray(prep["planes"][qi]))
             ip1 = f32(prep["width"][qi]) * f32(ip_int)
@@ -198,16 +206,31 @@ def test_recall_on_par_with_reference_cpu(golden, name):
     path, z = golden[name]
     base = regen_base(z["meta"], z["gen"])
     gt = z["gt_ids"]
-    assert np.array_equal(po.exact_knn(base, z["queries"][:4], 10)[0], gt[:4, :10])
+    m = fixture_metric(z)
+    assert np.array_equal(po.exact_knn(base, z["queries"][:4], 10, m)[0], gt[:4, :10])
     for k, nprobe, van in z["grid"]:
         tag = f"k{k}_np{nprobe}_v{van}"
-        ref = po.distance_recall(base, z["queries"], gt, z[f"refcpu_k{k}_np{nprobe}"], int(k))
+        ref = po.distance_recall(base, z["queries"], gt, z[f"refcpu_k{k}_np{nprobe}"], int(k), m)
         for sfx in ("T", "L"):
-            other = po.distance_recall(base, z["queries"], gt, z[f"ids{sfx}_{tag}"], int(k))
+            other = po.distance_recall(base, z["queries"], gt, z[f"ids{sfx}_{tag}"], int(k), m)
             assert other >= ref - 0.02, (tag, sfx, other, ref)
         if int(k) >= 10:
-            mine = po.distance_recall(base, z["queries"], gt, z[f"ids_{tag}"], int(k))
+            mine = po.distance_recall(base, z["queries"], gt, z[f"ids_{tag}"], int(k), m)
             assert mine >= ref - 0.06, (tag, mine, ref)
+
+
+def test_inner_product_fixture_is_searched_as_inner_product(golden):
+    """The IP fixture's header says METRIC_IP; the oracle's results rank by the estimate of
+    1 - <q, x>: its top-1 id has, on most queries, the largest exact inner product."""
+    path, z = golden["ip128"]
+    assert po.read_ivf_file(path)["metric"] == 1 and fixture_metric(z) == 1
+    base = regen_base(z["meta"], z["gen"])
+    ids = z["ids_k10_np8_v5"]
+    ip = np.einsum("qd,qd->q", base[ids[:, 0]].astype(np.float64), z["queries"].astype(np.float64))
+    best = (base.astype(np.float64) @ z["queries"].astype(np.float64).T).max(0)
+    assert np.mean(np.isclose(ip, best)) >= 0.9
+    d = z["dist_k10_np8_v5"]
+    assert np.all(np.abs(d[:, 0] - (1 - best)) < 0.1)
 
 
 def test_query_prep_matches_reference_formulas(golden):
