@@ -442,25 +442,53 @@ struct Engine {
         cl_size.alloc(nlist);
         CUDA_TRY(cudaMemcpy(cl_start.p, starts.data(), nlist * 4, cudaMemcpyHostToDevice));
         CUDA_TRY(cudaMemcpy(cl_size.p, sizes.data(), nlist * 4, cudaMemcpyHostToDevice));
-        DevBuf<uint8_t> tmp_long;
-        DevBuf<float2> tmp_exf;
-        DevBuf<uint32_t> tmp_ids;
-        tmp_long.alloc(N * LC);
-        tmp_exf.alloc(N);
-        tmp_ids.alloc(N);
-        CUDA_TRY(cudaMemcpy(tmp_long.p, h_long, N * LC, cudaMemcpyHostToDevice));
-        CUDA_TRY(cudaMemcpy(tmp_exf.p, h_exf, N * 8, cudaMemcpyHostToDevice));
-        CUDA_TRY(cudaMemcpy(tmp_ids.p, h_ids, N * 4, cudaMemcpyHostToDevice));
         this->h_ids.assign(h_ids, h_ids + N);
-        // Repack the adapter's word-major 1-bit codes + float[N][3] factors into scan planes.
-        DevBuf<uint32_t> tmp_short;
-        DevBuf<float> tmp_fac;
-        tmp_short.alloc(N * (D / 32));
-        tmp_fac.alloc(N * 3);
-        CUDA_TRY(cudaMemcpy(tmp_short.p, h_short, N * (D / 32) * 4, cudaMemcpyHostToDevice));
-        CUDA_TRY(cudaMemcpy(tmp_fac.p, h_short_factors, N * 12, cudaMemcpyHostToDevice));
+        // The adapter's arrays are staged through bounded buffers, a batch of whole clusters
+        // (at most kLoadBatch vectors, or the largest cluster) at a time, so the device holds
+        // the resident index plus one batch during loading: word-major 1-bit codes and
+        // float[N][3] factors are repacked into scan planes, the 7-bit ex codes, ex factors
+        // and ids into the refine rows and meta words.
         scan4.alloc(N * (G16 + 1));
-        repack_scan_planes(tmp_short.p, tmp_fac.p);
+        rows.alloc(std::max<uint64_t>(N * D / 16, 1));
+        meta.alloc(std::max<uint64_t>(N, 1));
+        {
+            constexpr uint64_t kLoadBatch = 1ull << 23;
+            const uint64_t cap_v = std::max<uint64_t>(kLoadBatch, largest);
+            const uint64_t W = D / 32;
+            DevBuf<uint8_t> tmp_long;
+            DevBuf<float2> tmp_exf;
+            DevBuf<uint32_t> tmp_ids, tmp_short;
+            DevBuf<float> tmp_fac;
+            tmp_long.alloc(cap_v * LC);
+            tmp_exf.alloc(cap_v);
+            tmp_ids.alloc(cap_v);
+            tmp_short.alloc(cap_v * W);
+            tmp_fac.alloc(cap_v * 3);
+            for (uint64_t c0 = 0; c0 < nlist;) {
+                const uint64_t v0 = starts[c0];
+                uint64_t c1 = c0, v1 = v0;
+                while (c1 < nlist && (c1 == c0 || v1 + sizes[c1] - v0 <= cap_v)) v1 += sizes[c1++];
+                const uint64_t m = v1 - v0;
+                if (m) {
+                    CUDA_TRY(cudaMemcpy(tmp_long.p, h_long + v0 * LC, m * LC, cudaMemcpyHostToDevice));
+                    CUDA_TRY(cudaMemcpy(tmp_exf.p, h_exf + v0 * 2, m * 8, cudaMemcpyHostToDevice));
+                    CUDA_TRY(cudaMemcpy(tmp_ids.p, h_ids + v0, m * 4, cudaMemcpyHostToDevice));
+                    CUDA_TRY(cudaMemcpy(tmp_short.p, h_short + v0 * W, m * W * 4,
+                                        cudaMemcpyHostToDevice));
+                    CUDA_TRY(cudaMemcpy(tmp_fac.p, h_short_factors + v0 * 3, m * 12,
+                                        cudaMemcpyHostToDevice));
+                    repack_scan_planes(tmp_short.p, tmp_fac.p, c0, c1, v0);
+                    build_refine_rows_kernel<<<static_cast<unsigned>(c1 - c0), 256, 0, stream>>>(
+                        tmp_long.p, tmp_exf.p, tmp_ids.p, scan4.p, cl_start.p, cl_size.p,
+                        static_cast<int>(D), G16, LC, static_cast<uint32_t>(c0), v0,
+                        reinterpret_cast<uint8_t *>(rows.p), meta.p);
+                    CUDA_TRY(cudaGetLastError());
+                    // the staging buffers are reused by the next batch
+                    CUDA_TRY(cudaStreamSynchronize(stream));
+                }
+                c0 = c1;
+            }
+        }
         {
             std::vector<uint32_t> chunk(nlist + 1, 0);
             for (uint64_t c = 0; c < nlist; ++c) chunk[c + 1] = chunk[c] + (sizes[c] + 31) / 32;
@@ -472,12 +500,6 @@ struct Engine {
                 scan4.p, cl_start.p, cl_size.p, cl_chunk.p, G16, chunk_range.p, cl_range.p);
             CUDA_TRY(cudaGetLastError());
         }
-        rows.alloc(std::max<uint64_t>(N * D / 16, 1));
-        meta.alloc(std::max<uint64_t>(N, 1));
-        build_refine_rows_kernel<<<static_cast<unsigned>(nlist), 256, 0, stream>>>(
-            tmp_long.p, tmp_exf.p, tmp_ids.p, scan4.p, cl_start.p, cl_size.p, static_cast<int>(D),
-            G16, LC, reinterpret_cast<uint8_t *>(rows.p), meta.p);
-        CUDA_TRY(cudaGetLastError());
         CUDA_TRY(cudaStreamSynchronize(stream));
         loaded = true;
         ++ws_gen;
@@ -611,7 +633,9 @@ struct Engine {
         shard_clusters = kept;
     }
 
-    void repack_scan_planes(const uint32_t *d_short, const float *d_fac);
+    // Scan planes of clusters [c0, c1) from a staged batch whose first vector is v0.
+    void repack_scan_planes(const uint32_t *d_short, const float *d_fac, uint64_t c0, uint64_t c1,
+                            uint64_t v0);
 
     // ---------------------------------------------------------------- workspace
     uint64_t vanguard_depth(uint64_t nprobe) const {
@@ -870,31 +894,36 @@ struct Engine {
 // ------------------------------------------------------------------------------------
 // repack: adapter layout -> scan planes (one CTA per cluster)
 // ------------------------------------------------------------------------------------
+// short_data / fac hold a staged batch of whole clusters starting at vector v0; this launch
+// covers clusters c0 + blockIdx.x.
 __global__ void repack_kernel(const uint32_t *__restrict__ short_data,
                               const float *__restrict__ fac, const uint32_t *__restrict__ cl_start,
-                              const uint32_t *__restrict__ cl_size, int W, int G16,
-                              uint4 *__restrict__ scan4) {
-    const int c = blockIdx.x;
+                              const uint32_t *__restrict__ cl_size, int W, int G16, uint32_t c0,
+                              uint64_t v0, uint4 *__restrict__ scan4) {
+    const uint32_t c = c0 + blockIdx.x;
     const uint32_t s = cl_start[c], n = cl_size[c];
+    const uint64_t ls = s - v0;  // the cluster's first vector within the batch
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
         for (int g = 0; g < G16; ++g) {
             uint32_t w[4];
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
                 const int word = 4 * g + t;
-                w[t] = word < W ? short_data[(size_t)s * W + (size_t)word * n + i] : 0u;
+                w[t] = word < W ? short_data[ls * W + (size_t)word * n + i] : 0u;
             }
             scan4[(size_t)(G16 + 1) * s + (size_t)g * n + i] = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        const float *f = fac + (size_t)(s + i) * 3;
+        const float *f = fac + (ls + i) * 3;
         scan4[(size_t)(G16 + 1) * s + (size_t)G16 * n + i] =
             make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), 0u);
     }
 }
 
-void Engine::repack_scan_planes(const uint32_t *d_short, const float *d_fac) {
-    repack_kernel<<<static_cast<unsigned>(nlist), 256, 0, stream>>>(
-        d_short, d_fac, cl_start.p, cl_size.p, static_cast<int>(D / 32), G16, scan4.p);
+void Engine::repack_scan_planes(const uint32_t *d_short, const float *d_fac, uint64_t c0,
+                                uint64_t c1, uint64_t v0) {
+    repack_kernel<<<static_cast<unsigned>(c1 - c0), 256, 0, stream>>>(
+        d_short, d_fac, cl_start.p, cl_size.p, static_cast<int>(D / 32), G16,
+        static_cast<uint32_t>(c0), v0, scan4.p);
     CUDA_TRY(cudaGetLastError());
 }
 

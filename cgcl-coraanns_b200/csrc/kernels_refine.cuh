@@ -55,23 +55,24 @@ __device__ __forceinline__ uint32_t code4(const uint32_t (&ew)[14], uint32_t rbi
     return low | top | msb;
 }
 
-// One CTA per cluster, at load: the refine rows (the 8-bit codes c = 128 b + u of every
-// dimension, decoded by code4 from the ex codes and the 1-bit code words in the scan planes)
-// and the meta words {f_add_ex, f_rescale_ex, id, 0} of its vectors.
+// One CTA per cluster (clusters c0 + blockIdx.x), at load: the refine rows (the 8-bit codes
+// c = 128 b + u of every dimension, decoded by code4 from the ex codes and the 1-bit code
+// words in the scan planes) and the meta words {f_add_ex, f_rescale_ex, id, 0} of its
+// vectors. long_codes / exf / ids hold a staged batch of whole clusters starting at vector v0.
 __global__ void __launch_bounds__(256) build_refine_rows_kernel(
     const uint8_t *__restrict__ long_codes, const float2 *__restrict__ exf,
     const uint32_t *__restrict__ ids, const uint4 *__restrict__ scan4,
     const uint32_t *__restrict__ cl_start, const uint32_t *__restrict__ cl_size, int D, int G16,
-    int LC, uint8_t *__restrict__ rows, uint4 *__restrict__ meta) {
-    const int c = blockIdx.x;
+    int LC, uint32_t c0, uint64_t v0, uint8_t *__restrict__ rows, uint4 *__restrict__ meta) {
+    const uint32_t c = c0 + blockIdx.x;
     const uint32_t s = cl_start[c], n = cl_size[c];
     for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-        const size_t gid = (size_t)s + i;
+        const size_t gid = (size_t)s + i, lid = gid - v0;
         uint32_t *row = reinterpret_cast<uint32_t *>(rows + gid * D);
         for (int blk = 0; blk < D / 64; ++blk) {
             // 56 ex-code bytes of the block (rows of LC = 7 D / 8 bytes: 8-byte aligned)
             const uint32_t *eb =
-                reinterpret_cast<const uint32_t *>(long_codes + gid * LC + 56 * blk);
+                reinterpret_cast<const uint32_t *>(long_codes + lid * LC + 56 * blk);
             uint32_t ew[14];
             for (int t = 0; t < 14; ++t) ew[t] = eb[t];
             const uint4 cw = scan4[(size_t)(G16 + 1) * s + (size_t)(blk / 2) * n + i];
@@ -80,8 +81,8 @@ __global__ void __launch_bounds__(256) build_refine_rows_kernel(
             for (int d0 = 0; d0 < 64; d0 += 4)
                 row[(64 * blk + d0) / 4] = code4(ew, d0 < 32 ? r0 : r1, d0);
         }
-        const float2 f = exf[gid];
-        meta[gid] = make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), ids[gid], 0u);
+        const float2 f = exf[lid];
+        meta[gid] = make_uint4(__float_as_uint(f.x), __float_as_uint(f.y), ids[lid], 0u);
     }
 }
 
