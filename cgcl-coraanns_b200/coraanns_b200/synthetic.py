@@ -86,7 +86,8 @@ def _nearest(x, cent, cn):
 
 def train_centroids(mix: Mixture, nlist, sample=1 << 21, iters=2):
     """IVF partition: Lloyd iterations on a sample of the first chunks, started at the
-    generating centres (nlist == ncomp), as the reference's k-means + nearest assignment
+    generating centres (nlist == ncomp; their directions for unit-normalised data, where the
+    components' means lie), as the reference's k-means + nearest assignment
     (tools/data/train_ivf.py) would end near them."""
     xs, got, j = [], 0, 0
     while got < sample and j < mix.n_chunks:
@@ -96,6 +97,8 @@ def train_centroids(mix: Mixture, nlist, sample=1 << 21, iters=2):
         j += 1
     x = torch.cat(xs)
     c = mix.centres[:nlist].clone()
+    if mix.normalise:
+        c = c / c.norm(dim=1, keepdim=True)
     for _ in range(iters):
         a = torch.cat([_nearest(x[s:s + CHUNK], c, (c * c).sum(1)) for s in range(0, len(x), CHUNK)])
         sums = torch.zeros_like(c).index_add_(0, a, x)
