@@ -75,11 +75,14 @@ class Mixture:
 
 
 def _nearest(x, cent, cn):
-    """Nearest centroid (squared L2) of each row, exact fp32 arithmetic (no TF32)."""
+    """Nearest centroid (squared L2) of each row, exact fp32 arithmetic (no TF32), in row
+    blocks whose distance matrix stays near 2 GB."""
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
+    rows = max(1, (1 << 29) // cent.shape[0])
     try:
-        return (cn[None, :] - 2 * x @ cent.T).argmin(1)
+        return torch.cat([(cn[None, :] - 2 * x[s:s + rows] @ cent.T).argmin(1)
+                          for s in range(0, x.shape[0], rows)])
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
 

@@ -121,6 +121,7 @@ struct SearchView {
     int warp_select_limit;       // keys a warp may collect before queueing a block selection
     int topk_warp_limit;         // the same for the threshold / final top-k (topk_warp_kernel)
     int refine_full_code;        // refine with <q', 128 b + u> instead of 128 ip1 + ip2
+    int refine_pipelined;        // refine_kernel keeps two row blocks in flight per thread
 };
 
 // ---- factor ranges and the lower-bound test that skips whole chunks -------------------
