@@ -302,6 +302,100 @@ def auto_shards(sd, world, dev) -> int:
 
 
 # ------------------------------------------------------------------------------------
+# cluster-sharded sub-measurement (N > 1)
+# ------------------------------------------------------------------------------------
+def measure_sharded(args, sd, q, k, nprobe, kernel_type, eng_single, local, world, dev, total):
+    """The same N GPUs as one cluster-sharded copy of the index answering one batch (the
+    north star's multi-GPU layout; strong scaling): every rank loads its shard, the search's
+    two exchanges are NCCL all-gathers, and the whole search (engine launches and both
+    all-gathers) is also captured in one CUDA graph per rank and replayed. Reported beside
+    the headline: QPS eager and replayed (max over ranks of the CUDA-event time), the
+    single-GPU time of the same batch on each rank's own full copy, the strong-scaling
+    efficiency t_single / (N t_sharded), bit-identity with the single-GPU result, and every
+    rank's stage times (eager, with stage events)."""
+    import torch
+    import torch.distributed as dist
+    from coraanns_b200.shard import ShardedIndex
+    nq = q.shape[0]
+    six = ShardedIndex(local)
+    six.engine.set_ip_kernel_type(kernel_type)
+    six.load_search_data(sd)
+    six.prepare_workspace(nq, k, nprobe)
+    od = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    oi = torch.empty((nq, k), dtype=torch.int32, device=dev)
+    sd_ = torch.empty_like(od)
+    si = torch.empty_like(oi)
+    st = torch.cuda.Stream(dev)
+
+    def single():
+        eng_single.search_device(q.data_ptr(), nq, k, nprobe, sd_.data_ptr(), si.data_ptr(),
+                                 st.cuda_stream)
+
+    def timed(fn, reps):
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return total(e0.elapsed_time(e1) / reps, dist.ReduceOp.MAX)
+
+    eager = lambda: six.search_device(q, k, nprobe, od, oi)  # noqa: E731
+    cur = torch.cuda.current_stream(dev)
+    st.wait_stream(cur)
+    single()
+    cur.wait_stream(st)
+    for _ in range(args.warmup):
+        eager()
+    torch.cuda.synchronize()
+    six.engine.check_device()
+    eng_single.check_device()
+    identical = bool(torch.equal(od, sd_) and torch.equal(oi, si))
+    identical = total(1.0 if identical else 0.0, dist.ReduceOp.MIN) == 1.0
+
+    def single_ordered():
+        st.wait_stream(torch.cuda.current_stream(dev))
+        single()
+        torch.cuda.current_stream(dev).wait_stream(st)
+
+    reps = max(args.steps, 20)
+    ms_single = timed(single_ordered, reps)
+    ms_eager = timed(eager, reps)
+    six.capture(q, k, nprobe, od, oi)
+    six.replay()
+    torch.cuda.synchronize()
+    ms_graph = timed(six.replay, reps)
+    six.engine.check_device()
+    same_graph = total(1.0 if (torch.equal(od, sd_) and torch.equal(oi, si)) else 0.0,
+                       dist.ReduceOp.MIN) == 1.0
+    six.release_graph()
+    # stage times of every rank (eager launches with stage events)
+    import coraanns_b200 as cb
+    six.engine.set_profiling(True)
+    eager()
+    torch.cuda.synchronize()
+    six.engine.stage_reset()
+    for _ in range(5):
+        eager()
+    torch.cuda.synchronize()
+    cnt, tot = six.engine.stage_totals()
+    six.engine.set_profiling(False)
+    mine = torch.tensor([tot[s] / max(cnt, 1) for s in cb.STAGES], dtype=torch.float64, device=dev)
+    allr = torch.empty((world, len(cb.STAGES)), dtype=torch.float64, device=dev)
+    dist.all_gather_into_tensor(allr, mine)
+    six.close()
+    best = min(ms_eager, ms_graph)
+    return dict(layout=f"one copy of the index, {world} cluster shards, {nq} queries",
+                qps_eager=nq / (ms_eager / 1e3), qps_graph=nq / (ms_graph / 1e3),
+                ms_eager=ms_eager, ms_graph=ms_graph, ms_single_gpu=ms_single,
+                strong_scaling_efficiency=ms_single / (world * best),
+                identical_to_single_gpu=identical and same_graph,
+                stage_ms_per_rank=[dict(zip(cb.STAGES, map(float, r))) for r in allr.cpu().numpy()])
+
+
+# ------------------------------------------------------------------------------------
 # streamed configurations (one GPU)
 # ------------------------------------------------------------------------------------
 def run_stream(args, name, cfg):
@@ -522,6 +616,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shards", type=int, default=0,
                     help="GPUs per copy of the index (cluster shards); 0 = as memory requires")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="with N > 1 GPUs, skip the cluster-sharded sub-measurement")
     ap.add_argument("--queries", type=int, default=0,
                     help="search only the first N queries of the batch (profiling a GPU's "
                          "slice of a multi-GPU run); 0 = the whole batch")
@@ -880,6 +976,11 @@ def main():
     if rank == 0 and world == 1 and not args.no_cpu_baseline and index_path is not None:
         cpu_base, _ = cpu_reference_qps(index_path, q_np, k, chosen, target_seconds=15.0)
 
+    sharded = None
+    if world > 1 and shards == 1 and not args.no_sharded:
+        sharded = measure_sharded(args, sd, q, k, chosen, estimators[estimator], eng, local,
+                                  world, dev, total)
+
     if world == 1:
         parallelism = "single"
     elif shards == 1:
@@ -916,6 +1017,8 @@ def main():
             e2e=dict(value=e2e_qps, unit="queries/s", h2d_bytes_per_step=nq * cfg["dim"] * 4,
                      d2h_bytes_per_step=nq * k * 8),
             gpu_launches=launches, clocks=clk.summary())
+        if sharded is not None:
+            line["sharded"] = sharded
         emit(line)
     eng.close()
     if index_path is not None and index_path.exists():

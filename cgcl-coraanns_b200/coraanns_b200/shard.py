@@ -120,6 +120,7 @@ class ShardedIndex:
         self.device = device
         self._bufs = None
         self._stream = None
+        self._graph = None
         self.exchange = torch_exchange(group)
 
     # loading: the engine keeps only this rank's clusters
@@ -184,6 +185,40 @@ class ShardedIndex:
                                out_i)
         cur.wait_stream(self._stream)
 
+    def capture(self, queries, k, nprobe, out_d, out_i):
+        """Captures one whole sharded search (the engine's launches and both NCCL
+        all-gathers) into a CUDA graph on this rank, for replay(); every rank captures the
+        same search. The buffers are baked in: replay() searches `queries` into out_d / out_i
+        as they hold at replay time. Run one eager search first (communicator set-up), and
+        release the graph (release_graph / close) before the process group is destroyed."""
+        import torch
+        self.release_graph()
+        g = torch.cuda.CUDAGraph()
+        if self._stream is None:
+            self._stream = torch.cuda.Stream(self.device)
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.graph(g, stream=self._stream, capture_error_mode="relaxed"):
+            run_sharded_search(self, self.exchange, queries, queries.shape[0], k, nprobe, out_d,
+                               out_i)
+        self._graph = g
+
+    def replay(self):
+        """Replays the captured search on this index's stream, ordered after torch's current
+        stream and before its later work; not synchronised."""
+        import torch
+        if self._graph is None:
+            raise LogicError("capture a search before replaying it")
+        cur = torch.cuda.current_stream(self.device)
+        self._stream.wait_stream(cur)
+        with torch.cuda.stream(self._stream):
+            self._graph.replay()
+        cur.wait_stream(self._stream)
+
+    def release_graph(self):
+        if self._graph is not None:
+            self._graph.reset()
+            self._graph = None
+
     def search(self, h_queries, k, nprobe):
         """Host arrays in and out (queries copied to this rank's GPU)."""
         import torch
@@ -197,4 +232,5 @@ class ShardedIndex:
         return d, i
 
     def close(self):
+        self.release_graph()
         self.engine.close()

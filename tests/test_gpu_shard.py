@@ -167,7 +167,20 @@ def _nccl_worker(rank, world, port, out_q):
         ix.prepare_workspace(len(q), 100, 8)
         d, i = ix.search(q, 100, 8)
         ok = np.array_equal(i, z["ids_k100_np8_v5"]) and d.tobytes() == z["dist_k100_np8_v5"].tobytes()
-        ix.close()
+        # the whole sharded search (engine launches + both all-gathers) captured in one CUDA
+        # graph and replayed twice returns the same bytes
+        dq = torch.from_numpy(q).cuda()
+        od = torch.full((len(q), 100), -1.0, device="cuda")
+        oi = torch.full((len(q), 100), -1, dtype=torch.int32, device="cuda")
+        ix.capture(dq, 100, 8, od, oi)
+        for _ in range(2):
+            od.fill_(-1.0)
+            ix.replay()
+            torch.cuda.synchronize()
+            ix.engine.check_device()
+            ok = ok and np.array_equal(oi.cpu().numpy().view(np.uint32), i) and \
+                od.cpu().numpy().tobytes() == d.tobytes()
+        ix.close()  # releases the graph before the process group goes
         out_q.put((rank, ok))
     finally:
         dist.destroy_process_group()
