@@ -208,10 +208,10 @@ inline void launch_guarded_select(float *approx, const float *chunk_min, uint64_
             cent, cmax, iD, kApproxEpsTF32, probe_ids, probe_g, fallback);
         CUDA_TRY(cudaGetLastError());
         guarded_select_kernel<<<static_cast<unsigned>(2 * num_sms), 256, bsm, st>>>(
-            approx, static_cast<int>(nlist), approx_ld(nlist), inp, ccap, qr, qnorm2, cent, cmax,
-            iD, kApproxEpsTF32, probe_ids, probe_g, fallback);
+            approx, chunk_min, static_cast<int>(nlist), approx_ld(nlist), inp, ccap, qr, qnorm2,
+            cent, cmax, iD, kApproxEpsTF32, probe_ids, probe_g, fallback);
     } else {
-        guarded_select_kernel<<<inq, 256, bsm, st>>>(approx, static_cast<int>(nlist),
+        guarded_select_kernel<<<inq, 256, bsm, st>>>(approx, chunk_min, static_cast<int>(nlist),
                                                      approx_ld(nlist), inp, ccap, qr, qnorm2, cent,
                                                      cmax, iD, kApproxEpsTF32, probe_ids, probe_g,
                                                      nullptr);

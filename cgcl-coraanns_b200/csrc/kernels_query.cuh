@@ -246,31 +246,37 @@ __device__ __forceinline__ float exact_centroid_dist(const float *__restrict__ x
 // written over its approximate row. Dynamic shared memory: see guarded_select_smem().
 // list == nullptr: query blockIdx.x; otherwise the queries list[1 .. list[0]] (grid-stride),
 // the ones guarded_select_warp_kernel handed over.
-__device__ void guarded_select_block(int q, float *__restrict__ approx, int nlist, size_t ld,
+__device__ void guarded_select_block(int q, float *__restrict__ approx,
+                                     const float *__restrict__ chunk_min, int nlist, size_t ld,
                                      int nprobe, int cand_cap, const float *__restrict__ qr,
                                      const float *__restrict__ qnorm2,
                                      const float *__restrict__ cent, float cmax, int D, double eps,
                                      int *__restrict__ probe_ids, float *__restrict__ probe_g);
 
 __global__ void __launch_bounds__(256) guarded_select_kernel(
-    float *__restrict__ approx, int nlist, size_t ld, int nprobe, int cand_cap,
-    const float *__restrict__ qr, const float *__restrict__ qnorm2, const float *__restrict__ cent,
-    float cmax, int D, double eps, int *__restrict__ probe_ids, float *__restrict__ probe_g,
-    const uint32_t *__restrict__ list) {
+    float *__restrict__ approx, const float *__restrict__ chunk_min, int nlist, size_t ld,
+    int nprobe, int cand_cap, const float *__restrict__ qr, const float *__restrict__ qnorm2,
+    const float *__restrict__ cent, float cmax, int D, double eps, int *__restrict__ probe_ids,
+    float *__restrict__ probe_g, const uint32_t *__restrict__ list) {
     if (!list) {
-        guarded_select_block(blockIdx.x, approx, nlist, ld, nprobe, cand_cap, qr, qnorm2, cent,
-                             cmax, D, eps, probe_ids, probe_g);
+        guarded_select_block(blockIdx.x, approx, chunk_min, nlist, ld, nprobe, cand_cap, qr,
+                             qnorm2, cent, cmax, D, eps, probe_ids, probe_g);
         return;
     }
     const uint32_t n = list[0];
     for (uint32_t j = blockIdx.x; j < n; j += gridDim.x) {
-        guarded_select_block(static_cast<int>(list[1 + j]), approx, nlist, ld, nprobe, cand_cap,
-                             qr, qnorm2, cent, cmax, D, eps, probe_ids, probe_g);
+        guarded_select_block(static_cast<int>(list[1 + j]), approx, chunk_min, nlist, ld, nprobe,
+                             cand_cap, qr, qnorm2, cent, cmax, D, eps, probe_ids, probe_g);
         __syncthreads();  // shared memory is reused by the next query
     }
 }
 
-__device__ void guarded_select_block(int q, float *__restrict__ approx, int nlist, size_t ld,
+// chunk_min (nullable): the probe GEMM's per-chunk row minima. With them, and at least nprobe
+// chunks, the upper bound of tau comes from a selection over the chunk minima (nlist / 32
+// keys) instead of the whole row, and the band is collected from the chunks whose minimum
+// lies inside it.
+__device__ void guarded_select_block(int q, float *__restrict__ approx,
+                                     const float *__restrict__ chunk_min, int nlist, size_t ld,
                                      int nprobe, int cand_cap, const float *__restrict__ qr,
                                      const float *__restrict__ qnorm2,
                                      const float *__restrict__ cent, float cmax, int D, double eps,
@@ -287,12 +293,21 @@ __device__ void guarded_select_block(int q, float *__restrict__ approx, int nlis
     for (int j = threadIdx.x; j < D; j += blockDim.x) x[j] = qr[(size_t)q * D + j];
     if (threadIdx.x == 0) s_ncand = 0;
     auto approx_key = [&](uint32_t c) -> uint64_t { return make_key(row[c], c); };
-    block_select_smallest(approx_key, static_cast<uint32_t>(nlist), nprobe, sel, scratch);
+    const int nchunk = (nlist + 31) / 32;
+    const float *cm = chunk_min ? chunk_min + (size_t)q * chunk_stride(nlist) : nullptr;
+    if (cm && nchunk >= nprobe) {
+        // the nprobe-th smallest chunk minimum bounds tau from above (nprobe distinct chunks
+        // hold a centroid at or below it)
+        auto chunk_key = [&](uint32_t j) -> uint64_t { return make_key(__ldg(cm + j), j); };
+        block_select_smallest(chunk_key, static_cast<uint32_t>(nchunk), nprobe, sel, scratch);
+    } else {
+        block_select_smallest(approx_key, static_cast<uint32_t>(nlist), nprobe, sel, scratch);
+    }
     const double tau = (double)unord_f32(static_cast<uint32_t>(sel[nprobe - 1] >> 32));
     const double r = sqrt((double)qnorm2[q]) + (double)cmax;
     const double bound = tau + 2.0 * (eps * r * r + 1e-30);
     for (int c = threadIdx.x; c < nlist; c += blockDim.x) {
-        if ((double)row[c] <= bound) {
+        if ((!cm || (double)__ldg(cm + (c >> 5)) <= bound) && (double)row[c] <= bound) {
             const int pos = atomicAdd(&s_ncand, 1);
             if (pos < cand_cap) cidx[pos] = static_cast<uint32_t>(c);
         }
@@ -325,8 +340,8 @@ __host__ __device__ inline size_t guarded_select_smem(int nprobe, int cand_cap, 
 }
 
 // One warp per query (8 per CTA), nprobe <= 32: the same selection without block-wide radix
-// passes. The nprobe-th smallest of the 32 lane minima, tau_ub, is >= tau (nprobe values lie
-// at or below it), so {approx <= tau_ub + 2E} contains the guard band {approx <= tau + 2E},
+// passes. The nprobe-th smallest chunk minimum, tau_ub, is >= tau (nprobe values lie at or
+// below it), so {approx <= tau_ub + 2E} contains the guard band {approx <= tau + 2E},
 // and recomputing that superset exactly selects the same probes (a centroid outside the band
 // can never beat one of the true top-nprobe). It is normally a few dozen centroids; a query
 // whose set exceeds kGuardWarpBand is queued in fallback[1..] (count in fallback[0]) for
@@ -362,11 +377,34 @@ __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
     const float *cm = chunk_min + (size_t)q * chunk_stride(nlist);
     for (int j = lane; j < D; j += 32) x[j] = qr[(size_t)q * D + j];
 
-    float mn = FLT_MAX;
-    for (int c = lane; c < nchunk; c += 32) mn = fminf(mn, __ldg(cm + c));
-    const uint64_t kth = __shfl_sync(0xffffffffu,
-                                     warp_sort_lane_keys(make_key(mn, lane), lane), nprobe - 1);
-    const double tau_ub = (double)unord_f32(static_cast<uint32_t>(kth >> 32));
+    // tau_ub: the nprobe-th smallest chunk minimum (nprobe distinct chunks each hold a
+    // centroid at or below it, so it bounds the nprobe-th smallest approximate distance from
+    // above, and is that distance itself when the nprobe nearest lie in distinct chunks).
+    // Rows of at most 32 chunks: one chunk per lane, sorted; longer rows: an exact radix
+    // selection over the chunk minima's order keys, one bit per warp-wide count.
+    double tau_ub;
+    if (nchunk <= 32) {
+        const float mn = lane < nchunk ? __ldg(cm + lane) : FLT_MAX;
+        const uint64_t kth = __shfl_sync(0xffffffffu,
+                                         warp_sort_lane_keys(make_key(mn, lane), lane), nprobe - 1);
+        tau_ub = (double)unord_f32(static_cast<uint32_t>(kth >> 32));
+    } else {
+        uint32_t prefix = 0, remaining = static_cast<uint32_t>(nprobe);
+        for (int bit = 31; bit >= 0; --bit) {
+            const uint32_t above = bit == 31 ? 0u : ~((2u << bit) - 1u);  // bits above `bit`
+            uint32_t cnt = 0;
+            for (int c = lane; c < nchunk; c += 32) {
+                const uint32_t key = ord_f32(__ldg(cm + c));
+                cnt += ((key & above) == prefix && !((key >> bit) & 1u)) ? 1u : 0u;
+            }
+            cnt = __reduce_add_sync(0xffffffffu, cnt);
+            if (cnt < remaining) {
+                remaining -= cnt;
+                prefix |= 1u << bit;
+            }
+        }
+        tau_ub = (double)unord_f32(prefix);
+    }
     const double r = sqrt((double)qnorm2[q]) + (double)cmax;
     const double bound = tau_ub + 2.0 * (eps * r * r + 1e-30);
 
