@@ -87,11 +87,13 @@ def _nearest(x, cent, cn):
         torch.backends.cuda.matmul.allow_tf32 = prev
 
 
-def train_centroids(mix: Mixture, nlist, sample=1 << 21, iters=2):
-    """IVF partition: Lloyd iterations on a sample of the first chunks, started at the
+def train_centroids(mix: Mixture, nlist, sample=1 << 21, iters=2, init="centres"):
+    """IVF partition: Lloyd iterations on a sample of the first chunks, as the reference's
+    k-means + nearest assignment (tools/data/train_ivf.py). init="centres" starts at the
     generating centres (nlist == ncomp; their directions for unit-normalised data, where the
-    components' means lie), as the reference's k-means + nearest assignment
-    (tools/data/train_ivf.py) would end near them."""
+    components' means lie), where k-means would end near them for equal-weight mixtures;
+    init="sample" starts at nlist vectors of the sample (as Faiss's k-means does), which gives
+    heavy components of a skewed mixture several centroids."""
     xs, got, j = [], 0, 0
     while got < sample and j < mix.n_chunks:
         x, _, _ = mix.chunk_at(j)
@@ -99,9 +101,13 @@ def train_centroids(mix: Mixture, nlist, sample=1 << 21, iters=2):
         got += xs[-1].shape[0]
         j += 1
     x = torch.cat(xs)
-    c = mix.centres[:nlist].clone()
-    if mix.normalise:
-        c = c / c.norm(dim=1, keepdim=True)
+    if init == "sample":
+        g = torch.Generator(device=mix.dev).manual_seed(mix.seed + 17)
+        c = x[torch.randperm(x.shape[0], generator=g, device=mix.dev)[:nlist]].clone()
+    else:
+        c = mix.centres[:nlist].clone()
+        if mix.normalise:
+            c = c / c.norm(dim=1, keepdim=True)
     for _ in range(iters):
         a = torch.cat([_nearest(x[s:s + CHUNK], c, (c * c).sum(1)) for s in range(0, len(x), CHUNK)])
         sums = torch.zeros_like(c).index_add_(0, a, x)
