@@ -291,7 +291,6 @@ struct Engine {
     // Upper bound on the HBM buffer holding the vanguard pairs' lower bounds; larger
     // worst cases fall back to rescanning the vanguard clusters.
     uint64_t lows_budget = 16ull << 30;
-    bool refine_pipelined = true;  // see refine_row_term
     int warp_select_limit = kWarpSelectBuf;  // see vanguard_select_warp_kernel
     int topk_warp_limit = kWarpTopBuf;       // see topk_warp_kernel
 
@@ -339,14 +338,13 @@ struct Engine {
         uint32_t *d_oi = nullptr;
         cudaStream_t st = nullptr;
         int wsl = 0, twl = 0;
-        bool reuse = false, full_code = false, lut = false, rpipe = false;
+        bool reuse = false, full_code = false, lut = false;
         int metric = 0;
         bool same(const GraphKey &o) const {
             return d_q == o.d_q && nq == o.nq && k == o.k && np == o.np && ws_gen == o.ws_gen &&
                    vanguard == o.vanguard && d_od == o.d_od && d_oi == o.d_oi && st == o.st &&
                    wsl == o.wsl && twl == o.twl && reuse == o.reuse &&
-                   full_code == o.full_code && lut == o.lut && metric == o.metric &&
-                   rpipe == o.rpipe;
+                   full_code == o.full_code && lut == o.lut && metric == o.metric;
         }
     };
     GraphKey graph_key;
@@ -1023,7 +1021,7 @@ SearchView Engine::search_view() const {
                       T1.p, bound.p,
                       cand_cnt.p, seed_cnt.p, cand_rec.p, cand_key.p, lows.p, vg_off.p, lows.n,
                       lows_top.p, err.p, warp_select_limit, topk_warp_limit,
-                      refine_full_code ? 1 : 0, refine_pipelined ? 1 : 0};
+                      refine_full_code ? 1 : 0};
 }
 
 void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, float *d_od,
@@ -1052,7 +1050,6 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     key.full_code = refine_full_code;
     key.lut = lut_mode();
     key.metric = metric;
-    key.rpipe = refine_pipelined;
     if (!graph_exec || !graph_key.same(key)) {
         drop_graph();
         CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeRelaxed));
@@ -1948,9 +1945,6 @@ int cora_set_tuning(cora_engine *engine, const char *key, int64_t value) {
             if (value < 0) cora::fail(CORA_EINVAL, "vanguard_lows_budget must be >= 0");
             if (e.ws_ready) cora::fail(CORA_ESTATE, "set the lows budget before prepare_workspace");
             e.lows_budget = static_cast<uint64_t>(value);
-        } else if (k == "refine_pipelined") {
-            if (value != 0 && value != 1) cora::fail(CORA_EINVAL, "refine_pipelined must be 0 or 1");
-            e.refine_pipelined = value != 0;
         } else if (k == "search_graphs") {
             if (value != 0 && value != 1) cora::fail(CORA_EINVAL, "search_graphs must be 0 or 1");
             e.search_graphs = value != 0;

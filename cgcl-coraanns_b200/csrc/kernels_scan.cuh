@@ -121,7 +121,6 @@ struct SearchView {
     int warp_select_limit;       // keys a warp may collect before queueing a block selection
     int topk_warp_limit;         // the same for the threshold / final top-k (topk_warp_kernel)
     int refine_full_code;        // refine with <q', 128 b + u> instead of 128 ip1 + ip2
-    int refine_pipelined;        // refine_kernel keeps two row blocks in flight per thread
 };
 
 // ---- factor ranges and the lower-bound test that skips whole chunks -------------------
@@ -978,15 +977,11 @@ __global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, Sear
 constexpr int kWarpSelectMax = 32;   // largest `keep` handled one warp per pair
 constexpr int kWarpSelectBuf = 256;  // keys at or below the first threshold a warp may hold
 
-// One warp per vanguard pair (8 per CTA), keep S <= 32, one pass over the pair's lows. The
-// S-th smallest of the 32 lane minima of the first batch (16 lows per lane) bounds the S-th
-// smallest key from above (S lanes hold a low at or below it), so the warp collects only the
-// keys (low, gid) with low < T0 and key <= tau, tau starting at that bound. When the
-// collection would outgrow its buffer, it is sorted and cut to its S smallest keys, whose
-// last becomes the new tau (no later key above it can be a seed). The number of lows below
-// T0 is counted in the same pass. A pair whose keys do not fit even after the cut (more than
-// warp_select_limit - S keys of one batch at or below tau, or a limit below S) is queued in
-// fallback[1..] (count in fallback[0]) for vanguard_select_kernel.
+// One warp per vanguard pair (8 per CTA), keep <= 32. The keep-th smallest of the 32 lane
+// minima bounds the keep-th smallest key from above, so every seed is among the keys at or
+// below it; those (normally a few dozen) are collected and sorted. A pair whose collection
+// exceeds kWarpSelectBuf is queued in fallback[1..] (count in fallback[0]) for
+// vanguard_select_kernel.
 __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
     IndexView ix, SearchView sv, const uint8_t *__restrict__ owned,
     uint32_t *__restrict__ fallback) {
@@ -1002,80 +997,50 @@ __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
     const float4 *L4 = reinterpret_cast<const float4 *>(sv.lows + sv.vg_off[pi]);
     const float T0 = sv.T0[q];
     const int S = sv.keep;
-    const uint32_t cap = static_cast<uint32_t>(sv.warp_select_limit);
-    uint64_t *b = buf[w];
-    uint64_t tau = kKeyMax;
-    uint32_t m = 0, cnt = 0;
-    bool spill = false;
+    // Pass 1: each lane's smallest low (NaN lows drop out of fminf). tau_f, the S-th
+    // smallest lane minimum, bounds the seeds: when tau_f < T0 the S lanes at or below it
+    // hold S lows <= tau_f below T0, so the S smallest keys all have low <= tau_f; when
+    // tau_f >= T0 every low < T0 is collected.
+    const float inf = __int_as_float(0x7f800000);
+    float mn = inf;
     for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
         float l[4 * kLowsUnroll];
         load_lows4(L4, n, b4 + lane, l);
-        if (b4 == 0) {
-            // first batch: the bound from the lane minima (NaN lows drop out of fminf; a
-            // bound at or above T0 collects every low below T0)
-            float mn = __int_as_float(0x7f800000);
 #pragma unroll
-            for (int e = 0; e < 4 * kLowsUnroll; ++e) mn = fminf(mn, l[e]);
-            const float tf = unord_f32(static_cast<uint32_t>(
-                __shfl_sync(0xffffffffu, warp_sort_lane_keys(make_key(mn, lane), lane), S - 1) >> 32));
-            tau = make_key(tf, 0xFFFFFFFFu);  // every gid of a low equal to the bound
-        }
+        for (int e = 0; e < 4 * kLowsUnroll; ++e) mn = fminf(mn, l[e]);
+    }
+    const float tau_f = unord_f32(static_cast<uint32_t>(
+        __shfl_sync(0xffffffffu, warp_sort_lane_keys(make_key(mn, lane), lane), S - 1) >> 32));
+    // Pass 2: count the lows < T0 and collect every key with low < T0 and low <= tau_f (-0
+    // and +0 compare equal here, so the set contains every key the exact bound would take)
+    const float *L = sv.lows + sv.vg_off[pi];
+    uint64_t *b = buf[w];
+    uint32_t m = 0, cnt = 0;
+    for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
+        float l[4 * kLowsUnroll];
+        load_lows4(L4, n, b4 + lane, l);
         uint32_t take = 0;
 #pragma unroll
         for (int e = 0; e < 4 * kLowsUnroll; ++e) {
             const bool below = l[e] < T0;
             cnt += below ? 1u : 0u;
-            const bool t = below && make_key(l[e], s + lows_index(b4, lane, e)) <= tau;
-            take |= (t ? 1u : 0u) << e;
+            take |= (below && l[e] <= tau_f ? 1u : 0u) << e;
         }
         const uint32_t mine = __popc(take);
         const uint32_t incl = warp_inclusive_sum(mine, lane);
         const uint32_t got = __shfl_sync(0xffffffffu, incl, 31);
-        if (got == 0) continue;
-        if (m + got > cap) {  // cut the collection to its S smallest keys and tighten tau
-            int sort_n = 32;
-            while (sort_n < static_cast<int>(m)) sort_n <<= 1;
-            for (int i = m + lane; i < sort_n; i += 32) b[i] = kKeyMax;
-            __syncwarp();
-            warp_sort_smem(b, sort_n, lane);
-            if (m >= static_cast<uint32_t>(S)) {
-                tau = b[S - 1];
-                m = S;
-            }
-            // keys of this batch above the new tau are no seeds
-#pragma unroll
-            for (int e = 0; e < 4 * kLowsUnroll; ++e)
-                if (((take >> e) & 1u) && make_key(l[e], s + lows_index(b4, lane, e)) > tau)
-                    take &= ~(1u << e);
-            const uint32_t mine2 = __popc(take);
-            const uint32_t incl2 = warp_inclusive_sum(mine2, lane);
-            const uint32_t got2 = __shfl_sync(0xffffffffu, incl2, 31);
-            if (m + got2 > cap) {
-                spill = true;
-                break;
-            }
-            uint32_t pos = m + incl2 - mine2;
-            for (uint32_t mm = take; mm; mm &= mm - 1, ++pos) {
-                const uint32_t i = lows_index(b4, lane, __ffs(mm) - 1);
-                b[pos] = make_key(l[__ffs(mm) - 1], s + i);
-            }
-            m += got2;
-            __syncwarp();
-            continue;
-        }
         uint32_t pos = m + incl - mine;
         for (uint32_t mm = take; mm; mm &= mm - 1, ++pos) {
             const uint32_t i = lows_index(b4, lane, __ffs(mm) - 1);
-            b[pos] = make_key(l[__ffs(mm) - 1], s + i);
+            if (pos < static_cast<uint32_t>(kWarpSelectBuf)) b[pos] = make_key(L[i], s + i);
         }
         m += got;
-        __syncwarp();
     }
-    if (spill) {
+    const uint32_t total = __reduce_add_sync(0xffffffffu, cnt);
+    if (m > static_cast<uint32_t>(sv.warp_select_limit)) {
         if (lane == 0) fallback[1 + atomicAdd(fallback, 1u)] = static_cast<uint32_t>(pi);
         return;
     }
-    const uint32_t total = __reduce_add_sync(0xffffffffu, cnt);
     int sort_n = 32;
     while (sort_n < static_cast<int>(m)) sort_n <<= 1;
     for (int i = m + lane; i < sort_n; i += 32) b[i] = kKeyMax;

@@ -212,8 +212,6 @@ int cora_set_vanguard_lows_budget(cora_engine *engine, uint64_t bytes);
  *                          a vanguard pair before it hands the pair to a block-wide
  *                          selection (0 sends every pair to the block selection);
  *  "topk_warp_limit"       the same for the threshold and final top-k of a query (k <= 32);
- *  "refine_pipelined"      1 (default): the refinement keeps two 64-byte blocks of a
- *                          candidate's row in flight per thread; 0: one block at a time;
  *  "search_graphs"         1 (default): cora_search / cora_search_device replay a captured
  *                          CUDA graph of the whole search (rebuilt when the buffers, shape,
  *                          stream or configuration change; not used while profiling or
