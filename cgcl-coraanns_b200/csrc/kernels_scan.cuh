@@ -515,7 +515,7 @@ __device__ __forceinline__ void lut_offsets(const uint4 &code, uint32_t (&nib)[3
 #pragma unroll
     for (int t = 0; t < 4; ++t)
 #pragma unroll
-        for (int n = 0; n < 8; ++n) nib[8 * t + n] = (x[t] >> (26 - 4 * n)) & 0x3Cu;
+        for (int n = 0; n < 8; ++n) nib[8 * t + n] = ((x[t] >> (28 - 4 * n)) & 0xFu) << 2;
 }
 __device__ __forceinline__ float ip_from_lut_offsets(const uint32_t (&nib)[32],
                                                      const float *__restrict__ T) {
