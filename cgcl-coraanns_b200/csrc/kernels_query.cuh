@@ -61,23 +61,32 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
     constexpr int kTpg = 256 / kGroups;  // threads per group
     const int grp = threadIdx.x / kTpg;
     const double *sqg = sq + grp * kRotQueries * dim;
-    for (int j = threadIdx.x % kTpg; j < D; j += kTpg) {
-        double acc[kRotQueries];
+    // a thread carries output dims j and j + kTpg together, so each query value read from
+    // shared memory feeds two chains (the loads, not the fp64 FMAs, bound this loop)
+    for (int j = threadIdx.x % kTpg; j < D; j += 2 * kTpg) {
+        const int j2 = j + kTpg;
+        const bool two = j2 < D;
+        double acc[kRotQueries], acc2[kRotQueries];
 #pragma unroll
-        for (int qq = 0; qq < kRotQueries; ++qq) acc[qq] = 0.0;
+        for (int qq = 0; qq < kRotQueries; ++qq) acc[qq] = acc2[qq] = 0.0;
         // rotator values are loaded eight rows ahead of their use (dim % 8 == 0 is not
         // assumed: the tail rows read as 0 and are not accumulated)
         for (int i0 = 0; i0 < dim; i0 += 8) {
-            double p[8];
+            double p[8], p2[8];
 #pragma unroll
-            for (int u = 0; u < 8; ++u)
+            for (int u = 0; u < 8; ++u) {
                 p[u] = i0 + u < dim ? __ldg(rotator + (size_t)(i0 + u) * D + j) : 0.0;
+                p2[u] = two && i0 + u < dim ? __ldg(rotator + (size_t)(i0 + u) * D + j2) : 0.0;
+            }
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
                 if (i0 + u < dim) {
 #pragma unroll
-                    for (int qq = 0; qq < kRotQueries; ++qq)
-                        acc[qq] = __fma_rn(sqg[qq * dim + i0 + u], p[u], acc[qq]);
+                    for (int qq = 0; qq < kRotQueries; ++qq) {
+                        const double xv = sqg[qq * dim + i0 + u];
+                        acc[qq] = __fma_rn(xv, p[u], acc[qq]);
+                        acc2[qq] = __fma_rn(xv, p2[u], acc2[qq]);
+                    }
                 }
             }
         }
@@ -87,6 +96,11 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
             const float v = (float)acc[qq];
             sr[qa * D + j] = v;
             if (qa < nqb) qr_out[(size_t)(q0 + qa) * D + j] = v;
+            if (two) {
+                const float v2 = (float)acc2[qq];
+                sr[qa * D + j2] = v2;
+                if (qa < nqb) qr_out[(size_t)(q0 + qa) * D + j2] = v2;
+            }
         }
     }
     __syncthreads();
