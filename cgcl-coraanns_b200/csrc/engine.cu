@@ -219,6 +219,16 @@ inline void launch_guarded_select(float *approx, const float *chunk_min, uint64_
     CUDA_TRY(cudaGetLastError());
 }
 
+// refine_kernel for one query per CTA; rows longer than 128 bytes load their blocks ahead.
+inline void launch_refine(const IndexView &ix, const SearchView &sv, int D, int np, int mode,
+                          int nq, cudaStream_t st) {
+    const size_t sm = refine_smem(D, np);
+    auto *kern = D > 128 ? refine_kernel<true> : refine_kernel<false>;
+    CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+    kern<<<static_cast<unsigned>(nq), kRefineThreads, sm, st>>>(ix, sv, mode);
+    CUDA_TRY(cudaGetLastError());
+}
+
 // Cluster-to-shard plan: longest-processing-time greedy on cluster sizes (every vector of an
 // index costs the same bytes), largest cluster first (ties: lower cluster id) onto the least
 // loaded shard (ties: lower rank). Deterministic, so every rank derives the same plan.
@@ -1170,10 +1180,7 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
         CUDA_TRY(cudaGetLastError());
     }
     mark(6, st);
-    const size_t refine_sm = refine_smem(static_cast<int>(D), static_cast<int>(np));
-    CUDA_TRY(cudaFuncSetAttribute(refine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)refine_sm));
-    refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 0);
+    launch_refine(ix, sv, static_cast<int>(D), static_cast<int>(np), 0, inq, st);
     CUDA_TRY(cudaGetLastError());
     mark(7, st);
     launch_topk(0, nullptr, nullptr, seed_keys_out, st);
@@ -1280,10 +1287,7 @@ void Engine::enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uin
     }
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));
     mark(11, st);
-    const size_t refine_sm = refine_smem(static_cast<int>(D), static_cast<int>(last_np));
-    CUDA_TRY(cudaFuncSetAttribute(refine_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)refine_sm));
-    refine_kernel<<<inq, kRefineThreads, refine_sm, st>>>(ix, sv, 1);
+    launch_refine(ix, sv, static_cast<int>(D), static_cast<int>(last_np), 1, inq, st);
     CUDA_TRY(cudaGetLastError());
     mark(12, st);
     // 5. final top-k

@@ -139,10 +139,18 @@ __device__ __forceinline__ void block_code8_ip(const double *__restrict__ x,
     }
 }
 
-// The refinement of one candidate row: the factor t of f_rescale_ex. (Loading the row's
-// blocks two ahead of the chain through three register buffers was measured: no gain, and
-// 168 instead of 40 registers.)
-template <int kForm>
+__device__ __forceinline__ void load_block(uint4 (&v)[4], const uint4 *__restrict__ row, int blk) {
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = __ldg(row + 4 * blk + u);
+}
+
+// The refinement of one candidate row: the factor t of f_rescale_ex. kPipelined (long rows,
+// D > 128): the row's 64-byte blocks are loaded two ahead of the one being accumulated
+// (three register buffers in rotation), so a thread keeps 128 bytes of its row in flight
+// during the fp64 chain (measured at D = 768: 0.90 instead of 1.62 ms for 2000 queries x
+// ~1500 candidates); at D <= 128 (two blocks per row) it gains nothing and its registers
+// (168 instead of 40) cost occupancy, so those rows are loaded block by block.
+template <int kForm, bool kPipelined>
 __device__ __forceinline__ float refine_row_term(const uint4 *__restrict__ row, int nblocks,
                                                  const double *__restrict__ x,
                                                  const uint32_t *__restrict__ qw,
@@ -151,11 +159,26 @@ __device__ __forceinline__ float refine_row_term(const uint4 *__restrict__ row, 
     double acc = 0.0;
     int ip = 0;
     float la0 = 0.0f, la1 = 0.0f;
-    for (int blk = 0; blk < nblocks; ++blk) {
-        uint4 v[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) v[u] = __ldg(row + 4 * blk + u);
-        block_code8_ip<kForm>(x + 64 * blk, qw, T, blk, v, acc, ip, la0, la1);
+    if (kPipelined) {
+        uint4 a[4], b[4], c[4];
+        load_block(a, row, 0);
+        if (nblocks > 1) load_block(b, row, 1);
+        for (int blk = 0; blk < nblocks; blk += 3) {
+            if (blk + 2 < nblocks) load_block(c, row, blk + 2);
+            block_code8_ip<kForm>(x + 64 * blk, qw, T, blk, a, acc, ip, la0, la1);
+            if (blk + 1 >= nblocks) break;
+            if (blk + 3 < nblocks) load_block(a, row, blk + 3);
+            block_code8_ip<kForm>(x + 64 * (blk + 1), qw, T, blk + 1, b, acc, ip, la0, la1);
+            if (blk + 2 >= nblocks) break;
+            if (blk + 4 < nblocks) load_block(b, row, blk + 4);
+            block_code8_ip<kForm>(x + 64 * (blk + 2), qw, T, blk + 2, c, acc, ip, la0, la1);
+        }
+    } else {
+        for (int blk = 0; blk < nblocks; ++blk) {
+            uint4 v[4];
+            load_block(v, row, blk);
+            block_code8_ip<kForm>(x + 64 * blk, qw, T, blk, v, acc, ip, la0, la1);
+        }
     }
     if (kForm == kRefineFullCode) return __fadd_rn(__double2float_rn(acc), kb);
     // ip1 exactly as the scan forms it; 128 * ip1 is exact
@@ -173,6 +196,8 @@ __device__ __forceinline__ float refine_row_term(const uint4 *__restrict__ row, 
 __host__ __device__ __forceinline__ size_t refine_smem(int D, int nprobe) {
     return (size_t)D * 8 + (size_t)D + (size_t)D * 16 + (size_t)nprobe * sizeof(ProbeInfo);
 }
+// kLongRows: D > 128 (the rows' blocks are loaded two ahead, see refine_row_term).
+template <bool kLongRows>
 __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, SearchView sv,
                                                                 int mode) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -275,11 +300,11 @@ __global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, Se
         const uint32_t id = mt.z;
         float t;  // the factor of f_rescale_ex
         if (form == kRefineSplitInt)
-            t = refine_row_term<kRefineSplitInt>(row, nblocks, x, qw, T, width, kb);
+            t = refine_row_term<kRefineSplitInt, kLongRows>(row, nblocks, x, qw, T, width, kb);
         else if (form == kRefineSplitLut)
-            t = refine_row_term<kRefineSplitLut>(row, nblocks, x, qw, T, width, kb);
+            t = refine_row_term<kRefineSplitLut, kLongRows>(row, nblocks, x, qw, T, width, kb);
         else
-            t = refine_row_term<kRefineFullCode>(row, nblocks, x, qw, T, width, kb);
+            t = refine_row_term<kRefineFullCode, kLongRows>(row, nblocks, x, qw, T, width, kb);
         const float ex_d = __fadd_rn(__fadd_rn(f.x, p.g), __fmul_rn(f.y, t));
         sv.cand_key[(size_t)q * sv.cap + i] = make_key(ex_d, id);
     }

@@ -343,11 +343,9 @@ __device__ __forceinline__ void half_add(uint32_t &s, uint32_t &c, uint32_t a, u
 constexpr int kCsaLevels = CORA_CSA_LEVELS;
 static_assert(kCsaLevels >= 2 && kCsaLevels <= 8, "adder tree depth");
 // Resident CTAs per SM that scan_kernel's register budget is sized for: 4 (<= 64 registers)
-// for D <= 128 with the integer estimator, where it was measured 3% faster than 2 or 3 on
-// config 2; 2 above, and with the LUT estimator (whose tables' shared memory allows 2 per SM
-// at D <= 128 anyway).
+// for D <= 128, where it was measured 3% faster than 2 or 3 on config 2; 2 above.
 #ifndef CORA_SCAN_MINB
-#define CORA_SCAN_MINB(G16, kLut) ((G16) == 1 && !(kLut) ? 4 : 2)
+#define CORA_SCAN_MINB(G16) ((G16) == 1 ? 4 : 2)
 #endif
 
 // sum_j 2^j sum_t popc(x_t & p'_{j,t}) for one group; P points at the group's plane words
@@ -507,28 +505,6 @@ __device__ __forceinline__ float ip_from_lut(const uint4 (&code)[G16], const flo
     return __fadd_rn(acc0, acc1);
 }
 
-// The same sum for D <= 128 from the code's nibbles pre-extracted as byte offsets into a
-// table group (nib[8w + n] = 4 * nibble n of word w), which one vector's pairs share: each
-// lookup is then an address add, a shared load and the fp32 add, in the same order.
-__device__ __forceinline__ void lut_offsets(const uint4 &code, uint32_t (&nib)[32]) {
-    const uint32_t x[4] = {code.x, code.y, code.z, code.w};
-#pragma unroll
-    for (int t = 0; t < 4; ++t)
-#pragma unroll
-        for (int n = 0; n < 8; ++n) nib[8 * t + n] = ((x[t] >> (28 - 4 * n)) & 0xFu) << 2;
-}
-__device__ __forceinline__ float ip_from_lut_offsets(const uint32_t (&nib)[32],
-                                                     const float *__restrict__ T) {
-    const char *Tb = reinterpret_cast<const char *>(T);
-    float acc0 = 0.0f, acc1 = 0.0f;
-#pragma unroll
-    for (int g = 0; g < 32; g += 2) {
-        acc0 = __fadd_rn(acc0, *reinterpret_cast<const float *>(Tb + g * 64 + nib[g]));
-        acc1 = __fadd_rn(acc1, *reinterpret_cast<const float *>(Tb + (g + 1) * 64 + nib[g + 1]));
-    }
-    return __fadd_rn(acc0, acc1);
-}
-
 // Widens query q's fp16 tables (4 D halves) into dst (kLutFloats fp32, zero past 4 D), one
 // 16-byte load per thread and step; the calling threads cover [tid0, tid0 + nthreads).
 template <int G16>
@@ -608,7 +584,7 @@ __device__ __forceinline__ void write_seeds(const SearchView &sv, int q, int r, 
 // kLut: ip1 from the LUT estimator (each pair's tables staged in shared memory as fp32;
 // items hold at most ScanShape::kLutPairs pairs).
 template <int G16, bool kWriteLows, bool kLut>
-__global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16, kLut)) scan_kernel(
+__global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel(
     IndexView ix, SearchView sv, const ScanItem *__restrict__ items,
     const uint32_t *__restrict__ n_items_ptr, const uint32_t *__restrict__ pairs,
     int *__restrict__ item_counter) {
@@ -780,10 +756,7 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16, kLut)) scan_
                 float4 f[V];
                 int bias[V];
                 uint32_t e[V][kBytes ? 32 * G16 : 1];
-                constexpr bool kLutOff = kLut && G16 == 1;  // nibble offsets extracted once
-                uint32_t nib[V][kLutOff ? 32 : 1];
                 (void)bias;
-                (void)nib;
                 bool valid[V];
 #pragma unroll
                 for (int v = 0; v < V; ++v) {
@@ -800,8 +773,6 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16, kLut)) scan_
                     }
                     if constexpr (kBytes)
                         split_code_bytes<G16>(code[v], e[v]);
-                    else if constexpr (kLutOff)
-                        lut_offsets(code[v][0], nib[v]);
                     else if constexpr (!kLut)
                         bias[v] = code_bias<G16>(code[v]);
                 }
@@ -815,9 +786,7 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16, kLut)) scan_
                         const int i = vb + v * kScanThreads + threadIdx.x;
                         const float4 pj = s_par[j];
                         float ip1;
-                        if constexpr (kLutOff) {
-                            ip1 = ip_from_lut_offsets(nib[v], reinterpret_cast<const float *>(P));
-                        } else if constexpr (kLut) {
+                        if constexpr (kLut) {
                             ip1 = ip_from_lut<G16>(code[v], reinterpret_cast<const float *>(P));
                         } else {
                             int ip;
