@@ -475,6 +475,37 @@ __device__ __forceinline__ int ip_int_from_bytes(const uint32_t (&e)[32 * G16],
     return (acc[0] + acc[1]) + (acc[2] + acc[3]);
 }
 
+// The same sum for D > 128, where the whole split code would not fit in registers: each
+// 128-dim group of the code is split when it is used (32 logic ops, then 32 dp4a against the
+// group's 32 query byte words).
+#ifndef CORA_SCAN_DP4A_WIDE
+#define CORA_SCAN_DP4A_WIDE 1
+#endif
+constexpr bool kScanDp4aWide = CORA_SCAN_DP4A_WIDE != 0;
+// cw: the vector's code words in the staged tile (group g at cw[g * stride]).
+template <int G16>
+__device__ __forceinline__ int ip_int_from_bytes_grouped(const uint4 *__restrict__ cw, int stride,
+                                                         const uint32_t *__restrict__ Q) {
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll 1
+    for (int g = 0; g < G16; ++g) {  // rolled: one group's query words in registers at a time
+        const uint4 c = cw[g * stride];
+        const uint32_t x[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int w = 4 * g + t;
+            const uint4 a = *reinterpret_cast<const uint4 *>(Q + 8 * w);
+            const uint4 b = *reinterpret_cast<const uint4 *>(Q + 8 * w + 4);
+            const uint32_t qa[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int s = 0; s < 8; ++s)
+                acc[s & 3] = __dp4a(static_cast<int>((x[t] >> s) & 0x01010101u),
+                                    static_cast<int>(qa[s]), acc[s & 3]);
+        }
+    }
+    return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+}
+
 // Copies a query's two's-complement bit-planes into shared memory as offset-binary planes
 // (plane 7 inverted), the form ip_int_from_planes consumes.
 __device__ __forceinline__ uint32_t offset_binary_word(uint32_t w, int word_index, int W4) {
@@ -594,6 +625,8 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
     // D <= 128), offset-binary bit-planes otherwise; both are 8 * W4 words per query. With
     // the LUT estimator: kLutFloats fp32 table entries per pair.
     constexpr bool kBytes = kScanDp4a && G16 == 1 && !kLut;
+    // D > 128: byte words too, the code split group by group (ip_int_from_bytes_grouped)
+    constexpr bool kBytesWide = kScanDp4a && kScanDp4aWide && G16 > 1 && !kLut;
     constexpr int kQB = kLut ? Sh::kLutFloats : 8 * W4;  // 32-bit words per pair
     extern __shared__ __align__(16) unsigned char smem_raw[];
     uint4 *stage = reinterpret_cast<uint4 *>(smem_raw);
@@ -706,8 +739,8 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
             for (int i = threadIdx.x; i < pc * kQB; i += blockDim.x) {
                 const int j = i / kQB, r = i - j * kQB;
                 const uint32_t *pl = sv.planes + (size_t)s_q[j] * 8 * W4;
-                s_planes[i] = kBytes ? query_byte_word(pl, r >> 3, r & 7, W4)
-                                     : offset_binary_word(pl[r], r, W4);
+                s_planes[i] = (kBytes || kBytesWide) ? query_byte_word(pl, r >> 3, r & 7, W4)
+                                                     : offset_binary_word(pl[r], r, W4);
             }
         }
         __syncthreads();
@@ -773,7 +806,7 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
                     }
                     if constexpr (kBytes)
                         split_code_bytes<G16>(code[v], e[v]);
-                    else if constexpr (!kLut)
+                    else if constexpr (!kLut && !kBytesWide)
                         bias[v] = code_bias<G16>(code[v]);
                 }
                 // lows pass: every pair in order; main pass: the pairs this warp's chunk keeps
@@ -792,6 +825,8 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
                             int ip;
                             if constexpr (kBytes)
                                 ip = ip_int_from_bytes<G16>(e[v], P);
+                            else if constexpr (kBytesWide)  // (V == 1 for G16 > 1)
+                                ip = ip_int_from_bytes_grouped<G16>(sb + i, TV, P);
                             else
                                 ip = ip_int_from_planes<G16>(code[v], P, bias[v]);
                             // ip1 = width * ip_int (+ 0 in the reference: width >= 1e-30 and
