@@ -218,6 +218,22 @@ class ClockSampler:
                 "samples": len(self.rows)}
 
 
+def launches_per_search(nprobe, k, mode, shards, estimator, metric):
+    """Kernels one search launches: rotation, probe GEMM, probe selection (warp kernel + its
+    block fallback when nprobe <= 32), seed refine, threshold, main grouping (4), main scan,
+    refine, merge (threshold and final top-k: warp kernel + block fallback each when
+    k <= 32); with stored vanguard lows also vanguard grouping (4), lows scan, seed selection
+    (warp + block fallback when keep <= 128) and the lows filter (pair list + filter), else
+    one vanguard rescan; +2 exchange steps (gather_threshold / gather_merge) when sharded;
+    +1 LUT build for the LUT estimator; +1 additive-term kernel for inner product."""
+    sel = 2 if nprobe <= 32 else 1
+    vsel = 2 if max(k, 20) <= 128 else 1
+    topk = 2 if k <= 32 else 1
+    return (9 + sel + 2 * topk + ((7 + vsel) if mode == 1 else 1)
+            + (2 if shards > 1 else 0) + (1 if estimator == "lut" else 0) + (1 if metric else 0))
+
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -600,7 +616,8 @@ def run_stream(args, name, cfg):
         roofline=roofline, cpu_baseline=cpu_base,
         e2e=dict(value=e2e_qps, unit="queries/s", h2d_bytes_per_step=nq * cfg["dim"] * 4,
                  d2h_bytes_per_step=nq * k * 8),
-        gpu_launches=None, clocks=clk.summary())
+        gpu_launches=launches_per_search(chosen, k, mode, 1, estimator, metric) * args.steps
+        * len(rep_ms), clocks=clk.summary())
     emit(line)
     eng.close()
 
@@ -619,6 +636,13 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shards", type=int, default=0,
                     help="GPUs per copy of the index (cluster shards); 0 = as memory requires")
+    ap.add_argument("--estimator", choices=["auto", "bitwise", "lut"], default="auto",
+                    help="the scan's estimator; auto times whichever of the reference's two "
+                         "kernel types reaches the recall target fastest (forcing one also skips "
+                         "the full-code side measurement: for short profiling runs)")
+    ap.add_argument("--min-seconds", type=float, default=1.0,
+                    help="repeat the timed K steps until they span this long (at least 3 "
+                         "repeats when > 0; 0: one repeat, for profiling)")
     ap.add_argument("--no-sharded", action="store_true",
                     help="with N > 1 GPUs, skip the cluster-sharded sub-measurement")
     ap.add_argument("--queries", type=int, default=0,
@@ -808,6 +832,8 @@ def main():
         return total(e0.elapsed_time(e1) / reps, dist.ReduceOp.MAX if world > 1 else None)
 
     estimators = {"bitwise": cb.KernelType.Bitwise, "lut": cb.KernelType.Lut4Bit}
+    if args.estimator != "auto":
+        estimators = {args.estimator: estimators[args.estimator]}
     sweeps, candidates = {}, {}
     for name, kt in estimators.items():
         eng.set_ip_kernel_type(kt)
@@ -822,7 +848,7 @@ def main():
     eng.set_ip_kernel_type(cb.KernelType.Bitwise)
     eng.set_refine_full_code(True)
     full_code = {}
-    for npb in nprobes:
+    for npb in (nprobes if args.estimator == "auto" else []):
         search_dev(npb)
         r = recall_now()
         if r >= TARGET_RECALL or npb == nprobes[-1]:
@@ -834,8 +860,8 @@ def main():
     if candidates:
         estimator = min(candidates, key=lambda n: candidates[n]["ms"])
         chosen = candidates[estimator]["nprobe"]
-    else:  # no configuration reaches the target: the default estimator at the largest nprobe
-        estimator, chosen = "bitwise", nprobes[-1]
+    else:  # no configuration reaches the target: the first estimator at the largest nprobe
+        estimator, chosen = next(iter(estimators)), nprobes[-1]
     eng.set_ip_kernel_type(estimators[estimator])
     sweep = sweeps[estimator]
     log(f"[bench] recall sweeps {sweeps} -> {estimator} estimator, nprobe {chosen}")
@@ -879,7 +905,8 @@ def main():
 
     with ClockSampler(local) as clk:
         per_step = [timed_repeat()]
-        n_rep = torch.tensor([max(3, min(200, int(1000.0 / max(per_step[0] * args.steps, 1e-3)) + 1))],
+        want = int(1000.0 * args.min_seconds / max(per_step[0] * args.steps, 1e-3)) + 1
+        n_rep = torch.tensor([1 if args.min_seconds <= 0 else max(3, min(200, want))],
                              dtype=torch.int64, device=dev)
         if world > 1:
             dist.broadcast(n_rep, 0)
@@ -961,18 +988,7 @@ def main():
                          "exceed the physical DRAM traffic, which the scan kernel keeps at a "
                          "fraction of it: it is bound by its integer dot-product pipe); "
                          "search_per_query = (B_scan + B_refine) x QPS; rank 0's launches")
-    # Kernels per search: rotation, probe GEMM, probe selection (warp kernel + its block
-    # fallback when nprobe <= 32), seed refine, threshold, main grouping (4), main scan,
-    # refine, merge (threshold and final top-k: warp kernel + block fallback each when
-    # k <= 32); with stored vanguard lows also vanguard grouping (4), lows scan, seed
-    # selection (warp + block fallback when keep <= 32) and the lows filter (pair list +
-    # filter), else one vanguard rescan; +2 exchange steps (gather_threshold / gather_merge)
-    # when sharded.
-    sel = 2 if chosen <= 32 else 1
-    vsel = 2 if max(k, 20) <= 32 else 1
-    topk = 2 if k <= 32 else 1
-    per_search = (9 + sel + 2 * topk + ((7 + vsel) if mode == 1 else 1)
-                  + (2 if shards > 1 else 0) + (1 if estimator == "lut" else 0))
+    per_search = launches_per_search(chosen, k, mode, shards, estimator, metric=0)
     launches = per_search * args.steps * len(rep_ms)
 
     cpu_base = None

@@ -1169,8 +1169,13 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
             // one warp per pair; the rare pair with too many keys below the first bound
             // is finished by a grid-stride block selection over the queued list
             CUDA_TRY(cudaMemsetAsync(select_fallback.p, 0, 4, st));
-            vanguard_select_warp_kernel<<<(n_van + 7) / 8, 256, 0, st>>>(ix, sv, own,
-                                                                         select_fallback.p);
+            const unsigned grid = (n_van + 7) / 8;
+            if (keep <= 32)
+                vanguard_select_warp_kernel<1><<<grid, 256, 0, st>>>(ix, sv, own, select_fallback.p);
+            else if (keep <= 64)
+                vanguard_select_warp_kernel<2><<<grid, 256, 0, st>>>(ix, sv, own, select_fallback.p);
+            else
+                vanguard_select_warp_kernel<4><<<grid, 256, 0, st>>>(ix, sv, own, select_fallback.p);
             CUDA_TRY(cudaGetLastError());
             vanguard_select_kernel<<<static_cast<unsigned>(2 * num_sms), 256, sm, st>>>(
                 ix, sv, own, select_fallback.p);

@@ -1009,14 +1009,16 @@ __global__ void __launch_bounds__(256) vanguard_filter_kernel(IndexView ix, Sear
 }
 
 // ---- warp-level seed selection for keep <= 32 -----------------------------------------
-constexpr int kWarpSelectMax = 32;   // largest `keep` handled one warp per pair
+constexpr int kWarpSelectMax = 128;  // largest `keep` handled one warp per pair
 constexpr int kWarpSelectBuf = 256;  // keys at or below the first threshold a warp may hold
 
-// One warp per vanguard pair (8 per CTA), keep <= 32. The keep-th smallest of the 32 lane
-// minima bounds the keep-th smallest key from above, so every seed is among the keys at or
-// below it; those (normally a few dozen) are collected and sorted. A pair whose collection
-// exceeds kWarpSelectBuf is queued in fallback[1..] (count in fallback[0]) for
+// One warp per vanguard pair (8 per CTA), keep <= 32 T (T <= 4). Each lane keeps its T
+// smallest lows; the keep-th smallest of those 32 T values bounds the keep-th smallest key
+// from above (keep of them lie at or below it), so every seed is among the keys at or below
+// it; those (normally little more than keep) are collected and sorted. A pair whose
+// collection exceeds kWarpSelectBuf is queued in fallback[1..] (count in fallback[0]) for
 // vanguard_select_kernel.
+template <int T>
 __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
     IndexView ix, SearchView sv, const uint8_t *__restrict__ owned,
     uint32_t *__restrict__ fallback) {
@@ -1032,24 +1034,44 @@ __global__ void __launch_bounds__(256) vanguard_select_warp_kernel(
     const float4 *L4 = reinterpret_cast<const float4 *>(sv.lows + sv.vg_off[pi]);
     const float T0 = sv.T0[q];
     const int S = sv.keep;
-    // Pass 1: each lane's smallest low (NaN lows drop out of fminf). tau_f, the S-th
-    // smallest lane minimum, bounds the seeds: when tau_f < T0 the S lanes at or below it
-    // hold S lows <= tau_f below T0, so the S smallest keys all have low <= tau_f; when
-    // tau_f >= T0 every low < T0 is collected.
+    // Pass 1: each lane's T smallest lows (branch-free insertion; NaN lows drop out of
+    // fminf / fmaxf). tau_f, the S-th smallest of the 32 T values, bounds the seeds: when
+    // tau_f < T0, S values at or below it are lows below T0, so the S smallest keys all have
+    // low <= tau_f; when tau_f >= T0 every low < T0 is collected.
     const float inf = __int_as_float(0x7f800000);
-    float mn = inf;
+    float mn[T];
+#pragma unroll
+    for (int t = 0; t < T; ++t) mn[t] = inf;
     for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
         float l[4 * kLowsUnroll];
         load_lows4(L4, n, b4 + lane, l);
 #pragma unroll
-        for (int e = 0; e < 4 * kLowsUnroll; ++e) mn = fminf(mn, l[e]);
+        for (int e = 0; e < 4 * kLowsUnroll; ++e) {
+            float x = fminf(l[e], inf);  // NaN -> inf: an inserted NaN would duplicate a value
+#pragma unroll
+            for (int t = 0; t < T; ++t) {
+                const float lo = fminf(mn[t], x);
+                x = fmaxf(mn[t], x);
+                mn[t] = lo;
+            }
+        }
     }
-    const float tau_f = unord_f32(static_cast<uint32_t>(
-        __shfl_sync(0xffffffffu, warp_sort_lane_keys(make_key(mn, lane), lane), S - 1) >> 32));
+    uint64_t *b = buf[w];
+    float tau_f;
+    if (T == 1) {
+        tau_f = unord_f32(static_cast<uint32_t>(
+            __shfl_sync(0xffffffffu, warp_sort_lane_keys(make_key(mn[0], lane), lane), S - 1) >> 32));
+    } else {
+#pragma unroll
+        for (int t = 0; t < T; ++t) b[lane * T + t] = make_key(mn[t], lane * T + t);
+        __syncwarp();
+        warp_sort_smem(b, 32 * T, lane);
+        tau_f = unord_f32(static_cast<uint32_t>(b[S - 1] >> 32));
+        __syncwarp();
+    }
     // Pass 2: count the lows < T0 and collect every key with low < T0 and low <= tau_f (-0
     // and +0 compare equal here, so the set contains every key the exact bound would take)
     const float *L = sv.lows + sv.vg_off[pi];
-    uint64_t *b = buf[w];
     uint32_t m = 0, cnt = 0;
     for (uint32_t b4 = 0; 4 * b4 < n; b4 += 32 * kLowsUnroll) {
         float l[4 * kLowsUnroll];
