@@ -242,15 +242,16 @@ def measured_peaks():
     return 6650.0, "fallback (6.65 TB/s)"
 
 
-def profiled_traffic(config):
-    """DRAM bytes (read + write) of one launch of the scan's lows pass (the dominant kernel),
-    from the committed ncu summary of the full-size config-2 workload (None for other
-    configs, or before that capture exists)."""
+def profiled_traffic(config, estimator):
+    """DRAM bytes (read + write) of one launch of the scan's lows pass (the dominant kernel)
+    with the given estimator, from the committed ncu summary of the full-size config-2
+    workload (None for other configs, or before that capture exists)."""
     p = ROOT / "profiles" / "scan_kernel_cfg2_dram.md"
     if config != "cfg2" or not p.exists():
         return None
+    key = f"dram_bytes_lows_pass_full_size_{estimator}:"
     for line in p.read_text().splitlines():
-        if line.startswith("dram_bytes_lows_pass_full_size:"):
+        if line.startswith(key):
             return int(line.split(":")[1])
     return None
 
@@ -467,10 +468,13 @@ def run_stream(args, name, cfg):
 
     # every (estimator, nprobe) result of the sweep, scored exactly in one pass
     estimators = {"bitwise": cb.KernelType.Bitwise, "lut": cb.KernelType.Lut4Bit}
+    if args.estimator != "auto":
+        estimators = {args.estimator: estimators[args.estimator]}
+    nprobes = [args.nprobe] if args.nprobe else cfg["nprobes"]
     runs, results = [], []
     for ename, kt in estimators.items():
         eng.set_ip_kernel_type(kt)
-        for npb in cfg["nprobes"]:
+        for npb in nprobes:
             search_dev(npb)
             torch.cuda.synchronize()
             eng.check_device()
@@ -486,7 +490,7 @@ def run_stream(args, name, cfg):
         r = synthetic.distance_recall(gt_ids, gt_d, results[j], exact[:, j * k:(j + 1) * k], k)
         sweeps.setdefault(ename, {})[npb] = round(r, 4)
     for ename, kt in estimators.items():
-        for npb in cfg["nprobes"]:
+        for npb in nprobes:
             if sweeps[ename][npb] >= TARGET_RECALL:
                 eng.set_ip_kernel_type(kt)
                 candidates[ename] = dict(nprobe=npb, recall=sweeps[ename][npb], ms=quick_ms(npb))
@@ -495,7 +499,7 @@ def run_stream(args, name, cfg):
         estimator = min(candidates, key=lambda n: candidates[n]["ms"])
         chosen = candidates[estimator]["nprobe"]
     else:
-        estimator, chosen = "bitwise", cfg["nprobes"][-1]
+        estimator, chosen = next(iter(estimators)), nprobes[-1]
     eng.set_ip_kernel_type(estimators[estimator])
     log(f"[bench] recall sweeps {sweeps} -> {estimator} estimator, nprobe {chosen}")
 
@@ -526,7 +530,8 @@ def run_stream(args, name, cfg):
 
     with ClockSampler(0) as clk:
         per_step = [timed_repeat()]
-        for _ in range(max(2, min(50, int(1000.0 / max(per_step[0] * args.steps, 1e-3))))):
+        want = int(1000.0 * args.min_seconds / max(per_step[0] * args.steps, 1e-3)) + 1
+        for _ in range(0 if args.min_seconds <= 0 else max(2, min(50, want - 1))):
             per_step.append(timed_repeat())
     eng.check_device()
     rep_ms = np.array(per_step)
@@ -971,7 +976,7 @@ def main():
         kern_ms = stage_avg["vanguard_scan"] + stage_avg["main_scan"]
         kern_bytes, kern = scan_bytes, "scan_kernel (vanguard rescan + main pass)"
     achieved = kern_bytes / (kern_ms / 1e3) / 1e9 if kern_ms > 0 else None
-    traffic = profiled_traffic(args.config) if (world == 1 and mode == 1) else None
+    traffic = profiled_traffic(args.config, estimator) if (world == 1 and mode == 1) else None
     # whole search, per-query accounting: (B_scan + B_refine) over this GPU's search time,
     # B_refine = refined survivors x (7D/8 + 8 + 4) bytes
     b_search = scan_bytes + local_refined * (7 * D // 8 + 12)
