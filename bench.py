@@ -218,6 +218,13 @@ class ClockSampler:
                 "samples": len(self.rows)}
 
 
+def apply_tuning(engine, pairs):
+    """cora_set_tuning for each KEY=VALUE of --tuning."""
+    for kv in pairs:
+        key, _, val = kv.partition("=")
+        engine.set_tuning(key, int(val))
+
+
 def launches_per_search(nprobe, k, mode, shards, estimator, metric):
     """Kernels one search launches: rotation, probe GEMM, probe selection (warp kernel + its
     block fallback when nprobe <= 32), seed refine, threshold, main grouping (4), main scan,
@@ -337,6 +344,7 @@ def measure_sharded(args, sd, q, k, nprobe, kernel_type, eng_single, local, worl
     from coraanns_b200.shard import ShardedIndex
     nq = q.shape[0]
     six = ShardedIndex(local)
+    apply_tuning(six.engine, args.tuning)
     six.engine.set_ip_kernel_type(kernel_type)
     six.load_search_data(sd)
     six.prepare_workspace(nq, k, nprobe)
@@ -441,6 +449,7 @@ def run_stream(args, name, cfg):
     torch.cuda.empty_cache()
 
     eng = cb.HybridIndex(0)
+    apply_tuning(eng, args.tuning)
     eng.set_vanguard_size(cfg["vanguard"])
     eng.set_queue_capacity(1 << 28)  # candidate records per search (16 B each)
     t2 = time.time()
@@ -648,6 +657,9 @@ def main():
     ap.add_argument("--min-seconds", type=float, default=1.0,
                     help="repeat the timed K steps until they span this long (at least 3 "
                          "repeats when > 0; 0: one repeat, for profiling)")
+    ap.add_argument("--tuning", action="append", default=[], metavar="KEY=VALUE",
+                    help="engine tuning key (cora_set_tuning) applied to every engine, e.g. "
+                         "refine_lanes=4; repeatable")
     ap.add_argument("--no-sharded", action="store_true",
                     help="with N > 1 GPUs, skip the cluster-sharded sub-measurement")
     ap.add_argument("--queries", type=int, default=0,
@@ -785,6 +797,7 @@ def main():
         groups = [dist.new_group(list(range(g * shards, (g + 1) * shards)))
                   for g in range(replicas)]
         six = ShardedIndex(local, group=groups[rep])
+        apply_tuning(six.engine, args.tuning)
         six.load_search_data(sd)
         six.prepare_workspace(nq, k, max(nprobes))
         eng = six.engine
@@ -795,6 +808,7 @@ def main():
                 six.search_device(qs, k, nprobe, out_d, out_i)
     else:
         eng = cb.HybridIndex(local)
+        apply_tuning(eng, args.tuning)
         eng.load_search_data(sd)
         eng.prepare_workspace(nq, k, max(nprobes))
 

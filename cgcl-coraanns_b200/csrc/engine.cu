@@ -219,11 +219,54 @@ inline void launch_guarded_select(float *approx, const float *chunk_min, uint64_
     CUDA_TRY(cudaGetLastError());
 }
 
-// refine_kernel for one query per CTA; rows longer than 128 bytes load their blocks ahead.
+// refine_kernel instantiation for rows of D bytes and `lanes` lanes per row (8 needs D % 128
+// == 0): kC, the chunks a lane loads per round, is its chunk count D / (16 lanes) rounded up
+// to one of 1, 2, 4, 6, 8 (with one lane per row kRefineRowChunks: 4, half of the eight
+// partials per round, or 8; rows longer than kC chunks per lane take several rounds).
+template <int kForm>
+RefineKernelFn pick_refine(int D, int lanes) {
+    const int nl = D / (16 * lanes);
+    if (lanes == 1) return kRefineRowChunks == 4 ? refine_kernel<1, 4, kForm> : refine_kernel<1, 8, kForm>;
+    if (lanes == 8) {
+        if (nl <= 1) return refine_kernel<8, 1, kForm>;
+        if (nl <= 2) return refine_kernel<8, 2, kForm>;
+        if (nl <= 4) return refine_kernel<8, 4, kForm>;
+        if (nl <= 6) return refine_kernel<8, 6, kForm>;
+        return refine_kernel<8, 8, kForm>;
+    }
+    if (nl <= 2) return refine_kernel<4, 2, kForm>;
+    if (nl <= 4) return refine_kernel<4, 4, kForm>;
+    if (nl <= 6) return refine_kernel<4, 6, kForm>;
+    return refine_kernel<4, 8, kForm>;
+}
+
+// Lanes per refine row: 1 or 4 when asked for, 8 when asked for and D % 128 == 0 (else 4);
+// by default 4 for rows longer than 128 bytes and 1 otherwise (measured at D = 768, cfg4s:
+// candidates 0.80 / 0.93 / 0.88 ms with 4 / 1 / 8 lanes; at D = 128, config 2: 0.283 /
+// 0.235 / 0.399 ms).
+inline int refine_lanes_for(int D, int want) {
+    if (want == 8) return D % 128 == 0 ? 8 : 4;
+    if (want == 4 || want == 1) return want;
+    return D > 128 ? 4 : 1;
+}
+
+// One query per CTA: the exact refinement (thread per candidate) when an exact base is set,
+// else the lane-shared refine_kernel of the search's refinement form.
 inline void launch_refine(const IndexView &ix, const SearchView &sv, int D, int np, int mode,
-                          int nq, cudaStream_t st) {
+                          int nq, int lanes_want, cudaStream_t st) {
     const size_t sm = refine_smem(D, np);
-    auto *kern = D > 128 ? refine_kernel<true> : refine_kernel<false>;
+    RefineKernelFn kern;
+    if (ix.exact_base) {
+        kern = refine_exact_kernel;
+    } else {
+        const int lanes = refine_lanes_for(D, lanes_want);
+        if (sv.refine_full_code)
+            kern = pick_refine<kRefineFullCode>(D, lanes);
+        else if (sv.lut_mode)
+            kern = pick_refine<kRefineSplitLut>(D, lanes);
+        else
+            kern = pick_refine<kRefineSplitInt>(D, lanes);
+    }
     CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
     kern<<<static_cast<unsigned>(nq), kRefineThreads, sm, st>>>(ix, sv, mode);
     CUDA_TRY(cudaGetLastError());
@@ -303,6 +346,7 @@ struct Engine {
     uint64_t lows_budget = 16ull << 30;
     int warp_select_limit = kWarpSelectBuf;  // see vanguard_select_warp_kernel
     int topk_warp_limit = kWarpTopBuf;       // see topk_warp_kernel
+    int refine_lanes = 0;                    // lanes per refine row: 0 default, 1, 4, 8
 
     // workspace
     bool ws_ready = false;
@@ -347,13 +391,13 @@ struct Engine {
         float *d_od = nullptr;
         uint32_t *d_oi = nullptr;
         cudaStream_t st = nullptr;
-        int wsl = 0, twl = 0;
+        int wsl = 0, twl = 0, rl = 0;
         bool reuse = false, full_code = false, lut = false;
         int metric = 0;
         bool same(const GraphKey &o) const {
             return d_q == o.d_q && nq == o.nq && k == o.k && np == o.np && ws_gen == o.ws_gen &&
                    vanguard == o.vanguard && d_od == o.d_od && d_oi == o.d_oi && st == o.st &&
-                   wsl == o.wsl && twl == o.twl && reuse == o.reuse &&
+                   wsl == o.wsl && twl == o.twl && rl == o.rl && reuse == o.reuse &&
                    full_code == o.full_code && lut == o.lut && metric == o.metric;
         }
     };
@@ -1056,6 +1100,7 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
     key.st = st;
     key.wsl = warp_select_limit;
     key.twl = topk_warp_limit;
+    key.rl = refine_lanes;
     key.reuse = cross_query_reuse;
     key.full_code = refine_full_code;
     key.lut = lut_mode();
@@ -1185,7 +1230,7 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
         CUDA_TRY(cudaGetLastError());
     }
     mark(6, st);
-    launch_refine(ix, sv, static_cast<int>(D), static_cast<int>(np), 0, inq, st);
+    launch_refine(ix, sv, static_cast<int>(D), static_cast<int>(np), 0, inq, refine_lanes, st);
     CUDA_TRY(cudaGetLastError());
     mark(7, st);
     launch_topk(0, nullptr, nullptr, seed_keys_out, st);
@@ -1292,7 +1337,7 @@ void Engine::enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uin
     }
     if (gpu_filter_timing) CUDA_TRY(cudaEventRecord(ev_filter1, st));
     mark(11, st);
-    launch_refine(ix, sv, static_cast<int>(D), static_cast<int>(last_np), 1, inq, st);
+    launch_refine(ix, sv, static_cast<int>(D), static_cast<int>(last_np), 1, inq, refine_lanes, st);
     CUDA_TRY(cudaGetLastError());
     mark(12, st);
     // 5. final top-k
@@ -1950,6 +1995,10 @@ int cora_set_tuning(cora_engine *engine, const char *key, int64_t value) {
             if (value < 0 || value > cora::kWarpTopBuf)
                 cora::fail(CORA_EINVAL, "topk_warp_limit must be in [0, 256]");
             e.topk_warp_limit = static_cast<int>(value);
+        } else if (k == "refine_lanes") {
+            if (value != 0 && value != 1 && value != 4 && value != 8)
+                cora::fail(CORA_EINVAL, "refine_lanes must be 0, 1, 4 or 8");
+            e.refine_lanes = static_cast<int>(value);
         } else if (k == "vanguard_lows_budget") {
             if (value < 0) cora::fail(CORA_EINVAL, "vanguard_lows_budget must be >= 0");
             if (e.ws_ready) cora::fail(CORA_ESTATE, "set the lows budget before prepare_workspace");

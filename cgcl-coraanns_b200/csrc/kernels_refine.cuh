@@ -22,8 +22,9 @@ namespace cora {
 #ifndef CORA_REFINE_THREADS
 #define CORA_REFINE_THREADS 128
 #endif
-// threads per query in refine_kernel; measured on config 2 (candidate refine): 64 -> 0.202
-// ms, 128 -> 0.192, 256 -> 0.188 (seed refine 0.080 / 0.072 / 0.075)
+// threads per query (one CTA) of the refine kernels; measured on config 2 with one thread
+// per candidate: 64 -> 0.202 ms, 128 -> 0.192, 256 -> 0.188 (seed refine 0.080 / 0.072 /
+// 0.075)
 constexpr int kRefineThreads = CORA_REFINE_THREADS;
 
 struct ProbeInfo {  // per (query, probe rank), staged in shared memory by refine_kernel
@@ -91,222 +92,347 @@ __global__ void __launch_bounds__(256) build_refine_rows_kernel(
 // product (opt-in).
 enum RefineForm : int { kRefineSplitInt = 0, kRefineSplitLut = 1, kRefineFullCode = 2 };
 
-// One 64-dim block (index blk) of a refine row (v: its 64 codes c = 128 b + u, 4 per word,
-// dimension order) against the rotated query x (fp64, shared memory), continuing the fp64
-// chain `acc` in ascending dimension order (every product is exact in fp64). Each byte
-// becomes the double c (or u = c & 127) exactly as (2^52 + c) - 2^52 from its bit pattern,
-// so the loop runs no conversion instructions.
+// Summation order of the refinement's fp64 inner products (the kernels below and the oracle
+// form them identically): a refine row is read as 16-byte chunks, chunk c = dimensions
+// 16c .. 16c + 15. Partial sum j (j = 0 .. 7) runs over the chunks c with c % 8 == j, chunks
+// ascending and dimensions ascending within a chunk, one fma per dimension (every product
+// x_d * c_d is exact in fp64); the eight partials are combined as
+// ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7)) and the sum is rounded once to fp32.
+// Partials without chunks (D < 128) stay +0.
+constexpr int kRefinePartials = 8;
+// Shared-memory stride of a chunk's 16 query doubles: 2 doubles of padding put the chunks
+// that the lanes of a row read at once (128 bytes apart otherwise: one bank) into distinct
+// banks.
+constexpr int kXChunk = 18;
+// Chunks a lane loads per round with one lane per row (4 or 8).
+#ifndef CORA_REFINE_ROW_CHUNKS
+#define CORA_REFINE_ROW_CHUNKS 4
+#endif
+constexpr int kRefineRowChunks = CORA_REFINE_ROW_CHUNKS;
+
+// One chunk of a refine row (v: the 8-bit codes c = 128 b + u of dims 16c .. 16c + 15, 4 per
+// word, dimension order) against the rotated query (xc = x + 16 c, fp64 in shared memory),
+// continuing partial sum `acc`. Each byte becomes the double c (or u = c & 127) exactly as
+// (2^52 + c) - 2^52 from its bit pattern.
 //   kRefineSplitInt: acc accumulates <x, u>, and ip accumulates sum_i b_i qint_i with dp4a
-//     over the code words' top bits and the query's qint bytes (qw: qint of dims 4t .. 4t + 3
-//     as the signed bytes of word t), exact in int32;
-//   kRefineSplitLut: acc accumulates <x, u>, and la0 / la1 the LUT estimator's sums: row
-//     word t (dims 4t .. 4t + 3) is nibble group t, whose pattern is the four code bits (dim
-//     4t at bit 3); even groups go to la0, odd ones to la1, in ascending order (the scan's
-//     order, ip_from_lut), from the fp32 tables T (16 per group);
+//     over the code words' top bits and the query's qint bytes (qv: qint of the chunk's dims,
+//     4 per word as signed bytes), exact in int32;
+//   kRefineSplitLut: acc accumulates <x, u> (the LUT sums are formed separately);
 //   kRefineFullCode: acc accumulates <x, 128 b + u>.
 template <int kForm>
-__device__ __forceinline__ void block_code8_ip(const double *__restrict__ x,
-                                               const uint32_t *__restrict__ qw,
-                                               const float *__restrict__ T, int blk,
-                                               const uint4 (&v)[4], double &acc, int &ip,
-                                               float &la0, float &la1) {
+__device__ __forceinline__ void chunk_code8_ip(const double *__restrict__ xc, const uint4 qv,
+                                               const uint4 v, double &acc, int &ip) {
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t q4[4] = {qv.x, qv.y, qv.z, qv.w};
+    const double2 *x2 = reinterpret_cast<const double2 *>(xc);
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-        const uint32_t w4[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+    for (int h = 0; h < 4; ++h) {
+        const uint32_t w = kForm == kRefineFullCode ? w4[h] : (w4[h] & 0x7F7F7F7Fu);
+        if (kForm == kRefineSplitInt)
+            ip = __dp4a(static_cast<int>((w4[h] >> 7) & 0x01010101u), static_cast<int>(q4[h]), ip);
+        const double2 xa = x2[2 * h], xb = x2[2 * h + 1];
+        const double xs[4] = {xa.x, xa.y, xb.x, xb.y};
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-            const uint32_t w = kForm == kRefineFullCode ? w4[h] : (w4[h] & 0x7F7F7F7Fu);
-            if (kForm == kRefineSplitInt)
-                ip = __dp4a(static_cast<int>((w4[h] >> 7) & 0x01010101u),
-                            static_cast<int>(qw[16 * blk + 4 * t + h]), ip);
-            if (kForm == kRefineSplitLut) {
-                const uint32_t pat = ((w4[h] >> 4) & 8u) | ((w4[h] >> 13) & 4u) |
-                                     ((w4[h] >> 22) & 2u) | (w4[h] >> 31);
-                const float e = T[(16 * blk + 4 * t + h) * 16 + pat];
-                if (h & 1)
-                    la1 = __fadd_rn(la1, e);
-                else
-                    la0 = __fadd_rn(la0, e);
-            }
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const uint32_t c = __byte_perm(w, 0u, 0x4440u | i);
-                const double cd = __dsub_rn(__hiloint2double(0x43300000, static_cast<int>(c)),
-                                            4503599627370496.0);
-                acc = __fma_rn(x[16 * t + 4 * h + i], cd, acc);
-            }
+        for (int i = 0; i < 4; ++i) {
+            const uint32_t c = __byte_perm(w, 0u, 0x4440u | i);
+            const double cd = __dsub_rn(__hiloint2double(0x43300000, static_cast<int>(c)),
+                                        4503599627370496.0);
+            acc = __fma_rn(xs[i], cd, acc);
         }
     }
 }
 
-__device__ __forceinline__ void load_block(uint4 (&v)[4], const uint4 *__restrict__ row, int blk) {
+// The LUT estimator's nibble patterns of a chunk's four 4-dimension groups, group k at bits
+// 4k .. 4k + 3: the group's code bits b (the bytes' top bits), its first dimension at bit 3
+// of the pattern (the order of ip_from_lut).
+__device__ __forceinline__ uint32_t chunk_patterns(const uint4 v) {
+    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+    uint32_t out = 0;
 #pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = __ldg(row + 4 * blk + u);
-}
-
-// The refinement of one candidate row: the factor t of f_rescale_ex. kPipelined (long rows,
-// D > 128): the row's 64-byte blocks are loaded two ahead of the one being accumulated
-// (three register buffers in rotation), so a thread keeps 128 bytes of its row in flight
-// during the fp64 chain (measured at D = 768: 0.90 instead of 1.62 ms for 2000 queries x
-// ~1500 candidates); at D <= 128 (two blocks per row) it gains nothing and its registers
-// (168 instead of 40) cost occupancy, so those rows are loaded block by block.
-template <int kForm, bool kPipelined>
-__device__ __forceinline__ float refine_row_term(const uint4 *__restrict__ row, int nblocks,
-                                                 const double *__restrict__ x,
-                                                 const uint32_t *__restrict__ qw,
-                                                 const float *__restrict__ T, float width,
-                                                 float kb) {
-    double acc = 0.0;
-    int ip = 0;
-    float la0 = 0.0f, la1 = 0.0f;
-    if (kPipelined) {
-        uint4 a[4], b[4], c[4];
-        load_block(a, row, 0);
-        if (nblocks > 1) load_block(b, row, 1);
-        for (int blk = 0; blk < nblocks; blk += 3) {
-            if (blk + 2 < nblocks) load_block(c, row, blk + 2);
-            block_code8_ip<kForm>(x + 64 * blk, qw, T, blk, a, acc, ip, la0, la1);
-            if (blk + 1 >= nblocks) break;
-            if (blk + 3 < nblocks) load_block(a, row, blk + 3);
-            block_code8_ip<kForm>(x + 64 * (blk + 1), qw, T, blk + 1, b, acc, ip, la0, la1);
-            if (blk + 2 >= nblocks) break;
-            if (blk + 4 < nblocks) load_block(b, row, blk + 4);
-            block_code8_ip<kForm>(x + 64 * (blk + 2), qw, T, blk + 2, c, acc, ip, la0, la1);
-        }
-    } else {
-        for (int blk = 0; blk < nblocks; ++blk) {
-            uint4 v[4];
-            load_block(v, row, blk);
-            block_code8_ip<kForm>(x + 64 * blk, qw, T, blk, v, acc, ip, la0, la1);
-        }
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t w = w4[k];
+        out |= (((w >> 4) & 8u) | ((w >> 13) & 4u) | ((w >> 22) & 2u) | (w >> 31)) << (4 * k);
     }
-    if (kForm == kRefineFullCode) return __fadd_rn(__double2float_rn(acc), kb);
-    // ip1 exactly as the scan forms it; 128 * ip1 is exact
-    const float ip1 = kForm == kRefineSplitInt ? __fmul_rn(width, static_cast<float>(ip))
-                                               : __fadd_rn(la0, la1);
-    return __fadd_rn(__fadd_rn(__fmul_rn(128.0f, ip1), __double2float_rn(acc)), kb);
+    return out;
 }
 
-// One CTA per query, one thread per candidate: a candidate's refine row (its 8-bit codes, D
-// bytes, 32-byte sectors used whole) and its meta word are loaded before its fp64 chain.
-// mode 0 refines the vanguard seeds [0, cnt) and records the seed count; mode 1 refines the
-// main candidates [seed_cnt, cnt). Dynamic shared memory (refine_smem): the query as D
-// doubles, its qint as D / 4 words of signed bytes, its LUT tables as 4 D floats, nprobe
-// ProbeInfo.
+// Dynamic shared memory of the refine kernels: the query as D / 16 chunks of kXChunk doubles
+// (the raw query, dim <= D doubles, for the exact refinement), its qint as D / 4 words of
+// signed bytes, its LUT tables as 4 D floats, nprobe ProbeInfo.
+__host__ __device__ __forceinline__ size_t refine_x_doubles(int D) {
+    return (size_t)(D / 16) * kXChunk;
+}
 __host__ __device__ __forceinline__ size_t refine_smem(int D, int nprobe) {
-    return (size_t)D * 8 + (size_t)D + (size_t)D * 16 + (size_t)nprobe * sizeof(ProbeInfo);
+    return refine_x_doubles(D) * 8 + (size_t)D + (size_t)D * 16 +
+           (size_t)nprobe * sizeof(ProbeInfo);
 }
-// kLongRows: D > 128 (the rows' blocks are loaded two ahead, see refine_row_term).
-template <bool kLongRows>
-__global__ void __launch_bounds__(kRefineThreads) refine_kernel(IndexView ix, SearchView sv,
-                                                                int mode) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    double *x = reinterpret_cast<double *>(smem_raw);
-    uint32_t *qw = reinterpret_cast<uint32_t *>(x + ix.D);
-    float *T = reinterpret_cast<float *>(qw + ix.D / 4);
-    ProbeInfo *pinfo = reinterpret_cast<ProbeInfo *>(T + 4 * ix.D);
-    const int q = blockIdx.x;
-    const uint32_t cnt = sv.cand_cnt[q];
-    const uint32_t cap = static_cast<uint32_t>(sv.cap);
-    uint32_t from, to;
-    if (mode == 0) {
-        from = 0;
-        to = min(cnt, cap);
-        if (threadIdx.x == 0) sv.seed_cnt[q] = to;
-    } else {
-        from = sv.seed_cnt[q];
-        to = min(cnt, cap);
-    }
-    if (from >= to) return;  // uniform across the block
-    const bool exact = ix.exact_base != nullptr;
-    // x: the rotated query (ex-code estimate), or the raw query (exact refinement)
+
+// Stages the refinement's per-query operands in shared memory: x (the rotated query, or the
+// raw query when `exact`), the LUT tables widened to fp32 (LUT form), qint words (integer
+// form), and the probes' cluster ranges and additive terms.
+__device__ __forceinline__ void refine_stage(const IndexView &ix, const SearchView &sv, int q,
+                                             int np, bool exact, double *x, uint32_t *qw,
+                                             float *T, ProbeInfo *pinfo) {
     if (exact) {
         for (int j = threadIdx.x; j < ix.dim; j += blockDim.x)
             x[j] = static_cast<double>(sv.raw_q[(size_t)q * ix.dim + j]);
     } else {
         for (int j = threadIdx.x; j < ix.D; j += blockDim.x)
-            x[j] = static_cast<double>(sv.qr[(size_t)q * ix.D + j]);
-        // the LUT estimator's tables, widened to fp32
-        if (sv.lut_mode)
+            x[(j / 16) * kXChunk + j % 16] = static_cast<double>(sv.qr[(size_t)q * ix.D + j]);
+        if (sv.lut_mode && !sv.refine_full_code)
             for (int i = threadIdx.x; i < 4 * ix.D; i += blockDim.x)
                 T[i] = __half2float(sv.lut[(size_t)q * 4 * ix.D + i]);
-        // qint of dims 4t .. 4t + 3 from the query's two's-complement bit-planes (plane b,
-        // word j / 32, bit 31 - j % 32 holds bit b of qint_j & 0xFF): byte i of word t
-        const int W4 = 4 * ix.G16;
-        const uint32_t *pl = sv.planes + (size_t)q * 8 * W4;
-        for (int t = threadIdx.x; t < ix.D / 4; t += blockDim.x) {
-            uint32_t word = 0;
+        if (!sv.lut_mode && !sv.refine_full_code) {
+            // qint of dims 4t .. 4t + 3 from the query's two's-complement bit-planes (plane
+            // b, word j / 32, bit 31 - j % 32 holds bit b of qint_j & 0xFF): byte i of word t
+            const int W4 = 4 * ix.G16;
+            const uint32_t *pl = sv.planes + (size_t)q * 8 * W4;
+            for (int t = threadIdx.x; t < ix.D / 4; t += blockDim.x) {
+                uint32_t word = 0;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int j = 4 * t + i;
-                uint32_t byte = 0;
+                for (int i = 0; i < 4; ++i) {
+                    const int j = 4 * t + i;
+                    uint32_t byte = 0;
 #pragma unroll
-                for (int b = 0; b < 8; ++b) byte |= ((pl[b * W4 + j / 32] >> (31 - j % 32)) & 1u) << b;
-                word |= byte << (8 * i);
+                    for (int b = 0; b < 8; ++b)
+                        byte |= ((pl[b * W4 + j / 32] >> (31 - j % 32)) & 1u) << b;
+                    word |= byte << (8 * i);
+                }
+                qw[t] = word;
             }
-            qw[t] = word;
         }
     }
-    const int np = mode == 0 ? sv.veff : sv.nprobe;
     for (int r = threadIdx.x; r < np; r += blockDim.x) {
         const int c = sv.probe_ids[(size_t)q * sv.nprobe + r];
         pinfo[r] = ProbeInfo{ix.cl_start[c], ix.cl_size[c], sv.probe_ga[(size_t)q * sv.nprobe + r]};
     }
+}
+
+// The candidate range of a refine launch: mode 0 refines the vanguard seeds [0, cnt) and
+// records the seed count, mode 1 the main candidates [seed_cnt, cnt); false when empty.
+__device__ __forceinline__ bool refine_range(const SearchView &sv, int q, int mode,
+                                             uint32_t &from, uint32_t &to) {
+    const uint32_t cnt = sv.cand_cnt[q];
+    const uint32_t cap = static_cast<uint32_t>(sv.cap);
+    to = min(cnt, cap);
+    if (mode == 0) {
+        from = 0;
+        if (threadIdx.x == 0) sv.seed_cnt[q] = to;
+    } else {
+        from = sv.seed_cnt[q];
+    }
+    return from < to;
+}
+
+using RefineKernelFn = void (*)(IndexView, SearchView, int);
+
+// One CTA per query; kLanes lanes (1, 4 or 8) take a candidate's row: lane l of a row's group
+// loads and accumulates chunks l, l + kLanes, ... (kC at a time), so with 4 or 8 lanes each
+// load instruction reads 16 kLanes consecutive bytes of a row, and holds partial sums
+// l + kLanes t (with one lane per row: all eight, and the warp's 32 rows read the same query
+// doubles at once). The partials are combined in the fixed order above by xor-shuffles
+// between the row's lanes and in-lane adds (fp64 addition commutes, so every lane of the row
+// ends with the same bits); the integer estimate ip_int is reduced by shuffles (exact); the
+// LUT form's two fp32 chains (even groups, odd groups, ascending, as the scan forms them) run
+// in the row's even and odd lanes over the chunks' patterns, gathered by shuffles (both in
+// the one lane when kLanes is 1). Lane 0 writes the key.
+// CTAs per SM the one-lane-per-row kernel is compiled for (48 registers, a few bytes of
+// spill; measured at D = 128: candidates 0.248 -> 0.241 ms against the uncapped 64)
+#ifndef CORA_REFINE_ROW_MINB
+#define CORA_REFINE_ROW_MINB 10
+#endif
+template <int kLanes, int kC, int kForm>
+__global__ void __launch_bounds__(kRefineThreads, kLanes == 1 ? CORA_REFINE_ROW_MINB : 1)
+    refine_kernel(IndexView ix, SearchView sv, int mode) {
+    static_assert(kLanes == 1 || kLanes == 4 || kLanes == 8, "1, 4 or 8 lanes per row");
+    constexpr int P = kRefinePartials / kLanes;  // partials per lane
+    // a round covers whole partial cycles, or (one lane per row, kC = 4) half of one: the
+    // rounds then alternate between partials 0 .. 3 and 4 .. 7
+    static_assert(kC % P == 0 || (kLanes == 1 && kC == 4), "rounds and partials");
+    constexpr int kRowsPerWarp = 32 / kLanes;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    double *x = reinterpret_cast<double *>(smem_raw);
+    uint32_t *qw = reinterpret_cast<uint32_t *>(x + refine_x_doubles(ix.D));
+    float *T = reinterpret_cast<float *>(qw + ix.D / 4);
+    ProbeInfo *pinfo = reinterpret_cast<ProbeInfo *>(T + 4 * ix.D);
+    const int q = blockIdx.x;
+    uint32_t from, to;
+    if (!refine_range(sv, q, mode, from, to)) return;  // uniform across the block
+    const int np = mode == 0 ? sv.veff : sv.nprobe;
+    refine_stage(ix, sv, q, np, false, x, qw, T, pinfo);
     __syncthreads();
     const float kb = sv.scal[q].kb, width = sv.scal[q].width;
-    const int form = sv.refine_full_code ? kRefineFullCode
-                                         : (sv.lut_mode ? kRefineSplitLut : kRefineSplitInt);
-    const int nblocks = ix.D / 64;
-    const int row4 = ix.D / 16;  // uint4 per refine row
+    const int lane = threadIdx.x & 31, gl = lane % kLanes, gw = lane / kLanes;
+    const int warp = threadIdx.x >> 5, nwarp = blockDim.x >> 5;
+    const int nl = ix.D / (16 * kLanes);  // chunks per lane (the host picks kLanes | D / 16)
+    const int row4 = ix.D / 16;
+    const uint4 *qw4 = reinterpret_cast<const uint4 *>(qw);
+    for (uint32_t base = from + warp * kRowsPerWarp; base < to;
+         base += nwarp * kRowsPerWarp) {  // warp-uniform: every lane takes the shuffles
+        const uint32_t i = base + gw;
+        bool ok = i < to;
+        uint32_t gid = 0, pr = 0;
+        if (ok) {
+            const uint64_t rec = sv.cand_rec[(size_t)q * sv.cap + i];
+            gid = static_cast<uint32_t>(rec & 0xFFFFFFFFu);
+            pr = static_cast<uint32_t>(rec >> 32);
+            // a record outside its probe's cluster is reported, never dereferenced
+            if (pr >= static_cast<uint32_t>(np) || gid - pinfo[pr].start >= pinfo[pr].size) {
+                if (gl == 0) {
+                    atomicOr(sv.err, kDevBadInput);
+                    sv.cand_key[(size_t)q * sv.cap + i] = kKeyMax;
+                }
+                ok = false;
+            }
+        }
+        uint4 mt = make_uint4(0u, 0u, 0u, 0u);
+        if (ok && gl == 0) mt = __ldg(ix.meta + gid);  // {f_add_ex, f_rescale_ex, id, 0}
+        const uint4 *row = ix.rows + (size_t)gid * row4 + gl;
+        double acc[P];
+#pragma unroll
+        for (int t = 0; t < P; ++t) acc[t] = 0.0;
+        int ip = 0;
+        float la = 0.0f;   // LUT form: even lanes the even groups' chain, odd lanes the odd one
+        float la1 = 0.0f;  // (one lane per row: la the even chain, la1 the odd one)
+        for (int s0 = 0; s0 < nl; s0 += kC) {
+            uint4 v[kC];
+#pragma unroll
+            for (int u = 0; u < kC; ++u)
+                v[u] = (ok && s0 + u < nl) ? __ldg(row + kLanes * (s0 + u))
+                                           : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int u = 0; u < kC; ++u) {
+                if (s0 + u < nl) {
+                    const int c = gl + kLanes * (s0 + u);
+                    const uint4 qv = kForm == kRefineSplitInt ? qw4[c] : make_uint4(0u, 0u, 0u, 0u);
+                    if constexpr (kC % P == 0) {
+                        chunk_code8_ip<kForm>(x + kXChunk * c, qv, v[u], acc[u % P], ip);
+                    } else {
+                        if (s0 & 4)
+                            chunk_code8_ip<kForm>(x + kXChunk * c, qv, v[u], acc[4 + u], ip);
+                        else
+                            chunk_code8_ip<kForm>(x + kXChunk * c, qv, v[u], acc[u], ip);
+                    }
+                }
+            }
+            if (kForm == kRefineSplitLut) {
+                uint32_t pats[kC];
+#pragma unroll
+                for (int u = 0; u < kC; ++u) pats[u] = chunk_patterns(v[u]);
+                const int par = gl & 1;
+#pragma unroll
+                for (int u = 0; u < kC; ++u) {
+                    if (s0 + u < nl) {  // uniform
+#pragma unroll
+                        for (int l = 0; l < kLanes; ++l) {
+                            const uint32_t m =
+                                kLanes == 1 ? pats[u] : __shfl_sync(0xffffffffu, pats[u], l, kLanes);
+                            const int c = l + kLanes * (s0 + u);
+                            if (kLanes == 1) {
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) {
+                                    const float e = T[(4 * c + k) * 16 + ((m >> (4 * k)) & 15u)];
+                                    if (k & 1)
+                                        la1 = __fadd_rn(la1, e);
+                                    else
+                                        la = __fadd_rn(la, e);
+                                }
+                            } else {
+#pragma unroll
+                                for (int k2 = 0; k2 < 2; ++k2) {
+                                    const int k = 2 * k2 + par;
+                                    la = __fadd_rn(la, T[(4 * c + k) * 16 + ((m >> (4 * k)) & 15u)]);
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        // combine the partials: ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7))
+#pragma unroll
+        for (int b = 1; b < kRefinePartials; b <<= 1) {
+            if (b < kLanes) {
+#pragma unroll
+                for (int t = 0; t < P; ++t)
+                    acc[t] = __dadd_rn(acc[t], __shfl_xor_sync(0xffffffffu, acc[t], b));
+            } else {
+                const int tb = b / kLanes;
+#pragma unroll
+                for (int t = 0; t < P; t += 2 * tb) acc[t] = __dadd_rn(acc[t], acc[t + tb]);
+            }
+        }
+        float ip1 = 0.0f;
+        if (kForm == kRefineSplitInt) {
+#pragma unroll
+            for (int b = 1; b < kLanes; b <<= 1) ip += __shfl_xor_sync(0xffffffffu, ip, b);
+            ip1 = __fmul_rn(width, static_cast<float>(ip));  // as the scan forms it
+        } else if (kForm == kRefineSplitLut) {
+            if (kLanes == 1)
+                ip1 = __fadd_rn(la, la1);
+            else
+                ip1 = __fadd_rn(__shfl_sync(0xffffffffu, la, 0, kLanes),
+                                __shfl_sync(0xffffffffu, la, 1, kLanes));
+        }
+        if (ok && gl == 0) {
+            float t;  // the factor of f_rescale_ex; 128 * ip1 is exact
+            if (kForm == kRefineFullCode)
+                t = __fadd_rn(__double2float_rn(acc[0]), kb);
+            else
+                t = __fadd_rn(__fadd_rn(__fmul_rn(128.0f, ip1), __double2float_rn(acc[0])), kb);
+            const float ex_d = __fadd_rn(__fadd_rn(__uint_as_float(mt.x), pinfo[pr].g),
+                                         __fmul_rn(__uint_as_float(mt.y), t));
+            sv.cand_key[(size_t)q * sv.cap + i] = make_key(ex_d, mt.z);
+        }
+    }
+}
+
+// Exact refinement (--exact-base): one CTA per query, one thread per candidate, the exact
+// squared L2 distance to the candidate's fp32 base row as an fp64 fma chain over the raw
+// dimensions ascending, rounded once (cpu_refinement.cpp:168-181); a vector whose row is
+// missing is dropped (its key never ranks or sets a threshold). Modes as refine_kernel.
+__global__ void __launch_bounds__(kRefineThreads) refine_exact_kernel(IndexView ix,
+                                                                      SearchView sv, int mode) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    double *x = reinterpret_cast<double *>(smem_raw);
+    uint32_t *qw = reinterpret_cast<uint32_t *>(x + refine_x_doubles(ix.D));
+    float *T = reinterpret_cast<float *>(qw + ix.D / 4);
+    ProbeInfo *pinfo = reinterpret_cast<ProbeInfo *>(T + 4 * ix.D);
+    const int q = blockIdx.x;
+    uint32_t from, to;
+    if (!refine_range(sv, q, mode, from, to)) return;  // uniform across the block
+    const int np = mode == 0 ? sv.veff : sv.nprobe;
+    refine_stage(ix, sv, q, np, true, x, qw, T, pinfo);
+    __syncthreads();
     for (uint32_t i = from + threadIdx.x; i < to; i += blockDim.x) {
         const uint64_t rec = sv.cand_rec[(size_t)q * sv.cap + i];
         const uint32_t gid = static_cast<uint32_t>(rec & 0xFFFFFFFFu);
         const uint32_t pr = static_cast<uint32_t>(rec >> 32);
-        // a record outside its probe's cluster is reported, never dereferenced
         if (pr >= static_cast<uint32_t>(np) || gid - pinfo[pr].start >= pinfo[pr].size) {
             atomicOr(sv.err, kDevBadInput);
             sv.cand_key[(size_t)q * sv.cap + i] = kKeyMax;
             continue;
         }
-        const ProbeInfo p = pinfo[pr];
-        const uint4 mt = __ldg(ix.meta + gid);  // {f_add_ex, f_rescale_ex, id, 0}
-        if (exact) {
-            // exact squared L2 distance to the base row, the fp64 fma chain over the raw
-            // dimensions ascending, rounded once (cpu_refinement.cpp:168-181); a vector whose
-            // row is missing is dropped (its key never ranks or sets a threshold)
-            uint64_t key = kKeyMax;
-            if (__ldg(ix.exact_ok + gid)) {
-                const float *b = ix.exact_base + (size_t)gid * ix.dim;
-                double acc = 0.0;
-                for (int j0 = 0; j0 < ix.dim; j0 += 8) {
-                    float bv[8];
+        uint64_t key = kKeyMax;
+        if (__ldg(ix.exact_ok + gid)) {
+            const uint32_t id = __ldg(ix.meta + gid).z;
+            const float *b = ix.exact_base + (size_t)gid * ix.dim;
+            double acc = 0.0;
+            for (int j0 = 0; j0 < ix.dim; j0 += 8) {
+                float bv[8];
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) bv[u] = j0 + u < ix.dim ? __ldg(b + j0 + u) : 0.0f;
+                for (int u = 0; u < 8; ++u) bv[u] = j0 + u < ix.dim ? __ldg(b + j0 + u) : 0.0f;
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        if (j0 + u < ix.dim) {
-                            const double d = __dsub_rn(x[j0 + u], static_cast<double>(bv[u]));
-                            acc = __fma_rn(d, d, acc);
-                        }
+                for (int u = 0; u < 8; ++u) {
+                    if (j0 + u < ix.dim) {
+                        const double d = __dsub_rn(x[j0 + u], static_cast<double>(bv[u]));
+                        acc = __fma_rn(d, d, acc);
                     }
                 }
-                key = make_key(__double2float_rn(acc), mt.z);
             }
-            sv.cand_key[(size_t)q * sv.cap + i] = key;
-            continue;
+            key = make_key(__double2float_rn(acc), id);
         }
-        const uint4 *row = ix.rows + (size_t)gid * row4;
-        const float2 f = make_float2(__uint_as_float(mt.x), __uint_as_float(mt.y));
-        const uint32_t id = mt.z;
-        float t;  // the factor of f_rescale_ex
-        if (form == kRefineSplitInt)
-            t = refine_row_term<kRefineSplitInt, kLongRows>(row, nblocks, x, qw, T, width, kb);
-        else if (form == kRefineSplitLut)
-            t = refine_row_term<kRefineSplitLut, kLongRows>(row, nblocks, x, qw, T, width, kb);
-        else
-            t = refine_row_term<kRefineFullCode, kLongRows>(row, nblocks, x, qw, T, width, kb);
-        const float ex_d = __fadd_rn(__fadd_rn(f.x, p.g), __fmul_rn(f.y, t));
-        sv.cand_key[(size_t)q * sv.cap + i] = make_key(ex_d, id);
+        sv.cand_key[(size_t)q * sv.cap + i] = key;
     }
 }
 

@@ -536,6 +536,32 @@ __device__ __forceinline__ float ip_from_lut(const uint4 (&code)[G16], const flo
     return __fadd_rn(acc0, acc1);
 }
 
+// ip_from_lut for long codes (G16 >= 3): the code words are read from the staged tile group
+// by group (cw: the vector's words, group g at cw[g * stride]) in a rolled loop, so the
+// unrolled form's registers (and spills) are not needed; the same additions in the same order.
+template <int G16>
+__device__ __forceinline__ float ip_from_lut_grouped(const uint4 *__restrict__ cw, int stride,
+                                                     const float *__restrict__ T) {
+    float acc0 = 0.0f, acc1 = 0.0f;
+#pragma unroll 1
+    for (int g = 0; g < G16; ++g) {
+        const uint4 c = cw[g * stride];
+        const uint32_t x[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const float *Tw = T + (4 * g + t) * 128;
+#pragma unroll
+            for (int n = 0; n < 8; n += 2) {
+                acc0 = __fadd_rn(acc0, Tw[n * 16 + ((x[t] >> (28 - 4 * n)) & 0xFu)]);
+                acc1 = __fadd_rn(acc1, Tw[(n + 1) * 16 + ((x[t] >> (24 - 4 * n)) & 0xFu)]);
+            }
+        }
+    }
+    return __fadd_rn(acc0, acc1);
+}
+// G16 from which the LUT scans take ip_from_lut_grouped
+constexpr int kLutGroupedFrom = 3;
+
 // Widens query q's fp16 tables (4 D halves) into dst (kLutFloats fp32, zero past 4 D), one
 // 16-byte load per thread and step; the calling threads cover [tid0, tid0 + nthreads).
 template <int G16>
@@ -820,7 +846,11 @@ __global__ void __launch_bounds__(kScanThreads, CORA_SCAN_MINB(G16)) scan_kernel
                         const float4 pj = s_par[j];
                         float ip1;
                         if constexpr (kLut) {
-                            ip1 = ip_from_lut<G16>(code[v], reinterpret_cast<const float *>(P));
+                            if constexpr (G16 >= kLutGroupedFrom)  // (V == 1)
+                                ip1 = ip_from_lut_grouped<G16>(sb + i, TV,
+                                                               reinterpret_cast<const float *>(P));
+                            else
+                                ip1 = ip_from_lut<G16>(code[v], reinterpret_cast<const float *>(P));
                         } else {
                             int ip;
                             if constexpr (kBytes)
@@ -1193,7 +1223,9 @@ __global__ void __launch_bounds__(kScanThreads) vanguard_rescan_kernel(
             const float4 f = make_float4(__uint_as_float(fr.x), __uint_as_float(fr.y),
                                          __uint_as_float(fr.z), 0.0f);
             float ip1;
-            if constexpr (kLut) {
+            if constexpr (kLut && G16 >= kLutGroupedFrom) {
+                ip1 = ip_from_lut_grouped<G16>(sb + i, TV, reinterpret_cast<const float *>(s_planes));
+            } else if constexpr (kLut) {
                 ip1 = ip_from_lut<G16>(code, reinterpret_cast<const float *>(s_planes));
             } else {
                 const int ip = ip_int_from_planes<G16>(code, s_planes, code_bias<G16>(code));

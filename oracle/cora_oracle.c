@@ -278,22 +278,34 @@ void cora_oracle_decode_ex7(const uint8_t *code, uint64_t D, uint8_t *u) {
     }
 }
 
+/* The refinement's fp64 inner product sum_d qr_d * c_d of D integer codes c (c_d < 256),
+ * in this engine's fixed summation order: 16-dimension chunks (chunk k = dims 16k .. 16k + 15),
+ * partial sum j over the chunks k with k % 8 == j (chunks ascending, dims ascending in a
+ * chunk; every product is exact in fp64), combined as ((p0 + p1) + (p2 + p3)) +
+ * ((p4 + p5) + (p6 + p7)), rounded once to fp32. The reference (ip64_fxu7_avx,
+ * utils/space.hpp:677-762) sums in its own fp32 SIMD order; the two agree to rounding. */
+static float refine_dot(const float *qr, const uint8_t *c, uint64_t D) {
+    double p[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+    for (uint64_t d = 0; d < D; ++d) p[(d / 16) % 8] += (double)qr[d] * (double)c[d];
+    const double a = (p[0] + p[1]) + (p[2] + p[3]);
+    const double b = (p[4] + p[5]) + (p[6] + p[7]);
+    return (float)(a + b);
+}
+
 /* Refinement inner product of the full (1 + ex_bits)-bit code with the rotated query:
  * ipT = sum_d q'_d * (2^ex_bits * b_d + u_d), b the 1-bit code (bit 31-(d%32) of word d/32),
  * u the decoded 7-bit ex code. The reference forms the same quantity as
  * 2^ex_bits * ip1 + ip2 (cpu_refinement.cpp:183-191) with ip1 taken from its fp16-LUT or
- * 8-bit-query scan; here it is one fp64 accumulation in ascending dimension order (every
- * product is exact in fp64), rounded once to fp32. */
+ * 8-bit-query scan; here it is one fp64 sum (refine_dot's order), rounded once to fp32. */
 float cora_oracle_ip_total(const float *qr, const uint32_t *bits, const uint8_t *code,
                            uint64_t D) {
     uint8_t u[4096];
     cora_oracle_decode_ex7(code, D, u);
-    double acc = 0.0;
     for (uint64_t d = 0; d < D; ++d) {
         const uint32_t bit = (bits[d / 32] >> (31 - (d % 32))) & 1u;
-        acc += (double)qr[d] * (double)(128u * bit + u[d]);
+        u[d] = (uint8_t)(128u * bit + u[d]);
     }
-    return (float)acc;
+    return refine_dot(qr, u, D);
 }
 
 /* Full-code form (opt-in): ex = (f_add_ex + g) + f_rescale_ex * (ipT + kb), ipT the
@@ -305,14 +317,12 @@ float cora_oracle_ex(const cora_oracle_index *ix, uint64_t gid, float ip_total, 
 }
 
 /* ip2 of cpu_refinement.cpp:183-185: <q', u> over the decoded 7-bit ex code, the quantity
- * ip64_fxu7_avx (utils/space.hpp:677-762) computes; here one fp64 accumulation in
- * ascending dimension order (products exact), rounded once. */
+ * ip64_fxu7_avx (utils/space.hpp:677-762) computes; here one fp64 sum in refine_dot's order
+ * (products exact), rounded once. */
 float cora_oracle_ip_ex(const float *qr, const uint8_t *code, uint64_t D) {
     uint8_t u[4096];
     cora_oracle_decode_ex7(code, D, u);
-    double acc = 0.0;
-    for (uint64_t d = 0; d < D; ++d) acc += (double)qr[d] * (double)u[d];
-    return (float)acc;
+    return refine_dot(qr, u, D);
 }
 
 /* cpu_refinement.cpp:186-191 (= split_distance_boosting, estimator.hpp:86-103):

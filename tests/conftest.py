@@ -87,3 +87,49 @@ def kat_fixture(count=32768, topk=100, clusters=8, queries=5, dim=96, padded=128
     order = np.argsort(lf[:, 0], kind="stable")
     expected = np.sort(order[:topk]).astype(np.uint32)
     return sd, q, expected
+
+
+# ------------------------------------------------------------------------------------
+# Summation-order known-answer fixture of the refinement's fp64 inner product: identity
+# rotation, one cluster whose centroid is the query (g = 0), all-zero 1-bit codes and scan
+# factors (ip1 = 0, every low 0), ex factors (0, 1), so each vector's distance is
+# ip2 + kb with ip2 = <q, u>. The query puts +-2^55 at the first dimension of every 16-dim
+# chunk (alternating sign), 1 at the second and a small value at the third; each vector has
+# u = 1 at dims 16a, 16a + 1, 16b, 16b + 1 (chunks a < b of opposite sign) and small codes at
+# every third dimension. In ascending dimension order every term between the two large ones
+# is rounded against 2^55; in the chunked order (partial sums over chunks mod 8) the large
+# terms sit in their own partials, so the two orders give different sums.
+# ------------------------------------------------------------------------------------
+def order_kat_fixture(D, n=32):
+    import torch
+    from coraanns_b200 import builder
+    nch = D // 16
+    q = np.zeros(D, np.float32)
+    for k in range(nch):
+        q[16 * k] = np.float32((1 if k % 2 == 0 else -1) * 2.0 ** 55)
+        q[16 * k + 1] = 1.0
+        q[16 * k + 2] = np.float32(0.125 * (k + 1))
+    rng = np.random.default_rng(D)
+    u = np.zeros((n, D), np.uint8)
+    for v in range(n):
+        a = int(rng.integers(0, nch - 1))
+        b = int(rng.integers(a + 1, nch))
+        if (b - a) % 2 == 0:  # b > a + 1 here: b - 1 keeps a < b and flips the sign
+            b -= 1
+        for c in (a, b):
+            u[v, 16 * c] = 1
+            u[v, 16 * c + 1] = 1
+        for k in range(nch):
+            u[v, 16 * k + 2] = (v + 3 * k) % 128
+    sd = dict(num=n, dim=D, D=D, nlist=1, ex_bits=7)
+    sd["centroids"] = q[None, :].copy()
+    sd["rotator"] = np.eye(D, dtype=np.float32)
+    sd["short_data"] = np.zeros(n * D // 32, np.uint32)
+    sd["short_factors"] = np.zeros((n, 3), np.float32)
+    sd["long_codes"] = builder._pack_ex7(torch.from_numpy(u)).numpy().reshape(-1)
+    ef = np.zeros((n, 2), np.float32)
+    ef[:, 1] = 1.0
+    sd["ex_factors"] = ef
+    sd["ids"] = np.arange(n, dtype=np.uint32)
+    sd["sizes"] = np.array([n], np.uint64)
+    return sd, q[None, :].copy(), u

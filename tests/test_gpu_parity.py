@@ -320,3 +320,26 @@ def test_search_graph_replay_matches_eager(cb, golden):
     assert results[1][-3] != results[1][-2]  # the two refinement forms rank differently here
     assert results[1] == results[0]
     e.close()
+
+
+@pytest.mark.parametrize("k", [8, 32])
+@pytest.mark.parametrize("lanes", [0, 1, 4, 8])
+@pytest.mark.parametrize("sfx", ["", "T", "L"])
+@pytest.mark.parametrize("D", [64, 128, 192, 768])
+def test_refine_sum_order_kat(cb, D, sfx, lanes, k):
+    """The refinement's fp64 sums follow the chunked order (eight partials over 16-dim chunks
+    mod 8, fixed combination tree) with every lane layout of the refine kernel: on the order
+    fixture, where ascending-order summation gives other sums, seeds (k = 32: every vector)
+    and main candidates (k = 8) match the oracle bit for bit."""
+    from conftest import order_kat_fixture
+    sd, q, _ = order_kat_fixture(D)
+    ref = po.OracleIndex(sd, **FORMS[sfx]).search(q, k, 1, vanguard=5, with_details=True)
+    e = _engine(cb, sd=sd, nq=1, k=k, nprobe=1, **FORMS[sfx])
+    e.set_tuning("refine_lanes", lanes)
+    e.reset_buffer(q)
+    d, i = e.search(q, k, 1)
+    e.check_device()
+    assert np.array_equal(e.debug("cand_count", 1).astype(np.uint64), ref["cand_count"])
+    assert np.array_equal(i, ref["ids"])
+    assert d.tobytes() == ref["dist"].tobytes()
+    e.close()

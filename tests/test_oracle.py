@@ -313,3 +313,28 @@ def test_searchdata_restatement_matches_live_reference(golden):
     sd = po.search_data(po.read_ivf_file(path))
     for k in SD_KEYS:
         assert np.asarray(sd[k]).tobytes() == np.asarray(rsd[k]).tobytes(), k
+
+
+@pytest.mark.parametrize("D", [64, 128, 192, 768])
+def test_refinement_sum_order_kat(D):
+    """The oracle's ip2 follows the chunked summation order (eight partial sums over the
+    16-dim chunks mod 8, combined ((p0 + p1) + (p2 + p3)) + ((p4 + p5) + (p6 + p7))), and on
+    the order fixture that order differs from ascending-dimension summation."""
+    from conftest import order_kat_fixture
+    sd, q, u = order_kat_fixture(D)
+    codes = np.asarray(sd["long_codes"]).reshape(sd["num"], D * 7 // 8)
+    x = np.ascontiguousarray(q[0])
+    differs = 0
+    for v in range(sd["num"]):
+        mine = po.lib().cora_oracle_ip_ex(x, codes[v].copy(), D)
+        terms = x.astype(np.float64) * u[v].astype(np.float64)
+        p = [0.0] * 8
+        for d in range(D):
+            p[(d // 16) % 8] += float(terms[d])
+        chunked = np.float32(((p[0] + p[1]) + (p[2] + p[3])) + ((p[4] + p[5]) + (p[6] + p[7])))
+        seq = 0.0
+        for d in range(D):
+            seq += float(terms[d])
+        assert np.float32(mine).tobytes() == chunked.tobytes()
+        differs += np.float32(seq) != chunked
+    assert differs >= sd["num"] // 2, differs
