@@ -74,6 +74,10 @@ STREAM_CONFIGS = {
     # a small case of the same shape (tests of the streamed path, profiling)
     "cfg4s": dict(n=4_000_000, dim=768, nlist=2048, nq=2000, sigma=0.2, qnoise=0.05, k=100,
                   nprobes=[16, 32, 64], seed=20261208, metric=1, zipf=None, vanguard=5),
+    # config 4's probing stage (10K queries against 32768 centroids of d768) over a small
+    # base (profiling the rotation, probe GEMM and probe selection at full size)
+    "cfg4p": dict(n=4_000_000, dim=768, nlist=32768, nq=10_000, sigma=0.2, qnoise=0.05, k=100,
+                  nprobes=[32], seed=20261209, metric=1, zipf=None, vanguard=5),
 }
 
 

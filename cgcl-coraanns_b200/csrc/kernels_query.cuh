@@ -378,6 +378,9 @@ __host__ __device__ inline size_t guarded_select_warp_smem(int D) {
 // (chunk_min[q * chunk_stride(nlist) + j] = min of row q's columns 32j .. 32j + 31): lane l's
 // group is its chunks l, l + 32, ..., and only the chunks whose minimum is inside the band
 // are read from the distance row (128 coalesced bytes each), so a row is not read in full.
+// Rows of up to 32 kGuardRadixRegs chunks (nlist <= 32768) keep their chunk minima in
+// registers for the radix selection of guarded_select_warp_kernel.
+constexpr int kGuardRadixRegs = 32;
 __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
     const float *__restrict__ approx, const float *__restrict__ chunk_min, int nlist, size_t ld,
     int nq, int nprobe, const float *__restrict__ qr, const float *__restrict__ qnorm2,
@@ -406,6 +409,28 @@ __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
         const uint64_t kth = __shfl_sync(0xffffffffu,
                                          warp_sort_lane_keys(make_key(mn, lane), lane), nprobe - 1);
         tau_ub = (double)unord_f32(static_cast<uint32_t>(kth >> 32));
+    } else if (nchunk <= 32 * kGuardRadixRegs) {
+        // the row's chunk minima as order keys in registers (padding: the largest key)
+        uint32_t kr[kGuardRadixRegs];
+#pragma unroll
+        for (int i = 0; i < kGuardRadixRegs; ++i) {
+            const int c = lane + 32 * i;
+            kr[i] = c < nchunk ? ord_f32(__ldg(cm + c)) : 0xFFFFFFFFu;
+        }
+        uint32_t prefix = 0, remaining = static_cast<uint32_t>(nprobe);
+        for (int bit = 31; bit >= 0; --bit) {
+            const uint32_t above = bit == 31 ? 0u : ~((2u << bit) - 1u);  // bits above `bit`
+            uint32_t cnt = 0;
+#pragma unroll
+            for (int i = 0; i < kGuardRadixRegs; ++i)
+                cnt += ((kr[i] & above) == prefix && !((kr[i] >> bit) & 1u)) ? 1u : 0u;
+            cnt = __reduce_add_sync(0xffffffffu, cnt);
+            if (cnt < remaining) {
+                remaining -= cnt;
+                prefix |= 1u << bit;
+            }
+        }
+        tau_ub = (double)unord_f32(prefix);
     } else {
         uint32_t prefix = 0, remaining = static_cast<uint32_t>(nprobe);
         for (int bit = 31; bit >= 0; --bit) {

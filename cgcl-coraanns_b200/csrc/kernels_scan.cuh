@@ -475,9 +475,20 @@ __device__ __forceinline__ int ip_int_from_bytes(const uint32_t (&e)[32 * G16],
     return (acc[0] + acc[1]) + (acc[2] + acc[3]);
 }
 
-// The same sum for D > 128, where the whole split code would not fit in registers: each
-// 128-dim group of the code is split when it is used (32 logic ops, then 32 dp4a against the
-// group's 32 query byte words).
+// Unsigned-by-signed byte dot product: sum of a's 4 unsigned bytes times b's 4 signed bytes,
+// plus c (PTX dp4a.u32.s32).
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// The same sum for D > 128, where the whole split code would not fit in registers. Each
+// 128-dim group of the code is used where it lies in the staged tile: the code word's bits s,
+// s + 8, s + 16, s + 24 are masked in place (x & (0x01010101 << s), bytes 0 or 2^s), so
+// dp4a over unsigned bytes gives 2^s times the plane's partial sum; accumulator s collects
+// plane s and is shifted back once at the end (exact: |2^s * sum| <= 2^7 * 1024 * 128 <
+// 2^31). One logic op and one dp4a per 4 dimensions, instead of a shift, a mask and a dp4a.
 #ifndef CORA_SCAN_DP4A_WIDE
 #define CORA_SCAN_DP4A_WIDE 1
 #endif
@@ -486,7 +497,7 @@ constexpr bool kScanDp4aWide = CORA_SCAN_DP4A_WIDE != 0;
 template <int G16>
 __device__ __forceinline__ int ip_int_from_bytes_grouped(const uint4 *__restrict__ cw, int stride,
                                                          const uint32_t *__restrict__ Q) {
-    int acc[4] = {0, 0, 0, 0};
+    int acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll 1
     for (int g = 0; g < G16; ++g) {  // rolled: one group's query words in registers at a time
         const uint4 c = cw[g * stride];
@@ -499,11 +510,11 @@ __device__ __forceinline__ int ip_int_from_bytes_grouped(const uint4 *__restrict
             const uint32_t qa[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
             for (int s = 0; s < 8; ++s)
-                acc[s & 3] = __dp4a(static_cast<int>((x[t] >> s) & 0x01010101u),
-                                    static_cast<int>(qa[s]), acc[s & 3]);
+                acc[s] = dp4a_us(x[t] & (0x01010101u << s), qa[s], acc[s]);
         }
     }
-    return (acc[0] + acc[1]) + (acc[2] + acc[3]);
+    return ((acc[0] + (acc[1] >> 1)) + ((acc[2] >> 2) + (acc[3] >> 3))) +
+           (((acc[4] >> 4) + (acc[5] >> 5)) + ((acc[6] >> 6) + (acc[7] >> 7)));
 }
 
 // Copies a query's two's-complement bit-planes into shared memory as offset-binary planes
