@@ -607,7 +607,7 @@ def run_stream(args, name, cfg):
         tt = time.perf_counter()
         o.search(q_np[:probe_n], k, chosen, vanguard=cfg["vanguard"], threads=threads)
         per_q = max((time.perf_counter() - tt) / probe_n, 1e-6)
-        m = int(min(nq, max(probe_n, 12.0 / per_q)))
+        m = int(min(nq, max(probe_n, 20.0 / per_q)))
         tt = time.perf_counter()
         o.search(q_np[:m], k, chosen, vanguard=cfg["vanguard"], threads=threads)
         dt = time.perf_counter() - tt

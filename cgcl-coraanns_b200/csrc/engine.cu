@@ -223,9 +223,14 @@ inline void launch_guarded_select(float *approx, const float *chunk_min, uint64_
 // == 0): kC, the chunks a lane loads per round, is its chunk count D / (16 lanes) rounded up
 // to one of 1, 2, 4, 6, 8 (with one lane per row kRefineRowChunks: 4, half of the eight
 // partials per round, or 8; rows longer than kC chunks per lane take several rounds).
+// at most this many chunks per lane and round (measured at D = 768 with 4 lanes, cfg4s:
+// candidates 0.795 / 0.903 / 0.850 ms with rounds of 4 / 6 / 8 chunks)
+#ifndef CORA_REFINE_KC_MAX
+#define CORA_REFINE_KC_MAX 4
+#endif
 template <int kForm>
 RefineKernelFn pick_refine(int D, int lanes) {
-    const int nl = D / (16 * lanes);
+    const int nl = std::min(D / (16 * lanes), CORA_REFINE_KC_MAX);
     if (lanes == 1) return kRefineRowChunks == 4 ? refine_kernel<1, 4, kForm> : refine_kernel<1, 8, kForm>;
     if (lanes == 8) {
         if (nl <= 1) return refine_kernel<8, 1, kForm>;

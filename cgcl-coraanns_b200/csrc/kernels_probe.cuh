@@ -165,8 +165,13 @@ __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    // tiles in query-block-fastest order: the CTAs of a wave share one or two centroid
+    // blocks (read from DRAM once, then from L2) while the query matrix stays in L2; in
+    // centroid-block-fastest order every wave streamed the whole centroid matrix again
+    // (3.75 GB of DRAM reads for 131 MB of operands at config 4)
     const int ntn = (nlist + kPgBN - 1) / kPgBN;
-    const int tiles = ((nq + kPgBM - 1) / kPgBM) * ntn;
+    const int ntm = (nq + kPgBM - 1) / kPgBM;
+    const int tiles = ntm * ntn;
     const int KC = D / kPgBK;
 
     if (threadIdx.x == 0) {
@@ -193,7 +198,7 @@ __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
             uint32_t s = 0, ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                const int m0 = (t / ntn) * kPgBM, n0 = (t % ntn) * kPgBN;
+                const int m0 = (t % ntm) * kPgBM, n0 = (t / ntm) * kPgBN;
                 for (int kc = 0; kc < KC; ++kc) {
                     if (!(ok = mbar_wait_bounded(empty + s, ph ^ 1, err))) break;
                     mbar_arrive_expect_tx(full + s, kPgStageA + kPgStageB);
@@ -253,7 +258,7 @@ __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
         uint32_t acc = 0, aph = 0, obuf = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-            const int m0 = (t / ntn) * kPgBM, n0 = (t % ntn) * kPgBN;
+            const int m0 = (t % ntm) * kPgBM, n0 = (t / ntm) * kPgBN;
             ok = ok && mbar_wait_bounded(tfull + acc, aph, err);
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
             // every epilogue thread takes part in the barriers below even after a timeout

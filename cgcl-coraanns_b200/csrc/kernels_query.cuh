@@ -61,49 +61,53 @@ __global__ void __launch_bounds__(256) rotate_prep_kernel(
     constexpr int kTpg = 256 / kGroups;  // threads per group
     const int grp = threadIdx.x / kTpg;
     const double *sqg = sq + grp * kRotQueries * dim;
-    // D > 128 (kQ == kRotQueries): a thread carries output dims j and j + kTpg together, so
-    // each query value read from shared memory feeds two chains (the loads, not the fp64
-    // FMAs, bound this loop there: 0.27 instead of 0.31 ms for 2000 queries at D = 768); the
-    // D <= 128 form has one column per thread anyway, and the second set of registers would
-    // only cost it occupancy.
-    constexpr bool kTwoCols = kQ == kRotQueries;
-    for (int j = threadIdx.x % kTpg; j < D; j += (kTwoCols ? 2 : 1) * kTpg) {
-        const int j2 = j + kTpg;
-        const bool two = kTwoCols && j2 < D;
-        double acc[kRotQueries], acc2[kRotQueries];
+    // D > 128 (kQ == kRotQueries): a thread carries output dims j, j + kTpg and j + 2 kTpg
+    // together (one pass over D = 768), so each query value read from shared memory feeds
+    // three chains (the loads, not the fp64 FMAs, bound this loop: 1.13 ms with two columns
+    // and two passes for 10K queries at D = 768, LSU pipe 52%); the D <= 128 form has one
+    // column per thread anyway, and more registers would only cost it occupancy.
+    constexpr int kCols = kQ == kRotQueries ? 3 : 1;
+    constexpr int kRows = kCols > 1 ? 4 : 8;  // rotator rows loaded ahead of their use
+    for (int j = threadIdx.x % kTpg; j < D; j += kCols * kTpg) {
+        double acc[kCols][kRotQueries];
 #pragma unroll
-        for (int qq = 0; qq < kRotQueries; ++qq) acc[qq] = acc2[qq] = 0.0;
-        // rotator values are loaded eight rows ahead of their use (dim % 8 == 0 is not
-        // assumed: the tail rows read as 0 and are not accumulated)
-        for (int i0 = 0; i0 < dim; i0 += 8) {
-            double p[8], p2[8];
+        for (int cc = 0; cc < kCols; ++cc)
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
-                p[u] = i0 + u < dim ? __ldg(rotator + (size_t)(i0 + u) * D + j) : 0.0;
-                p2[u] = two && i0 + u < dim ? __ldg(rotator + (size_t)(i0 + u) * D + j2) : 0.0;
+            for (int qq = 0; qq < kRotQueries; ++qq) acc[cc][qq] = 0.0;
+        // dim % kRows == 0 is not assumed: the tail rows read as 0 and are not accumulated
+        for (int i0 = 0; i0 < dim; i0 += kRows) {
+            double p[kCols][kRows];
+#pragma unroll
+            for (int cc = 0; cc < kCols; ++cc) {
+                const int jc = j + cc * kTpg;
+#pragma unroll
+                for (int u = 0; u < kRows; ++u)
+                    p[cc][u] = jc < D && i0 + u < dim ? __ldg(rotator + (size_t)(i0 + u) * D + jc)
+                                                      : 0.0;
             }
 #pragma unroll
-            for (int u = 0; u < 8; ++u) {
+            for (int u = 0; u < kRows; ++u) {
                 if (i0 + u < dim) {
 #pragma unroll
                     for (int qq = 0; qq < kRotQueries; ++qq) {
                         const double xv = sqg[qq * dim + i0 + u];
-                        acc[qq] = __fma_rn(xv, p[u], acc[qq]);
-                        acc2[qq] = __fma_rn(xv, p2[u], acc2[qq]);
+#pragma unroll
+                        for (int cc = 0; cc < kCols; ++cc)
+                            acc[cc][qq] = __fma_rn(xv, p[cc][u], acc[cc][qq]);
                     }
                 }
             }
         }
 #pragma unroll
-        for (int qq = 0; qq < kRotQueries; ++qq) {
-            const int qa = grp * kRotQueries + qq;
-            const float v = (float)acc[qq];
-            sr[qa * D + j] = v;
-            if (qa < nqb) qr_out[(size_t)(q0 + qa) * D + j] = v;
-            if (two) {
-                const float v2 = (float)acc2[qq];
-                sr[qa * D + j2] = v2;
-                if (qa < nqb) qr_out[(size_t)(q0 + qa) * D + j2] = v2;
+        for (int cc = 0; cc < kCols; ++cc) {
+            const int jc = j + cc * kTpg;
+            if (jc >= D) continue;
+#pragma unroll
+            for (int qq = 0; qq < kRotQueries; ++qq) {
+                const int qa = grp * kRotQueries + qq;
+                const float v = (float)acc[cc][qq];
+                sr[qa * D + jc] = v;
+                if (qa < nqb) qr_out[(size_t)(q0 + qa) * D + jc] = v;
             }
         }
     }
@@ -236,16 +240,33 @@ __device__ __forceinline__ float exact_centroid_dist(const float *__restrict__ x
                                                      const float *__restrict__ c, int D) {
     double acc = 0.0;
     const float4 *c4 = reinterpret_cast<const float4 *>(c);
-    for (int j0 = 0; j0 < D; j0 += 32) {
-        float4 v[8];
+    // 32 dimensions per step, the next step's row segment loaded before this one's chain
+    // (D % 64 == 0: the steps come in pairs, so the two buffers keep fixed registers)
+    float4 va[8], vb[8];
 #pragma unroll
-        for (int t = 0; t < 8; ++t) v[t] = __ldg(c4 + j0 / 4 + t);
+    for (int t = 0; t < 8; ++t) va[t] = __ldg(c4 + t);
+    for (int j0 = 0; j0 < D; j0 += 64) {
+#pragma unroll
+        for (int t = 0; t < 8; ++t) vb[t] = __ldg(c4 + (j0 + 32) / 4 + t);
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
-            const float cv[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
+            const float cv[4] = {va[t].x, va[t].y, va[t].z, va[t].w};
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const double d = __dsub_rn((double)x[j0 + 4 * t + u], (double)cv[u]);
+                acc = __fma_rn(d, d, acc);
+            }
+        }
+        if (j0 + 64 < D) {
+#pragma unroll
+            for (int t = 0; t < 8; ++t) va[t] = __ldg(c4 + (j0 + 64) / 4 + t);
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+            const float cv[4] = {vb[t].x, vb[t].y, vb[t].z, vb[t].w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const double d = __dsub_rn((double)x[j0 + 32 + 4 * t + u], (double)cv[u]);
                 acc = __fma_rn(d, d, acc);
             }
         }
