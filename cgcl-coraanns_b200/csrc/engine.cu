@@ -141,6 +141,10 @@ inline CUtensorMap map_f32_2d(const float *base, uint64_t cols, uint64_t rows, u
 
 inline uint64_t approx_ld(uint64_t nlist) { return (nlist + 3) & ~uint64_t(3); }
 
+// Centroid matrices above this size are multiplied in query-block-fastest tile order (see
+// probe_gemm_kernel).
+constexpr uint64_t kPgQueryFastBytes = 32ull << 20;
+
 // approx[q * ld + c] = ||q'||^2 + ||c||^2 - 2 <q', c> for every query and centroid, on the
 // tensor cores (probe_gemm_kernel; persistent, one CTA per SM at most).
 inline void launch_probe_gemm(const float *qr, const float *qnorm2, uint64_t nq, uint64_t D,
@@ -155,9 +159,10 @@ inline void launch_probe_gemm(const float *qr, const float *qnorm2, uint64_t nq,
                                   (int)sm));
     const uint64_t tiles = ((nq + kPgBM - 1) / kPgBM) * ((nlist + kPgBN - 1) / kPgBN);
     const unsigned grid = static_cast<unsigned>(std::min<uint64_t>(tiles, (uint64_t)num_sms));
+    const int qfast = nlist * D * sizeof(float) > kPgQueryFastBytes ? 1 : 0;
     probe_gemm_kernel<<<grid, kPgThreads, sm, st>>>(tq, tc, to, qnorm2, cnorm2,
                                                     static_cast<int>(nq), static_cast<int>(nlist),
-                                                    static_cast<int>(D), chunk_min, err);
+                                                    static_cast<int>(D), chunk_min, qfast, err);
     CUDA_TRY(cudaGetLastError());
 }
 

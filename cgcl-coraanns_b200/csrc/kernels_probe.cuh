@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
     const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_c,
     const __grid_constant__ CUtensorMap tm_out, const float *__restrict__ qnorm2,
     const float *__restrict__ cnorm2, int nq, int nlist, int D, float *__restrict__ chunk_min,
-    int *err) {
+    int qfast, int *err) {
     extern __shared__ unsigned char pg_smem_raw[];
     unsigned char *smem = reinterpret_cast<unsigned char *>(
         (reinterpret_cast<uintptr_t>(pg_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -165,10 +165,12 @@ __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_done + 1);
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    // tiles in query-block-fastest order: the CTAs of a wave share one or two centroid
-    // blocks (read from DRAM once, then from L2) while the query matrix stays in L2; in
-    // centroid-block-fastest order every wave streamed the whole centroid matrix again
-    // (3.75 GB of DRAM reads for 131 MB of operands at config 4)
+    // Tile order. qfast (large centroid matrices): query-block-fastest, so the CTAs of a
+    // wave share one or two centroid blocks (read from DRAM once, then from L2) while the
+    // query matrix stays in L2; centroid-block-fastest, every wave streamed the whole
+    // centroid matrix again (3.75 GB of DRAM reads for 131 MB of operands at config 4).
+    // Otherwise centroid-block-fastest: the centroids stay in L2 anyway and a wave writes
+    // whole output rows (config 2: 0.060 against 0.072 ms).
     const int ntn = (nlist + kPgBN - 1) / kPgBN;
     const int ntm = (nq + kPgBM - 1) / kPgBM;
     const int tiles = ntm * ntn;
@@ -198,7 +200,7 @@ __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
             uint32_t s = 0, ph = 0;
             bool ok = true;
             for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
-                const int m0 = (t % ntm) * kPgBM, n0 = (t / ntm) * kPgBN;
+                const int m0 = (qfast ? t % ntm : t / ntn) * kPgBM, n0 = (qfast ? t / ntm : t % ntn) * kPgBN;
                 for (int kc = 0; kc < KC; ++kc) {
                     if (!(ok = mbar_wait_bounded(empty + s, ph ^ 1, err))) break;
                     mbar_arrive_expect_tx(full + s, kPgStageA + kPgStageB);
@@ -258,7 +260,7 @@ __global__ void __launch_bounds__(kPgThreads, 1) probe_gemm_kernel(
         uint32_t acc = 0, aph = 0, obuf = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
-            const int m0 = (t % ntm) * kPgBM, n0 = (t / ntm) * kPgBN;
+            const int m0 = (qfast ? t % ntm : t / ntn) * kPgBM, n0 = (qfast ? t / ntm : t % ntn) * kPgBN;
             ok = ok && mbar_wait_bounded(tfull + acc, aph, err);
             ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
             // every epilogue thread takes part in the barriers below even after a timeout

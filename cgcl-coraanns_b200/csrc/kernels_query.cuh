@@ -240,33 +240,16 @@ __device__ __forceinline__ float exact_centroid_dist(const float *__restrict__ x
                                                      const float *__restrict__ c, int D) {
     double acc = 0.0;
     const float4 *c4 = reinterpret_cast<const float4 *>(c);
-    // 32 dimensions per step, the next step's row segment loaded before this one's chain
-    // (D % 64 == 0: the steps come in pairs, so the two buffers keep fixed registers)
-    float4 va[8], vb[8];
+    for (int j0 = 0; j0 < D; j0 += 32) {
+        float4 v[8];
 #pragma unroll
-    for (int t = 0; t < 8; ++t) va[t] = __ldg(c4 + t);
-    for (int j0 = 0; j0 < D; j0 += 64) {
-#pragma unroll
-        for (int t = 0; t < 8; ++t) vb[t] = __ldg(c4 + (j0 + 32) / 4 + t);
+        for (int t = 0; t < 8; ++t) v[t] = __ldg(c4 + j0 / 4 + t);
 #pragma unroll
         for (int t = 0; t < 8; ++t) {
-            const float cv[4] = {va[t].x, va[t].y, va[t].z, va[t].w};
+            const float cv[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
                 const double d = __dsub_rn((double)x[j0 + 4 * t + u], (double)cv[u]);
-                acc = __fma_rn(d, d, acc);
-            }
-        }
-        if (j0 + 64 < D) {
-#pragma unroll
-            for (int t = 0; t < 8; ++t) va[t] = __ldg(c4 + (j0 + 64) / 4 + t);
-        }
-#pragma unroll
-        for (int t = 0; t < 8; ++t) {
-            const float cv[4] = {vb[t].x, vb[t].y, vb[t].z, vb[t].w};
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const double d = __dsub_rn((double)x[j0 + 32 + 4 * t + u], (double)cv[u]);
                 acc = __fma_rn(d, d, acc);
             }
         }
@@ -399,9 +382,34 @@ __host__ __device__ inline size_t guarded_select_warp_smem(int D) {
 // (chunk_min[q * chunk_stride(nlist) + j] = min of row q's columns 32j .. 32j + 31): lane l's
 // group is its chunks l, l + 32, ..., and only the chunks whose minimum is inside the band
 // are read from the distance row (128 coalesced bytes each), so a row is not read in full.
-// Rows of up to 32 kGuardRadixRegs chunks (nlist <= 32768) keep their chunk minima in
-// registers for the radix selection of guarded_select_warp_kernel.
-constexpr int kGuardRadixRegs = 32;
+// The nprobe-th smallest of a row's nchunk <= 32 R chunk minima (cm), by an exact radix
+// selection over their order keys held in registers (R per lane, padding: the largest key),
+// one bit per warp-wide count.
+template <int R>
+__device__ __forceinline__ float radix_tau_regs(const float *__restrict__ cm, int nchunk,
+                                                int nprobe, int lane) {
+    uint32_t kr[R];
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const int c = lane + 32 * i;
+        kr[i] = c < nchunk ? ord_f32(__ldg(cm + c)) : 0xFFFFFFFFu;
+    }
+    uint32_t prefix = 0, remaining = static_cast<uint32_t>(nprobe);
+    for (int bit = 31; bit >= 0; --bit) {
+        const uint32_t above = bit == 31 ? 0u : ~((2u << bit) - 1u);  // bits above `bit`
+        uint32_t cnt = 0;
+#pragma unroll
+        for (int i = 0; i < R; ++i)
+            cnt += ((kr[i] & above) == prefix && !((kr[i] >> bit) & 1u)) ? 1u : 0u;
+        cnt = __reduce_add_sync(0xffffffffu, cnt);
+        if (cnt < remaining) {
+            remaining -= cnt;
+            prefix |= 1u << bit;
+        }
+    }
+    return unord_f32(prefix);
+}
+
 __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
     const float *__restrict__ approx, const float *__restrict__ chunk_min, int nlist, size_t ld,
     int nq, int nprobe, const float *__restrict__ qr, const float *__restrict__ qnorm2,
@@ -423,35 +431,22 @@ __global__ void __launch_bounds__(256) guarded_select_warp_kernel(
     // centroid at or below it, so it bounds the nprobe-th smallest approximate distance from
     // above, and is that distance itself when the nprobe nearest lie in distinct chunks).
     // Rows of at most 32 chunks: one chunk per lane, sorted; longer rows: an exact radix
-    // selection over the chunk minima's order keys, one bit per warp-wide count.
+    // selection over the chunk minima's order keys, one bit per warp-wide count (the keys
+    // in registers up to 1024 chunks, nlist <= 32768).
     double tau_ub;
     if (nchunk <= 32) {
         const float mn = lane < nchunk ? __ldg(cm + lane) : FLT_MAX;
         const uint64_t kth = __shfl_sync(0xffffffffu,
                                          warp_sort_lane_keys(make_key(mn, lane), lane), nprobe - 1);
         tau_ub = (double)unord_f32(static_cast<uint32_t>(kth >> 32));
-    } else if (nchunk <= 32 * kGuardRadixRegs) {
-        // the row's chunk minima as order keys in registers (padding: the largest key)
-        uint32_t kr[kGuardRadixRegs];
-#pragma unroll
-        for (int i = 0; i < kGuardRadixRegs; ++i) {
-            const int c = lane + 32 * i;
-            kr[i] = c < nchunk ? ord_f32(__ldg(cm + c)) : 0xFFFFFFFFu;
-        }
-        uint32_t prefix = 0, remaining = static_cast<uint32_t>(nprobe);
-        for (int bit = 31; bit >= 0; --bit) {
-            const uint32_t above = bit == 31 ? 0u : ~((2u << bit) - 1u);  // bits above `bit`
-            uint32_t cnt = 0;
-#pragma unroll
-            for (int i = 0; i < kGuardRadixRegs; ++i)
-                cnt += ((kr[i] & above) == prefix && !((kr[i] >> bit) & 1u)) ? 1u : 0u;
-            cnt = __reduce_add_sync(0xffffffffu, cnt);
-            if (cnt < remaining) {
-                remaining -= cnt;
-                prefix |= 1u << bit;
-            }
-        }
-        tau_ub = (double)unord_f32(prefix);
+    } else if (nchunk <= 128) {
+        tau_ub = (double)radix_tau_regs<4>(cm, nchunk, nprobe, lane);
+    } else if (nchunk <= 256) {
+        tau_ub = (double)radix_tau_regs<8>(cm, nchunk, nprobe, lane);
+    } else if (nchunk <= 512) {
+        tau_ub = (double)radix_tau_regs<16>(cm, nchunk, nprobe, lane);
+    } else if (nchunk <= 1024) {
+        tau_ub = (double)radix_tau_regs<32>(cm, nchunk, nprobe, lane);
     } else {
         uint32_t prefix = 0, remaining = static_cast<uint32_t>(nprobe);
         for (int bit = 31; bit >= 0; --bit) {
