@@ -70,7 +70,7 @@ STREAM_CONFIGS = {
     # several centroids (cluster sizes stay heavy-tailed)
     "cfg3": dict(n=100_000_000, dim=768, nlist=65536, nq=10_000, sigma=0.25, qnoise=0.05, k=10,
                  nprobes=[16, 24, 32, 48, 64, 96, 128, 192, 256], seed=20261203, metric=1,
-                 zipf=1.1, vanguard=5, init="sample"),
+                 zipf=1.1, vanguard=5, init="sample", queue=1 << 30),
     # a small case of the same shape (tests of the streamed path, profiling)
     "cfg4s": dict(n=4_000_000, dim=768, nlist=2048, nq=2000, sigma=0.2, qnoise=0.05, k=100,
                   nprobes=[16, 32, 64], seed=20261208, metric=1, zipf=None, vanguard=5),
@@ -78,6 +78,17 @@ STREAM_CONFIGS = {
     # base (profiling the rotation, probe GEMM and probe selection at full size)
     "cfg4p": dict(n=4_000_000, dim=768, nlist=32768, nq=10_000, sigma=0.2, qnoise=0.05, k=100,
                   nprobes=[32], seed=20261209, metric=1, zipf=None, vanguard=5),
+}
+
+# Configurations generated per shard under torchrun (one rank per GPU): the clusters are the
+# mixture's components, each rank generates and quantises only the clusters cora_shard_plan
+# gives it, and the search runs cluster-sharded over all ranks.
+SHARD_GEN_CONFIGS = {
+    "cfg5": dict(n=1_000_000_000, dim=96, nlist=262_144, sigma=0.25, qnoise=0.05, nq=10_000,
+                 k=10, nprobes=[64, 128, 256, 512, 1024], seed=20261205, block=1024),
+    # a small case of the same construction (the path's check at 1-2 GPUs)
+    "cfg5s": dict(n=40_000_000, dim=96, nlist=16_384, sigma=0.25, qnoise=0.05, nq=10_000,
+                  k=10, nprobes=[16, 32, 64, 128], seed=20261206, block=256),
 }
 
 
@@ -455,7 +466,9 @@ def run_stream(args, name, cfg):
     eng = cb.HybridIndex(0)
     apply_tuning(eng, args.tuning)
     eng.set_vanguard_size(cfg["vanguard"])
-    eng.set_queue_capacity(1 << 28)  # candidate records per search (16 B each)
+    # candidate records per search (16 B each); the Zipf configuration's heavy clusters
+    # (largest 160K vectors) need more than 2^28 / 10K per query
+    eng.set_queue_capacity(cfg.get("queue", 1 << 28))
     t2 = time.time()
     eng.load_search_data(sd)
     eng.prepare_workspace(nq, k, max(cfg["nprobes"]))
@@ -641,6 +654,226 @@ def run_stream(args, name, cfg):
 
 
 # ------------------------------------------------------------------------------------
+# per-shard generated configurations (one copy of the index over all ranks)
+# ------------------------------------------------------------------------------------
+def run_shard_gen(args, name, cfg):
+    """BASELINE config 5's construction: every rank generates, quantises and loads only its
+    own clusters (cora_load_shard_arrays), so no host holds the whole index; ranks build in
+    waves sized to the host's memory. The ground truth is the merge of every shard's exact
+    top-k; recall is distance-aware with exact scores gathered from the owning shards. The
+    search is one cluster-sharded copy over all ranks answering one batch (strong scaling),
+    replayed from one CUDA graph per rank (engine launches and both NCCL all-gathers); QPS is
+    the batch over the max-over-ranks device time."""
+    import gc
+    import psutil
+    import torch
+    import torch.distributed as dist
+    import coraanns_b200 as cb
+    from coraanns_b200 import synthetic
+    from coraanns_b200.shard import ShardedIndex, shard_plan
+
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    timeout = __import__("datetime").timedelta(seconds=900)
+    if "MASTER_ADDR" in os.environ:
+        dist.init_process_group("nccl", timeout=timeout, device_id=dev)
+    else:
+        import socket
+        with socket.socket() as sk:
+            sk.bind(("127.0.0.1", 0))
+            port = sk.getsockname()[1]
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=0,
+                                world_size=1, timeout=timeout, device_id=dev)
+
+    def total(x, op):
+        t = torch.tensor([float(x)], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    k, nq, nprobes = cfg["k"], cfg["nq"], list(cfg["nprobes"])
+    if args.nprobe:
+        nprobes = [args.nprobe]
+    t0 = time.time()
+    mix = synthetic.ComponentShards(cfg["n"], cfg["dim"], cfg["nlist"], cfg["sigma"],
+                                    cfg["seed"], device=dev, block=cfg["block"])
+    owner = shard_plan(mix.counts, world)
+    local_n = int(mix.counts[owner == rank].sum())
+    per_rank = [total(local_n if r == rank else 0, dist.ReduceOp.SUM) for r in range(world)]
+    host_need = max(per_rank) * synthetic.shard_bytes_per_vector(cfg["dim"])
+    avail = total(psutil.virtual_memory().available if rank == 0 else 0, dist.ReduceOp.SUM)
+    wave = max(1, min(world, int(0.5 * avail // max(host_need, 1))))
+    six = ShardedIndex(local)
+    apply_tuning(six.engine, args.tuning)
+    for w in range((world + wave - 1) // wave):
+        if rank // wave == w:
+            sd = synthetic.build_shard(mix, owner, rank, metric=0, seed=cfg["seed"], log=log)
+            six.engine.load_shard_arrays(sd, mix.counts)
+            del sd
+            gc.collect()
+        dist.barrier()
+    six._verify()
+    build_s = time.time() - t0
+    log(f"[bench] {name}: {world} shards of {per_rank[0]:.0f}..{max(per_rank):.0f} vectors "
+        f"built and loaded in {build_s:.1f}s (waves of {wave})")
+
+    q = mix.queries(nq, cfg["qnoise"])
+    q_np = q.cpu().numpy()
+    t1 = time.time()
+    li, ld = synthetic.ground_truth_shard(mix, owner, rank, q, k)
+    gi = [torch.empty_like(li) for _ in range(world)]
+    gd = [torch.empty_like(ld) for _ in range(world)]
+    dist.all_gather(gi, li)
+    dist.all_gather(gd, ld)
+    gt_ids, gt_d = synthetic.merge_topk(torch.cat(gi, 1), torch.cat(gd, 1), k)
+    log(f"[bench] ground truth (merged over shards) in {time.time() - t1:.1f}s")
+
+    six.prepare_workspace(nq, k, max(nprobes))
+    od = torch.empty((nq, k), dtype=torch.float32, device=dev)
+    oi = torch.empty((nq, k), dtype=torch.int32, device=dev)
+
+    def recall_now():
+        ids = oi.to(torch.int64)
+        sc = synthetic.exact_scores_shard(mix, owner, rank, q, ids)
+        dist.all_reduce(sc, op=dist.ReduceOp.MIN)
+        return synthetic.distance_recall(gt_ids, gt_d, ids, sc, k)
+
+    def timed(fn, reps):
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return total(e0.elapsed_time(e1) / reps, dist.ReduceOp.MAX)
+
+    estimators = {"bitwise": cb.KernelType.Bitwise, "lut": cb.KernelType.Lut4Bit}
+    if args.estimator != "auto":
+        estimators = {args.estimator: estimators[args.estimator]}
+    sweeps, candidates = {}, {}
+    for ename, kt in estimators.items():
+        six.engine.set_ip_kernel_type(kt)
+        for npb in nprobes:
+            six.search_device(q, k, npb, od, oi)
+            torch.cuda.synchronize()
+            six.engine.check_device()
+            r = recall_now()
+            sweeps.setdefault(ename, {})[npb] = round(r, 4)
+            if r >= TARGET_RECALL and ename not in candidates:
+                ms = timed(lambda: six.search_device(q, k, npb, od, oi), 3)  # noqa: B023
+                candidates[ename] = dict(nprobe=npb, recall=round(r, 4), ms=ms)
+    if candidates:
+        estimator = min(candidates, key=lambda n: candidates[n]["ms"])
+        chosen = candidates[estimator]["nprobe"]
+    else:
+        estimator, chosen = next(iter(estimators)), nprobes[-1]
+    six.engine.set_ip_kernel_type(estimators[estimator])
+    log(f"[bench] recall sweeps {sweeps} -> {estimator} estimator, nprobe {chosen}")
+
+    eager = lambda: six.search_device(q, k, chosen, od, oi)  # noqa: E731
+    for _ in range(args.warmup):
+        eager()
+    torch.cuda.synchronize()
+    six.engine.check_device()
+    six.capture(q, k, chosen, od, oi)
+    for _ in range(args.warmup):
+        six.replay()
+    torch.cuda.synchronize()
+    six.engine.check_device()
+    with ClockSampler(local) as clk:
+        per_step = [timed(six.replay, args.steps)]
+        want = int(1000.0 * args.min_seconds / max(per_step[0] * args.steps, 1e-3)) + 1
+        for _ in range(0 if args.min_seconds <= 0 else max(2, min(50, want - 1))):
+            per_step.append(timed(six.replay, args.steps))
+    six.engine.check_device()
+    six.release_graph()
+    ms = float(np.median(per_step))
+    qps = nq / (ms / 1e3)
+    recall = recall_now()
+
+    # stage times per rank (eager, stage events)
+    six.engine.set_profiling(True)
+    eager()
+    torch.cuda.synchronize()
+    six.engine.stage_reset()
+    for _ in range(3):
+        eager()
+    torch.cuda.synchronize()
+    cnt, tot = six.engine.stage_totals()
+    six.engine.set_profiling(False)
+    mine = torch.tensor([tot[s_] / max(cnt, 1) for s_ in cb.STAGES], dtype=torch.float64,
+                        device=dev)
+    allr = torch.empty((world, len(cb.STAGES)), dtype=torch.float64, device=dev)
+    dist.all_gather_into_tensor(allr, mine)
+    stage_ranks = [dict(zip(cb.STAGES, map(float, r_))) for r_ in allr.cpu().numpy()]
+
+    # end to end through the public API: host queries in, host results out, every step
+    for _ in range(args.warmup):
+        six.search(q_np, k, chosen)
+    dist.barrier()
+    e2e_steps = args.steps * len(per_step)
+    tt = time.perf_counter()
+    for _ in range(e2e_steps):
+        six.search(q_np, k, chosen)
+    e2e_s = total((time.perf_counter() - tt) / e2e_steps, dist.ReduceOp.MAX)
+
+    # roofline of the lows pass on this rank: its vanguard pairs' clusters
+    probes = six.engine.debug("probe_ids", nq, chosen)
+    veff = min(max(six.engine.get_vanguard_size(), 1), chosen)
+    vg = probes[:, :veff]
+    D = builder_padded(cfg["dim"])
+    lows_bytes = int(mix.counts[vg][owner[vg] == rank].sum()) * (D // 8 + 12)
+    kern_ms = stage_ranks[rank]["vanguard_scan"]
+    achieved = lows_bytes / (kern_ms / 1e3) / 1e9 if kern_ms > 0 else None
+    peak, peak_src = measured_peaks()
+    roof = dict(bound="hbm", kernel="scan_kernel lows pass (this rank's vanguard pairs)",
+                achieved=achieved, peak=peak, unit="GB/s",
+                frac=(achieved / peak) if achieved else None, traffic=None, peak_source=peak_src,
+                algorithmic_bytes_per_launch=lows_bytes, launch_ms=kern_ms, rank=rank,
+                note="bytes = n_c*(D/8+12) per (query, probed cluster) of the launch")
+    roofs = [None] * world
+    dist.all_gather_object(roofs, roof)
+    mode = six.engine.get_vanguard_mode()
+    per_search = launches_per_search(chosen, k, mode, world, estimator, 0)
+    if rank == 0:
+        line = dict(
+            metric=f"QPS at recall@{k}>=0.95 (IVF-RaBitQ search)", value=qps, unit="queries/s",
+            n_gpus=world, steps=args.steps, warmup=args.warmup, ms_per_step=ms,
+            higher_is_better=True, scaling="strong", vs_baseline=None,
+            dtype="i8+f32" if estimator == "bitwise" else "f16+f32",
+            data=f"synthetic (seeded Gaussian mixture, BASELINE {name[:4]} shape, each shard's "
+                 "clusters generated by its own rank)",
+            config=dict(workload=f"{name}: {cfg['n']} x d{cfg['dim']} L2, nlist {cfg['nlist']} "
+                                 f"(the mixture's components), 8-bit RaBitQ, {nq} queries, "
+                                 f"topk {k}, cluster-sharded over {world} GPUs",
+                        nprobe=chosen, recall=round(recall, 4), estimator=estimator,
+                        recall_sweeps=sweeps, qualifying=candidates, shards=world,
+                        vectors_per_shard=[int(v) for v in per_rank], build_s=round(build_s, 1),
+                        build_waves=wave, timed_repeats=len(per_step),
+                        stage_ms_per_rank=stage_ranks,
+                        l2_flush="inputs exceed L2 (index codes > 126 MB)",
+                        cpu_baseline_note="no host holds the whole index; the reference's CPU "
+                                          "search is timed on configs 1-4"),
+            roofline=roofs[0], roofline_per_rank=roofs, cpu_baseline=None,
+            e2e=dict(value=nq / e2e_s, unit="queries/s", h2d_bytes_per_step=nq * cfg["dim"] * 4,
+                     d2h_bytes_per_step=nq * k * 8),
+            gpu_launches=per_search * args.steps * len(per_step), clocks=clk.summary())
+        emit(line)
+    six.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def builder_padded(dim):
+    from coraanns_b200 import builder
+    return builder.padded_dim(dim)
+
+
+# ------------------------------------------------------------------------------------
 # main
 # ------------------------------------------------------------------------------------
 def main():
@@ -649,7 +882,8 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(STREAM_CONFIGS), default="cfg2")
+    ap.add_argument("--config", choices=sorted(CONFIGS) + sorted(STREAM_CONFIGS)
+                    + sorted(SHARD_GEN_CONFIGS), default="cfg2")
     ap.add_argument("--nprobe", type=int, default=0, help="fix nprobe instead of sweeping")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--shards", type=int, default=0,
@@ -673,6 +907,13 @@ def main():
     redirect_stdout()
     if args.warmup < 3 and args.impl == "ours":
         args.warmup = 3
+    if args.config in SHARD_GEN_CONFIGS:
+        if args.impl != "ours":
+            emit({"impl": args.impl, "unavailable": f"{args.config}: no host holds the whole "
+                                                    "index for the reference's CPU search"})
+            return
+        run_shard_gen(args, args.config, SHARD_GEN_CONFIGS[args.config])
+        return
     if args.config in STREAM_CONFIGS:
         if int(os.environ.get("WORLD_SIZE", 1)) > 1 or args.impl != "ours":
             emit({"impl": args.impl, "unavailable": f"{args.config} runs on one GPU, ours only"})

@@ -43,6 +43,7 @@ EXPORTS = [
     "cora_set_vanguard_lows_budget", "cora_set_tuning", "cora_get_vanguard_mode",
     "cora_get_candidate_capacity", "cora_probe_noalloc", "cora_probe_noalloc_scratch_limit",
     "cora_probe_noalloc_status",
+    "cora_load_shard_arrays",
     "cora_shard_plan", "cora_shard_configure", "cora_shard_info", "cora_shard_exchange_words",
     "cora_shard_search_begin", "cora_shard_search_resume", "cora_shard_search_end",
 ]
@@ -104,6 +105,8 @@ def _bind(L):
     _sig(L, "cora_probe_noalloc", C.c_int, _p, _p, _u64, _u64, _p, _p, _p)
     _sig(L, "cora_probe_noalloc_scratch_limit", _u64)
     _sig(L, "cora_probe_noalloc_status", C.c_int, _p, _p)
+    _sig(L, "cora_load_shard_arrays", C.c_int, _p, _u64, _u64, _u64, _u64, _u64, _p, _p, _p, _p,
+         _p, _p, _p, _p, _p)
     _sig(L, "cora_shard_plan", C.c_int, _p, _u64, C.c_uint32, _p)
     _sig(L, "cora_shard_configure", C.c_int, _p, C.c_uint32, C.c_uint32)
     _sig(L, "cora_shard_info", C.c_int, _p, _p)
@@ -233,6 +236,20 @@ class HybridIndex:
                                     sd["centroids"], sd["rotator"], sd["short_data"],
                                     sd["short_factors"], sd["long_codes"], sd["ex_factors"],
                                     sd["ids"], sd["sizes"])
+
+    def load_shard_arrays(self, sd: dict, global_sizes):
+        """Load a shard from a SearchData-layout dict that holds only this shard's clusters
+        (sd["sizes"]: the local sizes, zero for the other clusters; every centroid) given the
+        whole index's cluster sizes; see cora_load_shard_arrays."""
+        self.set_metric(int(sd.get("metric", 0)))
+        arrs = [np.ascontiguousarray(sd[k], dt) for k, dt in (
+            ("centroids", np.float32), ("rotator", np.float32), ("short_data", np.uint32),
+            ("short_factors", np.float32), ("long_codes", np.uint8), ("ex_factors", np.float32),
+            ("ids", np.uint32), ("sizes", np.uint64))]
+        gs = np.ascontiguousarray(global_sizes, np.uint64)
+        _check(_lib.cora_load_shard_arrays(self._h, int(sd["num"]), int(sd["dim"]), int(sd["D"]),
+                                           int(sd["nlist"]), int(sd["ex_bits"]),
+                                           *[_ptr(a) for a in arrs], _ptr(gs)))
 
     def load_index_file(self, path):
         _check(_lib.cora_load_index_file(self._h, str(path).encode()))

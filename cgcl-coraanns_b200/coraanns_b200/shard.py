@@ -132,6 +132,12 @@ class ShardedIndex:
         self.engine.load_search_data(sd)
         self._verify()
 
+    def load_shard_arrays(self, sd_local, global_sizes):
+        """This rank's clusters only (shard_search_data's layout, built or read by this rank
+        alone) and the whole index's cluster sizes."""
+        self.engine.load_shard_arrays(sd_local, global_sizes)
+        self._verify()
+
     def _verify(self):
         import torch
         import torch.distributed as dist

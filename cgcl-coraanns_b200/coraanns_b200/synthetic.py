@@ -186,37 +186,50 @@ def _scores(q, x, metric):
     return (x * x).sum(1)[None, :] - 2 * (q @ x.T)
 
 
+def _gt_update(best_d, best_i, x, gid, q, k, metric, keep, qblock):
+    """Folds the vectors x (ids gid, int64) into the running exact top-k (best_d, best_i):
+    an fp32 filter keeps the `keep` best per query, whose fp64 scores decide; order by
+    (fp64 distance, id)."""
+    nq = q.shape[0]
+    for b in range(0, nq, qblock):
+        qb = q[b:b + qblock]
+        sc = _scores(qb, x, metric)
+        _, vi = torch.topk(sc, min(keep, x.shape[0]), dim=1, largest=False)
+        xv = x[vi].double()                                   # qb x keep x dim
+        if metric == 1:
+            ex = -(xv * qb.double()[:, None, :]).sum(2)
+        else:
+            ex = ((xv - qb.double()[:, None, :]) ** 2).sum(2)
+        cd = torch.cat([best_d[b:b + qblock], ex], 1)
+        ci = torch.cat([best_i[b:b + qblock], gid[vi]], 1)
+        # (distance, id) order: stable sort by id, then stable by distance
+        o = torch.argsort(ci, dim=1, stable=True)
+        cd, ci = torch.gather(cd, 1, o), torch.gather(ci, 1, o)
+        o = torch.argsort(cd, dim=1, stable=True)[:, :k]
+        best_d[b:b + qblock] = torch.gather(cd, 1, o)
+        best_i[b:b + qblock] = torch.gather(ci, 1, o)
+
+
+def _gt_init(q, k):
+    nq = q.shape[0]
+    return (torch.full((nq, k), float("inf"), dtype=torch.float64, device=q.device),
+            torch.zeros((nq, k), dtype=torch.int64, device=q.device))
+
+
 def ground_truth_stream(mix: Mixture, q, k, metric=0, keep=None, qblock=2048):
     """Exact top-k of every query over the whole base: per chunk an fp32 filter keeps the
     `keep` best per query, whose fp64 scores are computed from the chunk's vectors; the
     final top-k is by (fp64 distance, id) over all kept candidates. Returns (ids int64,
     distances fp64): squared L2, or minus the inner product."""
     keep = keep or max(2 * k, 64)
-    nq = q.shape[0]
-    best_d = torch.full((nq, k), float("inf"), dtype=torch.float64, device=q.device)
-    best_i = torch.zeros((nq, k), dtype=torch.int64, device=q.device)
+    best_d, best_i = _gt_init(q, k)
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
         for j in range(mix.n_chunks):
             x, _, s = mix.chunk_at(j)
-            for b in range(0, nq, qblock):
-                qb = q[b:b + qblock]
-                sc = _scores(qb, x, metric)
-                _, vi = torch.topk(sc, min(keep, x.shape[0]), dim=1, largest=False)
-                xv = x[vi].double()                                   # qb x keep x dim
-                if metric == 1:
-                    ex = -(xv * qb.double()[:, None, :]).sum(2)
-                else:
-                    ex = ((xv - qb.double()[:, None, :]) ** 2).sum(2)
-                cd = torch.cat([best_d[b:b + qblock], ex], 1)
-                ci = torch.cat([best_i[b:b + qblock], vi + s], 1)
-                # (distance, id) order: stable sort by id, then stable by distance
-                o = torch.argsort(ci, dim=1, stable=True)
-                cd, ci = torch.gather(cd, 1, o), torch.gather(ci, 1, o)
-                o = torch.argsort(cd, dim=1, stable=True)[:, :k]
-                best_d[b:b + qblock] = torch.gather(cd, 1, o)
-                best_i[b:b + qblock] = torch.gather(ci, 1, o)
+            gid = torch.arange(s, s + x.shape[0], device=x.device)
+            _gt_update(best_d, best_i, x, gid, q, k, metric, keep, qblock)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
     return best_i, best_d
@@ -253,3 +266,166 @@ def distance_recall(gt_ids, gt_d, res_ids, res_d_exact, k):
     dup[:, 1:] = (srt[:, 1:] == srt[:, :-1]) & (srt[:, 1:] >= 0)
     hits = (srt >= 0).sum() - dup.sum()
     return float(hits) / (r.shape[0] * k)
+
+
+# ------------------------------------------------------------------------------------
+# Per-shard generation (the base is generated per shard from a seed)
+# ------------------------------------------------------------------------------------
+class ComponentShards:
+    """n vectors of a Gaussian mixture with `ncomp` equally weighted components (centres
+    N(0, 1), per-component sigma) whose IVF clusters are its components: cluster c holds the
+    counts[c] vectors drawn from component c (multinomial counts from the seed), and its
+    centroid is the component's centre. Vector ids are cluster-major: cluster c's vectors
+    are base[c] .. base[c] + counts[c] - 1. Clusters are generated in blocks of `block`
+    clusters, block b from its own generator, so a shard regenerates exactly its clusters'
+    vectors without any other shard's data or any exchange."""
+
+    def __init__(self, n, dim, ncomp, sigma, seed, device="cuda", block=1024):
+        self.n, self.dim, self.ncomp, self.sigma, self.seed = n, dim, ncomp, sigma, seed
+        self.dev = torch.device(device)
+        self.block = block
+        rng = np.random.default_rng(seed)
+        self.counts = rng.multinomial(n, np.full(ncomp, 1.0 / ncomp)).astype(np.int64)
+        self.base = np.concatenate([[0], np.cumsum(self.counts)[:-1]]).astype(np.int64)
+        g = torch.Generator(device=self.dev).manual_seed(seed)
+        self.centres = torch.randn(ncomp, dim, generator=g, device=self.dev)
+
+    @property
+    def n_blocks(self):
+        return (self.ncomp + self.block - 1) // self.block
+
+    def block_at(self, b, keep=None):
+        """(vectors, cluster labels, global ids) of the clusters of block b; with `keep` (a
+        bool mask over clusters) only the kept clusters' vectors (all are generated, so the
+        result does not depend on the mask)."""
+        c0, c1 = b * self.block, min(self.ncomp, (b + 1) * self.block)
+        cnt = torch.as_tensor(self.counts[c0:c1], device=self.dev)
+        lab = torch.repeat_interleave(torch.arange(c0, c1, device=self.dev), cnt)
+        g = torch.Generator(device=self.dev).manual_seed(self.seed * 1_000_003 + 7919 * (b + 1))
+        x = self.centres[lab] + self.sigma * torch.randn(lab.shape[0], self.dim, generator=g,
+                                                         device=self.dev)
+        gid = torch.arange(int(self.base[c0]), int(self.base[c0]) + lab.shape[0], device=self.dev)
+        if keep is not None:
+            m = torch.as_tensor(keep[c0:c1], device=self.dev)[lab - c0]
+            x, lab, gid = x[m], lab[m], gid[m]
+        return x, lab, gid
+
+    def queries(self, nq, qnoise, salt=1):
+        g = torch.Generator(device=self.dev).manual_seed(self.seed * 1_000_003 - salt)
+        lab = torch.randint(0, self.ncomp, (nq,), generator=g, device=self.dev)
+        q = (self.centres[lab] + self.sigma * torch.randn(nq, self.dim, generator=g, device=self.dev)
+             + qnoise * torch.randn(nq, self.dim, generator=g, device=self.dev))
+        return q.contiguous()
+
+    def blocks_with(self, keep):
+        """Blocks holding at least one kept cluster."""
+        return [b for b in range(self.n_blocks)
+                if keep[b * self.block:(b + 1) * self.block].any()]
+
+
+def shard_bytes_per_vector(dim):
+    """Host bytes of one vector in a shard's SearchData arrays."""
+    D = builder.padded_dim(dim)
+    return D // 32 * 4 + 12 + D * 7 // 8 + 8 + 4
+
+
+def build_shard(mix: ComponentShards, owner, rank, metric=0, seed=7, log=None):
+    """This shard's SearchData-layout arrays (host memory): every rotated centroid, the owned
+    clusters' vectors quantised against their centroid in cluster order, sizes zero for the
+    other clusters (what cora_load_shard_arrays takes)."""
+    dev = mix.dev
+    own = np.asarray(owner) == rank
+    sizes = np.where(own, mix.counts, 0).astype(np.int64)
+    n = int(sizes.sum())
+    dim, nlist = mix.dim, mix.ncomp
+    D = builder.padded_dim(dim)
+    W, lc = D // 32, D * 7 // 8
+    starts = np.concatenate([[0], np.cumsum(sizes)[:-1]]).astype(np.int64)
+    starts_d = torch.as_tensor(starts, device=dev)
+    sizes_d = torch.as_tensor(sizes, device=dev)
+    base_d = torch.as_tensor(mix.base, device=dev)
+    P = torch.as_tensor(builder.random_rotation(dim, seed), device=dev)
+    crot = (mix.centres.double() @ P.double()).float()
+    t_const = builder.const_scaling_factor(D, 7, seed + 1)
+    short = np.empty(n * W, np.uint32)
+    fac = np.empty((n, 3), np.float32)
+    lcs = np.empty((n, lc), np.uint8)
+    exf = np.empty((n, 2), np.float32)
+    ids = np.empty(n, np.uint32)
+    done = 0
+    for b in mix.blocks_with(own):
+        x, lab, gid = mix.block_at(b, keep=own)
+        for t in range(0, x.shape[0], 1 << 18):
+            xs, cl, gi = x[t:t + (1 << 18)], lab[t:t + (1 << 18)], gid[t:t + (1 << 18)]
+            xr = (xs.double() @ P.double()).float()
+            bits, f, code, ef = builder._quantize_rows(xr, crot[cl], t_const, metric=metric)
+            i_in = gi - base_d[cl]                               # index within the cluster
+            pos = starts_d[cl] + i_in                            # position in the shard
+            words = builder._words(bits)                         # m x W (int64)
+            widx = ((starts_d[cl] * W + i_in)[:, None]
+                    + torch.arange(W, device=dev)[None, :] * sizes_d[cl][:, None])
+            short[widx.cpu().numpy().ravel()] = words.cpu().numpy().astype(np.uint32).ravel()
+            pn = pos.cpu().numpy()
+            fac[pn] = f.cpu().numpy()
+            exf[pn] = ef.cpu().numpy()
+            lcs[pn] = builder._pack_ex7(code).cpu().numpy()
+            ids[pn] = gi.cpu().numpy().astype(np.uint32)
+        done += x.shape[0]
+        if log and b % 32 == 31:
+            log(f"[synthetic] shard {rank}: quantised {done} / {n}")
+    return dict(num=n, dim=dim, D=D, nlist=nlist, ex_bits=7, centroids=crot.cpu().numpy(),
+                rotator=P.cpu().numpy(), short_data=short, short_factors=fac,
+                long_codes=lcs.reshape(-1), ex_factors=exf, ids=ids,
+                sizes=sizes.astype(np.uint64), t_const=t_const, metric=metric)
+
+
+def ground_truth_shard(mix: ComponentShards, owner, rank, q, k, metric=0, keep=None,
+                       qblock=2048):
+    """Exact top-k (as ground_truth_stream) over this shard's clusters only; the global
+    ground truth is the (distance, id) merge of every shard's (merge_topk)."""
+    keep = keep or max(2 * k, 64)
+    own = np.asarray(owner) == rank
+    best_d, best_i = _gt_init(q, k)
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        for b in mix.blocks_with(own):
+            x, _, gid = mix.block_at(b, keep=own)
+            _gt_update(best_d, best_i, x, gid, q, k, metric, keep, qblock)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    return best_i, best_d
+
+
+def merge_topk(ids, dists, k):
+    """Top-k by (distance, id) of per-shard results concatenated along dim 1."""
+    o = torch.argsort(ids, dim=1, stable=True)
+    d, i = torch.gather(dists, 1, o), torch.gather(ids, 1, o)
+    o = torch.argsort(d, dim=1, stable=True)[:, :k]
+    return torch.gather(i, 1, o), torch.gather(d, 1, o)
+
+
+def exact_scores_shard(mix: ComponentShards, owner, rank, q, ids, metric=0):
+    """exact_scores over this shard's clusters: +inf for ids held by other shards (the
+    elementwise minimum over shards gives every score)."""
+    ids = torch.as_tensor(ids, dtype=torch.int64, device=q.device)
+    out = torch.full(ids.shape, float("inf"), dtype=torch.float64, device=q.device)
+    own = np.asarray(owner) == rank
+    qd = q.double()
+    for b in mix.blocks_with(own):
+        c0, c1 = b * mix.block, min(mix.ncomp, (b + 1) * mix.block)
+        s, e = int(mix.base[c0]), int(mix.base[c1 - 1] + mix.counts[c1 - 1])
+        sel = (ids >= s) & (ids < e)
+        if not bool(sel.any()):
+            continue
+        x, lab, gid = mix.block_at(b)  # every cluster of the block (row = id - s)
+        qi, col = torch.nonzero(sel, as_tuple=True)
+        row = ids[qi, col] - s
+        mine = torch.as_tensor(own, device=q.device)[lab[row]]
+        qi, col, row = qi[mine], col[mine], row[mine]
+        xv = x[row].double()
+        if metric == 1:
+            out[qi, col] = -(xv * qd[qi]).sum(1)
+        else:
+            out[qi, col] = ((xv - qd[qi]) ** 2).sum(1)
+    return out

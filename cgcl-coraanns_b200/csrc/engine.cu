@@ -1811,6 +1811,45 @@ int cora_shard_configure(cora_engine *engine, uint32_t rank, uint32_t world) {
     });
 }
 
+int cora_load_shard_arrays(cora_engine *engine, uint64_t local_vecs, uint64_t d, uint64_t p_d,
+                           uint64_t n_centroids, uint64_t ex_b, const float *h_centroids,
+                           const float *h_rotator, const uint32_t *h_short_data,
+                           const float *h_short_factors, const uint8_t *h_long_code,
+                           const float *h_ex_factors, const uint32_t *h_ids,
+                           const uint64_t *h_local_sizes, const uint64_t *h_global_sizes) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        if (e.loaded) cora::fail(CORA_ESTATE, "index already loaded");
+        if (!h_local_sizes || !h_global_sizes || n_centroids == 0)
+            cora::fail(CORA_EINVAL, "null cluster sizes");
+        std::vector<int32_t> owner(n_centroids, 0);
+        if (e.shard_world > 1)
+            cora::plan_shards(h_global_sizes, n_centroids, e.shard_world, owner.data());
+        std::vector<uint8_t> mask(n_centroids, 0);
+        uint64_t local = 0, kept = 0;
+        for (uint64_t c = 0; c < n_centroids; ++c) {
+            const bool own = owner[c] == static_cast<int32_t>(e.shard_rank);
+            if (h_local_sizes[c] != (own ? h_global_sizes[c] : 0))
+                cora::fail(CORA_EINVAL, "cluster " + std::to_string(c) +
+                                            ": local size differs from this shard's plan");
+            if (own) {
+                mask[c] = 1;
+                local += h_global_sizes[c];
+                ++kept;
+            }
+        }
+        if (local != local_vecs) cora::fail(CORA_EINVAL, "local cluster sizes differ from local_vecs");
+        if (e.shard_world <= 1) {
+            e.load_any(local_vecs, d, p_d, n_centroids, ex_b, h_centroids, h_rotator, h_short_data,
+                       h_short_factors, h_long_code, h_ex_factors, h_ids, h_local_sizes);
+            return;
+        }
+        e.load_shard_local(local_vecs, d, p_d, n_centroids, ex_b, h_centroids, h_rotator,
+                           h_short_data, h_short_factors, h_long_code, h_ex_factors, h_ids,
+                           h_local_sizes, mask, kept);
+    });
+}
+
 int cora_shard_info(const cora_engine *engine, uint64_t *out4) {
     return guarded([&] {
         const Engine &e = eng(engine);

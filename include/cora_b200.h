@@ -238,6 +238,19 @@ uint64_t cora_get_candidate_capacity(const cora_engine *engine);
  * is the top-k of all) plus its device error word, so that every rank reports a failure on
  * any shard. Results equal an unsharded search of the whole index, bit for bit. */
 
+/* Loads a shard from arrays that hold only its own clusters (no counterpart in the
+ * reference): for an index too large for one host, each rank builds or reads just the
+ * clusters that cora_shard_plan(h_global_sizes, world) gives it. Arguments as
+ * cora_load_from_raw_pointers, with the arrays in cluster order over the owned clusters
+ * (local_vecs vectors), h_local_sizes[c] = h_global_sizes[c] for owned clusters and 0 for
+ * the others (CORA_EINVAL otherwise), and every centroid. Call after cora_shard_configure;
+ * with world 1 it loads the whole index. */
+int cora_load_shard_arrays(cora_engine *engine, uint64_t local_vecs, uint64_t d, uint64_t p_d,
+                           uint64_t n_centroids, uint64_t ex_b, const float *h_centroids,
+                           const float *h_rotator, const uint32_t *h_short_data,
+                           const float *h_short_factors, const uint8_t *h_long_code,
+                           const float *h_ex_factors, const uint32_t *h_ids,
+                           const uint64_t *h_local_sizes, const uint64_t *h_global_sizes);
 /* Longest-processing-time plan over cluster sizes: owner_out[c] = shard of cluster c. */
 int cora_shard_plan(const uint64_t *sizes, uint64_t nlist, uint32_t world, int32_t *owner_out);
 /* Makes the engine load only shard `rank` of `world` (call before loading; world 1 = whole

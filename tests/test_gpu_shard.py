@@ -121,6 +121,63 @@ def test_local_shards_synthetic_match_unsharded(cb):
     ls.close()
 
 
+def test_shard_arrays_built_per_shard_match_whole_index(cb):
+    """Shard engines loaded from arrays of their own clusters only (cora_load_shard_arrays),
+    each built alone by per-shard generation, search bit-identically to the engine that
+    holds the whole index; a local size that disagrees with the plan is rejected."""
+    import torch
+    from coraanns_b200 import synthetic
+    from coraanns_b200.shard import exchange_words, shard_plan
+    mix = synthetic.ComponentShards(400_000, 96, 512, 0.25, seed=3, device="cuda", block=64)
+    world, k, nprobe = 3, 10, 16
+    owner = shard_plan(mix.counts, world)
+    q = mix.queries(256, 0.05).cpu().numpy()
+    whole = synthetic.build_shard(mix, np.zeros(mix.ncomp, np.int32), 0, seed=5)
+    e = cb.HybridIndex(0)
+    e.load_search_data(whole)
+    e.prepare_workspace(len(q), k, nprobe)
+    e.reset_buffer(q)
+    want_d, want_i = e.search(q, k, nprobe)
+    e.close()
+    engines = []
+    for r in range(world):
+        s = cb.HybridIndex(0)
+        s.shard_configure(r, world)
+        s.load_shard_arrays(synthetic.build_shard(mix, owner, r, seed=5), mix.counts)
+        s.prepare_workspace(len(q), k, nprobe)
+        engines.append(s)
+    w = exchange_words(len(q), k)
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        dq = torch.from_numpy(q).cuda()
+        sends = [torch.empty(w, dtype=torch.int64, device="cuda") for _ in range(world)]
+        recv = torch.empty(world * w, dtype=torch.int64, device="cuda")
+        od = torch.empty((len(q), k), dtype=torch.float32, device="cuda")
+        oi = torch.empty((len(q), k), dtype=torch.int32, device="cuda")
+        for s, b in zip(engines, sends):
+            s.shard_search_begin(dq.data_ptr(), len(q), k, nprobe, b.data_ptr(), st.cuda_stream)
+        torch.cat(sends, out=recv)
+        for s, b in zip(engines, sends):
+            s.shard_search_resume(recv.data_ptr(), b.data_ptr())
+        torch.cat(sends, out=recv)
+        engines[0].shard_search_end(recv.data_ptr(), od.data_ptr(), oi.data_ptr())
+    st.synchronize()
+    for s in engines:
+        s.check_device()
+        s.close()
+    assert np.array_equal(oi.cpu().numpy().view(np.uint32), want_i)
+    assert od.cpu().numpy().tobytes() == want_d.tobytes()
+    bad = synthetic.build_shard(mix, owner, 0, seed=5)
+    bad["sizes"] = bad["sizes"].copy()
+    c = int(np.flatnonzero(owner != 0)[0])
+    bad["sizes"][c] = 1
+    s = cb.HybridIndex(0)
+    s.shard_configure(0, world)
+    with pytest.raises(cb.InvalidArgument, match="plan"):
+        s.load_shard_arrays(bad, mix.counts)
+    s.close()
+
+
 def test_sharded_engine_rules(cb):
     path = str(GOLDEN / "demo.index")
     e = cb.HybridIndex(0)

@@ -43,3 +43,51 @@ def test_stream_ground_truth_and_scores(metric):
     sc = synthetic.exact_scores(mix, q, ids, metric)
     assert np.allclose(sc.numpy(), want_d, rtol=1e-12, atol=1e-12)
     assert synthetic.distance_recall(ids, d, ids.numpy(), sc, 10) == 1.0
+
+
+def _component_fixture(world=3):
+    from coraanns_b200 import synthetic
+    from coraanns_b200.shard import shard_plan
+    mix = synthetic.ComponentShards(30_000, 40, 64, 0.25, seed=11, device="cpu", block=16)
+    owner = shard_plan(mix.counts, world)
+    return mix, owner
+
+
+def test_shard_build_equals_slice_of_whole_build():
+    """Each shard built alone from its own clusters (per-shard generation) holds exactly the
+    arrays the whole index's build gives that shard (shard_search_data)."""
+    from coraanns_b200 import builder, synthetic
+    from coraanns_b200.shard import shard_search_data
+    mix, owner = _component_fixture()
+    xs, labs = [], []
+    for b in range(mix.n_blocks):
+        x, lab, gid = mix.block_at(b)
+        assert int(gid[0]) == sum(int(v.shape[0]) for v in xs)  # cluster-major ids
+        xs.append(x)
+        labs.append(lab)
+    full = builder.build_index(torch.cat(xs), mix.centres, torch.cat(labs), seed=5)
+    assert np.array_equal(full["sizes"].astype(np.int64), mix.counts)
+    for r in range(3):
+        want = shard_search_data(full, owner, r)
+        got = synthetic.build_shard(mix, owner, r, seed=5)
+        assert got["num"] == want["num"] > 0
+        for key in ("centroids", "rotator", "short_data", "short_factors", "long_codes",
+                    "ex_factors", "ids", "sizes"):
+            assert np.asarray(got[key]).tobytes() == np.asarray(want[key]).tobytes(), key
+
+
+def test_shard_ground_truth_merges_to_whole():
+    from coraanns_b200 import synthetic
+    mix, owner = _component_fixture()
+    q = mix.queries(40, 0.05)
+    parts = [synthetic.ground_truth_shard(mix, owner, r, q, 10) for r in range(3)]
+    ids, d = synthetic.merge_topk(torch.cat([p[0] for p in parts], 1),
+                                  torch.cat([p[1] for p in parts], 1), 10)
+    best_d, best_i = synthetic._gt_init(q, 10)
+    for b in range(mix.n_blocks):
+        x, _, gid = mix.block_at(b)
+        synthetic._gt_update(best_d, best_i, x, gid, q, 10, 0, 64, 2048)
+    assert torch.equal(ids, best_i) and torch.equal(d, best_d)
+    # exact scores of every returned id, each from its own shard
+    sc = torch.stack([synthetic.exact_scores_shard(mix, owner, r, q, ids) for r in range(3)])
+    assert torch.equal(sc.min(0).values, best_d)
