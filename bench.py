@@ -85,10 +85,10 @@ STREAM_CONFIGS = {
 # gives it, and the search runs cluster-sharded over all ranks.
 SHARD_GEN_CONFIGS = {
     "cfg5": dict(n=1_000_000_000, dim=96, nlist=262_144, sigma=0.25, qnoise=0.05, nq=10_000,
-                 k=10, nprobes=[64, 128, 256, 512, 1024], seed=20261205, block=1024),
+                 k=10, nprobes=[64, 128, 256, 512, 1024], seed=20261205),
     # a small case of the same construction (the path's check at 1-2 GPUs)
     "cfg5s": dict(n=40_000_000, dim=96, nlist=16_384, sigma=0.25, qnoise=0.05, nq=10_000,
-                  k=10, nprobes=[16, 32, 64, 128], seed=20261206, block=256),
+                  k=10, nprobes=[16, 32, 64, 128], seed=20261206),
 }
 
 
@@ -698,7 +698,7 @@ def run_shard_gen(args, name, cfg):
         nprobes = [args.nprobe]
     t0 = time.time()
     mix = synthetic.ComponentShards(cfg["n"], cfg["dim"], cfg["nlist"], cfg["sigma"],
-                                    cfg["seed"], device=dev, block=cfg["block"])
+                                    cfg["seed"], device=dev)
     owner = shard_plan(mix.counts, world)
     local_n = int(mix.counts[owner == rank].sum())
     per_rank = [total(local_n if r == rank else 0, dist.ReduceOp.SUM) for r in range(world)]

@@ -276,39 +276,49 @@ class ComponentShards:
     N(0, 1), per-component sigma) whose IVF clusters are its components: cluster c holds the
     counts[c] vectors drawn from component c (multinomial counts from the seed), and its
     centroid is the component's centre. Vector ids are cluster-major: cluster c's vectors
-    are base[c] .. base[c] + counts[c] - 1. Clusters are generated in blocks of `block`
-    clusters, block b from its own generator, so a shard regenerates exactly its clusters'
-    vectors without any other shard's data or any exchange."""
+    are base[c] .. base[c] + counts[c] - 1. Each cluster's noise comes from its own
+    generator, so a shard generates exactly its own clusters' vectors, without any other
+    shard's data or any exchange."""
 
-    def __init__(self, n, dim, ncomp, sigma, seed, device="cuda", block=1024):
+    def __init__(self, n, dim, ncomp, sigma, seed, device="cuda"):
         self.n, self.dim, self.ncomp, self.sigma, self.seed = n, dim, ncomp, sigma, seed
         self.dev = torch.device(device)
-        self.block = block
         rng = np.random.default_rng(seed)
         self.counts = rng.multinomial(n, np.full(ncomp, 1.0 / ncomp)).astype(np.int64)
         self.base = np.concatenate([[0], np.cumsum(self.counts)[:-1]]).astype(np.int64)
         g = torch.Generator(device=self.dev).manual_seed(seed)
         self.centres = torch.randn(ncomp, dim, generator=g, device=self.dev)
 
-    @property
-    def n_blocks(self):
-        return (self.ncomp + self.block - 1) // self.block
-
-    def block_at(self, b, keep=None):
-        """(vectors, cluster labels, global ids) of the clusters of block b; with `keep` (a
-        bool mask over clusters) only the kept clusters' vectors (all are generated, so the
-        result does not depend on the mask)."""
-        c0, c1 = b * self.block, min(self.ncomp, (b + 1) * self.block)
-        cnt = torch.as_tensor(self.counts[c0:c1], device=self.dev)
-        lab = torch.repeat_interleave(torch.arange(c0, c1, device=self.dev), cnt)
-        g = torch.Generator(device=self.dev).manual_seed(self.seed * 1_000_003 + 7919 * (b + 1))
-        x = self.centres[lab] + self.sigma * torch.randn(lab.shape[0], self.dim, generator=g,
-                                                         device=self.dev)
-        gid = torch.arange(int(self.base[c0]), int(self.base[c0]) + lab.shape[0], device=self.dev)
-        if keep is not None:
-            m = torch.as_tensor(keep[c0:c1], device=self.dev)[lab - c0]
-            x, lab, gid = x[m], lab[m], gid[m]
+    def clusters(self, cids):
+        """(vectors, cluster labels, global ids) of the clusters `cids` (ascending), in
+        cluster order."""
+        cids = np.asarray(cids, np.int64)
+        noise = []
+        for c in cids:
+            g = torch.Generator(device=self.dev).manual_seed(self.seed * 1_000_003 + 7919 * (int(c) + 1))
+            noise.append(torch.randn(int(self.counts[c]), self.dim, generator=g, device=self.dev))
+        cnt = torch.as_tensor(self.counts[cids], device=self.dev)
+        c_d = torch.as_tensor(cids, device=self.dev)
+        lab = torch.repeat_interleave(c_d, cnt)
+        first = torch.repeat_interleave(torch.as_tensor(self.base[cids], device=self.dev), cnt)
+        start = torch.repeat_interleave(torch.cumsum(cnt, 0) - cnt, cnt)
+        gid = first + torch.arange(lab.shape[0], device=self.dev) - start
+        x = self.centres[lab] + self.sigma * torch.cat(noise) if noise else \
+            torch.empty((0, self.dim), device=self.dev)
         return x, lab, gid
+
+    def batches(self, keep=None, rows=1 << 22):
+        """clusters() of the kept clusters (all when keep is None), ascending, in batches of
+        whole clusters of about `rows` vectors."""
+        cids = np.arange(self.ncomp) if keep is None else np.flatnonzero(keep)
+        i = 0
+        while i < len(cids):
+            j, m = i, 0
+            while j < len(cids) and (j == i or m + self.counts[cids[j]] <= rows):
+                m += int(self.counts[cids[j]])
+                j += 1
+            yield self.clusters(cids[i:j])
+            i = j
 
     def queries(self, nq, qnoise, salt=1):
         g = torch.Generator(device=self.dev).manual_seed(self.seed * 1_000_003 - salt)
@@ -316,11 +326,6 @@ class ComponentShards:
         q = (self.centres[lab] + self.sigma * torch.randn(nq, self.dim, generator=g, device=self.dev)
              + qnoise * torch.randn(nq, self.dim, generator=g, device=self.dev))
         return q.contiguous()
-
-    def blocks_with(self, keep):
-        """Blocks holding at least one kept cluster."""
-        return [b for b in range(self.n_blocks)
-                if keep[b * self.block:(b + 1) * self.block].any()]
 
 
 def shard_bytes_per_vector(dim):
@@ -353,8 +358,7 @@ def build_shard(mix: ComponentShards, owner, rank, metric=0, seed=7, log=None):
     exf = np.empty((n, 2), np.float32)
     ids = np.empty(n, np.uint32)
     done = 0
-    for b in mix.blocks_with(own):
-        x, lab, gid = mix.block_at(b, keep=own)
+    for bi, (x, lab, gid) in enumerate(mix.batches(own)):
         for t in range(0, x.shape[0], 1 << 18):
             xs, cl, gi = x[t:t + (1 << 18)], lab[t:t + (1 << 18)], gid[t:t + (1 << 18)]
             xr = (xs.double() @ P.double()).float()
@@ -371,7 +375,7 @@ def build_shard(mix: ComponentShards, owner, rank, metric=0, seed=7, log=None):
             lcs[pn] = builder._pack_ex7(code).cpu().numpy()
             ids[pn] = gi.cpu().numpy().astype(np.uint32)
         done += x.shape[0]
-        if log and b % 32 == 31:
+        if log and bi % 16 == 15:
             log(f"[synthetic] shard {rank}: quantised {done} / {n}")
     return dict(num=n, dim=dim, D=D, nlist=nlist, ex_bits=7, centroids=crot.cpu().numpy(),
                 rotator=P.cpu().numpy(), short_data=short, short_factors=fac,
@@ -389,8 +393,7 @@ def ground_truth_shard(mix: ComponentShards, owner, rank, q, k, metric=0, keep=N
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
-        for b in mix.blocks_with(own):
-            x, _, gid = mix.block_at(b, keep=own)
+        for x, _, gid in mix.batches(own):
             _gt_update(best_d, best_i, x, gid, q, k, metric, keep, qblock)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
@@ -407,23 +410,30 @@ def merge_topk(ids, dists, k):
 
 def exact_scores_shard(mix: ComponentShards, owner, rank, q, ids, metric=0):
     """exact_scores over this shard's clusters: +inf for ids held by other shards (the
-    elementwise minimum over shards gives every score)."""
+    elementwise minimum over shards gives every score). Only the owned clusters that hold a
+    requested id are generated."""
     ids = torch.as_tensor(ids, dtype=torch.int64, device=q.device)
     out = torch.full(ids.shape, float("inf"), dtype=torch.float64, device=q.device)
     own = np.asarray(owner) == rank
+    valid = (ids >= 0) & (ids < mix.n)
+    cl = np.searchsorted(mix.base, ids.clamp(0, mix.n - 1).cpu().numpy(), side="right") - 1
+    need = np.zeros(mix.ncomp, bool)
+    need[np.unique(cl[valid.cpu().numpy()])] = True
+    need &= own
+    cl_d = torch.as_tensor(cl, device=q.device)
     qd = q.double()
-    for b in mix.blocks_with(own):
-        c0, c1 = b * mix.block, min(mix.ncomp, (b + 1) * mix.block)
-        s, e = int(mix.base[c0]), int(mix.base[c1 - 1] + mix.counts[c1 - 1])
-        sel = (ids >= s) & (ids < e)
+    for x, lab, gid in mix.batches(need):
+        s, e = int(gid[0]), int(gid[-1]) + 1  # the batch's clusters are consecutive ids
+        sel = valid & (ids >= s) & (ids < e) & torch.as_tensor(need, device=q.device)[cl_d]
         if not bool(sel.any()):
             continue
-        x, lab, gid = mix.block_at(b)  # every cluster of the block (row = id - s)
         qi, col = torch.nonzero(sel, as_tuple=True)
-        row = ids[qi, col] - s
-        mine = torch.as_tensor(own, device=q.device)[lab[row]]
-        qi, col, row = qi[mine], col[mine], row[mine]
-        xv = x[row].double()
+        # row of id within the batch: ids of the batch's clusters are not contiguous across
+        # clusters that are not consecutive, so look each id up among gid
+        pos = torch.searchsorted(gid, ids[qi, col])
+        hit = (pos < gid.shape[0]) & (gid[pos.clamp(max=gid.shape[0] - 1)] == ids[qi, col])
+        qi, col, pos = qi[hit], col[hit], pos[hit]
+        xv = x[pos].double()
         if metric == 1:
             out[qi, col] = -(xv * qd[qi]).sum(1)
         else:

@@ -128,7 +128,7 @@ def test_shard_arrays_built_per_shard_match_whole_index(cb):
     import torch
     from coraanns_b200 import synthetic
     from coraanns_b200.shard import exchange_words, shard_plan
-    mix = synthetic.ComponentShards(400_000, 96, 512, 0.25, seed=3, device="cuda", block=64)
+    mix = synthetic.ComponentShards(400_000, 96, 512, 0.25, seed=3, device="cuda")
     world, k, nprobe = 3, 10, 16
     owner = shard_plan(mix.counts, world)
     q = mix.queries(256, 0.05).cpu().numpy()

@@ -48,7 +48,7 @@ def test_stream_ground_truth_and_scores(metric):
 def _component_fixture(world=3):
     from coraanns_b200 import synthetic
     from coraanns_b200.shard import shard_plan
-    mix = synthetic.ComponentShards(30_000, 40, 64, 0.25, seed=11, device="cpu", block=16)
+    mix = synthetic.ComponentShards(30_000, 40, 64, 0.25, seed=11, device="cpu")
     owner = shard_plan(mix.counts, world)
     return mix, owner
 
@@ -59,13 +59,12 @@ def test_shard_build_equals_slice_of_whole_build():
     from coraanns_b200 import builder, synthetic
     from coraanns_b200.shard import shard_search_data
     mix, owner = _component_fixture()
-    xs, labs = [], []
-    for b in range(mix.n_blocks):
-        x, lab, gid = mix.block_at(b)
-        assert int(gid[0]) == sum(int(v.shape[0]) for v in xs)  # cluster-major ids
-        xs.append(x)
-        labs.append(lab)
-    full = builder.build_index(torch.cat(xs), mix.centres, torch.cat(labs), seed=5)
+    x, lab, gid = mix.clusters(np.arange(mix.ncomp))
+    assert torch.equal(gid, torch.arange(mix.n))  # cluster-major ids
+    # batches of whole clusters regenerate the same vectors
+    xb = torch.cat([b[0] for b in mix.batches(rows=1000)])
+    assert torch.equal(xb, x)
+    full = builder.build_index(x, mix.centres, lab, seed=5)
     assert np.array_equal(full["sizes"].astype(np.int64), mix.counts)
     for r in range(3):
         want = shard_search_data(full, owner, r)
@@ -84,8 +83,7 @@ def test_shard_ground_truth_merges_to_whole():
     ids, d = synthetic.merge_topk(torch.cat([p[0] for p in parts], 1),
                                   torch.cat([p[1] for p in parts], 1), 10)
     best_d, best_i = synthetic._gt_init(q, 10)
-    for b in range(mix.n_blocks):
-        x, _, gid = mix.block_at(b)
+    for x, _, gid in mix.batches(rows=5000):
         synthetic._gt_update(best_d, best_i, x, gid, q, 10, 0, 64, 2048)
     assert torch.equal(ids, best_i) and torch.equal(d, best_d)
     # exact scores of every returned id, each from its own shard
