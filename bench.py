@@ -754,18 +754,25 @@ def run_shard_gen(args, name, cfg):
     estimators = {"bitwise": cb.KernelType.Bitwise, "lut": cb.KernelType.Lut4Bit}
     if args.estimator != "auto":
         estimators = {args.estimator: estimators[args.estimator]}
+    # per estimator: nprobe ascending up to the first that reaches the target, or until
+    # the recall stops rising (two points within 0.001: more probes do not help)
     sweeps, candidates = {}, {}
     for ename, kt in estimators.items():
         six.engine.set_ip_kernel_type(kt)
+        prev = -1.0
         for npb in nprobes:
             six.search_device(q, k, npb, od, oi)
             torch.cuda.synchronize()
             six.engine.check_device()
             r = recall_now()
             sweeps.setdefault(ename, {})[npb] = round(r, 4)
-            if r >= TARGET_RECALL and ename not in candidates:
+            if r >= TARGET_RECALL:
                 ms = timed(lambda: six.search_device(q, k, npb, od, oi), 3)  # noqa: B023
                 candidates[ename] = dict(nprobe=npb, recall=round(r, 4), ms=ms)
+                break
+            if r - prev < 1e-3:
+                break
+            prev = r
     if candidates:
         estimator = min(candidates, key=lambda n: candidates[n]["ms"])
         chosen = candidates[estimator]["nprobe"]
