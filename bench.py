@@ -70,7 +70,7 @@ STREAM_CONFIGS = {
     # several centroids (cluster sizes stay heavy-tailed)
     "cfg3": dict(n=100_000_000, dim=768, nlist=65536, nq=10_000, sigma=0.25, qnoise=0.05, k=10,
                  nprobes=[16, 24, 32, 48, 64, 96, 128, 192, 256], seed=20261203, metric=1,
-                 zipf=1.1, vanguard=5, init="sample", queue=1 << 30),
+                 zipf=1.1, vanguard=5, init="sample", queue=1 << 31),
     # a small case of the same shape (tests of the streamed path, profiling)
     "cfg4s": dict(n=4_000_000, dim=768, nlist=2048, nq=2000, sigma=0.2, qnoise=0.05, k=100,
                   nprobes=[16, 32, 64], seed=20261208, metric=1, zipf=None, vanguard=5),
@@ -467,7 +467,7 @@ def run_stream(args, name, cfg):
     apply_tuning(eng, args.tuning)
     eng.set_vanguard_size(cfg["vanguard"])
     # candidate records per search (16 B each); the Zipf configuration's heavy clusters
-    # (largest 160K vectors) need more than 2^28 / 10K per query
+    # (largest ~150K vectors) need more than 2^30 / 10K per query
     eng.set_queue_capacity(cfg.get("queue", 1 << 28))
     t2 = time.time()
     eng.load_search_data(sd)
@@ -497,13 +497,17 @@ def run_stream(args, name, cfg):
     if args.estimator != "auto":
         estimators = {args.estimator: estimators[args.estimator]}
     nprobes = [args.nprobe] if args.nprobe else cfg["nprobes"]
-    runs, results = [], []
+    runs, results, overflow = [], [], {}
     for ename, kt in estimators.items():
         eng.set_ip_kernel_type(kt)
         for npb in nprobes:
             search_dev(npb)
             torch.cuda.synchronize()
-            eng.check_device()
+            try:
+                eng.check_device()
+            except cb.CoraRuntimeError as ex:  # candidates beyond the HBM queue: larger
+                overflow[ename] = dict(nprobe=npb, error=str(ex))  # nprobes would be too
+                break
             runs.append((ename, npb))
             results.append(out_i.to(torch.int64).clone())
     eng.set_ip_kernel_type(cb.KernelType.Bitwise)
@@ -517,7 +521,7 @@ def run_stream(args, name, cfg):
         sweeps.setdefault(ename, {})[npb] = round(r, 4)
     for ename, kt in estimators.items():
         for npb in nprobes:
-            if sweeps[ename][npb] >= TARGET_RECALL:
+            if sweeps.get(ename, {}).get(npb, 0.0) >= TARGET_RECALL:
                 eng.set_ip_kernel_type(kt)
                 candidates[ename] = dict(nprobe=npb, recall=sweeps[ename][npb], ms=quick_ms(npb))
                 break
@@ -638,8 +642,9 @@ def run_stream(args, name, cfg):
                              f"{'inner product (unit vectors)' if metric else 'L2'}, "
                              f"nlist {cfg['nlist']}, 8-bit RaBitQ, {nq} queries, topk {k}"
                              + (f", Zipf({cfg['zipf']}) component weights" if cfg["zipf"] else ""),
-                    nprobe=chosen, recall=sweeps[estimator].get(chosen),
+                    nprobe=chosen, recall=sweeps.get(estimator, {}).get(chosen),
                     estimator=estimator, recall_sweeps=sweeps, qualifying=candidates,
+                    sweep_stopped_by_queue_overflow=overflow or None,
                     vanguard=cfg["vanguard"], vanguard_mode="lows" if mode == 1 else "rescan",
                     candidates_per_query=refined / nq, stage_ms=stage_avg,
                     largest_cluster=int(sizes.max()), timed_repeats=len(rep_ms),

@@ -45,7 +45,8 @@ EXPORTS = [
     "cora_probe_noalloc_status",
     "cora_load_shard_arrays",
     "cora_shard_plan", "cora_shard_configure", "cora_shard_info", "cora_shard_exchange_words",
-    "cora_shard_search_begin", "cora_shard_search_resume", "cora_shard_search_end",
+    "cora_shard_search_begin", "cora_shard_probe_words", "cora_shard_search_probe",
+    "cora_shard_search_begin_probed", "cora_shard_search_resume", "cora_shard_search_end",
 ]
 
 _p = C.c_void_p
@@ -112,6 +113,9 @@ def _bind(L):
     _sig(L, "cora_shard_info", C.c_int, _p, _p)
     _sig(L, "cora_shard_exchange_words", _u64, _u64, _u64)
     _sig(L, "cora_shard_search_begin", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p)
+    _sig(L, "cora_shard_probe_words", _u64, _u64, _u64, C.c_uint32)
+    _sig(L, "cora_shard_search_probe", C.c_int, _p, _p, _u64, _u64, _u64, _p, _p)
+    _sig(L, "cora_shard_search_begin_probed", C.c_int, _p, _p, _p)
     _sig(L, "cora_shard_search_resume", C.c_int, _p, _p, _p)
     _sig(L, "cora_shard_search_end", C.c_int, _p, _p, _p, _p)
 
@@ -345,6 +349,16 @@ class HybridIndex:
         _check(_lib.cora_shard_search_begin(self._h, C.c_void_p(d_queries), num_queries, topk,
                                             nprobe, C.c_void_p(d_send),
                                             C.c_void_p(stream) if stream else None))
+
+    def shard_search_probe(self, d_queries: int, num_queries, topk, nprobe, d_send: int,
+                           stream: int = 0):
+        _check(_lib.cora_shard_search_probe(self._h, C.c_void_p(d_queries), num_queries, topk,
+                                            nprobe, C.c_void_p(d_send),
+                                            C.c_void_p(stream) if stream else None))
+
+    def shard_search_begin_probed(self, d_recv: int, d_send: int):
+        _check(_lib.cora_shard_search_begin_probed(self._h, C.c_void_p(d_recv),
+                                                   C.c_void_p(d_send)))
 
     def shard_search_resume(self, d_recv: int, d_send: int):
         _check(_lib.cora_shard_search_resume(self._h, C.c_void_p(d_recv), C.c_void_p(d_send)))

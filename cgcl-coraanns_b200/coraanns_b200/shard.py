@@ -10,6 +10,10 @@ is three engine calls with two all-gathers between them, which this module runs 
     resume -> all-gather each shard's top-k keys (+ its device error word)
     end    -> top-k of all shards
 
+By default (``split_probe``) the probing is also split: each shard runs the probe GEMM and
+the exact top-nprobe for its slice of the queries only, and a first all-gather of the probe
+lists precedes ``begin`` (``probe -> all-gather -> begin_probed``).
+
 The result equals an unsharded search of the whole index bit for bit (the reference searches
 on one GPU only; this layer has no counterpart there).
 
@@ -78,10 +82,25 @@ def torch_exchange(group=None):
     return exchange
 
 
-def run_sharded_search(backend, exchange, queries, nq, k, nprobe, out_d, out_i):
-    """One search across all shards: every rank calls this with the same arguments."""
+def probe_words(nq: int, nprobe: int, world: int) -> int:
+    """u64 words of one shard's probe-exchange buffer (its slice of the probe lists + one
+    status word)."""
+    return int(_lib.cora_shard_probe_words(nq, nprobe, world))
+
+
+def run_sharded_search(backend, exchange, queries, nq, k, nprobe, out_d, out_i,
+                       split_probe=False):
+    """One search across all shards: every rank calls this with the same arguments. With
+    split_probe each shard probes only its slice of the queries and a first all-gather
+    exchanges the probe lists (backend.probe / begin_probed)."""
     send, recv = backend.buffers(nq, k)
-    backend.begin(queries, nq, k, nprobe, send)
+    if split_probe:
+        psend, precv = backend.probe_buffers(nq, nprobe)
+        backend.probe(queries, nq, k, nprobe, psend)
+        exchange(psend, precv)
+        backend.begin_probed(precv, send)
+    else:
+        backend.begin(queries, nq, k, nprobe, send)
     exchange(send, recv)
     backend.resume(recv, send)
     exchange(send, recv)
@@ -110,7 +129,7 @@ class ShardedIndex:
     other ranks of `group` (torch.distributed, NCCL). Every rank loads the same index and
     calls search with the same queries and arguments."""
 
-    def __init__(self, device: int, group=None):
+    def __init__(self, device: int, group=None, split_probe: bool = True):
         import torch.distributed as dist
         self.group = group
         self.rank = dist.get_rank(group)
@@ -118,7 +137,11 @@ class ShardedIndex:
         self.engine = HybridIndex(device)
         self.engine.shard_configure(self.rank, self.world)
         self.device = device
+        # probing split by query over the shards (an extra all-gather of probe lists); the
+        # probing stage then costs each shard 1 / world of its single-GPU time
+        self.split_probe = split_probe and self.world > 1
         self._bufs = None
+        self._pbufs = None
         self._stream = None
         self._graph = None
         self.exchange = torch_exchange(group)
@@ -158,6 +181,9 @@ class ShardedIndex:
         dev = f"cuda:{self.device}"
         self._bufs = (torch.empty(w, dtype=torch.int64, device=dev),
                       torch.empty(self.world * w, dtype=torch.int64, device=dev))
+        pw = probe_words(max_queries, max_nprobe, self.world)
+        self._pbufs = (torch.empty(pw, dtype=torch.int64, device=dev),
+                       torch.empty(self.world * pw, dtype=torch.int64, device=dev))
 
     # backend protocol of run_sharded_search
     def buffers(self, nq, k):
@@ -165,6 +191,20 @@ class ShardedIndex:
             raise LogicError("prepare workspace before searching")
         w = exchange_words(nq, k)
         return self._bufs[0][:w], self._bufs[1][:self.world * w]
+
+    def probe_buffers(self, nq, nprobe):
+        if self._pbufs is None:
+            raise LogicError("prepare workspace before searching")
+        w = probe_words(nq, nprobe, self.world)
+        return self._pbufs[0][:w], self._pbufs[1][:self.world * w]
+
+    def probe(self, queries, nq, k, nprobe, send):
+        import torch
+        self.engine.shard_search_probe(queries.data_ptr(), nq, k, nprobe, send.data_ptr(),
+                                       torch.cuda.current_stream(self.device).cuda_stream)
+
+    def begin_probed(self, recv, send):
+        self.engine.shard_search_begin_probed(recv.data_ptr(), send.data_ptr())
 
     def begin(self, queries, nq, k, nprobe, send):
         import torch
@@ -188,7 +228,7 @@ class ShardedIndex:
         self._stream.wait_stream(cur)
         with torch.cuda.stream(self._stream):
             run_sharded_search(self, self.exchange, queries, queries.shape[0], k, nprobe, out_d,
-                               out_i)
+                               out_i, self.split_probe)
         cur.wait_stream(self._stream)
 
     def capture(self, queries, k, nprobe, out_d, out_i):
@@ -205,7 +245,7 @@ class ShardedIndex:
         torch.cuda.synchronize(self.device)
         with torch.cuda.graph(g, stream=self._stream, capture_error_mode="relaxed"):
             run_sharded_search(self, self.exchange, queries, queries.shape[0], k, nprobe, out_d,
-                               out_i)
+                               out_i, self.split_probe)
         self._graph = g
 
     def replay(self):

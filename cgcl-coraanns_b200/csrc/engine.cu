@@ -853,6 +853,10 @@ struct Engine {
                         uint32_t *d_oi, cudaStream_t st);
     void enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, cudaStream_t st,
                        uint64_t *seed_keys_out);
+    void enqueue_rotate(const float *d_q, uint64_t nq, uint64_t k, uint64_t np, cudaStream_t st);
+    void enqueue_probe_range(uint64_t q0, uint64_t q1, cudaStream_t st);
+    void enqueue_probe_gadd(cudaStream_t st);
+    void enqueue_vanguard(uint64_t *seed_keys_out);
     void enqueue_back(const uint64_t *seed_recv, int world, float *d_od, uint32_t *d_oi,
                       uint64_t *topk_keys_out);
     void enqueue_final(const uint64_t *topk_recv, int world, float *d_od, uint32_t *d_oi);
@@ -1150,15 +1154,22 @@ void Engine::enqueue_search(const float *d_q, uint64_t nq, uint64_t k, uint64_t 
 // (T1) or, for a sharded search, this shard's k smallest seed keys into seed_keys_out.
 void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t np,
                            cudaStream_t st, uint64_t *seed_keys_out) {
+    enqueue_rotate(d_q, nq, k, np, st);
+    enqueue_probe_range(0, nq, st);
+    enqueue_probe_gadd(st);
+    mark(3, st);
+    enqueue_vanguard(seed_keys_out);
+}
+
+// Steps 0-1 of a search: counters, rotation, query factors, bit-planes (and LUT tables) of
+// every query of the batch.
+void Engine::enqueue_rotate(const float *d_q, uint64_t nq, uint64_t k, uint64_t np,
+                            cudaStream_t st) {
     last_stream = st;
     last_nq = nq;
     last_k = k;
     last_np = np;
     last_dq = d_q;
-    const int inq = static_cast<int>(nq), ik = static_cast<int>(k);
-    const uint64_t veff = vanguard_depth(np);
-    const uint64_t keep = std::max<uint64_t>(k, kVanguardMinKeep);
-
     CUDA_TRY(cudaMemsetAsync(err.p, 0, 4, st));
     CUDA_TRY(cudaMemsetAsync(stats.p, 0, 16, st));
     CUDA_TRY(cudaMemsetAsync(cand_cnt.p, 0, nq * 4, st));
@@ -1178,29 +1189,48 @@ void Engine::enqueue_front(const float *d_q, uint64_t nq, uint64_t k, uint64_t n
         }
     }
     mark(1, st);
-    // 2. coarse probing: approximate distances for every (query, centroid), then the exact
-    //    top-nprobe among the guarded candidates
-    {
-        launch_probe_gemm(qr.p, qnorm2.p, nq, D, centroids.p, cnorm2.p, nlist, gmat.p, cmin.p,
-                          num_sms, st, err.p);
+}
+
+// Step 2 for queries [q0, q1) of the batch: approximate distances for every (query,
+// centroid) on the tensor cores, then the exact top-nprobe among the guarded candidates.
+void Engine::enqueue_probe_range(uint64_t q0, uint64_t q1, cudaStream_t st) {
+    const uint64_t np = last_np, m = q1 - q0;
+    if (m > 0) {
+        launch_probe_gemm(qr.p + q0 * D, qnorm2.p + q0, m, D, centroids.p, cnorm2.p, nlist,
+                          gmat.p, cmin.p, num_sms, st, err.p);
         mark(2, st);
         // select_fallback (>= 1 + nq words) is free until the vanguard stage
-        launch_guarded_select(gmat.p, cmin.p, nlist, nq, np, qr.p, qnorm2.p, centroids.p, cmax,
-                              D, probe_ids.p, probe_g.p, select_fallback.p, num_sms, st);
-        if (metric == 1) {  // inner product: the additive term -<q', c'> of every probe
-            ip_gadd_kernel<<<static_cast<unsigned>((nq + 7) / 8), 256, 0, st>>>(
-                qr.p, centroids.p, probe_ids.p, static_cast<int>(nq), static_cast<int>(np),
-                static_cast<int>(D), probe_ga.p);
-            CUDA_TRY(cudaGetLastError());
-        }
+        launch_guarded_select(gmat.p, cmin.p, nlist, m, np, qr.p + q0 * D, qnorm2.p + q0,
+                              centroids.p, cmax, D, probe_ids.p + q0 * np, probe_g.p + q0 * np,
+                              select_fallback.p, num_sms, st);
+    } else {
+        mark(2, st);
     }
-    mark(3, st);
+}
+
+// Inner product: the additive term -<q', c'> of every probe of the batch.
+void Engine::enqueue_probe_gadd(cudaStream_t st) {
+    if (metric != 1) return;
+    const uint64_t nq = last_nq;
+    ip_gadd_kernel<<<static_cast<unsigned>((nq + 7) / 8), 256, 0, st>>>(
+        qr.p, centroids.p, probe_ids.p, static_cast<int>(nq), static_cast<int>(last_np),
+        static_cast<int>(D), probe_ga.p);
+    CUDA_TRY(cudaGetLastError());
+}
+
+// Steps 3-5 of a search (probe lists in place): the vanguard pairs' seeds, their refinement
+// and the threshold (or, sharded, this shard's k smallest seed keys into seed_keys_out).
+void Engine::enqueue_vanguard(uint64_t *seed_keys_out) {
+    cudaStream_t st = last_stream;
+    const uint64_t nq = last_nq, k = last_k, np = last_np;
+    const int inq = static_cast<int>(nq);
+    const uint64_t veff = vanguard_depth(np);
+    const uint64_t keep = std::max<uint64_t>(k, kVanguardMinKeep);
     const bool lows_mode = lows.n > 0;
     const IndexView ix = index_view();
     const SearchView sv = search_view();
     const uint8_t *own = owned.n ? owned.p : nullptr;
     const ScanLaunch L = scan_launch(ix, sv, st);
-    (void)ik;
     const int iveff = static_cast<int>(veff);
     const unsigned n_van = static_cast<unsigned>(nq * veff);
     // 3. vanguard pairs: seeds (best `keep` keys per pair among low < T0)
@@ -1875,6 +1905,63 @@ int cora_shard_search_begin(cora_engine *engine, const float *d_queries, uint64_
         cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e.stream;
         e.split_phase = 0;
         e.enqueue_front(d_queries, num_queries, topk, nprobe, st, d_send);
+        e.split_phase = 1;
+    });
+}
+
+uint64_t cora_shard_probe_words(uint64_t num_queries, uint64_t nprobe, uint32_t world) {
+    if (world == 0) return 0;
+    return (num_queries + world - 1) / world * nprobe + 1;
+}
+
+int cora_shard_search_probe(cora_engine *engine, const float *d_queries, uint64_t num_queries,
+                            uint64_t topk, uint64_t nprobe, uint64_t *d_send, void *stream) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        e.validate_ws(num_queries, topk, nprobe);
+        if (!d_queries || !d_send) cora::fail(CORA_EINVAL, "invalid device search buffers");
+        if (e.shard_world > 256) cora::fail(CORA_EINVAL, "at most 256 shards");
+        CUDA_TRY(cudaSetDevice(e.device));
+        cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : e.stream;
+        e.split_phase = 0;
+        const uint64_t world = e.shard_world, slice = (num_queries + world - 1) / world;
+        const uint64_t q0 = std::min<uint64_t>(num_queries, e.shard_rank * slice);
+        const uint64_t q1 = std::min<uint64_t>(num_queries, q0 + slice);
+        e.enqueue_rotate(d_queries, num_queries, topk, nprobe, st);
+        e.enqueue_probe_range(q0, q1, st);
+        const uint64_t stride = cora_shard_probe_words(num_queries, nprobe, e.shard_world);
+        const size_t n = (q1 - q0) * nprobe;
+        cora::pack_probes_kernel<<<static_cast<unsigned>(std::max<size_t>(1, std::min<size_t>(
+                                       (n + 255) / 256, 4 * (size_t)e.num_sms))),
+                                   256, 0, st>>>(e.probe_ids.p + q0 * nprobe,
+                                                 e.probe_g.p + q0 * nprobe, n, e.err.p, d_send,
+                                                 stride);
+        CUDA_TRY(cudaGetLastError());
+        e.split_phase = 3;
+    });
+}
+
+int cora_shard_search_begin_probed(cora_engine *engine, const uint64_t *d_recv,
+                                   uint64_t *d_send) {
+    return guarded([&] {
+        Engine &e = eng(engine);
+        if (e.split_phase != 3) cora::fail(CORA_ESTATE, "shard search: probe must come first");
+        if (!d_recv || !d_send) cora::fail(CORA_EINVAL, "invalid exchange buffers");
+        CUDA_TRY(cudaSetDevice(e.device));
+        e.split_phase = 0;
+        cudaStream_t st = e.last_stream;
+        const uint64_t nq = e.last_nq, np = e.last_np, world = e.shard_world;
+        const uint64_t slice = (nq + world - 1) / world;
+        cora::unpack_probes_kernel<<<static_cast<unsigned>(std::max<uint64_t>(1, std::min<uint64_t>(
+                                         (nq * np + 255) / 256, 4 * (uint64_t)e.num_sms))),
+                                     256, 0, st>>>(d_recv, static_cast<int>(world),
+                                                   cora_shard_probe_words(nq, np, e.shard_world),
+                                                   slice, nq, static_cast<int>(np), e.probe_ids.p,
+                                                   e.probe_g.p, e.err.p);
+        CUDA_TRY(cudaGetLastError());
+        e.enqueue_probe_gadd(st);
+        e.mark(3, st);
+        e.enqueue_vanguard(d_send);
         e.split_phase = 1;
     });
 }

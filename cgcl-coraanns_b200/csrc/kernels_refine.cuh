@@ -627,6 +627,43 @@ __global__ void __launch_bounds__(256) topk_warp_kernel(SearchView sv, int mode,
 // exchange buffer: k keys per query, then one word (a device error word in the final
 // exchange). One CTA per query; dynamic shared memory: next_pow2(k) keys.
 
+// Probe exchange (probing split by query over the shards): shard r probes queries
+// [r s, min(nq, (r + 1) s)), s = ceil(nq / world), and sends one word per (query, probe rank)
+// of its slice, (bits of g << 32) | cluster, then its device error word.
+__global__ void __launch_bounds__(256) pack_probes_kernel(const int *__restrict__ probe_ids,
+                                                          const float *__restrict__ probe_g,
+                                                          size_t n, const int *__restrict__ err,
+                                                          uint64_t *__restrict__ out,
+                                                          size_t stride) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x)
+        out[i] = (static_cast<uint64_t>(__float_as_uint(probe_g[i])) << 32) |
+                 static_cast<uint32_t>(probe_ids[i]);
+    if (blockIdx.x == 0 && threadIdx.x == 0) out[stride - 1] = static_cast<uint32_t>(*err);
+}
+
+// Every shard's slice back into the probe lists of the whole batch (nq x np), and every
+// shard's error word ORed into this shard's.
+__global__ void __launch_bounds__(256) unpack_probes_kernel(const uint64_t *__restrict__ recv,
+                                                            int world, size_t stride, size_t slice,
+                                                            size_t nq, int np,
+                                                            int *__restrict__ probe_ids,
+                                                            float *__restrict__ probe_g,
+                                                            int *__restrict__ err) {
+    const size_t n = nq * np;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const size_t q = i / np, r = q / slice;
+        const uint64_t w = recv[r * stride + (q - r * slice) * np + (i - q * np)];
+        probe_ids[i] = static_cast<int>(static_cast<uint32_t>(w));
+        probe_g[i] = __uint_as_float(static_cast<uint32_t>(w >> 32));
+    }
+    if (blockIdx.x == 0 && threadIdx.x < world) {
+        const int e = static_cast<int>(recv[threadIdx.x * stride + stride - 1]);
+        if (e) atomicOr(err, e);
+    }
+}
+
 // T1 = min(T0, k-th smallest seed key over every shard) (the single-GPU threshold_kernel
 // over the union of the shards' seeds, which contains the k smallest).
 __global__ void __launch_bounds__(256) gather_threshold_kernel(const uint64_t *__restrict__ recv,

@@ -262,6 +262,17 @@ uint64_t cora_shard_exchange_words(uint64_t num_queries, uint64_t topk);
 /* Enqueue on `stream` (NULL: the engine's stream); return without synchronising. */
 int cora_shard_search_begin(cora_engine *engine, const float *d_queries, uint64_t num_queries,
                             uint64_t topk, uint64_t nprobe, uint64_t *d_send, void *stream);
+/* Probing split by query over the shards (in place of cora_shard_search_begin): shard r
+ * rotates every query but runs the probe GEMM and the exact top-nprobe only for queries
+ * [r s, min(nq, (r + 1) s)), s = ceil(nq / world), writing that slice's probe lists to d_send
+ * (cora_shard_probe_words(nq, nprobe, world) u64); after an all-gather of those buffers (rank
+ * order), cora_shard_search_begin_probed takes every shard's slices and continues as
+ * cora_shard_search_begin does (d_send: the first exchange's buffer). The probing stage then
+ * costs each shard 1 / world of its single-GPU time; results are the same bits. */
+uint64_t cora_shard_probe_words(uint64_t num_queries, uint64_t nprobe, uint32_t world);
+int cora_shard_search_probe(cora_engine *engine, const float *d_queries, uint64_t num_queries,
+                            uint64_t topk, uint64_t nprobe, uint64_t *d_send, void *stream);
+int cora_shard_search_begin_probed(cora_engine *engine, const uint64_t *d_recv, uint64_t *d_send);
 int cora_shard_search_resume(cora_engine *engine, const uint64_t *d_recv, uint64_t *d_send);
 int cora_shard_search_end(cora_engine *engine, const uint64_t *d_recv, float *d_final_dists,
                           uint32_t *d_final_pids);

@@ -40,9 +40,9 @@ class LocalShards:
             e.prepare_workspace(nq, k, nprobe)
             self.engines.append(e)
 
-    def search(self, q, k, nprobe):
+    def search(self, q, k, nprobe, split=False):
         import torch
-        from coraanns_b200.shard import exchange_words
+        from coraanns_b200.shard import exchange_words, probe_words
         nq, world = q.shape[0], len(self.engines)
         w = exchange_words(nq, k)
         st = torch.cuda.Stream()
@@ -52,8 +52,18 @@ class LocalShards:
             recv = torch.empty(world * w, dtype=torch.int64, device="cuda")
             outs = [(torch.empty((nq, k), dtype=torch.float32, device="cuda"),
                      torch.empty((nq, k), dtype=torch.int32, device="cuda")) for _ in range(world)]
-            for e, s in zip(self.engines, sends):
-                e.shard_search_begin(dq.data_ptr(), nq, k, nprobe, s.data_ptr(), st.cuda_stream)
+            if split:  # each engine probes its slice of the queries; the lists are exchanged
+                pw = probe_words(nq, nprobe, world)
+                psends = [torch.empty(pw, dtype=torch.int64, device="cuda") for _ in range(world)]
+                precv = torch.empty(world * pw, dtype=torch.int64, device="cuda")
+                for e, ps in zip(self.engines, psends):
+                    e.shard_search_probe(dq.data_ptr(), nq, k, nprobe, ps.data_ptr(), st.cuda_stream)
+                torch.cat(psends, out=precv)
+                for e, s in zip(self.engines, sends):
+                    e.shard_search_begin_probed(precv.data_ptr(), s.data_ptr())
+            else:
+                for e, s in zip(self.engines, sends):
+                    e.shard_search_begin(dq.data_ptr(), nq, k, nprobe, s.data_ptr(), st.cuda_stream)
             torch.cat(sends, out=recv)
             for e, s in zip(self.engines, sends):
                 e.shard_search_resume(recv.data_ptr(), s.data_ptr())
@@ -74,15 +84,16 @@ CASES = [("demo", 10, 8, 5), ("demo", 50, 8, 2), ("demo", 10, 16, 0), ("d96", 10
          ("d200", 10, 8, 2), ("d150", 20, 8, 1)]
 
 
+@pytest.mark.parametrize("split", [False, True])
 @pytest.mark.parametrize("world", [2, 3])
 @pytest.mark.parametrize("lows", [True, False])
 @pytest.mark.parametrize("name,k,nprobe,van", CASES)
-def test_local_shards_match_oracle(cb, name, k, nprobe, van, world, lows):
+def test_local_shards_match_oracle(cb, name, k, nprobe, van, world, lows, split):
     z = np.load(GOLDEN / f"{name}.npz")
     q = z["queries"]
     path = str(GOLDEN / f"{name}.index")
     ls = LocalShards(cb, lambda e: e.load_index_file(path), world, len(q), k, nprobe, van, lows)
-    outs = ls.search(q, k, nprobe)
+    outs = ls.search(q, k, nprobe, split=split)
     want_d, want_i = z[f"dist_k{k}_np{nprobe}_v{van}"], z[f"ids_k{k}_np{nprobe}_v{van}"]
     for d, i in outs:
         assert np.array_equal(i, want_i)
@@ -116,8 +127,9 @@ def test_local_shards_synthetic_match_unsharded(cb):
     want_d, want_i = full.search(q, k, nprobe)
     full.close()
     ls = LocalShards(cb, lambda e: e.load_search_data(sd), 4, nq, k, nprobe)
-    for d, i in ls.search(q, k, nprobe):
-        assert np.array_equal(i, want_i) and d.tobytes() == want_d.tobytes()
+    for split in (False, True):
+        for d, i in ls.search(q, k, nprobe, split=split):
+            assert np.array_equal(i, want_i) and d.tobytes() == want_d.tobytes()
     ls.close()
 
 
@@ -193,6 +205,8 @@ def test_sharded_engine_rules(cb):
         e.search(q, 10, 4)  # a shard alone cannot answer
     with pytest.raises(cb.LogicError):
         e.shard_search_resume(1, 1)  # before begin
+    with pytest.raises(cb.LogicError, match="probe"):
+        e.shard_search_begin_probed(1, 1)  # before probe
     info = e.shard_info()
     assert info["rank"] == 1 and info["world"] == 2 and 0 < info["vectors"] < 4096
     e.close()
@@ -237,6 +251,10 @@ def _nccl_worker(rank, world, port, out_q):
             ix.engine.check_device()
             ok = ok and np.array_equal(oi.cpu().numpy().view(np.uint32), i) and \
                 od.cpu().numpy().tobytes() == d.tobytes()
+        # the same search with every shard probing the whole batch (no probe exchange)
+        ix.split_probe = False
+        d2, i2 = ix.search(q, 100, 8)
+        ok = ok and np.array_equal(i2, i) and d2.tobytes() == d.tobytes()
         ix.close()  # releases the graph before the process group goes
         out_q.put((rank, ok))
     finally:
