@@ -1273,8 +1273,13 @@ def main():
 
     sharded = None
     if world > 1 and shards == 1 and not args.no_sharded:
-        sharded = measure_sharded(args, sd, q, k, chosen, estimators[estimator], eng, local,
-                                  world, dev, total)
+        # a side measurement: its failure is recorded, not fatal to the headline line (a rank
+        # stuck in a collective leaves it when the process group's timeout expires)
+        try:
+            sharded = measure_sharded(args, sd, q, k, chosen, estimators[estimator], eng,
+                                      local, world, dev, total)
+        except Exception as ex:  # noqa: BLE001
+            sharded = {"error": f"{type(ex).__name__}: {ex}"[:500]}
 
     if world == 1:
         parallelism = "single"
