@@ -46,3 +46,17 @@ def test_null_engine_calls_are_rejected_without_a_gpu():
     assert rc == cb.CORA_EINVAL
     assert b"null engine" in cb._lib.cora_last_error()
     assert cb._lib.cora_get_vanguard_size(None) == 0
+
+
+def test_shard_entry_points_reject_null_engines_and_size_probe_buffers():
+    """The shard-local load and the split-probing calls validate their handle before any
+    device work; the probe exchange holds ceil(nq / world) * nprobe words + a status word."""
+    import coraanns_b200 as cb
+    L = cb._lib
+    z = [None] * 9
+    assert L.cora_load_shard_arrays(None, 1, 64, 64, 1, 7, *z) == cb.CORA_EINVAL
+    assert L.cora_shard_search_probe(None, None, 1, 1, 1, None, None) == cb.CORA_EINVAL
+    assert L.cora_shard_search_begin_probed(None, None, None) == cb.CORA_EINVAL
+    assert L.cora_shard_probe_words(10_000, 8, 3) == 3334 * 8 + 1
+    assert L.cora_shard_probe_words(5, 4, 8) == 1 * 4 + 1
+    assert L.cora_shard_probe_words(5, 4, 0) == 0
