@@ -240,19 +240,21 @@ def apply_tuning(engine, pairs):
         engine.set_tuning(key, int(val))
 
 
-def launches_per_search(nprobe, k, mode, shards, estimator, metric):
+def launches_per_search(nprobe, k, mode, shards, estimator, metric, split_probe=False):
     """Kernels one search launches: rotation, probe GEMM, probe selection (warp kernel + its
     block fallback when nprobe <= 32), seed refine, threshold, main grouping (4), main scan,
     refine, merge (threshold and final top-k: warp kernel + block fallback each when
     k <= 32); with stored vanguard lows also vanguard grouping (4), lows scan, seed selection
     (warp + block fallback when keep <= 128) and the lows filter (pair list + filter), else
-    one vanguard rescan; +2 exchange steps (gather_threshold / gather_merge) when sharded;
+    one vanguard rescan; +2 exchange steps (gather_threshold / gather_merge) when sharded,
+    +2 more (pack / unpack of the probe lists) with the probing split by query;
     +1 LUT build for the LUT estimator; +1 additive-term kernel for inner product."""
     sel = 2 if nprobe <= 32 else 1
     vsel = 2 if max(k, 20) <= 128 else 1
     topk = 2 if k <= 32 else 1
     return (9 + sel + 2 * topk + ((7 + vsel) if mode == 1 else 1)
-            + (2 if shards > 1 else 0) + (1 if estimator == "lut" else 0) + (1 if metric else 0))
+            + (2 if shards > 1 else 0) + (2 if shards > 1 and split_probe else 0)
+            + (1 if estimator == "lut" else 0) + (1 if metric else 0))
 
 
 
@@ -735,7 +737,11 @@ def run_shard_gen(args, name, cfg):
     gt_ids, gt_d = synthetic.merge_topk(torch.cat(gi, 1), torch.cat(gd, 1), k)
     log(f"[bench] ground truth (merged over shards) in {time.time() - t1:.1f}s")
 
-    six.prepare_workspace(nq, k, max(nprobes))
+    # the shape limit queries x nlist < 2^31 (validate_search_shape, as the reference's):
+    # the batch is searched in equal query chunks (the reference CLI's --query-chunk)
+    qmax = (2 ** 31 - 1) // cfg["nlist"]
+    chunk = -(-nq // -(-nq // qmax))
+    six.prepare_workspace(chunk, k, max(nprobes))
     od = torch.empty((nq, k), dtype=torch.float32, device=dev)
     oi = torch.empty((nq, k), dtype=torch.int32, device=dev)
 
@@ -766,13 +772,13 @@ def run_shard_gen(args, name, cfg):
         six.engine.set_ip_kernel_type(kt)
         prev = -1.0
         for npb in nprobes:
-            six.search_device(q, k, npb, od, oi)
+            six.search_device(q, k, npb, od, oi, chunk)
             torch.cuda.synchronize()
             six.engine.check_device()
             r = recall_now()
             sweeps.setdefault(ename, {})[npb] = round(r, 4)
             if r >= TARGET_RECALL:
-                ms = timed(lambda: six.search_device(q, k, npb, od, oi), 3)  # noqa: B023
+                ms = timed(lambda: six.search_device(q, k, npb, od, oi, chunk), 3)  # noqa: B023
                 candidates[ename] = dict(nprobe=npb, recall=round(r, 4), ms=ms)
                 break
             if r - prev < 1e-3:
@@ -786,12 +792,12 @@ def run_shard_gen(args, name, cfg):
     six.engine.set_ip_kernel_type(estimators[estimator])
     log(f"[bench] recall sweeps {sweeps} -> {estimator} estimator, nprobe {chosen}")
 
-    eager = lambda: six.search_device(q, k, chosen, od, oi)  # noqa: E731
+    eager = lambda: six.search_device(q, k, chosen, od, oi, chunk)  # noqa: E731
     for _ in range(args.warmup):
         eager()
     torch.cuda.synchronize()
     six.engine.check_device()
-    six.capture(q, k, chosen, od, oi)
+    six.capture(q, k, chosen, od, oi, chunk)
     for _ in range(args.warmup):
         six.replay()
     torch.cuda.synchronize()
@@ -825,32 +831,37 @@ def run_shard_gen(args, name, cfg):
 
     # end to end through the public API: host queries in, host results out, every step
     for _ in range(args.warmup):
-        six.search(q_np, k, chosen)
+        six.search(q_np, k, chosen, chunk)
     dist.barrier()
     e2e_steps = args.steps * len(per_step)
     tt = time.perf_counter()
     for _ in range(e2e_steps):
-        six.search(q_np, k, chosen)
+        six.search(q_np, k, chosen, chunk)
     e2e_s = total((time.perf_counter() - tt) / e2e_steps, dist.ReduceOp.MAX)
 
-    # roofline of the lows pass on this rank: its vanguard pairs' clusters
-    probes = six.engine.debug("probe_ids", nq, chosen)
+    # roofline of the lows pass on this rank: its vanguard pairs' clusters (the probe lists
+    # of the last chunk, scaled to the batch)
+    nlast = nq - (nq - 1) // chunk * chunk
+    probes = six.engine.debug("probe_ids", nlast, chosen)
     veff = min(max(six.engine.get_vanguard_size(), 1), chosen)
     vg = probes[:, :veff]
     D = builder_padded(cfg["dim"])
-    lows_bytes = int(mix.counts[vg][owner[vg] == rank].sum()) * (D // 8 + 12)
-    kern_ms = stage_ranks[rank]["vanguard_scan"]
+    lows_bytes = int(int(mix.counts[vg][owner[vg] == rank].sum()) * (D // 8 + 12) * nq / nlast)
+    nchunks = -(-nq // chunk)
+    kern_ms = stage_ranks[rank]["vanguard_scan"] * nchunks  # stage times are per chunk search
     achieved = lows_bytes / (kern_ms / 1e3) / 1e9 if kern_ms > 0 else None
     peak, peak_src = measured_peaks()
     roof = dict(bound="hbm", kernel="scan_kernel lows pass (this rank's vanguard pairs)",
                 achieved=achieved, peak=peak, unit="GB/s",
                 frac=(achieved / peak) if achieved else None, traffic=None, peak_source=peak_src,
                 algorithmic_bytes_per_launch=lows_bytes, launch_ms=kern_ms, rank=rank,
-                note="bytes = n_c*(D/8+12) per (query, probed cluster) of the launch")
+                note="bytes = n_c*(D/8+12) per (query, probed cluster) of the batch's lows "
+                     "passes (one per query chunk)")
     roofs = [None] * world
     dist.all_gather_object(roofs, roof)
     mode = six.engine.get_vanguard_mode()
-    per_search = launches_per_search(chosen, k, mode, world, estimator, 0)
+    per_search = launches_per_search(chosen, k, mode, world, estimator, 0,
+                                     six.split_probe) * nchunks
     if rank == 0:
         line = dict(
             metric=f"QPS at recall@{k}>=0.95 (IVF-RaBitQ search)", value=qps, unit="queries/s",
@@ -865,8 +876,8 @@ def run_shard_gen(args, name, cfg):
                         nprobe=chosen, recall=round(recall, 4), estimator=estimator,
                         recall_sweeps=sweeps, qualifying=candidates, shards=world,
                         vectors_per_shard=[int(v) for v in per_rank], build_s=round(build_s, 1),
-                        build_waves=wave, timed_repeats=len(per_step),
-                        stage_ms_per_rank=stage_ranks,
+                        build_waves=wave, timed_repeats=len(per_step), query_chunk=chunk,
+                        stage_ms_per_rank=stage_ranks, stage_ms_are="per query-chunk search",
                         l2_flush="inputs exceed L2 (index codes > 126 MB)",
                         cpu_baseline_note="no host holds the whole index; the reference's CPU "
                                           "search is timed on configs 1-4"),

@@ -217,21 +217,30 @@ class ShardedIndex:
     def end(self, recv, out_d, out_i):
         self.engine.shard_search_end(recv.data_ptr(), out_d.data_ptr(), out_i.data_ptr())
 
-    def search_device(self, queries, k, nprobe, out_d, out_i):
+    def _run_chunks(self, queries, k, nprobe, out_d, out_i, chunk):
+        nq = queries.shape[0]
+        step = nq if not chunk else int(chunk)
+        for a in range(0, nq, step):
+            b = min(nq, a + step)
+            run_sharded_search(self, self.exchange, queries[a:b], b - a, k, nprobe, out_d[a:b],
+                               out_i[a:b], self.split_probe)
+
+    def search_device(self, queries, k, nprobe, out_d, out_i, chunk=None):
         """Device tensors, ordered after torch's current stream and before its later work;
         not synchronised. The search and its all-gathers run on this index's own stream
-        (the engine's launches and NCCL's must share one non-default stream)."""
+        (the engine's launches and NCCL's must share one non-default stream). `chunk`: search
+        the batch in slices of at most that many queries (the shape limit queries x nlist
+        < 2^31, as the reference's --query-chunk)."""
         import torch
         if self._stream is None:
             self._stream = torch.cuda.Stream(self.device)
         cur = torch.cuda.current_stream(self.device)
         self._stream.wait_stream(cur)
         with torch.cuda.stream(self._stream):
-            run_sharded_search(self, self.exchange, queries, queries.shape[0], k, nprobe, out_d,
-                               out_i, self.split_probe)
+            self._run_chunks(queries, k, nprobe, out_d, out_i, chunk)
         cur.wait_stream(self._stream)
 
-    def capture(self, queries, k, nprobe, out_d, out_i):
+    def capture(self, queries, k, nprobe, out_d, out_i, chunk=None):
         """Captures one whole sharded search (the engine's launches and both NCCL
         all-gathers) into a CUDA graph on this rank, for replay(); every rank captures the
         same search. The buffers are baked in: replay() searches `queries` into out_d / out_i
@@ -244,8 +253,7 @@ class ShardedIndex:
             self._stream = torch.cuda.Stream(self.device)
         torch.cuda.synchronize(self.device)
         with torch.cuda.graph(g, stream=self._stream, capture_error_mode="relaxed"):
-            run_sharded_search(self, self.exchange, queries, queries.shape[0], k, nprobe, out_d,
-                               out_i, self.split_probe)
+            self._run_chunks(queries, k, nprobe, out_d, out_i, chunk)
         self._graph = g
 
     def replay(self):
@@ -265,14 +273,14 @@ class ShardedIndex:
             self._graph.reset()
             self._graph = None
 
-    def search(self, h_queries, k, nprobe):
+    def search(self, h_queries, k, nprobe, chunk=None):
         """Host arrays in and out (queries copied to this rank's GPU)."""
         import torch
         q = torch.from_numpy(np.ascontiguousarray(h_queries, np.float32)).to(
             f"cuda:{self.device}", non_blocking=True)
         out_d = torch.empty((q.shape[0], k), dtype=torch.float32, device=q.device)
         out_i = torch.empty((q.shape[0], k), dtype=torch.int32, device=q.device)
-        self.search_device(q, k, nprobe, out_d, out_i)
+        self.search_device(q, k, nprobe, out_d, out_i, chunk)
         d, i = out_d.cpu().numpy(), out_i.cpu().numpy().view(np.uint32)
         self.engine.check_device()
         return d, i
