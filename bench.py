@@ -720,6 +720,7 @@ def run_shard_gen(args, name, cfg):
             six.engine.load_shard_arrays(sd, mix.counts)
             del sd
             gc.collect()
+            torch.cuda.empty_cache()
         dist.barrier()
     six._verify()
     build_s = time.time() - t0
@@ -736,6 +737,9 @@ def run_shard_gen(args, name, cfg):
     dist.all_gather(gd, ld)
     gt_ids, gt_d = synthetic.merge_topk(torch.cat(gi, 1), torch.cat(gd, 1), k)
     log(f"[bench] ground truth (merged over shards) in {time.time() - t1:.1f}s")
+    del gi, gd, li, ld
+    gc.collect()
+    torch.cuda.empty_cache()  # the ground truth's score blocks stay cached otherwise
 
     # the shape limit queries x nlist < 2^31 (validate_search_shape, as the reference's):
     # the batch is searched in equal query chunks (the reference CLI's --query-chunk)
