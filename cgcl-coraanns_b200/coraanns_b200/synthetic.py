@@ -384,7 +384,7 @@ def build_shard(mix: ComponentShards, owner, rank, metric=0, seed=7, log=None):
 
 
 def ground_truth_shard(mix: ComponentShards, owner, rank, q, k, metric=0, keep=None,
-                       qblock=2048):
+                       qblock=1024, rows=1 << 20):
     """Exact top-k (as ground_truth_stream) over this shard's clusters only; the global
     ground truth is the (distance, id) merge of every shard's (merge_topk)."""
     keep = keep or max(2 * k, 64)
@@ -393,7 +393,7 @@ def ground_truth_shard(mix: ComponentShards, owner, rank, q, k, metric=0, keep=N
     prev = torch.backends.cuda.matmul.allow_tf32
     torch.backends.cuda.matmul.allow_tf32 = False
     try:
-        for x, _, gid in mix.batches(own):
+        for x, _, gid in mix.batches(own, rows=rows):  # score blocks of qblock x rows
             _gt_update(best_d, best_i, x, gid, q, k, metric, keep, qblock)
     finally:
         torch.backends.cuda.matmul.allow_tf32 = prev
