@@ -255,6 +255,10 @@ def _nccl_worker(rank, world, port, out_q):
         ix.split_probe = False
         d2, i2 = ix.search(q, 100, 8)
         ok = ok and np.array_equal(i2, i) and d2.tobytes() == d.tobytes()
+        # and in query chunks (an uneven last chunk), probing split again
+        ix.split_probe = True
+        d3, i3 = ix.search(q, 100, 8, chunk=max(1, len(q) // 3 + 1))
+        ok = ok and np.array_equal(i3, i) and d3.tobytes() == d.tobytes()
         ix.close()  # releases the graph before the process group goes
         out_q.put((rank, ok))
     finally:
